@@ -1,0 +1,380 @@
+"""Benchmark of the B200 Q4_K / Q6_K matvec (BASELINE.json metric: weight GB/s and % of HBM peak).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--workload NAME] [--impl kq|reference]
+
+One JSON line on rank 0. A step is one matvec over one weight matrix in HBM (the workload's
+shape), its weights rotating over enough copies that their total exceeds twice the 126 MB L2,
+so every step streams from DRAM. Workloads:
+
+  q6k_head   configs[1]  Q6_K 32000 x 4096, batch 1   (default; the metric's config)
+  q4k        configs[0]  Q4_K 4096 x 4096, batch 1
+  sweep      configs[3]  Q4_K 14336 x 4096, batch --batch (1..8)
+
+With N GPUs (torchrun) every rank runs its own replica: the single matvec does not shard
+("replicas only"), so `scaling` is "weak" and `value` sums the ranks' bytes over the slowest
+rank's time. `--impl reference` times the CPU implementation of the path (the oracle's AVX2 C
+port, all host threads) on the same workload; under torchrun only rank 0 runs it.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import re
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+if ROOT not in sys.path:
+    sys.path.insert(0, ROOT)
+
+L2_BYTES = 126 * 1024 * 1024
+FALLBACK_HBM_GBS = 6650.0
+
+WORKLOADS = {
+    "q6k_head": dict(qtype=6, rows=32000, k=4096, batch=1, source="BASELINE configs[1]"),
+    "q4k": dict(qtype=4, rows=4096, k=4096, batch=1, source="BASELINE configs[0]"),
+    "sweep": dict(qtype=4, rows=14336, k=4096, batch=None, source="BASELINE configs[3]"),
+}
+
+
+def parse_args(argv=None):
+    ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20000)
+    ap.add_argument("--warmup", type=int, default=200)
+    ap.add_argument("--workload", default="q6k_head", choices=sorted(WORKLOADS))
+    ap.add_argument("--batch", type=int, default=1)
+    ap.add_argument("--impl", default="kq", choices=["kq", "reference"])
+    ap.add_argument("--e2e-steps", type=int, default=2000, help="steps of the end-to-end leg")
+    ap.add_argument("--cpu-seconds", type=float, default=12.0, help="CPU-baseline time budget")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    return ap.parse_args(argv)
+
+
+def measured_peak():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            v = float(json.load(f)["hbm_gbs"])
+        return v, "measured"
+    except Exception:
+        return FALLBACK_HBM_GBS, "fallback"
+
+
+def profiled_traffic(name: str):
+    """Per-launch DRAM bytes (read + write) of the dominant kernel from the committed ncu
+    summary for this workload, or None."""
+    path = os.path.join(ROOT, "profiles", f"{name}.md")
+    try:
+        text = open(path).read()
+    except OSError:
+        return None
+    m = re.search(r"traffic_bytes_per_launch:\s*([0-9]+)", text)
+    return int(m.group(1)) if m else None
+
+
+class ClockSampler:
+    """nvidia-smi clock / throttle-reason samples while the timed region runs."""
+
+    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device: int):
+        self.device = device
+        self.proc = None
+        self.path = None
+
+    def start(self):
+        fd, self.path = tempfile.mkstemp(prefix="kq_clocks_", suffix=".csv")
+        os.close(fd)
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.device}", f"--query-gpu={self.QUERY}",
+                 "--format=csv,noheader,nounits", "-lms", "50"],
+                stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+        except OSError:
+            self.proc = None
+        time.sleep(0.15)
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        time.sleep(0.1)
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        rows = []
+        for line in open(self.path):
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) >= 9:
+                rows.append(parts)
+        os.unlink(self.path)
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
+        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
+        smax = [float(r[2]) for r in rows if r[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({n for r in rows for n, v in zip(names, r[5:9]) if v.lower() == "active"})
+        return {"sm_mhz": statistics.median(sm) if sm else None,
+                "sm_max_mhz": max(smax) if smax else None, "reasons": reasons,
+                "samples": len(rows)}
+
+
+def dist_setup():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return world, rank, local
+
+
+def workload_shape(args):
+    w = dict(WORKLOADS[args.workload])
+    if w["batch"] is None:
+        w["batch"] = args.batch
+    return w
+
+
+def cpu_matvec_timing(qtype, Wh, x, rows, K, seconds, threads):
+    """Repeats the CPU matvec on a row sample until `seconds` pass; returns (GB/s, sample)."""
+    import oracle
+
+    bb = 144 if qtype == 4 else 210
+    rb = (K // 256) * bb
+    t0 = time.perf_counter()
+    oracle.matvec_cpu(qtype, Wh, x, rows, K, threads)
+    one = time.perf_counter() - t0
+    # sample rows so that one call is ~ seconds / 8, at least 256 rows
+    sample_rows = max(256, min(rows, int(rows * (seconds / 8) / max(one, 1e-6))))
+    reps = 0
+    t0 = time.perf_counter()
+    while True:
+        oracle.matvec_cpu(qtype, Wh[: sample_rows * rb], x, sample_rows, K, threads)
+        reps += 1
+        if time.perf_counter() - t0 >= seconds:
+            break
+    el = time.perf_counter() - t0
+    gbs = sample_rows * rb * reps / el / 1e9
+    sample = f"{reps} x {sample_rows} rows of the {rows}x{K} Q{qtype}_K matrix, batch {x.shape[0]}, {el:.1f} s"
+    return gbs, sample
+
+
+def run_reference(args):
+    """The reference arm: the CPU implementation of the path (the oracle's AVX2 port)."""
+    import numpy as np
+
+    import oracle
+
+    world, rank, _ = dist_setup()
+    if rank != 0:
+        return 0
+    w = workload_shape(args)
+    qtype, rows, K, batch = w["qtype"], w["rows"], w["k"], w["batch"]
+    threads = oracle.cpu_threads()
+    bb = 144 if qtype == 4 else 210
+    rb = (K // 256) * bb
+    Wh = oracle.fill(qtype, oracle.stream_key(2026, qtype), 0, rows * K // 256)
+    x = np.random.default_rng(0).standard_normal((batch, K), dtype=np.float32)
+    t0 = time.perf_counter()
+    oracle.matvec_cpu(qtype, Wh, x, rows, K, threads)
+    one = time.perf_counter() - t0
+    total_budget = 90.0
+    per_step = total_budget / max(1, args.steps + args.warmup)
+    sample_rows = max(64, min(rows, int(rows * per_step / max(one, 1e-6))))
+    for _ in range(args.warmup):
+        oracle.matvec_cpu(qtype, Wh[: sample_rows * rb], x, sample_rows, K, threads)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        oracle.matvec_cpu(qtype, Wh[: sample_rows * rb], x, sample_rows, K, threads)
+    el = time.perf_counter() - t0
+    gbs = sample_rows * rb * args.steps / el / 1e9
+    sample = (f"each step {sample_rows} of {rows} rows of the Q{qtype}_K {rows}x{K} matrix, "
+              f"batch {batch}")
+    line = {
+        "impl": "reference", "metric": "weight GB/s", "value": round(gbs, 3), "unit": "GB/s",
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(el / args.steps * 1e3, 4), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": config_of(args, w, world),
+        "cpu_baseline": {"value": round(gbs, 3), "unit": "GB/s", "cores": threads, "kind": "port",
+                         "sample": sample},
+        "e2e": {"value": round(gbs, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "gpu_launches": 0,
+        "note": "fxeqxmulfx/kernite has no k-quant path and no Rust toolchain here; the CPU "
+                "implementation timed is this repo's AVX2+FMA C port (oracle/kq_cpu.c)",
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def config_of(args, w, world):
+    return {
+        "workload": f"{args.workload}: Q{w['qtype']}_K {w['rows']}x{w['k']} batch {w['batch']} ({w['source']})",
+        "qtype": f"Q{w['qtype']}_K", "rows": w["rows"], "k": w["k"], "batch": w["batch"],
+        "parallelism": f"replicas x{world}" if world > 1 else "single",
+    }
+
+
+def main(argv=None):
+    args = parse_args(argv)
+    if args.impl == "reference":
+        return run_reference(args)
+
+    import numpy as np
+    import torch
+
+    import kernite_b200 as kb
+
+    world, rank, local = dist_setup()
+    torch.cuda.set_device(local)
+    dist = None
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+    kernels = kb.Kernels.load(local)
+    w = workload_shape(args)
+    qtype, rows, K, batch = w["qtype"], w["rows"], w["k"], w["batch"]
+    wbytes = kb.matrix_bytes(qtype, rows, K)
+    algo_bytes = wbytes + batch * K * 4 + batch * rows * 4
+    copies = max(2, -(-2 * L2_BYTES // wbytes) + 1)
+    nblk = rows * K // 256
+    Ws = []
+    for c in range(copies):
+        W = torch.empty(wbytes, dtype=torch.uint8, device="cuda")
+        kernels.fill(qtype, W, 0, nblk, kb.stream_key(2026 + c, qtype))
+        Ws.append(W)
+    rng = np.random.default_rng(rank)
+    x = torch.from_numpy(rng.standard_normal((batch, K), dtype=np.float32)).cuda()
+    y = torch.empty(batch, rows, device="cuda")
+    stream = torch.cuda.Stream()
+    torch.cuda.synchronize()
+
+    def step(i):
+        kernels.matvec(qtype, y, Ws[i % copies], x, rows, K, batch, flags=kb.FLAG_WEIGHTS_STATIC,
+                       stream=stream)
+
+    with torch.cuda.stream(stream):
+        for i in range(args.warmup):
+            step(i)
+    torch.cuda.synchronize()
+    kernels.device_error()
+
+    sampler = ClockSampler(local)
+    sampler.start()
+    if dist:
+        dist.barrier()
+    torch.cuda.synchronize()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ev0.record(stream)
+    for i in range(args.steps):
+        step(i)
+    ev1.record(stream)
+    torch.cuda.synchronize()
+    if dist:
+        dist.barrier()
+    clocks = sampler.stop()
+    ms = ev0.elapsed_time(ev1)
+    kernels.device_error()
+    if dist:
+        t = torch.tensor([ms], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    ms_step = ms / args.steps
+    value = world * wbytes * args.steps / (ms / 1e3) / 1e9
+
+    # end to end through the public API: pinned x in, y out, every step
+    e2e = run_e2e(kernels, kb, torch, qtype, Ws, rows, K, batch, args.e2e_steps, dist)
+
+    peak, peak_kind = measured_peak()
+    achieved = algo_bytes / (ms_step / 1e3) / 1e9
+    traffic = profiled_traffic(args.workload if args.workload != "sweep" else f"sweep_b{batch}")
+    roofline = {"bound": "hbm", "achieved": round(achieved, 2), "peak": peak, "unit": "GB/s",
+                "frac": round(achieved / peak, 4), "traffic": traffic,
+                "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)" if peak_kind == "measured"
+                else "fallback 6650 GB/s", "algorithmic_bytes_per_launch": algo_bytes}
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        import oracle
+
+        Wh = Ws[0].cpu().numpy()
+        gbs, sample = cpu_matvec_timing(qtype, Wh, x.cpu().numpy(), rows, K, args.cpu_seconds,
+                                        oracle.cpu_threads())
+        cpu = {"value": round(gbs, 3), "unit": "GB/s", "cores": oracle.cpu_threads(), "kind": "port",
+               "sample": sample}
+
+    if rank == 0:
+        cfg = config_of(args, w, world)
+        cfg["l2"] = f"weights rotate over {copies} copies ({copies * wbytes / 1e6:.0f} MB > 2x L2)"
+        line = {
+            "metric": "weight GB/s", "value": round(value, 2), "unit": "GB/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_step, 6),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic", "config": cfg,
+            "hbm_frac": round(achieved / peak, 4),
+            "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e,
+            "gpu_launches": args.steps, "clocks": clocks,
+        }
+        print(json.dumps(line), flush=True)
+    kernels.close()
+    if dist:
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
+def run_e2e(kernels, kb, torch, qtype, Ws, rows, K, batch, steps, dist):
+    """The same matvec through kernite_b200's public API with host buffers: each step copies its
+    x from pinned host memory, launches, and reads y back into pinned host memory."""
+    import numpy as np
+
+    copies = len(Ws)
+    xh = torch.from_numpy(np.random.default_rng(1).standard_normal((batch, K), dtype=np.float32)).pin_memory()
+    yh = torch.empty(batch, rows).pin_memory()
+    xd = torch.empty(batch, K, device="cuda")
+    yd = torch.empty(batch, rows, device="cuda")
+    s = torch.cuda.Stream()
+    fn = kernels.matvec_q4k if qtype == 4 else kernels.matvec_q6k
+
+    def step(i):
+        with torch.cuda.stream(s):
+            xd.copy_(xh, non_blocking=True)
+            fn(yd, Ws[i % copies], xd, rows, K, batch, stream=s)
+            yh.copy_(yd, non_blocking=True)
+        s.synchronize()
+
+    for i in range(20):
+        step(i)
+    if dist:
+        dist.barrier()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(s)
+    for i in range(steps):
+        step(i)
+    e1.record(s)
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1)
+    if dist:
+        t = torch.tensor([ms], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    world = dist.get_world_size() if dist else 1
+    wbytes = kb.matrix_bytes(qtype, rows, K)
+    return {"value": round(world * wbytes * steps / (ms / 1e3) / 1e9, 2), "unit": "GB/s",
+            "h2d_bytes_per_step": batch * K * 4, "d2h_bytes_per_step": batch * rows * 4,
+            "steps": steps, "ms_per_step": round(ms / steps, 5)}
+
+
+if __name__ == "__main__":
+    sys.exit(main())

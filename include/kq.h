@@ -1,0 +1,150 @@
+/*
+ * kq.h -- the C ABI of the B200 Q4_K / Q6_K matvec library (libkq.so).
+ *
+ * This is the drop-in boundary. fxeqxmulfx/kernite calls a kernel through a macro-generated
+ * launcher `unsafe fn <kernel>(&self, grid: Grid, params...) -> Result<(), kernite_cuda::Error>`
+ * (crates/macros/src/gpu.rs:276-328) on a `Kernels` struct that `Kernels::load(&Cuda)` fills by
+ * loading a module (crates/macros/src/gpu.rs:74-98, crates/cuda/src/lib.rs:945-1016), and
+ * launches with `cuLaunchKernel` (crates/cuda/src/lib.rs:1045-1054). Each entry point below
+ * replaces one piece of that, as its comment says; INTEGRATION.md shows the Rust binding.
+ *
+ * Conventions (kernite-cuda's, kept):
+ *  - Device pointers are plain 64-bit addresses, exactly what `kernite_cuda::Ptr::addr()`
+ *    gives (crates/cuda/src/lib.rs:776-837). The library never owns a caller's buffer.
+ *  - Every entry point returns 0 on success, or an error code: a CUDA error number (< 1000),
+ *    or one of KQ_E_* below. kq_last_error() then gives the thread's last error as
+ *    "<call>: <NAME> (<n>): <meaning>[: detail]", the shape of kernite_cuda::Error's Display
+ *    (crates/cuda/src/lib.rs:290-324). Arguments are checked before any launch; a bad
+ *    argument is KQ_E_INVALID, never a device fault.
+ *  - Launches are asynchronous on the given stream (NULL = the legacy default stream, on which
+ *    kernite launches everything, crates/cuda/src/lib.rs:1051).
+ *  - A kq_ctx is for the thread and GPU that made it, as a kernite `Cuda` is
+ *    (crates/cuda/src/lib.rs:27-35). Entry points make the ctx's device current if it is not.
+ *
+ * Safety contract (kernite's launcher contract, crates/cuda/src/lib.rs:1035-1044): every pointer
+ * must be device memory of the ctx's GPU, valid until the launch completes; the host must not
+ * touch memory a launch writes until it completes.
+ *
+ * Formats: Q4_K super-block = 144 bytes {fp16 d, fp16 dmin, u8 scales[12], u8 qs[128]};
+ * Q6_K super-block = 210 bytes {u8 ql[128], u8 qh[64], i8 scales[16], fp16 d}; 256 weights
+ * each (GGML k-quant layout). A matrix of `rows` x `k` is rows * (k/256) consecutive blocks,
+ * row-major.
+ */
+#ifndef KQ_H
+#define KQ_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define KQ_ABI_VERSION 1
+
+enum {
+    KQ_OK = 0,
+    KQ_E_INVALID = 1001,     /* an argument was rejected before launch */
+    KQ_E_UNSUPPORTED = 1002, /* a valid request this build does not serve (e.g. a shape limit) */
+    KQ_E_DEVICE = 1003,      /* the device reported a failed bounded wait (see kq_device_error) */
+    KQ_E_COMM = 1004         /* a multi-GPU exchange failed */
+};
+
+/* Quantisation types, GGML's type numbers. */
+enum { KQ_TYPE_Q4_K = 12, KQ_TYPE_Q6_K = 14 };
+
+/* What a matvec does to x before the product, and to each output after it. */
+enum { KQ_PROLOGUE_NONE = 0, KQ_PROLOGUE_RMSNORM = 1 };
+enum { KQ_EPILOGUE_NONE = 0, KQ_EPILOGUE_PAIR_PRODUCT = 1 };
+
+/* Flags for kq_matvec_desc.flags. */
+enum {
+    /* The weights were written before the previous kernel on the stream began: the kernel may
+     * start streaming them before that kernel ends (programmatic dependent launch). */
+    KQ_FLAG_WEIGHTS_STATIC = 1u << 0,
+    /* Launch without the programmatic-dependent-launch attribute. */
+    KQ_FLAG_NO_PDL = 1u << 1
+};
+
+typedef struct kq_ctx kq_ctx;
+typedef void* kq_stream; /* a cudaStream_t / CUstream; NULL = legacy default stream */
+
+/* Opens GPU `device`: retains its primary context (the one kernite-cuda's Cuda::on retains,
+ * crates/cuda/src/lib.rs:570-617, so buffers from kernite's Cuda::alloc are valid here), reads
+ * its attributes and prepares every kernel of the library. Replaces Cuda::on(i) followed by the
+ * macro's Kernels::load(&cuda) (crates/macros/src/gpu.rs:74-98). */
+int kq_ctx_create(int device, kq_ctx** out);
+
+/* Frees what the ctx owns. Replaces `Drop for Module` (crates/cuda/src/lib.rs:1129-1138). */
+int kq_ctx_destroy(kq_ctx* ctx);
+
+/* The calling thread's last error, NUL-terminated into buf (truncated to len). Returns the
+ * full length. Replaces kernite_cuda::Error's Display (crates/cuda/src/lib.rs:290-324). */
+size_t kq_last_error(char* buf, size_t len);
+
+/* The ctx's GPU: its ordinal, SM count and opt-in shared memory per block. Replaces
+ * Cuda::multiprocessors / max_shared (crates/cuda/src/lib.rs:602-631). */
+int kq_ctx_info(const kq_ctx* ctx, int* device, int* sm_count, int* max_smem_per_block);
+
+/* Waits for the ctx's device, then reads and clears the device error word that the kernels'
+ * bounded waits set instead of hanging. 0 if clear, KQ_E_DEVICE (with a message naming the
+ * wait) if a kernel gave up. No reference counterpart: kernite's kernels have no bounded waits. */
+int kq_device_error(kq_ctx* ctx);
+
+/* y[b*rows + r] = sum_k W[r,k] * x[b*k + k'] for b < batch, r < rows: the Q4_K matvec.
+ * batch 1..8 on the CUDA cores. W: 16-byte aligned; x: 16-byte aligned f32; y: f32.
+ * Replaces a macro launcher `kernels.matvec_q4k(grid, y, w, x, rows, k)` of kernite's shape
+ * (crates/macros/src/gpu.rs:276-328); the grid is the library's choice, not the caller's. */
+int kq_matvec_q4k(kq_ctx* ctx, uint64_t y, uint64_t w, uint64_t x, uint32_t rows, uint32_t k,
+                  uint32_t batch, kq_stream stream);
+
+/* The same for Q6_K (210-byte blocks; rows may start at any even byte offset). */
+int kq_matvec_q6k(kq_ctx* ctx, uint64_t y, uint64_t w, uint64_t x, uint32_t rows, uint32_t k,
+                  uint32_t batch, kq_stream stream);
+
+/* The general form: strides, fused prologue/epilogue, flags. */
+typedef struct kq_matvec_desc {
+    uint32_t type;     /* KQ_TYPE_Q4_K or KQ_TYPE_Q6_K */
+    uint32_t rows, k;  /* W is rows x k; k % 256 == 0 */
+    uint32_t batch;    /* vectors, 1..8 */
+    uint64_t y, w, x;  /* device addresses */
+    uint64_t ldx;      /* floats between vectors of x (>= k, multiple of 4); 0 = k */
+    uint64_t ldy;      /* floats between vectors of y; 0 = rows (or rows/2 for PAIR_PRODUCT) */
+    uint32_t prologue; /* KQ_PROLOGUE_*: RMSNORM uses x / sqrt(mean(x^2) + eps) */
+    uint32_t epilogue; /* KQ_EPILOGUE_*: PAIR_PRODUCT writes y[r/2] = v(r) * v(r+1) * pair_scale
+                          for even r (rows must be even) */
+    float eps;
+    float pair_scale;
+    uint32_t flags;    /* KQ_FLAG_* */
+    uint32_t reserved;
+} kq_matvec_desc;
+
+/* Replaces the same launcher as kq_matvec_q4k, with kernite's per-kernel instance choice
+ * (examples/matmul/src/gpu.rs:360-391) made from the descriptor. */
+int kq_matvec(kq_ctx* ctx, const kq_matvec_desc* desc, kq_stream stream);
+
+/* out[256*i + e] = weight e of block i, for nblocks blocks at w, in the canonical order
+ * w = (f32(d)*f32(sc))*f32(q) - f32(dmin)*f32(m) (Q4_K) / (f32(d)*f32(scale))*f32(q-32) (Q6_K),
+ * each operation rounded to f32: bit-exact with the CPU decode. A verification kernel. No
+ * reference counterpart (kernite has no k-quant decode); its bit-exact discipline follows
+ * examples/matmul/src/reference.rs:1-10. */
+int kq_dequant_q4k(kq_ctx* ctx, uint64_t out, uint64_t w, uint64_t nblocks, kq_stream stream);
+int kq_dequant_q6k(kq_ctx* ctx, uint64_t out, uint64_t w, uint64_t nblocks, kq_stream stream);
+
+/* Writes synthetic blocks [block0, block0 + nblocks) of the tensor whose stream key is `key`
+ * at w (w points at block0): counter-based splitmix64, so any range is reproducible on the CPU.
+ * Q4_K: scale/quant bytes uniform, d and dmin = fp16(uniform[2^-10, 2^-6]); Q6_K: ql/qh bytes
+ * uniform, scales uniform in [-64, 63], d = fp16(uniform[2^-12, 2^-8]). Stands in for the
+ * seeded xorshift inputs of examples/matmul/src/main.rs:116-125. */
+int kq_fill_q4k(kq_ctx* ctx, uint64_t w, uint64_t block0, uint64_t nblocks, uint64_t key,
+                kq_stream stream);
+int kq_fill_q6k(kq_ctx* ctx, uint64_t w, uint64_t block0, uint64_t nblocks, uint64_t key,
+                kq_stream stream);
+
+/* The stream key of tensor `tensor` under `seed` (host function; the same as the oracle's). */
+uint64_t kq_stream_key(uint64_t seed, uint64_t tensor);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* KQ_H */

@@ -1,0 +1,248 @@
+"""kernite_b200 -- a B200-native Q4_K / Q6_K matvec behind kernite-cuda's call surface.
+
+The product is ``libkq.so`` (hand-written CUDA for sm_100a behind the C ABI in
+``include/kq.h``). This module is the host-side mirror of fxeqxmulfx/kernite's interface for the
+path, bound with ctypes:
+
+* :class:`Cuda` -- a GPU, as ``kernite_cuda::Cuda::on(i)`` (crates/cuda/src/lib.rs:570-617).
+* :class:`Kernels` -- the loaded kernels, as a macro-generated ``Kernels::load(&cuda)``
+  (crates/macros/src/gpu.rs:74-98), with one launcher per kernel, as the macro's
+  ``unsafe fn <kernel>(&self, grid, params...) -> Result<(), Error>``
+  (crates/macros/src/gpu.rs:276-328). The grid is the library's choice, so launchers take no grid.
+* :class:`Error` -- ``kernite_cuda::Error{call, message, log}`` (crates/cuda/src/lib.rs:280-324).
+
+Pointers are device addresses (``int``) or CUDA tensors (their ``data_ptr()``), the caller's
+buffers; nothing here allocates for a launch. There is no CPU fallback: without ``libkq.so``
+every entry point raises.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+from typing import Any
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "libkq.so")
+
+KQ_OK = 0
+KQ_E_INVALID = 1001
+KQ_E_UNSUPPORTED = 1002
+KQ_E_DEVICE = 1003
+KQ_E_COMM = 1004
+
+TYPE_Q4_K = 12
+TYPE_Q6_K = 14
+PROLOGUE_NONE = 0
+PROLOGUE_RMSNORM = 1
+EPILOGUE_NONE = 0
+EPILOGUE_PAIR_PRODUCT = 1
+FLAG_WEIGHTS_STATIC = 1
+FLAG_NO_PDL = 2
+
+Q4K_BYTES = 144
+Q6K_BYTES = 210
+QK = 256
+
+# Every symbol include/kq.h declares (tests check the library exports each).
+EXPORTS = (
+    "kq_ctx_create", "kq_ctx_destroy", "kq_last_error", "kq_ctx_info", "kq_device_error",
+    "kq_matvec_q4k", "kq_matvec_q6k", "kq_matvec", "kq_dequant_q4k", "kq_dequant_q6k",
+    "kq_fill_q4k", "kq_fill_q6k", "kq_stream_key",
+)
+
+
+class Error(RuntimeError):
+    """What went wrong in a call: ``call`` (the C function), ``message``, and ``code``."""
+
+    def __init__(self, call: str, message: str, code: int = -1, log: str = ""):
+        self.call = call
+        self.message = message
+        self.code = code
+        self.log = log
+        super().__init__(f"{call}: {message}" + (f"\n{log}" if log else ""))
+
+
+class KqMatvecDesc(ctypes.Structure):
+    _fields_ = [
+        ("type", ctypes.c_uint32), ("rows", ctypes.c_uint32), ("k", ctypes.c_uint32),
+        ("batch", ctypes.c_uint32), ("y", ctypes.c_uint64), ("w", ctypes.c_uint64),
+        ("x", ctypes.c_uint64), ("ldx", ctypes.c_uint64), ("ldy", ctypes.c_uint64),
+        ("prologue", ctypes.c_uint32), ("epilogue", ctypes.c_uint32), ("eps", ctypes.c_float),
+        ("pair_scale", ctypes.c_float), ("flags", ctypes.c_uint32), ("reserved", ctypes.c_uint32),
+    ]
+
+
+_lib: ctypes.CDLL | None = None
+
+
+def lib() -> ctypes.CDLL:
+    """The loaded ``libkq.so``; raises :class:`Error` if it is not built."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    if not os.path.exists(LIB_PATH):
+        raise Error("dlopen", f"{LIB_PATH} is missing: build it with `python -m kernite_b200.build`")
+    L = ctypes.CDLL(LIB_PATH)
+    vp = ctypes.c_void_p
+    u32, u64, i32 = ctypes.c_uint32, ctypes.c_uint64, ctypes.c_int
+    L.kq_ctx_create.argtypes = [i32, ctypes.POINTER(vp)]
+    L.kq_ctx_destroy.argtypes = [vp]
+    L.kq_last_error.argtypes = [ctypes.c_char_p, ctypes.c_size_t]
+    L.kq_last_error.restype = ctypes.c_size_t
+    L.kq_ctx_info.argtypes = [vp, ctypes.POINTER(i32), ctypes.POINTER(i32), ctypes.POINTER(i32)]
+    L.kq_device_error.argtypes = [vp]
+    for name in ("kq_matvec_q4k", "kq_matvec_q6k"):
+        getattr(L, name).argtypes = [vp, u64, u64, u64, u32, u32, u32, vp]
+    L.kq_matvec.argtypes = [vp, ctypes.POINTER(KqMatvecDesc), vp]
+    for name in ("kq_dequant_q4k", "kq_dequant_q6k"):
+        getattr(L, name).argtypes = [vp, u64, u64, u64, vp]
+    for name in ("kq_fill_q4k", "kq_fill_q6k"):
+        getattr(L, name).argtypes = [vp, u64, u64, u64, u64, vp]
+    L.kq_stream_key.argtypes = [u64, u64]
+    L.kq_stream_key.restype = u64
+    for name in EXPORTS:
+        fn = getattr(L, name)
+        if name not in ("kq_last_error", "kq_stream_key"):
+            fn.restype = i32
+    _lib = L
+    return L
+
+
+def last_error() -> str:
+    L = lib()
+    n = L.kq_last_error(None, 0)
+    buf = ctypes.create_string_buffer(n + 1)
+    L.kq_last_error(buf, n + 1)
+    return buf.value.decode(errors="replace")
+
+
+def _check(rc: int, call: str) -> None:
+    if rc != 0:
+        msg = last_error()
+        head, _, rest = msg.partition(": ")
+        raise Error(head or call, rest or msg, rc)
+
+
+def _addr(p: Any) -> int:
+    if p is None:
+        return 0
+    if isinstance(p, int):
+        return p
+    if hasattr(p, "data_ptr"):
+        if hasattr(p, "is_cuda") and not p.is_cuda:
+            raise Error("kernite_b200", "a tensor given as a device pointer is on the CPU")
+        return int(p.data_ptr())
+    raise TypeError(f"not a device pointer: {type(p)!r}")
+
+
+def _stream(s: Any) -> int | None:
+    if s is None:
+        return None
+    if isinstance(s, int):
+        return s or None
+    if hasattr(s, "cuda_stream"):
+        return int(s.cuda_stream) or None
+    raise TypeError(f"not a stream: {type(s)!r}")
+
+
+def stream_key(seed: int, tensor: int) -> int:
+    """The stream key of synthetic tensor ``tensor`` under ``seed`` (as the oracle's)."""
+    return int(lib().kq_stream_key(seed & (2**64 - 1), tensor & (2**64 - 1)))
+
+
+class Cuda:
+    """GPU ``index``, opened: ``kernite_cuda::Cuda::on(index)``."""
+
+    def __init__(self, index: int = 0):
+        self.index = index
+
+    @classmethod
+    def on(cls, index: int) -> "Cuda":
+        return cls(index)
+
+    @classmethod
+    def new(cls) -> "Cuda":
+        return cls(0)
+
+
+class Kernels:
+    """The library's kernels loaded on one GPU; one launcher per kernel.
+
+    Every launcher is asynchronous on ``stream`` (None = the legacy default stream, where
+    kernite launches) and has kernite's launcher contract: pointers are device memory of this
+    GPU, valid and untouched by the host until the launch completes."""
+
+    def __init__(self, ctx: int, cuda: Cuda):
+        self._ctx = ctypes.c_void_p(ctx)
+        self.cuda = cuda
+        dev, sms, smem = ctypes.c_int(), ctypes.c_int(), ctypes.c_int()
+        _check(lib().kq_ctx_info(self._ctx, ctypes.byref(dev), ctypes.byref(sms), ctypes.byref(smem)),
+               "kq_ctx_info")
+        self.device, self.sm_count, self.max_shared = dev.value, sms.value, smem.value
+
+    @classmethod
+    def load(cls, cuda: Cuda | int = 0) -> "Kernels":
+        if isinstance(cuda, int):
+            cuda = Cuda.on(cuda)
+        ctx = ctypes.c_void_p()
+        _check(lib().kq_ctx_create(cuda.index, ctypes.byref(ctx)), "kq_ctx_create")
+        return cls(ctx.value, cuda)
+
+    def close(self) -> None:
+        if self._ctx:
+            lib().kq_ctx_destroy(self._ctx)
+            self._ctx = ctypes.c_void_p()
+
+    def __del__(self):  # pragma: no cover - best effort
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    @property
+    def handle(self) -> int:
+        return int(self._ctx.value or 0)
+
+    # ----------------------------------------------------------------- launchers
+
+    def matvec_q4k(self, y, w, x, rows: int, k: int, batch: int = 1, stream=None) -> None:
+        """``y[b*rows + r] = sum_k W[r,k] x[b*k + k]``, W in Q4_K blocks."""
+        _check(lib().kq_matvec_q4k(self._ctx, _addr(y), _addr(w), _addr(x), rows, k, batch,
+                                   _stream(stream)), "kq_matvec_q4k")
+
+    def matvec_q6k(self, y, w, x, rows: int, k: int, batch: int = 1, stream=None) -> None:
+        """The same for Q6_K blocks."""
+        _check(lib().kq_matvec_q6k(self._ctx, _addr(y), _addr(w), _addr(x), rows, k, batch,
+                                   _stream(stream)), "kq_matvec_q6k")
+
+    def matvec(self, qtype: int, y, w, x, rows: int, k: int, batch: int = 1, *, ldx: int = 0,
+               ldy: int = 0, prologue: int = PROLOGUE_NONE, epilogue: int = EPILOGUE_NONE,
+               eps: float = 0.0, pair_scale: float = 1.0, flags: int = 0, stream=None) -> None:
+        """The general matvec (``kq_matvec``); qtype is 4/6 or TYPE_Q4_K/TYPE_Q6_K."""
+        t = {4: TYPE_Q4_K, 6: TYPE_Q6_K}.get(qtype, qtype)
+        d = KqMatvecDesc(type=t, rows=rows, k=k, batch=batch, y=_addr(y), w=_addr(w), x=_addr(x),
+                         ldx=ldx, ldy=ldy, prologue=prologue, epilogue=epilogue, eps=eps,
+                         pair_scale=pair_scale, flags=flags, reserved=0)
+        _check(lib().kq_matvec(self._ctx, ctypes.byref(d), _stream(stream)), "kq_matvec")
+
+    def dequant(self, qtype: int, out, w, nblocks: int, stream=None) -> None:
+        """Bit-exact decode of ``nblocks`` blocks into f32 (verification kernel)."""
+        fn = lib().kq_dequant_q4k if qtype in (4, TYPE_Q4_K) else lib().kq_dequant_q6k
+        _check(fn(self._ctx, _addr(out), _addr(w), nblocks, _stream(stream)), "kq_dequant")
+
+    def fill(self, qtype: int, w, block0: int, nblocks: int, key: int, stream=None) -> None:
+        """Synthetic blocks [block0, block0 + nblocks) of the keyed tensor, written at w."""
+        fn = lib().kq_fill_q4k if qtype in (4, TYPE_Q4_K) else lib().kq_fill_q6k
+        _check(fn(self._ctx, _addr(w), block0, nblocks, key & (2**64 - 1), _stream(stream)), "kq_fill")
+
+    def device_error(self) -> None:
+        """Synchronises the GPU and raises if a kernel's bounded wait gave up."""
+        _check(lib().kq_device_error(self._ctx), "kq_device_error")
+
+
+def block_bytes(qtype: int) -> int:
+    return Q4K_BYTES if qtype in (4, TYPE_Q4_K) else Q6K_BYTES
+
+
+def matrix_bytes(qtype: int, rows: int, k: int) -> int:
+    return rows * (k // QK) * block_bytes(qtype)

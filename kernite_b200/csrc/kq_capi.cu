@@ -1,0 +1,212 @@
+// kq_capi.cu -- the C ABI (include/kq.h): contexts, errors, argument checks, dispatch.
+//
+// Errors keep the shape of fxeqxmulfx/kernite's kernite_cuda::Error (crates/cuda/src/lib.rs:
+// 290-324): the failing call, then "NAME (number): meaning" for a CUDA error, then any detail.
+// The message is per thread, as a Rust Result is per call.
+#include <cuda_runtime.h>
+
+#include <cstdio>
+#include <cstring>
+#include <string>
+
+#include "kq_device.cuh"
+#include "kq_internal.h"
+
+// The device error word that bounded waits write instead of hanging. A file-scope device
+// variable: every GPU that loads the library has its own copy; host code takes its address with
+// cudaGetSymbolAddress per device in kq_ctx_create.
+__device__ unsigned g_kq_error_word;
+
+namespace kq {
+
+namespace {
+thread_local std::string t_last_error;
+}
+
+int fail(int code, const char* call, const std::string& detail) {
+  t_last_error = std::string(call) + ": " + detail;
+  return code;
+}
+
+int cuda_fail(cudaError_t e, const char* call, const std::string& detail) {
+  std::string msg = std::string(call) + ": " + cudaGetErrorName(e) + " (" +
+                    std::to_string(static_cast<int>(e)) + "): " + cudaGetErrorString(e);
+  if (!detail.empty()) msg += ": " + detail;
+  t_last_error = msg;
+  cudaGetLastError();  // a launch-configuration error is not sticky; do not leave it pending
+  return static_cast<int>(e);
+}
+
+int enter(const kq_ctx* ctx) {
+  int cur = -1;
+  cudaError_t e = cudaGetDevice(&cur);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+  if (cur != ctx->device) {
+    e = cudaSetDevice(ctx->device);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaSetDevice");
+  }
+  return KQ_OK;
+}
+
+}  // namespace kq
+
+using kq::cuda_fail;
+using kq::fail;
+
+extern "C" {
+
+int kq_ctx_create(int device, kq_ctx** out) {
+  if (!out) return fail(KQ_E_INVALID, "kq_ctx_create", "null out pointer");
+  *out = nullptr;
+  int count = 0;
+  cudaError_t e = cudaGetDeviceCount(&count);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaGetDeviceCount");
+  if (device < 0 || device >= count)
+    return fail(KQ_E_INVALID, "kq_ctx_create",
+                "no GPU " + std::to_string(device) + " (the program sees " + std::to_string(count) +
+                    ")");
+  e = cudaSetDevice(device);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaSetDevice");
+  int major = 0, minor = 0;
+  cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, device);
+  cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, device);
+  if (major != 10 || minor != 0)
+    return fail(KQ_E_UNSUPPORTED, "kq_ctx_create",
+                "this library is built for sm_100a (B200); GPU " + std::to_string(device) +
+                    " is sm_" + std::to_string(major) + std::to_string(minor));
+  kq_ctx* ctx = new kq_ctx();
+  ctx->device = device;
+  cudaDeviceGetAttribute(&ctx->sm_count, cudaDevAttrMultiProcessorCount, device);
+  cudaDeviceGetAttribute(&ctx->max_smem, cudaDevAttrMaxSharedMemoryPerBlockOptin, device);
+  // Leave room for the kernels' static shared memory.
+  ctx->max_smem -= 2048;
+  void* p = nullptr;
+  e = cudaGetSymbolAddress(&p, g_kq_error_word);
+  if (e != cudaSuccess) {
+    delete ctx;
+    return cuda_fail(e, "cudaGetSymbolAddress", "device error word");
+  }
+  ctx->err = static_cast<unsigned*>(p);
+  e = cudaMemset(ctx->err, 0, sizeof(unsigned));
+  if (e != cudaSuccess) {
+    delete ctx;
+    return cuda_fail(e, "cudaMemset", "device error word");
+  }
+  int rc = kq::matvec_prepare(ctx);
+  if (rc == KQ_OK) rc = kq::aux_prepare(ctx);
+  if (rc != KQ_OK) {
+    delete ctx;
+    return rc;
+  }
+  *out = ctx;
+  return KQ_OK;
+}
+
+int kq_ctx_destroy(kq_ctx* ctx) {
+  delete ctx;
+  return KQ_OK;
+}
+
+size_t kq_last_error(char* buf, size_t len) {
+  const std::string& m = kq::t_last_error;
+  if (buf && len) {
+    const size_t n = m.size() < len - 1 ? m.size() : len - 1;
+    std::memcpy(buf, m.data(), n);
+    buf[n] = '\0';
+  }
+  return m.size();
+}
+
+int kq_ctx_info(const kq_ctx* ctx, int* device, int* sm_count, int* max_smem_per_block) {
+  if (!ctx) return fail(KQ_E_INVALID, "kq_ctx_info", "null ctx");
+  if (device) *device = ctx->device;
+  if (sm_count) *sm_count = ctx->sm_count;
+  if (max_smem_per_block) *max_smem_per_block = ctx->max_smem;
+  return KQ_OK;
+}
+
+int kq_device_error(kq_ctx* ctx) {
+  if (!ctx) return fail(KQ_E_INVALID, "kq_device_error", "null ctx");
+  int rc = kq::enter(ctx);
+  if (rc) return rc;
+  cudaError_t e = cudaDeviceSynchronize();
+  if (e != cudaSuccess) return cuda_fail(e, "cudaDeviceSynchronize");
+  unsigned word = 0;
+  e = cudaMemcpy(&word, ctx->err, sizeof(word), cudaMemcpyDeviceToHost);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaMemcpy", "device error word");
+  if (word == kq::kErrNone) return KQ_OK;
+  cudaMemset(ctx->err, 0, sizeof(unsigned));
+  const char* what = word == kq::kErrWaitFull    ? "a consumer gave up waiting for a bulk copy"
+                     : word == kq::kErrWaitEmpty ? "the producer gave up waiting for a free slot"
+                     : word == kq::kErrWaitPeer  ? "a wait on another GPU's flag gave up"
+                                                 : "unknown";
+  return fail(KQ_E_DEVICE, "kq_device_error",
+              "device error word " + std::to_string(word) + ": " + what);
+}
+
+static int matvec_simple(kq_ctx* ctx, uint32_t type, uint64_t y, uint64_t w, uint64_t x,
+                         uint32_t rows, uint32_t k, uint32_t batch, kq_stream stream) {
+  if (!ctx) return fail(KQ_E_INVALID, "kq_matvec", "null ctx");
+  kq_matvec_desc d = {};
+  d.type = type;
+  d.rows = rows;
+  d.k = k;
+  d.batch = batch;
+  d.y = y;
+  d.w = w;
+  d.x = x;
+  int rc = kq::enter(ctx);
+  if (rc) return rc;
+  return kq::matvec(ctx, d, static_cast<cudaStream_t>(stream));
+}
+
+int kq_matvec_q4k(kq_ctx* ctx, uint64_t y, uint64_t w, uint64_t x, uint32_t rows, uint32_t k,
+                  uint32_t batch, kq_stream stream) {
+  return matvec_simple(ctx, KQ_TYPE_Q4_K, y, w, x, rows, k, batch, stream);
+}
+
+int kq_matvec_q6k(kq_ctx* ctx, uint64_t y, uint64_t w, uint64_t x, uint32_t rows, uint32_t k,
+                  uint32_t batch, kq_stream stream) {
+  return matvec_simple(ctx, KQ_TYPE_Q6_K, y, w, x, rows, k, batch, stream);
+}
+
+int kq_matvec(kq_ctx* ctx, const kq_matvec_desc* desc, kq_stream stream) {
+  if (!ctx || !desc) return fail(KQ_E_INVALID, "kq_matvec", "null ctx or descriptor");
+  int rc = kq::enter(ctx);
+  if (rc) return rc;
+  return kq::matvec(ctx, *desc, static_cast<cudaStream_t>(stream));
+}
+
+int kq_dequant_q4k(kq_ctx* ctx, uint64_t out, uint64_t w, uint64_t nblocks, kq_stream stream) {
+  if (!ctx) return fail(KQ_E_INVALID, "kq_dequant_q4k", "null ctx");
+  int rc = kq::enter(ctx);
+  if (rc) return rc;
+  return kq::dequant(ctx, 4, out, w, nblocks, static_cast<cudaStream_t>(stream));
+}
+
+int kq_dequant_q6k(kq_ctx* ctx, uint64_t out, uint64_t w, uint64_t nblocks, kq_stream stream) {
+  if (!ctx) return fail(KQ_E_INVALID, "kq_dequant_q6k", "null ctx");
+  int rc = kq::enter(ctx);
+  if (rc) return rc;
+  return kq::dequant(ctx, 6, out, w, nblocks, static_cast<cudaStream_t>(stream));
+}
+
+int kq_fill_q4k(kq_ctx* ctx, uint64_t w, uint64_t block0, uint64_t nblocks, uint64_t key,
+                kq_stream stream) {
+  if (!ctx) return fail(KQ_E_INVALID, "kq_fill_q4k", "null ctx");
+  int rc = kq::enter(ctx);
+  if (rc) return rc;
+  return kq::fill(ctx, 4, w, block0, nblocks, key, static_cast<cudaStream_t>(stream));
+}
+
+int kq_fill_q6k(kq_ctx* ctx, uint64_t w, uint64_t block0, uint64_t nblocks, uint64_t key,
+                kq_stream stream) {
+  if (!ctx) return fail(KQ_E_INVALID, "kq_fill_q6k", "null ctx");
+  int rc = kq::enter(ctx);
+  if (rc) return rc;
+  return kq::fill(ctx, 6, w, block0, nblocks, key, static_cast<cudaStream_t>(stream));
+}
+
+uint64_t kq_stream_key(uint64_t seed, uint64_t tensor) { return kq::stream_key(seed, tensor); }
+
+}  // extern "C"

@@ -1,0 +1,584 @@
+// kq_matvec.cu -- the Q4_K / Q6_K streaming matvec on the CUDA cores, batch 1..8.
+//
+// y[b, r] = sum_k W[r, k] * x[b, k], W in GGML k-quant blocks (144-byte Q4_K, 210-byte Q6_K).
+//
+// Shape of the kernel (one persistent CTA per SM):
+//  * Each CTA owns a contiguous range of rows, i.e. a contiguous byte range of W. A producer
+//    warp streams it, a tile of P rows at a time, into a ring of shared-memory slots with
+//    cp.async.bulk (TMA, 1-D) copies of the 16-byte-aligned superset of each tile; an mbarrier
+//    per slot counts the bytes in. Q6_K rows whose blocks start at any even offset need nothing
+//    special: the consumer reads bytes at the tile's offset from the aligned base.
+//  * The consumer warps form P "teams", one row of the tile each. Within a team every lane owns
+//    a fixed 64/B-weight part of each row (part `pi` of block `kb`), so its slice of x stays in
+//    registers for the whole kernel and shared memory only carries weights.
+//  * A lane turns each 4- or 6-bit quant q into the float 2 + q/64 with one PRMT (q placed in
+//    mantissa bits 16..23 under exponent 2^1; Q4_K's high nibbles sit in bits 8..15, giving
+//    2 + q/1024) and accumulates x * that with packed f32x2 FMAs. The offsets are removed per
+//    sub-block with the lane's own sums of x:  sum q*x = 64*S - 128*X  (or 1024*S - 2048*X).
+//    Q4_K: y += d*(sc_A*sum q*x_A + sc_B*sum q*x_B) - dmin*(m_A*X_A + m_B*X_B).
+//    Q6_K: y += d*sc_g*(sum q*x_g - 32*X_g) per group of 16.
+//  * Lanes reduce by warp shuffles, warps of a team through shared memory, once per tile.
+//
+// The GGML block layouts and the decode follow the public format (see the CPU restatement in
+// oracle/kq_oracle.c); the pattern "one output row per team, FMA chain over k" is the matvec of
+// fxeqxmulfx/kernite's examples/microgpt/src/gpu.rs:100-131, re-shaped for HBM streaming.
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cstdio>
+
+#include "kq_device.cuh"
+#include "kq_internal.h"
+
+namespace kq {
+namespace {
+
+struct MatvecArgs {
+  const uint8_t* W;
+  const float* x;
+  float* y;
+  unsigned* err;
+  uint64_t ldx, ldy;      // floats between vectors
+  uint64_t total_bytes;   // rows * row bytes
+  uint32_t rows, nb, batch;
+  uint32_t team_warps, teams, per_team, ring, slot_bytes;  // tile = teams * per_team rows
+  uint32_t row_unit, prologue, epilogue, flags;
+  float eps, pair_scale;
+};
+
+template <int QT>
+struct Fmt;
+template <>
+struct Fmt<4> {
+  static constexpr int kBlk = kQ4KBytes;
+  static constexpr int kSpan = 128;  // parts per block = kSpan / L
+  static constexpr int kGroups = 2;  // sub-block groups per part (low / high nibbles)
+};
+template <>
+struct Fmt<6> {
+  static constexpr int kBlk = kQ6KBytes;
+  static constexpr int kSpan = 64;
+  static constexpr int kGroups = 4;  // elements l, l+32, l+64, l+96 of a half
+};
+
+// Batch template -> l-values per lane part, and the block size the registers allow.
+template <int B>
+struct Geo {
+  static constexpr int kL4 = B == 1 ? 32 : (B == 2 ? 16 : 8);  // Q4_K
+  static constexpr int kL6 = B == 1 ? 16 : (B == 2 ? 8 : 4);   // Q6_K
+  // 512 threads leave 128 registers a thread; 384 leave 168; 288 (rounded to 384) the same.
+  static constexpr int kMaxThreads = B <= 2 ? 512 : (B == 4 ? 384 : 288);
+};
+
+__device__ __forceinline__ float2 f2(float a, float b) { return make_float2(a, b); }
+
+// quant byte i of `v` (< 128) as the float 2 + q/64
+template <int I>
+__device__ __forceinline__ float prmt_lo(uint32_t v) {
+  return as_f32(__byte_perm(v, 0x40u, 0x4055u | (I << 8)));
+}
+// high-nibble byte i of `v` (16*q) as the float 2 + q/1024
+template <int I>
+__device__ __forceinline__ float prmt_hi(uint32_t v) {
+  return as_f32(__byte_perm(v, 0x40u, 0x4505u | (I << 4)));
+}
+
+template <int QT, int B>
+__global__ void __launch_bounds__(Geo<B>::kMaxThreads, 1) matvec_kernel(const MatvecArgs a) {
+  constexpr int kBlk = Fmt<QT>::kBlk;
+  constexpr int L = QT == 4 ? Geo<B>::kL4 : Geo<B>::kL6;
+  constexpr int PPB = Fmt<QT>::kSpan / L;  // lane parts per block
+  constexpr int G = Fmt<QT>::kGroups;
+  constexpr int W = L / 4;                  // quant words per group per row
+
+  extern __shared__ __align__(128) uint8_t smem[];
+  __shared__ int s_failed;
+  __shared__ float s_norm[32][8];
+
+  const uint32_t RB = a.nb * kBlk;
+  const uint32_t consumers = a.teams * a.team_warps;
+  const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+
+  // The ring starts at the first 128-byte boundary of dynamic shared memory (the host adds
+  // 128 bytes of slack for this).
+  uint8_t* ring = smem + ((128u - (smem_u32(smem) & 127u)) & 127u);
+  float* red = reinterpret_cast<float*>(ring + a.ring * a.slot_bytes);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(red + 2 * consumers * a.per_team * B);
+  const uint32_t ring_s = smem_u32(ring);
+  auto full_bar = [&](uint32_t s) { return smem_u32(&bars[s]); };
+  auto empty_bar = [&](uint32_t s) { return smem_u32(&bars[a.ring + s]); };
+
+  // This CTA's rows, in units of row_unit (pairs for the pair-product epilogue).
+  const uint64_t units = a.rows / a.row_unit;
+  const uint32_t r_begin = static_cast<uint32_t>(units * blockIdx.x / gridDim.x) * a.row_unit;
+  const uint32_t r_end = static_cast<uint32_t>(units * (blockIdx.x + 1) / gridDim.x) * a.row_unit;
+  const uint32_t SR = a.teams * a.per_team;  // rows per tile; row rs0 + u*teams + team
+  const uint32_t ntiles = (r_end - r_begin + SR - 1) / SR;
+
+  if (threadIdx.x == 0) {
+    s_failed = 0;
+    for (uint32_t s = 0; s < a.ring; ++s) {
+      mbar_init(full_bar(s), 1);
+      mbar_init(empty_bar(s), consumers);
+    }
+    fence_mbar_init();
+  }
+  __syncthreads();
+  pdl_launch_dependents();
+
+  // ------------------------------------------------------------------ producer warp
+  if (warp == consumers) {
+    if (lane == 0) {
+      if (!(a.flags & KQ_FLAG_WEIGHTS_STATIC)) pdl_wait();
+      const uint64_t pol = policy_evict_first();
+      const uint64_t end_floor = a.total_bytes & ~uint64_t(15);
+      for (uint32_t t = 0; t < ntiles; ++t) {
+        const uint32_t s = t % a.ring;
+        if (t >= a.ring) {
+          if (s_failed) break;
+          if (!mbar_wait(empty_bar(s), ((t / a.ring) - 1) & 1)) {
+            s_failed = 1;
+            report_error(a.err, kErrWaitEmpty);
+            break;
+          }
+        }
+        const uint32_t rs0 = r_begin + t * SR;
+        const uint32_t rs1 = min(rs0 + SR, r_end);
+        const uint64_t b0 = uint64_t(rs0) * RB, b1 = uint64_t(rs1) * RB;
+        const uint64_t a0 = b0 & ~uint64_t(15);
+        uint64_t a1 = (b1 + 15) & ~uint64_t(15);
+        const uint32_t slot = ring_s + s * a.slot_bytes;
+        if (a1 > end_floor) {
+          // The last tile of W ends off a 16-byte boundary: its last bytes (fewer than 16, an
+          // even count) are read with plain loads, the rest by the bulk copy.
+          for (uint64_t i = end_floor; i < a.total_bytes; i += 2) {
+            const uint16_t v = __ldg(reinterpret_cast<const unsigned short*>(a.W + i));
+            sts_u16(slot + static_cast<uint32_t>(i - a0), v);
+          }
+          a1 = end_floor;
+        }
+        const uint32_t bytes = static_cast<uint32_t>(a1 - a0);
+        mbar_arrive_expect_tx(full_bar(s), bytes);
+        if (bytes) bulk_g2s(slot, a.W + a0, bytes, full_bar(s), pol);
+      }
+    }
+    return;
+  }
+
+  // ------------------------------------------------------------------ consumers
+  const uint32_t team = warp / a.team_warps;
+  const uint32_t tw = warp % a.team_warps;
+  const uint32_t tl = tw * 32 + lane;
+  const bool active = tl < PPB * a.nb;
+  const uint32_t kb = active ? tl / PPB : 0;
+  const uint32_t pi = tl % PPB;
+  // The part's place in its block: Q4_K chunk c (64 weights) or Q6_K half h (128 weights),
+  // and its first l-value.
+  constexpr uint32_t kPartsPerUnit = 32 / L;
+  const uint32_t unit = pi / kPartsPerUnit;           // c (Q4_K) or h (Q6_K)
+  const uint32_t l0 = (pi % kPartsPerUnit) * L;
+  const uint32_t base_off = QT == 4 ? 64 * unit : 128 * unit;  // element offset in the block
+
+  pdl_wait();  // x may be the previous kernel's output
+
+  // x slice in registers: xr[b][g][m] = (x[e], x[e+1]) with e = kb*256 + base_off + 32g + l0 + 2m
+  float2 xr[B][G][L / 2];
+  float xs[B][G];
+#pragma unroll
+  for (int b = 0; b < B; ++b) {
+#pragma unroll
+    for (int g = 0; g < G; ++g) {
+      xs[b][g] = 0.f;
+#pragma unroll
+      for (int m = 0; m < L / 2; ++m) xr[b][g][m] = f2(0.f, 0.f);
+    }
+  }
+  if (active) {
+#pragma unroll
+    for (int b = 0; b < B; ++b) {
+      if (b < static_cast<int>(a.batch)) {
+        const float* xb = a.x + b * a.ldx + uint64_t(kb) * kQK + base_off + l0;
+#pragma unroll
+        for (int g = 0; g < G; ++g) {
+#pragma unroll
+          for (int m = 0; m < L / 4; ++m) {
+            const float4 v = __ldg(reinterpret_cast<const float4*>(xb + 32 * g + 4 * m));
+            xr[b][g][2 * m] = f2(v.x, v.y);
+            xr[b][g][2 * m + 1] = f2(v.z, v.w);
+          }
+        }
+      }
+    }
+  }
+
+  if (a.prologue == KQ_PROLOGUE_RMSNORM) {
+    // Each CTA normalises x by its own full-vector sum of squares (x is L2-resident).
+    const uint32_t nthreads = consumers * 32;
+    const uint32_t K = a.nb * kQK;
+    float ss[B];
+#pragma unroll
+    for (int b = 0; b < B; ++b) {
+      ss[b] = 0.f;
+      if (b < static_cast<int>(a.batch)) {
+        const float* xb = a.x + b * a.ldx;
+        for (uint32_t k = threadIdx.x; k < K; k += nthreads) {
+          const float v = xb[k];
+          ss[b] = fmaf(v, v, ss[b]);
+        }
+      }
+#pragma unroll
+      for (int o = 16; o; o >>= 1) ss[b] += __shfl_xor_sync(0xffffffffu, ss[b], o);
+      if (lane == 0) s_norm[warp][b] = ss[b];
+    }
+    named_barrier(1, nthreads);
+#pragma unroll
+    for (int b = 0; b < B; ++b) {
+      float t = 0.f;
+      for (uint32_t w = 0; w < consumers; ++w) t += s_norm[w][b];
+      const float scale = 1.0f / sqrtf(t / static_cast<float>(K) + a.eps);
+#pragma unroll
+      for (int g = 0; g < G; ++g)
+#pragma unroll
+        for (int m = 0; m < L / 2; ++m) {
+          xr[b][g][m].x *= scale;
+          xr[b][g][m].y *= scale;
+        }
+    }
+  }
+
+  // The lane's sums of x per group, pre-scaled for the offset removal.
+#pragma unroll
+  for (int b = 0; b < B; ++b)
+#pragma unroll
+    for (int g = 0; g < G; ++g) {
+      float t = 0.f;
+#pragma unroll
+      for (int m = 0; m < L / 2; ++m) t += xr[b][g][m].x + xr[b][g][m].y;
+      xs[b][g] = t;
+    }
+
+  // Q4_K scale/min unpack constants for the lane's two sub-blocks j0 = 2c, j1 = 2c+1.
+  const bool upper = unit >= 2;
+  const uint32_t sh0 = 8 * ((2 * unit) & 3), sh1 = 8 * ((2 * unit + 1) & 3);
+
+  for (uint32_t t = 0; t < ntiles; ++t) {
+    const uint32_t s = t % a.ring;
+    if (!s_failed && !mbar_wait(full_bar(s), (t / a.ring) & 1)) {
+      s_failed = 1;
+      report_error(a.err, kErrWaitFull);
+    }
+    const uint32_t rs0 = r_begin + t * SR;
+    const uint32_t rs1 = min(rs0 + SR, r_end);
+    const uint32_t delta = static_cast<uint32_t>((uint64_t(rs0) * RB) & 15);
+    float* rbuf = red + (t & 1) * consumers * a.per_team * B;
+    for (uint32_t u = 0; u < a.per_team; ++u) {
+    const uint32_t rho = u * a.teams + team;  // row within the tile
+    const uint32_t row = rs0 + rho;
+    float acc[B];
+#pragma unroll
+    for (int b = 0; b < B; ++b) acc[b] = 0.f;
+
+    if (active && row < rs1 && !s_failed) {
+      const uint32_t blk = ring_s + s * a.slot_bytes + delta + rho * RB + kb * kBlk;
+      if constexpr (QT == 4) {
+        const uint4 hdr = lds_v4(blk);
+        uint32_t q[W];
+        if constexpr (W == 8) {
+          const uint4 q0 = lds_v4(blk + 16 + 32 * unit + l0);
+          const uint4 q1 = lds_v4(blk + 32 + 32 * unit + l0);
+          q[0] = q0.x; q[1] = q0.y; q[2] = q0.z; q[3] = q0.w;
+          q[4] = q1.x; q[5] = q1.y; q[6] = q1.z; q[7] = q1.w;
+        } else if constexpr (W == 4) {
+          const uint4 q0 = lds_v4(blk + 16 + 32 * unit + l0);
+          q[0] = q0.x; q[1] = q0.y; q[2] = q0.z; q[3] = q0.w;
+        } else {
+          const uint2 q0 = lds_v2(blk + 16 + 32 * unit + l0);
+          q[0] = q0.x; q[1] = q0.y;
+        }
+        float2 sa[B], sb[B];
+#pragma unroll
+        for (int b = 0; b < B; ++b) { sa[b] = f2(0.f, 0.f); sb[b] = f2(0.f, 0.f); }
+#pragma unroll
+        for (int w = 0; w < W; ++w) {
+          const uint32_t lo = q[w] & 0x0F0F0F0Fu, hi = q[w] & 0xF0F0F0F0u;
+          const float2 fa = f2(prmt_lo<0>(lo), prmt_lo<1>(lo));
+          const float2 fb = f2(prmt_lo<2>(lo), prmt_lo<3>(lo));
+          const float2 ga = f2(prmt_hi<0>(hi), prmt_hi<1>(hi));
+          const float2 gb = f2(prmt_hi<2>(hi), prmt_hi<3>(hi));
+#pragma unroll
+          for (int b = 0; b < B; ++b) {
+            sa[b] = __ffma2_rn(xr[b][0][2 * w], fa, sa[b]);
+            sa[b] = __ffma2_rn(xr[b][0][2 * w + 1], fb, sa[b]);
+            sb[b] = __ffma2_rn(xr[b][1][2 * w], ga, sb[b]);
+            sb[b] = __ffma2_rn(xr[b][1][2 * w + 1], gb, sb[b]);
+          }
+        }
+        // scales and mins of sub-blocks 2c and 2c+1
+        uint32_t sc0, m0, sc1, m1;
+        if (!upper) {
+          sc0 = (hdr.y >> sh0) & 63u; m0 = (hdr.z >> sh0) & 63u;
+          sc1 = (hdr.y >> sh1) & 63u; m1 = (hdr.z >> sh1) & 63u;
+        } else {
+          sc0 = ((hdr.w >> sh0) & 15u) | (((hdr.y >> (sh0 + 6)) & 3u) << 4);
+          m0 = ((hdr.w >> (sh0 + 4)) & 15u) | (((hdr.z >> (sh0 + 6)) & 3u) << 4);
+          sc1 = ((hdr.w >> sh1) & 15u) | (((hdr.y >> (sh1 + 6)) & 3u) << 4);
+          m1 = ((hdr.w >> (sh1 + 4)) & 15u) | (((hdr.z >> (sh1 + 6)) & 3u) << 4);
+        }
+        const float d = h2f(hdr.x & 0xffffu), dmin = h2f(hdr.x >> 16);
+        const float fsc0 = static_cast<float>(sc0), fsc1 = static_cast<float>(sc1);
+        const float fm0 = static_cast<float>(m0), fm1 = static_cast<float>(m1);
+#pragma unroll
+        for (int b = 0; b < B; ++b) {
+          const float qa = fmaf(64.f, sa[b].x + sa[b].y, -128.f * xs[b][0]);
+          const float qb = fmaf(1024.f, sb[b].x + sb[b].y, -2048.f * xs[b][1]);
+          const float pos = fmaf(fsc0, qa, fsc1 * qb);
+          const float neg = fmaf(fm0, xs[b][0], fm1 * xs[b][1]);
+          acc[b] = fmaf(d, pos, -dmin * neg);
+        }
+      } else {
+        uint32_t qa[W], qb[W], qh[W];
+        lds_words_unaligned<W>(blk + 64 * unit + l0, qa);
+        lds_words_unaligned<W>(blk + 64 * unit + 32 + l0, qb);
+        lds_words_unaligned<W>(blk + 128 + 32 * unit + l0, qh);
+        const uint32_t sbase = blk + 192 + 8 * unit + (l0 >> 4);
+        float fsc[4];
+#pragma unroll
+        for (int g = 0; g < 4; ++g) fsc[g] = static_cast<float>(lds_s8(sbase + 2 * g));
+        const float d = h2f(lds_u16(blk + 208));
+        float2 sg[B][4];
+#pragma unroll
+        for (int b = 0; b < B; ++b)
+#pragma unroll
+          for (int g = 0; g < 4; ++g) sg[b][g] = f2(0.f, 0.f);
+#pragma unroll
+        for (int w = 0; w < W; ++w) {
+          uint32_t qg[4];
+          qg[0] = (qa[w] & 0x0F0F0F0Fu) | ((qh[w] << 4) & 0x30303030u);
+          qg[1] = (qb[w] & 0x0F0F0F0Fu) | ((qh[w] << 2) & 0x30303030u);
+          qg[2] = ((qa[w] >> 4) & 0x0F0F0F0Fu) | (qh[w] & 0x30303030u);
+          qg[3] = ((qb[w] >> 4) & 0x0F0F0F0Fu) | ((qh[w] >> 2) & 0x30303030u);
+#pragma unroll
+          for (int g = 0; g < 4; ++g) {
+            const float2 f01 = f2(prmt_lo<0>(qg[g]), prmt_lo<1>(qg[g]));
+            const float2 f23 = f2(prmt_lo<2>(qg[g]), prmt_lo<3>(qg[g]));
+#pragma unroll
+            for (int b = 0; b < B; ++b) {
+              sg[b][g] = __ffma2_rn(xr[b][g][2 * w], f01, sg[b][g]);
+              sg[b][g] = __ffma2_rn(xr[b][g][2 * w + 1], f23, sg[b][g]);
+            }
+          }
+        }
+#pragma unroll
+        for (int b = 0; b < B; ++b) {
+          float t = 0.f;
+#pragma unroll
+          for (int g = 0; g < 4; ++g) {
+            // sum (q - 32) x = 64 S - 128 X - 32 X
+            const float qx = fmaf(64.f, sg[b][g].x + sg[b][g].y, -160.f * xs[b][g]);
+            t = fmaf(fsc[g], qx, t);
+          }
+          acc[b] = d * t;
+        }
+      }
+    }
+
+    // lanes -> warp
+#pragma unroll
+    for (int b = 0; b < B; ++b) {
+#pragma unroll
+      for (int o = 16; o; o >>= 1) acc[b] += __shfl_xor_sync(0xffffffffu, acc[b], o);
+    }
+    if (lane == 0) {
+#pragma unroll
+      for (int b = 0; b < B; ++b) rbuf[(u * consumers + warp) * B + b] = acc[b];
+    }
+    }  // rows of this team in the tile
+    __syncwarp();
+    if (lane == 0) mbar_arrive(empty_bar(s));  // this warp is done reading slot s
+    named_barrier(1, consumers * 32);
+
+    // warps of a team -> row; then the epilogue. Row rho of the tile is team rho % teams,
+    // pass rho / teams; its warps' partials sit at rbuf[((rho / teams) * consumers + team *
+    // team_warps + w) * B + b].
+    auto row_sum = [&](uint32_t rho, uint32_t b) {
+      const uint32_t base = (rho / a.teams) * consumers + (rho % a.teams) * a.team_warps;
+      float v = 0.f;
+      for (uint32_t w = 0; w < a.team_warps; ++w) v += rbuf[(base + w) * B + b];
+      return v;
+    };
+    const uint32_t nthreads = consumers * 32;
+    if (a.epilogue == KQ_EPILOGUE_PAIR_PRODUCT) {
+      for (uint32_t o = threadIdx.x; o < (SR / 2) * B; o += nthreads) {
+        const uint32_t i = o / B, b = o % B;
+        const uint32_t r = rs0 + 2 * i;
+        if (r < rs1 && b < a.batch)
+          a.y[b * a.ldy + r / 2] = row_sum(2 * i, b) * row_sum(2 * i + 1, b) * a.pair_scale;
+      }
+    } else {
+      for (uint32_t o = threadIdx.x; o < SR * B; o += nthreads) {
+        const uint32_t rho = o / B, b = o % B;
+        const uint32_t r = rs0 + rho;
+        if (r < rs1 && b < a.batch) a.y[b * a.ldy + r] = row_sum(rho, b);
+      }
+    }
+  }
+}
+
+struct Instance {
+  const void* fn;
+  int max_threads;
+  int l4, l6;
+};
+
+template <int QT, int B>
+Instance instance() {
+  return Instance{reinterpret_cast<const void*>(&matvec_kernel<QT, B>), Geo<B>::kMaxThreads,
+                  Geo<B>::kL4, Geo<B>::kL6};
+}
+
+Instance pick(int qt, int bt) {
+  if (qt == 4) {
+    switch (bt) {
+      case 1: return instance<4, 1>();
+      case 2: return instance<4, 2>();
+      case 4: return instance<4, 4>();
+      default: return instance<4, 8>();
+    }
+  }
+  switch (bt) {
+    case 1: return instance<6, 1>();
+    case 2: return instance<6, 2>();
+    case 4: return instance<6, 4>();
+    default: return instance<6, 8>();
+  }
+}
+
+constexpr uint32_t kRingBudget = 160 * 1024;  // bytes of ring per CTA we aim for
+constexpr uint64_t kTileTarget = 24 * 1024;   // bytes per tile we aim for
+
+}  // namespace
+
+int matvec_prepare(kq_ctx* ctx) {
+  for (int qt : {4, 6})
+    for (int bt : {1, 2, 4, 8}) {
+      const Instance in = pick(qt, bt);
+      cudaError_t e = cudaFuncSetAttribute(in.fn, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                           ctx->max_smem);
+      if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute", "matvec kernel");
+    }
+  return KQ_OK;
+}
+
+int matvec(kq_ctx* ctx, const kq_matvec_desc& d, cudaStream_t stream) {
+  const char* call = "kq_matvec";
+  int qt;
+  if (d.type == KQ_TYPE_Q4_K)
+    qt = 4;
+  else if (d.type == KQ_TYPE_Q6_K)
+    qt = 6;
+  else
+    return fail(KQ_E_INVALID, call, "type must be KQ_TYPE_Q4_K (12) or KQ_TYPE_Q6_K (14)");
+  if (d.rows == 0 || d.k == 0 || d.k % kQK != 0)
+    return fail(KQ_E_INVALID, call,
+                "rows must be > 0 and k a positive multiple of 256 (rows " +
+                    std::to_string(d.rows) + ", k " + std::to_string(d.k) + ")");
+  if (d.batch < 1 || d.batch > 8)
+    return fail(KQ_E_INVALID, call, "batch must be 1..8 (got " + std::to_string(d.batch) + ")");
+  if (!d.w || !d.x || !d.y) return fail(KQ_E_INVALID, call, "null pointer");
+  if (d.w % 16 || d.x % 16 || d.y % 4)
+    return fail(KQ_E_INVALID, call, "w and x must be 16-byte aligned, y 4-byte aligned");
+  if (d.prologue > KQ_PROLOGUE_RMSNORM || d.epilogue > KQ_EPILOGUE_PAIR_PRODUCT)
+    return fail(KQ_E_INVALID, call, "unknown prologue or epilogue");
+  const bool pair = d.epilogue == KQ_EPILOGUE_PAIR_PRODUCT;
+  if (pair && d.rows % 2) return fail(KQ_E_INVALID, call, "pair product needs an even row count");
+  const uint64_t ldx = d.ldx ? d.ldx : d.k;
+  const uint64_t out_rows = pair ? d.rows / 2 : d.rows;
+  const uint64_t ldy = d.ldy ? d.ldy : out_rows;
+  if (ldx < d.k || ldx % 4) return fail(KQ_E_INVALID, call, "ldx must be >= k and a multiple of 4");
+  if (ldy < out_rows) return fail(KQ_E_INVALID, call, "ldy must be >= the output rows");
+
+  const int bt = d.batch == 1 ? 1 : d.batch == 2 ? 2 : d.batch <= 4 ? 4 : 8;
+  const Instance in = pick(qt, bt);
+  const int L = qt == 4 ? in.l4 : in.l6;
+  const uint32_t blk = qt == 4 ? kQ4KBytes : kQ6KBytes;
+  const uint32_t ppb = (qt == 4 ? 128 : 64) / L;
+  const uint32_t nb = d.k / kQK;
+  const uint32_t team_lanes = ppb * nb;
+  const uint32_t team_warps = (team_lanes + 31) / 32;
+  const uint32_t max_consumers = in.max_threads / 32 - 1;
+  if (team_warps > max_consumers)
+    return fail(KQ_E_UNSUPPORTED, call,
+                "k " + std::to_string(d.k) + " is past this build's limit for batch " +
+                    std::to_string(d.batch) + " (" + std::to_string(max_consumers * 32 / ppb * kQK) +
+                    ")");
+  uint32_t pmax = max_consumers / team_warps;
+  if (pair) pmax &= ~1u;
+  if (pmax == 0) return fail(KQ_E_UNSUPPORTED, call, "k too large for the pair-product epilogue");
+
+  const uint32_t row_unit = pair ? 2 : 1;
+  const uint64_t units = d.rows / row_unit;
+  const uint32_t grid = static_cast<uint32_t>(std::min<uint64_t>(ctx->sm_count, units));
+  const uint64_t rows_per_cta = ((units + grid - 1) / grid) * row_unit;
+  // Teams: as many as fit, trimmed so that the CTA's rows split evenly over its tiles.
+  const uint64_t rounds = (rows_per_cta + pmax - 1) / pmax;
+  uint32_t P = static_cast<uint32_t>((rows_per_cta + rounds - 1) / rounds);
+  if (pair) P += P & 1;
+  const uint64_t rb = uint64_t(nb) * blk;
+  // Rows per team per tile: tiles of about kTileTarget bytes, no more rows than the CTA has.
+  uint32_t U = static_cast<uint32_t>(std::max<uint64_t>(1, kTileTarget / (uint64_t(P) * rb)));
+  U = static_cast<uint32_t>(std::min<uint64_t>(U, (rows_per_cta + P - 1) / P));
+  if (pair && (P * U) % 2) ++U;
+  const uint32_t slot = static_cast<uint32_t>(((uint64_t(P) * U * rb + 32 + 127) / 128) * 128);
+  const uint32_t consumers = P * team_warps;
+  const uint32_t red_bytes = 2 * consumers * U * bt * 4;
+  const uint32_t fixed = red_bytes + 2 * 8 * 8 + 128;
+  uint32_t ring = std::min<uint32_t>(8, std::max<uint32_t>(2, kRingBudget / slot));
+  while (ring > 2 && ring * slot + fixed > static_cast<uint32_t>(ctx->max_smem)) --ring;
+  const uint32_t smem = ring * slot + fixed;
+  if (smem > static_cast<uint32_t>(ctx->max_smem))
+    return fail(KQ_E_UNSUPPORTED, call, "row tile does not fit in shared memory (k too large)");
+
+  MatvecArgs args;
+  args.W = reinterpret_cast<const uint8_t*>(d.w);
+  args.x = reinterpret_cast<const float*>(d.x);
+  args.y = reinterpret_cast<float*>(d.y);
+  args.err = ctx->err;
+  args.ldx = ldx;
+  args.ldy = ldy;
+  args.total_bytes = uint64_t(d.rows) * rb;
+  args.rows = d.rows;
+  args.nb = nb;
+  args.batch = d.batch;
+  args.team_warps = team_warps;
+  args.teams = P;
+  args.per_team = U;
+  args.ring = ring;
+  args.slot_bytes = slot;
+  args.row_unit = row_unit;
+  args.prologue = d.prologue;
+  args.epilogue = d.epilogue;
+  args.flags = d.flags;
+  args.eps = d.eps;
+  args.pair_scale = d.pair_scale;
+
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3((consumers + 1) * 32);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = (d.flags & KQ_FLAG_NO_PDL) ? 0 : 1;
+  void* params[] = {&args};
+  cudaError_t e = cudaLaunchKernelExC(&cfg, in.fn, params);
+  if (e != cudaSuccess)
+    return cuda_fail(e, "cudaLaunchKernelExC",
+                     "matvec grid " + std::to_string(grid) + " x " +
+                         std::to_string((consumers + 1) * 32) + " threads, " +
+                         std::to_string(smem) + " B shared");
+  return KQ_OK;
+}
+
+}  // namespace kq

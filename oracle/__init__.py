@@ -1,0 +1,177 @@
+"""ctypes binding of the CPU oracle (kq_oracle.c) and the CPU baseline (kq_cpu.c).
+
+TEST INFRASTRUCTURE ONLY. Only tests/, ``__graft_entry__.smoke()`` and bench.py's CPU-baseline
+leg import this module, as the checker or as the timed CPU baseline; the product path
+(``kernite_b200``, ``libkq.so``) never does.
+
+The k-quant path does not exist in fxeqxmulfx/kernite. The oracle restates the GGML k-quant
+format; it is pinned against gguf-py 0.19.0's numpy dequantizer (``gguf/quants.py``,
+``Q4_K.dequantize_blocks`` / ``Q6_K.dequantize_blocks``) through the fixtures in
+``tests/golden/``, and its fp16 decode against kernite's table in
+``crates/cuda/src/half.rs:165-180``.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+import subprocess
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "liboracle.so")
+
+Q4K_BYTES = 144
+Q6K_BYTES = 210
+QK = 256
+
+_lib = None
+
+
+def build(force: bool = False) -> str:
+    """Compile oracle/liboracle.so with make (gcc). Returns the library path."""
+    if force or not os.path.exists(LIB_PATH):
+        subprocess.run(["make", "-C", HERE, "-s"], check=True)
+    return LIB_PATH
+
+
+def lib() -> ctypes.CDLL:
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIB_PATH):
+            build()
+        L = ctypes.CDLL(LIB_PATH)
+        u8p = ctypes.POINTER(ctypes.c_uint8)
+        f32p = ctypes.POINTER(ctypes.c_float)
+        f64p = ctypes.POINTER(ctypes.c_double)
+        L.kqo_fp16_to_f32.argtypes = [ctypes.c_uint16]
+        L.kqo_fp16_to_f32.restype = ctypes.c_float
+        L.kqo_f32_to_fp16.argtypes = [ctypes.c_float]
+        L.kqo_f32_to_fp16.restype = ctypes.c_uint16
+        L.kqo_q4k_scale_min.argtypes = [u8p, ctypes.c_int, u8p, u8p]
+        L.kqo_q4k_scale_min.restype = None
+        for name in ("kqo_dequant_q4k", "kqo_dequant_q6k"):
+            fn = getattr(L, name)
+            fn.argtypes = [u8p, ctypes.c_size_t, f32p]
+            fn.restype = None
+        L.kqo_matvec_ref.argtypes = [
+            ctypes.c_int, u8p, f32p, ctypes.c_uint32, ctypes.c_uint32, ctypes.c_uint32,
+            ctypes.c_uint32, ctypes.c_uint64, ctypes.c_uint64, f64p, f64p,
+        ]
+        L.kqo_matvec_ref.restype = None
+        for name in ("kqo_fill_q4k", "kqo_fill_q6k"):
+            fn = getattr(L, name)
+            fn.argtypes = [u8p, ctypes.c_uint64, ctypes.c_uint64, ctypes.c_uint64]
+            fn.restype = None
+        L.kqo_stream_key.argtypes = [ctypes.c_uint64, ctypes.c_uint64]
+        L.kqo_stream_key.restype = ctypes.c_uint64
+        L.kqo_splitmix_at.argtypes = [ctypes.c_uint64, ctypes.c_uint64]
+        L.kqo_splitmix_at.restype = ctypes.c_uint64
+        L.kqo_matvec_cpu.argtypes = [
+            ctypes.c_int, u8p, f32p, ctypes.c_uint32, ctypes.c_uint32, ctypes.c_uint32, f32p,
+            ctypes.c_int,
+        ]
+        L.kqo_matvec_cpu.restype = ctypes.c_int
+        _lib = L
+    return _lib
+
+
+def _u8(a: np.ndarray):
+    assert a.dtype == np.uint8 and a.flags.c_contiguous
+    return a.ctypes.data_as(ctypes.POINTER(ctypes.c_uint8))
+
+
+def _f32(a: np.ndarray):
+    assert a.dtype == np.float32 and a.flags.c_contiguous
+    return a.ctypes.data_as(ctypes.POINTER(ctypes.c_float))
+
+
+def _f64(a: np.ndarray):
+    assert a.dtype == np.float64 and a.flags.c_contiguous
+    return a.ctypes.data_as(ctypes.POINTER(ctypes.c_double))
+
+
+def block_bytes(qtype: int) -> int:
+    return {4: Q4K_BYTES, 6: Q6K_BYTES}[qtype]
+
+
+def fp16_to_f32(h: int) -> float:
+    return lib().kqo_fp16_to_f32(h)
+
+
+def f32_to_fp16(x: float) -> int:
+    return lib().kqo_f32_to_fp16(x)
+
+
+def q4k_scale_min(scales12: bytes, j: int) -> tuple[int, int]:
+    buf = np.frombuffer(bytes(scales12), dtype=np.uint8).copy()
+    sc = ctypes.c_uint8()
+    m = ctypes.c_uint8()
+    lib().kqo_q4k_scale_min(_u8(buf), j, ctypes.byref(sc), ctypes.byref(m))
+    return sc.value, m.value
+
+
+def dequant(qtype: int, blocks: np.ndarray) -> np.ndarray:
+    """Dequantise raw block bytes (uint8, n*BLK) into n*256 float32, canonical order."""
+    blocks = np.ascontiguousarray(blocks, dtype=np.uint8).reshape(-1)
+    n = blocks.size // block_bytes(qtype)
+    assert n * block_bytes(qtype) == blocks.size
+    out = np.empty(n * QK, dtype=np.float32)
+    fn = lib().kqo_dequant_q4k if qtype == 4 else lib().kqo_dequant_q6k
+    fn(_u8(blocks), n, _f32(out))
+    return out
+
+
+def stream_key(seed: int, tensor: int) -> int:
+    return lib().kqo_stream_key(seed & (2**64 - 1), tensor & (2**64 - 1))
+
+
+def splitmix_at(key: int, i: int) -> int:
+    return lib().kqo_splitmix_at(key, i)
+
+
+def fill(qtype: int, key: int, b0: int, n: int) -> np.ndarray:
+    """Blocks [b0, b0+n) of the synthetic tensor with stream key `key`, as raw bytes."""
+    out = np.empty(n * block_bytes(qtype), dtype=np.uint8)
+    fn = lib().kqo_fill_q4k if qtype == 4 else lib().kqo_fill_q6k
+    fn(_u8(out), key, b0, n)
+    return out
+
+
+def matvec_ref(qtype: int, W: np.ndarray, x: np.ndarray, K: int, r0: int, r1: int):
+    """Reference y and bound (f64) for rows [r0, r1) of W (raw bytes holding all rows from 0)
+    against x of shape (batch, K). Returns arrays of shape (batch, r1 - r0)."""
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    if x.ndim == 1:
+        x = x[None, :]
+    batch = x.shape[0]
+    assert x.shape[1] == K
+    W = np.ascontiguousarray(W, dtype=np.uint8).reshape(-1)
+    rows_alloc = r1  # outputs indexed by absolute row
+    y = np.zeros(batch * rows_alloc, dtype=np.float64)
+    bound = np.zeros(batch * rows_alloc, dtype=np.float64)
+    lib().kqo_matvec_ref(qtype, _u8(W), _f32(x), K, r0, r1, batch, K, rows_alloc, _f64(y), _f64(bound))
+    y = y.reshape(batch, rows_alloc)[:, r0:r1]
+    bound = bound.reshape(batch, rows_alloc)[:, r0:r1]
+    return y, bound
+
+
+def matvec_cpu(qtype: int, W: np.ndarray, x: np.ndarray, rows: int, K: int, threads: int = 1) -> np.ndarray:
+    """The AVX2 CPU baseline: y of shape (batch, rows), f32."""
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    if x.ndim == 1:
+        x = x[None, :]
+    batch = x.shape[0]
+    y = np.empty(batch * rows, dtype=np.float32)
+    rc = lib().kqo_matvec_cpu(qtype, _u8(np.ascontiguousarray(W).reshape(-1)), _f32(x), rows, K, batch, _f32(y), threads)
+    if rc != 0:
+        raise ValueError(f"kqo_matvec_cpu failed: {rc}")
+    return y.reshape(batch, rows)
+
+
+def cpu_threads() -> int:
+    """Host threads available to this process (the CPU baseline uses all of them)."""
+    try:
+        return len(os.sched_getaffinity(0))
+    except AttributeError:  # pragma: no cover
+        return os.cpu_count() or 1

@@ -1,0 +1,74 @@
+"""The C-ABI library loads and exports every entry point include/kq.h declares. No compute: these
+run without a GPU."""
+import ctypes
+import os
+import re
+import subprocess
+
+import oracle
+
+import kernite_b200 as kb
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def header_functions() -> set[str]:
+    names = set()
+    for fn in sorted(os.listdir(os.path.join(ROOT, "include"))):
+        if fn.endswith(".h"):
+            text = open(os.path.join(ROOT, "include", fn)).read()
+            text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+            names |= set(re.findall(r"\b(kq_[a-z0-9_]+)\s*\(", text))
+    return names
+
+
+def test_library_exports_every_declared_symbol():
+    L = kb.lib()
+    declared = header_functions()
+    assert declared, "no declarations found in include/"
+    missing = [n for n in sorted(declared) if not hasattr(L, n)]
+    assert not missing, missing
+
+
+def test_python_binding_lists_every_declared_symbol():
+    assert header_functions() == set(kb.EXPORTS)
+
+
+def test_stream_key_matches_oracle():
+    for seed, t in [(0, 0), (1234, 7), (2**63 + 5, 99)]:
+        assert kb.stream_key(seed, t) == oracle.stream_key(seed, t)
+
+
+def test_last_error_is_a_string():
+    assert isinstance(kb.last_error(), str)
+
+
+def test_ctx_create_rejects_null_out():
+    L = kb.lib()
+    rc = L.kq_ctx_create(0, None)
+    assert rc == kb.KQ_E_INVALID
+    assert "kq_ctx_create" in kb.last_error()
+
+
+def test_entry_points_reject_null_ctx():
+    L = kb.lib()
+    assert L.kq_matvec_q4k(None, 0, 0, 0, 1, 256, 1, None) == kb.KQ_E_INVALID
+    assert L.kq_dequant_q6k(None, 0, 0, 1, None) == kb.KQ_E_INVALID
+    assert L.kq_fill_q4k(None, 0, 0, 1, 0, None) == kb.KQ_E_INVALID
+    d = kb.KqMatvecDesc()
+    assert L.kq_matvec(None, ctypes.byref(d), None) == kb.KQ_E_INVALID
+
+
+def test_desc_layout_matches_header(tmp_path):
+    # the C compiler's layout of kq_matvec_desc against the ctypes mirror
+    src = tmp_path / "layout.c"
+    src.write_text(
+        '#include <stdio.h>\n#include <stddef.h>\n#include "kq.h"\n'
+        'int main(void){printf("%zu %zu %zu %zu %zu\\n", sizeof(kq_matvec_desc),'
+        ' offsetof(kq_matvec_desc, y), offsetof(kq_matvec_desc, prologue),'
+        ' offsetof(kq_matvec_desc, eps), offsetof(kq_matvec_desc, flags));return 0;}\n')
+    exe = tmp_path / "layout"
+    subprocess.run(["gcc", "-I", os.path.join(ROOT, "include"), str(src), "-o", str(exe)], check=True)
+    got = [int(v) for v in subprocess.run([str(exe)], capture_output=True, text=True, check=True).stdout.split()]
+    D = kb.KqMatvecDesc
+    assert got == [ctypes.sizeof(D), D.y.offset, D.prologue.offset, D.eps.offset, D.flags.offset]
