@@ -153,15 +153,35 @@ __device__ __forceinline__ void sts_u16(uint32_t addr, uint16_t v) {
   asm volatile("st.shared.u16 [%0], %1;" ::"r"(addr), "h"(v) : "memory");
 }
 
+template <int OFF>
+__device__ __forceinline__ uint32_t lds_u32_at(uint32_t base) {
+  uint32_t v;
+  asm volatile("ld.shared.u32 %0, [%1+%2];" : "=r"(v) : "r"(base), "n"(OFF));
+  return v;
+}
+
+template <int I, int N>
+struct UnalignedWords {
+  __device__ __forceinline__ static void load(uint32_t base, uint32_t (&w)[N + 1]) {
+    w[I] = lds_u32_at<4 * I>(base);
+    UnalignedWords<I + 1, N>::load(base, w);
+  }
+};
+template <int N>
+struct UnalignedWords<N, N> {
+  __device__ __forceinline__ static void load(uint32_t base, uint32_t (&w)[N + 1]) {
+    w[N] = lds_u32_at<4 * N>(base);
+  }
+};
+
 // `N` 32-bit words starting at shared address `addr`, which is only 2-byte aligned: N+1 aligned
-// loads and a funnel shift per word.
+// loads (immediate offsets from one base) and a funnel shift per word.
 template <int N>
 __device__ __forceinline__ void lds_words_unaligned(uint32_t addr, uint32_t (&out)[N]) {
   const uint32_t base = addr & ~3u;
   const uint32_t sh = (addr & 3u) * 8u;
   uint32_t w[N + 1];
-#pragma unroll
-  for (int i = 0; i <= N; ++i) w[i] = lds_u32(base + 4u * i);
+  UnalignedWords<0, N>::load(base, w);
 #pragma unroll
   for (int i = 0; i < N; ++i) out[i] = __funnelshift_r(w[i], w[i + 1], sh);
 }

@@ -30,6 +30,11 @@
 #include "kq_device.cuh"
 #include "kq_internal.h"
 
+// 1: accumulate with packed f32x2 FMAs (two weights an instruction); 0: scalar FMAs.
+#ifndef KQ_PACKED_FMA
+#define KQ_PACKED_FMA 1
+#endif
+
 namespace kq {
 namespace {
 
@@ -132,11 +137,11 @@ __global__ void __launch_bounds__(Geo<B>::kMaxThreads, 1) matvec_kernel(const Ma
       if (!(a.flags & KQ_FLAG_WEIGHTS_STATIC)) pdl_wait();
       const uint64_t pol = policy_evict_first();
       const uint64_t end_floor = a.total_bytes & ~uint64_t(15);
-      for (uint32_t t = 0; t < ntiles; ++t) {
-        const uint32_t s = t % a.ring;
+      uint32_t s = 0, phase = 0;  // slot and the parity of its current use
+      for (uint32_t t = 0; t < ntiles; ++t, s = (s + 1 == a.ring) ? 0 : s + 1, phase ^= (s == 0)) {
         if (t >= a.ring) {
           if (s_failed) break;
-          if (!mbar_wait(empty_bar(s), ((t / a.ring) - 1) & 1)) {
+          if (!mbar_wait(empty_bar(s), phase ^ 1)) {
             s_failed = 1;
             report_error(a.err, kErrWaitEmpty);
             break;
@@ -181,18 +186,16 @@ __global__ void __launch_bounds__(Geo<B>::kMaxThreads, 1) matvec_kernel(const Ma
 
   pdl_wait();  // x may be the previous kernel's output
 
-  // x slice in registers: xr[b][g][m] = (x[e], x[e+1]) with e = kb*256 + base_off + 32g + l0 + 2m
+  // x slice in registers, in pairs: xr[b][g][m] = x[b, e], x[b, e+1] with
+  // e = kb*256 + base_off + 32g + l0 + 2m
   float2 xr[B][G][L / 2];
   float xs[B][G];
 #pragma unroll
-  for (int b = 0; b < B; ++b) {
+  for (int b = 0; b < B; ++b)
 #pragma unroll
-    for (int g = 0; g < G; ++g) {
-      xs[b][g] = 0.f;
+    for (int g = 0; g < G; ++g)
 #pragma unroll
       for (int m = 0; m < L / 2; ++m) xr[b][g][m] = f2(0.f, 0.f);
-    }
-  }
   if (active) {
 #pragma unroll
     for (int b = 0; b < B; ++b) {
@@ -215,20 +218,16 @@ __global__ void __launch_bounds__(Geo<B>::kMaxThreads, 1) matvec_kernel(const Ma
     // Each CTA normalises x by its own full-vector sum of squares (x is L2-resident).
     const uint32_t nthreads = consumers * 32;
     const uint32_t K = a.nb * kQK;
-    float ss[B];
 #pragma unroll
     for (int b = 0; b < B; ++b) {
-      ss[b] = 0.f;
+      float ss = 0.f;
       if (b < static_cast<int>(a.batch)) {
         const float* xb = a.x + b * a.ldx;
-        for (uint32_t k = threadIdx.x; k < K; k += nthreads) {
-          const float v = xb[k];
-          ss[b] = fmaf(v, v, ss[b]);
-        }
+        for (uint32_t k = threadIdx.x; k < K; k += nthreads) ss = fmaf(xb[k], xb[k], ss);
       }
 #pragma unroll
-      for (int o = 16; o; o >>= 1) ss[b] += __shfl_xor_sync(0xffffffffu, ss[b], o);
-      if (lane == 0) s_norm[warp][b] = ss[b];
+      for (int o = 16; o; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+      if (lane == 0) s_norm[warp][b] = ss;
     }
     named_barrier(1, nthreads);
 #pragma unroll
@@ -244,9 +243,10 @@ __global__ void __launch_bounds__(Geo<B>::kMaxThreads, 1) matvec_kernel(const Ma
           xr[b][g][m].y *= scale;
         }
     }
+    named_barrier(1, nthreads);  // s_norm is read by all before anyone reuses shared memory
   }
 
-  // The lane's sums of x per group, pre-scaled for the offset removal.
+  // The lane's sums of x per group, for the offset removal.
 #pragma unroll
   for (int b = 0; b < B; ++b)
 #pragma unroll
@@ -261,164 +261,254 @@ __global__ void __launch_bounds__(Geo<B>::kMaxThreads, 1) matvec_kernel(const Ma
   const bool upper = unit >= 2;
   const uint32_t sh0 = 8 * ((2 * unit) & 3), sh1 = 8 * ((2 * unit + 1) & 3);
 
+  // Rows: a tile holds teams * per_team rows; this team takes row_unit consecutive rows per
+  // round, so the two rows of a pair-product stay in one team.
+  const uint32_t R = a.row_unit;
+  float* tbuf = red + team * (2u * a.team_warps * a.per_team * B);
+  float held[B];
+#pragma unroll
+  for (int b = 0; b < B; ++b) held[b] = 0.f;
+
+  const uint32_t rounds = a.per_team / R;     // rounds of R rows per tile for this team
+  const uint32_t round_stride = a.teams * R;  // rows between a team's rounds
+  uint32_t s = 0, phase = 0;                  // ring slot and the parity of its current use
   for (uint32_t t = 0; t < ntiles; ++t) {
-    const uint32_t s = t % a.ring;
-    if (!s_failed && !mbar_wait(full_bar(s), (t / a.ring) & 1)) {
+    if (!s_failed && !mbar_wait(full_bar(s), phase)) {
       s_failed = 1;
       report_error(a.err, kErrWaitFull);
     }
+    const bool failed = s_failed != 0;
     const uint32_t rs0 = r_begin + t * SR;
     const uint32_t rs1 = min(rs0 + SR, r_end);
     const uint32_t delta = static_cast<uint32_t>((uint64_t(rs0) * RB) & 15);
-    float* rbuf = red + (t & 1) * consumers * a.per_team * B;
-    for (uint32_t u = 0; u < a.per_team; ++u) {
-    const uint32_t rho = u * a.teams + team;  // row within the tile
-    const uint32_t row = rs0 + rho;
-    float acc[B];
+    const uint32_t slot_base = ring_s + s * a.slot_bytes + delta + kb * kBlk;
+    float* tb = tbuf + (t & 1) * a.team_warps * a.per_team * B;
+    for (uint32_t rr = 0, u = 0; rr < rounds; ++rr)
+    for (uint32_t sub = 0; sub < R; ++sub, ++u) {
+      const uint32_t rho = rr * round_stride + team * R + sub;  // row within the tile
+      const uint32_t row = rs0 + rho;
+      float acc[B];
 #pragma unroll
-    for (int b = 0; b < B; ++b) acc[b] = 0.f;
+      for (int b = 0; b < B; ++b) acc[b] = 0.f;
 
-    if (active && row < rs1 && !s_failed) {
-      const uint32_t blk = ring_s + s * a.slot_bytes + delta + rho * RB + kb * kBlk;
-      if constexpr (QT == 4) {
-        const uint4 hdr = lds_v4(blk);
-        uint32_t q[W];
-        if constexpr (W == 8) {
-          const uint4 q0 = lds_v4(blk + 16 + 32 * unit + l0);
-          const uint4 q1 = lds_v4(blk + 32 + 32 * unit + l0);
-          q[0] = q0.x; q[1] = q0.y; q[2] = q0.z; q[3] = q0.w;
-          q[4] = q1.x; q[5] = q1.y; q[6] = q1.z; q[7] = q1.w;
-        } else if constexpr (W == 4) {
-          const uint4 q0 = lds_v4(blk + 16 + 32 * unit + l0);
-          q[0] = q0.x; q[1] = q0.y; q[2] = q0.z; q[3] = q0.w;
-        } else {
-          const uint2 q0 = lds_v2(blk + 16 + 32 * unit + l0);
-          q[0] = q0.x; q[1] = q0.y;
-        }
-        float2 sa[B], sb[B];
-#pragma unroll
-        for (int b = 0; b < B; ++b) { sa[b] = f2(0.f, 0.f); sb[b] = f2(0.f, 0.f); }
-#pragma unroll
-        for (int w = 0; w < W; ++w) {
-          const uint32_t lo = q[w] & 0x0F0F0F0Fu, hi = q[w] & 0xF0F0F0F0u;
-          const float2 fa = f2(prmt_lo<0>(lo), prmt_lo<1>(lo));
-          const float2 fb = f2(prmt_lo<2>(lo), prmt_lo<3>(lo));
-          const float2 ga = f2(prmt_hi<0>(hi), prmt_hi<1>(hi));
-          const float2 gb = f2(prmt_hi<2>(hi), prmt_hi<3>(hi));
-#pragma unroll
-          for (int b = 0; b < B; ++b) {
-            sa[b] = __ffma2_rn(xr[b][0][2 * w], fa, sa[b]);
-            sa[b] = __ffma2_rn(xr[b][0][2 * w + 1], fb, sa[b]);
-            sb[b] = __ffma2_rn(xr[b][1][2 * w], ga, sb[b]);
-            sb[b] = __ffma2_rn(xr[b][1][2 * w + 1], gb, sb[b]);
+      if (active && row < rs1 && !failed) {
+        const uint32_t blk = slot_base + rho * RB;
+        if constexpr (QT == 4) {
+          const uint4 hdr = lds_v4(blk);
+          uint32_t q[W];
+          if constexpr (W == 8) {
+            const uint4 q0 = lds_v4(blk + 16 + 32 * unit + l0);
+            const uint4 q1 = lds_v4(blk + 32 + 32 * unit + l0);
+            q[0] = q0.x; q[1] = q0.y; q[2] = q0.z; q[3] = q0.w;
+            q[4] = q1.x; q[5] = q1.y; q[6] = q1.z; q[7] = q1.w;
+          } else if constexpr (W == 4) {
+            const uint4 q0 = lds_v4(blk + 16 + 32 * unit + l0);
+            q[0] = q0.x; q[1] = q0.y; q[2] = q0.z; q[3] = q0.w;
+          } else {
+            const uint2 q0 = lds_v2(blk + 16 + 32 * unit + l0);
+            q[0] = q0.x; q[1] = q0.y;
           }
-        }
-        // scales and mins of sub-blocks 2c and 2c+1
-        uint32_t sc0, m0, sc1, m1;
-        if (!upper) {
-          sc0 = (hdr.y >> sh0) & 63u; m0 = (hdr.z >> sh0) & 63u;
-          sc1 = (hdr.y >> sh1) & 63u; m1 = (hdr.z >> sh1) & 63u;
-        } else {
-          sc0 = ((hdr.w >> sh0) & 15u) | (((hdr.y >> (sh0 + 6)) & 3u) << 4);
-          m0 = ((hdr.w >> (sh0 + 4)) & 15u) | (((hdr.z >> (sh0 + 6)) & 3u) << 4);
-          sc1 = ((hdr.w >> sh1) & 15u) | (((hdr.y >> (sh1 + 6)) & 3u) << 4);
-          m1 = ((hdr.w >> (sh1 + 4)) & 15u) | (((hdr.z >> (sh1 + 6)) & 3u) << 4);
-        }
-        const float d = h2f(hdr.x & 0xffffu), dmin = h2f(hdr.x >> 16);
-        const float fsc0 = static_cast<float>(sc0), fsc1 = static_cast<float>(sc1);
-        const float fm0 = static_cast<float>(m0), fm1 = static_cast<float>(m1);
+          // Accumulate S_A = sum x (2 + q/64) over the low nibbles (sub-block 2c) and
+          // S_B = sum x (2 + q/1024) over the high nibbles (sub-block 2c+1).
+#if KQ_PACKED_FMA
+          float2 sa[B], sb[B];
 #pragma unroll
-        for (int b = 0; b < B; ++b) {
-          const float qa = fmaf(64.f, sa[b].x + sa[b].y, -128.f * xs[b][0]);
-          const float qb = fmaf(1024.f, sb[b].x + sb[b].y, -2048.f * xs[b][1]);
-          const float pos = fmaf(fsc0, qa, fsc1 * qb);
-          const float neg = fmaf(fm0, xs[b][0], fm1 * xs[b][1]);
-          acc[b] = fmaf(d, pos, -dmin * neg);
-        }
-      } else {
-        uint32_t qa[W], qb[W], qh[W];
-        lds_words_unaligned<W>(blk + 64 * unit + l0, qa);
-        lds_words_unaligned<W>(blk + 64 * unit + 32 + l0, qb);
-        lds_words_unaligned<W>(blk + 128 + 32 * unit + l0, qh);
-        const uint32_t sbase = blk + 192 + 8 * unit + (l0 >> 4);
-        float fsc[4];
+          for (int b = 0; b < B; ++b) { sa[b] = f2(0.f, 0.f); sb[b] = f2(0.f, 0.f); }
 #pragma unroll
-        for (int g = 0; g < 4; ++g) fsc[g] = static_cast<float>(lds_s8(sbase + 2 * g));
-        const float d = h2f(lds_u16(blk + 208));
-        float2 sg[B][4];
-#pragma unroll
-        for (int b = 0; b < B; ++b)
-#pragma unroll
-          for (int g = 0; g < 4; ++g) sg[b][g] = f2(0.f, 0.f);
-#pragma unroll
-        for (int w = 0; w < W; ++w) {
-          uint32_t qg[4];
-          qg[0] = (qa[w] & 0x0F0F0F0Fu) | ((qh[w] << 4) & 0x30303030u);
-          qg[1] = (qb[w] & 0x0F0F0F0Fu) | ((qh[w] << 2) & 0x30303030u);
-          qg[2] = ((qa[w] >> 4) & 0x0F0F0F0Fu) | (qh[w] & 0x30303030u);
-          qg[3] = ((qb[w] >> 4) & 0x0F0F0F0Fu) | ((qh[w] >> 2) & 0x30303030u);
-#pragma unroll
-          for (int g = 0; g < 4; ++g) {
-            const float2 f01 = f2(prmt_lo<0>(qg[g]), prmt_lo<1>(qg[g]));
-            const float2 f23 = f2(prmt_lo<2>(qg[g]), prmt_lo<3>(qg[g]));
+          for (int w = 0; w < W; ++w) {
+            const uint32_t lo = q[w] & 0x0F0F0F0Fu, hi = q[w] & 0xF0F0F0F0u;
+            const float2 fa = f2(prmt_lo<0>(lo), prmt_lo<1>(lo));
+            const float2 fb = f2(prmt_lo<2>(lo), prmt_lo<3>(lo));
+            const float2 ga = f2(prmt_hi<0>(hi), prmt_hi<1>(hi));
+            const float2 gb = f2(prmt_hi<2>(hi), prmt_hi<3>(hi));
 #pragma unroll
             for (int b = 0; b < B; ++b) {
-              sg[b][g] = __ffma2_rn(xr[b][g][2 * w], f01, sg[b][g]);
-              sg[b][g] = __ffma2_rn(xr[b][g][2 * w + 1], f23, sg[b][g]);
+              sa[b] = __ffma2_rn(xr[b][0][2 * w], fa, sa[b]);
+              sb[b] = __ffma2_rn(xr[b][1][2 * w], ga, sb[b]);
+              sa[b] = __ffma2_rn(xr[b][0][2 * w + 1], fb, sa[b]);
+              sb[b] = __ffma2_rn(xr[b][1][2 * w + 1], gb, sb[b]);
+            }
+          }
+#define KQ_SA(b) (sa[b].x + sa[b].y)
+#define KQ_SB(b) (sb[b].x + sb[b].y)
+#else
+          float sa[B][2], sb[B][2];
+#pragma unroll
+          for (int b = 0; b < B; ++b) { sa[b][0] = sa[b][1] = sb[b][0] = sb[b][1] = 0.f; }
+#pragma unroll
+          for (int w = 0; w < W; ++w) {
+            const uint32_t lo = q[w] & 0x0F0F0F0Fu, hi = q[w] & 0xF0F0F0F0u;
+            const float f0 = prmt_lo<0>(lo), f1 = prmt_lo<1>(lo), f2v = prmt_lo<2>(lo), f3 = prmt_lo<3>(lo);
+            const float g0 = prmt_hi<0>(hi), g1 = prmt_hi<1>(hi), g2 = prmt_hi<2>(hi), g3 = prmt_hi<3>(hi);
+#pragma unroll
+            for (int b = 0; b < B; ++b) {
+              float& A = sa[b][w & 1];
+              float& Bv = sb[b][w & 1];
+              A = fmaf(xr[b][0][2 * w].x, f0, A);
+              Bv = fmaf(xr[b][1][2 * w].x, g0, Bv);
+              A = fmaf(xr[b][0][2 * w].y, f1, A);
+              Bv = fmaf(xr[b][1][2 * w].y, g1, Bv);
+              A = fmaf(xr[b][0][2 * w + 1].x, f2v, A);
+              Bv = fmaf(xr[b][1][2 * w + 1].x, g2, Bv);
+              A = fmaf(xr[b][0][2 * w + 1].y, f3, A);
+              Bv = fmaf(xr[b][1][2 * w + 1].y, g3, Bv);
+            }
+          }
+#define KQ_SA(b) (sa[b][0] + sa[b][1])
+#define KQ_SB(b) (sb[b][0] + sb[b][1])
+#endif
+          // scales and mins of sub-blocks 2c and 2c+1
+          uint32_t sc0, m0, sc1, m1;
+          if (!upper) {
+            sc0 = (hdr.y >> sh0) & 63u; m0 = (hdr.z >> sh0) & 63u;
+            sc1 = (hdr.y >> sh1) & 63u; m1 = (hdr.z >> sh1) & 63u;
+          } else {
+            sc0 = ((hdr.w >> sh0) & 15u) | (((hdr.y >> (sh0 + 6)) & 3u) << 4);
+            m0 = ((hdr.w >> (sh0 + 4)) & 15u) | (((hdr.z >> (sh0 + 6)) & 3u) << 4);
+            sc1 = ((hdr.w >> sh1) & 15u) | (((hdr.y >> (sh1 + 6)) & 3u) << 4);
+            m1 = ((hdr.w >> (sh1 + 4)) & 15u) | (((hdr.z >> (sh1 + 6)) & 3u) << 4);
+          }
+          const float d = h2f(hdr.x & 0xffffu), dmin = h2f(hdr.x >> 16);
+          const float fsc0 = static_cast<float>(sc0), fsc1 = static_cast<float>(sc1);
+          const float fm0 = static_cast<float>(m0), fm1 = static_cast<float>(m1);
+#pragma unroll
+          for (int b = 0; b < B; ++b) {
+            const float qa = fmaf(64.f, KQ_SA(b), -128.f * xs[b][0]);
+            const float qb = fmaf(1024.f, KQ_SB(b), -2048.f * xs[b][1]);
+            const float pos = fmaf(fsc0, qa, fsc1 * qb);
+            const float neg = fmaf(fm0, xs[b][0], fm1 * xs[b][1]);
+            acc[b] = fmaf(d, pos, -dmin * neg);
+          }
+#undef KQ_SA
+#undef KQ_SB
+        } else {
+          uint32_t qa[W], qb[W], qh[W];
+          lds_words_unaligned<W>(blk + 64 * unit + l0, qa);
+          lds_words_unaligned<W>(blk + 64 * unit + 32 + l0, qb);
+          lds_words_unaligned<W>(blk + 128 + 32 * unit + l0, qh);
+          const uint32_t sbase = blk + 192 + 8 * unit + (l0 >> 4);
+          float fsc[4];
+#pragma unroll
+          for (int g = 0; g < 4; ++g) fsc[g] = static_cast<float>(lds_s8(sbase + 2 * g));
+          const float d = h2f(lds_u16(blk + 208));
+#if KQ_PACKED_FMA
+          float2 sg[B][4];
+#pragma unroll
+          for (int b = 0; b < B; ++b)
+#pragma unroll
+            for (int g = 0; g < 4; ++g) sg[b][g] = f2(0.f, 0.f);
+#else
+          float sg[B][4];
+#pragma unroll
+          for (int b = 0; b < B; ++b)
+#pragma unroll
+            for (int g = 0; g < 4; ++g) sg[b][g] = 0.f;
+#endif
+#pragma unroll
+          for (int w = 0; w < W; ++w) {
+            uint32_t qg[4];
+            qg[0] = (qa[w] & 0x0F0F0F0Fu) | ((qh[w] << 4) & 0x30303030u);
+            qg[1] = (qb[w] & 0x0F0F0F0Fu) | ((qh[w] << 2) & 0x30303030u);
+            qg[2] = ((qa[w] >> 4) & 0x0F0F0F0Fu) | (qh[w] & 0x30303030u);
+            qg[3] = ((qb[w] >> 4) & 0x0F0F0F0Fu) | ((qh[w] >> 2) & 0x30303030u);
+#pragma unroll
+            for (int g = 0; g < 4; ++g) {
+#if KQ_PACKED_FMA
+              const float2 f01 = f2(prmt_lo<0>(qg[g]), prmt_lo<1>(qg[g]));
+              const float2 f23 = f2(prmt_lo<2>(qg[g]), prmt_lo<3>(qg[g]));
+#pragma unroll
+              for (int b = 0; b < B; ++b) {
+                sg[b][g] = __ffma2_rn(xr[b][g][2 * w], f01, sg[b][g]);
+                sg[b][g] = __ffma2_rn(xr[b][g][2 * w + 1], f23, sg[b][g]);
+              }
+#else
+              const float f0 = prmt_lo<0>(qg[g]), f1 = prmt_lo<1>(qg[g]);
+              const float f2v = prmt_lo<2>(qg[g]), f3 = prmt_lo<3>(qg[g]);
+#pragma unroll
+              for (int b = 0; b < B; ++b) {
+                sg[b][g] = fmaf(xr[b][g][2 * w].x, f0, sg[b][g]);
+                sg[b][g] = fmaf(xr[b][g][2 * w].y, f1, sg[b][g]);
+                sg[b][g] = fmaf(xr[b][g][2 * w + 1].x, f2v, sg[b][g]);
+                sg[b][g] = fmaf(xr[b][g][2 * w + 1].y, f3, sg[b][g]);
+              }
+#endif
+            }
+          }
+#pragma unroll
+          for (int b = 0; b < B; ++b) {
+            float tt = 0.f;
+#pragma unroll
+            for (int g = 0; g < 4; ++g) {
+              // sum (q - 32) x = 64 S - 128 X - 32 X
+#if KQ_PACKED_FMA
+              const float qx = fmaf(64.f, sg[b][g].x + sg[b][g].y, -160.f * xs[b][g]);
+#else
+              const float qx = fmaf(64.f, sg[b][g], -160.f * xs[b][g]);
+#endif
+              tt = fmaf(fsc[g], qx, tt);
+            }
+            acc[b] = d * tt;
+          }
+        }
+      }
+
+      // lanes -> warp
+#pragma unroll
+      for (int b = 0; b < B; ++b) {
+#pragma unroll
+        for (int o = 16; o; o >>= 1) acc[b] += __shfl_xor_sync(0xffffffffu, acc[b], o);
+      }
+      if (a.team_warps == 1) {
+        // one warp is the whole team: lane 0 has the row
+        if (lane == 0 && row < rs1) {
+#pragma unroll
+          for (int b = 0; b < B; ++b) {
+            if (b < static_cast<int>(a.batch)) {
+              if (R == 1) {
+                a.y[b * a.ldy + row] = acc[b];
+              } else if ((u & 1) == 0) {
+                held[b] = acc[b];
+              } else {
+                a.y[b * a.ldy + row / 2] = held[b] * acc[b] * a.pair_scale;
+              }
             }
           }
         }
+      } else if (lane == 0) {
 #pragma unroll
-        for (int b = 0; b < B; ++b) {
-          float t = 0.f;
-#pragma unroll
-          for (int g = 0; g < 4; ++g) {
-            // sum (q - 32) x = 64 S - 128 X - 32 X
-            const float qx = fmaf(64.f, sg[b][g].x + sg[b][g].y, -160.f * xs[b][g]);
-            t = fmaf(fsc[g], qx, t);
-          }
-          acc[b] = d * t;
-        }
+        for (int b = 0; b < B; ++b) tb[(u * a.team_warps + tw) * B + b] = acc[b];
       }
-    }
-
-    // lanes -> warp
-#pragma unroll
-    for (int b = 0; b < B; ++b) {
-#pragma unroll
-      for (int o = 16; o; o >>= 1) acc[b] += __shfl_xor_sync(0xffffffffu, acc[b], o);
-    }
-    if (lane == 0) {
-#pragma unroll
-      for (int b = 0; b < B; ++b) rbuf[(u * consumers + warp) * B + b] = acc[b];
-    }
     }  // rows of this team in the tile
     __syncwarp();
     if (lane == 0) mbar_arrive(empty_bar(s));  // this warp is done reading slot s
-    named_barrier(1, consumers * 32);
+    if (++s == a.ring) {
+      s = 0;
+      phase ^= 1;
+    }
 
-    // warps of a team -> row; then the epilogue. Row rho of the tile is team rho % teams,
-    // pass rho / teams; its warps' partials sit at rbuf[((rho / teams) * consumers + team *
-    // team_warps + w) * B + b].
-    auto row_sum = [&](uint32_t rho, uint32_t b) {
-      const uint32_t base = (rho / a.teams) * consumers + (rho % a.teams) * a.team_warps;
-      float v = 0.f;
-      for (uint32_t w = 0; w < a.team_warps; ++w) v += rbuf[(base + w) * B + b];
-      return v;
-    };
-    const uint32_t nthreads = consumers * 32;
-    if (a.epilogue == KQ_EPILOGUE_PAIR_PRODUCT) {
-      for (uint32_t o = threadIdx.x; o < (SR / 2) * B; o += nthreads) {
-        const uint32_t i = o / B, b = o % B;
-        const uint32_t r = rs0 + 2 * i;
-        if (r < rs1 && b < a.batch)
-          a.y[b * a.ldy + r / 2] = row_sum(2 * i, b) * row_sum(2 * i + 1, b) * a.pair_scale;
-      }
-    } else {
-      for (uint32_t o = threadIdx.x; o < SR * B; o += nthreads) {
-        const uint32_t rho = o / B, b = o % B;
-        const uint32_t r = rs0 + rho;
-        if (r < rs1 && b < a.batch) a.y[b * a.ldy + r] = row_sum(rho, b);
+    if (a.team_warps > 1) {
+      // warps of a team -> its rows, by the team's first warp
+      named_barrier(1 + team, a.team_warps * 32);
+      if (tw == 0) {
+        const uint32_t nout = (a.per_team / R) * B;
+        for (uint32_t o = lane; o < nout; o += 32) {
+          const uint32_t i = o / B, b = o % B;  // B is a compile-time power of two
+          const uint32_t u0 = i * R;
+          const uint32_t rho = i * round_stride + team * R;
+          const uint32_t row = rs0 + rho;
+          if (row < rs1 && b < a.batch) {
+            float v0 = 0.f;
+            for (uint32_t w = 0; w < a.team_warps; ++w) v0 += tb[(u0 * a.team_warps + w) * B + b];
+            if (R == 1) {
+              a.y[b * a.ldy + row] = v0;
+            } else {
+              float v1 = 0.f;
+              for (uint32_t w = 0; w < a.team_warps; ++w)
+                v1 += tb[((u0 + 1) * a.team_warps + w) * B + b];
+              a.y[b * a.ldy + row / 2] = v0 * v1 * a.pair_scale;
+            }
+          }
+        }
       }
     }
   }
@@ -511,9 +601,7 @@ int matvec(kq_ctx* ctx, const kq_matvec_desc& d, cudaStream_t stream) {
                 "k " + std::to_string(d.k) + " is past this build's limit for batch " +
                     std::to_string(d.batch) + " (" + std::to_string(max_consumers * 32 / ppb * kQK) +
                     ")");
-  uint32_t pmax = max_consumers / team_warps;
-  if (pair) pmax &= ~1u;
-  if (pmax == 0) return fail(KQ_E_UNSUPPORTED, call, "k too large for the pair-product epilogue");
+  const uint32_t pmax = std::min<uint32_t>(15, max_consumers / team_warps);  // named barriers 1..15
 
   const uint32_t row_unit = pair ? 2 : 1;
   const uint64_t units = d.rows / row_unit;
@@ -521,13 +609,12 @@ int matvec(kq_ctx* ctx, const kq_matvec_desc& d, cudaStream_t stream) {
   const uint64_t rows_per_cta = ((units + grid - 1) / grid) * row_unit;
   // Teams: as many as fit, trimmed so that the CTA's rows split evenly over its tiles.
   const uint64_t rounds = (rows_per_cta + pmax - 1) / pmax;
-  uint32_t P = static_cast<uint32_t>((rows_per_cta + rounds - 1) / rounds);
-  if (pair) P += P & 1;
+  const uint32_t P = static_cast<uint32_t>((rows_per_cta + rounds - 1) / rounds);
   const uint64_t rb = uint64_t(nb) * blk;
   // Rows per team per tile: tiles of about kTileTarget bytes, no more rows than the CTA has.
   uint32_t U = static_cast<uint32_t>(std::max<uint64_t>(1, kTileTarget / (uint64_t(P) * rb)));
   U = static_cast<uint32_t>(std::min<uint64_t>(U, (rows_per_cta + P - 1) / P));
-  if (pair && (P * U) % 2) ++U;
+  if (pair) U += U & 1;  // a team takes both rows of a pair
   const uint32_t slot = static_cast<uint32_t>(((uint64_t(P) * U * rb + 32 + 127) / 128) * 128);
   const uint32_t consumers = P * team_warps;
   const uint32_t red_bytes = 2 * consumers * U * bt * 4;
