@@ -53,6 +53,8 @@ def parse_args(argv=None):
     ap.add_argument("--warmup", type=int, default=200)
     ap.add_argument("--workload", default="q6k_head", choices=sorted(WORKLOADS))
     ap.add_argument("--batch", type=int, default=1)
+    ap.add_argument("--path", default="auto", choices=["auto", "tc", "cc"],
+                    help="tensor cores, CUDA cores, or the library's choice")
     ap.add_argument("--impl", default="kq", choices=["kq", "reference"])
     ap.add_argument("--e2e-steps", type=int, default=2000, help="steps of the end-to-end leg")
     ap.add_argument("--cpu-seconds", type=float, default=12.0, help="CPU-baseline time budget")
@@ -222,6 +224,7 @@ def config_of(args, w, world):
     return {
         "workload": f"{args.workload}: Q{w['qtype']}_K {w['rows']}x{w['k']} batch {w['batch']} ({w['source']})",
         "qtype": f"Q{w['qtype']}_K", "rows": w["rows"], "k": w["k"], "batch": w["batch"],
+        "path": args.path,
         "parallelism": f"replicas x{world}" if world > 1 else "single",
     }
 
@@ -264,9 +267,11 @@ def main(argv=None):
     stream = torch.cuda.Stream()
     torch.cuda.synchronize()
 
+    path_flag = {"auto": 0, "tc": kb.FLAG_TENSOR_CORES, "cc": kb.FLAG_CUDA_CORES}[args.path]
+
     def step(i, s):
-        kernels.matvec(qtype, y, Ws[i % copies], x, rows, K, batch, flags=kb.FLAG_WEIGHTS_STATIC,
-                       stream=s)
+        kernels.matvec(qtype, y, Ws[i % copies], x, rows, K, batch,
+                       flags=kb.FLAG_WEIGHTS_STATIC | path_flag, stream=s)
 
     # The timed loop replays CUDA graphs of launches (captured with their programmatic-
     # dependent-launch edges): a graph of G steps, G a multiple of the weight copies so that

@@ -63,7 +63,11 @@ enum {
      * start streaming them before that kernel ends (programmatic dependent launch). */
     KQ_FLAG_WEIGHTS_STATIC = 1u << 0,
     /* Launch without the programmatic-dependent-launch attribute. */
-    KQ_FLAG_NO_PDL = 1u << 1
+    KQ_FLAG_NO_PDL = 1u << 1,
+    /* Use the tensor-core (tcgen05) kernel; Q4_K only. */
+    KQ_FLAG_TENSOR_CORES = 1u << 2,
+    /* Use the CUDA-core kernel (batch <= 8). Without either flag the library chooses. */
+    KQ_FLAG_CUDA_CORES = 1u << 3
 };
 
 typedef struct kq_ctx kq_ctx;
@@ -92,13 +96,13 @@ int kq_ctx_info(const kq_ctx* ctx, int* device, int* sm_count, int* max_smem_per
 int kq_device_error(kq_ctx* ctx);
 
 /* y[b*rows + r] = sum_k W[r,k] * x[b*k + k'] for b < batch, r < rows: the Q4_K matvec.
- * batch 1..8 on the CUDA cores. W: 16-byte aligned; x: 16-byte aligned f32; y: f32.
+ * batch 1..64 (above 8 on the tensor cores). W: 16-byte aligned; x: 16-byte aligned f32; y: f32.
  * Replaces a macro launcher `kernels.matvec_q4k(grid, y, w, x, rows, k)` of kernite's shape
  * (crates/macros/src/gpu.rs:276-328); the grid is the library's choice, not the caller's. */
 int kq_matvec_q4k(kq_ctx* ctx, uint64_t y, uint64_t w, uint64_t x, uint32_t rows, uint32_t k,
                   uint32_t batch, kq_stream stream);
 
-/* The same for Q6_K (210-byte blocks; rows may start at any even byte offset). */
+/* The same for Q6_K (210-byte blocks; rows may start at any even byte offset); batch 1..8. */
 int kq_matvec_q6k(kq_ctx* ctx, uint64_t y, uint64_t w, uint64_t x, uint32_t rows, uint32_t k,
                   uint32_t batch, kq_stream stream);
 
@@ -106,7 +110,7 @@ int kq_matvec_q6k(kq_ctx* ctx, uint64_t y, uint64_t w, uint64_t x, uint32_t rows
 typedef struct kq_matvec_desc {
     uint32_t type;     /* KQ_TYPE_Q4_K or KQ_TYPE_Q6_K */
     uint32_t rows, k;  /* W is rows x k; k % 256 == 0 */
-    uint32_t batch;    /* vectors, 1..8 */
+    uint32_t batch;    /* vectors: 1..64 for Q4_K, 1..8 for Q6_K */
     uint64_t y, w, x;  /* device addresses */
     uint64_t ldx;      /* floats between vectors of x (>= k, multiple of 4); 0 = k */
     uint64_t ldy;      /* floats between vectors of y; 0 = rows (or rows/2 for PAIR_PRODUCT) */

@@ -40,6 +40,8 @@ EPILOGUE_NONE = 0
 EPILOGUE_PAIR_PRODUCT = 1
 FLAG_WEIGHTS_STATIC = 1
 FLAG_NO_PDL = 2
+FLAG_TENSOR_CORES = 4
+FLAG_CUDA_CORES = 8
 
 Q4K_BYTES = 144
 Q6K_BYTES = 210

@@ -92,9 +92,17 @@ int kq_ctx_create(int device, kq_ctx** out) {
     delete ctx;
     return cuda_fail(e, "cudaMemset", "device error word");
   }
+  e = cudaMalloc(&ctx->scratch, kq::kCtxScratchBytes);
+  if (e != cudaSuccess) {
+    delete ctx;
+    return cuda_fail(e, "cudaMalloc", "context scratch");
+  }
+  ctx->scratch_bytes = kq::kCtxScratchBytes;
   int rc = kq::matvec_prepare(ctx);
+  if (rc == KQ_OK) rc = kq::mma_prepare(ctx);
   if (rc == KQ_OK) rc = kq::aux_prepare(ctx);
   if (rc != KQ_OK) {
+    cudaFree(ctx->scratch);
     delete ctx;
     return rc;
   }
@@ -103,6 +111,11 @@ int kq_ctx_create(int device, kq_ctx** out) {
 }
 
 int kq_ctx_destroy(kq_ctx* ctx) {
+  if (!ctx) return KQ_OK;
+  if (ctx->scratch) {
+    kq::enter(ctx);
+    cudaFree(ctx->scratch);  // waits for the device, so no launch still reads it
+  }
   delete ctx;
   return KQ_OK;
 }

@@ -13,9 +13,15 @@ struct kq_ctx {
   int sm_count = 0;
   int max_smem = 0;       // opt-in dynamic shared memory per block
   unsigned* err = nullptr;  // the device error word (a file-scope __device__ variable)
+  // Scratch the tensor-core path converts X into (allocated once, at creation).
+  void* scratch = nullptr;
+  uint64_t scratch_bytes = 0;
 };
 
 namespace kq {
+
+// Scratch bytes a context allocates: the B operand of a k = 32768, batch = 64 tensor-core call.
+constexpr uint64_t kCtxScratchBytes = 4ull << 20;
 
 // Records the thread's last error as "<call>: <detail>" and returns `code`.
 int fail(int code, const char* call, const std::string& detail);
@@ -25,6 +31,11 @@ int cuda_fail(cudaError_t e, const char* call, const std::string& detail = std::
 int enter(const kq_ctx* ctx);
 
 int matvec_prepare(kq_ctx* ctx);
+int mma_prepare(kq_ctx* ctx);
+bool mma_supports(const kq_matvec_desc& d);
+int mma_matvec(kq_ctx* ctx, const kq_matvec_desc& d, uint64_t ldx, uint64_t ldy,
+               cudaStream_t stream);
+uint64_t mma_scratch_bytes(uint32_t k, uint32_t batch);
 int matvec(kq_ctx* ctx, const kq_matvec_desc& d, cudaStream_t stream);
 
 int aux_prepare(kq_ctx* ctx);

@@ -572,8 +572,12 @@ int matvec(kq_ctx* ctx, const kq_matvec_desc& d, cudaStream_t stream) {
     return fail(KQ_E_INVALID, call,
                 "rows must be > 0 and k a positive multiple of 256 (rows " +
                     std::to_string(d.rows) + ", k " + std::to_string(d.k) + ")");
-  if (d.batch < 1 || d.batch > 8)
-    return fail(KQ_E_INVALID, call, "batch must be 1..8 (got " + std::to_string(d.batch) + ")");
+  const uint32_t max_batch = qt == 4 ? 64 : 8;
+  if (d.batch < 1 || d.batch > max_batch)
+    return fail(KQ_E_INVALID, call,
+                "batch must be 1.." + std::to_string(max_batch) + " (got " + std::to_string(d.batch) + ")");
+  if ((d.flags & KQ_FLAG_TENSOR_CORES) && (d.flags & KQ_FLAG_CUDA_CORES))
+    return fail(KQ_E_INVALID, call, "KQ_FLAG_TENSOR_CORES and KQ_FLAG_CUDA_CORES exclude each other");
   if (!d.w || !d.x || !d.y) return fail(KQ_E_INVALID, call, "null pointer");
   if (d.w % 16 || d.x % 16 || d.y % 4)
     return fail(KQ_E_INVALID, call, "w and x must be 16-byte aligned, y 4-byte aligned");
@@ -587,6 +591,16 @@ int matvec(kq_ctx* ctx, const kq_matvec_desc& d, cudaStream_t stream) {
   if (ldx < d.k || ldx % 4) return fail(KQ_E_INVALID, call, "ldx must be >= k and a multiple of 4");
   if (ldy < out_rows) return fail(KQ_E_INVALID, call, "ldy must be >= the output rows");
 
+  // Path: the tensor cores above batch 8 (and when asked), the CUDA cores otherwise.
+  const bool want_tc = (d.flags & KQ_FLAG_TENSOR_CORES) || (d.batch > 8 && !(d.flags & KQ_FLAG_CUDA_CORES));
+  if (want_tc) {
+    if (!mma_supports(d))
+      return fail(KQ_E_UNSUPPORTED, call,
+                  "the tensor-core kernel serves Q4_K without prologue/epilogue, batch 1..64");
+    return mma_matvec(ctx, d, ldx, ldy, stream);
+  }
+  if (d.batch > 8)
+    return fail(KQ_E_UNSUPPORTED, call, "the CUDA-core kernel serves batch 1..8");
   const int bt = d.batch == 1 ? 1 : d.batch == 2 ? 2 : d.batch <= 4 ? 4 : 8;
   const Instance in = pick(qt, bt);
   const int L = qt == 4 ? in.l4 : in.l6;

@@ -213,7 +213,7 @@ def test_invalid_arguments_are_rejected_before_launch(kernels):
     cases = [
         dict(rows=4, k=300, batch=1),
         dict(rows=4, k=256, batch=0),
-        dict(rows=4, k=256, batch=9),
+        dict(rows=4, k=256, batch=65),
         dict(rows=0, k=256, batch=1),
     ]
     for c in cases:
@@ -267,3 +267,76 @@ def test_70b_shapes_sampled_rows_and_linearity(kernels, qtype, rows, K):
     _, b1 = oracle.matvec_ref(qtype, Wh, np.abs(x1) + np.abs(x2), K, 0, 64)
     assert (np.abs(y12[:, :64] - y1[:, :64] - y2[:, :64]) <= 3 * TOL * b1).all()
     assert np.isfinite(y12).all()
+
+
+# ---------------------------------------------------------------- tensor-core (tcgen05) path
+
+TC_SHAPES = [
+    # (rows, K, batch)
+    (1, 256, 1), (100, 256, 1), (128, 512, 1), (129, 4096, 1), (300, 11008, 1), (4096, 4096, 1),
+    (333, 4096, 2), (257, 4096, 8), (333, 4096, 17), (77, 8192, 33), (1000, 4096, 64),
+    (14336, 4096, 16), (5000, 4096, 40),
+]
+
+
+@pytest.mark.parametrize("rows,K,batch", TC_SHAPES)
+def test_tensor_core_matvec_matches_oracle(kernels, rows, K, batch):
+    W = dev_weights(kernels, 4, rows, K, kb.stream_key(3000 + rows, K + batch))
+    x = np.random.default_rng(rows + K + batch).standard_normal((batch, K), dtype=np.float32)
+    y = run_matvec(kernels, 4, W, x, rows, K, flags=kb.FLAG_TENSOR_CORES)
+    y_ref, bound = oracle.matvec_ref(4, W.cpu().numpy(), x, K, 0, rows)
+    check(y, y_ref, bound, f"tc {rows}x{K} b{batch}")
+
+
+def test_tensor_core_integer_inputs_are_exact(kernels):
+    rows, K, batch = 300, 1024, 5
+    Wn = oracle.fill(4, oracle.stream_key(78, 4), 0, rows * K // 256)
+    blocks = Wn.reshape(-1, 144)
+    blocks[:, 0:2] = np.array([0x2400], dtype=np.uint16).view(np.uint8)  # d = 2^-6
+    blocks[:, 2:4] = np.array([0x2800], dtype=np.uint16).view(np.uint8)  # dmin = 2^-5
+    W = torch.from_numpy(blocks.reshape(-1).copy()).cuda()
+    x = np.random.default_rng(4).integers(-2, 3, size=(batch, K)).astype(np.float32)
+    y = run_matvec(kernels, 4, W, x, rows, K, flags=kb.FLAG_TENSOR_CORES)
+    y_ref, _ = oracle.matvec_ref(4, blocks.reshape(-1), x, K, 0, rows)
+    assert np.array_equal(y, y_ref.astype(np.float32))
+
+
+def test_tensor_core_strided_and_canaries(kernels):
+    rows, K, batch, ldx, ldy = 211, 2048, 19, 2048 + 20, 211 + 13
+    W = dev_weights(kernels, 4, rows, K, kb.stream_key(31, 4))
+    xs = np.random.default_rng(31).standard_normal((batch, ldx), dtype=np.float32)
+    xd = torch.from_numpy(xs).cuda()
+    y = torch.full((batch, ldy), float("nan"), device="cuda")
+    kernels.matvec(4, y, W, xd, rows, K, batch, ldx=ldx, ldy=ldy, flags=kb.FLAG_TENSOR_CORES)
+    torch.cuda.synchronize()
+    yh = y.cpu().numpy()
+    y_ref, bound = oracle.matvec_ref(4, W.cpu().numpy(), np.ascontiguousarray(xs[:, :K]), K, 0, rows)
+    check(yh[:, :rows], y_ref, bound)
+    assert np.isnan(yh[:, rows:]).all()
+
+
+@pytest.mark.parametrize("batch", [1, 4, 8])
+def test_both_paths_agree(kernels, batch):
+    rows, K = 1500, 4096
+    W = dev_weights(kernels, 4, rows, K, kb.stream_key(32, batch))
+    x = np.random.default_rng(batch).standard_normal((batch, K), dtype=np.float32)
+    y_tc = run_matvec(kernels, 4, W, x, rows, K, flags=kb.FLAG_TENSOR_CORES)
+    y_cc = run_matvec(kernels, 4, W, x, rows, K, flags=kb.FLAG_CUDA_CORES)
+    _, bound = oracle.matvec_ref(4, W.cpu().numpy(), x, K, 0, rows)
+    assert (np.abs(y_tc - y_cc) <= 2 * TOL * bound).all()
+
+
+def test_path_flags_are_checked(kernels):
+    W = torch.empty(144 * 16, dtype=torch.uint8, device="cuda")
+    x = torch.zeros(4096 * 64, device="cuda")
+    y = torch.zeros(4096 * 64, device="cuda")
+    with pytest.raises(kb.Error) as e:
+        kernels.matvec(4, y, W, x, 1, 4096, 1, flags=kb.FLAG_TENSOR_CORES | kb.FLAG_CUDA_CORES)
+    assert e.value.code == kb.KQ_E_INVALID
+    with pytest.raises(kb.Error) as e:  # Q6_K has no tensor-core kernel yet
+        kernels.matvec(6, y, W, x, 1, 256, 1, flags=kb.FLAG_TENSOR_CORES)
+    assert e.value.code == kb.KQ_E_UNSUPPORTED
+    with pytest.raises(kb.Error) as e:  # the CUDA cores stop at batch 8
+        kernels.matvec(4, y, W, x, 1, 256, 9, flags=kb.FLAG_CUDA_CORES)
+    assert e.value.code == kb.KQ_E_UNSUPPORTED
+    kernels.device_error()
