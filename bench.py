@@ -8,7 +8,9 @@ so every step streams from DRAM. Workloads:
 
   q6k_head   configs[1]  Q6_K 32000 x 4096, batch 1   (default; the metric's config)
   q4k        configs[0]  Q4_K 4096 x 4096, batch 1
-  sweep      configs[3]  Q4_K 14336 x 4096, batch --batch (1..8)
+  sweep      configs[3]  Q4_K 14336 x 4096, batch --batch (1..64)
+  stack7b    configs[2]  Llama-7B-shaped decode matvec stack, decode tokens/s
+  stack70b   configs[4]  Llama-70B-shaped stack, rows sharded over the N GPUs (NCCL all-gathers)
 
 With N GPUs (torchrun) every rank runs its own replica: the single matvec does not shard
 ("replicas only"), so `scaling` is "weak" and `value` sums the ranks' bytes over the slowest
@@ -46,12 +48,15 @@ WORKLOADS = {
 }
 
 
+STACKS = {"stack7b": "7b", "stack70b": "70b"}
+
+
 def parse_args(argv=None):
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=20000)
     ap.add_argument("--warmup", type=int, default=200)
-    ap.add_argument("--workload", default="q6k_head", choices=sorted(WORKLOADS))
+    ap.add_argument("--workload", default="q6k_head", choices=sorted(WORKLOADS) + sorted(STACKS))
     ap.add_argument("--batch", type=int, default=1)
     ap.add_argument("--path", default="auto", choices=["auto", "tc", "cc"],
                     help="tensor cores, CUDA cores, or the library's choice")
@@ -231,6 +236,8 @@ def config_of(args, w, world):
 
 def main(argv=None):
     args = parse_args(argv)
+    if args.workload in STACKS:
+        return run_stack(args)
     if args.impl == "reference":
         return run_reference(args)
 
@@ -414,6 +421,200 @@ def run_e2e(kernels, kb, torch, qtype, Ws, rows, K, batch, steps, dist):
     return {"value": round(world * wbytes * steps / (ms / 1e3) / 1e9, 2), "unit": "GB/s",
             "h2d_bytes_per_step": batch * K * 4, "d2h_bytes_per_step": batch * rows * 4,
             "steps": steps, "ms_per_step": round(ms / steps, 5)}
+
+
+def _init_dist(torch, world, local):
+    if world == 1:
+        return None
+    import datetime
+
+    import torch.distributed as dist
+
+    dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=180),
+                            device_id=torch.device("cuda", local))
+    return dist
+
+
+def stack_cpu_seconds_per_token(cfg, threads):
+    """CPU baseline for a stack: one layer's matvecs and the head timed with the AVX2 port,
+    scaled to the stack's layer count. Returns (seconds per token, sample)."""
+    import numpy as np
+
+    import oracle
+
+    from kernite_b200 import stack as st
+
+    rng = np.random.default_rng(0)
+    t_layer = 0.0
+    for name, qtype, rows, k in cfg.matrices():
+        W = oracle.fill(qtype, oracle.stream_key(cfg.seed, cfg.tensor_id(0, name)), 0, rows * k // st.QK)
+        x = rng.standard_normal((1, k), dtype=np.float32)
+        oracle.matvec_cpu(qtype, W, x, rows, k, threads)  # warm
+        t0 = time.perf_counter()
+        oracle.matvec_cpu(qtype, W, x, rows, k, threads)
+        t_layer += time.perf_counter() - t0
+        del W
+    H = oracle.fill(6, oracle.stream_key(cfg.seed, cfg.tensor_id(cfg.layers, "head")), 0,
+                    cfg.vocab * cfg.hidden // st.QK)
+    xh = rng.standard_normal((1, cfg.hidden), dtype=np.float32)
+    t0 = time.perf_counter()
+    oracle.matvec_cpu(6, H, xh, cfg.vocab, cfg.hidden, threads)
+    t_head = time.perf_counter() - t0
+    sec = cfg.layers * t_layer + t_head
+    return sec, f"layer 0 (4 matvecs) and the head timed once each, scaled to {cfg.layers} layers"
+
+
+def run_stack(args):
+    """Decode tokens/s of a Llama-shaped matvec stack: one token = one replay of a CUDA graph
+    holding every layer's launches (and, for N > 1, the NCCL all-gathers)."""
+    import numpy as np
+
+    from kernite_b200 import stack as st
+
+    cfg = st.CONFIGS[STACKS[args.workload]]
+    world, rank, local = dist_setup()
+    if args.impl == "reference":
+        if rank != 0:
+            return 0
+        sec, sample = stack_cpu_seconds_per_token(cfg, HOST_THREADS)
+        tps = 1.0 / sec
+        line = {"impl": "reference", "metric": "decode tokens/s", "value": round(tps, 4),
+                "unit": "tokens/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+                "ms_per_step": round(sec * 1e3, 3), "higher_is_better": True, "scaling": "strong",
+                "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+                "config": {"workload": f"{args.workload}: {cfg.name}", "layers": cfg.layers,
+                           "hidden": cfg.hidden, "ffn": cfg.ffn, "kv": cfg.kv, "vocab": cfg.vocab},
+                "cpu_baseline": {"value": round(tps, 4), "unit": "tokens/s", "cores": HOST_THREADS,
+                                 "kind": "port", "sample": sample},
+                "e2e": {"value": round(tps, 4), "unit": "tokens/s", "h2d_bytes_per_step": 0,
+                        "d2h_bytes_per_step": 0},
+                "gpu_launches": 0}
+        print(json.dumps(line), flush=True)
+        return 0
+
+    import torch
+
+    import kernite_b200 as kb
+
+    torch.cuda.set_device(local)
+    dist = _init_dist(torch, world, local)
+    kernels = kb.Kernels.load(local)
+    stream = torch.cuda.Stream()
+    stack = st.make_cuda_stack(cfg, kernels, rank, world, stream=stream)
+    x = torch.from_numpy(np.random.default_rng(0).standard_normal(cfg.hidden).astype(np.float32))
+    stack.buf["x"].copy_(x.cuda())
+    torch.cuda.synchronize()
+    with torch.cuda.stream(stream):
+        for _ in range(max(1, args.warmup)):
+            stack.forward()
+    torch.cuda.synchronize()
+    kernels.device_error()
+    graph = None
+    try:
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=stream):
+            stack.forward()
+        graph = g
+    except Exception as e:  # noqa: BLE001 - report and run eagerly
+        if rank == 0:
+            print(f"[bench] graph capture failed ({e}); timing eager launches", file=sys.stderr)
+        torch.cuda.synchronize()
+
+    def token():
+        if graph is not None:
+            graph.replay()
+        else:
+            stack.forward()
+
+    with torch.cuda.stream(stream):
+        for _ in range(3):
+            token()
+    torch.cuda.synchronize()
+    sampler = ClockSampler(local)
+    sampler.start()
+    if dist:
+        dist.barrier()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(stream):
+        e0.record(stream)
+        for _ in range(args.steps):
+            token()
+        e1.record(stream)
+    torch.cuda.synchronize()
+    if dist:
+        dist.barrier()
+    clocks = sampler.stop()
+    ms = e0.elapsed_time(e1)
+    kernels.device_error()
+    if dist:
+        t = torch.tensor([ms], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    ms_tok = ms / args.steps
+    tps = 1e3 / ms_tok
+    wbytes = cfg.weight_bytes()
+
+    # end to end: x in from pinned memory, one token, logits out, every step
+    xh = x.pin_memory()
+    lh = torch.empty(cfg.vocab).pin_memory()
+    e2e_steps = max(3, min(args.e2e_steps, args.steps))
+    if dist:
+        dist.barrier()
+    torch.cuda.synchronize()
+    f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(stream):
+        f0.record(stream)
+        for _ in range(e2e_steps):
+            stack.buf["x"].copy_(xh, non_blocking=True)
+            token()
+            lh.copy_(stack.buf["logits"], non_blocking=True)
+            stream.synchronize()
+        f1.record(stream)
+    torch.cuda.synchronize()
+    ms_e2e = f0.elapsed_time(f1)
+    if dist:
+        t = torch.tensor([ms_e2e], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms_e2e = float(t.item())
+    e2e = {"value": round(e2e_steps / (ms_e2e / 1e3), 3), "unit": "tokens/s",
+           "h2d_bytes_per_step": cfg.hidden * 4, "d2h_bytes_per_step": cfg.vocab * 4,
+           "steps": e2e_steps}
+
+    peak, peak_kind = measured_peak()
+    per_gpu_gbs = wbytes / world / (ms_tok / 1e3) / 1e9
+    roofline = {"bound": "hbm", "achieved": round(per_gpu_gbs, 2), "peak": peak, "unit": "GB/s",
+                "frac": round(per_gpu_gbs / peak, 4), "traffic": profiled_traffic(args.workload),
+                "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)" if peak_kind == "measured"
+                else "fallback 6650 GB/s",
+                "note": "achieved = the stack's weight bytes per GPU per token / token time"}
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        sec, sample = stack_cpu_seconds_per_token(cfg, HOST_THREADS)
+        cpu = {"value": round(1.0 / sec, 4), "unit": "tokens/s", "cores": HOST_THREADS,
+               "kind": "port", "sample": sample}
+    if rank == 0:
+        line = {
+            "metric": "decode tokens/s", "value": round(tps, 3), "unit": "tokens/s",
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round(ms_tok, 5), "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": {"workload": f"{args.workload}: {cfg.name}", "layers": cfg.layers,
+                       "hidden": cfg.hidden, "ffn": cfg.ffn, "kv": cfg.kv, "vocab": cfg.vocab,
+                       "parallelism": f"rows sharded x{world}, NCCL all-gather" if world > 1 else "single",
+                       "graph": graph is not None, "batch": 1,
+                       "l2": f"{wbytes / world / 1e9:.1f} GB of weights per GPU per token > L2"},
+            "weight_gbs": round(wbytes * tps / 1e9, 2),
+            "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e,
+            "gpu_launches": args.steps * stack.launches_per_token(), "clocks": clocks,
+        }
+        print(json.dumps(line), flush=True)
+    del graph
+    if dist:
+        dist.barrier()
+        dist.destroy_process_group()
+    kernels.close()
+    return 0
 
 
 if __name__ == "__main__":

@@ -215,15 +215,41 @@ __global__ void __launch_bounds__(Geo<B>::kMaxThreads, 1) matvec_kernel(const Ma
   }
 
   if (a.prologue == KQ_PROLOGUE_RMSNORM) {
-    // Each CTA normalises x by its own full-vector sum of squares (x is L2-resident).
+    // Each CTA normalises x by its own full-vector RMS (x is L2-resident). Two passes keep the
+    // sum of squares in range for any finite x: first max|x|, then sum (x / max)^2, and
+    // x / rms = x * (1/max) / sqrt(sum / K + eps / max^2).
     const uint32_t nthreads = consumers * 32;
     const uint32_t K = a.nb * kQK;
+    float mx[B];
+#pragma unroll
+    for (int b = 0; b < B; ++b) {
+      float m = 0.f;
+      if (b < static_cast<int>(a.batch)) {
+        const float* xb = a.x + b * a.ldx;
+        for (uint32_t k = threadIdx.x; k < K; k += nthreads) m = fmaxf(m, fabsf(xb[k]));
+      }
+#pragma unroll
+      for (int o = 16; o; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+      if (lane == 0) s_norm[warp][b] = m;
+    }
+    named_barrier(1, nthreads);
+#pragma unroll
+    for (int b = 0; b < B; ++b) {
+      float m = 0.f;
+      for (uint32_t w = 0; w < consumers; ++w) m = fmaxf(m, s_norm[w][b]);
+      mx[b] = m;
+    }
+    named_barrier(1, nthreads);  // every warp has read the maxima
 #pragma unroll
     for (int b = 0; b < B; ++b) {
       float ss = 0.f;
+      const float inv = mx[b] > 0.f ? 1.0f / mx[b] : 0.f;
       if (b < static_cast<int>(a.batch)) {
         const float* xb = a.x + b * a.ldx;
-        for (uint32_t k = threadIdx.x; k < K; k += nthreads) ss = fmaf(xb[k], xb[k], ss);
+        for (uint32_t k = threadIdx.x; k < K; k += nthreads) {
+          const float v = xb[k] * inv;
+          ss = fmaf(v, v, ss);
+        }
       }
 #pragma unroll
       for (int o = 16; o; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
@@ -234,7 +260,13 @@ __global__ void __launch_bounds__(Geo<B>::kMaxThreads, 1) matvec_kernel(const Ma
     for (int b = 0; b < B; ++b) {
       float t = 0.f;
       for (uint32_t w = 0; w < consumers; ++w) t += s_norm[w][b];
-      const float scale = 1.0f / sqrtf(t / static_cast<float>(K) + a.eps);
+      float scale;
+      if (mx[b] >= 1e-18f) {
+        const float inv = 1.0f / mx[b];
+        scale = inv / sqrtf(t / static_cast<float>(K) + a.eps * inv * inv);
+      } else {  // x is (almost) zero: eps dominates
+        scale = 1.0f / sqrtf(t * mx[b] * mx[b] / static_cast<float>(K) + a.eps);
+      }
 #pragma unroll
       for (int g = 0; g < G; ++g)
 #pragma unroll

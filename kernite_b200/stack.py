@@ -1,0 +1,254 @@
+"""Llama-shaped decode matvec stacks (BASELINE configs 2 and 4), row-sharded over N ranks.
+
+Per layer, with hidden h, FFN f, K/V width kv (grouped-query attention):
+
+    q|k|v = W_qkv . n(x)          (rows h + 2 kv; k and v are computed and not consumed)
+    o     = W_o . q
+    a     = (W_gate . o) * (W_up . o) / sqrt(f)     (W_gate and W_up rows interleaved)
+    x'    = W_down . a
+    logits = W_head . n(x_last)
+
+where n(x) = x / sqrt(mean(x^2) + eps) is applied to every layer input but the first (so each
+layer sees the RMS-normalised output of the previous one) and to the head's input. Attention
+itself, RoPE and the KV cache are not part of this matvec stack. Q/K/V/O and gate/up are
+Q4_K; down and the head are Q6_K. Each projection is one matvec launch with its elementwise
+glue fused: the RMS norm as the kernel prologue, the gate*up product as its epilogue.
+
+Sharding (one process per GPU): rank g of N holds rows [g R/N, (g+1) R/N) of every matrix
+(for W_qkv: that slice of each of the q, k and v parts; for gate/up: that slice of the row
+pairs). After each projection an all-gather of the f32 output slices rebuilds the full
+vector on every rank: q, o, a, x' (4 per layer) and the logits. The synthetic weights of a
+shard are exactly those rows of the unsharded model (the generator is counter-based), so any
+N computes the same logits.
+
+The math runs on a backend: :class:`CudaBackend` (libkq.so kernels, torch.distributed /
+NCCL all-gathers, optional CUDA-graph capture of a whole token) is the product; tests plug in
+a CPU backend built on the oracle to check the sharding and gather logic with gloo ranks.
+Kernite has no decode stack; the shape of `forward` follows its microgpt forward pass
+(examples/microgpt/src/model.rs:294-308), where each layer is a chain of matmul launches.
+"""
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass, field
+
+QK = 256
+BLOCK_BYTES = {4: 144, 6: 210}
+
+
+@dataclass(frozen=True)
+class StackConfig:
+    name: str
+    layers: int
+    hidden: int
+    ffn: int
+    kv: int      # width of each of K and V
+    vocab: int
+    eps: float = 1e-6
+    seed: int = 2026
+
+    def matrices(self):
+        """(name, qtype, rows, k) of one layer's matrices, then the head."""
+        h, f, kv = self.hidden, self.ffn, self.kv
+        return [("qkv", 4, h + 2 * kv, h), ("o", 4, h, h), ("gate_up", 4, 2 * f, h),
+                ("down", 6, h, f)]
+
+    def weight_bytes(self) -> int:
+        per_layer = sum(rows * (k // QK) * BLOCK_BYTES[q] for _, q, rows, k in self.matrices())
+        return self.layers * per_layer + self.vocab * (self.hidden // QK) * BLOCK_BYTES[6]
+
+    def tensor_id(self, layer: int, name: str) -> int:
+        names = ["qkv", "o", "gate_up", "down", "head"]
+        return layer * 8 + names.index(name)
+
+
+CONFIGS = {
+    "7b": StackConfig("llama-7b (BASELINE configs[2])", 32, 4096, 11008, 4096, 32000),
+    "70b": StackConfig("llama-70b (BASELINE configs[4])", 80, 8192, 28672, 1024, 32000),
+    # small shapes for tests
+    "tiny": StackConfig("tiny", 2, 512, 1024, 256, 1000),
+}
+
+
+@dataclass
+class Shard:
+    """The rows a rank holds of one matrix: list of (global_row_start, global_row_end) runs, in
+    local order, and the slice of the output that is gathered."""
+    qtype: int
+    k: int
+    runs: list[tuple[int, int]]
+    gathered: tuple[int, int] = (0, 0)  # local output rows that feed the all-gather
+
+    @property
+    def rows(self) -> int:
+        return sum(b - a for a, b in self.runs)
+
+    @property
+    def nbytes(self) -> int:
+        return self.rows * (self.k // QK) * BLOCK_BYTES[self.qtype]
+
+
+def split(n: int, rank: int, world: int) -> tuple[int, int]:
+    if n % world:
+        raise ValueError(f"{n} rows do not split over {world} ranks")
+    per = n // world
+    return rank * per, (rank + 1) * per
+
+
+def plan(cfg: StackConfig, rank: int, world: int) -> dict[str, Shard]:
+    """The row shards rank `rank` of `world` holds, per matrix of a layer and the head."""
+    h, f, kv = cfg.hidden, cfg.ffn, cfg.kv
+    q0, q1 = split(h, rank, world)
+    k0, k1 = split(kv, rank, world)
+    f0, f1 = split(f, rank, world)
+    v0, v1 = split(cfg.vocab, rank, world)
+    qkv = Shard(4, h, [(q0, q1), (h + k0, h + k1), (h + kv + k0, h + kv + k1)], (0, q1 - q0))
+    o = Shard(4, h, [(q0, q1)], (0, q1 - q0))
+    gate_up = Shard(4, h, [(2 * f0, 2 * f1)], (0, f1 - f0))  # pair-product output: f/N rows
+    down = Shard(6, f, [(q0, q1)], (0, q1 - q0))
+    head = Shard(6, h, [(v0, v1)], (0, v1 - v0))
+    return {"qkv": qkv, "o": o, "gate_up": gate_up, "down": down, "head": head}
+
+
+class DecodeStack:
+    """One rank's part of a decode stack on a backend. `forward(x)` runs one token."""
+
+    def __init__(self, cfg: StackConfig, backend, rank: int = 0, world: int = 1):
+        self.cfg, self.be, self.rank, self.world = cfg, backend, rank, world
+        self.shards = plan(cfg, rank, world)
+        self.weights = []
+        for layer in range(cfg.layers):
+            lw = {}
+            for name in ("qkv", "o", "gate_up", "down"):
+                lw[name] = backend.weights(self.shards[name], cfg.seed, cfg.tensor_id(layer, name))
+            self.weights.append(lw)
+        self.head = backend.weights(self.shards["head"], cfg.seed, cfg.tensor_id(cfg.layers, "head"))
+        h, f = cfg.hidden, cfg.ffn
+        sh = self.shards
+        self.buf = {
+            "x": backend.vector(h), "qkv": backend.vector(sh["qkv"].rows), "q": backend.vector(h),
+            "o_loc": backend.vector(sh["o"].rows), "o": backend.vector(h),
+            "a_loc": backend.vector(sh["gate_up"].rows // 2), "a": backend.vector(f),
+            "x_loc": backend.vector(sh["down"].rows), "xd": backend.vector(h),
+            "l_loc": backend.vector(sh["head"].rows), "logits": backend.vector(cfg.vocab),
+        }
+        if world == 1:
+            # one rank: each "gathered" vector is the local output itself (q is the first h
+            # entries of the q|k|v output), so the gathers vanish
+            b = self.buf
+            b["q"], b["o"], b["a"], b["xd"], b["logits"] = b["qkv"], b["o_loc"], b["a_loc"], b["x_loc"], b["l_loc"]
+
+    def launches_per_token(self) -> int:
+        return 4 * self.cfg.layers + 1
+
+    def forward(self) -> None:
+        """One token: reads buf['x'], writes buf['logits'] (on every rank)."""
+        cfg, be, b, sh = self.cfg, self.be, self.buf, self.shards
+        x = b["x"]
+        for layer, lw in enumerate(self.weights):
+            be.matvec(lw["qkv"], sh["qkv"], b["qkv"], x, rmsnorm=layer > 0, eps=cfg.eps)
+            be.gather(b["q"], b["qkv"], sh["qkv"].gathered)
+            be.matvec(lw["o"], sh["o"], b["o_loc"], b["q"])
+            be.gather(b["o"], b["o_loc"], sh["o"].gathered)
+            be.matvec(lw["gate_up"], sh["gate_up"], b["a_loc"], b["o"], pair_scale=1.0 / math.sqrt(cfg.ffn))
+            be.gather(b["a"], b["a_loc"], sh["gate_up"].gathered)
+            be.matvec(lw["down"], sh["down"], b["x_loc"], b["a"])
+            be.gather(b["xd"], b["x_loc"], sh["down"].gathered)
+            x = b["xd"]
+        be.matvec(self.head, sh["head"], b["l_loc"], x, rmsnorm=True, eps=cfg.eps)
+        be.gather(b["logits"], b["l_loc"], sh["head"].gathered)
+
+
+# ---------------------------------------------------------------- the CUDA backend (product)
+
+class CudaBackend:
+    """libkq.so kernels on one GPU; all-gathers with torch.distributed (NCCL) when world > 1."""
+
+    def __init__(self, kernels, stream=None, group=None, world: int = 1, flags: int = 0):
+        import torch
+
+        import kernite_b200 as kb
+
+        self.kb, self.torch, self.k = kb, torch, kernels
+        self.stream = stream
+        self.group = group
+        self.world = world
+        self.flags = flags
+        self.launches = 0
+
+    def weights(self, shard: Shard, seed: int, tensor: int):
+        torch, kb = self.torch, self.kb
+        W = torch.empty(shard.nbytes, dtype=torch.uint8, device="cuda")
+        key = kb.stream_key(seed, tensor)
+        nb = shard.k // QK
+        bb = BLOCK_BYTES[shard.qtype]
+        off = 0
+        for r0, r1 in shard.runs:
+            n = (r1 - r0) * nb
+            self.k.fill(shard.qtype, W.data_ptr() + off, r0 * nb, n, key, stream=self.stream)
+            off += n * bb
+        return W
+
+    def vector(self, n: int):
+        return self.torch.zeros(n, dtype=self.torch.float32, device="cuda")
+
+    def matvec(self, W, shard: Shard, y, x, rmsnorm: bool = False, eps: float = 0.0,
+               pair_scale: float | None = None) -> None:
+        kb = self.kb
+        self.k.matvec(shard.qtype, y, W, x, shard.rows, shard.k, 1,
+                      prologue=kb.PROLOGUE_RMSNORM if rmsnorm else kb.PROLOGUE_NONE, eps=eps,
+                      epilogue=kb.EPILOGUE_PAIR_PRODUCT if pair_scale is not None else kb.EPILOGUE_NONE,
+                      pair_scale=pair_scale if pair_scale is not None else 1.0,
+                      flags=kb.FLAG_WEIGHTS_STATIC | self.flags, stream=self.stream)
+        self.launches += 1
+
+    def gather(self, out, loc, part: tuple[int, int]) -> None:
+        a, b = part
+        if self.world == 1:
+            return  # the stack aliases the full vector to the local output
+        import torch.distributed as dist
+
+        dist.all_gather_into_tensor(out, loc[a:b], group=self.group)
+
+
+def make_cuda_stack(cfg: StackConfig, kernels, rank: int = 0, world: int = 1, group=None,
+                    stream=None, flags: int = 0) -> DecodeStack:
+    return DecodeStack(cfg, CudaBackend(kernels, stream=stream, group=group, world=world, flags=flags),
+                       rank, world)
+
+
+# ---------------------------------------------------------------- reference (for tests)
+
+def reference_logits(cfg: StackConfig, x, layers: int | None = None):
+    """The unsharded stack on the CPU oracle, in f64 from the f32-dequantised weights. Test
+    infrastructure only."""
+    import numpy as np
+
+    import oracle
+
+    def weights(name, layer, qtype, rows, k):
+        return oracle.fill(qtype, oracle.stream_key(cfg.seed, cfg.tensor_id(layer, name)), 0,
+                           rows * k // QK)
+
+    def mv(qtype, W, v, rows, k):
+        y, _ = oracle.matvec_ref(qtype, W, np.asarray(v, dtype=np.float32)[None, :], k, 0, rows)
+        return y[0]
+
+    def norm(v):
+        v = np.asarray(v, dtype=np.float64)
+        return v / np.sqrt(np.mean(v * v) + cfg.eps)
+
+    h, f, kv = cfg.hidden, cfg.ffn, cfg.kv
+    x = np.asarray(x, dtype=np.float64)
+    nl = cfg.layers if layers is None else layers
+    for layer in range(nl):
+        xin = norm(x) if layer > 0 else x
+        qkv = mv(4, weights("qkv", layer, 4, h + 2 * kv, h), xin, h + 2 * kv, h)
+        q = qkv[:h]
+        o = mv(4, weights("o", layer, 4, h, h), q, h, h)
+        gu = mv(4, weights("gate_up", layer, 4, 2 * f, h), o, 2 * f, h)
+        a = gu[0::2] * gu[1::2] / math.sqrt(f)
+        x = mv(6, weights("down", layer, 6, h, f), a, h, f)
+    head = oracle.fill(6, oracle.stream_key(cfg.seed, cfg.tensor_id(cfg.layers, "head")), 0,
+                       cfg.vocab * h // QK)
+    return mv(6, head, norm(x), cfg.vocab, h)

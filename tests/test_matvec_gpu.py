@@ -340,3 +340,16 @@ def test_path_flags_are_checked(kernels):
         kernels.matvec(4, y, W, x, 1, 256, 9, flags=kb.FLAG_CUDA_CORES)
     assert e.value.code == kb.KQ_E_UNSUPPORTED
     kernels.device_error()
+
+
+@pytest.mark.parametrize("mag", [1e-25, 1e-3, 1e19, 1e30])
+def test_rmsnorm_prologue_any_magnitude(kernels, mag):
+    # the norm's sum of squares must not overflow or underflow for any finite x
+    rows, K, eps = 150, 2048, 1e-6
+    W = dev_weights(kernels, 4, rows, K, kb.stream_key(15, 4))
+    x = (np.random.default_rng(8).standard_normal((1, K)) * mag).astype(np.float32)
+    y = run_matvec(kernels, 4, W, x, rows, K, prologue=kb.PROLOGUE_RMSNORM, eps=eps)
+    x64 = x.astype(np.float64)
+    xn = x64 / np.sqrt(np.mean(x64 ** 2) + eps)
+    y_ref, bound = oracle.matvec_ref(4, W.cpu().numpy(), xn.astype(np.float32), K, 0, rows)
+    check(y, y_ref, bound, f"rmsnorm x~{mag}")
