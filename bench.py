@@ -509,16 +509,15 @@ def run_stack(args):
             stack.forward()
     torch.cuda.synchronize()
     kernels.device_error()
-    graph = None
+    graph = torch.cuda.CUDAGraph()
     try:
-        g = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(g, stream=stream):
+        with torch.cuda.graph(graph, stream=stream):
             stack.forward()
-        graph = g
     except Exception as e:  # noqa: BLE001 - report and run eagerly
         if rank == 0:
             print(f"[bench] graph capture failed ({e}); timing eager launches", file=sys.stderr)
         torch.cuda.synchronize()
+        graph = None
 
     def token():
         if graph is not None:
@@ -609,7 +608,12 @@ def run_stack(args):
             "gpu_launches": args.steps * stack.launches_per_token(), "clocks": clocks,
         }
         print(json.dumps(line), flush=True)
-    del graph
+    # A graph holding NCCL calls must be released before the process group goes, or the
+    # teardown waits for good.
+    torch.cuda.synchronize()
+    if graph is not None:
+        graph.reset()
+    graph = None
     if dist:
         dist.barrier()
         dist.destroy_process_group()
