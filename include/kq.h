@@ -148,6 +148,25 @@ int kq_fill_q6k(kq_ctx* ctx, uint64_t w, uint64_t block0, uint64_t nblocks, uint
 /* The stream key of tensor `tensor` under `seed` (host function; the same as the oracle's). */
 uint64_t kq_stream_key(uint64_t seed, uint64_t tensor);
 
+/* The tensor-core Q4_K matvec of kq_matvec_q4k (batch 1..64) for callers that cannot allocate
+ * device memory: code running while a CUDA graph is being captured, a serving process whose
+ * memory pool has already reserved the GPU, or a latency-critical path where a cudaMalloc
+ * would stall. It takes no kq_ctx (creating one allocates) and calls no cudaMalloc, cudaFree
+ * or other allocating routine. No counterpart in the reference: kernite always allocates
+ * through Cuda::alloc.
+ *   - Its scratch (X in f16, k * npad * 2 bytes, npad = batch rounded up to 16, 32 or 64) is a
+ *     static 1 MiB device array that every GPU loading the library holds until the process
+ *     exits; larger requests (k > 32768 up to batch 16, > 16384 up to 32, > 8192 up to 64) are
+ *     rejected with KQ_E_INVALID and a message saying so.
+ *   - All calls share that array and it keeps the last call's contents; each call rewrites all
+ *     of it that it reads. Calls that overlap on the GPU (different streams, or different host
+ *     threads) race on it: serialise them.
+ *   - The first call on a device sets that device up (attributes, kernel limits, the array's
+ *     device address) with the device current; make it before any stream capture.
+ * y is batch x rows f32 (row stride rows), x is batch x k f32 (stride k), W as kq_matvec_q4k. */
+int kq_matvec_q4k_noalloc(uint64_t y, uint64_t w, uint64_t x, uint32_t rows, uint32_t k,
+                          uint32_t batch, kq_stream stream);
+
 #ifdef __cplusplus
 }
 #endif

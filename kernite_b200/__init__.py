@@ -51,7 +51,7 @@ QK = 256
 EXPORTS = (
     "kq_ctx_create", "kq_ctx_destroy", "kq_last_error", "kq_ctx_info", "kq_device_error",
     "kq_matvec_q4k", "kq_matvec_q6k", "kq_matvec", "kq_dequant_q4k", "kq_dequant_q6k",
-    "kq_fill_q4k", "kq_fill_q6k", "kq_stream_key",
+    "kq_fill_q4k", "kq_fill_q6k", "kq_stream_key", "kq_matvec_q4k_noalloc",
 )
 
 
@@ -104,6 +104,7 @@ def lib() -> ctypes.CDLL:
         getattr(L, name).argtypes = [vp, u64, u64, u64, u64, vp]
     L.kq_stream_key.argtypes = [u64, u64]
     L.kq_stream_key.restype = u64
+    L.kq_matvec_q4k_noalloc.argtypes = [u64, u64, u64, u32, u32, u32, vp]
     for name in EXPORTS:
         fn = getattr(L, name)
         if name not in ("kq_last_error", "kq_stream_key"):
@@ -238,6 +239,12 @@ class Kernels:
         """Synthetic blocks [block0, block0 + nblocks) of the keyed tensor, written at w."""
         fn = lib().kq_fill_q4k if qtype in (4, TYPE_Q4_K) else lib().kq_fill_q6k
         _check(fn(self._ctx, _addr(w), block0, nblocks, key & (2**64 - 1), _stream(stream)), "kq_fill")
+
+    def matvec_q4k_noalloc(self, y, w, x, rows: int, k: int, batch: int = 1, stream=None) -> None:
+        """The tensor-core Q4_K matvec without any device allocation (static scratch); see
+        ``kq_matvec_q4k_noalloc`` in include/kq.h. Uses the current device."""
+        _check(lib().kq_matvec_q4k_noalloc(_addr(y), _addr(w), _addr(x), rows, k, batch,
+                                           _stream(stream)), "kq_matvec_q4k_noalloc")
 
     def device_error(self) -> None:
         """Synchronises the GPU and raises if a kernel's bounded wait gave up."""

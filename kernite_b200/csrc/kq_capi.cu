@@ -37,6 +37,14 @@ int cuda_fail(cudaError_t e, const char* call, const std::string& detail) {
   return static_cast<int>(e);
 }
 
+int error_word_address(unsigned** out) {
+  void* p = nullptr;
+  const cudaError_t e = cudaGetSymbolAddress(&p, g_kq_error_word);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaGetSymbolAddress", "device error word");
+  *out = static_cast<unsigned*>(p);
+  return KQ_OK;
+}
+
 int enter(const kq_ctx* ctx) {
   int cur = -1;
   cudaError_t e = cudaGetDevice(&cur);

@@ -27,6 +27,8 @@ constexpr uint64_t kCtxScratchBytes = 4ull << 20;
 int fail(int code, const char* call, const std::string& detail);
 // Records a CUDA error as "<call>: <NAME> (<n>): <meaning>[: detail]" and returns its number.
 int cuda_fail(cudaError_t e, const char* call, const std::string& detail = std::string());
+// The current device's address of the library's device error word.
+int error_word_address(unsigned** out);
 // Makes the ctx's device current if it is not.
 int enter(const kq_ctx* ctx);
 

@@ -29,6 +29,8 @@
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <mutex>
+#include <string>
 
 #include "kq_device.cuh"
 #include "kq_internal.h"
@@ -426,3 +428,126 @@ int mma_matvec(kq_ctx* ctx, const kq_matvec_desc& d, uint64_t ldx, uint64_t ldy,
 }
 
 }  // namespace kq
+
+// ------------------------------------------------------------------------------------------------
+// kq_matvec_q4k_noalloc: the tensor-core Q4_K matvec for callers that cannot allocate device
+// memory -- code that runs while a CUDA graph is being captured, inside a server whose memory
+// pool has already reserved the GPU, or anywhere a cudaMalloc would stall a latency budget. It
+// needs no kq_ctx (whose creation allocates scratch): the X scratch lives in the file-scope
+// array below, which every GPU that loads this library holds until the process exits.
+
+namespace {
+
+// 1 MiB: the f16 B operand of one call, k * (batch rounded up to 16, 32 or 64) * 2 bytes.
+constexpr uint64_t kNoAllocScratchBytes = 1ull << 20;
+static __device__ __align__(256) uint8_t g_noalloc_scratch[kNoAllocScratchBytes];
+
+constexpr int kMaxDevices = 64;
+struct NoAllocDevice {
+  bool ready = false;
+  int sm_count = 0;
+  void* scratch = nullptr;  // device address of g_noalloc_scratch on this GPU
+  unsigned* err = nullptr;  // device address of the library's error word on this GPU
+};
+NoAllocDevice g_noalloc_devices[kMaxDevices];
+std::mutex g_noalloc_mutex;
+
+// Set-up, once per device, with that device current: attributes, the kernels' shared-memory
+// limit, and the device addresses of the static scratch and of the error word. The names of
+// those arrays are host-side stand-ins in host code, so only cudaGetSymbolAddress gives an
+// address a kernel may use.
+int noalloc_setup(int dev, NoAllocDevice** out) {
+  std::lock_guard<std::mutex> lock(g_noalloc_mutex);
+  NoAllocDevice& d = g_noalloc_devices[dev];
+  if (!d.ready) {
+    int major = 0, minor = 0;
+    cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev);
+    cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, dev);
+    if (major != 10 || minor != 0)
+      return kq::fail(KQ_E_UNSUPPORTED, "kq_matvec_q4k_noalloc", "this library is built for sm_100a (B200)");
+    cudaError_t e = cudaDeviceGetAttribute(&d.sm_count, cudaDevAttrMultiProcessorCount, dev);
+    if (e != cudaSuccess) return kq::cuda_fail(e, "cudaDeviceGetAttribute");
+    for (uint32_t n : {16u, 32u, 64u}) {
+      const void* fn = n == 16 ? kq::mma_fn<16>() : n == 32 ? kq::mma_fn<32>() : kq::mma_fn<64>();
+      e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, kq::smem_for(n));
+      if (e != cudaSuccess) return kq::cuda_fail(e, "cudaFuncSetAttribute", "tensor-core matvec kernel");
+    }
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+    if (e != cudaSuccess) return kq::cuda_fail(e, "cudaGetSymbolAddress", "static scratch");
+    d.scratch = p;
+    const int rc = kq::error_word_address(&d.err);
+    if (rc) return rc;
+    d.ready = true;
+  }
+  *out = &d;
+  return KQ_OK;
+}
+
+}  // namespace
+
+extern "C" int kq_matvec_q4k_noalloc(uint64_t y, uint64_t w, uint64_t x, uint32_t rows, uint32_t k,
+                                     uint32_t batch, kq_stream stream) {
+  const char* call = "kq_matvec_q4k_noalloc";
+  if (rows == 0 || k == 0 || k % kq::kQK != 0)
+    return kq::fail(KQ_E_INVALID, call, "rows must be > 0 and k a positive multiple of 256");
+  if (batch < 1 || batch > 64) return kq::fail(KQ_E_INVALID, call, "batch must be 1..64");
+  if (!w || !x || !y) return kq::fail(KQ_E_INVALID, call, "null pointer");
+  if (w % 16 || x % 16 || y % 4)
+    return kq::fail(KQ_E_INVALID, call, "w and x must be 16-byte aligned, y 4-byte aligned");
+  const uint64_t need = kq::mma_scratch_bytes(k, batch);
+  if (need > kNoAllocScratchBytes)
+    return kq::fail(KQ_E_INVALID, call,
+                    "k " + std::to_string(k) + " at batch " + std::to_string(batch) + " needs " +
+                        std::to_string(need) + " bytes of scratch, past the static " +
+                        std::to_string(kNoAllocScratchBytes) +
+                        " (k <= 32768 up to batch 16, 16384 up to 32, 8192 up to 64)");
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return kq::cuda_fail(e, "cudaGetDevice");
+  if (dev < 0 || dev >= kMaxDevices) return kq::fail(KQ_E_UNSUPPORTED, call, "device ordinal past 63");
+  NoAllocDevice* d = nullptr;
+  int rc = noalloc_setup(dev, &d);
+  if (rc) return rc;
+
+  const uint32_t npad = kq::npad_for(batch);
+  const uint32_t nb = k / kq::kQK;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  const cudaStream_t s = static_cast<cudaStream_t>(stream);
+  {
+    const uint32_t total = nb * 32 * npad;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(std::min<uint32_t>((total + 255) / 256, d->sm_count * 4));
+    cfg.blockDim = dim3(256);
+    cfg.stream = s;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    e = cudaLaunchKernelEx(&cfg, kq::xperm_kernel, reinterpret_cast<uint4*>(d->scratch),
+                           reinterpret_cast<const float*>(x), uint64_t(k), nb, batch, npad);
+    if (e != cudaSuccess) return kq::cuda_fail(e, "cudaLaunchKernelEx", "X pre-pass");
+  }
+  kq::MmaArgs args;
+  args.W = reinterpret_cast<const uint8_t*>(w);
+  args.xp = static_cast<const uint8_t*>(d->scratch);
+  args.y = reinterpret_cast<float*>(y);
+  args.err = d->err;
+  args.ldy = rows;
+  args.rows = rows;
+  args.nb = nb;
+  args.batch = batch;
+  args.flags = 0;
+  const void* fn = npad == 16 ? kq::mma_fn<16>() : npad == 32 ? kq::mma_fn<32>() : kq::mma_fn<64>();
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(std::min<uint32_t>(d->sm_count, rows));
+  cfg.blockDim = dim3(kq::kThreads);
+  cfg.dynamicSmemBytes = kq::smem_for(npad);
+  cfg.stream = s;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  void* params[] = {&args};
+  e = cudaLaunchKernelExC(&cfg, fn, params);
+  if (e != cudaSuccess) return kq::cuda_fail(e, "cudaLaunchKernelExC", "tensor-core matvec");
+  return KQ_OK;
+}
