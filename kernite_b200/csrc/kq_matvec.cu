@@ -32,7 +32,7 @@
 
 // 1: accumulate with packed f32x2 FMAs (two weights an instruction); 0: scalar FMAs.
 #ifndef KQ_PACKED_FMA
-#define KQ_PACKED_FMA 1
+#define KQ_PACKED_FMA 0
 #endif
 
 namespace kq {
@@ -575,8 +575,16 @@ Instance pick(int qt, int bt) {
   }
 }
 
-constexpr uint32_t kRingBudget = 160 * 1024;  // bytes of ring per CTA we aim for
-constexpr uint64_t kTileTarget = 24 * 1024;   // bytes per tile we aim for
+// Tiles of ~96 KB in a ring of ~210 KB: fewer, larger tiles amortise the per-tile hand-offs
+// (mbarrier waits, the team barrier and reduction), which measured faster than 24-64 KB tiles.
+#ifndef KQ_TILE_KB
+#define KQ_TILE_KB 96
+#endif
+#ifndef KQ_RING_KB
+#define KQ_RING_KB 210
+#endif
+constexpr uint32_t kRingBudget = KQ_RING_KB * 1024;  // bytes of ring per CTA we aim for
+constexpr uint64_t kTileTarget = KQ_TILE_KB * 1024;  // bytes per tile we aim for
 
 }  // namespace
 
