@@ -61,6 +61,8 @@ def parse_args(argv=None):
     ap.add_argument("--path", default="auto", choices=["auto", "tc", "cc"],
                     help="tensor cores, CUDA cores, or the library's choice")
     ap.add_argument("--impl", default="kq", choices=["kq", "reference"])
+    ap.add_argument("--exchange", default="nccl", choices=["nccl", "push"],
+                    help="sharded stacks: NCCL all-gathers, or the matvec's own push to peer memory")
     ap.add_argument("--e2e-steps", type=int, default=2000, help="steps of the end-to-end leg")
     ap.add_argument("--cpu-seconds", type=float, default=12.0, help="CPU-baseline time budget")
     ap.add_argument("--no-cpu-baseline", action="store_true")
@@ -500,7 +502,8 @@ def run_stack(args):
     dist = _init_dist(torch, world, local)
     kernels = kb.Kernels.load(local)
     stream = torch.cuda.Stream()
-    stack = st.make_cuda_stack(cfg, kernels, rank, world, stream=stream)
+    push = args.exchange == "push" and world > 1
+    stack = st.make_cuda_stack(cfg, kernels, rank, world, stream=stream, push=push)
     x = torch.from_numpy(np.random.default_rng(0).standard_normal(cfg.hidden).astype(np.float32))
     stack.buf["x"].copy_(x.cuda())
     torch.cuda.synchronize()
@@ -600,7 +603,8 @@ def run_stack(args):
             "vs_baseline": None, "dtype": "f32", "data": "synthetic",
             "config": {"workload": f"{args.workload}: {cfg.name}", "layers": cfg.layers,
                        "hidden": cfg.hidden, "ffn": cfg.ffn, "kv": cfg.kv, "vocab": cfg.vocab,
-                       "parallelism": f"rows sharded x{world}, NCCL all-gather" if world > 1 else "single",
+                       "parallelism": (f"rows sharded x{world}, " + ("push to peer memory" if push else
+                                       "NCCL all-gather")) if world > 1 else "single",
                        "graph": graph is not None, "batch": 1,
                        "l2": f"{wbytes / world / 1e9:.1f} GB of weights per GPU per token > L2"},
             "weight_gbs": round(wbytes * tps / 1e9, 2),
@@ -614,6 +618,8 @@ def run_stack(args):
     if graph is not None:
         graph.reset()
     graph = None
+    if push:
+        stack.be.close()
     if dist:
         dist.barrier()
         dist.destroy_process_group()

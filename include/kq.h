@@ -148,6 +148,47 @@ int kq_fill_q6k(kq_ctx* ctx, uint64_t w, uint64_t block0, uint64_t nblocks, uint
 /* The stream key of tensor `tensor` under `seed` (host function; the same as the oracle's). */
 uint64_t kq_stream_key(uint64_t seed, uint64_t tensor);
 
+/* ---- Row-sharded stacks: a matvec whose epilogue also pushes its outputs to other GPUs ----
+ *
+ * With the rows of a matrix split over N GPUs, every GPU needs the whole output vector for the
+ * next matvec. kq_matvec_push does the exchange inside the matvec: each output row r <
+ * push_rows is also stored at y[p] + r for every p < npush (the full-vector buffers of all
+ * ranks, this one included, mapped with kq_peer_open), and each CTA, once its rows are stored
+ * everywhere, adds its row count to counter[p] with a system-scope fence before it. A launch
+ * whose x is such a full vector first waits (bounded, acquire) until its rank's counter
+ * wait_counter reaches (*epoch - 1) * wait_mul + wait_add, then reads x through L2. Batch 1,
+ * CUDA-core kernel. No reference counterpart: kernite has no collective; its only inter-GPU
+ * operation is Buffer::copy_from over cuMemcpyPeer (crates/cuda/src/lib.rs:405-439). */
+typedef struct kq_push_desc {
+    uint32_t npush;        /* ranks to store to (0..8) */
+    uint32_t push_rows;    /* output rows (in output units) that are pushed: rows [0, push_rows) */
+    uint64_t y[8];         /* per rank: address of this rank's slice in that rank's full vector */
+    uint64_t counter[8];   /* per rank: its arrival counter (u64) for that full vector */
+    uint64_t wait_counter; /* 0, or this rank's counter for x (u64) */
+    uint64_t epoch;        /* address of this rank's token counter (u64), read on the device */
+    uint64_t wait_mul, wait_add;
+} kq_push_desc;
+
+int kq_matvec_push(kq_ctx* ctx, const kq_matvec_desc* desc, const kq_push_desc* push,
+                   kq_stream stream);
+
+/* Stream-ordered wait (one thread, bounded, acquire) until *counter >= (*epoch - 1) * wait_mul +
+ * wait_add, for a caller that reads a pushed full vector with its own code (the last one of a
+ * step, which no later kq_matvec_push waits for). A wait that gives up sets the device error
+ * word (kq_device_error) and returns, so the stream goes on. */
+int kq_wait_counter(kq_ctx* ctx, uint64_t counter, uint64_t epoch, uint64_t wait_mul,
+                    uint64_t wait_add, kq_stream stream);
+
+/* Device memory other GPUs can map: cudaMalloc'd, zeroed, with its CUDA IPC handle (64 bytes)
+ * written to ipc_handle. Replaces the peer side of Buffer::copy_from (crates/cuda/src/lib.rs:
+ * 405-439), which copies through cuMemcpyPeer instead of mapping. */
+int kq_peer_alloc(kq_ctx* ctx, uint64_t bytes, uint64_t* ptr, void* ipc_handle);
+/* Maps another process's kq_peer_alloc memory from its IPC handle (peer access enabled). */
+int kq_peer_open(kq_ctx* ctx, const void* ipc_handle, uint64_t* ptr);
+/* Unmaps memory kq_peer_open mapped / frees memory kq_peer_alloc allocated. */
+int kq_peer_close(kq_ctx* ctx, uint64_t ptr);
+int kq_peer_free(kq_ctx* ctx, uint64_t ptr);
+
 /* The tensor-core Q4_K matvec of kq_matvec_q4k (batch 1..64) for callers that cannot allocate
  * device memory: code running while a CUDA graph is being captured, a serving process whose
  * memory pool has already reserved the GPU, or a latency-critical path where a cudaMalloc

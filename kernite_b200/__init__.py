@@ -52,6 +52,7 @@ EXPORTS = (
     "kq_ctx_create", "kq_ctx_destroy", "kq_last_error", "kq_ctx_info", "kq_device_error",
     "kq_matvec_q4k", "kq_matvec_q6k", "kq_matvec", "kq_dequant_q4k", "kq_dequant_q6k",
     "kq_fill_q4k", "kq_fill_q6k", "kq_stream_key", "kq_matvec_q4k_noalloc",
+    "kq_matvec_push", "kq_wait_counter", "kq_peer_alloc", "kq_peer_open", "kq_peer_close", "kq_peer_free",
 )
 
 
@@ -75,6 +76,17 @@ class KqMatvecDesc(ctypes.Structure):
         ("pair_scale", ctypes.c_float), ("flags", ctypes.c_uint32), ("reserved", ctypes.c_uint32),
     ]
 
+
+class KqPushDesc(ctypes.Structure):
+    _fields_ = [
+        ("npush", ctypes.c_uint32), ("push_rows", ctypes.c_uint32),
+        ("y", ctypes.c_uint64 * 8), ("counter", ctypes.c_uint64 * 8),
+        ("wait_counter", ctypes.c_uint64), ("epoch", ctypes.c_uint64),
+        ("wait_mul", ctypes.c_uint64), ("wait_add", ctypes.c_uint64),
+    ]
+
+
+IPC_HANDLE_BYTES = 64
 
 _lib: ctypes.CDLL | None = None
 
@@ -105,6 +117,12 @@ def lib() -> ctypes.CDLL:
     L.kq_stream_key.argtypes = [u64, u64]
     L.kq_stream_key.restype = u64
     L.kq_matvec_q4k_noalloc.argtypes = [u64, u64, u64, u32, u32, u32, vp]
+    L.kq_matvec_push.argtypes = [vp, ctypes.POINTER(KqMatvecDesc), ctypes.POINTER(KqPushDesc), vp]
+    L.kq_wait_counter.argtypes = [vp, u64, u64, u64, u64, vp]
+    L.kq_peer_alloc.argtypes = [vp, u64, ctypes.POINTER(u64), ctypes.c_char_p]
+    L.kq_peer_open.argtypes = [vp, ctypes.c_char_p, ctypes.POINTER(u64)]
+    L.kq_peer_close.argtypes = [vp, u64]
+    L.kq_peer_free.argtypes = [vp, u64]
     for name in EXPORTS:
         fn = getattr(L, name)
         if name not in ("kq_last_error", "kq_stream_key"):
@@ -246,9 +264,53 @@ class Kernels:
         _check(lib().kq_matvec_q4k_noalloc(_addr(y), _addr(w), _addr(x), rows, k, batch,
                                            _stream(stream)), "kq_matvec_q4k_noalloc")
 
+    def matvec_push(self, qtype: int, y, w, x, rows: int, k: int, push: "KqPushDesc", *,
+                    prologue: int = PROLOGUE_NONE, epilogue: int = EPILOGUE_NONE, eps: float = 0.0,
+                    pair_scale: float = 1.0, flags: int = 0, stream=None) -> None:
+        """Batch-1 matvec whose epilogue also stores rows [0, push.push_rows) into every rank's
+        full vector and counts them there (``kq_matvec_push``)."""
+        t = {4: TYPE_Q4_K, 6: TYPE_Q6_K}.get(qtype, qtype)
+        d = KqMatvecDesc(type=t, rows=rows, k=k, batch=1, y=_addr(y), w=_addr(w), x=_addr(x),
+                         ldx=0, ldy=0, prologue=prologue, epilogue=epilogue, eps=eps,
+                         pair_scale=pair_scale, flags=flags, reserved=0)
+        _check(lib().kq_matvec_push(self._ctx, ctypes.byref(d), ctypes.byref(push), _stream(stream)),
+               "kq_matvec_push")
+
+    def wait_counter(self, counter: int, epoch: int, wait_mul: int, wait_add: int, stream=None) -> None:
+        """Stream-ordered bounded wait until *counter >= (*epoch - 1) * wait_mul + wait_add."""
+        _check(lib().kq_wait_counter(self._ctx, counter, epoch, wait_mul, wait_add, _stream(stream)),
+               "kq_wait_counter")
+
+    def peer_alloc(self, nbytes: int) -> tuple[int, bytes]:
+        """Zeroed device memory other GPUs can map; returns (address, 64-byte IPC handle)."""
+        ptr = ctypes.c_uint64()
+        h = ctypes.create_string_buffer(IPC_HANDLE_BYTES)
+        _check(lib().kq_peer_alloc(self._ctx, nbytes, ctypes.byref(ptr), h), "kq_peer_alloc")
+        return ptr.value, h.raw
+
+    def peer_open(self, handle: bytes) -> int:
+        ptr = ctypes.c_uint64()
+        _check(lib().kq_peer_open(self._ctx, handle, ctypes.byref(ptr)), "kq_peer_open")
+        return ptr.value
+
+    def peer_close(self, ptr: int) -> None:
+        _check(lib().kq_peer_close(self._ctx, ptr), "kq_peer_close")
+
+    def peer_free(self, ptr: int) -> None:
+        _check(lib().kq_peer_free(self._ctx, ptr), "kq_peer_free")
+
     def device_error(self) -> None:
         """Synchronises the GPU and raises if a kernel's bounded wait gave up."""
         _check(lib().kq_device_error(self._ctx), "kq_device_error")
+
+
+class DeviceArray:
+    """A view of raw device memory that torch (and others) can wrap without a copy through
+    ``__cuda_array_interface__``: ``torch.as_tensor(DeviceArray(ptr, n), device="cuda")``."""
+
+    def __init__(self, ptr: int, n: int, typestr: str = "<f4"):
+        self.__cuda_array_interface__ = {"shape": (n,), "typestr": typestr, "data": (ptr, False),
+                                         "version": 3, "strides": None, "stream": None}
 
 
 def block_bytes(qtype: int) -> int:

@@ -146,7 +146,24 @@ uint64_t stream_key(uint64_t seed, uint64_t tensor) {
   return mix64(mix64(seed * 0xd1342543de82ef95ull + tensor) ^ 0x632be59bd9b4e019ull);
 }
 
+__global__ void wait_counter_kernel(unsigned* err, const unsigned long long* cnt,
+                                    const unsigned long long* epoch, uint64_t mul, uint64_t add) {
+  wait_count(err, cnt, epoch, mul, add);
+}
+
 int aux_prepare(kq_ctx*) { return KQ_OK; }
+
+int wait_counter(kq_ctx* ctx, uint64_t counter, uint64_t epoch, uint64_t mul, uint64_t add,
+                 cudaStream_t s) {
+  const char* call = "kq_wait_counter";
+  if (!counter || !epoch || counter % 8 || epoch % 8)
+    return fail(KQ_E_INVALID, call, "counter and epoch must be non-null and 8-byte aligned");
+  wait_counter_kernel<<<1, 1, 0, s>>>(ctx->err, reinterpret_cast<const unsigned long long*>(counter),
+                                      reinterpret_cast<const unsigned long long*>(epoch), mul, add);
+  const cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "cudaLaunchKernel", call);
+  return KQ_OK;
+}
 
 int dequant(kq_ctx* ctx, int type, uint64_t out, uint64_t w, uint64_t nblocks, cudaStream_t s) {
   const char* call = type == 4 ? "kq_dequant_q4k" : "kq_dequant_q6k";

@@ -230,4 +230,74 @@ int kq_fill_q6k(kq_ctx* ctx, uint64_t w, uint64_t block0, uint64_t nblocks, uint
 
 uint64_t kq_stream_key(uint64_t seed, uint64_t tensor) { return kq::stream_key(seed, tensor); }
 
+int kq_matvec_push(kq_ctx* ctx, const kq_matvec_desc* desc, const kq_push_desc* push,
+                   kq_stream stream) {
+  if (!ctx || !desc || !push) return fail(KQ_E_INVALID, "kq_matvec_push", "null ctx, descriptor or push");
+  int rc = kq::enter(ctx);
+  if (rc) return rc;
+  return kq::matvec(ctx, *desc, static_cast<cudaStream_t>(stream), push);
+}
+
+int kq_wait_counter(kq_ctx* ctx, uint64_t counter, uint64_t epoch, uint64_t wait_mul,
+                    uint64_t wait_add, kq_stream stream) {
+  if (!ctx) return fail(KQ_E_INVALID, "kq_wait_counter", "null ctx");
+  int rc = kq::enter(ctx);
+  if (rc) return rc;
+  return kq::wait_counter(ctx, counter, epoch, wait_mul, wait_add, static_cast<cudaStream_t>(stream));
+}
+
+int kq_peer_alloc(kq_ctx* ctx, uint64_t bytes, uint64_t* ptr, void* ipc_handle) {
+  if (!ctx || !ptr || !ipc_handle || !bytes) return fail(KQ_E_INVALID, "kq_peer_alloc", "null argument or zero size");
+  int rc = kq::enter(ctx);
+  if (rc) return rc;
+  void* p = nullptr;
+  cudaError_t e = cudaMalloc(&p, bytes);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaMalloc", "peer memory");
+  e = cudaMemset(p, 0, bytes);
+  if (e != cudaSuccess) {
+    cudaFree(p);
+    return cuda_fail(e, "cudaMemset", "peer memory");
+  }
+  cudaIpcMemHandle_t h;
+  e = cudaIpcGetMemHandle(&h, p);
+  if (e != cudaSuccess) {
+    cudaFree(p);
+    return cuda_fail(e, "cudaIpcGetMemHandle");
+  }
+  std::memcpy(ipc_handle, &h, sizeof(h));
+  *ptr = reinterpret_cast<uint64_t>(p);
+  return KQ_OK;
+}
+
+int kq_peer_open(kq_ctx* ctx, const void* ipc_handle, uint64_t* ptr) {
+  if (!ctx || !ipc_handle || !ptr) return fail(KQ_E_INVALID, "kq_peer_open", "null argument");
+  int rc = kq::enter(ctx);
+  if (rc) return rc;
+  cudaIpcMemHandle_t h;
+  std::memcpy(&h, ipc_handle, sizeof(h));
+  void* p = nullptr;
+  const cudaError_t e = cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaIpcOpenMemHandle");
+  *ptr = reinterpret_cast<uint64_t>(p);
+  return KQ_OK;
+}
+
+int kq_peer_close(kq_ctx* ctx, uint64_t ptr) {
+  if (!ctx || !ptr) return fail(KQ_E_INVALID, "kq_peer_close", "null argument");
+  int rc = kq::enter(ctx);
+  if (rc) return rc;
+  const cudaError_t e = cudaIpcCloseMemHandle(reinterpret_cast<void*>(ptr));
+  if (e != cudaSuccess) return cuda_fail(e, "cudaIpcCloseMemHandle");
+  return KQ_OK;
+}
+
+int kq_peer_free(kq_ctx* ctx, uint64_t ptr) {
+  if (!ctx || !ptr) return fail(KQ_E_INVALID, "kq_peer_free", "null argument");
+  int rc = kq::enter(ctx);
+  if (rc) return rc;
+  const cudaError_t e = cudaFree(reinterpret_cast<void*>(ptr));
+  if (e != cudaSuccess) return cuda_fail(e, "cudaFree", "peer memory");
+  return KQ_OK;
+}
+
 }  // extern "C"

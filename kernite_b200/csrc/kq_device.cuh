@@ -37,6 +37,33 @@ __device__ __forceinline__ void report_error(unsigned* err, unsigned code) {
   if (err) atomicCAS(err, 0u, code);
 }
 
+__device__ __forceinline__ unsigned long long ld_acquire_sys(const unsigned long long* p) {
+  unsigned long long v;
+  asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+
+// Waits (acquire, system scope) until *cnt >= (*epoch - 1) * mul + add: the arrival count other
+// GPUs add to after storing into this GPU's memory. Gives up after kWaitBudgetNs, at once when
+// an earlier wait already failed (so one missing rank costs one budget, not one per launch), and
+// then records kErrWaitPeer and returns false.
+__device__ __forceinline__ bool wait_count(unsigned* err, const unsigned long long* cnt,
+                                           const unsigned long long* epoch, uint64_t mul,
+                                           uint64_t add) {
+  const unsigned long long target = (ld_acquire_sys(epoch) - 1ull) * mul + add;
+  if (ld_acquire_sys(cnt) >= target) return true;
+  bool ok = false;
+  if (!(err && *reinterpret_cast<volatile unsigned*>(err))) {
+    const uint64_t t0 = globaltimer();
+    while (!(ok = ld_acquire_sys(cnt) >= target)) {
+      if (globaltimer() - t0 > kWaitBudgetNs) break;
+      __nanosleep(64);
+    }
+  }
+  if (!ok) report_error(err, kErrWaitPeer);
+  return ok;
+}
+
 // ---------------------------------------------------------------- mbarriers
 
 __device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {

@@ -38,9 +38,12 @@ bool mma_supports(const kq_matvec_desc& d);
 int mma_matvec(kq_ctx* ctx, const kq_matvec_desc& d, uint64_t ldx, uint64_t ldy,
                cudaStream_t stream);
 uint64_t mma_scratch_bytes(uint32_t k, uint32_t batch);
-int matvec(kq_ctx* ctx, const kq_matvec_desc& d, cudaStream_t stream);
+int matvec(kq_ctx* ctx, const kq_matvec_desc& d, cudaStream_t stream,
+           const kq_push_desc* push = nullptr);
 
 int aux_prepare(kq_ctx* ctx);
+int wait_counter(kq_ctx* ctx, uint64_t counter, uint64_t epoch, uint64_t mul, uint64_t add,
+                 cudaStream_t s);
 int dequant(kq_ctx* ctx, int type, uint64_t out, uint64_t w, uint64_t nblocks, cudaStream_t s);
 int fill(kq_ctx* ctx, int type, uint64_t w, uint64_t block0, uint64_t nblocks, uint64_t key,
          cudaStream_t s);

@@ -49,7 +49,17 @@ struct MatvecArgs {
   uint32_t team_warps, teams, per_team, ring, slot_bytes;  // tile = teams * per_team rows
   uint32_t row_unit, prologue, epilogue, flags;
   float eps, pair_scale;
+  // push exchange (kq_matvec_push); npush == 0 otherwise
+  uint32_t npush, push_rows;
+  float* push_y[8];
+  unsigned long long* push_cnt[8];
+  const unsigned long long* wait_cnt;
+  const unsigned long long* epoch;
+  uint64_t wait_mul, wait_add;
 };
+
+// Named barrier among the consumer warps for the push exchange (teams use 1..14).
+constexpr uint32_t kPushBarrier = 15;
 
 template <int QT>
 struct Fmt;
@@ -185,6 +195,12 @@ __global__ void __launch_bounds__(Geo<B>::kMaxThreads, 1) matvec_kernel(const Ma
   const uint32_t base_off = QT == 4 ? 64 * unit : 128 * unit;  // element offset in the block
 
   pdl_wait();  // x may be the previous kernel's output
+  if (a.wait_cnt) {
+    // x is a full vector other GPUs push into: wait until every rank's rows of this step are in
+    if (threadIdx.x == 0 && !wait_count(a.err, a.wait_cnt, a.epoch, a.wait_mul, a.wait_add))
+      s_failed = 1;
+    named_barrier(kPushBarrier, consumers * 32);
+  }
 
   // x slice in registers, in pairs: xr[b][g][m] = x[b, e], x[b, e+1] with
   // e = kb*256 + base_off + 32g + l0 + 2m
@@ -205,7 +221,7 @@ __global__ void __launch_bounds__(Geo<B>::kMaxThreads, 1) matvec_kernel(const Ma
         for (int g = 0; g < G; ++g) {
 #pragma unroll
           for (int m = 0; m < L / 4; ++m) {
-            const float4 v = __ldg(reinterpret_cast<const float4*>(xb + 32 * g + 4 * m));
+            const float4 v = __ldcg(reinterpret_cast<const float4*>(xb + 32 * g + 4 * m));
             xr[b][g][2 * m] = f2(v.x, v.y);
             xr[b][g][2 * m + 1] = f2(v.z, v.w);
           }
@@ -226,7 +242,7 @@ __global__ void __launch_bounds__(Geo<B>::kMaxThreads, 1) matvec_kernel(const Ma
       float m = 0.f;
       if (b < static_cast<int>(a.batch)) {
         const float* xb = a.x + b * a.ldx;
-        for (uint32_t k = threadIdx.x; k < K; k += nthreads) m = fmaxf(m, fabsf(xb[k]));
+        for (uint32_t k = threadIdx.x; k < K; k += nthreads) m = fmaxf(m, fabsf(__ldcg(xb + k)));
       }
 #pragma unroll
       for (int o = 16; o; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
@@ -247,7 +263,7 @@ __global__ void __launch_bounds__(Geo<B>::kMaxThreads, 1) matvec_kernel(const Ma
       if (b < static_cast<int>(a.batch)) {
         const float* xb = a.x + b * a.ldx;
         for (uint32_t k = threadIdx.x; k < K; k += nthreads) {
-          const float v = xb[k] * inv;
+          const float v = __ldcg(xb + k) * inv;
           ss = fmaf(v, v, ss);
         }
       }
@@ -301,6 +317,11 @@ __global__ void __launch_bounds__(Geo<B>::kMaxThreads, 1) matvec_kernel(const Ma
 #pragma unroll
   for (int b = 0; b < B; ++b) held[b] = 0.f;
 
+  // Batch 1 push: output `o` (< push_rows) also goes to every rank's full vector.
+  auto push_out = [&](uint32_t o, float v) {
+    if (o < a.push_rows)
+      for (uint32_t p = 0; p < a.npush; ++p) a.push_y[p][o] = v;
+  };
   const uint32_t rounds = a.per_team / R;     // rounds of R rows per tile for this team
   const uint32_t round_stride = a.teams * R;  // rows between a team's rounds
   uint32_t s = 0, phase = 0;                  // ring slot and the parity of its current use
@@ -498,10 +519,13 @@ __global__ void __launch_bounds__(Geo<B>::kMaxThreads, 1) matvec_kernel(const Ma
             if (b < static_cast<int>(a.batch)) {
               if (R == 1) {
                 a.y[b * a.ldy + row] = acc[b];
+                push_out(row, acc[b]);
               } else if ((u & 1) == 0) {
                 held[b] = acc[b];
               } else {
-                a.y[b * a.ldy + row / 2] = held[b] * acc[b] * a.pair_scale;
+                const float v = held[b] * acc[b] * a.pair_scale;
+                a.y[b * a.ldy + row / 2] = v;
+                push_out(row / 2, v);
               }
             }
           }
@@ -533,15 +557,29 @@ __global__ void __launch_bounds__(Geo<B>::kMaxThreads, 1) matvec_kernel(const Ma
             for (uint32_t w = 0; w < a.team_warps; ++w) v0 += tb[(u0 * a.team_warps + w) * B + b];
             if (R == 1) {
               a.y[b * a.ldy + row] = v0;
+              push_out(row, v0);
             } else {
               float v1 = 0.f;
               for (uint32_t w = 0; w < a.team_warps; ++w)
                 v1 += tb[((u0 + 1) * a.team_warps + w) * B + b];
-              a.y[b * a.ldy + row / 2] = v0 * v1 * a.pair_scale;
+              const float v = v0 * v1 * a.pair_scale;
+              a.y[b * a.ldy + row / 2] = v;
+              push_out(row / 2, v);
             }
           }
         }
       }
+    }
+  }
+
+  if (a.npush) {
+    // every row this CTA pushed is stored everywhere before its count is added anywhere
+    __threadfence_system();
+    named_barrier(kPushBarrier, consumers * 32);
+    if (threadIdx.x == 0) {
+      const uint32_t o0 = r_begin / a.row_unit, o1 = min(r_end / a.row_unit, a.push_rows);
+      if (o1 > o0)
+        for (uint32_t p = 0; p < a.npush; ++p) atomicAdd_system(a.push_cnt[p], (unsigned long long)(o1 - o0));
     }
   }
 }
@@ -599,8 +637,8 @@ int matvec_prepare(kq_ctx* ctx) {
   return KQ_OK;
 }
 
-int matvec(kq_ctx* ctx, const kq_matvec_desc& d, cudaStream_t stream) {
-  const char* call = "kq_matvec";
+int matvec(kq_ctx* ctx, const kq_matvec_desc& d, cudaStream_t stream, const kq_push_desc* push) {
+  const char* call = push ? "kq_matvec_push" : "kq_matvec";
   int qt;
   if (d.type == KQ_TYPE_Q4_K)
     qt = 4;
@@ -632,7 +670,17 @@ int matvec(kq_ctx* ctx, const kq_matvec_desc& d, cudaStream_t stream) {
   if (ldy < out_rows) return fail(KQ_E_INVALID, call, "ldy must be >= the output rows");
 
   // Path: the tensor cores above batch 8 (and when asked), the CUDA cores otherwise.
-  const bool want_tc = (d.flags & KQ_FLAG_TENSOR_CORES) || (d.batch > 8 && !(d.flags & KQ_FLAG_CUDA_CORES));
+  if (push) {
+    if (d.batch != 1 || (d.flags & KQ_FLAG_TENSOR_CORES))
+      return fail(KQ_E_INVALID, call, "the push exchange serves batch 1 on the CUDA-core kernel");
+    if (push->npush > 8) return fail(KQ_E_INVALID, call, "npush must be 0..8");
+    for (uint32_t p = 0; p < push->npush; ++p)
+      if (!push->y[p] || !push->counter[p] || push->y[p] % 4 || push->counter[p] % 8)
+        return fail(KQ_E_INVALID, call, "push target " + std::to_string(p) + " is null or misaligned");
+    if (push->wait_counter && (!push->epoch || push->wait_counter % 8 || push->epoch % 8))
+      return fail(KQ_E_INVALID, call, "wait_counter needs an 8-byte aligned epoch and counter");
+  }
+  const bool want_tc = !push && ((d.flags & KQ_FLAG_TENSOR_CORES) || (d.batch > 8 && !(d.flags & KQ_FLAG_CUDA_CORES)));
   if (want_tc) {
     if (!mma_supports(d))
       return fail(KQ_E_UNSUPPORTED, call,
@@ -655,7 +703,7 @@ int matvec(kq_ctx* ctx, const kq_matvec_desc& d, cudaStream_t stream) {
                 "k " + std::to_string(d.k) + " is past this build's limit for batch " +
                     std::to_string(d.batch) + " (" + std::to_string(max_consumers * 32 / ppb * kQK) +
                     ")");
-  const uint32_t pmax = std::min<uint32_t>(15, max_consumers / team_warps);  // named barriers 1..15
+  const uint32_t pmax = std::min<uint32_t>(14, max_consumers / team_warps);  // named barriers 1..14
 
   const uint32_t row_unit = pair ? 2 : 1;
   const uint64_t units = d.rows / row_unit;
@@ -701,6 +749,17 @@ int matvec(kq_ctx* ctx, const kq_matvec_desc& d, cudaStream_t stream) {
   args.flags = d.flags;
   args.eps = d.eps;
   args.pair_scale = d.pair_scale;
+  args.npush = push ? push->npush : 0;
+  args.push_rows = push ? push->push_rows : 0;
+  for (int p = 0; p < 8; ++p) {
+    args.push_y[p] = push && p < static_cast<int>(push->npush) ? reinterpret_cast<float*>(push->y[p]) : nullptr;
+    args.push_cnt[p] = push && p < static_cast<int>(push->npush)
+                           ? reinterpret_cast<unsigned long long*>(push->counter[p]) : nullptr;
+  }
+  args.wait_cnt = push && push->wait_counter ? reinterpret_cast<const unsigned long long*>(push->wait_counter) : nullptr;
+  args.epoch = push && push->wait_counter ? reinterpret_cast<const unsigned long long*>(push->epoch) : nullptr;
+  args.wait_mul = push ? push->wait_mul : 0;
+  args.wait_add = push ? push->wait_add : 0;
 
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(grid);

@@ -110,6 +110,35 @@ def plan(cfg: StackConfig, rank: int, world: int) -> dict[str, Shard]:
     return {"qkv": qkv, "o": o, "gate_up": gate_up, "down": down, "head": head}
 
 
+FULL_KEYS = ("q", "o", "a", "xd", "logits")
+
+
+def full_sizes(cfg: StackConfig) -> dict[str, int]:
+    return {"q": cfg.hidden, "o": cfg.hidden, "a": cfg.ffn, "xd": cfg.hidden, "logits": cfg.vocab}
+
+
+def push_layout(cfg: StackConfig) -> tuple[dict[str, int], int]:
+    """Byte offsets in a rank's exchange region (identical on every rank): one u64 arrival
+    counter per full vector and the token counter ("epoch") in the first 256 bytes, then the
+    full vectors, each 256-byte aligned. Returns (offsets, total bytes)."""
+    off = {f"cnt_{k}": 8 * i for i, k in enumerate(FULL_KEYS)}
+    off["epoch"] = 8 * len(FULL_KEYS)
+    pos = 256
+    for k, n in full_sizes(cfg).items():
+        off[k] = pos
+        pos += (n * 4 + 255) // 256 * 256
+    return off, pos
+
+
+def push_target(cfg: StackConfig, key: str, occurrence: int) -> tuple[int, int]:
+    """(wait_mul, wait_add) for reading full vector `key` after its occurrence-th write of a
+    token (1-based): every write adds the vector's length to its counter, so before token t's
+    occurrence o the counter must reach (t - 1) * writes_per_token * len + o * len."""
+    n = full_sizes(cfg)[key]
+    per_token = (1 if key == "logits" else cfg.layers) * n
+    return per_token, occurrence * n
+
+
 class DecodeStack:
     """One rank's part of a decode stack on a backend. `forward(x)` runs one token."""
 
@@ -125,12 +154,14 @@ class DecodeStack:
         self.head = backend.weights(self.shards["head"], cfg.seed, cfg.tensor_id(cfg.layers, "head"))
         h, f = cfg.hidden, cfg.ffn
         sh = self.shards
+        full = getattr(backend, "full_vectors", None)
+        fv = full(cfg, rank, world) if full else {k: backend.vector(n) for k, n in full_sizes(cfg).items()}
         self.buf = {
-            "x": backend.vector(h), "qkv": backend.vector(sh["qkv"].rows), "q": backend.vector(h),
-            "o_loc": backend.vector(sh["o"].rows), "o": backend.vector(h),
-            "a_loc": backend.vector(sh["gate_up"].rows // 2), "a": backend.vector(f),
-            "x_loc": backend.vector(sh["down"].rows), "xd": backend.vector(h),
-            "l_loc": backend.vector(sh["head"].rows), "logits": backend.vector(cfg.vocab),
+            "x": backend.vector(h), "qkv": backend.vector(sh["qkv"].rows), "q": fv["q"],
+            "o_loc": backend.vector(sh["o"].rows), "o": fv["o"],
+            "a_loc": backend.vector(sh["gate_up"].rows // 2), "a": fv["a"],
+            "x_loc": backend.vector(sh["down"].rows), "xd": fv["xd"],
+            "l_loc": backend.vector(sh["head"].rows), "logits": fv["logits"],
         }
         if world == 1:
             # one rank: each "gathered" vector is the local output itself (q is the first h
@@ -139,32 +170,48 @@ class DecodeStack:
             b["q"], b["o"], b["a"], b["xd"], b["logits"] = b["qkv"], b["o_loc"], b["a_loc"], b["x_loc"], b["l_loc"]
 
     def launches_per_token(self) -> int:
-        return 4 * self.cfg.layers + 1
+        """This library's kernels per token: the matvecs, plus the closing wait of the push
+        exchange."""
+        return 4 * self.cfg.layers + 1 + (1 if getattr(self.be, "push", False) else 0)
 
     def forward(self) -> None:
         """One token: reads buf['x'], writes buf['logits'] (on every rank)."""
         cfg, be, b, sh = self.cfg, self.be, self.buf, self.shards
+        begin = getattr(be, "begin_token", None)
+        if begin:
+            begin()
         x = b["x"]
         for layer, lw in enumerate(self.weights):
-            be.matvec(lw["qkv"], sh["qkv"], b["qkv"], x, rmsnorm=layer > 0, eps=cfg.eps)
+            be.matvec(lw["qkv"], sh["qkv"], b["qkv"], x, rmsnorm=layer > 0, eps=cfg.eps,
+                      out=("q", sh["qkv"].gathered), src=("xd", layer) if layer > 0 else None)
             be.gather(b["q"], b["qkv"], sh["qkv"].gathered)
-            be.matvec(lw["o"], sh["o"], b["o_loc"], b["q"])
+            be.matvec(lw["o"], sh["o"], b["o_loc"], b["q"], out=("o", sh["o"].gathered), src=("q", layer + 1))
             be.gather(b["o"], b["o_loc"], sh["o"].gathered)
-            be.matvec(lw["gate_up"], sh["gate_up"], b["a_loc"], b["o"], pair_scale=1.0 / math.sqrt(cfg.ffn))
+            be.matvec(lw["gate_up"], sh["gate_up"], b["a_loc"], b["o"], pair_scale=1.0 / math.sqrt(cfg.ffn),
+                      out=("a", sh["gate_up"].gathered), src=("o", layer + 1))
             be.gather(b["a"], b["a_loc"], sh["gate_up"].gathered)
-            be.matvec(lw["down"], sh["down"], b["x_loc"], b["a"])
+            be.matvec(lw["down"], sh["down"], b["x_loc"], b["a"], out=("xd", sh["down"].gathered),
+                      src=("a", layer + 1))
             be.gather(b["xd"], b["x_loc"], sh["down"].gathered)
             x = b["xd"]
-        be.matvec(self.head, sh["head"], b["l_loc"], x, rmsnorm=True, eps=cfg.eps)
+        be.matvec(self.head, sh["head"], b["l_loc"], x, rmsnorm=True, eps=cfg.eps,
+                  out=("logits", sh["head"].gathered), src=("xd", cfg.layers) if self.cfg.layers else None)
         be.gather(b["logits"], b["l_loc"], sh["head"].gathered)
+        end = getattr(be, "end_token", None)
+        if end:
+            end()
 
 
 # ---------------------------------------------------------------- the CUDA backend (product)
 
 class CudaBackend:
-    """libkq.so kernels on one GPU; all-gathers with torch.distributed (NCCL) when world > 1."""
+    """libkq.so kernels on one GPU. With world > 1 the exchange after each projection is either
+    an NCCL all-gather (torch.distributed), or -- push=True -- done by the matvec itself: its
+    epilogue stores its rows into every rank's full vector over CUDA IPC peer mappings and
+    counts them there, and the next matvec waits for the count (kq_matvec_push)."""
 
-    def __init__(self, kernels, stream=None, group=None, world: int = 1, flags: int = 0):
+    def __init__(self, kernels, stream=None, group=None, world: int = 1, flags: int = 0,
+                 push: bool = False, rank: int = 0):
         import torch
 
         import kernite_b200 as kb
@@ -173,9 +220,59 @@ class CudaBackend:
         self.stream = stream
         self.group = group
         self.world = world
+        self.rank = rank
         self.flags = flags
+        self.push = push and world > 1
         self.launches = 0
+        self.region = None
+        self.peers: list[int] = []
 
+    # ---------------------------------------------------------------- push exchange set-up
+    def full_vectors(self, cfg: StackConfig, rank: int, world: int):
+        torch, kb = self.torch, self.kb
+        if not self.push:
+            return {k: self.vector(n) for k, n in full_sizes(cfg).items()}
+        import torch.distributed as dist
+
+        self.cfg = cfg
+        self.off, nbytes = push_layout(cfg)
+        ptr, handle = self.k.peer_alloc(nbytes)
+        self.region = ptr
+        handles = [None] * world
+        dist.all_gather_object(handles, handle, group=self.group)
+        self.peers = [ptr if p == rank else self.k.peer_open(handles[p]) for p in range(world)]
+        view = lambda off, n, t="<f4": torch.as_tensor(kb.DeviceArray(ptr + off, n, t), device="cuda")
+        self.epoch = view(self.off["epoch"], 1, "<i8")
+        return {k: view(self.off[k], n) for k, n in full_sizes(cfg).items()}
+
+    def begin_token(self) -> None:
+        if self.push:
+            with self.torch.cuda.stream(self.stream) if self.stream is not None else _null():
+                self.epoch.add_(1)
+
+    def end_token(self) -> None:
+        # the other ranks' logits rows are the one push no later launch waits for
+        if self.push:
+            self.k.wait_counter(self.region + self.off["cnt_logits"], self.region + self.off["epoch"],
+                                *push_target(self.cfg, "logits", 1), stream=self.stream)
+            self.launches += 1
+
+    def close(self) -> None:
+        """Unmaps the peers' regions and frees this rank's, once every rank is done with them
+        (a collective step: all ranks call it)."""
+        self.torch.cuda.synchronize()
+        if self.push:
+            import torch.distributed as dist
+
+            dist.barrier(group=self.group)
+        for p, ptr in enumerate(self.peers):
+            if p != self.rank:
+                self.k.peer_close(ptr)
+        if self.region:
+            self.k.peer_free(self.region)
+        self.peers, self.region = [], None
+
+    # ---------------------------------------------------------------- weights and vectors
     def weights(self, shard: Shard, seed: int, tensor: int):
         torch, kb = self.torch, self.kb
         W = torch.empty(shard.nbytes, dtype=torch.uint8, device="cuda")
@@ -193,28 +290,51 @@ class CudaBackend:
         return self.torch.zeros(n, dtype=self.torch.float32, device="cuda")
 
     def matvec(self, W, shard: Shard, y, x, rmsnorm: bool = False, eps: float = 0.0,
-               pair_scale: float | None = None) -> None:
+               pair_scale: float | None = None, out=None, src=None) -> None:
         kb = self.kb
-        self.k.matvec(shard.qtype, y, W, x, shard.rows, shard.k, 1,
-                      prologue=kb.PROLOGUE_RMSNORM if rmsnorm else kb.PROLOGUE_NONE, eps=eps,
-                      epilogue=kb.EPILOGUE_PAIR_PRODUCT if pair_scale is not None else kb.EPILOGUE_NONE,
-                      pair_scale=pair_scale if pair_scale is not None else 1.0,
-                      flags=kb.FLAG_WEIGHTS_STATIC | self.flags, stream=self.stream)
+        kw = dict(prologue=kb.PROLOGUE_RMSNORM if rmsnorm else kb.PROLOGUE_NONE, eps=eps,
+                  epilogue=kb.EPILOGUE_PAIR_PRODUCT if pair_scale is not None else kb.EPILOGUE_NONE,
+                  pair_scale=pair_scale if pair_scale is not None else 1.0,
+                  flags=kb.FLAG_WEIGHTS_STATIC | self.flags, stream=self.stream)
+        if self.push and out is not None:
+            key, (a, b) = out
+            d = kb.KqPushDesc()
+            d.npush = self.world
+            d.push_rows = b - a
+            for p, base in enumerate(self.peers):
+                d.y[p] = base + self.off[key] + 4 * self.rank * (b - a)
+                d.counter[p] = base + self.off[f"cnt_{key}"]
+            if src is not None:
+                skey, occ = src
+                d.wait_counter = self.region + self.off[f"cnt_{skey}"]
+                d.epoch = self.region + self.off["epoch"]
+                d.wait_mul, d.wait_add = push_target(self.cfg, skey, occ)
+            self.k.matvec_push(shard.qtype, y, W, x, shard.rows, shard.k, d, **kw)
+        else:
+            self.k.matvec(shard.qtype, y, W, x, shard.rows, shard.k, 1, **kw)
         self.launches += 1
 
     def gather(self, out, loc, part: tuple[int, int]) -> None:
-        a, b = part
-        if self.world == 1:
-            return  # the stack aliases the full vector to the local output
+        if self.world == 1 or self.push:
+            return  # aliased (one rank) or pushed by the matvec itself
         import torch.distributed as dist
 
+        a, b = part
         dist.all_gather_into_tensor(out, loc[a:b], group=self.group)
 
 
+class _null:
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *a):
+        return False
+
+
 def make_cuda_stack(cfg: StackConfig, kernels, rank: int = 0, world: int = 1, group=None,
-                    stream=None, flags: int = 0) -> DecodeStack:
-    return DecodeStack(cfg, CudaBackend(kernels, stream=stream, group=group, world=world, flags=flags),
-                       rank, world)
+                    stream=None, flags: int = 0, push: bool = False) -> DecodeStack:
+    return DecodeStack(cfg, CudaBackend(kernels, stream=stream, group=group, world=world, flags=flags,
+                                        push=push, rank=rank), rank, world)
 
 
 # ---------------------------------------------------------------- reference (for tests)

@@ -1,6 +1,8 @@
 """One rank of the sharded decode stack on the GPU (launched by tests/test_stack_multigpu.py
-under torchrun): runs the tiny and a 2-layer 70B-shaped stack over NCCL, eagerly and from a
-CUDA graph, and checks the logits on every rank against the unsharded CPU reference."""
+under torchrun): runs the tiny and a 2-layer 70B-shaped stack with both exchanges (NCCL
+all-gathers, and the matvec's own push over peer mappings), one token eagerly and two more
+replayed from a CUDA graph, each token on new input, and checks the logits on every rank
+against the unsharded CPU reference."""
 import dataclasses
 import datetime
 import os
@@ -23,31 +25,47 @@ def main():
                             device_id=torch.device("cuda", local))
     kernels = kb.Kernels.load(local)
     ok = True
-    for name, cfg in (("tiny", st.CONFIGS["tiny"]), ("70b-2", dataclasses.replace(st.CONFIGS["70b"], layers=2))):
-        x = np.random.default_rng(3).standard_normal(cfg.hidden).astype(np.float32)
-        stream = torch.cuda.Stream()
-        s = st.make_cuda_stack(cfg, kernels, rank, world, stream=stream)
-        s.buf["x"].copy_(torch.from_numpy(x).cuda())
-        torch.cuda.synchronize()
-        with torch.cuda.stream(stream):
-            s.forward()
-        torch.cuda.synchronize()
-        eager = s.buf["logits"].cpu().numpy()
-        g = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(g, stream=stream):
-            s.forward()
-        s.buf["logits"].zero_()
-        g.replay()
-        torch.cuda.synchronize()
-        replay = s.buf["logits"].cpu().numpy()
-        del g
-        kernels.device_error()
-        ref = st.reference_logits(cfg, x)
-        tol = 1e-4 * np.abs(ref).max()
-        good = np.abs(eager - ref).max() <= tol and np.array_equal(eager, replay)
-        print(f"rank {rank}/{world} {name}: max|err| {np.abs(eager - ref).max():.3e} (tol {tol:.3e}) "
-              f"graph==eager {np.array_equal(eager, replay)}", flush=True)
-        ok = ok and good
+    refs = {}
+    for exchange in ("nccl", "push"):
+        for name, cfg in (("tiny", st.CONFIGS["tiny"]), ("70b-2", dataclasses.replace(st.CONFIGS["70b"], layers=2))):
+            xs = [np.random.default_rng(3 + t).standard_normal(cfg.hidden).astype(np.float32) for t in range(3)]
+            for t, x in enumerate(xs):
+                if (name, t) not in refs:
+                    refs[name, t] = st.reference_logits(cfg, x)
+            stream = torch.cuda.Stream()
+            s = st.make_cuda_stack(cfg, kernels, rank, world, stream=stream, push=exchange == "push")
+            s.buf["x"].copy_(torch.from_numpy(xs[0]).cuda())
+            torch.cuda.synchronize()
+            with torch.cuda.stream(stream):
+                s.forward()
+            torch.cuda.synchronize()
+            out = [s.buf["logits"].cpu().numpy()]
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, stream=stream):
+                s.forward()
+            for x in xs[1:]:
+                s.buf["x"].copy_(torch.from_numpy(x).cuda())
+                torch.cuda.synchronize()
+                g.replay()
+                torch.cuda.synchronize()
+                out.append(s.buf["logits"].cpu().numpy())
+            g.reset()
+            del g
+            try:
+                kernels.device_error()
+            except kb.Error as e:  # keep taking the collective steps; fail at the end
+                print(f"rank {rank}: {e}", flush=True)
+                ok = False
+            if exchange == "push":
+                s.be.close()
+            for t, y in enumerate(out):
+                ref = refs[name, t]
+                tol = 1e-4 * np.abs(ref).max()
+                err = np.abs(y - ref).max()
+                good = err <= tol
+                print(f"rank {rank}/{world} {exchange} {name} token {t}: max|err| {err:.3e} (tol {tol:.3e})",
+                      flush=True)
+                ok = ok and good
     flag = torch.tensor([1 if ok else 0], device="cuda")
     dist.all_reduce(flag, op=dist.ReduceOp.MIN)
     dist.barrier()

@@ -33,7 +33,7 @@ class OracleBackend:
     def vector(self, n):
         return torch.zeros(n, dtype=torch.float32)
 
-    def matvec(self, W, shard, y, x, rmsnorm=False, eps=0.0, pair_scale=None):
+    def matvec(self, W, shard, y, x, rmsnorm=False, eps=0.0, pair_scale=None, out=None, src=None):
         v = x.numpy().astype(np.float64)
         if rmsnorm:
             v = v / np.sqrt(np.mean(v * v) + eps)
@@ -117,3 +117,15 @@ def test_single_rank_oracle_backend_matches_reference():
     np.testing.assert_allclose(s.buf["logits"].numpy(), ref, rtol=1e-4, atol=1e-4 * np.abs(ref).max())
     assert s.launches_per_token() == 4 * cfg.layers + 1
     assert math.isfinite(float(np.abs(ref).max()))
+
+
+def test_push_layout_and_targets():
+    cfg = st.CONFIGS["70b"]
+    off, total = st.push_layout(cfg)
+    assert off["epoch"] == 40 and all(off[k] % 256 == 0 for k in st.FULL_KEYS)
+    assert total >= off["logits"] + 4 * cfg.vocab
+    # q is written once per layer: before token t's layer-L read the counter holds
+    # (t-1) * layers * h from earlier tokens and (L+1) * h from this one
+    mul, add = st.push_target(cfg, "q", 3)
+    assert mul == cfg.layers * cfg.hidden and add == 3 * cfg.hidden
+    assert st.push_target(cfg, "logits", 1) == (cfg.vocab, cfg.vocab)
