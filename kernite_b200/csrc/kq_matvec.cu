@@ -58,6 +58,13 @@ struct MatvecArgs {
   uint64_t wait_mul, wait_add;
 };
 
+// x loads: L1-cached, so the teams of a CTA share one L2 read of each line. Not the
+// non-coherent path: with the push exchange x is written by other GPUs while this kernel runs
+// (before thread 0's acquire, which the CTA barrier orders before these loads).
+__device__ __forceinline__ float4 ld_x4(const float* p) {
+  return *reinterpret_cast<const float4*>(p);
+}
+
 // Named barrier among the consumer warps for the push exchange (teams use 1..14).
 constexpr uint32_t kPushBarrier = 15;
 
@@ -108,7 +115,7 @@ __global__ void __launch_bounds__(Geo<B>::kMaxThreads, 1) matvec_kernel(const Ma
 
   extern __shared__ __align__(128) uint8_t smem[];
   __shared__ int s_failed;
-  __shared__ float s_norm[32][8];
+  __shared__ double s_norm[16][8];  // [consumer warp][batch]; static shared memory stays < 2 KB
 
   const uint32_t RB = a.nb * kBlk;
   const uint32_t consumers = a.teams * a.team_warps;
@@ -221,7 +228,7 @@ __global__ void __launch_bounds__(Geo<B>::kMaxThreads, 1) matvec_kernel(const Ma
         for (int g = 0; g < G; ++g) {
 #pragma unroll
           for (int m = 0; m < L / 4; ++m) {
-            const float4 v = __ldcg(reinterpret_cast<const float4*>(xb + 32 * g + 4 * m));
+            const float4 v = ld_x4(xb + 32 * g + 4 * m);
             xr[b][g][2 * m] = f2(v.x, v.y);
             xr[b][g][2 * m + 1] = f2(v.z, v.w);
           }
@@ -231,58 +238,30 @@ __global__ void __launch_bounds__(Geo<B>::kMaxThreads, 1) matvec_kernel(const Ma
   }
 
   if (a.prologue == KQ_PROLOGUE_RMSNORM) {
-    // Each CTA normalises x by its own full-vector RMS (x is L2-resident). Two passes keep the
-    // sum of squares in range for any finite x: first max|x|, then sum (x / max)^2, and
-    // x / rms = x * (1/max) / sqrt(sum / K + eps / max^2).
-    const uint32_t nthreads = consumers * 32;
-    const uint32_t K = a.nb * kQK;
-    float mx[B];
+    // Every team's lanes hold all of x, so team 0's registers give the sum of squares. It is
+    // taken in f64, where the square of any finite f32 neither overflows nor underflows.
 #pragma unroll
     for (int b = 0; b < B; ++b) {
-      float m = 0.f;
-      if (b < static_cast<int>(a.batch)) {
-        const float* xb = a.x + b * a.ldx;
-        for (uint32_t k = threadIdx.x; k < K; k += nthreads) m = fmaxf(m, fabsf(__ldcg(xb + k)));
-      }
+      double t = 0.0;
 #pragma unroll
-      for (int o = 16; o; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-      if (lane == 0) s_norm[warp][b] = m;
-    }
-    named_barrier(1, nthreads);
+      for (int g = 0; g < G; ++g)
 #pragma unroll
-    for (int b = 0; b < B; ++b) {
-      float m = 0.f;
-      for (uint32_t w = 0; w < consumers; ++w) m = fmaxf(m, s_norm[w][b]);
-      mx[b] = m;
-    }
-    named_barrier(1, nthreads);  // every warp has read the maxima
-#pragma unroll
-    for (int b = 0; b < B; ++b) {
-      float ss = 0.f;
-      const float inv = mx[b] > 0.f ? 1.0f / mx[b] : 0.f;
-      if (b < static_cast<int>(a.batch)) {
-        const float* xb = a.x + b * a.ldx;
-        for (uint32_t k = threadIdx.x; k < K; k += nthreads) {
-          const float v = __ldcg(xb + k) * inv;
-          ss = fmaf(v, v, ss);
+        for (int m = 0; m < L / 2; ++m) {
+          const double u = xr[b][g][m].x, v = xr[b][g][m].y;
+          t = fma(u, u, t);
+          t = fma(v, v, t);
         }
-      }
 #pragma unroll
-      for (int o = 16; o; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
-      if (lane == 0) s_norm[warp][b] = ss;
+      for (int o = 16; o; o >>= 1) t += __shfl_xor_sync(0xffffffffu, t, o);
+      if (lane == 0) s_norm[warp][b] = t;
     }
-    named_barrier(1, nthreads);
+    named_barrier(1, consumers * 32);
+    const double K = static_cast<double>(a.nb) * kQK;
 #pragma unroll
     for (int b = 0; b < B; ++b) {
-      float t = 0.f;
-      for (uint32_t w = 0; w < consumers; ++w) t += s_norm[w][b];
-      float scale;
-      if (mx[b] >= 1e-18f) {
-        const float inv = 1.0f / mx[b];
-        scale = inv / sqrtf(t / static_cast<float>(K) + a.eps * inv * inv);
-      } else {  // x is (almost) zero: eps dominates
-        scale = 1.0f / sqrtf(t * mx[b] * mx[b] / static_cast<float>(K) + a.eps);
-      }
+      double t = 0.0;
+      for (uint32_t w = 0; w < a.team_warps; ++w) t += s_norm[w][b];
+      const float scale = static_cast<float>(1.0 / sqrt(t / K + static_cast<double>(a.eps)));
 #pragma unroll
       for (int g = 0; g < G; ++g)
 #pragma unroll
@@ -291,7 +270,6 @@ __global__ void __launch_bounds__(Geo<B>::kMaxThreads, 1) matvec_kernel(const Ma
           xr[b][g][m].y *= scale;
         }
     }
-    named_barrier(1, nthreads);  // s_norm is read by all before anyone reuses shared memory
   }
 
   // The lane's sums of x per group, for the offset removal.
@@ -317,11 +295,6 @@ __global__ void __launch_bounds__(Geo<B>::kMaxThreads, 1) matvec_kernel(const Ma
 #pragma unroll
   for (int b = 0; b < B; ++b) held[b] = 0.f;
 
-  // Batch 1 push: output `o` (< push_rows) also goes to every rank's full vector.
-  auto push_out = [&](uint32_t o, float v) {
-    if (o < a.push_rows)
-      for (uint32_t p = 0; p < a.npush; ++p) a.push_y[p][o] = v;
-  };
   const uint32_t rounds = a.per_team / R;     // rounds of R rows per tile for this team
   const uint32_t round_stride = a.teams * R;  // rows between a team's rounds
   uint32_t s = 0, phase = 0;                  // ring slot and the parity of its current use
@@ -519,13 +492,10 @@ __global__ void __launch_bounds__(Geo<B>::kMaxThreads, 1) matvec_kernel(const Ma
             if (b < static_cast<int>(a.batch)) {
               if (R == 1) {
                 a.y[b * a.ldy + row] = acc[b];
-                push_out(row, acc[b]);
               } else if ((u & 1) == 0) {
                 held[b] = acc[b];
               } else {
-                const float v = held[b] * acc[b] * a.pair_scale;
-                a.y[b * a.ldy + row / 2] = v;
-                push_out(row / 2, v);
+                a.y[b * a.ldy + row / 2] = held[b] * acc[b] * a.pair_scale;
               }
             }
           }
@@ -557,14 +527,11 @@ __global__ void __launch_bounds__(Geo<B>::kMaxThreads, 1) matvec_kernel(const Ma
             for (uint32_t w = 0; w < a.team_warps; ++w) v0 += tb[(u0 * a.team_warps + w) * B + b];
             if (R == 1) {
               a.y[b * a.ldy + row] = v0;
-              push_out(row, v0);
             } else {
               float v1 = 0.f;
               for (uint32_t w = 0; w < a.team_warps; ++w)
                 v1 += tb[((u0 + 1) * a.team_warps + w) * B + b];
-              const float v = v0 * v1 * a.pair_scale;
-              a.y[b * a.ldy + row / 2] = v;
-              push_out(row / 2, v);
+              a.y[b * a.ldy + row / 2] = v0 * v1 * a.pair_scale;
             }
           }
         }
@@ -573,14 +540,18 @@ __global__ void __launch_bounds__(Geo<B>::kMaxThreads, 1) matvec_kernel(const Ma
   }
 
   if (a.npush) {
-    // every row this CTA pushed is stored everywhere before its count is added anywhere
+    // Batch-1 push: once the CTA's outputs are in y, copy those below push_rows into every
+    // rank's full vector, and only then (system fence) add their count on each rank.
+    named_barrier(kPushBarrier, consumers * 32);
+    const uint32_t o0 = r_begin / a.row_unit, o1 = min(r_end / a.row_unit, a.push_rows);
+    for (uint32_t o = o0 + threadIdx.x; o < o1; o += consumers * 32) {
+      const float v = __ldcg(a.y + o);
+      for (uint32_t p = 0; p < a.npush; ++p) a.push_y[p][o] = v;
+    }
     __threadfence_system();
     named_barrier(kPushBarrier, consumers * 32);
-    if (threadIdx.x == 0) {
-      const uint32_t o0 = r_begin / a.row_unit, o1 = min(r_end / a.row_unit, a.push_rows);
-      if (o1 > o0)
-        for (uint32_t p = 0; p < a.npush; ++p) atomicAdd_system(a.push_cnt[p], (unsigned long long)(o1 - o0));
-    }
+    if (threadIdx.x == 0 && o1 > o0)
+      for (uint32_t p = 0; p < a.npush; ++p) atomicAdd_system(a.push_cnt[p], (unsigned long long)(o1 - o0));
   }
 }
 
