@@ -58,8 +58,8 @@ def parse_args(argv=None):
     ap.add_argument("--warmup", type=int, default=200)
     ap.add_argument("--workload", default="q6k_head", choices=sorted(WORKLOADS) + sorted(STACKS))
     ap.add_argument("--batch", type=int, default=1)
-    ap.add_argument("--path", default="auto", choices=["auto", "tc", "cc"],
-                    help="tensor cores, CUDA cores, or the library's choice")
+    ap.add_argument("--path", default="auto", choices=["auto", "tc", "cc", "wm"],
+                    help="tensor cores (tcgen05), CUDA cores, warp-level MMA, or the library's choice")
     ap.add_argument("--impl", default="kq", choices=["kq", "reference"])
     ap.add_argument("--exchange", default="nccl", choices=["nccl", "push"],
                     help="sharded stacks: NCCL all-gathers, or the matvec's own push to peer memory")
@@ -276,7 +276,8 @@ def main(argv=None):
     stream = torch.cuda.Stream()
     torch.cuda.synchronize()
 
-    path_flag = {"auto": 0, "tc": kb.FLAG_TENSOR_CORES, "cc": kb.FLAG_CUDA_CORES}[args.path]
+    path_flag = {"auto": 0, "tc": kb.FLAG_TENSOR_CORES, "cc": kb.FLAG_CUDA_CORES,
+                 "wm": kb.FLAG_WARP_MMA}[args.path]
 
     def step(i, s):
         kernels.matvec(qtype, y, Ws[i % copies], x, rows, K, batch,

@@ -66,8 +66,13 @@ enum {
     KQ_FLAG_NO_PDL = 1u << 1,
     /* Use the tensor-core (tcgen05) kernel; Q4_K only. */
     KQ_FLAG_TENSOR_CORES = 1u << 2,
-    /* Use the CUDA-core kernel (batch <= 8). Without either flag the library chooses. */
-    KQ_FLAG_CUDA_CORES = 1u << 3
+    /* Use the CUDA-core kernel (batch <= 8, f32 multiply-adds). */
+    KQ_FLAG_CUDA_CORES = 1u << 3,
+    /* Use the warp-MMA kernel (Q4_K batch 1..8, Q6_K batch 1): dequantisation in registers into
+     * exact f16 operands, products on the tensor cores through mma.sync, f32 accumulation.
+     * Without a path flag the library chooses: warp-MMA where it serves the request, the
+     * tensor-core kernel above batch 8, the CUDA-core kernel otherwise. */
+    KQ_FLAG_WARP_MMA = 1u << 4
 };
 
 typedef struct kq_ctx kq_ctx;

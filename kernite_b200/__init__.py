@@ -42,6 +42,7 @@ FLAG_WEIGHTS_STATIC = 1
 FLAG_NO_PDL = 2
 FLAG_TENSOR_CORES = 4
 FLAG_CUDA_CORES = 8
+FLAG_WARP_MMA = 16
 
 Q4K_BYTES = 144
 Q6K_BYTES = 210

@@ -108,6 +108,7 @@ int kq_ctx_create(int device, kq_ctx** out) {
   ctx->scratch_bytes = kq::kCtxScratchBytes;
   int rc = kq::matvec_prepare(ctx);
   if (rc == KQ_OK) rc = kq::mma_prepare(ctx);
+  if (rc == KQ_OK) rc = kq::warpmma_prepare(ctx);
   if (rc == KQ_OK) rc = kq::aux_prepare(ctx);
   if (rc != KQ_OK) {
     cudaFree(ctx->scratch);

@@ -625,8 +625,12 @@ int matvec(kq_ctx* ctx, const kq_matvec_desc& d, cudaStream_t stream, const kq_p
   if (d.batch < 1 || d.batch > max_batch)
     return fail(KQ_E_INVALID, call,
                 "batch must be 1.." + std::to_string(max_batch) + " (got " + std::to_string(d.batch) + ")");
-  if ((d.flags & KQ_FLAG_TENSOR_CORES) && (d.flags & KQ_FLAG_CUDA_CORES))
-    return fail(KQ_E_INVALID, call, "KQ_FLAG_TENSOR_CORES and KQ_FLAG_CUDA_CORES exclude each other");
+  {
+    const uint32_t paths = d.flags & (KQ_FLAG_TENSOR_CORES | KQ_FLAG_CUDA_CORES | KQ_FLAG_WARP_MMA);
+    if (paths & (paths - 1))
+      return fail(KQ_E_INVALID, call,
+                  "KQ_FLAG_TENSOR_CORES, KQ_FLAG_CUDA_CORES and KQ_FLAG_WARP_MMA exclude each other");
+  }
   if (!d.w || !d.x || !d.y) return fail(KQ_E_INVALID, call, "null pointer");
   if (d.w % 16 || d.x % 16 || d.y % 4)
     return fail(KQ_E_INVALID, call, "w and x must be 16-byte aligned, y 4-byte aligned");
@@ -650,6 +654,16 @@ int matvec(kq_ctx* ctx, const kq_matvec_desc& d, cudaStream_t stream, const kq_p
         return fail(KQ_E_INVALID, call, "push target " + std::to_string(p) + " is null or misaligned");
     if (push->wait_counter && (!push->epoch || push->wait_counter % 8 || push->epoch % 8))
       return fail(KQ_E_INVALID, call, "wait_counter needs an 8-byte aligned epoch and counter");
+  }
+  if (d.flags & KQ_FLAG_WARP_MMA) {
+    if (push || !warpmma_supports(d))
+      return fail(KQ_E_UNSUPPORTED, call,
+                  "the warp-MMA kernel serves Q4_K batch 1..8 and Q6_K batch 1, without push");
+    return warpmma_matvec(ctx, d, ldx, ldy, stream);
+  }
+  if (!push && !(d.flags & (KQ_FLAG_TENSOR_CORES | KQ_FLAG_CUDA_CORES)) && warpmma_supports(d)) {
+    const int rc = warpmma_matvec(ctx, d, ldx, ldy, stream);
+    if (rc != KQ_E_UNSUPPORTED) return rc;  // a shape it cannot hold goes to the CUDA cores
   }
   const bool want_tc = !push && ((d.flags & KQ_FLAG_TENSOR_CORES) || (d.batch > 8 && !(d.flags & KQ_FLAG_CUDA_CORES)));
   if (want_tc) {

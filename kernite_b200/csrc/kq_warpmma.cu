@@ -1,0 +1,897 @@
+// kq_warpmma.cu -- the Q4_K / Q6_K matvec for batch 1..8 with the multiply-adds on the tensor
+// cores through warp-level MMA (mma.sync m16n8k16: f16 operands from registers, f32 accumulate).
+//
+// y[b, r] = sum_k W[r, k] * x[b, k], W in GGML k-quant blocks (144-byte Q4_K, 210-byte Q6_K).
+//
+// Why warp-level MMA for a matvec: the work is HBM-bound, and what limits a CUDA-core kernel is
+// the instruction count per weight (every 4- or 6-bit quant has to become its own f32 before an
+// FMA). Here a thread turns two quants into one f16x2 MMA operand register with one LOP3 (the
+// 1024 + q magic) and one HFMA2 that applies the sub-block scale exactly, and the tensor core does
+// the products. The A operand comes straight from registers, which tcgen05.mma cannot take (its A
+// lives in shared or tensor memory, which would add a write and a read of 2 bytes per weight).
+//
+// Shape (one persistent CTA per SM, contiguous rows per CTA):
+//  * A producer warp streams tiles of 16 rows x up to 16 super-blocks into a ring of shared
+//    memory slots with cp.async.bulk (TMA, 1-D): one copy for a tile of whole rows, else one per
+//    row segment. An mbarrier per slot counts the bytes in; Q6_K blocks at any even offset need
+//    nothing special (readers use the byte offset from the aligned copy).
+//  * Consumer warp w takes super-block w of every tile: 16 MMAs (K = 16 each) over the tile's
+//    16 rows. The 16 rows are the MMA's M, x (with the batch) is its N. Thread (g, c) of the
+//    warp builds the A registers of rows g and g+8 from the bytes of its quarter of the block
+//    (Q4_K: qs chunk c = sub-blocks 2c, 2c+1; Q6_K: sub-blocks c and c+4 of each half).
+//  * The order of K inside an MMA is free as long as A and B agree, so each thread pairs the
+//    nibbles its LOP3 masks give it, and x is laid out to match: at the start of the kernel every
+//    CTA converts x into a table of MMA B fragments in shared memory.
+//  * x goes in as an f16 pair hi + lo (hi = f16(x), lo = f16(x - hi)) in two B columns, so the
+//    products carry ~22 bits of x: batch <= 4 fits one n8 MMA (column 2b + part), batch 5..8
+//    takes two (hi, lo). x is first scaled by a power of two (per vector, undone at the end) when
+//    its largest entry is at or above 2^10 (Q4_K) / 2^14 (Q6_K), or below 1, so that f16 never
+//    overflows (Q4_K's sub-block sums of x included) and small vectors do not sink into f16
+//    subnormals.
+//  * Q4_K: A = q*sc exactly (integers <= 945), D = sum q*sc*x; the min term sum_j m_j X_j
+//    (X_j = sum of x over sub-block j) is one more MMA per block with A = m_j; then
+//    y += d*D - dmin*Dmin in f32.
+//  * Q6_K (batch 1): A = q - 32 exactly; the 8 columns of the MMA separate the 8 sub-blocks of a
+//    half block (B[k][n] = x_k if k lies in sub-block n, else 0), so D[row][n] = sum over
+//    sub-block n of (q-32)*x and the int8 scales are applied in f32: y += d * sum_n sc_n D_n.
+//    x enters as hi only here (no column is left for lo): relative error <= 2^-11 per product,
+//    inside the 1e-3 * sum|w x| bound with room to spare, because Q6_K has no min term.
+//  * Lanes' partial rows go to shared memory per band of 16 rows; every few bands the warps
+//    meet at a barrier and sum them in a fixed order (deterministic), then write y.
+//
+// The GGML block layouts and the decode follow the public format (the CPU restatement in
+// oracle/kq_oracle.c); the pattern "one output row per group of lanes, FMA chain over k" is the
+// matvec of fxeqxmulfx/kernite's examples/microgpt/src/gpu.rs:100-131, re-shaped for HBM.
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <string>
+
+#include "kq_device.cuh"
+#include "kq_internal.h"
+
+namespace kq {
+namespace {
+
+constexpr uint32_t kMaxWarps = 16;    // consumer warps (one per super-block of a tile)
+constexpr uint32_t kTileRows = 16;    // rows of a tile = the MMA's M
+constexpr uint32_t kRedBudget = 16384;  // bytes of shared memory for partial rows
+// Q4_K table: bytes per (block, n-tile, column): 16 MMAs x 4 threads x 8 bytes, plus 32 bytes
+// of padding so that the columns' rows start on different banks.
+constexpr uint32_t kNStride = 16 * 32 + 32;
+constexpr uint32_t kZeroBytes = 1024 + 64;  // covers every MMA offset of one block's fragments
+
+constexpr uint32_t kMagic = 0x64006400u;  // f16x2 (1024, 1024): OR a 10-bit field in = 1024 + v
+
+struct WarpMmaArgs {
+  const uint8_t* W;
+  const float* x;
+  float* y;
+  unsigned* err;
+  uint64_t ldx, ldy;
+  uint64_t total_bytes, row_bytes;
+  uint32_t rows, nb, batch;
+  uint32_t nkt;          // K-tiles per band (super-blocks split as evenly as possible)
+  uint32_t nwc;          // consumer warps = super-blocks in the widest K-tile
+  uint32_t ring, slot_bytes, seg_bytes;  // seg_bytes: shared-memory pitch of a tile's rows
+  uint32_t table_off, mtable_off, ublk_off, zero_off, red_off, bars_off;  // shared-memory layout
+  uint32_t zero;         // 0: multipliers built from it are opaque to the compiler
+  uint32_t ncol;         // B columns in use per n-tile
+  uint32_t fb;           // bands of partial rows kept before a flush
+  uint32_t row_unit, prologue, epilogue, flags;
+  float eps, pair_scale;
+};
+
+// ---------------------------------------------------------------- register-level helpers
+
+__device__ __forceinline__ uint32_t lop_and_or(uint32_t a, uint32_t b, uint32_t c) {
+  uint32_t d;  // (a & b) | c
+  asm("lop3.b32 %0, %1, %2, %3, 0xEA;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+  return d;
+}
+
+__device__ __forceinline__ uint32_t hfma2(uint32_t a, uint32_t b, uint32_t c) {
+  uint32_t d;
+  asm("fma.rn.f16x2 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+  return d;
+}
+
+__device__ __forceinline__ uint32_t hadd2(uint32_t a, uint32_t b) {
+  uint32_t d;
+  asm("add.rn.f16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+  return d;
+}
+
+__device__ __forceinline__ uint32_t hmul2(uint32_t a, uint32_t b) {
+  uint32_t d;
+  asm("mul.rn.f16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+  return d;
+}
+
+// x >> 8 and x >> (8 - s) as multiply-highs, x << s as a multiply: the same bits, computed on
+// the FMA pipe, which the dequantisation leaves idle, instead of the ALU it saturates. The
+// multipliers come in as values the compiler cannot see are powers of two.
+__device__ __forceinline__ uint32_t mulhi(uint32_t x, uint32_t m) {
+  uint32_t d;
+  asm("mul.hi.u32 %0, %1, %2;" : "=r"(d) : "r"(x), "r"(m));
+  return d;
+}
+__device__ __forceinline__ uint32_t mullo(uint32_t x, uint32_t m) {
+  uint32_t d;
+  asm("mul.lo.u32 %0, %1, %2;" : "=r"(d) : "r"(x), "r"(m));
+  return d;
+}
+
+// 16 bytes at shared address `addr` as 4 words, for an address whose alignment class the whole
+// warp shares: ALIGN 16, 8 or 4 loads directly; ALIGN 2 loads the 4-byte-aligned superset and
+// funnel-shifts.
+template <int ALIGN>
+__device__ __forceinline__ void lds16(uint32_t addr, uint32_t (&w)[4]) {
+  if constexpr (ALIGN == 16) {
+    const uint4 v = lds_v4(addr);
+    w[0] = v.x; w[1] = v.y; w[2] = v.z; w[3] = v.w;
+  } else if constexpr (ALIGN == 8) {
+    const uint2 v0 = lds_v2(addr), v1 = lds_v2(addr + 8);
+    w[0] = v0.x; w[1] = v0.y; w[2] = v1.x; w[3] = v1.y;
+  } else if constexpr (ALIGN == 4) {
+#pragma unroll
+    for (int i = 0; i < 4; ++i) w[i] = lds_u32(addr + 4 * i);
+  } else {
+    lds_words_unaligned<4>(addr, w);
+  }
+}
+
+// D += A * B for one m16n8k16 tile (A row-major 16x16 f16, B column-major 16x8 f16, f32 D).
+__device__ __forceinline__ void mma16816(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2,
+                                         uint32_t a3, uint32_t b0, uint32_t b1) {
+  asm("mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, "
+      "{%8, %9}, {%0, %1, %2, %3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+// The f16 part `hi` (p = 0) or `lo` (p = 1) of v: hi = f16(v), lo = f16(v - hi).
+__device__ __forceinline__ __half part(float v, uint32_t p) {
+  const __half h = __float2half_rn(v);
+  if (p == 0) return h;
+  return __float2half_rn(v - __half2float(h));
+}
+
+constexpr uint32_t f16x2_const(uint16_t lo, uint16_t hi) {
+  return static_cast<uint32_t>(lo) | (static_cast<uint32_t>(hi) << 16);
+}
+
+// f16 bit patterns of the constants the decode uses
+constexpr uint16_t kH1 = 0x3C00;        // 1.0
+constexpr uint16_t kH16th = 0x2C00;     // 0.0625
+constexpr uint16_t kHm64 = 0xD400;      // -64
+constexpr uint16_t kHm96 = 0xD600;      // -96
+constexpr uint16_t kHm1024 = 0xE400;    // -1024
+constexpr uint16_t kHm1056 = 0xE420;    // -1056
+
+// ---------------------------------------------------------------- Q6_K block
+
+// 16 bytes at a 16-byte window offset, from the 32-byte aligned window [base, base + 32):
+// words W..W+3 of it, funnel-shifted right by fs bits (0 or 16).
+template <int W>
+__device__ __forceinline__ void lds16_window(uint32_t base, uint32_t fs, uint32_t (&out)[4]) {
+  const uint4 v0 = lds_v4(base), v1 = lds_v4(base + 16);
+  const uint32_t w[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
+#pragma unroll
+  for (int k = 0; k < 4; ++k) out[k] = __funnelshift_r(w[W + k], w[W + k + 1], fs);
+}
+
+// The quants of one Q6_K super-block for thread (g, c): L[hf][row][i] = ql words (16 bytes at
+// 64 hf + 16c), Q[hf][row][i] = qh words (16 bytes at 128 + 32 hf + 16 (c & 1)), rows g and g+8.
+// MODE -1: every address 16-byte aligned; 0..3: all lanes share the offset 4 MODE + fs/8 within
+// 16 bytes (two 16-byte loads and a funnel shift); -2: anything (4-byte loads and funnel shifts).
+template <int MODE>
+__device__ __forceinline__ void q6_load(uint32_t ag, uint32_t ah, uint32_t c, uint32_t fs,
+                                        uint32_t (&L)[2][2][4], uint32_t (&Q)[2][2][4]) {
+#pragma unroll
+  for (int hf = 0; hf < 2; ++hf)
+#pragma unroll
+    for (int r = 0; r < 2; ++r) {
+      const uint32_t base = r ? ah : ag;
+      const uint32_t al = base + 64 * hf + 16 * c, aq = base + 128 + 32 * hf + 16 * (c & 1);
+      if constexpr (MODE == -1) {
+        lds16<16>(al, L[hf][r]);
+        lds16<16>(aq, Q[hf][r]);
+      } else if constexpr (MODE >= 0) {
+        lds16_window<MODE>(al & ~15u, fs, L[hf][r]);
+        lds16_window<MODE>(aq & ~15u, fs, Q[hf][r]);
+      } else {
+        lds16<2>(al, L[hf][r]);
+        lds16<2>(aq, Q[hf][r]);
+      }
+    }
+}
+
+// One Q6_K super-block of rows g (at shared address ag) and g+8 (ah) for thread (g, c) of a warp,
+// from its quants L, Q: 16 MMAs, A = q - 32 exactly (lo halves hold 1024 + q, hi halves
+// 1024 + 16 q), the eight MMA columns being the eight 16-element sub-blocks of a half; then
+// y += d * sum_n sc_n D_n.
+__device__ __forceinline__ void q6_block(uint32_t ag, uint32_t ah, uint32_t c, uint32_t tab_kb,
+                                         uint32_t k24, uint32_t kT, uint32_t kT13, float dg,
+                                         float dh, const uint32_t (&L)[2][2][4],
+                                         const uint32_t (&Q)[2][2][4], float (&yacc)[2][2]) {
+#pragma unroll
+  for (int hf = 0; hf < 2; ++hf) {
+    float acc0[4] = {0.f, 0.f, 0.f, 0.f}, acc1[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+#pragma unroll
+      for (int o = 0; o < 2; ++o) {
+        // byte pairs (0, 2) for o = 0, (1, 3) for o = 1
+        const uint32_t Lg = o ? mulhi(L[hf][0][i], k24) : L[hf][0][i];
+        const uint32_t Lh = o ? mulhi(L[hf][1][i], k24) : L[hf][1][i];
+        const uint32_t Tg = o ? mulhi(Q[hf][0][i], kT13) : mullo(Q[hf][0][i], kT);
+        const uint32_t Th = o ? mulhi(Q[hf][1][i], kT13) : mullo(Q[hf][1][i], kT);
+        const uint32_t lo_g = lop_and_or(Lg, 0x000F000Fu, lop_and_or(Tg, 0x00300030u, kMagic));
+        const uint32_t lo_h = lop_and_or(Lh, 0x000F000Fu, lop_and_or(Th, 0x00300030u, kMagic));
+        const uint32_t hi_g = lop_and_or(Lg, 0x00F000F0u, lop_and_or(Tg, 0x03000300u, kMagic));
+        const uint32_t hi_h = lop_and_or(Lh, 0x00F000F0u, lop_and_or(Th, 0x03000300u, kMagic));
+        const uint32_t a0 = hadd2(lo_g, f16x2_const(kHm1056, kHm1056));
+        const uint32_t a1 = hadd2(lo_h, f16x2_const(kHm1056, kHm1056));
+        const uint32_t a2 = hfma2(hi_g, f16x2_const(kH16th, kH16th), f16x2_const(kHm96, kHm96));
+        const uint32_t a3 = hfma2(hi_h, f16x2_const(kH16th, kH16th), f16x2_const(kHm96, kHm96));
+        const uint2 bf = lds_v2(tab_kb + (hf * 8 + 2 * i + o) * 64);
+        if (o == 0)
+          mma16816(acc0, a0, a1, a2, a3, bf.x, bf.y);
+        else
+          mma16816(acc1, a0, a1, a2, a3, bf.x, bf.y);
+      }
+    }
+    // columns 2c, 2c+1 = sub-blocks 2c, 2c+1 of this half: scales 8 hf + 2c, +1
+    const uint32_t sg = lds_u16(ag + 192 + 8 * hf + 2 * c);
+    const uint32_t sh = lds_u16(ah + 192 + 8 * hf + 2 * c);
+    const float sg0 = static_cast<float>(static_cast<int8_t>(sg & 0xffu));
+    const float sg1 = static_cast<float>(static_cast<int8_t>(sg >> 8));
+    const float sh0 = static_cast<float>(static_cast<int8_t>(sh & 0xffu));
+    const float sh1 = static_cast<float>(static_cast<int8_t>(sh >> 8));
+    yacc[0][0] += dg * fmaf(sg0, acc0[0] + acc1[0], sg1 * (acc0[1] + acc1[1]));
+    yacc[1][0] += dh * fmaf(sh0, acc0[2] + acc1[2], sh1 * (acc0[3] + acc1[3]));
+  }
+}
+
+// ---------------------------------------------------------------- the kernel
+
+// QT: 4 or 6. NT: n8 tiles per MMA step (2 when batch 5..8 takes hi and lo in separate tiles).
+// HILO: x enters as hi + lo (else hi only).
+template <int QT, int NT, bool HILO>
+__global__ void __launch_bounds__((kMaxWarps + 1) * 32, 1) warpmma_kernel(const WarpMmaArgs a) {
+  constexpr uint32_t kBlk = QT == 4 ? kQ4KBytes : kQ6KBytes;
+  constexpr int kTarget = QT == 4 ? 10 : 14;  // x is scaled so that max |x| < 2^kTarget
+
+  extern __shared__ __align__(128) uint8_t smem[];
+  __shared__ int s_failed;
+  __shared__ double s_sq[kMaxWarps][8];  // [consumer warp][vector] sums of squares of x
+  __shared__ float s_ns[8];                // per vector: the RMS-norm factor (1 without norm)
+
+  uint8_t* base = smem + ((128u - (smem_u32(smem) & 127u)) & 127u);
+  const uint32_t ring_s = smem_u32(base);
+  const uint32_t table_s = ring_s + a.table_off;
+  const uint32_t mtable_s = ring_s + a.mtable_off;
+  float* ublk = reinterpret_cast<float*>(base + a.ublk_off);  // [vector][block]: 2^-shift of x
+  float* red = reinterpret_cast<float*>(base + a.red_off);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(base + a.bars_off);
+  auto full_bar = [&](uint32_t s) { return smem_u32(&bars[s]); };
+  auto empty_bar = [&](uint32_t s) { return smem_u32(&bars[a.ring + s]); };
+
+  const uint32_t nwc = a.nwc;
+  const uint32_t nthr = nwc * 32;
+  const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint64_t RB = a.row_bytes;
+
+  const uint64_t units = a.rows / a.row_unit;
+  const uint32_t r_begin = static_cast<uint32_t>(units * blockIdx.x / gridDim.x) * a.row_unit;
+  const uint32_t r_end = static_cast<uint32_t>(units * (blockIdx.x + 1) / gridDim.x) * a.row_unit;
+  const uint32_t nbands = (r_end - r_begin + kTileRows - 1) / kTileRows;
+  const uint32_t ntiles = nbands * a.nkt;
+
+  if (threadIdx.x == 0) {
+    s_failed = 0;
+    for (uint32_t s = 0; s < a.ring; ++s) {
+      mbar_init(full_bar(s), 1);
+      mbar_init(empty_bar(s), nwc);
+    }
+    fence_mbar_init();
+  }
+  __syncthreads();
+  pdl_launch_dependents();
+
+  // ------------------------------------------------------------------ producer warp
+  // Lane r of the producer warp copies row r of each tile (16 rows, one bulk copy each, at the
+  // padded pitch); lane 0 posts the tile's byte count on its slot's mbarrier.
+  if (warp == nwc) {
+    if (!(a.flags & KQ_FLAG_WEIGHTS_STATIC)) pdl_wait();
+    const uint64_t pol = policy_evict_first();
+    const uint64_t end_floor = a.total_bytes & ~uint64_t(15);
+    uint32_t s = 0, phase = 0;
+    for (uint32_t t = 0; t < ntiles; ++t) {
+      if (t >= a.ring) {
+        int ok = 1;
+        if (lane == 0) {
+          if (s_failed) {
+            ok = 0;
+          } else if (!mbar_wait_sleep(empty_bar(s), phase ^ 1)) {
+            s_failed = 1;
+            report_error(a.err, kErrWaitEmpty);
+            ok = 0;
+          }
+        }
+        if (!__shfl_sync(0xffffffffu, ok, 0)) break;
+      }
+      const uint32_t band = t / a.nkt, kt = t % a.nkt;
+      const uint32_t r0 = r_begin + band * kTileRows;
+      const uint32_t r1 = min(r0 + kTileRows, r_end);
+      const uint32_t slot = ring_s + s * a.slot_bytes;
+      const uint32_t kc0 = kt * a.nb / a.nkt, kc1 = (kt + 1) * a.nb / a.nkt;
+      const uint32_t r = r0 + lane;
+      uint64_t a0 = 0, a1 = 0;
+      if (lane < kTileRows && r < r1) {
+        const uint64_t b0 = uint64_t(r) * RB + uint64_t(kc0) * kBlk;
+        const uint64_t b1 = uint64_t(r) * RB + uint64_t(kc1) * kBlk;
+        a0 = b0 & ~uint64_t(15);
+        a1 = (b1 + 15) & ~uint64_t(15);
+        if (a1 > end_floor) {
+          // the end of W is off a 16-byte boundary: its last bytes (an even count, < 16) are
+          // read with plain loads
+          const uint32_t dst = slot + lane * a.seg_bytes;
+          for (uint64_t i = end_floor; i < a.total_bytes; i += 2)
+            sts_u16(dst + static_cast<uint32_t>(i - a0),
+                    __ldg(reinterpret_cast<const unsigned short*>(a.W + i)));
+          a1 = end_floor;
+        }
+        if (a1 < a0) a1 = a0;
+      }
+      uint32_t bytes = static_cast<uint32_t>(a1 - a0), total = bytes;
+#pragma unroll
+      for (int o = 16; o; o >>= 1) total += __shfl_xor_sync(0xffffffffu, total, o);
+      __syncwarp();
+      if (lane == 0) mbar_arrive_expect_tx(full_bar(s), total);
+      __syncwarp();
+      if (bytes) bulk_g2s(slot + lane * a.seg_bytes, a.W + a0, bytes, full_bar(s), pol);
+      if (++s == a.ring) {
+        s = 0;
+        phase ^= 1;
+      }
+    }
+    return;
+  }
+
+  // ------------------------------------------------------------------ consumers
+  const uint32_t tid = threadIdx.x;  // 0 .. nthr-1
+  const uint32_t g = lane >> 2, c = lane & 3;
+  const uint32_t B = a.batch;
+
+  pdl_wait();  // x may be the previous kernel's output
+
+  // ---- x prologue, one pass. Each warp takes 256-element blocks of x (one super-block of one
+  // vector: an "x-block"), four at a time with all 32 loads of a lane in flight. Per x-block:
+  //  * the sum of squares (f64, for the RMS norm, which is a scalar and is applied to y at the
+  //    end) and max |x|;
+  //  * a power of two s for the block: 1 when max |x| is in [1, 2^kTarget), else the one that
+  //    brings it just under 2^kTarget (f16 never overflows, Q4_K's sub-block sums of x included;
+  //    tiny blocks do not sink into f16 subnormals; small-integer inputs stay exact); 1/s is
+  //    kept for the fix-up;
+  //  * the scaled values, split into f16 parts, go to their places in the B-fragment table;
+  //  * Q4_K: the sums of its eight 32-element sub-blocks (a reduce-scatter by shuffles).
+  {
+    if (lane == 0)
+      for (int b = 0; b < 8; ++b) s_sq[warp][b] = 0.0;
+    const uint32_t nxb = a.nb * B;
+    for (uint32_t xb0 = warp; xb0 < nxb; xb0 += 4 * nwc) {
+      float v[4][8];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const uint32_t xb = xb0 + j * nwc;
+        if (xb < nxb) {
+          const uint32_t b = xb / a.nb, kb = xb - b * a.nb;
+          const float* src = a.x + b * a.ldx + kb * kQK + lane;
+#pragma unroll
+          for (int r = 0; r < 8; ++r) v[j][r] = src[32 * r];
+        }
+      }
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const uint32_t xb = xb0 + j * nwc;
+        if (xb >= nxb) break;
+        const uint32_t b = xb / a.nb, kb = xb - b * a.nb;
+        double sq = 0.0;
+        float mx = 0.f;
+#pragma unroll
+        for (int r = 0; r < 8; ++r) {
+          sq = fma(static_cast<double>(v[j][r]), static_cast<double>(v[j][r]), sq);
+          mx = fmaxf(mx, fabsf(v[j][r]));
+        }
+#pragma unroll
+        for (int o = 16; o; o >>= 1) {
+          sq += __shfl_xor_sync(0xffffffffu, sq, o);
+          mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+        }
+        int e = 1;
+        if (mx > 0.f && isfinite(mx)) frexpf(mx, &e);  // mx = f * 2^e, f in [0.5, 1)
+        const int sh = (e > kTarget || e <= 0) ? max(-126, min(126, kTarget - e)) : 0;
+        const float sc = ldexpf(1.f, sh);
+        if (lane == 0) {
+          s_sq[warp][b] += sq;
+          ublk[b * a.nb + kb] = ldexpf(1.f, -sh);
+        }
+#pragma unroll
+        for (int r = 0; r < 8; ++r) v[j][r] *= sc;
+        if constexpr (QT == 4) {
+          // entry (kb, t, n, m, c), 8 bytes at ((kb NT + t) ncol + n) kNStride + 32 m + 8 c:
+          // regs (b0b1, b2b3) of thread (g = n, c) in MMA m of block kb, n-tile t. For
+          // MMA m = 2i + o, thread c holds b0b1 = x[64c + 4i + o], x[64c + 32 + 4i + o + 2] and
+          // b2b3 = x[64c + 32 + 4i + o], x[64c + 4i + o + 2]: element 64c + 32 hb + 4i + w
+          // (w = o + 2 s2) sits in reg hb ^ s2, half s2. Here element = 32 r + lane.
+          const uint32_t i = (lane >> 2) & 7, w = lane & 3;
+          const uint32_t o = w & 1, s2 = w >> 1;
+          const uint32_t m = 2 * i + o;
+#pragma unroll
+          for (int r = 0; r < 8; ++r) {
+            const uint32_t c_r = r >> 1, hb = r & 1;
+            const uint32_t within = 32 * m + 8 * c_r + (((hb ^ s2) << 2) | (s2 << 1));
+#pragma unroll
+            for (uint32_t pp = 0; pp < (HILO ? 2u : 1u); ++pp) {
+              const uint32_t t = (HILO && NT == 2) ? pp : 0u;
+              const uint32_t n = HILO ? (NT == 1 ? 2 * b + pp : b) : b;
+              sts_u16(table_s + ((kb * NT + t) * a.ncol + n) * kNStride + within,
+                      __half_as_ushort(part(v[j][r], pp)));
+            }
+          }
+          // sub-block sums X_r = sum over lanes of v[r]: reduce-scatter by lane bits 4, 3, 2,
+          // then a butterfly over bits 1, 0; lane l ends with X_((l >> 2) & 7).
+          float w4[4], w2[2];
+          const bool b4 = (lane >> 4) & 1, b3 = (lane >> 3) & 1, b2 = (lane >> 2) & 1;
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            const float keep = b4 ? v[j][q + 4] : v[j][q], give = b4 ? v[j][q] : v[j][q + 4];
+            w4[q] = keep + __shfl_xor_sync(0xffffffffu, give, 16);
+          }
+#pragma unroll
+          for (int q = 0; q < 2; ++q) {
+            const float keep = b3 ? w4[q + 2] : w4[q], give = b3 ? w4[q] : w4[q + 2];
+            w2[q] = keep + __shfl_xor_sync(0xffffffffu, give, 8);
+          }
+          float X = (b2 ? w2[1] : w2[0]) + __shfl_xor_sync(0xffffffffu, b2 ? w2[0] : w2[1], 4);
+          X += __shfl_xor_sync(0xffffffffu, X, 2);
+          X += __shfl_xor_sync(0xffffffffu, X, 1);
+          if ((lane & 3) == 0) {
+            // min entry (kb, t, n, c), 4 bytes at ((kb NT + t) ncol + n) 16 + 4c: b0b1 of the min
+            // MMA = (X_2c, X_2c+1) of vector b
+            const uint32_t jj = (lane >> 2) & 7;
+#pragma unroll
+            for (uint32_t pp = 0; pp < (HILO ? 2u : 1u); ++pp) {
+              const uint32_t t = (HILO && NT == 2) ? pp : 0u;
+              const uint32_t n = HILO ? (NT == 1 ? 2 * b + pp : b) : b;
+              sts_u16(mtable_s + ((kb * NT + t) * a.ncol + n) * 16 + 4 * (jj >> 1) + 2 * (jj & 1),
+                      __half_as_ushort(part(X, pp)));
+            }
+          }
+        } else {
+          // entry (kb, h, m, c, u) = 8 bytes, read by thread (g, c) with g & 3 == c and u = g >> 2:
+          // u = 0: (pair of sub-block c, 0); u = 1: (0, pair of sub-block c + 4). Element
+          // 128h + 64u + 16c + 4i + w (w = o + 2 s2, m = 2i + o) sits in reg u, half s2, and
+          // the same half of the other reg is zero. Here element = 32 r + lane.
+          const uint32_t i = (lane >> 2) & 3, w = lane & 3, o = w & 1, s2 = w >> 1;
+#pragma unroll
+          for (int r = 0; r < 8; ++r) {
+            const uint32_t h = r >> 2, u = (r >> 1) & 1, cc = ((r & 1) << 1) | (lane >> 4);
+            const uint32_t ent = (((kb * 2 + h) * 8 + 2 * i + o) * 4 + cc) * 2 + u;
+            sts_u16(table_s + ent * 8 + u * 4 + s2 * 2, __half_as_ushort(__float2half_rn(v[j][r])));
+            sts_u16(table_s + ent * 8 + (u ^ 1) * 4 + s2 * 2, 0);
+          }
+        }
+      }
+    }
+    // a zeroed region that lanes without a B column read their fragments from
+    for (uint32_t i = tid; i < kZeroBytes / 4; i += nthr)
+      asm volatile("st.shared.u32 [%0], %1;" ::"r"(ring_s + a.zero_off + 4 * i), "r"(0u) : "memory");
+    named_barrier(1, nthr);
+    if (tid < B) {
+      float ns = 1.f;
+      if (a.prologue == KQ_PROLOGUE_RMSNORM) {
+        double t = 0.0;
+        for (uint32_t w = 0; w < nwc; ++w) t += s_sq[w][tid];
+        ns = static_cast<float>(
+            1.0 / sqrt(t / (static_cast<double>(a.nb) * kQK) + static_cast<double>(a.eps)));
+      }
+      s_ns[tid] = ns;  // read at the flushes, which start with a barrier
+    }
+  }
+
+  // ---- per-thread constants
+  // Q4_K scale/min unpack (sub-blocks j = 2c, 2c+1; bytes p, p+1 of the header words)
+  const uint32_t p = 2 * (c & 1);
+  const bool upper = c >= 2;
+  const uint32_t sel_sc = upper ? (p | ((4 + p) << 4) | ((p + 1) << 8) | ((5 + p) << 12))
+                                : ((4 + p) | ((4 + p) << 4) | ((5 + p) << 8) | ((5 + p) << 12));
+  const uint32_t m_lo = upper ? 0x000F000Fu : 0x003F003Fu;
+  const uint32_t m_hi = upper ? 0x00300030u : 0u;
+  const uint32_t sh_m = upper ? 4u : 0u;
+  // Q6_K: the qh bit pairs of this thread's groups go to bits 4-5 / 8-9 of each byte pair, by a
+  // shift of sT = 4 (c < 2) or 2 (c >= 2) for bytes 0, 2 and of 8 - sT right for bytes 1, 3
+  // B-fragment table offsets of this thread; lanes without a column read the zero region
+  const bool tab_on = QT == 4 ? (g < a.ncol) : ((g & 3) == c);
+  const uint32_t tab_lane = QT == 4 ? g * kNStride + c * 8 : (c * 2 + (g >> 2)) * 8;
+  const uint32_t zero_s = ring_s + a.zero_off + (QT == 4 ? c * 8 : 0);
+  const uint32_t k24 = (1u << 24) << a.zero;              // >> 8
+  const uint32_t kT = (1u << (QT == 6 ? (c >= 2 ? 2 : 4) : 0)) << a.zero;    // << sT
+  const uint32_t kT13 = (1u << (QT == 6 ? (c >= 2 ? 26 : 28) : 0)) << a.zero;  // >> (8 - sT)
+  // the vectors whose outputs this thread accumulates (Q4_K: c, or 2c and 2c+1; Q6_K: 0)
+  const uint32_t vb0 = QT == 6 ? 0u : ((HILO && NT == 1) ? c : 2 * c);
+  const uint32_t vb1 = min(vb0 + 1, B - 1);
+  const uint32_t vb0c = min(vb0, B - 1);
+
+  float yacc[2][2] = {{0.f, 0.f}, {0.f, 0.f}};  // rows g, g+8 x this thread's vectors
+  uint32_t s = 0, phase = 0;
+  for (uint32_t t = 0; t < ntiles; ++t) {
+    bool ok = !*reinterpret_cast<volatile int*>(&s_failed);
+    if (ok && !mbar_wait_sleep(full_bar(s), phase)) {
+      ok = false;
+      s_failed = 1;
+      report_error(a.err, kErrWaitFull);
+    }
+    // warp-uniform, so that every lane takes the same path to the (.aligned) MMAs
+    const bool failed = __any_sync(0xffffffffu, !ok);
+    const uint32_t band = t / a.nkt, kt = t % a.nkt;
+    const uint32_t r0 = r_begin + band * kTileRows;
+    const uint32_t kc0 = kt * a.nb / a.nkt, kc1 = (kt + 1) * a.nb / a.nkt;
+    const uint32_t kb = kc0 + warp;
+    const uint32_t slot = ring_s + s * a.slot_bytes;
+    if (kb < kc1 && !failed) {
+      // shared-memory addresses of this block in rows g and g+8 of the tile
+      uint32_t ag, ah;
+      {
+        const uint64_t off = uint64_t(kc0) * kBlk;
+        ag = slot + g * a.seg_bytes + static_cast<uint32_t>((uint64_t(r0 + g) * RB + off) & 15) +
+             warp * kBlk;
+        ah = slot + (g + 8) * a.seg_bytes +
+             static_cast<uint32_t>((uint64_t(r0 + g + 8) * RB + off) & 15) + warp * kBlk;
+      }
+
+      if constexpr (QT == 4) {
+        const uint4 hg = lds_v4(ag), hh = lds_v4(ah);
+        const uint4 qg0 = lds_v4(ag + 16 + 32 * c), qg1 = lds_v4(ag + 32 + 32 * c);
+        const uint4 qh0 = lds_v4(ah + 16 + 32 * c), qh1 = lds_v4(ah + 32 + 32 * c);
+        // scales -> S = (sc_lo, sc_hi/16), Z = (-1024 sc_lo, -64 sc_hi), their swaps, mins
+        uint32_t Sg, Zg, S2g, Z2g, Amg, Sh, Zh, S2h, Z2h, Amh;
+        auto prep = [&](const uint4& hd, uint32_t& S, uint32_t& Z, uint32_t& S2, uint32_t& Z2,
+                        uint32_t& Am) {
+          const uint32_t ts = __byte_perm(hd.w, hd.y, sel_sc);
+          const uint32_t M = lop_and_or(ts, m_lo, lop_and_or(ts >> 10, m_hi, kMagic));
+          S = hfma2(M, f16x2_const(kH1, kH16th), f16x2_const(kHm1024, kHm64));
+          Z = hmul2(S, f16x2_const(kHm1024, kHm1024));
+          S2 = __byte_perm(S, 0, 0x1032);
+          Z2 = __byte_perm(Z, 0, 0x1032);
+          const uint32_t tm = __byte_perm(hd.w, hd.z, sel_sc);
+          const uint32_t Mm = lop_and_or(tm >> sh_m, m_lo, lop_and_or(tm >> 10, m_hi, kMagic));
+          Am = hadd2(Mm, f16x2_const(kHm1024, kHm1024));
+        };
+        prep(hg, Sg, Zg, S2g, Z2g, Amg);
+        prep(hh, Sh, Zh, S2h, Z2h, Amh);
+        const uint32_t qg[8] = {qg0.x, qg0.y, qg0.z, qg0.w, qg1.x, qg1.y, qg1.z, qg1.w};
+        const uint32_t qh[8] = {qh0.x, qh0.y, qh0.z, qh0.w, qh1.x, qh1.y, qh1.z, qh1.w};
+        float acc0[NT][4], acc1[NT][4], accm[NT][4];
+#pragma unroll
+        for (int tt = 0; tt < NT; ++tt)
+#pragma unroll
+          for (int j = 0; j < 4; ++j) acc0[tt][j] = acc1[tt][j] = accm[tt][j] = 0.f;
+        uint32_t tab_t[NT];
+#pragma unroll
+        for (int tt = 0; tt < NT; ++tt)
+          tab_t[tt] = tab_on ? table_s + (kb * NT + tt) * a.ncol * kNStride + tab_lane : zero_s;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+#pragma unroll
+          for (int o = 0; o < 2; ++o) {
+            const uint32_t wg = o ? mulhi(qg[i], k24) : qg[i];
+            const uint32_t wh = o ? mulhi(qh[i], k24) : qh[i];
+            const uint32_t a0 = hfma2(lop_and_or(wg, 0x00F0000Fu, kMagic), Sg, Zg);
+            const uint32_t a1 = hfma2(lop_and_or(wh, 0x00F0000Fu, kMagic), Sh, Zh);
+            const uint32_t a2 = hfma2(lop_and_or(wg, 0x000F00F0u, kMagic), S2g, Z2g);
+            const uint32_t a3 = hfma2(lop_and_or(wh, 0x000F00F0u, kMagic), S2h, Z2h);
+            const uint32_t m = 2 * i + o;
+#pragma unroll
+            for (int tt = 0; tt < NT; ++tt) {
+              const uint2 bf = lds_v2(tab_t[tt] + 32 * m);
+              if (o == 0)
+                mma16816(acc0[tt], a0, a1, a2, a3, bf.x, bf.y);
+              else
+                mma16816(acc1[tt], a0, a1, a2, a3, bf.x, bf.y);
+            }
+          }
+        }
+        // the min term: A = (m_2c, m_2c+1) in slots 2c, 2c+1 of rows g, g+8
+#pragma unroll
+        for (int tt = 0; tt < NT; ++tt) {
+          const uint32_t bm =
+              lds_u32(tab_on ? mtable_s + ((kb * NT + tt) * a.ncol + g) * 16 + 4 * c : zero_s);
+          mma16816(accm[tt], Amg, Amh, 0u, 0u, bm, 0u);
+        }
+        const float dg = h2f(hg.x & 0xffffu), dmg = h2f(hg.x >> 16);
+        const float dh = h2f(hh.x & 0xffffu), dmh = h2f(hh.x >> 16);
+        const float u0 = ublk[vb0c * a.nb + kb], u1 = ublk[vb1 * a.nb + kb];
+        if constexpr (HILO && NT == 1) {
+          // columns 2c (hi) and 2c+1 (lo) are vector c
+          const float Dg = (acc0[0][0] + acc1[0][0]) + (acc0[0][1] + acc1[0][1]);
+          const float Dh = (acc0[0][2] + acc1[0][2]) + (acc0[0][3] + acc1[0][3]);
+          yacc[0][0] += u0 * (dg * Dg - dmg * (accm[0][0] + accm[0][1]));
+          yacc[1][0] += u0 * (dh * Dh - dmh * (accm[0][2] + accm[0][3]));
+        } else if constexpr (HILO) {
+          // tile 0 hi, tile 1 lo; columns 2c, 2c+1 are vectors 2c, 2c+1
+#pragma unroll
+          for (int j = 0; j < 2; ++j) {
+            const float uj = j ? u1 : u0;
+            const float Dg = (acc0[0][j] + acc1[0][j]) + (acc0[1][j] + acc1[1][j]);
+            const float Dh = (acc0[0][2 + j] + acc1[0][2 + j]) + (acc0[1][2 + j] + acc1[1][2 + j]);
+            yacc[0][j] += uj * (dg * Dg - dmg * (accm[0][j] + accm[1][j]));
+            yacc[1][j] += uj * (dh * Dh - dmh * (accm[0][2 + j] + accm[1][2 + j]));
+          }
+        } else {
+#pragma unroll
+          for (int j = 0; j < 2; ++j) {
+            const float uj = j ? u1 : u0;
+            yacc[0][j] += uj * (dg * (acc0[0][j] + acc1[0][j]) - dmg * accm[0][j]);
+            yacc[1][j] += uj * (dh * (acc0[0][2 + j] + acc1[0][2 + j]) - dmh * accm[0][2 + j]);
+          }
+        }
+      } else {
+        // Q6_K, batch 1: thread (g, c) owns sub-blocks c and c+4 of each half of the block
+        const float u0 = ublk[kb];
+        const float dg = u0 * h2f(lds_u16(ag + 208)), dh = u0 * h2f(lds_u16(ah + 208));
+        const uint32_t tab_kb = tab_on ? table_s + kb * 1024 + tab_lane : zero_s;
+        // the block's quants, loaded in the form the rows' common alignment allows
+        uint32_t L[2][2][4], Q[2][2][4];
+        const uint32_t o0 = __shfl_sync(0xffffffffu, ag & 15u, 0);
+        if (__all_sync(0xffffffffu, (ag & 15u) == o0 && (ah & 15u) == o0)) {
+          const uint32_t fs = 8 * (o0 & 3);
+          switch (o0 >> 2) {
+            case 0:
+              if (o0 == 0) q6_load<-1>(ag, ah, c, fs, L, Q);
+              else q6_load<0>(ag, ah, c, fs, L, Q);
+              break;
+            case 1: q6_load<1>(ag, ah, c, fs, L, Q); break;
+            case 2: q6_load<2>(ag, ah, c, fs, L, Q); break;
+            default: q6_load<3>(ag, ah, c, fs, L, Q); break;
+          }
+        } else {
+          q6_load<-2>(ag, ah, c, 0, L, Q);
+        }
+        q6_block(ag, ah, c, tab_kb, k24, kT, kT13, dg, dh, L, Q, yacc);
+      }
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(empty_bar(s));
+    if (++s == a.ring) {
+      s = 0;
+      phase ^= 1;
+    }
+
+    if (kt + 1 == a.nkt) {
+      // The band is done: this warp's partial rows go to the reduction buffer.
+      const uint32_t bi = band % a.fb;
+      if constexpr (QT == 6) {
+        // the four threads of a row hold different sub-blocks of vector 0
+#pragma unroll
+        for (int r = 0; r < 2; ++r) {
+          yacc[r][0] += __shfl_xor_sync(0xffffffffu, yacc[r][0], 1);
+          yacc[r][0] += __shfl_xor_sync(0xffffffffu, yacc[r][0], 2);
+        }
+        if (c == 0) {
+          red[((bi * kTileRows + g) * nwc + warp) * B] = yacc[0][0];
+          red[((bi * kTileRows + g + 8) * nwc + warp) * B] = yacc[1][0];
+        }
+      } else {
+#pragma unroll
+        for (int j = 0; j < 2; ++j) {
+          const uint32_t b = (HILO && NT == 1) ? (j == 0 ? c : 8u) : 2 * c + j;
+          if (b < B) {
+            red[((bi * kTileRows + g) * nwc + warp) * B + b] = yacc[0][j];
+            red[((bi * kTileRows + g + 8) * nwc + warp) * B + b] = yacc[1][j];
+          }
+        }
+      }
+      yacc[0][0] = yacc[0][1] = yacc[1][0] = yacc[1][1] = 0.f;
+
+      if (bi + 1 == a.fb || band + 1 == nbands) {
+        // Flush: sum every warp's partial of each row in a fixed order and write y.
+        named_barrier(1, nthr);
+        const uint32_t band0 = band - bi;
+        const uint32_t R = a.row_unit;
+        const uint32_t nout = (bi + 1) * (kTileRows / R) * B;
+        for (uint32_t o = tid; o < nout; o += nthr) {
+          const uint32_t b = o % B;
+          const uint32_t q = o / B;  // output index within the flushed bands
+          const uint32_t row16 = (q % (kTileRows / R)) * R;
+          const uint32_t bj = q / (kTileRows / R);
+          const uint32_t row = r_begin + (band0 + bj) * kTileRows + row16;
+          if (row >= r_end) continue;
+          float v0 = 0.f;
+          const float* rp = red + ((bj * kTileRows + row16) * nwc) * B + b;
+          for (uint32_t w = 0; w < nwc; ++w) v0 += rp[w * B];
+          v0 *= s_ns[b];
+          if (R == 1) {
+            a.y[b * a.ldy + row] = v0;
+          } else {
+            float v1 = 0.f;
+            const float* rq = rp + nwc * B;
+            for (uint32_t w = 0; w < nwc; ++w) v1 += rq[w * B];
+            v1 *= s_ns[b];
+            a.y[b * a.ldy + row / 2] = v0 * v1 * a.pair_scale;
+          }
+        }
+        named_barrier(1, nthr);
+      }
+    }
+  }
+}
+
+struct Variant {
+  const void* fn;
+  int qt, nt;
+  bool hilo;
+};
+
+template <int QT, int NT, bool HILO>
+Variant variant() {
+  return Variant{reinterpret_cast<const void*>(&warpmma_kernel<QT, NT, HILO>), QT, NT, HILO};
+}
+
+const Variant kVariants[] = {variant<4, 1, true>(), variant<4, 2, true>(), variant<4, 1, false>(),
+                             variant<6, 1, false>()};
+
+}  // namespace
+
+int warpmma_prepare(kq_ctx* ctx) {
+  for (const Variant& v : kVariants) {
+    const cudaError_t e =
+        cudaFuncSetAttribute(v.fn, cudaFuncAttributeMaxDynamicSharedMemorySize, ctx->max_smem);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute", "warp-MMA matvec kernel");
+  }
+  return KQ_OK;
+}
+
+bool warpmma_supports(const kq_matvec_desc& d) {
+  if (d.type == KQ_TYPE_Q4_K) return d.batch >= 1 && d.batch <= 8;
+  if (d.type == KQ_TYPE_Q6_K) return d.batch == 1;
+  return false;
+}
+
+int warpmma_matvec(kq_ctx* ctx, const kq_matvec_desc& d, uint64_t ldx, uint64_t ldy,
+                   cudaStream_t stream) {
+  const char* call = "kq_matvec";
+  const bool q4 = d.type == KQ_TYPE_Q4_K;
+  const uint32_t blk = q4 ? kQ4KBytes : kQ6KBytes;
+  const uint32_t nb = d.k / kQK;
+  const uint64_t rb = uint64_t(nb) * blk;
+  // tile: 16 row segments of up to kc super-blocks (kc = the consumer warps), one bulk copy
+  // each (the 16-byte-aligned superset, so up to 30 bytes more), at a pitch whose residue mod 128
+  // makes the consumers' 16-byte loads free of bank conflicts: 16 for Q4_K (rows g, g+1
+  // interleave their 32-byte strides), 64 for Q6_K (rows g, g+1 take the two halves of 128 B)
+  const uint32_t target = q4 ? 16u : 64u;
+  auto slot_for = [&](uint32_t kc, uint32_t& seg_out) {
+    uint32_t seg_ = ((kc * blk + 30 + 15) / 16) * 16;
+    while (seg_ % 128 != target) seg_ += 16;
+    seg_out = seg_;
+    return kTileRows * seg_;
+  };
+  uint32_t nkt = (nb + kMaxWarps - 1) / kMaxWarps;
+  uint32_t nwc = (nb + nkt - 1) / nkt;
+  uint32_t seg = 0;
+  uint32_t slot = slot_for(nwc, seg);
+
+  // mode: Q4_K hi+lo in one n-tile (batch <= 4), hi+lo in two (batch 5..8), or hi only when
+  // the table of two would not leave room for a ring of two slots
+  int mode;  // index into kVariants
+  uint32_t ncol;
+  uint64_t table_bytes, mtable_bytes;
+  const uint32_t ublk_bytes = ((nb * d.batch * 4 + 15) / 16) * 16;
+  const uint64_t fixed_min =
+      2 * uint64_t(slot) + kTileRows * nwc * d.batch * 4 + ublk_bytes + kZeroBytes + 256 + 128;
+  if (q4) {
+    auto sizes = [&](uint32_t nt_, uint32_t ncol_) {
+      table_bytes = uint64_t(nb) * nt_ * ncol_ * kNStride;
+      mtable_bytes = uint64_t(nb) * nt_ * ncol_ * 16;
+      return table_bytes + mtable_bytes;
+    };
+    if (d.batch <= 4 && sizes(1, 2 * d.batch) + fixed_min <= uint64_t(ctx->max_smem)) {
+      mode = 0, ncol = 2 * d.batch;
+    } else if (d.batch > 4 && sizes(2, d.batch) + fixed_min <= uint64_t(ctx->max_smem)) {
+      mode = 1, ncol = d.batch;
+    } else {
+      mode = 2, ncol = d.batch;
+      sizes(1, d.batch);
+    }
+  } else {
+    mode = 3, ncol = 8;
+    table_bytes = uint64_t(nb) * 1024;
+    mtable_bytes = 0;
+  }
+  // Narrower K-tiles (fewer consumer warps, smaller slots) until two slots and one band of
+  // partial rows fit beside the table.
+  auto need_for = [&](uint32_t slot_, uint32_t nwc_) {
+    return table_bytes + mtable_bytes + ublk_bytes + kZeroBytes + 16 + 2 * 8 * 8 + 128 +
+           2 * uint64_t(slot_) + uint64_t(kTileRows) * nwc_ * d.batch * 4;
+  };
+  while (need_for(slot, nwc) > uint64_t(ctx->max_smem) && nwc > 1) {
+    ++nkt;
+    nwc = (nb + nkt - 1) / nkt;
+    slot = slot_for(nwc, seg);
+  }
+  if (need_for(slot, nwc) > uint64_t(ctx->max_smem))
+    return fail(KQ_E_UNSUPPORTED, call,
+                "k " + std::to_string(d.k) + " with batch " + std::to_string(d.batch) +
+                    " does not fit the warp-MMA kernel's shared memory");
+  // partial rows of up to 16 bands between flushes, in what two ring slots leave
+  const uint32_t band_red = kTileRows * nwc * d.batch * 4;
+  const uint64_t base_need = need_for(slot, nwc) - band_red;
+  const uint32_t fb = static_cast<uint32_t>(std::min<uint64_t>(
+      16, std::min<uint64_t>(kRedBudget, uint64_t(ctx->max_smem) - base_need) / band_red));
+  const uint32_t red_bytes = fb * band_red;
+  const uint64_t tail =
+      table_bytes + mtable_bytes + ublk_bytes + kZeroBytes + 16 + red_bytes + 2 * 8 * 8 + 128;
+  uint32_t ring = std::min<uint64_t>(8, (uint64_t(ctx->max_smem) - tail) / slot);
+  ring = std::max<uint32_t>(2, ring);
+
+  WarpMmaArgs args;
+  args.W = reinterpret_cast<const uint8_t*>(d.w);
+  args.x = reinterpret_cast<const float*>(d.x);
+  args.y = reinterpret_cast<float*>(d.y);
+  args.err = ctx->err;
+  args.ldx = ldx;
+  args.ldy = ldy;
+  args.total_bytes = uint64_t(d.rows) * rb;
+  args.row_bytes = rb;
+  args.rows = d.rows;
+  args.nb = nb;
+  args.batch = d.batch;
+  args.nkt = nkt;
+  args.nwc = nwc;
+  args.ring = ring;
+  args.slot_bytes = slot;
+  args.seg_bytes = seg;
+  args.table_off = ring * slot;
+  args.mtable_off = static_cast<uint32_t>(args.table_off + table_bytes);
+  args.ublk_off = static_cast<uint32_t>(((args.mtable_off + mtable_bytes + 15) / 16) * 16);
+  args.zero_off = args.ublk_off + ublk_bytes;
+  args.red_off = args.zero_off + kZeroBytes;
+  args.zero = 0;
+  args.bars_off = args.red_off + red_bytes;
+  args.ncol = ncol;
+  args.fb = fb;
+  args.row_unit = d.epilogue == KQ_EPILOGUE_PAIR_PRODUCT ? 2 : 1;
+  args.prologue = d.prologue;
+  args.epilogue = d.epilogue;
+  args.flags = d.flags;
+  args.eps = d.eps;
+  args.pair_scale = d.pair_scale;
+  const uint32_t smem = args.bars_off + 2 * 8 * 8 + 128;
+
+  const uint64_t units = d.rows / args.row_unit;
+  const uint32_t grid = static_cast<uint32_t>(std::min<uint64_t>(ctx->sm_count, units));
+
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3((nwc + 1) * 32);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = (d.flags & KQ_FLAG_NO_PDL) ? 0 : 1;
+  void* params[] = {&args};
+  const cudaError_t e = cudaLaunchKernelExC(&cfg, kVariants[mode].fn, params);
+  if (e != cudaSuccess)
+    return cuda_fail(e, "cudaLaunchKernelExC",
+                     "warp-MMA matvec grid " + std::to_string(grid) + " x " +
+                         std::to_string((nwc + 1) * 32) + " threads, " + std::to_string(smem) +
+                         " B shared");
+  return KQ_OK;
+}
+
+}  // namespace kq

@@ -98,12 +98,14 @@ SHAPES = [
 ]
 
 
+@pytest.mark.parametrize("path", ["auto", "cuda_cores"])
 @pytest.mark.parametrize("qtype,rows,K,batch", SHAPES)
-def test_matvec_matches_oracle(kernels, qtype, rows, K, batch):
+def test_matvec_matches_oracle(kernels, qtype, rows, K, batch, path):
     key = kb.stream_key(1000 + rows, K * 10 + qtype)
     W = dev_weights(kernels, qtype, rows, K, key)
     x = np.random.default_rng(rows * 7 + K + batch).standard_normal((batch, K), dtype=np.float32)
-    y = run_matvec(kernels, qtype, W, x, rows, K)
+    flags = kb.FLAG_CUDA_CORES if path == "cuda_cores" else 0
+    y = run_matvec(kernels, qtype, W, x, rows, K, flags=flags)
     y_ref, bound = oracle.matvec_ref(qtype, W.cpu().numpy(), x, K, 0, rows)
     check(y, y_ref, bound, f"q{qtype} {rows}x{K} b{batch}")
 
