@@ -77,6 +77,7 @@ struct WarpMmaArgs {
   uint32_t ring, slot_bytes, seg_bytes;  // seg_bytes: shared-memory pitch of a tile's rows
   uint32_t table_off, mtable_off, ublk_off, zero_off, red_off, bars_off;  // shared-memory layout
   uint32_t zero;         // 0: multipliers built from it are opaque to the compiler
+  uint32_t row_perm;     // 1: MMA row pairs are tile rows two apart (see pg)
   uint32_t ncol;         // B columns in use per n-tile
   uint32_t fb;           // bands of partial rows kept before a flush
   uint32_t row_unit, prologue, epilogue, flags;
@@ -330,7 +331,20 @@ __global__ void __launch_bounds__((kMaxWarps + 1) * 32, 1) warpmma_kernel(const 
       const uint32_t kc0 = kt * a.nb / a.nkt, kc1 = (kt + 1) * a.nb / a.nkt;
       const uint32_t r = r0 + lane;
       uint64_t a0 = 0, a1 = 0;
-      if (lane < kTileRows && r < r1) {
+      if (a.seg_bytes == 0) {
+        // whole rows: one copy of the tile's 16-byte-aligned superset, by lane 0
+        if (lane == 0) {
+          a0 = (uint64_t(r0) * RB) & ~uint64_t(15);
+          a1 = (uint64_t(r1) * RB + 15) & ~uint64_t(15);
+          if (a1 > end_floor) {
+            for (uint64_t i = end_floor; i < a.total_bytes; i += 2)
+              sts_u16(slot + static_cast<uint32_t>(i - a0),
+                      __ldg(reinterpret_cast<const unsigned short*>(a.W + i)));
+            a1 = end_floor;
+          }
+          if (a1 < a0) a1 = a0;
+        }
+      } else if (lane < kTileRows && r < r1) {
         const uint64_t b0 = uint64_t(r) * RB + uint64_t(kc0) * kBlk;
         const uint64_t b1 = uint64_t(r) * RB + uint64_t(kc1) * kBlk;
         a0 = b0 & ~uint64_t(15);
@@ -353,6 +367,7 @@ __global__ void __launch_bounds__((kMaxWarps + 1) * 32, 1) warpmma_kernel(const 
       if (lane == 0) mbar_arrive_expect_tx(full_bar(s), total);
       __syncwarp();
       if (bytes) bulk_g2s(slot + lane * a.seg_bytes, a.W + a0, bytes, full_bar(s), pol);
+      // (whole-row tiles: only lane 0 has bytes, and its destination is the slot itself)
       if (++s == a.ring) {
         s = 0;
         phase ^= 1;
@@ -521,6 +536,10 @@ __global__ void __launch_bounds__((kMaxWarps + 1) * 32, 1) warpmma_kernel(const 
   const uint32_t k24 = (1u << 24) << a.zero;              // >> 8
   const uint32_t kT = (1u << (QT == 6 ? (c >= 2 ? 2 : 4) : 0)) << a.zero;    // << sT
   const uint32_t kT13 = (1u << (QT == 6 ? (c >= 2 ? 26 : 28) : 0)) << a.zero;  // >> (8 - sT)
+  // MMA rows g and g+8 of this thread are tile rows pg and pg+8. With whole-row tiles whose row
+  // pitch is 32 or 96 mod 128 bytes, MMA rows (0,1), (2,3), ... are tile rows (0,2), (1,3), ...,
+  // 64 bytes apart mod 128, so the two rows of a quarter-warp's 16-byte loads take disjoint banks.
+  const uint32_t pg = a.row_perm ? ((g & 4) | ((g & 1) << 1) | ((g >> 1) & 1)) : g;
   // the vectors whose outputs this thread accumulates (Q4_K: c, or 2c and 2c+1; Q6_K: 0)
   const uint32_t vb0 = QT == 6 ? 0u : ((HILO && NT == 1) ? c : 2 * c);
   const uint32_t vb1 = min(vb0 + 1, B - 1);
@@ -545,12 +564,17 @@ __global__ void __launch_bounds__((kMaxWarps + 1) * 32, 1) warpmma_kernel(const 
     if (kb < kc1 && !failed) {
       // shared-memory addresses of this block in rows g and g+8 of the tile
       uint32_t ag, ah;
-      {
+      if (a.seg_bytes == 0) {
+        // whole rows back to back from the tile's aligned start
+        const uint32_t delta = static_cast<uint32_t>((uint64_t(r0) * RB) & 15);
+        ag = slot + delta + static_cast<uint32_t>(pg * RB) + warp * kBlk;
+        ah = ag + static_cast<uint32_t>(8 * RB);
+      } else {
         const uint64_t off = uint64_t(kc0) * kBlk;
-        ag = slot + g * a.seg_bytes + static_cast<uint32_t>((uint64_t(r0 + g) * RB + off) & 15) +
+        ag = slot + pg * a.seg_bytes + static_cast<uint32_t>((uint64_t(r0 + pg) * RB + off) & 15) +
              warp * kBlk;
-        ah = slot + (g + 8) * a.seg_bytes +
-             static_cast<uint32_t>((uint64_t(r0 + g + 8) * RB + off) & 15) + warp * kBlk;
+        ah = slot + (pg + 8) * a.seg_bytes +
+             static_cast<uint32_t>((uint64_t(r0 + pg + 8) * RB + off) & 15) + warp * kBlk;
       }
 
       if constexpr (QT == 4) {
@@ -682,16 +706,16 @@ __global__ void __launch_bounds__((kMaxWarps + 1) * 32, 1) warpmma_kernel(const 
           yacc[r][0] += __shfl_xor_sync(0xffffffffu, yacc[r][0], 2);
         }
         if (c == 0) {
-          red[((bi * kTileRows + g) * nwc + warp) * B] = yacc[0][0];
-          red[((bi * kTileRows + g + 8) * nwc + warp) * B] = yacc[1][0];
+          red[((bi * kTileRows + pg) * nwc + warp) * B] = yacc[0][0];
+          red[((bi * kTileRows + pg + 8) * nwc + warp) * B] = yacc[1][0];
         }
       } else {
 #pragma unroll
         for (int j = 0; j < 2; ++j) {
           const uint32_t b = (HILO && NT == 1) ? (j == 0 ? c : 8u) : 2 * c + j;
           if (b < B) {
-            red[((bi * kTileRows + g) * nwc + warp) * B + b] = yacc[0][j];
-            red[((bi * kTileRows + g + 8) * nwc + warp) * B + b] = yacc[1][j];
+            red[((bi * kTileRows + pg) * nwc + warp) * B + b] = yacc[0][j];
+            red[((bi * kTileRows + pg + 8) * nwc + warp) * B + b] = yacc[1][j];
           }
         }
       }
@@ -783,6 +807,14 @@ int warpmma_matvec(kq_ctx* ctx, const kq_matvec_desc& d, uint64_t ldx, uint64_t 
   uint32_t nwc = (nb + nkt - 1) / nkt;
   uint32_t seg = 0;
   uint32_t slot = slot_for(nwc, seg);
+  // A tile of whole rows goes in one copy (the copy engine's cost is per copy, ~75 ns per SM,
+  // so many small copies cap the bandwidth), its rows back to back.
+  auto whole_rows = [&]() {
+    if (nkt != 1) return;
+    seg = 0;
+    slot = static_cast<uint32_t>(((uint64_t(kTileRows) * rb + 32 + 127) / 128) * 128);
+  };
+  whole_rows();
 
   // mode: Q4_K hi+lo in one n-tile (batch <= 4), hi+lo in two (batch 5..8), or hi only when
   // the table of two would not leave room for a ring of two slots
@@ -822,6 +854,8 @@ int warpmma_matvec(kq_ctx* ctx, const kq_matvec_desc& d, uint64_t ldx, uint64_t 
     nwc = (nb + nkt - 1) / nkt;
     slot = slot_for(nwc, seg);
   }
+  const uint32_t rb128 = static_cast<uint32_t>(rb % 128);
+  const uint32_t row_perm = (seg == 0 && (rb128 == 32 || rb128 == 96)) ? 1u : 0u;
   if (need_for(slot, nwc) > uint64_t(ctx->max_smem))
     return fail(KQ_E_UNSUPPORTED, call,
                 "k " + std::to_string(d.k) + " with batch " + std::to_string(d.batch) +
@@ -860,6 +894,7 @@ int warpmma_matvec(kq_ctx* ctx, const kq_matvec_desc& d, uint64_t ldx, uint64_t 
   args.zero_off = args.ublk_off + ublk_bytes;
   args.red_off = args.zero_off + kZeroBytes;
   args.zero = 0;
+  args.row_perm = row_perm;
   args.bars_off = args.red_off + red_bytes;
   args.ncol = ncol;
   args.fb = fb;
