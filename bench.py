@@ -60,6 +60,8 @@ def parse_args(argv=None):
     ap.add_argument("--batch", type=int, default=1)
     ap.add_argument("--path", default="auto", choices=["auto", "tc", "cc", "wm"],
                     help="tensor cores (tcgen05), CUDA cores, warp-level MMA, or the library's choice")
+    ap.add_argument("--extra-flags", type=lambda v: int(v, 0), default=0,
+                    help="more descriptor flag bits OR-ed into every timed launch (A/B tests)")
     ap.add_argument("--impl", default="kq", choices=["kq", "reference"])
     ap.add_argument("--exchange", default="nccl", choices=["nccl", "push"],
                     help="sharded stacks: NCCL all-gathers, or the matvec's own push to peer memory")
@@ -281,7 +283,7 @@ def main(argv=None):
 
     def step(i, s):
         kernels.matvec(qtype, y, Ws[i % copies], x, rows, K, batch,
-                       flags=kb.FLAG_WEIGHTS_STATIC | path_flag, stream=s)
+                       flags=kb.FLAG_WEIGHTS_STATIC | path_flag | args.extra_flags, stream=s)
 
     # The timed loop replays CUDA graphs of launches (captured with their programmatic-
     # dependent-launch edges): a graph of G steps, G a multiple of the weight copies so that

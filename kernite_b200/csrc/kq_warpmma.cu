@@ -62,6 +62,13 @@ constexpr uint32_t kRedBudget = 16384;  // bytes of shared memory for partial ro
 constexpr uint32_t kNStride = 16 * 32 + 32;
 constexpr uint32_t kZeroBytes = 1024 + 64;  // covers every MMA offset of one block's fragments
 
+// A descriptor flag bit outside the public KQ_FLAG_* set: batch 1 on the other of the two
+// warp-MMA variants (Q4_K: integer instead of f16 operands, Q6_K: f16 instead of integer), so
+// both stay reachable for tests and A/B timing. The defaults are the faster one per type
+// (measured on B200: equal speed for Q6_K, where the integer variant's 24-bit x is the more
+// accurate; f16 7% faster for Q4_K).
+constexpr uint32_t kFlagAltBatch1 = 1u << 30;
+
 constexpr uint32_t kMagic = 0x64006400u;  // f16x2 (1024, 1024): OR a 10-bit field in = 1024 + v
 
 struct WarpMmaArgs {
@@ -163,6 +170,27 @@ constexpr uint32_t f16x2_const(uint16_t lo, uint16_t hi) {
   return static_cast<uint32_t>(lo) | (static_cast<uint32_t>(hi) << 16);
 }
 
+// D += A * B for one m16n8k32 integer tile (A row-major 16x32 u8, B column-major 32x8 s8, s32 D).
+__device__ __forceinline__ void imma16832(int (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2,
+                                          uint32_t a3, uint32_t b0, uint32_t b1) {
+  asm("mma.sync.aligned.m16n8k32.row.col.s32.u8.s8.s32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, "
+      "{%8, %9}, {%0, %1, %2, %3};"
+      : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+// x as three signed byte limbs: v = L2 * 2^16 + L1 * 2^8 + L0 for an integer |v| <= 2^22.
+__device__ __forceinline__ float limbs_to_f32(int l2, int l1, int l0) {
+  return fmaf(static_cast<float>(l2), 65536.f, static_cast<float>(l1 * 256 + l0));
+}
+
+// A small unsigned integer (< 2^23) in byte 0..1 or 2..3 of w as an f32, without the XU pipe:
+// the bytes go under the exponent of 2^23 and 2^23 comes off.
+template <int HALF>
+__device__ __forceinline__ float u16_to_f32(uint32_t w) {
+  return __uint_as_float(__byte_perm(w, 0x4B000000u, HALF ? 0x7432u : 0x7410u)) - 8388608.f;
+}
+
 // f16 bit patterns of the constants the decode uses
 constexpr uint16_t kH1 = 0x3C00;        // 1.0
 constexpr uint16_t kH16th = 0x2C00;     // 0.0625
@@ -207,6 +235,29 @@ __device__ __forceinline__ void q6_load(uint32_t ag, uint32_t ah, uint32_t c, ui
         lds16<2>(aq, Q[hf][r]);
       }
     }
+}
+
+// The quants of half hf of one Q6_K super-block for thread (g, c), rows g and g+8: L[row] = the
+// 16 ql bytes at 64 hf + 16c, Q[row] = the 16 qh bytes at 128 + 32 hf + 16 (c & 1). MODE as
+// for q6_load.
+template <int MODE>
+__device__ __forceinline__ void q6_load_half(uint32_t ag, uint32_t ah, uint32_t c, uint32_t hf,
+                                             uint32_t fs, uint32_t (&L)[2][4], uint32_t (&Q)[2][4]) {
+#pragma unroll
+  for (int r = 0; r < 2; ++r) {
+    const uint32_t base = r ? ah : ag;
+    const uint32_t al = base + 64 * hf + 16 * c, aq = base + 128 + 32 * hf + 16 * (c & 1);
+    if constexpr (MODE == -1) {
+      lds16<16>(al, L[r]);
+      lds16<16>(aq, Q[r]);
+    } else if constexpr (MODE >= 0) {
+      lds16_window<MODE>(al & ~15u, fs, L[r]);
+      lds16_window<MODE>(aq & ~15u, fs, Q[r]);
+    } else {
+      lds16<2>(al, L[r]);
+      lds16<2>(aq, Q[r]);
+    }
+  }
 }
 
 // One Q6_K super-block of rows g (at shared address ag) and g+8 (ah) for thread (g, c) of a warp,
@@ -259,8 +310,10 @@ __device__ __forceinline__ void q6_block(uint32_t ag, uint32_t ah, uint32_t c, u
 // ---------------------------------------------------------------- the kernel
 
 // QT: 4 or 6. NT: n8 tiles per MMA step (2 when batch 5..8 takes hi and lo in separate tiles).
-// HILO: x enters as hi + lo (else hi only).
-template <int QT, int NT, bool HILO>
+// HILO: x enters as hi + lo (else hi only). I8 (batch 1): integer MMAs, A = the raw quants as
+// bytes, x as three signed byte limbs (24-bit fixed point per 256-element block), the eight MMA
+// columns separating sub-blocks.
+template <int QT, int NT, bool HILO, bool I8>
 __global__ void __launch_bounds__((kMaxWarps + 1) * 32, 1) warpmma_kernel(const WarpMmaArgs a) {
   constexpr uint32_t kBlk = QT == 4 ? kQ4KBytes : kQ6KBytes;
   constexpr int kTarget = QT == 4 ? 10 : 14;  // x is scaled so that max |x| < 2^kTarget
@@ -328,7 +381,9 @@ __global__ void __launch_bounds__((kMaxWarps + 1) * 32, 1) warpmma_kernel(const 
       const uint32_t r0 = r_begin + band * kTileRows;
       const uint32_t r1 = min(r0 + kTileRows, r_end);
       const uint32_t slot = ring_s + s * a.slot_bytes;
-      const uint32_t kc0 = kt * a.nb / a.nkt, kc1 = (kt + 1) * a.nb / a.nkt;
+      // K-tile kt: super-blocks [kc0, kc1), kq + (kt < kr) of them (the consumers' split)
+      const uint32_t kq = a.nb / a.nkt, kr = a.nb % a.nkt;
+      const uint32_t kc0 = kt * kq + min(kt, kr), kc1 = kc0 + kq + (kt < kr ? 1u : 0u);
       const uint32_t r = r0 + lane;
       uint64_t a0 = 0, a1 = 0;
       if (a.seg_bytes == 0) {
@@ -426,79 +481,141 @@ __global__ void __launch_bounds__((kMaxWarps + 1) * 32, 1) warpmma_kernel(const 
           sq += __shfl_xor_sync(0xffffffffu, sq, o);
           mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
         }
-        int e = 1;
-        if (mx > 0.f && isfinite(mx)) frexpf(mx, &e);  // mx = f * 2^e, f in [0.5, 1)
-        const int sh = (e > kTarget || e <= 0) ? max(-126, min(126, kTarget - e)) : 0;
-        const float sc = ldexpf(1.f, sh);
-        if (lane == 0) {
-          s_sq[warp][b] += sq;
-          ublk[b * a.nb + kb] = ldexpf(1.f, -sh);
-        }
-#pragma unroll
-        for (int r = 0; r < 8; ++r) v[j][r] *= sc;
-        if constexpr (QT == 4) {
-          // entry (kb, t, n, m, c), 8 bytes at ((kb NT + t) ncol + n) kNStride + 32 m + 8 c:
-          // regs (b0b1, b2b3) of thread (g = n, c) in MMA m of block kb, n-tile t. For
-          // MMA m = 2i + o, thread c holds b0b1 = x[64c + 4i + o], x[64c + 32 + 4i + o + 2] and
-          // b2b3 = x[64c + 32 + 4i + o], x[64c + 4i + o + 2]: element 64c + 32 hb + 4i + w
-          // (w = o + 2 s2) sits in reg hb ^ s2, half s2. Here element = 32 r + lane.
-          const uint32_t i = (lane >> 2) & 7, w = lane & 3;
-          const uint32_t o = w & 1, s2 = w >> 1;
-          const uint32_t m = 2 * i + o;
+        if constexpr (I8) {
+          // 24-bit fixed point for the block: the power of two that brings max |x| into
+          // [2^21, 2^22), so that x = (L2 2^16 + L1 2^8 + L0) 2^-sh with signed byte limbs
+          // |L2| <= 64, |L1|, |L0| <= 128 (an integer-valued x stays exact).
+          int e = 1;
+          if (mx > 0.f && isfinite(mx)) frexpf(mx, &e);  // mx = f * 2^e, f in [0.5, 1)
+          const int sh = mx > 0.f ? max(-126, min(126, 22 - e)) : 0;
+          const float sc = ldexpf(1.f, sh);
+          if (lane == 0) {
+            s_sq[warp][b] += sq;
+            ublk[b * a.nb + kb] = ldexpf(1.f, -sh);
+          }
+          int L[3][8];
 #pragma unroll
           for (int r = 0; r < 8; ++r) {
-            const uint32_t c_r = r >> 1, hb = r & 1;
-            const uint32_t within = 32 * m + 8 * c_r + (((hb ^ s2) << 2) | (s2 << 1));
+            const int X = __float2int_rn(v[j][r] * sc);
+            const int l0 = ((X + 128) & 255) - 128;
+            const int x1 = (X - l0) >> 8;
+            const int l1 = ((x1 + 128) & 255) - 128;
+            L[0][r] = l0;
+            L[1][r] = l1;
+            L[2][r] = (x1 - l1) >> 8;
+            // element 32 r + lane of the block: chunk 4 r + lane / 8 (24 bytes: 8 of each limb)
+            const uint32_t at = table_s + (kb * 32 + 4 * r + (lane >> 3)) * 24 + (lane & 7);
 #pragma unroll
-            for (uint32_t pp = 0; pp < (HILO ? 2u : 1u); ++pp) {
-              const uint32_t t = (HILO && NT == 2) ? pp : 0u;
-              const uint32_t n = HILO ? (NT == 1 ? 2 * b + pp : b) : b;
-              sts_u16(table_s + ((kb * NT + t) * a.ncol + n) * kNStride + within,
-                      __half_as_ushort(part(v[j][r], pp)));
-            }
+            for (int l = 0; l < 3; ++l)
+              asm volatile("st.shared.u8 [%0], %1;" ::"r"(at + 8 * l), "r"(L[l][r]) : "memory");
           }
-          // sub-block sums X_r = sum over lanes of v[r]: reduce-scatter by lane bits 4, 3, 2,
-          // then a butterfly over bits 1, 0; lane l ends with X_((l >> 2) & 7).
-          float w4[4], w2[2];
-          const bool b4 = (lane >> 4) & 1, b3 = (lane >> 3) & 1, b2 = (lane >> 2) & 1;
+          if constexpr (QT == 6) {
+            // C init of the MMAs: -32 * (sum of each limb over each 16-element sub-block), so
+            // that A = q (unsigned) gives sum (q - 32) x exactly. Element 32 r + lane is in
+            // sub-block 2r + lane/16 of the block: half r / 4, column (2r + lane/16) % 8.
 #pragma unroll
-          for (int q = 0; q < 4; ++q) {
-            const float keep = b4 ? v[j][q + 4] : v[j][q], give = b4 ? v[j][q] : v[j][q + 4];
-            w4[q] = keep + __shfl_xor_sync(0xffffffffu, give, 16);
-          }
+            for (int r = 0; r < 8; ++r)
 #pragma unroll
-          for (int q = 0; q < 2; ++q) {
-            const float keep = b3 ? w4[q + 2] : w4[q], give = b3 ? w4[q] : w4[q + 2];
-            w2[q] = keep + __shfl_xor_sync(0xffffffffu, give, 8);
-          }
-          float X = (b2 ? w2[1] : w2[0]) + __shfl_xor_sync(0xffffffffu, b2 ? w2[0] : w2[1], 4);
-          X += __shfl_xor_sync(0xffffffffu, X, 2);
-          X += __shfl_xor_sync(0xffffffffu, X, 1);
-          if ((lane & 3) == 0) {
-            // min entry (kb, t, n, c), 4 bytes at ((kb NT + t) ncol + n) 16 + 4c: b0b1 of the min
-            // MMA = (X_2c, X_2c+1) of vector b
-            const uint32_t jj = (lane >> 2) & 7;
+              for (int l = 0; l < 3; ++l) {
+                int t = L[l][r];
 #pragma unroll
-            for (uint32_t pp = 0; pp < (HILO ? 2u : 1u); ++pp) {
-              const uint32_t t = (HILO && NT == 2) ? pp : 0u;
-              const uint32_t n = HILO ? (NT == 1 ? 2 * b + pp : b) : b;
-              sts_u16(mtable_s + ((kb * NT + t) * a.ncol + n) * 16 + 4 * (jj >> 1) + 2 * (jj & 1),
-                      __half_as_ushort(part(X, pp)));
+                for (int o = 8; o; o >>= 1) t += __shfl_xor_sync(0xffffffffu, t, o);
+                if ((lane & 15) == 0) {
+                  const uint32_t hh = r >> 2, n = (2 * r + (lane >> 4)) & 7;
+                  asm volatile("st.shared.s32 [%0], %1;" ::"r"(mtable_s + (((kb * 2 + hh) * 3 + l) * 8 + n) * 4),
+                               "r"(-32 * t)
+                               : "memory");
+                }
+              }
+          } else {
+            // the sum of x (in limb units) over each 32-element sub-block r, for the min term
+#pragma unroll
+            for (int r = 0; r < 8; ++r) {
+              int t = (L[2][r] << 16) + (L[1][r] << 8) + L[0][r];
+#pragma unroll
+              for (int o = 16; o; o >>= 1) t += __shfl_xor_sync(0xffffffffu, t, o);
+              if (lane == 0)
+                asm volatile("st.shared.f32 [%0], %1;" ::"r"(mtable_s + (kb * 8 + r) * 4),
+                             "f"(static_cast<float>(t))
+                             : "memory");
             }
           }
         } else {
-          // entry (kb, h, m, c, u) = 8 bytes, read by thread (g, c) with g & 3 == c and u = g >> 2:
-          // u = 0: (pair of sub-block c, 0); u = 1: (0, pair of sub-block c + 4). Element
-          // 128h + 64u + 16c + 4i + w (w = o + 2 s2, m = 2i + o) sits in reg u, half s2, and
-          // the same half of the other reg is zero. Here element = 32 r + lane.
-          const uint32_t i = (lane >> 2) & 3, w = lane & 3, o = w & 1, s2 = w >> 1;
-#pragma unroll
-          for (int r = 0; r < 8; ++r) {
-            const uint32_t h = r >> 2, u = (r >> 1) & 1, cc = ((r & 1) << 1) | (lane >> 4);
-            const uint32_t ent = (((kb * 2 + h) * 8 + 2 * i + o) * 4 + cc) * 2 + u;
-            sts_u16(table_s + ent * 8 + u * 4 + s2 * 2, __half_as_ushort(__float2half_rn(v[j][r])));
-            sts_u16(table_s + ent * 8 + (u ^ 1) * 4 + s2 * 2, 0);
+          int e = 1;
+          if (mx > 0.f && isfinite(mx)) frexpf(mx, &e);  // mx = f * 2^e, f in [0.5, 1)
+          const int sh = (e > kTarget || e <= 0) ? max(-126, min(126, kTarget - e)) : 0;
+          const float sc = ldexpf(1.f, sh);
+          if (lane == 0) {
+            s_sq[warp][b] += sq;
+            ublk[b * a.nb + kb] = ldexpf(1.f, -sh);
           }
+  #pragma unroll
+          for (int r = 0; r < 8; ++r) v[j][r] *= sc;
+          if constexpr (QT == 4) {
+            // entry (kb, t, n, m, c), 8 bytes at ((kb NT + t) ncol + n) kNStride + 32 m + 8 c:
+            // regs (b0b1, b2b3) of thread (g = n, c) in MMA m of block kb, n-tile t. For
+            // MMA m = 2i + o, thread c holds b0b1 = x[64c + 4i + o], x[64c + 32 + 4i + o + 2] and
+            // b2b3 = x[64c + 32 + 4i + o], x[64c + 4i + o + 2]: element 64c + 32 hb + 4i + w
+            // (w = o + 2 s2) sits in reg hb ^ s2, half s2. Here element = 32 r + lane.
+            const uint32_t i = (lane >> 2) & 7, w = lane & 3;
+            const uint32_t o = w & 1, s2 = w >> 1;
+            const uint32_t m = 2 * i + o;
+  #pragma unroll
+            for (int r = 0; r < 8; ++r) {
+              const uint32_t c_r = r >> 1, hb = r & 1;
+              const uint32_t within = 32 * m + 8 * c_r + (((hb ^ s2) << 2) | (s2 << 1));
+  #pragma unroll
+              for (uint32_t pp = 0; pp < (HILO ? 2u : 1u); ++pp) {
+                const uint32_t t = (HILO && NT == 2) ? pp : 0u;
+                const uint32_t n = HILO ? (NT == 1 ? 2 * b + pp : b) : b;
+                sts_u16(table_s + ((kb * NT + t) * a.ncol + n) * kNStride + within,
+                        __half_as_ushort(part(v[j][r], pp)));
+              }
+            }
+            // sub-block sums X_r = sum over lanes of v[r]: reduce-scatter by lane bits 4, 3, 2,
+            // then a butterfly over bits 1, 0; lane l ends with X_((l >> 2) & 7).
+            float w4[4], w2[2];
+            const bool b4 = (lane >> 4) & 1, b3 = (lane >> 3) & 1, b2 = (lane >> 2) & 1;
+  #pragma unroll
+            for (int q = 0; q < 4; ++q) {
+              const float keep = b4 ? v[j][q + 4] : v[j][q], give = b4 ? v[j][q] : v[j][q + 4];
+              w4[q] = keep + __shfl_xor_sync(0xffffffffu, give, 16);
+            }
+  #pragma unroll
+            for (int q = 0; q < 2; ++q) {
+              const float keep = b3 ? w4[q + 2] : w4[q], give = b3 ? w4[q] : w4[q + 2];
+              w2[q] = keep + __shfl_xor_sync(0xffffffffu, give, 8);
+            }
+            float X = (b2 ? w2[1] : w2[0]) + __shfl_xor_sync(0xffffffffu, b2 ? w2[0] : w2[1], 4);
+            X += __shfl_xor_sync(0xffffffffu, X, 2);
+            X += __shfl_xor_sync(0xffffffffu, X, 1);
+            if ((lane & 3) == 0) {
+              // min entry (kb, t, n, c), 4 bytes at ((kb NT + t) ncol + n) 16 + 4c: b0b1 of the min
+              // MMA = (X_2c, X_2c+1) of vector b
+              const uint32_t jj = (lane >> 2) & 7;
+  #pragma unroll
+              for (uint32_t pp = 0; pp < (HILO ? 2u : 1u); ++pp) {
+                const uint32_t t = (HILO && NT == 2) ? pp : 0u;
+                const uint32_t n = HILO ? (NT == 1 ? 2 * b + pp : b) : b;
+                sts_u16(mtable_s + ((kb * NT + t) * a.ncol + n) * 16 + 4 * (jj >> 1) + 2 * (jj & 1),
+                        __half_as_ushort(part(X, pp)));
+              }
+            }
+          } else {
+            // entry (kb, h, m, c, u) = 8 bytes, read by thread (g, c) with g & 3 == c and u = g >> 2:
+            // u = 0: (pair of sub-block c, 0); u = 1: (0, pair of sub-block c + 4). Element
+            // 128h + 64u + 16c + 4i + w (w = o + 2 s2, m = 2i + o) sits in reg u, half s2, and
+            // the same half of the other reg is zero. Here element = 32 r + lane.
+            const uint32_t i = (lane >> 2) & 3, w = lane & 3, o = w & 1, s2 = w >> 1;
+  #pragma unroll
+            for (int r = 0; r < 8; ++r) {
+              const uint32_t h = r >> 2, u = (r >> 1) & 1, cc = ((r & 1) << 1) | (lane >> 4);
+              const uint32_t ent = (((kb * 2 + h) * 8 + 2 * i + o) * 4 + cc) * 2 + u;
+              sts_u16(table_s + ent * 8 + u * 4 + s2 * 2, __half_as_ushort(__float2half_rn(v[j][r])));
+              sts_u16(table_s + ent * 8 + (u ^ 1) * 4 + s2 * 2, 0);
+            }
+          }
+
         }
       }
     }
@@ -534,6 +651,11 @@ __global__ void __launch_bounds__((kMaxWarps + 1) * 32, 1) warpmma_kernel(const 
   const uint32_t tab_lane = QT == 4 ? g * kNStride + c * 8 : (c * 2 + (g >> 2)) * 8;
   const uint32_t zero_s = ring_s + a.zero_off + (QT == 4 ? c * 8 : 0);
   const uint32_t k24 = (1u << 24) << a.zero;              // >> 8
+  const uint32_t k28 = (1u << 28) << a.zero;              // >> 4
+  // I8 Q6_K: qh pairs to bits 4-5: low group by a multiply (x16 for c < 2, x4 for c >= 2), high
+  // group by a right shift (0 or 2)
+  const uint32_t kLo = (c >= 2 ? 4u : 16u) << a.zero;
+  const uint32_t sHi = c >= 2 ? 2u : 0u;
   const uint32_t kT = (1u << (QT == 6 ? (c >= 2 ? 2 : 4) : 0)) << a.zero;    // << sT
   const uint32_t kT13 = (1u << (QT == 6 ? (c >= 2 ? 26 : 28) : 0)) << a.zero;  // >> (8 - sT)
   // MMA rows g and g+8 of this thread are tile rows pg and pg+8. With whole-row tiles whose row
@@ -546,19 +668,28 @@ __global__ void __launch_bounds__((kMaxWarps + 1) * 32, 1) warpmma_kernel(const 
   const uint32_t vb0c = min(vb0, B - 1);
 
   float yacc[2][2] = {{0.f, 0.f}, {0.f, 0.f}};  // rows g, g+8 x this thread's vectors
-  uint32_t s = 0, phase = 0;
-  for (uint32_t t = 0; t < ntiles; ++t) {
+  // Tiles are walked band by band, K-tile by K-tile, with no divisions: K-tile kt has
+  // kq + (kt < kr) super-blocks (the producer splits the same way).
+  const uint32_t nkt = a.nkt, kq = a.nb / nkt, kr = a.nb % nkt;
+  const uint32_t rb32 = static_cast<uint32_t>(RB);
+  const uint32_t pg_rb = pg * rb32;
+  // When every row starts on a 16-byte boundary, a block's offset within 16 bytes is the same
+  // for all rows of a warp: (kb * block bytes) mod 16.
+  const bool rows16 = (rb32 & 15u) == 0;
+  uint32_t s = 0, phase = 0, bi = 0;
+  for (uint32_t band = 0; band < nbands; ++band) {
+  const uint32_t r0 = r_begin + band * kTileRows;
+  uint32_t kc0 = 0;
+  for (uint32_t kt = 0; kt < nkt; ++kt) {
+    const uint32_t kc1 = kc0 + kq + (kt < kr ? 1u : 0u);
     bool ok = !*reinterpret_cast<volatile int*>(&s_failed);
-    if (ok && !mbar_wait_sleep(full_bar(s), phase)) {
+    if (ok && !mbar_wait(full_bar(s), phase)) {
       ok = false;
       s_failed = 1;
       report_error(a.err, kErrWaitFull);
     }
     // warp-uniform, so that every lane takes the same path to the (.aligned) MMAs
     const bool failed = __any_sync(0xffffffffu, !ok);
-    const uint32_t band = t / a.nkt, kt = t % a.nkt;
-    const uint32_t r0 = r_begin + band * kTileRows;
-    const uint32_t kc0 = kt * a.nb / a.nkt, kc1 = (kt + 1) * a.nb / a.nkt;
     const uint32_t kb = kc0 + warp;
     const uint32_t slot = ring_s + s * a.slot_bytes;
     if (kb < kc1 && !failed) {
@@ -566,18 +697,138 @@ __global__ void __launch_bounds__((kMaxWarps + 1) * 32, 1) warpmma_kernel(const 
       uint32_t ag, ah;
       if (a.seg_bytes == 0) {
         // whole rows back to back from the tile's aligned start
-        const uint32_t delta = static_cast<uint32_t>((uint64_t(r0) * RB) & 15);
-        ag = slot + delta + static_cast<uint32_t>(pg * RB) + warp * kBlk;
-        ah = ag + static_cast<uint32_t>(8 * RB);
+        const uint32_t delta = (r0 * rb32) & 15u;
+        ag = slot + delta + pg_rb + warp * kBlk;
+        ah = ag + 8 * rb32;
       } else {
-        const uint64_t off = uint64_t(kc0) * kBlk;
-        ag = slot + pg * a.seg_bytes + static_cast<uint32_t>((uint64_t(r0 + pg) * RB + off) & 15) +
-             warp * kBlk;
-        ah = slot + (pg + 8) * a.seg_bytes +
-             static_cast<uint32_t>((uint64_t(r0 + pg + 8) * RB + off) & 15) + warp * kBlk;
+        const uint32_t off = kc0 * kBlk;
+        ag = slot + pg * a.seg_bytes + (((r0 + pg) * rb32 + off) & 15u) + warp * kBlk;
+        ah = slot + (pg + 8) * a.seg_bytes + (((r0 + pg + 8) * rb32 + off) & 15u) + warp * kBlk;
       }
+      // the offset within 16 bytes that every lane's block shares, or 16 when they differ
+      const uint32_t o16 = rows16 ? ((kb * kBlk) & 15u) : 16u;
 
-      if constexpr (QT == 4) {
+      if constexpr (I8) {
+        // Integer MMAs (batch 1). Column n of the MMA is sub-block n; the A registers of a step
+        // hold 4 + 4 quants of one sub-block (8 consecutive elements of it per thread), B the
+        // three limbs of the same 8 elements of x, read by the 4 lanes of the column's group.
+        const float u0 = ublk[kb];
+        int acc[3][4];
+        if constexpr (QT == 4) {
+          // 8 steps, step s = sub-block s = qs chunk s/2, nibble s%2; thread c: bytes 8c..8c+7
+          const uint4 hg = lds_v4(ag), hh = lds_v4(ah);
+#pragma unroll
+          for (int l = 0; l < 3; ++l) acc[l][0] = acc[l][1] = acc[l][2] = acc[l][3] = 0;
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            const uint2 wg = lds_v2(ag + 16 + 32 * q + 8 * c), wh = lds_v2(ah + 16 + 32 * q + 8 * c);
+#pragma unroll
+            for (int o = 0; o < 2; ++o) {
+              const int st = 2 * q + o;
+              const uint32_t a0 = (o ? mulhi(wg.x, k28) : wg.x) & 0x0F0F0F0Fu;
+              const uint32_t a1 = (o ? mulhi(wh.x, k28) : wh.x) & 0x0F0F0F0Fu;
+              const uint32_t a2 = (o ? mulhi(wg.y, k28) : wg.y) & 0x0F0F0F0Fu;
+              const uint32_t a3 = (o ? mulhi(wh.y, k28) : wh.y) & 0x0F0F0F0Fu;
+              const uint32_t bb = g == static_cast<uint32_t>(st) ? table_s + (kb * 32 + 4 * st + c) * 24 : zero_s;
+#pragma unroll
+              for (int l = 0; l < 3; ++l) {
+                const uint2 bf = lds_v2(bb + 8 * l);
+                imma16832(acc[l], a0, a1, a2, a3, bf.x, bf.y);
+              }
+            }
+          }
+          // scales and mins of sub-blocks 2c, 2c+1 (the thread's columns) as floats
+          auto scm = [&](const uint4& hd, float& s0, float& s1, float& m0, float& m1) {
+            const uint32_t ts = __byte_perm(hd.w, hd.y, sel_sc);
+            const uint32_t sc16 = (ts & m_lo) | ((ts >> 10) & m_hi);
+            const uint32_t tm = __byte_perm(hd.w, hd.z, sel_sc);
+            const uint32_t m16 = ((tm >> sh_m) & m_lo) | ((tm >> 10) & m_hi);
+            s0 = u16_to_f32<0>(sc16);
+            s1 = u16_to_f32<1>(sc16);
+            m0 = u16_to_f32<0>(m16);
+            m1 = u16_to_f32<1>(m16);
+          };
+          float sg0, sg1, mg0, mg1, sh0, sh1, mh0, mh1;
+          scm(hg, sg0, sg1, mg0, mg1);
+          scm(hh, sh0, sh1, mh0, mh1);
+          const float2 X = *reinterpret_cast<const float2*>(
+              reinterpret_cast<const uint8_t*>(base) + a.mtable_off + (kb * 8 + 2 * c) * 4);
+          const float dg = u0 * h2f(hg.x & 0xffffu), dmg = u0 * h2f(hg.x >> 16);
+          const float dh = u0 * h2f(hh.x & 0xffffu), dmh = u0 * h2f(hh.x >> 16);
+          const float v0 = limbs_to_f32(acc[2][0], acc[1][0], acc[0][0]);
+          const float v1 = limbs_to_f32(acc[2][1], acc[1][1], acc[0][1]);
+          const float v2 = limbs_to_f32(acc[2][2], acc[1][2], acc[0][2]);
+          const float v3 = limbs_to_f32(acc[2][3], acc[1][3], acc[0][3]);
+          yacc[0][0] += dg * fmaf(sg0, v0, sg1 * v1) - dmg * fmaf(mg0, X.x, mg1 * X.y);
+          yacc[1][0] += dh * fmaf(sh0, v2, sh1 * v3) - dmh * fmaf(mh0, X.x, mh1 * X.y);
+        } else {
+          // Q6_K: per half, 4 steps: s < 2 the low-nibble group (sub-block c, words 2(s&1),
+          // 2(s&1)+1 of the thread's 16 ql bytes), s >= 2 the high-nibble group (sub-block c+4)
+          const float dg = u0 * h2f(lds_u16(ag + 208)), dh = u0 * h2f(lds_u16(ah + 208));
+          const uint32_t o0 = o16 & 15u;
+          const bool same = o16 < 16u;
+          const uint32_t fs = 8 * (o0 & 3);
+#pragma unroll 1
+          for (uint32_t hf = 0; hf < 2; ++hf) {
+            uint32_t L[2][4], Q[2][4];
+            if (!same)
+              q6_load_half<-2>(ag, ah, c, hf, 0, L, Q);
+            else if (o0 == 0)
+              q6_load_half<-1>(ag, ah, c, hf, fs, L, Q);
+            else if (o0 < 4)
+              q6_load_half<0>(ag, ah, c, hf, fs, L, Q);
+            else if (o0 < 8)
+              q6_load_half<1>(ag, ah, c, hf, fs, L, Q);
+            else if (o0 < 12)
+              q6_load_half<2>(ag, ah, c, hf, fs, L, Q);
+            else
+              q6_load_half<3>(ag, ah, c, hf, fs, L, Q);
+#pragma unroll
+            for (int l = 0; l < 3; ++l) {
+              const uint2 ci = lds_v2(mtable_s + (((kb * 2 + hf) * 3 + l) * 8 + 2 * c) * 4);
+              acc[l][0] = acc[l][2] = static_cast<int>(ci.x);
+              acc[l][1] = acc[l][3] = static_cast<int>(ci.y);
+            }
+#pragma unroll
+            for (int st = 0; st < 4; ++st) {
+              const int w0 = 2 * (st & 1), w1 = w0 + 1;
+              uint32_t a0, a1, a2, a3;
+              if (st < 2) {
+                // low nibble | qh pair (bits 0-1 for c < 2, 2-3 for c >= 2) moved to bits 4-5
+                a0 = lop_and_or(L[0][w0], 0x0F0F0F0Fu, mullo(Q[0][w0], kLo) & 0x30303030u);
+                a1 = lop_and_or(L[1][w0], 0x0F0F0F0Fu, mullo(Q[1][w0], kLo) & 0x30303030u);
+                a2 = lop_and_or(L[0][w1], 0x0F0F0F0Fu, mullo(Q[0][w1], kLo) & 0x30303030u);
+                a3 = lop_and_or(L[1][w1], 0x0F0F0F0Fu, mullo(Q[1][w1], kLo) & 0x30303030u);
+              } else {
+                // high nibble | qh pair (bits 4-5 for c < 2, 6-7 for c >= 2) at bits 4-5
+                a0 = lop_and_or(mulhi(L[0][w0], k28), 0x0F0F0F0Fu, (Q[0][w0] >> sHi) & 0x30303030u);
+                a1 = lop_and_or(mulhi(L[1][w0], k28), 0x0F0F0F0Fu, (Q[1][w0] >> sHi) & 0x30303030u);
+                a2 = lop_and_or(mulhi(L[0][w1], k28), 0x0F0F0F0Fu, (Q[0][w1] >> sHi) & 0x30303030u);
+                a3 = lop_and_or(mulhi(L[1][w1], k28), 0x0F0F0F0Fu, (Q[1][w1] >> sHi) & 0x30303030u);
+              }
+              const bool on = g == (st < 2 ? c : c + 4);
+              const uint32_t bb =
+                  on ? table_s + (kb * 32 + 16 * hf + 8 * (st >> 1) + 2 * c + (st & 1)) * 24 : zero_s;
+#pragma unroll
+              for (int l = 0; l < 3; ++l) {
+                const uint2 bf = lds_v2(bb + 8 * l);
+                imma16832(acc[l], a0, a1, a2, a3, bf.x, bf.y);
+              }
+            }
+            // columns 2c, 2c+1 = sub-blocks 2c, 2c+1 of this half: scales 8 hf + 2c, +1
+            const uint32_t sg = lds_u16(ag + 192 + 8 * hf + 2 * c);
+            const uint32_t sh = lds_u16(ah + 192 + 8 * hf + 2 * c);
+            const float v0 = limbs_to_f32(acc[2][0], acc[1][0], acc[0][0]);
+            const float v1 = limbs_to_f32(acc[2][1], acc[1][1], acc[0][1]);
+            const float v2 = limbs_to_f32(acc[2][2], acc[1][2], acc[0][2]);
+            const float v3 = limbs_to_f32(acc[2][3], acc[1][3], acc[0][3]);
+            yacc[0][0] += dg * fmaf(static_cast<float>(static_cast<int8_t>(sg & 0xffu)), v0,
+                                    static_cast<float>(static_cast<int8_t>(sg >> 8)) * v1);
+            yacc[1][0] += dh * fmaf(static_cast<float>(static_cast<int8_t>(sh & 0xffu)), v2,
+                                    static_cast<float>(static_cast<int8_t>(sh >> 8)) * v3);
+          }
+        }
+      } else if constexpr (QT == 4) {
         const uint4 hg = lds_v4(ag), hh = lds_v4(ah);
         const uint4 qg0 = lds_v4(ag + 16 + 32 * c), qg1 = lds_v4(ag + 32 + 32 * c);
         const uint4 qh0 = lds_v4(ah + 16 + 32 * c), qh1 = lds_v4(ah + 32 + 32 * c);
@@ -670,8 +921,8 @@ __global__ void __launch_bounds__((kMaxWarps + 1) * 32, 1) warpmma_kernel(const 
         const uint32_t tab_kb = tab_on ? table_s + kb * 1024 + tab_lane : zero_s;
         // the block's quants, loaded in the form the rows' common alignment allows
         uint32_t L[2][2][4], Q[2][2][4];
-        const uint32_t o0 = __shfl_sync(0xffffffffu, ag & 15u, 0);
-        if (__all_sync(0xffffffffu, (ag & 15u) == o0 && (ah & 15u) == o0)) {
+        const uint32_t o0 = o16 & 15u;
+        if (o16 < 16u) {
           const uint32_t fs = 8 * (o0 & 3);
           switch (o0 >> 2) {
             case 0:
@@ -694,64 +945,66 @@ __global__ void __launch_bounds__((kMaxWarps + 1) * 32, 1) warpmma_kernel(const 
       s = 0;
       phase ^= 1;
     }
+    kc0 = kc1;
+  }  // K-tiles of the band
 
-    if (kt + 1 == a.nkt) {
-      // The band is done: this warp's partial rows go to the reduction buffer.
-      const uint32_t bi = band % a.fb;
-      if constexpr (QT == 6) {
-        // the four threads of a row hold different sub-blocks of vector 0
+  // The band is done: this warp's partial rows go to the reduction buffer.
+  if constexpr (QT == 6 || I8) {
+    // the four threads of a row hold different sub-blocks of vector 0
 #pragma unroll
-        for (int r = 0; r < 2; ++r) {
-          yacc[r][0] += __shfl_xor_sync(0xffffffffu, yacc[r][0], 1);
-          yacc[r][0] += __shfl_xor_sync(0xffffffffu, yacc[r][0], 2);
-        }
-        if (c == 0) {
-          red[((bi * kTileRows + pg) * nwc + warp) * B] = yacc[0][0];
-          red[((bi * kTileRows + pg + 8) * nwc + warp) * B] = yacc[1][0];
-        }
-      } else {
+    for (int r = 0; r < 2; ++r) {
+      yacc[r][0] += __shfl_xor_sync(0xffffffffu, yacc[r][0], 1);
+      yacc[r][0] += __shfl_xor_sync(0xffffffffu, yacc[r][0], 2);
+    }
+    if (c == 0) {
+      red[((bi * kTileRows + pg) * nwc + warp) * B] = yacc[0][0];
+      red[((bi * kTileRows + pg + 8) * nwc + warp) * B] = yacc[1][0];
+    }
+  } else {
 #pragma unroll
-        for (int j = 0; j < 2; ++j) {
-          const uint32_t b = (HILO && NT == 1) ? (j == 0 ? c : 8u) : 2 * c + j;
-          if (b < B) {
-            red[((bi * kTileRows + pg) * nwc + warp) * B + b] = yacc[0][j];
-            red[((bi * kTileRows + pg + 8) * nwc + warp) * B + b] = yacc[1][j];
-          }
-        }
-      }
-      yacc[0][0] = yacc[0][1] = yacc[1][0] = yacc[1][1] = 0.f;
-
-      if (bi + 1 == a.fb || band + 1 == nbands) {
-        // Flush: sum every warp's partial of each row in a fixed order and write y.
-        named_barrier(1, nthr);
-        const uint32_t band0 = band - bi;
-        const uint32_t R = a.row_unit;
-        const uint32_t nout = (bi + 1) * (kTileRows / R) * B;
-        for (uint32_t o = tid; o < nout; o += nthr) {
-          const uint32_t b = o % B;
-          const uint32_t q = o / B;  // output index within the flushed bands
-          const uint32_t row16 = (q % (kTileRows / R)) * R;
-          const uint32_t bj = q / (kTileRows / R);
-          const uint32_t row = r_begin + (band0 + bj) * kTileRows + row16;
-          if (row >= r_end) continue;
-          float v0 = 0.f;
-          const float* rp = red + ((bj * kTileRows + row16) * nwc) * B + b;
-          for (uint32_t w = 0; w < nwc; ++w) v0 += rp[w * B];
-          v0 *= s_ns[b];
-          if (R == 1) {
-            a.y[b * a.ldy + row] = v0;
-          } else {
-            float v1 = 0.f;
-            const float* rq = rp + nwc * B;
-            for (uint32_t w = 0; w < nwc; ++w) v1 += rq[w * B];
-            v1 *= s_ns[b];
-            a.y[b * a.ldy + row / 2] = v0 * v1 * a.pair_scale;
-          }
-        }
-        named_barrier(1, nthr);
+    for (int j = 0; j < 2; ++j) {
+      const uint32_t b = (HILO && NT == 1) ? (j == 0 ? c : 8u) : 2 * c + j;
+      if (b < B) {
+        red[((bi * kTileRows + pg) * nwc + warp) * B + b] = yacc[0][j];
+        red[((bi * kTileRows + pg + 8) * nwc + warp) * B + b] = yacc[1][j];
       }
     }
   }
+  yacc[0][0] = yacc[0][1] = yacc[1][0] = yacc[1][1] = 0.f;
+
+  if (bi + 1 == a.fb || band + 1 == nbands) {
+    // Flush: sum every warp's partial of each row in a fixed order and write y.
+    named_barrier(1, nthr);
+    const uint32_t band0 = band - bi;
+    const uint32_t R = a.row_unit;
+    const uint32_t nout = (bi + 1) * (kTileRows / R) * B;
+    for (uint32_t o = tid; o < nout; o += nthr) {
+      const uint32_t b = o % B;
+      const uint32_t q = o / B;  // output index within the flushed bands
+      const uint32_t row16 = (q % (kTileRows / R)) * R;
+      const uint32_t bj = q / (kTileRows / R);
+      const uint32_t row = r_begin + (band0 + bj) * kTileRows + row16;
+      if (row >= r_end) continue;
+      float v0 = 0.f;
+      const float* rp = red + ((bj * kTileRows + row16) * nwc) * B + b;
+      for (uint32_t w = 0; w < nwc; ++w) v0 += rp[w * B];
+      v0 *= s_ns[b];
+      if (R == 1) {
+        a.y[b * a.ldy + row] = v0;
+      } else {
+        float v1 = 0.f;
+        const float* rq = rp + nwc * B;
+        for (uint32_t w = 0; w < nwc; ++w) v1 += rq[w * B];
+        v1 *= s_ns[b];
+        a.y[b * a.ldy + row / 2] = v0 * v1 * a.pair_scale;
+      }
+    }
+    named_barrier(1, nthr);
+    bi = 0;
+  } else {
+    ++bi;
+  }
+  }  // bands
 }
 
 struct Variant {
@@ -760,13 +1013,14 @@ struct Variant {
   bool hilo;
 };
 
-template <int QT, int NT, bool HILO>
+template <int QT, int NT, bool HILO, bool I8 = false>
 Variant variant() {
-  return Variant{reinterpret_cast<const void*>(&warpmma_kernel<QT, NT, HILO>), QT, NT, HILO};
+  return Variant{reinterpret_cast<const void*>(&warpmma_kernel<QT, NT, HILO, I8>), QT, NT, HILO};
 }
 
 const Variant kVariants[] = {variant<4, 1, true>(), variant<4, 2, true>(), variant<4, 1, false>(),
-                             variant<6, 1, false>()};
+                             variant<6, 1, false>(), variant<4, 1, false, true>(),
+                             variant<6, 1, false, true>()};
 
 }  // namespace
 
@@ -824,7 +1078,17 @@ int warpmma_matvec(kq_ctx* ctx, const kq_matvec_desc& d, uint64_t ldx, uint64_t 
   const uint32_t ublk_bytes = ((nb * d.batch * 4 + 15) / 16) * 16;
   const uint64_t fixed_min =
       2 * uint64_t(slot) + kTileRows * nwc * d.batch * 4 + ublk_bytes + kZeroBytes + 256 + 128;
-  if (q4) {
+  // batch 1: the integer kernel, whose table is x's three byte limbs (3 bytes per element) plus
+  // per-sub-block sums (Q6_K: the MMAs' C init, Q4_K: the min term's sums of x)
+  const uint64_t i8_table = uint64_t(nb) * kQK * 3;
+  const uint64_t i8_mtable = q4 ? uint64_t(nb) * 8 * 4 : uint64_t(nb) * 2 * 3 * 8 * 4;
+  const bool want_i8 = (q4 != 0) == ((d.flags & kFlagAltBatch1) != 0);
+  if (d.batch == 1 && want_i8 &&
+      i8_table + i8_mtable + fixed_min <= uint64_t(ctx->max_smem)) {
+    mode = q4 ? 4 : 5, ncol = 8;
+    table_bytes = i8_table;
+    mtable_bytes = i8_mtable;
+  } else if (q4) {
     auto sizes = [&](uint32_t nt_, uint32_t ncol_) {
       table_bytes = uint64_t(nb) * nt_ * ncol_ * kNStride;
       mtable_bytes = uint64_t(nb) * nt_ * ncol_ * 16;

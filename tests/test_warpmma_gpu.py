@@ -200,3 +200,55 @@ def test_warpmma_rejects_what_it_does_not_serve(kernels):
         kernels.matvec(4, y, W, x, 1, 256, 1, flags=WM | kb.FLAG_CUDA_CORES)
     assert e.value.code == kb.KQ_E_INVALID
     kernels.device_error()
+
+
+# A descriptor flag bit the library keeps for itself (not part of include/kq.h): batch 1 on the
+# other warp-MMA variant (Q4_K: integer operands instead of f16; Q6_K: f16 instead of integer),
+# so both stay covered.
+ALT_BATCH1 = 1 << 30
+
+
+@pytest.mark.parametrize("qtype,rows,K", [(4, 300, 4096), (6, 333, 4096), (6, 77, 11008),
+                                          (4, 64, 28672), (6, 40, 28672)])
+def test_warpmma_other_batch1_variant_matches_oracle(kernels, qtype, rows, K):
+    W = dev_weights(kernels, qtype, rows, K, kb.stream_key(86, qtype))
+    x = np.random.default_rng(86).standard_normal((1, K), dtype=np.float32)
+    y = run(kernels, qtype, W, x, rows, K, flags=WM | ALT_BATCH1)
+    y_ref, bound = oracle.matvec_ref(qtype, W.cpu().numpy(), x, K, 0, rows)
+    check(y, y_ref, bound, f"other batch-1 variant q{qtype} {rows}x{K}")
+
+
+@pytest.mark.parametrize("qtype", [4, 6])
+@pytest.mark.parametrize("variant", [0, ALT_BATCH1])
+def test_warpmma_zero_weights_give_exact_zero(kernels, qtype, variant):
+    # every weight zero with nonzero scales around it: Q4_K sc = m = 0; Q6_K q = 32 (ql 0,
+    # qh bits 2 in every group) -- the sum must be exactly 0, as the reference's dot product is
+    rows, K = 100, 2048
+    Wn = oracle.fill(qtype, oracle.stream_key(87, qtype), 0, rows * K // 256)
+    blocks = Wn.reshape(-1, kb.block_bytes(qtype))
+    if qtype == 4:
+        blocks[:, 4:16] = 0
+    else:
+        blocks[:, 0:128] = 0
+        blocks[:, 128:192] = 0xAA
+    W = torch.from_numpy(blocks.reshape(-1).copy()).cuda()
+    x = np.random.default_rng(87).standard_normal((1, K), dtype=np.float32)
+    y = run(kernels, qtype, W, x, rows, K, flags=WM | variant)
+    assert np.array_equal(y, np.zeros_like(y))
+
+
+@pytest.mark.parametrize("qtype", [4, 6])
+def test_warpmma_other_batch1_variant_integer_inputs_are_exact(kernels, qtype):
+    rows, K = 300, 1024
+    Wn = oracle.fill(qtype, oracle.stream_key(88, qtype), 0, rows * K // 256)
+    blocks = Wn.reshape(-1, kb.block_bytes(qtype))
+    if qtype == 4:
+        blocks[:, 0:2] = np.array([0x2400], dtype=np.uint16).view(np.uint8)  # d = 2^-6
+        blocks[:, 2:4] = np.array([0x2800], dtype=np.uint16).view(np.uint8)  # dmin = 2^-5
+    else:
+        blocks[:, 208:210] = np.array([0x1C00], dtype=np.uint16).view(np.uint8)  # d = 2^-8
+    W = torch.from_numpy(blocks.reshape(-1).copy()).cuda()
+    x = np.random.default_rng(6).integers(-2, 3, size=(1, K)).astype(np.float32)
+    y = run(kernels, qtype, W, x, rows, K, flags=WM | ALT_BATCH1)
+    y_ref, _ = oracle.matvec_ref(qtype, blocks.reshape(-1), x, K, 0, rows)
+    assert np.array_equal(y, y_ref.astype(np.float32))
