@@ -15,8 +15,9 @@
 //    memory slots with cp.async.bulk (TMA, 1-D): one copy for a tile of whole rows, else one per
 //    row segment. An mbarrier per slot counts the bytes in; Q6_K blocks at any even offset need
 //    nothing special (readers use the byte offset from the aligned copy).
-//  * Consumer warp w takes super-block w of every tile: 16 MMAs (K = 16 each) over the tile's
-//    16 rows. The 16 rows are the MMA's M, x (with the batch) is its N. Thread (g, c) of the
+//  * A consumer warp takes one super-block of a tile: 16 MMAs (K = 16 each) over the tile's
+//    16 rows (warp w takes block w, or, with more warps than blocks, the warps take turns).
+//    The 16 rows are the MMA's M, x (with the batch) is its N. Thread (g, c) of the
 //    warp builds the A registers of rows g and g+8 from the bytes of its quarter of the block
 //    (Q4_K: qs chunk c = sub-blocks 2c, 2c+1; Q6_K: sub-blocks c and c+4 of each half).
 //  * The order of K inside an MMA is free as long as A and B agree, so each thread pairs the
@@ -54,12 +55,17 @@
 namespace kq {
 namespace {
 
-constexpr uint32_t kMaxWarps = 16;    // consumer warps (one per super-block of a tile)
+// Consumer warps: 19 + the producer = 5 warps per scheduler, which leaves 96 registers a thread
+// (each scheduler's register file holds 16K: 5 x 32 x 96 <= 16384; 6 warps would leave 80).
+constexpr uint32_t kMaxWarps = 19;
+constexpr uint32_t kTileBlocks = 16;  // super-blocks of a K-tile, at most
 constexpr uint32_t kTileRows = 16;    // rows of a tile = the MMA's M
 constexpr uint32_t kRedBudget = 16384;  // bytes of shared memory for partial rows
 // Q4_K table: bytes per (block, n-tile, column): 16 MMAs x 4 threads x 8 bytes, plus 32 bytes
 // of padding so that the columns' rows start on different banks.
 constexpr uint32_t kNStride = 16 * 32 + 32;
+// Q6_K integer path: load a whole super-block's quants before the MMAs (else half by half).
+constexpr bool kQ6WholeBlock = false;
 constexpr uint32_t kZeroBytes = 1024 + 64;  // covers every MMA offset of one block's fragments
 
 // A descriptor flag bit outside the public KQ_FLAG_* set: batch 1 on the other of the two
@@ -68,6 +74,9 @@ constexpr uint32_t kZeroBytes = 1024 + 64;  // covers every MMA offset of one bl
 // (measured on B200: equal speed for Q6_K, where the integer variant's 24-bit x is the more
 // accurate; f16 7% faster for Q4_K).
 constexpr uint32_t kFlagAltBatch1 = 1u << 30;
+// Another such bit: the other choice of consumer warps (one per super-block of the widest K-tile,
+// or kMaxWarps taking turns) for A/B timing.
+constexpr uint32_t kFlagWarpPerBlock = 1u << 29;
 
 constexpr uint32_t kMagic = 0x64006400u;  // f16x2 (1024, 1024): OR a 10-bit field in = 1024 + v
 
@@ -80,7 +89,7 @@ struct WarpMmaArgs {
   uint64_t total_bytes, row_bytes;
   uint32_t rows, nb, batch;
   uint32_t nkt;          // K-tiles per band (super-blocks split as evenly as possible)
-  uint32_t nwc;          // consumer warps = super-blocks in the widest K-tile
+  uint32_t nw;           // consumer warps (at least the super-blocks of the widest K-tile)
   uint32_t ring, slot_bytes, seg_bytes;  // seg_bytes: shared-memory pitch of a tile's rows
   uint32_t table_off, mtable_off, ublk_off, zero_off, red_off, bars_off;  // shared-memory layout
   uint32_t zero;         // 0: multipliers built from it are opaque to the compiler
@@ -179,6 +188,16 @@ __device__ __forceinline__ void imma16832(int (&d)[4], uint32_t a0, uint32_t a1,
       : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
 
+// D = A * B + C for one m16n8k32 integer tile, C given apart from D (the first step of a sum).
+__device__ __forceinline__ void imma16832_c(int (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2,
+                                            uint32_t a3, uint32_t b0, uint32_t b1, uint32_t c0,
+                                            uint32_t c1, uint32_t c2, uint32_t c3) {
+  asm("mma.sync.aligned.m16n8k32.row.col.s32.u8.s8.s32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, "
+      "{%8, %9}, {%10, %11, %12, %13};"
+      : "=r"(d[0]), "=r"(d[1]), "=r"(d[2]), "=r"(d[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "r"(c0), "r"(c1), "r"(c2), "r"(c3));
+}
+
 // x as three signed byte limbs: v = L2 * 2^16 + L1 * 2^8 + L0 for an integer |v| <= 2^22.
 __device__ __forceinline__ float limbs_to_f32(int l2, int l1, int l0) {
   return fmaf(static_cast<float>(l2), 65536.f, static_cast<float>(l1 * 256 + l0));
@@ -211,35 +230,11 @@ __device__ __forceinline__ void lds16_window(uint32_t base, uint32_t fs, uint32_
   for (int k = 0; k < 4; ++k) out[k] = __funnelshift_r(w[W + k], w[W + k + 1], fs);
 }
 
-// The quants of one Q6_K super-block for thread (g, c): L[hf][row][i] = ql words (16 bytes at
-// 64 hf + 16c), Q[hf][row][i] = qh words (16 bytes at 128 + 32 hf + 16 (c & 1)), rows g and g+8.
-// MODE -1: every address 16-byte aligned; 0..3: all lanes share the offset 4 MODE + fs/8 within
-// 16 bytes (two 16-byte loads and a funnel shift); -2: anything (4-byte loads and funnel shifts).
-template <int MODE>
-__device__ __forceinline__ void q6_load(uint32_t ag, uint32_t ah, uint32_t c, uint32_t fs,
-                                        uint32_t (&L)[2][2][4], uint32_t (&Q)[2][2][4]) {
-#pragma unroll
-  for (int hf = 0; hf < 2; ++hf)
-#pragma unroll
-    for (int r = 0; r < 2; ++r) {
-      const uint32_t base = r ? ah : ag;
-      const uint32_t al = base + 64 * hf + 16 * c, aq = base + 128 + 32 * hf + 16 * (c & 1);
-      if constexpr (MODE == -1) {
-        lds16<16>(al, L[hf][r]);
-        lds16<16>(aq, Q[hf][r]);
-      } else if constexpr (MODE >= 0) {
-        lds16_window<MODE>(al & ~15u, fs, L[hf][r]);
-        lds16_window<MODE>(aq & ~15u, fs, Q[hf][r]);
-      } else {
-        lds16<2>(al, L[hf][r]);
-        lds16<2>(aq, Q[hf][r]);
-      }
-    }
-}
-
 // The quants of half hf of one Q6_K super-block for thread (g, c), rows g and g+8: L[row] = the
-// 16 ql bytes at 64 hf + 16c, Q[row] = the 16 qh bytes at 128 + 32 hf + 16 (c & 1). MODE as
-// for q6_load.
+// 16 ql bytes at 64 hf + 16c, Q[row] = the 16 qh bytes at 128 + 32 hf + 16 (c & 1).
+// MODE -1: every address 16-byte aligned; 4 or 8: aligned to that many bytes (direct loads);
+// 0..3: all lanes share the offset 4 MODE + fs/8 within 16 bytes (two 16-byte loads and a funnel
+// shift); -2: anything (4-byte loads and funnel shifts).
 template <int MODE>
 __device__ __forceinline__ void q6_load_half(uint32_t ag, uint32_t ah, uint32_t c, uint32_t hf,
                                              uint32_t fs, uint32_t (&L)[2][4], uint32_t (&Q)[2][4]) {
@@ -250,6 +245,9 @@ __device__ __forceinline__ void q6_load_half(uint32_t ag, uint32_t ah, uint32_t 
     if constexpr (MODE == -1) {
       lds16<16>(al, L[r]);
       lds16<16>(aq, Q[r]);
+    } else if constexpr (MODE == 4 || MODE == 8) {
+      lds16<MODE>(al, L[r]);
+      lds16<MODE>(aq, Q[r]);
     } else if constexpr (MODE >= 0) {
       lds16_window<MODE>(al & ~15u, fs, L[r]);
       lds16_window<MODE>(aq & ~15u, fs, Q[r]);
@@ -258,6 +256,13 @@ __device__ __forceinline__ void q6_load_half(uint32_t ag, uint32_t ah, uint32_t 
       lds16<2>(aq, Q[r]);
     }
   }
+}
+
+template <int MODE>
+__device__ __forceinline__ void q6_load(uint32_t ag, uint32_t ah, uint32_t c, uint32_t fs,
+                                        uint32_t (&L)[2][2][4], uint32_t (&Q)[2][2][4]) {
+  q6_load_half<MODE>(ag, ah, c, 0, fs, L[0], Q[0]);
+  q6_load_half<MODE>(ag, ah, c, 1, fs, L[1], Q[1]);
 }
 
 // One Q6_K super-block of rows g (at shared address ag) and g+8 (ah) for thread (g, c) of a warp,
@@ -333,8 +338,8 @@ __global__ void __launch_bounds__((kMaxWarps + 1) * 32, 1) warpmma_kernel(const 
   auto full_bar = [&](uint32_t s) { return smem_u32(&bars[s]); };
   auto empty_bar = [&](uint32_t s) { return smem_u32(&bars[a.ring + s]); };
 
-  const uint32_t nwc = a.nwc;
-  const uint32_t nthr = nwc * 32;
+  const uint32_t nw = a.nw;
+  const uint32_t nthr = nw * 32;
   const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const uint64_t RB = a.row_bytes;
 
@@ -348,7 +353,7 @@ __global__ void __launch_bounds__((kMaxWarps + 1) * 32, 1) warpmma_kernel(const 
     s_failed = 0;
     for (uint32_t s = 0; s < a.ring; ++s) {
       mbar_init(full_bar(s), 1);
-      mbar_init(empty_bar(s), nwc);
+      mbar_init(empty_bar(s), nw);
     }
     fence_mbar_init();
   }
@@ -358,7 +363,7 @@ __global__ void __launch_bounds__((kMaxWarps + 1) * 32, 1) warpmma_kernel(const 
   // ------------------------------------------------------------------ producer warp
   // Lane r of the producer warp copies row r of each tile (16 rows, one bulk copy each, at the
   // padded pitch); lane 0 posts the tile's byte count on its slot's mbarrier.
-  if (warp == nwc) {
+  if (warp == nw) {
     if (!(a.flags & KQ_FLAG_WEIGHTS_STATIC)) pdl_wait();
     const uint64_t pol = policy_evict_first();
     const uint64_t end_floor = a.total_bytes & ~uint64_t(15);
@@ -452,11 +457,11 @@ __global__ void __launch_bounds__((kMaxWarps + 1) * 32, 1) warpmma_kernel(const 
     if (lane == 0)
       for (int b = 0; b < 8; ++b) s_sq[warp][b] = 0.0;
     const uint32_t nxb = a.nb * B;
-    for (uint32_t xb0 = warp; xb0 < nxb; xb0 += 4 * nwc) {
+    for (uint32_t xb0 = warp; xb0 < nxb; xb0 += 4 * nw) {
       float v[4][8];
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
-        const uint32_t xb = xb0 + j * nwc;
+        const uint32_t xb = xb0 + j * nw;
         if (xb < nxb) {
           const uint32_t b = xb / a.nb, kb = xb - b * a.nb;
           const float* src = a.x + b * a.ldx + kb * kQK + lane;
@@ -466,7 +471,7 @@ __global__ void __launch_bounds__((kMaxWarps + 1) * 32, 1) warpmma_kernel(const 
       }
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
-        const uint32_t xb = xb0 + j * nwc;
+        const uint32_t xb = xb0 + j * nw;
         if (xb >= nxb) break;
         const uint32_t b = xb / a.nb, kb = xb - b * a.nb;
         double sq = 0.0;
@@ -627,7 +632,7 @@ __global__ void __launch_bounds__((kMaxWarps + 1) * 32, 1) warpmma_kernel(const 
       float ns = 1.f;
       if (a.prologue == KQ_PROLOGUE_RMSNORM) {
         double t = 0.0;
-        for (uint32_t w = 0; w < nwc; ++w) t += s_sq[w][tid];
+        for (uint32_t w = 0; w < nw; ++w) t += s_sq[w][tid];
         ns = static_cast<float>(
             1.0 / sqrt(t / (static_cast<double>(a.nb) * kQK) + static_cast<double>(a.eps)));
       }
@@ -676,7 +681,9 @@ __global__ void __launch_bounds__((kMaxWarps + 1) * 32, 1) warpmma_kernel(const 
   // When every row starts on a 16-byte boundary, a block's offset within 16 bytes is the same
   // for all rows of a warp: (kb * block bytes) mod 16.
   const bool rows16 = (rb32 & 15u) == 0;
-  uint32_t s = 0, phase = 0, bi = 0;
+  // Unit j (super-block kc0 + j) of a tile goes to warp (rot + j) mod nw, rot advancing by the
+  // tile's super-block count, so the warps take turns when there are more warps than blocks.
+  uint32_t s = 0, phase = 0, bi = 0, rot = 0;
   for (uint32_t band = 0; band < nbands; ++band) {
   const uint32_t r0 = r_begin + band * kTileRows;
   uint32_t kc0 = 0;
@@ -690,7 +697,8 @@ __global__ void __launch_bounds__((kMaxWarps + 1) * 32, 1) warpmma_kernel(const 
     }
     // warp-uniform, so that every lane takes the same path to the (.aligned) MMAs
     const bool failed = __any_sync(0xffffffffu, !ok);
-    const uint32_t kb = kc0 + warp;
+    const uint32_t j = warp >= rot ? warp - rot : warp + nw - rot;
+    const uint32_t kb = kc0 + j;
     const uint32_t slot = ring_s + s * a.slot_bytes;
     if (kb < kc1 && !failed) {
       // shared-memory addresses of this block in rows g and g+8 of the tile
@@ -698,12 +706,12 @@ __global__ void __launch_bounds__((kMaxWarps + 1) * 32, 1) warpmma_kernel(const 
       if (a.seg_bytes == 0) {
         // whole rows back to back from the tile's aligned start
         const uint32_t delta = (r0 * rb32) & 15u;
-        ag = slot + delta + pg_rb + warp * kBlk;
+        ag = slot + delta + pg_rb + j * kBlk;
         ah = ag + 8 * rb32;
       } else {
         const uint32_t off = kc0 * kBlk;
-        ag = slot + pg * a.seg_bytes + (((r0 + pg) * rb32 + off) & 15u) + warp * kBlk;
-        ah = slot + (pg + 8) * a.seg_bytes + (((r0 + pg + 8) * rb32 + off) & 15u) + warp * kBlk;
+        ag = slot + pg * a.seg_bytes + (((r0 + pg) * rb32 + off) & 15u) + j * kBlk;
+        ah = slot + (pg + 8) * a.seg_bytes + (((r0 + pg + 8) * rb32 + off) & 15u) + j * kBlk;
       }
       // the offset within 16 bytes that every lane's block shares, or 16 when they differ
       const uint32_t o16 = rows16 ? ((kb * kBlk) & 15u) : 16u;
@@ -713,9 +721,9 @@ __global__ void __launch_bounds__((kMaxWarps + 1) * 32, 1) warpmma_kernel(const 
         // hold 4 + 4 quants of one sub-block (8 consecutive elements of it per thread), B the
         // three limbs of the same 8 elements of x, read by the 4 lanes of the column's group.
         const float u0 = ublk[kb];
-        int acc[3][4];
         if constexpr (QT == 4) {
           // 8 steps, step s = sub-block s = qs chunk s/2, nibble s%2; thread c: bytes 8c..8c+7
+          int acc[3][4];
           const uint4 hg = lds_v4(ag), hh = lds_v4(ah);
 #pragma unroll
           for (int l = 0; l < 3; ++l) acc[l][0] = acc[l][1] = acc[l][2] = acc[l][3] = 0;
@@ -768,27 +776,21 @@ __global__ void __launch_bounds__((kMaxWarps + 1) * 32, 1) warpmma_kernel(const 
           const uint32_t o0 = o16 & 15u;
           const bool same = o16 < 16u;
           const uint32_t fs = 8 * (o0 & 3);
-#pragma unroll 1
-          for (uint32_t hf = 0; hf < 2; ++hf) {
-            uint32_t L[2][4], Q[2][4];
-            if (!same)
-              q6_load_half<-2>(ag, ah, c, hf, 0, L, Q);
-            else if (o0 == 0)
-              q6_load_half<-1>(ag, ah, c, hf, fs, L, Q);
-            else if (o0 < 4)
-              q6_load_half<0>(ag, ah, c, hf, fs, L, Q);
-            else if (o0 < 8)
-              q6_load_half<1>(ag, ah, c, hf, fs, L, Q);
-            else if (o0 < 12)
-              q6_load_half<2>(ag, ah, c, hf, fs, L, Q);
-            else
-              q6_load_half<3>(ag, ah, c, hf, fs, L, Q);
+          // B fragments: thread (g, c) reads the table in steps 0-1 when g == c and in steps 2-3
+          // when g == c + 4 (entries kb*32 + 16 hf + 8 (st >> 1) + 2c + (st & 1), 24 bytes each),
+          // else the zero region; every step's address is one of two bases plus a constant.
+          const uint32_t tkb = table_s + (kb * 32 + 2 * c) * 24;
+          const uint32_t bA = g == c ? tkb : zero_s;
+          const uint32_t bB = g == c + 4 ? tkb + 8 * 24 : zero_s;
+          // accumulator start values: entries ((kb * 2 + hf) * 3 + l) * 8 + 2c, 4 bytes each
+          const uint32_t mkb = mtable_s + (kb * 48 + 2 * c) * 4;
+          // one half: 4 steps x 3 limbs, then the f32 epilogue of its 8 sub-blocks
+          auto half = [&](uint32_t hf, const uint32_t (&L)[2][4], const uint32_t (&Q)[2][4]) {
+            int acc[3][4];
+            uint2 ci[3];
 #pragma unroll
-            for (int l = 0; l < 3; ++l) {
-              const uint2 ci = lds_v2(mtable_s + (((kb * 2 + hf) * 3 + l) * 8 + 2 * c) * 4);
-              acc[l][0] = acc[l][2] = static_cast<int>(ci.x);
-              acc[l][1] = acc[l][3] = static_cast<int>(ci.y);
-            }
+            for (int l = 0; l < 3; ++l) ci[l] = lds_v2(mkb + hf * 96 + l * 32);
+            const uint32_t bAh = bA + hf * 384, bBh = bB + hf * 384;
 #pragma unroll
             for (int st = 0; st < 4; ++st) {
               const int w0 = 2 * (st & 1), w1 = w0 + 1;
@@ -806,13 +808,14 @@ __global__ void __launch_bounds__((kMaxWarps + 1) * 32, 1) warpmma_kernel(const 
                 a2 = lop_and_or(mulhi(L[0][w1], k28), 0x0F0F0F0Fu, (Q[0][w1] >> sHi) & 0x30303030u);
                 a3 = lop_and_or(mulhi(L[1][w1], k28), 0x0F0F0F0Fu, (Q[1][w1] >> sHi) & 0x30303030u);
               }
-              const bool on = g == (st < 2 ? c : c + 4);
-              const uint32_t bb =
-                  on ? table_s + (kb * 32 + 16 * hf + 8 * (st >> 1) + 2 * c + (st & 1)) * 24 : zero_s;
+              const uint32_t bb = (st < 2 ? bAh : bBh) + 24 * (st & 1);
 #pragma unroll
               for (int l = 0; l < 3; ++l) {
                 const uint2 bf = lds_v2(bb + 8 * l);
-                imma16832(acc[l], a0, a1, a2, a3, bf.x, bf.y);
+                if (st == 0)
+                  imma16832_c(acc[l], a0, a1, a2, a3, bf.x, bf.y, ci[l].x, ci[l].y, ci[l].x, ci[l].y);
+                else
+                  imma16832(acc[l], a0, a1, a2, a3, bf.x, bf.y);
               }
             }
             // columns 2c, 2c+1 = sub-blocks 2c, 2c+1 of this half: scales 8 hf + 2c, +1
@@ -826,6 +829,50 @@ __global__ void __launch_bounds__((kMaxWarps + 1) * 32, 1) warpmma_kernel(const 
                                     static_cast<float>(static_cast<int8_t>(sg >> 8)) * v1);
             yacc[1][0] += dh * fmaf(static_cast<float>(static_cast<int8_t>(sh & 0xffu)), v2,
                                     static_cast<float>(static_cast<int8_t>(sh >> 8)) * v3);
+          };
+          if constexpr (kQ6WholeBlock) {
+            // both halves' quants in registers at once, so their work interleaves
+            uint32_t L[2][2][4], Q[2][2][4];
+            if (!same)
+              q6_load<-2>(ag, ah, c, 0, L, Q);
+            else if (o0 == 0)
+              q6_load<-1>(ag, ah, c, fs, L, Q);
+            else if (o0 == 8)
+              q6_load<8>(ag, ah, c, fs, L, Q);
+            else if ((o0 & 3u) == 0)
+              q6_load<4>(ag, ah, c, fs, L, Q);
+            else if (o0 < 4)
+              q6_load<0>(ag, ah, c, fs, L, Q);
+            else if (o0 < 8)
+              q6_load<1>(ag, ah, c, fs, L, Q);
+            else if (o0 < 12)
+              q6_load<2>(ag, ah, c, fs, L, Q);
+            else
+              q6_load<3>(ag, ah, c, fs, L, Q);
+            half(0, L[0], Q[0]);
+            half(1, L[1], Q[1]);
+          } else {
+#pragma unroll 1
+            for (uint32_t hf = 0; hf < 2; ++hf) {
+              uint32_t L[2][4], Q[2][4];
+              if (!same)
+                q6_load_half<-2>(ag, ah, c, hf, 0, L, Q);
+              else if (o0 == 0)
+                q6_load_half<-1>(ag, ah, c, hf, fs, L, Q);
+              else if (o0 == 8)
+                q6_load_half<8>(ag, ah, c, hf, fs, L, Q);
+              else if ((o0 & 3u) == 0)
+                q6_load_half<4>(ag, ah, c, hf, fs, L, Q);
+              else if (o0 < 4)
+                q6_load_half<0>(ag, ah, c, hf, fs, L, Q);
+              else if (o0 < 8)
+                q6_load_half<1>(ag, ah, c, hf, fs, L, Q);
+              else if (o0 < 12)
+                q6_load_half<2>(ag, ah, c, hf, fs, L, Q);
+              else
+                q6_load_half<3>(ag, ah, c, hf, fs, L, Q);
+              half(hf, L, Q);
+            }
           }
         }
       } else if constexpr (QT == 4) {
@@ -945,6 +992,8 @@ __global__ void __launch_bounds__((kMaxWarps + 1) * 32, 1) warpmma_kernel(const 
       s = 0;
       phase ^= 1;
     }
+    rot += kc1 - kc0;
+    if (rot >= nw) rot -= nw;
     kc0 = kc1;
   }  // K-tiles of the band
 
@@ -957,16 +1006,16 @@ __global__ void __launch_bounds__((kMaxWarps + 1) * 32, 1) warpmma_kernel(const 
       yacc[r][0] += __shfl_xor_sync(0xffffffffu, yacc[r][0], 2);
     }
     if (c == 0) {
-      red[((bi * kTileRows + pg) * nwc + warp) * B] = yacc[0][0];
-      red[((bi * kTileRows + pg + 8) * nwc + warp) * B] = yacc[1][0];
+      red[((bi * kTileRows + pg) * nw + warp) * B] = yacc[0][0];
+      red[((bi * kTileRows + pg + 8) * nw + warp) * B] = yacc[1][0];
     }
   } else {
 #pragma unroll
     for (int j = 0; j < 2; ++j) {
       const uint32_t b = (HILO && NT == 1) ? (j == 0 ? c : 8u) : 2 * c + j;
       if (b < B) {
-        red[((bi * kTileRows + pg) * nwc + warp) * B + b] = yacc[0][j];
-        red[((bi * kTileRows + pg + 8) * nwc + warp) * B + b] = yacc[1][j];
+        red[((bi * kTileRows + pg) * nw + warp) * B + b] = yacc[0][j];
+        red[((bi * kTileRows + pg + 8) * nw + warp) * B + b] = yacc[1][j];
       }
     }
   }
@@ -986,15 +1035,15 @@ __global__ void __launch_bounds__((kMaxWarps + 1) * 32, 1) warpmma_kernel(const 
       const uint32_t row = r_begin + (band0 + bj) * kTileRows + row16;
       if (row >= r_end) continue;
       float v0 = 0.f;
-      const float* rp = red + ((bj * kTileRows + row16) * nwc) * B + b;
-      for (uint32_t w = 0; w < nwc; ++w) v0 += rp[w * B];
+      const float* rp = red + ((bj * kTileRows + row16) * nw) * B + b;
+      for (uint32_t w = 0; w < nw; ++w) v0 += rp[w * B];
       v0 *= s_ns[b];
       if (R == 1) {
         a.y[b * a.ldy + row] = v0;
       } else {
         float v1 = 0.f;
-        const float* rq = rp + nwc * B;
-        for (uint32_t w = 0; w < nwc; ++w) v1 += rq[w * B];
+        const float* rq = rp + nw * B;
+        for (uint32_t w = 0; w < nw; ++w) v1 += rq[w * B];
         v1 *= s_ns[b];
         a.y[b * a.ldy + row / 2] = v0 * v1 * a.pair_scale;
       }
@@ -1057,7 +1106,7 @@ int warpmma_matvec(kq_ctx* ctx, const kq_matvec_desc& d, uint64_t ldx, uint64_t 
     seg_out = seg_;
     return kTileRows * seg_;
   };
-  uint32_t nkt = (nb + kMaxWarps - 1) / kMaxWarps;
+  uint32_t nkt = (nb + kTileBlocks - 1) / kTileBlocks;
   uint32_t nwc = (nb + nkt - 1) / nkt;
   uint32_t seg = 0;
   uint32_t slot = slot_for(nwc, seg);
@@ -1077,7 +1126,7 @@ int warpmma_matvec(kq_ctx* ctx, const kq_matvec_desc& d, uint64_t ldx, uint64_t 
   uint64_t table_bytes, mtable_bytes;
   const uint32_t ublk_bytes = ((nb * d.batch * 4 + 15) / 16) * 16;
   const uint64_t fixed_min =
-      2 * uint64_t(slot) + kTileRows * nwc * d.batch * 4 + ublk_bytes + kZeroBytes + 256 + 128;
+      2 * uint64_t(slot) + kTileRows * kMaxWarps * d.batch * 4 + ublk_bytes + kZeroBytes + 256 + 128;
   // batch 1: the integer kernel, whose table is x's three byte limbs (3 bytes per element) plus
   // per-sub-block sums (Q6_K: the MMAs' C init, Q4_K: the min term's sums of x)
   const uint64_t i8_table = uint64_t(nb) * kQK * 3;
@@ -1109,24 +1158,33 @@ int warpmma_matvec(kq_ctx* ctx, const kq_matvec_desc& d, uint64_t ldx, uint64_t 
   }
   // Narrower K-tiles (fewer consumer warps, smaller slots) until two slots and one band of
   // partial rows fit beside the table.
-  auto need_for = [&](uint32_t slot_, uint32_t nwc_) {
+  auto need_for = [&](uint32_t slot_) {
     return table_bytes + mtable_bytes + ublk_bytes + kZeroBytes + 16 + 2 * 8 * 8 + 128 +
-           2 * uint64_t(slot_) + uint64_t(kTileRows) * nwc_ * d.batch * 4;
+           2 * uint64_t(slot_) + uint64_t(kTileRows) * kMaxWarps * d.batch * 4;
   };
-  while (need_for(slot, nwc) > uint64_t(ctx->max_smem) && nwc > 1) {
+  while (need_for(slot) > uint64_t(ctx->max_smem) && nwc > 1) {
     ++nkt;
     nwc = (nb + nkt - 1) / nkt;
     slot = slot_for(nwc, seg);
   }
+  // Consumer warps: kMaxWarps (the warps taking turns over a tile's blocks), or one per block of
+  // the widest K-tile. Measured on B200: turns are 3% faster for Q4_K up to batch 4 (more warps
+  // hide more latency), 2% slower at batch 8 (the two-tile MMAs' registers), and 3% slower for
+  // Q6_K rows on 16-byte boundaries, where a warp fixed to one block keeps one load form (the
+  // block's alignment) instead of cycling through all of them.
+  const bool rows16 = rb % 16 == 0;
+  const bool turns = q4 ? d.batch <= 4 : !rows16;
+  const bool per_block = !turns != ((d.flags & kFlagWarpPerBlock) != 0);
+  const uint32_t nw = per_block ? nwc : kMaxWarps;
   const uint32_t rb128 = static_cast<uint32_t>(rb % 128);
   const uint32_t row_perm = (seg == 0 && (rb128 == 32 || rb128 == 96)) ? 1u : 0u;
-  if (need_for(slot, nwc) > uint64_t(ctx->max_smem))
+  if (need_for(slot) > uint64_t(ctx->max_smem))
     return fail(KQ_E_UNSUPPORTED, call,
                 "k " + std::to_string(d.k) + " with batch " + std::to_string(d.batch) +
                     " does not fit the warp-MMA kernel's shared memory");
   // partial rows of up to 16 bands between flushes, in what two ring slots leave
-  const uint32_t band_red = kTileRows * nwc * d.batch * 4;
-  const uint64_t base_need = need_for(slot, nwc) - band_red;
+  const uint32_t band_red = kTileRows * nw * d.batch * 4;
+  const uint64_t base_need = need_for(slot) - uint64_t(kTileRows) * kMaxWarps * d.batch * 4;
   const uint32_t fb = static_cast<uint32_t>(std::min<uint64_t>(
       16, std::min<uint64_t>(kRedBudget, uint64_t(ctx->max_smem) - base_need) / band_red));
   const uint32_t red_bytes = fb * band_red;
@@ -1148,7 +1206,7 @@ int warpmma_matvec(kq_ctx* ctx, const kq_matvec_desc& d, uint64_t ldx, uint64_t 
   args.nb = nb;
   args.batch = d.batch;
   args.nkt = nkt;
-  args.nwc = nwc;
+  args.nw = nw;
   args.ring = ring;
   args.slot_bytes = slot;
   args.seg_bytes = seg;
@@ -1175,7 +1233,7 @@ int warpmma_matvec(kq_ctx* ctx, const kq_matvec_desc& d, uint64_t ldx, uint64_t 
 
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(grid);
-  cfg.blockDim = dim3((nwc + 1) * 32);
+  cfg.blockDim = dim3((nw + 1) * 32);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = stream;
   cudaLaunchAttribute attr[1];
@@ -1188,7 +1246,7 @@ int warpmma_matvec(kq_ctx* ctx, const kq_matvec_desc& d, uint64_t ldx, uint64_t 
   if (e != cudaSuccess)
     return cuda_fail(e, "cudaLaunchKernelExC",
                      "warp-MMA matvec grid " + std::to_string(grid) + " x " +
-                         std::to_string((nwc + 1) * 32) + " threads, " + std::to_string(smem) +
+                         std::to_string((nw + 1) * 32) + " threads, " + std::to_string(smem) +
                          " B shared");
   return KQ_OK;
 }
