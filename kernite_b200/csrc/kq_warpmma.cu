@@ -48,6 +48,7 @@
 
 #include <algorithm>
 #include <string>
+#include <type_traits>
 
 #include "kq_device.cuh"
 #include "kq_internal.h"
@@ -94,6 +95,7 @@ struct WarpMmaArgs {
   uint32_t table_off, mtable_off, ublk_off, zero_off, red_off, bars_off;  // shared-memory layout
   uint32_t zero;         // 0: multipliers built from it are opaque to the compiler
   uint32_t row_perm;     // 1: MMA row pairs are tile rows two apart (see pg)
+  uint32_t fixed_blocks; // 1: Q6_K integer path with warp w fixed to block w (whole 16-byte rows)
   uint32_t ncol;         // B columns in use per n-tile
   uint32_t fb;           // bands of partial rows kept before a flush
   uint32_t row_unit, prologue, epilogue, flags;
@@ -263,6 +265,91 @@ __device__ __forceinline__ void q6_load(uint32_t ag, uint32_t ah, uint32_t c, ui
                                         uint32_t (&L)[2][2][4], uint32_t (&Q)[2][2][4]) {
   q6_load_half<MODE>(ag, ah, c, 0, fs, L[0], Q[0]);
   q6_load_half<MODE>(ag, ah, c, 1, fs, L[1], Q[1]);
+}
+
+// 16 bytes at shared address `addr` whose residue mod 16 is known at compile time to be in
+// the class F: 16 (0), 8 (8), 4 (4 or 12), 2 (2 or 10), 6 (6 or 14). Aligned classes load
+// directly; for 2 and 6 the five 4-byte words from addr - 2 come in as 8- and 4-byte loads at
+// their natural alignment and each output word is a 16-bit funnel shift of two of them.
+template <int F>
+__device__ __forceinline__ void lds16_class(uint32_t addr, uint32_t (&w)[4]) {
+  if constexpr (F == 16 || F == 8 || F == 4) {
+    lds16<F>(addr, w);
+  } else {
+    const uint32_t b = addr - 2;
+    uint32_t v[5];
+    if constexpr (F == 2) {  // b = 0 mod 8
+      const uint2 p0 = lds_v2(b), p1 = lds_v2(b + 8);
+      v[0] = p0.x; v[1] = p0.y; v[2] = p1.x; v[3] = p1.y; v[4] = lds_u32(b + 16);
+    } else {                 // b = 4 mod 8
+      const uint2 p1 = lds_v2(b + 4), p2 = lds_v2(b + 12);
+      v[0] = lds_u32(b); v[1] = p1.x; v[2] = p1.y; v[3] = p2.x; v[4] = p2.y;
+    }
+#pragma unroll
+    for (int k = 0; k < 4; ++k) w[k] = __funnelshift_r(v[k], v[k + 1], 16);
+  }
+}
+
+// The residue class (for lds16_class) of a 2-byte aligned offset o mod 16.
+__host__ __device__ constexpr int residue_class(uint32_t o) {
+  return (o & 15u) == 0 ? 16 : (o & 7u) == 0 ? 8 : (o & 3u) == 0 ? 4 : (o & 7u) == 2 ? 2 : 6;
+}
+
+// One half hf of a Q6_K super-block on the integer path, rows g and g+8 of thread (g, c):
+// L[row] = the thread's 16 ql bytes, Q[row] = its 16 qh bytes. Per step, A = 4 + 4 6-bit quants
+// of one sub-block (ql nibble | qh pair << 4, as bytes); B = the three byte limbs of the same
+// elements of x (from the table, or zeros for lanes whose column is another sub-block); C of the
+// first step = -32 * the limb sums of the thread's sub-blocks. Then y += d * sum_n sc_n D_n.
+//  mkb: the accumulator start values of the block; bA, bB: this thread's B-fragment bases for
+//  steps 0-1 and 2-3; kLo, sHi: the qh-pair multiplier (low group) and shift (high group).
+__device__ __forceinline__ void q6i8_half(uint32_t hf, const uint32_t (&L)[2][4],
+                                          const uint32_t (&Q)[2][4], uint32_t ag, uint32_t ah,
+                                          uint32_t c, uint32_t mkb, uint32_t bA, uint32_t bB,
+                                          uint32_t kLo, uint32_t k28, uint32_t sHi, float dg,
+                                          float dh, float (&yacc)[2][2]) {
+  int acc[3][4];
+  uint2 ci[3];
+#pragma unroll
+  for (int l = 0; l < 3; ++l) ci[l] = lds_v2(mkb + hf * 96 + l * 32);
+  const uint32_t bAh = bA + hf * 384, bBh = bB + hf * 384;
+#pragma unroll
+  for (int st = 0; st < 4; ++st) {
+    const int w0 = 2 * (st & 1), w1 = w0 + 1;
+    uint32_t a0, a1, a2, a3;
+    if (st < 2) {
+      // low nibble | qh pair (bits 0-1 for c < 2, 2-3 for c >= 2) moved to bits 4-5
+      a0 = lop_and_or(L[0][w0], 0x0F0F0F0Fu, mullo(Q[0][w0], kLo) & 0x30303030u);
+      a1 = lop_and_or(L[1][w0], 0x0F0F0F0Fu, mullo(Q[1][w0], kLo) & 0x30303030u);
+      a2 = lop_and_or(L[0][w1], 0x0F0F0F0Fu, mullo(Q[0][w1], kLo) & 0x30303030u);
+      a3 = lop_and_or(L[1][w1], 0x0F0F0F0Fu, mullo(Q[1][w1], kLo) & 0x30303030u);
+    } else {
+      // high nibble | qh pair (bits 4-5 for c < 2, 6-7 for c >= 2) at bits 4-5
+      a0 = lop_and_or(mulhi(L[0][w0], k28), 0x0F0F0F0Fu, (Q[0][w0] >> sHi) & 0x30303030u);
+      a1 = lop_and_or(mulhi(L[1][w0], k28), 0x0F0F0F0Fu, (Q[1][w0] >> sHi) & 0x30303030u);
+      a2 = lop_and_or(mulhi(L[0][w1], k28), 0x0F0F0F0Fu, (Q[0][w1] >> sHi) & 0x30303030u);
+      a3 = lop_and_or(mulhi(L[1][w1], k28), 0x0F0F0F0Fu, (Q[1][w1] >> sHi) & 0x30303030u);
+    }
+    const uint32_t bb = (st < 2 ? bAh : bBh) + 24 * (st & 1);
+#pragma unroll
+    for (int l = 0; l < 3; ++l) {
+      const uint2 bf = lds_v2(bb + 8 * l);
+      if (st == 0)
+        imma16832_c(acc[l], a0, a1, a2, a3, bf.x, bf.y, ci[l].x, ci[l].y, ci[l].x, ci[l].y);
+      else
+        imma16832(acc[l], a0, a1, a2, a3, bf.x, bf.y);
+    }
+  }
+  // columns 2c, 2c+1 = sub-blocks 2c, 2c+1 of this half: scales 8 hf + 2c, +1
+  const uint32_t sg = lds_u16(ag + 192 + 8 * hf + 2 * c);
+  const uint32_t sh = lds_u16(ah + 192 + 8 * hf + 2 * c);
+  const float v0 = limbs_to_f32(acc[2][0], acc[1][0], acc[0][0]);
+  const float v1 = limbs_to_f32(acc[2][1], acc[1][1], acc[0][1]);
+  const float v2 = limbs_to_f32(acc[2][2], acc[1][2], acc[0][2]);
+  const float v3 = limbs_to_f32(acc[2][3], acc[1][3], acc[0][3]);
+  yacc[0][0] += dg * fmaf(static_cast<float>(static_cast<int8_t>(sg & 0xffu)), v0,
+                          static_cast<float>(static_cast<int8_t>(sg >> 8)) * v1);
+  yacc[1][0] += dh * fmaf(static_cast<float>(static_cast<int8_t>(sh & 0xffu)), v2,
+                          static_cast<float>(static_cast<int8_t>(sh >> 8)) * v3);
 }
 
 // One Q6_K super-block of rows g (at shared address ag) and g+8 (ah) for thread (g, c) of a warp,
@@ -681,6 +768,124 @@ __global__ void __launch_bounds__((kMaxWarps + 1) * 32, 1) warpmma_kernel(const 
   // When every row starts on a 16-byte boundary, a block's offset within 16 bytes is the same
   // for all rows of a warp: (kb * block bytes) mod 16.
   const bool rows16 = (rb32 & 15u) == 0;
+  // The band is done: this warp's partial rows go to the reduction buffer; every fb bands (and
+  // after the last) the warps meet and sum them in a fixed order into y.
+  auto band_end = [&](uint32_t band, uint32_t& bi) {
+    if constexpr (QT == 6 || I8) {
+      // the four threads of a row hold different sub-blocks of vector 0
+#pragma unroll
+      for (int r = 0; r < 2; ++r) {
+        yacc[r][0] += __shfl_xor_sync(0xffffffffu, yacc[r][0], 1);
+        yacc[r][0] += __shfl_xor_sync(0xffffffffu, yacc[r][0], 2);
+      }
+      if (c == 0) {
+        red[((bi * kTileRows + pg) * nw + warp) * B] = yacc[0][0];
+        red[((bi * kTileRows + pg + 8) * nw + warp) * B] = yacc[1][0];
+      }
+    } else {
+#pragma unroll
+      for (int j = 0; j < 2; ++j) {
+        const uint32_t b = (HILO && NT == 1) ? (j == 0 ? c : 8u) : 2 * c + j;
+        if (b < B) {
+          red[((bi * kTileRows + pg) * nw + warp) * B + b] = yacc[0][j];
+          red[((bi * kTileRows + pg + 8) * nw + warp) * B + b] = yacc[1][j];
+        }
+      }
+    }
+    yacc[0][0] = yacc[0][1] = yacc[1][0] = yacc[1][1] = 0.f;
+
+    if (bi + 1 == a.fb || band + 1 == nbands) {
+      // Flush: sum every warp's partial of each row in a fixed order and write y.
+      named_barrier(1, nthr);
+      const uint32_t band0 = band - bi;
+      const uint32_t R = a.row_unit;
+      const uint32_t nout = (bi + 1) * (kTileRows / R) * B;
+      for (uint32_t o = tid; o < nout; o += nthr) {
+        const uint32_t b = o % B;
+        const uint32_t q = o / B;  // output index within the flushed bands
+        const uint32_t row16 = (q % (kTileRows / R)) * R;
+        const uint32_t bj = q / (kTileRows / R);
+        const uint32_t row = r_begin + (band0 + bj) * kTileRows + row16;
+        if (row >= r_end) continue;
+        float v0 = 0.f;
+        const float* rp = red + ((bj * kTileRows + row16) * nw) * B + b;
+        for (uint32_t w = 0; w < nw; ++w) v0 += rp[w * B];
+        v0 *= s_ns[b];
+        if (R == 1) {
+          a.y[b * a.ldy + row] = v0;
+        } else {
+          float v1 = 0.f;
+          const float* rq = rp + nw * B;
+          for (uint32_t w = 0; w < nw; ++w) v1 += rq[w * B];
+          v1 *= s_ns[b];
+          a.y[b * a.ldy + row / 2] = v0 * v1 * a.pair_scale;
+        }
+      }
+      named_barrier(1, nthr);
+      bi = 0;
+    } else {
+      ++bi;
+    }
+  };
+
+  // Q6_K integer path, tiles of whole rows on 16-byte boundaries, one warp per block: warp w
+  // takes block w of every tile, so its block's offset within 16 bytes (2w mod 16) is fixed, and
+  // the loop is compiled once per residue class, with every address but the slot's hoisted.
+  if constexpr (QT == 6 && I8) {
+    if (a.fixed_blocks) {
+      auto fixed_loop = [&](auto cls) {
+        constexpr int F = decltype(cls)::value;
+        const uint32_t kb = warp;
+        const float u0 = ublk[kb];
+        const uint32_t tkb = table_s + (kb * 32 + 2 * c) * 24;
+        const uint32_t bA = g == c ? tkb : zero_s;
+        const uint32_t bB = g == c + 4 ? tkb + 8 * 24 : zero_s;
+        const uint32_t mkb = mtable_s + (kb * 48 + 2 * c) * 4;
+        const uint32_t rb32 = static_cast<uint32_t>(RB);
+        const uint32_t off_g = pg * rb32 + kb * kBlk;
+        uint32_t s = 0, phase = 0, bi = 0;
+        for (uint32_t band = 0; band < nbands; ++band) {
+          bool ok = !*reinterpret_cast<volatile int*>(&s_failed);
+          if (ok && !mbar_wait(full_bar(s), phase)) {
+            ok = false;
+            s_failed = 1;
+            report_error(a.err, kErrWaitFull);
+          }
+          if (!__any_sync(0xffffffffu, !ok)) {
+            const uint32_t ag = ring_s + s * a.slot_bytes + off_g, ah = ag + 8 * rb32;
+            const float dg = u0 * h2f(lds_u16(ag + 208)), dh = u0 * h2f(lds_u16(ah + 208));
+#pragma unroll 1
+            for (uint32_t hf = 0; hf < 2; ++hf) {
+              uint32_t L[2][4], Q[2][4];
+#pragma unroll
+              for (int r = 0; r < 2; ++r) {
+                const uint32_t base = r ? ah : ag;
+                lds16_class<F>(base + 64 * hf + 16 * c, L[r]);
+                lds16_class<F>(base + 128 + 32 * hf + 16 * (c & 1), Q[r]);
+              }
+              q6i8_half(hf, L, Q, ag, ah, c, mkb, bA, bB, kLo, k28, sHi, dg, dh, yacc);
+            }
+          }
+          __syncwarp();
+          if (lane == 0) mbar_arrive(empty_bar(s));
+          if (++s == a.ring) {
+            s = 0;
+            phase ^= 1;
+          }
+          band_end(band, bi);
+        }
+      };
+      switch (residue_class(warp * kBlk)) {
+        case 16: fixed_loop(std::integral_constant<int, 16>()); break;
+        case 8: fixed_loop(std::integral_constant<int, 8>()); break;
+        case 4: fixed_loop(std::integral_constant<int, 4>()); break;
+        case 2: fixed_loop(std::integral_constant<int, 2>()); break;
+        default: fixed_loop(std::integral_constant<int, 6>()); break;
+      }
+      return;
+    }
+  }
+
   // Unit j (super-block kc0 + j) of a tile goes to warp (rot + j) mod nw, rot advancing by the
   // tile's super-block count, so the warps take turns when there are more warps than blocks.
   uint32_t s = 0, phase = 0, bi = 0, rot = 0;
@@ -784,51 +989,8 @@ __global__ void __launch_bounds__((kMaxWarps + 1) * 32, 1) warpmma_kernel(const 
           const uint32_t bB = g == c + 4 ? tkb + 8 * 24 : zero_s;
           // accumulator start values: entries ((kb * 2 + hf) * 3 + l) * 8 + 2c, 4 bytes each
           const uint32_t mkb = mtable_s + (kb * 48 + 2 * c) * 4;
-          // one half: 4 steps x 3 limbs, then the f32 epilogue of its 8 sub-blocks
           auto half = [&](uint32_t hf, const uint32_t (&L)[2][4], const uint32_t (&Q)[2][4]) {
-            int acc[3][4];
-            uint2 ci[3];
-#pragma unroll
-            for (int l = 0; l < 3; ++l) ci[l] = lds_v2(mkb + hf * 96 + l * 32);
-            const uint32_t bAh = bA + hf * 384, bBh = bB + hf * 384;
-#pragma unroll
-            for (int st = 0; st < 4; ++st) {
-              const int w0 = 2 * (st & 1), w1 = w0 + 1;
-              uint32_t a0, a1, a2, a3;
-              if (st < 2) {
-                // low nibble | qh pair (bits 0-1 for c < 2, 2-3 for c >= 2) moved to bits 4-5
-                a0 = lop_and_or(L[0][w0], 0x0F0F0F0Fu, mullo(Q[0][w0], kLo) & 0x30303030u);
-                a1 = lop_and_or(L[1][w0], 0x0F0F0F0Fu, mullo(Q[1][w0], kLo) & 0x30303030u);
-                a2 = lop_and_or(L[0][w1], 0x0F0F0F0Fu, mullo(Q[0][w1], kLo) & 0x30303030u);
-                a3 = lop_and_or(L[1][w1], 0x0F0F0F0Fu, mullo(Q[1][w1], kLo) & 0x30303030u);
-              } else {
-                // high nibble | qh pair (bits 4-5 for c < 2, 6-7 for c >= 2) at bits 4-5
-                a0 = lop_and_or(mulhi(L[0][w0], k28), 0x0F0F0F0Fu, (Q[0][w0] >> sHi) & 0x30303030u);
-                a1 = lop_and_or(mulhi(L[1][w0], k28), 0x0F0F0F0Fu, (Q[1][w0] >> sHi) & 0x30303030u);
-                a2 = lop_and_or(mulhi(L[0][w1], k28), 0x0F0F0F0Fu, (Q[0][w1] >> sHi) & 0x30303030u);
-                a3 = lop_and_or(mulhi(L[1][w1], k28), 0x0F0F0F0Fu, (Q[1][w1] >> sHi) & 0x30303030u);
-              }
-              const uint32_t bb = (st < 2 ? bAh : bBh) + 24 * (st & 1);
-#pragma unroll
-              for (int l = 0; l < 3; ++l) {
-                const uint2 bf = lds_v2(bb + 8 * l);
-                if (st == 0)
-                  imma16832_c(acc[l], a0, a1, a2, a3, bf.x, bf.y, ci[l].x, ci[l].y, ci[l].x, ci[l].y);
-                else
-                  imma16832(acc[l], a0, a1, a2, a3, bf.x, bf.y);
-              }
-            }
-            // columns 2c, 2c+1 = sub-blocks 2c, 2c+1 of this half: scales 8 hf + 2c, +1
-            const uint32_t sg = lds_u16(ag + 192 + 8 * hf + 2 * c);
-            const uint32_t sh = lds_u16(ah + 192 + 8 * hf + 2 * c);
-            const float v0 = limbs_to_f32(acc[2][0], acc[1][0], acc[0][0]);
-            const float v1 = limbs_to_f32(acc[2][1], acc[1][1], acc[0][1]);
-            const float v2 = limbs_to_f32(acc[2][2], acc[1][2], acc[0][2]);
-            const float v3 = limbs_to_f32(acc[2][3], acc[1][3], acc[0][3]);
-            yacc[0][0] += dg * fmaf(static_cast<float>(static_cast<int8_t>(sg & 0xffu)), v0,
-                                    static_cast<float>(static_cast<int8_t>(sg >> 8)) * v1);
-            yacc[1][0] += dh * fmaf(static_cast<float>(static_cast<int8_t>(sh & 0xffu)), v2,
-                                    static_cast<float>(static_cast<int8_t>(sh >> 8)) * v3);
+            q6i8_half(hf, L, Q, ag, ah, c, mkb, bA, bB, kLo, k28, sHi, dg, dh, yacc);
           };
           if constexpr (kQ6WholeBlock) {
             // both halves' quants in registers at once, so their work interleaves
@@ -997,62 +1159,7 @@ __global__ void __launch_bounds__((kMaxWarps + 1) * 32, 1) warpmma_kernel(const 
     kc0 = kc1;
   }  // K-tiles of the band
 
-  // The band is done: this warp's partial rows go to the reduction buffer.
-  if constexpr (QT == 6 || I8) {
-    // the four threads of a row hold different sub-blocks of vector 0
-#pragma unroll
-    for (int r = 0; r < 2; ++r) {
-      yacc[r][0] += __shfl_xor_sync(0xffffffffu, yacc[r][0], 1);
-      yacc[r][0] += __shfl_xor_sync(0xffffffffu, yacc[r][0], 2);
-    }
-    if (c == 0) {
-      red[((bi * kTileRows + pg) * nw + warp) * B] = yacc[0][0];
-      red[((bi * kTileRows + pg + 8) * nw + warp) * B] = yacc[1][0];
-    }
-  } else {
-#pragma unroll
-    for (int j = 0; j < 2; ++j) {
-      const uint32_t b = (HILO && NT == 1) ? (j == 0 ? c : 8u) : 2 * c + j;
-      if (b < B) {
-        red[((bi * kTileRows + pg) * nw + warp) * B + b] = yacc[0][j];
-        red[((bi * kTileRows + pg + 8) * nw + warp) * B + b] = yacc[1][j];
-      }
-    }
-  }
-  yacc[0][0] = yacc[0][1] = yacc[1][0] = yacc[1][1] = 0.f;
-
-  if (bi + 1 == a.fb || band + 1 == nbands) {
-    // Flush: sum every warp's partial of each row in a fixed order and write y.
-    named_barrier(1, nthr);
-    const uint32_t band0 = band - bi;
-    const uint32_t R = a.row_unit;
-    const uint32_t nout = (bi + 1) * (kTileRows / R) * B;
-    for (uint32_t o = tid; o < nout; o += nthr) {
-      const uint32_t b = o % B;
-      const uint32_t q = o / B;  // output index within the flushed bands
-      const uint32_t row16 = (q % (kTileRows / R)) * R;
-      const uint32_t bj = q / (kTileRows / R);
-      const uint32_t row = r_begin + (band0 + bj) * kTileRows + row16;
-      if (row >= r_end) continue;
-      float v0 = 0.f;
-      const float* rp = red + ((bj * kTileRows + row16) * nw) * B + b;
-      for (uint32_t w = 0; w < nw; ++w) v0 += rp[w * B];
-      v0 *= s_ns[b];
-      if (R == 1) {
-        a.y[b * a.ldy + row] = v0;
-      } else {
-        float v1 = 0.f;
-        const float* rq = rp + nw * B;
-        for (uint32_t w = 0; w < nw; ++w) v1 += rq[w * B];
-        v1 *= s_ns[b];
-        a.y[b * a.ldy + row / 2] = v0 * v1 * a.pair_scale;
-      }
-    }
-    named_barrier(1, nthr);
-    bi = 0;
-  } else {
-    ++bi;
-  }
+  band_end(band, bi);
   }  // bands
 }
 
@@ -1217,6 +1324,7 @@ int warpmma_matvec(kq_ctx* ctx, const kq_matvec_desc& d, uint64_t ldx, uint64_t 
   args.red_off = args.zero_off + kZeroBytes;
   args.zero = 0;
   args.row_perm = row_perm;
+  args.fixed_blocks = (mode == 5 && nkt == 1 && seg == 0 && rows16 && nw == nwc) ? 1u : 0u;
   args.bars_off = args.red_off + red_bytes;
   args.ncol = ncol;
   args.fb = fb;

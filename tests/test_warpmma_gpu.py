@@ -252,3 +252,18 @@ def test_warpmma_other_batch1_variant_integer_inputs_are_exact(kernels, qtype):
     y = run(kernels, qtype, W, x, rows, K, flags=WM | ALT_BATCH1)
     y_ref, _ = oracle.matvec_ref(qtype, blocks.reshape(-1), x, K, 0, rows)
     assert np.array_equal(y, y_ref.astype(np.float32))
+
+
+OTHER_WARPS = 1 << 29  # the other consumer-warp arrangement (turns <-> one warp per block)
+
+
+@pytest.mark.parametrize("qtype,rows,K,batch", [(4, 300, 4096, 1), (4, 130, 4096, 4),
+                                                (4, 97, 8192, 8), (6, 333, 4096, 1),
+                                                (6, 77, 11008, 1), (4, 50, 28672, 2),
+                                                (6, 40, 2048, 1)])
+def test_warpmma_other_warp_arrangement_matches_oracle(kernels, qtype, rows, K, batch):
+    W = dev_weights(kernels, qtype, rows, K, kb.stream_key(89, qtype))
+    x = np.random.default_rng(89).standard_normal((batch, K), dtype=np.float32)
+    y = run(kernels, qtype, W, x, rows, K, flags=WM | OTHER_WARPS)
+    y_ref, bound = oracle.matvec_ref(qtype, W.cpu().numpy(), x, K, 0, rows)
+    check(y, y_ref, bound, f"other warp arrangement q{qtype} {rows}x{K} b{batch}")
