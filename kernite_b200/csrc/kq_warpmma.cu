@@ -561,17 +561,18 @@ __global__ void __launch_bounds__((kMaxWarps + 1) * 32, 1) warpmma_kernel(const 
         const uint32_t xb = xb0 + j * nw;
         if (xb >= nxb) break;
         const uint32_t b = xb / a.nb, kb = xb - b * a.nb;
-        double sq = 0.0;
+        double sq = 0.0;  // only the RMS norm needs it
         float mx = 0.f;
 #pragma unroll
-        for (int r = 0; r < 8; ++r) {
-          sq = fma(static_cast<double>(v[j][r]), static_cast<double>(v[j][r]), sq);
-          mx = fmaxf(mx, fabsf(v[j][r]));
-        }
+        for (int r = 0; r < 8; ++r) mx = fmaxf(mx, fabsf(v[j][r]));
 #pragma unroll
-        for (int o = 16; o; o >>= 1) {
-          sq += __shfl_xor_sync(0xffffffffu, sq, o);
-          mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+        for (int o = 16; o; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+        if (a.prologue == KQ_PROLOGUE_RMSNORM) {
+#pragma unroll
+          for (int r = 0; r < 8; ++r)
+            sq = fma(static_cast<double>(v[j][r]), static_cast<double>(v[j][r]), sq);
+#pragma unroll
+          for (int o = 16; o; o >>= 1) sq += __shfl_xor_sync(0xffffffffu, sq, o);
         }
         if constexpr (I8) {
           // 24-bit fixed point for the block: the power of two that brings max |x| into
@@ -605,20 +606,39 @@ __global__ void __launch_bounds__((kMaxWarps + 1) * 32, 1) warpmma_kernel(const 
             // C init of the MMAs: -32 * (sum of each limb over each 16-element sub-block), so
             // that A = q (unsigned) gives sum (q - 32) x exactly. Element 32 r + lane is in
             // sub-block 2r + lane/16 of the block: half r / 4, column (2r + lane/16) % 8.
+            // The 16-lane sums of a limb lie in [-2048, 2048], so two of them travel packed in
+            // one word (low + 65536 high, unpacked exactly): limbs 0 and 1 of r, and limb 2 of
+            // r and r + 1, 12 words instead of 24 through the shuffles.
+            int P[12];
 #pragma unroll
-            for (int r = 0; r < 8; ++r)
+            for (int r = 0; r < 8; ++r) P[r] = L[0][r] + L[1][r] * 65536;
 #pragma unroll
-              for (int l = 0; l < 3; ++l) {
-                int t = L[l][r];
+            for (int r = 0; r < 4; ++r) P[8 + r] = L[2][2 * r] + L[2][2 * r + 1] * 65536;
 #pragma unroll
-                for (int o = 8; o; o >>= 1) t += __shfl_xor_sync(0xffffffffu, t, o);
-                if ((lane & 15) == 0) {
-                  const uint32_t hh = r >> 2, n = (2 * r + (lane >> 4)) & 7;
-                  asm volatile("st.shared.s32 [%0], %1;" ::"r"(mtable_s + (((kb * 2 + hh) * 3 + l) * 8 + n) * 4),
-                               "r"(-32 * t)
-                               : "memory");
-                }
+            for (int o = 8; o; o >>= 1)
+#pragma unroll
+              for (int i = 0; i < 12; ++i) P[i] += __shfl_xor_sync(0xffffffffu, P[i], o);
+            if ((lane & 15) == 0) {
+              auto put = [&](int r, int l, int t) {
+                const uint32_t hh = r >> 2, n = (2 * r + (lane >> 4)) & 7;
+                asm volatile("st.shared.s32 [%0], %1;" ::"r"(mtable_s + (((kb * 2 + hh) * 3 + l) * 8 + n) * 4),
+                             "r"(-32 * t)
+                             : "memory");
+              };
+              auto lo16 = [](int w) { return static_cast<int>(static_cast<int16_t>(w & 0xffff)); };
+#pragma unroll
+              for (int r = 0; r < 8; ++r) {
+                const int t0 = lo16(P[r]);
+                put(r, 0, t0);
+                put(r, 1, (P[r] - t0) >> 16);
               }
+#pragma unroll
+              for (int r = 0; r < 4; ++r) {
+                const int t0 = lo16(P[8 + r]);
+                put(2 * r, 2, t0);
+                put(2 * r + 1, 2, (P[8 + r] - t0) >> 16);
+              }
+            }
           } else {
             // the sum of x (in limb units) over each 32-element sub-block r, for the min term
 #pragma unroll
