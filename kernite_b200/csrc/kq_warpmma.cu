@@ -604,39 +604,27 @@ __global__ void __launch_bounds__((kMaxWarps + 1) * 32, 1) warpmma_kernel(const 
           }
           if constexpr (QT == 6) {
             // C init of the MMAs: -32 * (sum of each limb over each 16-element sub-block), so
-            // that A = q (unsigned) gives sum (q - 32) x exactly. Element 32 r + lane is in
-            // sub-block 2r + lane/16 of the block: half r / 4, column (2r + lane/16) % 8.
-            // The 16-lane sums of a limb lie in [-2048, 2048], so two of them travel packed in
-            // one word (low + 65536 high, unpacked exactly): limbs 0 and 1 of r, and limb 2 of
-            // r and r + 1, 12 words instead of 24 through the shuffles.
-            int P[12];
+            // that A = q (unsigned) gives sum (q - 32) x exactly. The 48 sums (3 limbs x 16
+            // sub-blocks) are read back from the table just written: sub-block sb of the block
+            // is chunks 2 sb and 2 sb + 1, limb l the 8 bytes at 8 l of each; one dp4a per 4
+            // bytes. Lane i takes sums i and i + 32.
+            __syncwarp();
 #pragma unroll
-            for (int r = 0; r < 8; ++r) P[r] = L[0][r] + L[1][r] * 65536;
-#pragma unroll
-            for (int r = 0; r < 4; ++r) P[8 + r] = L[2][2 * r] + L[2][2 * r + 1] * 65536;
-#pragma unroll
-            for (int o = 8; o; o >>= 1)
-#pragma unroll
-              for (int i = 0; i < 12; ++i) P[i] += __shfl_xor_sync(0xffffffffu, P[i], o);
-            if ((lane & 15) == 0) {
-              auto put = [&](int r, int l, int t) {
-                const uint32_t hh = r >> 2, n = (2 * r + (lane >> 4)) & 7;
-                asm volatile("st.shared.s32 [%0], %1;" ::"r"(mtable_s + (((kb * 2 + hh) * 3 + l) * 8 + n) * 4),
+            for (int pass = 0; pass < 2; ++pass) {
+              const uint32_t i = lane + 32 * pass;
+              if (i < 48) {
+                const uint32_t l = i >> 4, sb = i & 15;
+                const uint32_t at = table_s + (kb * 32 + 2 * sb) * 24 + 8 * l;
+                const uint2 w0 = lds_v2(at), w1 = lds_v2(at + 24);
+                int t = __dp4a(static_cast<int>(w0.x), 0x01010101, 0);
+                t = __dp4a(static_cast<int>(w0.y), 0x01010101, t);
+                t = __dp4a(static_cast<int>(w1.x), 0x01010101, t);
+                t = __dp4a(static_cast<int>(w1.y), 0x01010101, t);
+                // entry ((kb * 2 + half) * 3 + l) * 8 + (sub-block within the half)
+                asm volatile("st.shared.s32 [%0], %1;" ::"r"(
+                                 mtable_s + ((kb * 2 + (sb >> 3)) * 24 + l * 8 + (sb & 7)) * 4),
                              "r"(-32 * t)
                              : "memory");
-              };
-              auto lo16 = [](int w) { return static_cast<int>(static_cast<int16_t>(w & 0xffff)); };
-#pragma unroll
-              for (int r = 0; r < 8; ++r) {
-                const int t0 = lo16(P[r]);
-                put(r, 0, t0);
-                put(r, 1, (P[r] - t0) >> 16);
-              }
-#pragma unroll
-              for (int r = 0; r < 4; ++r) {
-                const int t0 = lo16(P[8 + r]);
-                put(2 * r, 2, t0);
-                put(2 * r + 1, 2, (P[8 + r] - t0) >> 16);
               }
             }
           } else {
