@@ -110,6 +110,13 @@ __device__ __forceinline__ uint32_t lop_and_or(uint32_t a, uint32_t b, uint32_t 
   return d;
 }
 
+// The low nibble of each byte from lo, the high nibble from hi (one LOP3).
+__device__ __forceinline__ uint32_t nibble_select(uint32_t lo, uint32_t hi) {
+  uint32_t d;  // (lo & 0x0F0F0F0F) | (hi & 0xF0F0F0F0)
+  asm("lop3.b32 %0, %1, %2, %3, 0xB8;" : "=r"(d) : "r"(hi), "r"(0x0F0F0F0Fu), "r"(lo));
+  return d;
+}
+
 __device__ __forceinline__ uint32_t hfma2(uint32_t a, uint32_t b, uint32_t c) {
   uint32_t d;
   asm("fma.rn.f16x2 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
@@ -301,33 +308,41 @@ __host__ __device__ constexpr int residue_class(uint32_t o) {
 // elements of x (from the table, or zeros for lanes whose column is another sub-block); C of the
 // first step = -32 * the limb sums of the thread's sub-blocks. Then y += d * sum_n sc_n D_n.
 //  mkb: the accumulator start values of the block; bA, bB: this thread's B-fragment bases for
-//  steps 0-1 and 2-3; kLo, sHi: the qh-pair multiplier (low group) and shift (high group).
+//  steps 0-1 and 2-3; sHi: the shift that brings the thread's qh pairs to bits 0-1 and 4-5;
+//  k16, k28: 16 and 2^28 as values the compiler cannot see (x16 and >> 4 on the FMA pipe).
 __device__ __forceinline__ void q6i8_half(uint32_t hf, const uint32_t (&L)[2][4],
                                           const uint32_t (&Q)[2][4], uint32_t ag, uint32_t ah,
                                           uint32_t c, uint32_t mkb, uint32_t bA, uint32_t bB,
-                                          uint32_t kLo, uint32_t k28, uint32_t sHi, float dg,
+                                          uint32_t k16, uint32_t k28, uint32_t sHi, float dg,
                                           float dh, float (&yacc)[2][2]) {
   int acc[3][4];
   uint2 ci[3];
 #pragma unroll
   for (int l = 0; l < 3; ++l) ci[l] = lds_v2(mkb + hf * 96 + l * 32);
   const uint32_t bAh = bA + hf * 384, bBh = bB + hf * 384;
+  // V: the thread's two qh pairs of each element slot at bits 0-1 (low group) and 4-5 (high
+  // group) of each byte: qh bits 0-1 / 4-5 for c < 2, 2-3 / 6-7 for c >= 2 (sHi = 0 or 2)
+  uint32_t V[2][4];
+#pragma unroll
+  for (int r = 0; r < 2; ++r)
+#pragma unroll
+    for (int i = 0; i < 4; ++i) V[r][i] = (Q[r][i] >> sHi) & 0x33333333u;
 #pragma unroll
   for (int st = 0; st < 4; ++st) {
     const int w0 = 2 * (st & 1), w1 = w0 + 1;
     uint32_t a0, a1, a2, a3;
     if (st < 2) {
-      // low nibble | qh pair (bits 0-1 for c < 2, 2-3 for c >= 2) moved to bits 4-5
-      a0 = lop_and_or(L[0][w0], 0x0F0F0F0Fu, mullo(Q[0][w0], kLo) & 0x30303030u);
-      a1 = lop_and_or(L[1][w0], 0x0F0F0F0Fu, mullo(Q[1][w0], kLo) & 0x30303030u);
-      a2 = lop_and_or(L[0][w1], 0x0F0F0F0Fu, mullo(Q[0][w1], kLo) & 0x30303030u);
-      a3 = lop_and_or(L[1][w1], 0x0F0F0F0Fu, mullo(Q[1][w1], kLo) & 0x30303030u);
+      // low nibble | pair from bits 0-1 of V, moved to bits 4-5
+      a0 = nibble_select(L[0][w0], mullo(V[0][w0], k16));
+      a1 = nibble_select(L[1][w0], mullo(V[1][w0], k16));
+      a2 = nibble_select(L[0][w1], mullo(V[0][w1], k16));
+      a3 = nibble_select(L[1][w1], mullo(V[1][w1], k16));
     } else {
-      // high nibble | qh pair (bits 4-5 for c < 2, 6-7 for c >= 2) at bits 4-5
-      a0 = lop_and_or(mulhi(L[0][w0], k28), 0x0F0F0F0Fu, (Q[0][w0] >> sHi) & 0x30303030u);
-      a1 = lop_and_or(mulhi(L[1][w0], k28), 0x0F0F0F0Fu, (Q[1][w0] >> sHi) & 0x30303030u);
-      a2 = lop_and_or(mulhi(L[0][w1], k28), 0x0F0F0F0Fu, (Q[0][w1] >> sHi) & 0x30303030u);
-      a3 = lop_and_or(mulhi(L[1][w1], k28), 0x0F0F0F0Fu, (Q[1][w1] >> sHi) & 0x30303030u);
+      // high nibble | pair from bits 4-5 of V, in place
+      a0 = nibble_select(mulhi(L[0][w0], k28), V[0][w0]);
+      a1 = nibble_select(mulhi(L[1][w0], k28), V[1][w0]);
+      a2 = nibble_select(mulhi(L[0][w1], k28), V[0][w1]);
+      a3 = nibble_select(mulhi(L[1][w1], k28), V[1][w1]);
     }
     const uint32_t bb = (st < 2 ? bAh : bBh) + 24 * (st & 1);
 #pragma unroll
@@ -752,9 +767,8 @@ __global__ void __launch_bounds__((kMaxWarps + 1) * 32, 1) warpmma_kernel(const 
   const uint32_t zero_s = ring_s + a.zero_off + (QT == 4 ? c * 8 : 0);
   const uint32_t k24 = (1u << 24) << a.zero;              // >> 8
   const uint32_t k28 = (1u << 28) << a.zero;              // >> 4
-  // I8 Q6_K: qh pairs to bits 4-5: low group by a multiply (x16 for c < 2, x4 for c >= 2), high
-  // group by a right shift (0 or 2)
-  const uint32_t kLo = (c >= 2 ? 4u : 16u) << a.zero;
+  // I8 Q6_K: the shift of the thread's qh pairs (see q6i8_half), and 16 kept opaque
+  const uint32_t k16 = 16u << a.zero;
   const uint32_t sHi = c >= 2 ? 2u : 0u;
   const uint32_t kT = (1u << (QT == 6 ? (c >= 2 ? 2 : 4) : 0)) << a.zero;    // << sT
   const uint32_t kT13 = (1u << (QT == 6 ? (c >= 2 ? 26 : 28) : 0)) << a.zero;  // >> (8 - sT)
@@ -841,9 +855,10 @@ __global__ void __launch_bounds__((kMaxWarps + 1) * 32, 1) warpmma_kernel(const 
   // the loop is compiled once per residue class, with every address but the slot's hoisted.
   if constexpr (QT == 6 && I8) {
     if (a.fixed_blocks) {
+      const uint32_t fkb = warp;
       auto fixed_loop = [&](auto cls) {
         constexpr int F = decltype(cls)::value;
-        const uint32_t kb = warp;
+        const uint32_t kb = fkb;
         const float u0 = ublk[kb];
         const uint32_t tkb = table_s + (kb * 32 + 2 * c) * 24;
         const uint32_t bA = g == c ? tkb : zero_s;
@@ -871,7 +886,7 @@ __global__ void __launch_bounds__((kMaxWarps + 1) * 32, 1) warpmma_kernel(const 
                 lds16_class<F>(base + 64 * hf + 16 * c, L[r]);
                 lds16_class<F>(base + 128 + 32 * hf + 16 * (c & 1), Q[r]);
               }
-              q6i8_half(hf, L, Q, ag, ah, c, mkb, bA, bB, kLo, k28, sHi, dg, dh, yacc);
+              q6i8_half(hf, L, Q, ag, ah, c, mkb, bA, bB, k16, k28, sHi, dg, dh, yacc);
             }
           }
           __syncwarp();
@@ -883,7 +898,7 @@ __global__ void __launch_bounds__((kMaxWarps + 1) * 32, 1) warpmma_kernel(const 
           band_end(band, bi);
         }
       };
-      switch (residue_class(warp * kBlk)) {
+      switch (residue_class(fkb * kBlk)) {
         case 16: fixed_loop(std::integral_constant<int, 16>()); break;
         case 8: fixed_loop(std::integral_constant<int, 8>()); break;
         case 4: fixed_loop(std::integral_constant<int, 4>()); break;
@@ -998,7 +1013,7 @@ __global__ void __launch_bounds__((kMaxWarps + 1) * 32, 1) warpmma_kernel(const 
           // accumulator start values: entries ((kb * 2 + hf) * 3 + l) * 8 + 2c, 4 bytes each
           const uint32_t mkb = mtable_s + (kb * 48 + 2 * c) * 4;
           auto half = [&](uint32_t hf, const uint32_t (&L)[2][4], const uint32_t (&Q)[2][4]) {
-            q6i8_half(hf, L, Q, ag, ah, c, mkb, bA, bB, kLo, k28, sHi, dg, dh, yacc);
+            q6i8_half(hf, L, Q, ag, ah, c, mkb, bA, bB, k16, k28, sHi, dg, dh, yacc);
           };
           if constexpr (kQ6WholeBlock) {
             // both halves' quants in registers at once, so their work interleaves
