@@ -95,6 +95,7 @@ struct WarpMmaArgs {
   uint32_t table_off, mtable_off, ublk_off, zero_off, red_off, bars_off;  // shared-memory layout
   uint32_t zero;         // 0: multipliers built from it are opaque to the compiler
   uint32_t row_perm;     // 1: MMA row pairs are tile rows two apart (see pg)
+  uint32_t split_tile;   // 1: whole-row tile in two copies, rows 8..15 64 bytes further (see pg)
   uint32_t fixed_blocks; // 1: Q6_K integer path with warp w fixed to block w (whole 16-byte rows)
   uint32_t ncol;         // B columns in use per n-tile
   uint32_t fb;           // bands of partial rows kept before a flush
@@ -528,7 +529,18 @@ __global__ void __launch_bounds__((kMaxWarps + 1) * 32, 1) warpmma_kernel(const 
       __syncwarp();
       if (lane == 0) mbar_arrive_expect_tx(full_bar(s), total);
       __syncwarp();
-      if (bytes) bulk_g2s(slot + lane * a.seg_bytes, a.W + a0, bytes, full_bar(s), pol);
+      if (a.split_tile) {
+        // rows r0..r0+7 at the slot, rows r0+8.. 64 bytes past where they would follow (rows are
+        // whole and start on 16-byte boundaries here, so a1 - a0 = (r1 - r0) * RB)
+        if (lane == 0 && bytes) {
+          const uint32_t first = static_cast<uint32_t>(std::min<uint64_t>(bytes, 8 * RB));
+          bulk_g2s(slot, a.W + a0, first, full_bar(s), pol);
+          if (bytes > first)
+            bulk_g2s(slot + first + 64, a.W + a0 + first, bytes - first, full_bar(s), pol);
+        }
+      } else if (bytes) {
+        bulk_g2s(slot + lane * a.seg_bytes, a.W + a0, bytes, full_bar(s), pol);
+      }
       // (whole-row tiles: only lane 0 has bytes, and its destination is the slot itself)
       if (++s == a.ring) {
         s = 0;
@@ -772,10 +784,15 @@ __global__ void __launch_bounds__((kMaxWarps + 1) * 32, 1) warpmma_kernel(const 
   const uint32_t sHi = c >= 2 ? 2u : 0u;
   const uint32_t kT = (1u << (QT == 6 ? (c >= 2 ? 2 : 4) : 0)) << a.zero;    // << sT
   const uint32_t kT13 = (1u << (QT == 6 ? (c >= 2 ? 26 : 28) : 0)) << a.zero;  // >> (8 - sT)
-  // MMA rows g and g+8 of this thread are tile rows pg and pg+8. With whole-row tiles whose row
-  // pitch is 32 or 96 mod 128 bytes, MMA rows (0,1), (2,3), ... are tile rows (0,2), (1,3), ...,
-  // 64 bytes apart mod 128, so the two rows of a quarter-warp's 16-byte loads take disjoint banks.
-  const uint32_t pg = a.row_perm ? ((g & 4) | ((g & 1) << 1) | ((g >> 1) & 1)) : g;
+  // MMA rows g and g+8 of this thread are tile rows pg and ph (= pg + 8, or pg + 4 in a split
+  // tile). With whole-row tiles whose row pitch is 32 or 96 mod 128 bytes, MMA rows (0,1), (2,3),
+  // ... are tile rows (0,2), (1,3), ..., 64 bytes apart mod 128, so the two rows of a
+  // quarter-warp's 16-byte loads take disjoint banks. With a pitch of 0 mod 128 the tile is split
+  // (rows 8..15 stored 64 bytes further) and MMA rows (0,1), (2,3), ... are tile rows (0,8),
+  // (1,9), ... for g < 8 and (4,12), (5,13), ... for g + 8.
+  const uint32_t pg = a.split_tile ? ((g & 1) * 8 + (g >> 1))
+                                   : a.row_perm ? ((g & 4) | ((g & 1) << 1) | ((g >> 1) & 1)) : g;
+  const uint32_t ph = a.split_tile ? pg + 4 : pg + 8;
   // the vectors whose outputs this thread accumulates (Q4_K: c, or 2c and 2c+1; Q6_K: 0)
   const uint32_t vb0 = QT == 6 ? 0u : ((HILO && NT == 1) ? c : 2 * c);
   const uint32_t vb1 = min(vb0 + 1, B - 1);
@@ -786,7 +803,9 @@ __global__ void __launch_bounds__((kMaxWarps + 1) * 32, 1) warpmma_kernel(const 
   // kq + (kt < kr) super-blocks (the producer splits the same way).
   const uint32_t nkt = a.nkt, kq = a.nb / nkt, kr = a.nb % nkt;
   const uint32_t rb32 = static_cast<uint32_t>(RB);
-  const uint32_t pg_rb = pg * rb32;
+  // byte offsets of tile rows pg and ph in a whole-row slot
+  const uint32_t pg_rb = pg * rb32 + (a.split_tile && pg >= 8 ? 64u : 0u);
+  const uint32_t ph_rb = ph * rb32 + (a.split_tile && ph >= 8 ? 64u : 0u);
   // When every row starts on a 16-byte boundary, a block's offset within 16 bytes is the same
   // for all rows of a warp: (kb * block bytes) mod 16.
   const bool rows16 = (rb32 & 15u) == 0;
@@ -802,7 +821,7 @@ __global__ void __launch_bounds__((kMaxWarps + 1) * 32, 1) warpmma_kernel(const 
       }
       if (c == 0) {
         red[((bi * kTileRows + pg) * nw + warp) * B] = yacc[0][0];
-        red[((bi * kTileRows + pg + 8) * nw + warp) * B] = yacc[1][0];
+        red[((bi * kTileRows + ph) * nw + warp) * B] = yacc[1][0];
       }
     } else {
 #pragma unroll
@@ -810,7 +829,7 @@ __global__ void __launch_bounds__((kMaxWarps + 1) * 32, 1) warpmma_kernel(const 
         const uint32_t b = (HILO && NT == 1) ? (j == 0 ? c : 8u) : 2 * c + j;
         if (b < B) {
           red[((bi * kTileRows + pg) * nw + warp) * B + b] = yacc[0][j];
-          red[((bi * kTileRows + pg + 8) * nw + warp) * B + b] = yacc[1][j];
+          red[((bi * kTileRows + ph) * nw + warp) * B + b] = yacc[1][j];
         }
       }
     }
@@ -865,7 +884,7 @@ __global__ void __launch_bounds__((kMaxWarps + 1) * 32, 1) warpmma_kernel(const 
         const uint32_t bB = g == c + 4 ? tkb + 8 * 24 : zero_s;
         const uint32_t mkb = mtable_s + (kb * 48 + 2 * c) * 4;
         const uint32_t rb32 = static_cast<uint32_t>(RB);
-        const uint32_t off_g = pg * rb32 + kb * kBlk;
+        const uint32_t off_g = pg_rb + kb * kBlk, off_h = ph_rb + kb * kBlk;
         uint32_t s = 0, phase = 0, bi = 0;
         for (uint32_t band = 0; band < nbands; ++band) {
           bool ok = !*reinterpret_cast<volatile int*>(&s_failed);
@@ -875,7 +894,8 @@ __global__ void __launch_bounds__((kMaxWarps + 1) * 32, 1) warpmma_kernel(const 
             report_error(a.err, kErrWaitFull);
           }
           if (!__any_sync(0xffffffffu, !ok)) {
-            const uint32_t ag = ring_s + s * a.slot_bytes + off_g, ah = ag + 8 * rb32;
+            const uint32_t ag = ring_s + s * a.slot_bytes + off_g;
+            const uint32_t ah = ring_s + s * a.slot_bytes + off_h;
             const float dg = u0 * h2f(lds_u16(ag + 208)), dh = u0 * h2f(lds_u16(ah + 208));
 #pragma unroll 1
             for (uint32_t hf = 0; hf < 2; ++hf) {
@@ -935,11 +955,11 @@ __global__ void __launch_bounds__((kMaxWarps + 1) * 32, 1) warpmma_kernel(const 
         // whole rows back to back from the tile's aligned start
         const uint32_t delta = (r0 * rb32) & 15u;
         ag = slot + delta + pg_rb + j * kBlk;
-        ah = ag + 8 * rb32;
+        ah = slot + delta + ph_rb + j * kBlk;
       } else {
         const uint32_t off = kc0 * kBlk;
         ag = slot + pg * a.seg_bytes + (((r0 + pg) * rb32 + off) & 15u) + j * kBlk;
-        ah = slot + (pg + 8) * a.seg_bytes + (((r0 + pg + 8) * rb32 + off) & 15u) + j * kBlk;
+        ah = slot + ph * a.seg_bytes + (((r0 + ph) * rb32 + off) & 15u) + j * kBlk;
       }
       // the offset within 16 bytes that every lane's block shares, or 16 when they differ
       const uint32_t o16 = rows16 ? ((kb * kBlk) & 15u) : 16u;
@@ -1242,10 +1262,13 @@ int warpmma_matvec(kq_ctx* ctx, const kq_matvec_desc& d, uint64_t ldx, uint64_t 
   uint32_t slot = slot_for(nwc, seg);
   // A tile of whole rows goes in one copy (the copy engine's cost is per copy, ~75 ns per SM,
   // so many small copies cap the bandwidth), its rows back to back.
+  // Rows on a pitch of 0 mod 128 would put a quarter-warp's two rows on the same banks: such a
+  // tile goes in two copies, its rows 8..15 64 bytes further (see pg in the kernel).
+  const bool split = rb % 128 == 0;
   auto whole_rows = [&]() {
     if (nkt != 1) return;
     seg = 0;
-    slot = static_cast<uint32_t>(((uint64_t(kTileRows) * rb + 32 + 127) / 128) * 128);
+    slot = static_cast<uint32_t>(((uint64_t(kTileRows) * rb + 32 + (split ? 64 : 0) + 127) / 128) * 128);
   };
   whole_rows();
 
@@ -1347,6 +1370,7 @@ int warpmma_matvec(kq_ctx* ctx, const kq_matvec_desc& d, uint64_t ldx, uint64_t 
   args.red_off = args.zero_off + kZeroBytes;
   args.zero = 0;
   args.row_perm = row_perm;
+  args.split_tile = (seg == 0 && split) ? 1u : 0u;
   args.fixed_blocks = (mode == 5 && nkt == 1 && seg == 0 && rows16 && nw == nwc) ? 1u : 0u;
   args.bars_off = args.red_off + red_bytes;
   args.ncol = ncol;
