@@ -67,7 +67,10 @@ constexpr uint32_t kRedBudget = 16384;  // bytes of shared memory for partial ro
 constexpr uint32_t kNStride = 16 * 32 + 32;
 // Q6_K integer path: load a whole super-block's quants before the MMAs (else half by half).
 constexpr bool kQ6WholeBlock = false;
-constexpr uint32_t kZeroBytes = 1024 + 64;  // covers every MMA offset of one block's fragments
+constexpr uint32_t kZeroBytes = 1024 + 64;
+// The gap before rows 8..15 of a split tile: a Q4_K thread reads 16 bytes at 32-byte strides
+// (16 + 32c), which fill half the banks; a row 16 bytes (mod 32) further fills the other half.
+constexpr uint32_t kSplitGap = 16;  // covers every MMA offset of one block's fragments
 
 // A descriptor flag bit outside the public KQ_FLAG_* set: batch 1 on the other of the two
 // warp-MMA variants (Q4_K: integer instead of f16 operands, Q6_K: f16 instead of integer), so
@@ -95,7 +98,7 @@ struct WarpMmaArgs {
   uint32_t table_off, mtable_off, ublk_off, zero_off, red_off, bars_off;  // shared-memory layout
   uint32_t zero;         // 0: multipliers built from it are opaque to the compiler
   uint32_t row_perm;     // 1: MMA row pairs are tile rows two apart (see pg)
-  uint32_t split_tile;   // 1: whole-row tile in two copies, rows 8..15 64 bytes further (see pg)
+  uint32_t split_tile;   // 1: whole-row tile in two copies, rows 8..15 kSplitGap bytes further
   uint32_t fixed_blocks; // 1: Q6_K integer path with warp w fixed to block w (whole 16-byte rows)
   uint32_t ncol;         // B columns in use per n-tile
   uint32_t fb;           // bands of partial rows kept before a flush
@@ -530,13 +533,13 @@ __global__ void __launch_bounds__((kMaxWarps + 1) * 32, 1) warpmma_kernel(const 
       if (lane == 0) mbar_arrive_expect_tx(full_bar(s), total);
       __syncwarp();
       if (a.split_tile) {
-        // rows r0..r0+7 at the slot, rows r0+8.. 64 bytes past where they would follow (rows are
-        // whole and start on 16-byte boundaries here, so a1 - a0 = (r1 - r0) * RB)
+        // rows r0..r0+7 at the slot, rows r0+8.. kSplitGap bytes past where they would follow
+        // (rows are whole and start on 16-byte boundaries here, so a1 - a0 = (r1 - r0) * RB)
         if (lane == 0 && bytes) {
           const uint32_t first = static_cast<uint32_t>(std::min<uint64_t>(bytes, 8 * RB));
           bulk_g2s(slot, a.W + a0, first, full_bar(s), pol);
           if (bytes > first)
-            bulk_g2s(slot + first + 64, a.W + a0 + first, bytes - first, full_bar(s), pol);
+            bulk_g2s(slot + first + kSplitGap, a.W + a0 + first, bytes - first, full_bar(s), pol);
         }
       } else if (bytes) {
         bulk_g2s(slot + lane * a.seg_bytes, a.W + a0, bytes, full_bar(s), pol);
@@ -788,8 +791,8 @@ __global__ void __launch_bounds__((kMaxWarps + 1) * 32, 1) warpmma_kernel(const 
   // tile). With whole-row tiles whose row pitch is 32 or 96 mod 128 bytes, MMA rows (0,1), (2,3),
   // ... are tile rows (0,2), (1,3), ..., 64 bytes apart mod 128, so the two rows of a
   // quarter-warp's 16-byte loads take disjoint banks. With a pitch of 0 mod 128 the tile is split
-  // (rows 8..15 stored 64 bytes further) and MMA rows (0,1), (2,3), ... are tile rows (0,8),
-  // (1,9), ... for g < 8 and (4,12), (5,13), ... for g + 8.
+  // (rows 8..15 stored kSplitGap bytes further) and MMA rows (0,1), (2,3), ... are tile rows
+  // (0,8), (1,9), ... for g < 8 and (4,12), (5,13), ... for g + 8.
   const uint32_t pg = a.split_tile ? ((g & 1) * 8 + (g >> 1))
                                    : a.row_perm ? ((g & 4) | ((g & 1) << 1) | ((g >> 1) & 1)) : g;
   const uint32_t ph = a.split_tile ? pg + 4 : pg + 8;
@@ -804,8 +807,8 @@ __global__ void __launch_bounds__((kMaxWarps + 1) * 32, 1) warpmma_kernel(const 
   const uint32_t nkt = a.nkt, kq = a.nb / nkt, kr = a.nb % nkt;
   const uint32_t rb32 = static_cast<uint32_t>(RB);
   // byte offsets of tile rows pg and ph in a whole-row slot
-  const uint32_t pg_rb = pg * rb32 + (a.split_tile && pg >= 8 ? 64u : 0u);
-  const uint32_t ph_rb = ph * rb32 + (a.split_tile && ph >= 8 ? 64u : 0u);
+  const uint32_t pg_rb = pg * rb32 + (a.split_tile && pg >= 8 ? kSplitGap : 0u);
+  const uint32_t ph_rb = ph * rb32 + (a.split_tile && ph >= 8 ? kSplitGap : 0u);
   // When every row starts on a 16-byte boundary, a block's offset within 16 bytes is the same
   // for all rows of a warp: (kb * block bytes) mod 16.
   const bool rows16 = (rb32 & 15u) == 0;
@@ -1263,12 +1266,12 @@ int warpmma_matvec(kq_ctx* ctx, const kq_matvec_desc& d, uint64_t ldx, uint64_t 
   // A tile of whole rows goes in one copy (the copy engine's cost is per copy, ~75 ns per SM,
   // so many small copies cap the bandwidth), its rows back to back.
   // Rows on a pitch of 0 mod 128 would put a quarter-warp's two rows on the same banks: such a
-  // tile goes in two copies, its rows 8..15 64 bytes further (see pg in the kernel).
+  // tile goes in two copies, its rows 8..15 kSplitGap bytes further (see pg in the kernel).
   const bool split = rb % 128 == 0;
   auto whole_rows = [&]() {
     if (nkt != 1) return;
     seg = 0;
-    slot = static_cast<uint32_t>(((uint64_t(kTileRows) * rb + 32 + (split ? 64 : 0) + 127) / 128) * 128);
+    slot = static_cast<uint32_t>(((uint64_t(kTileRows) * rb + 32 + (split ? kSplitGap : 0) + 127) / 128) * 128);
   };
   whole_rows();
 
