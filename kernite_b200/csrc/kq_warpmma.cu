@@ -72,11 +72,10 @@ constexpr uint32_t kZeroBytes = 1024 + 64;
 // (16 + 32c), which fill half the banks; a row 16 bytes (mod 32) further fills the other half.
 constexpr uint32_t kSplitGap = 16;  // covers every MMA offset of one block's fragments
 
-// A descriptor flag bit outside the public KQ_FLAG_* set: batch 1 on the other of the two
-// warp-MMA variants (Q4_K: integer instead of f16 operands, Q6_K: f16 instead of integer), so
-// both stay reachable for tests and A/B timing. The defaults are the faster one per type
-// (measured on B200: equal speed for Q6_K, where the integer variant's 24-bit x is the more
-// accurate; f16 7% faster for Q4_K).
+// A descriptor flag bit outside the public KQ_FLAG_* set: batch 1 on the f16 warp-MMA variant
+// instead of the integer one, so both stay reachable for tests and A/B timing. The integer
+// variant is the default for both types (measured on B200: 10% faster for Q6_K, 1% for Q4_K,
+// and its 24-bit fixed-point x is the more accurate).
 constexpr uint32_t kFlagAltBatch1 = 1u << 30;
 // Another such bit: the other choice of consumer warps (one per super-block of the widest K-tile,
 // or kMaxWarps taking turns) for A/B timing.
@@ -973,29 +972,42 @@ __global__ void __launch_bounds__((kMaxWarps + 1) * 32, 1) warpmma_kernel(const 
         // three limbs of the same 8 elements of x, read by the 4 lanes of the column's group.
         const float u0 = ublk[kb];
         if constexpr (QT == 4) {
-          // 8 steps, step s = sub-block s = qs chunk s/2, nibble s%2; thread c: bytes 8c..8c+7
+          // Thread c owns qs chunk c (sub-blocks 2c: low nibbles, 2c+1: high). 8 steps (o, i):
+          // nibble o of bytes 8i..8i+7 of the chunk, i.e. elements 64c + 32o + 8i .. +7, whose x
+          // limbs are table chunk 8c + 4o + i; the lanes of MMA column n = 2c + o read them (two
+          // bases per thread, one per nibble, constant offsets per step), the others zeros.
           int acc[3][4];
           const uint4 hg = lds_v4(ag), hh = lds_v4(ah);
+          uint32_t Wg[8], Wh[8];
+          {
+            const uint4 g0 = lds_v4(ag + 16 + 32 * c), g1 = lds_v4(ag + 32 + 32 * c);
+            const uint4 h0 = lds_v4(ah + 16 + 32 * c), h1 = lds_v4(ah + 32 + 32 * c);
+            Wg[0] = g0.x; Wg[1] = g0.y; Wg[2] = g0.z; Wg[3] = g0.w;
+            Wg[4] = g1.x; Wg[5] = g1.y; Wg[6] = g1.z; Wg[7] = g1.w;
+            Wh[0] = h0.x; Wh[1] = h0.y; Wh[2] = h0.z; Wh[3] = h0.w;
+            Wh[4] = h1.x; Wh[5] = h1.y; Wh[6] = h1.z; Wh[7] = h1.w;
+          }
+          const uint32_t tc = table_s + (kb * 32 + 8 * c) * 24;
+          const uint32_t b0 = g == 2 * c ? tc : zero_s;
+          const uint32_t b1 = g == 2 * c + 1 ? tc + 4 * 24 : zero_s;
 #pragma unroll
-          for (int l = 0; l < 3; ++l) acc[l][0] = acc[l][1] = acc[l][2] = acc[l][3] = 0;
+          for (int o = 0; o < 2; ++o)
 #pragma unroll
-          for (int q = 0; q < 4; ++q) {
-            const uint2 wg = lds_v2(ag + 16 + 32 * q + 8 * c), wh = lds_v2(ah + 16 + 32 * q + 8 * c);
-#pragma unroll
-            for (int o = 0; o < 2; ++o) {
-              const int st = 2 * q + o;
-              const uint32_t a0 = (o ? mulhi(wg.x, k28) : wg.x) & 0x0F0F0F0Fu;
-              const uint32_t a1 = (o ? mulhi(wh.x, k28) : wh.x) & 0x0F0F0F0Fu;
-              const uint32_t a2 = (o ? mulhi(wg.y, k28) : wg.y) & 0x0F0F0F0Fu;
-              const uint32_t a3 = (o ? mulhi(wh.y, k28) : wh.y) & 0x0F0F0F0Fu;
-              const uint32_t bb = g == static_cast<uint32_t>(st) ? table_s + (kb * 32 + 4 * st + c) * 24 : zero_s;
+            for (int i = 0; i < 4; ++i) {
+              const uint32_t a0 = (o ? mulhi(Wg[2 * i], k28) : Wg[2 * i]) & 0x0F0F0F0Fu;
+              const uint32_t a1 = (o ? mulhi(Wh[2 * i], k28) : Wh[2 * i]) & 0x0F0F0F0Fu;
+              const uint32_t a2 = (o ? mulhi(Wg[2 * i + 1], k28) : Wg[2 * i + 1]) & 0x0F0F0F0Fu;
+              const uint32_t a3 = (o ? mulhi(Wh[2 * i + 1], k28) : Wh[2 * i + 1]) & 0x0F0F0F0Fu;
+              const uint32_t bb = (o ? b1 : b0) + 24 * i;
 #pragma unroll
               for (int l = 0; l < 3; ++l) {
                 const uint2 bf = lds_v2(bb + 8 * l);
-                imma16832(acc[l], a0, a1, a2, a3, bf.x, bf.y);
+                if (o == 0 && i == 0)
+                  imma16832_c(acc[l], a0, a1, a2, a3, bf.x, bf.y, 0u, 0u, 0u, 0u);
+                else
+                  imma16832(acc[l], a0, a1, a2, a3, bf.x, bf.y);
               }
             }
-          }
           // scales and mins of sub-blocks 2c, 2c+1 (the thread's columns) as floats
           auto scm = [&](const uint4& hd, float& s0, float& s1, float& m0, float& m1) {
             const uint32_t ts = __byte_perm(hd.w, hd.y, sel_sc);
@@ -1287,7 +1299,7 @@ int warpmma_matvec(kq_ctx* ctx, const kq_matvec_desc& d, uint64_t ldx, uint64_t 
   // per-sub-block sums (Q6_K: the MMAs' C init, Q4_K: the min term's sums of x)
   const uint64_t i8_table = uint64_t(nb) * kQK * 3;
   const uint64_t i8_mtable = q4 ? uint64_t(nb) * 8 * 4 : uint64_t(nb) * 2 * 3 * 8 * 4;
-  const bool want_i8 = (q4 != 0) == ((d.flags & kFlagAltBatch1) != 0);
+  const bool want_i8 = (d.flags & kFlagAltBatch1) == 0;
   if (d.batch == 1 && want_i8 &&
       i8_table + i8_mtable + fixed_min <= uint64_t(ctx->max_smem)) {
     mode = q4 ? 4 : 5, ncol = 8;

@@ -2,8 +2,9 @@
 oracle, through the C ABI.
 
 The kernel splits each row into tiles of up to 16 super-blocks (one warp each) and 16 rows (the
-MMA's M), converts x into f16 hi + lo operands (hi only for Q6_K and for tables too large for
-shared memory) and sums partial rows across warps. The shapes below sweep those seams: rows that
+MMA's M), converts x into three signed byte limbs (batch 1: integer MMAs, the default) or f16
+hi + lo operands (batch 2..8, and batch 1 with the ALT_BATCH1 bit; hi only for Q6_K and for
+tables too large for shared memory) and sums partial rows across warps. The shapes below sweep those seams: rows that
 leave a partial band of 16, K that takes one, two, three or seven K-tiles (including the 43-block
 K = 11008 rows that start off 16-byte boundaries), every batch size and each x-table mode. The
 bar is the north star's: |y - y_ref| <= 1e-3 * sum_k |w_k x_k| per output, y_ref in f64; inputs
