@@ -98,7 +98,7 @@ struct WarpMmaArgs {
   uint32_t zero;         // 0: multipliers built from it are opaque to the compiler
   uint32_t row_perm;     // 1: MMA row pairs are tile rows two apart (see pg)
   uint32_t split_tile;   // 1: whole-row tile in two copies, rows 8..15 kSplitGap bytes further
-  uint32_t fixed_blocks; // 1: Q6_K integer path with warp w fixed to block w (whole 16-byte rows)
+  uint32_t fixed_blocks; // 1: integer path with warp w fixed to block w (whole 16-byte rows)
   uint32_t ncol;         // B columns in use per n-tile
   uint32_t fb;           // bands of partial rows kept before a flush
   uint32_t row_unit, prologue, epilogue, flags;
@@ -415,6 +415,70 @@ __device__ __forceinline__ void q6_block(uint32_t ag, uint32_t ah, uint32_t c, u
     yacc[0][0] += dg * fmaf(sg0, acc0[0] + acc1[0], sg1 * (acc0[1] + acc1[1]));
     yacc[1][0] += dh * fmaf(sh0, acc0[2] + acc1[2], sh1 * (acc0[3] + acc1[3]));
   }
+}
+
+// One Q4_K super-block on the integer path, rows g and g+8 of thread (g, c). Thread c owns qs
+// chunk c (sub-blocks 2c: low nibbles, 2c+1: high). 8 steps (o, i): nibble o of bytes 8i..8i+7
+// of the chunk, i.e. elements 64c + 32o + 8i .. +7, whose x limbs are table chunk 8c + 4o + i;
+// the lanes of MMA column n = 2c + o read them (b0, b1: this thread's bases for o = 0, 1, or
+// the zero region), so column n sums sub-block n. Then y += d sum sc_n D_n - dmin sum m_n X_n.
+//  sel_sc, m_lo, m_hi, sh_m: the thread's 6-bit scale/min unpack; X: the sums of x (limb units)
+//  over sub-blocks 2c, 2c+1; u0: the block's 2^-shift of x.
+__device__ __forceinline__ void q4i8_block(uint32_t ag, uint32_t ah, uint32_t c, uint32_t b0,
+                                           uint32_t b1, uint32_t k28, uint32_t sel_sc,
+                                           uint32_t m_lo, uint32_t m_hi, uint32_t sh_m, float2 X,
+                                           float u0, float (&yacc)[2][2]) {
+  int acc[3][4];
+  const uint4 hg = lds_v4(ag), hh = lds_v4(ah);
+  uint32_t Wg[8], Wh[8];
+  {
+    const uint4 g0 = lds_v4(ag + 16 + 32 * c), g1 = lds_v4(ag + 32 + 32 * c);
+    const uint4 h0 = lds_v4(ah + 16 + 32 * c), h1 = lds_v4(ah + 32 + 32 * c);
+    Wg[0] = g0.x; Wg[1] = g0.y; Wg[2] = g0.z; Wg[3] = g0.w;
+    Wg[4] = g1.x; Wg[5] = g1.y; Wg[6] = g1.z; Wg[7] = g1.w;
+    Wh[0] = h0.x; Wh[1] = h0.y; Wh[2] = h0.z; Wh[3] = h0.w;
+    Wh[4] = h1.x; Wh[5] = h1.y; Wh[6] = h1.z; Wh[7] = h1.w;
+  }
+#pragma unroll
+  for (int o = 0; o < 2; ++o)
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const uint32_t a0 = (o ? mulhi(Wg[2 * i], k28) : Wg[2 * i]) & 0x0F0F0F0Fu;
+      const uint32_t a1 = (o ? mulhi(Wh[2 * i], k28) : Wh[2 * i]) & 0x0F0F0F0Fu;
+      const uint32_t a2 = (o ? mulhi(Wg[2 * i + 1], k28) : Wg[2 * i + 1]) & 0x0F0F0F0Fu;
+      const uint32_t a3 = (o ? mulhi(Wh[2 * i + 1], k28) : Wh[2 * i + 1]) & 0x0F0F0F0Fu;
+      const uint32_t bb = (o ? b1 : b0) + 24 * i;
+#pragma unroll
+      for (int l = 0; l < 3; ++l) {
+        const uint2 bf = lds_v2(bb + 8 * l);
+        if (o == 0 && i == 0)
+          imma16832_c(acc[l], a0, a1, a2, a3, bf.x, bf.y, 0u, 0u, 0u, 0u);
+        else
+          imma16832(acc[l], a0, a1, a2, a3, bf.x, bf.y);
+      }
+    }
+  // scales and mins of sub-blocks 2c, 2c+1 (the thread's columns) as floats
+  auto scm = [&](const uint4& hd, float& s0, float& s1, float& m0, float& m1) {
+    const uint32_t ts = __byte_perm(hd.w, hd.y, sel_sc);
+    const uint32_t sc16 = (ts & m_lo) | ((ts >> 10) & m_hi);
+    const uint32_t tm = __byte_perm(hd.w, hd.z, sel_sc);
+    const uint32_t m16 = ((tm >> sh_m) & m_lo) | ((tm >> 10) & m_hi);
+    s0 = u16_to_f32<0>(sc16);
+    s1 = u16_to_f32<1>(sc16);
+    m0 = u16_to_f32<0>(m16);
+    m1 = u16_to_f32<1>(m16);
+  };
+  float sg0, sg1, mg0, mg1, sh0, sh1, mh0, mh1;
+  scm(hg, sg0, sg1, mg0, mg1);
+  scm(hh, sh0, sh1, mh0, mh1);
+  const float dg = u0 * h2f(hg.x & 0xffffu), dmg = u0 * h2f(hg.x >> 16);
+  const float dh = u0 * h2f(hh.x & 0xffffu), dmh = u0 * h2f(hh.x >> 16);
+  const float v0 = limbs_to_f32(acc[2][0], acc[1][0], acc[0][0]);
+  const float v1 = limbs_to_f32(acc[2][1], acc[1][1], acc[0][1]);
+  const float v2 = limbs_to_f32(acc[2][2], acc[1][2], acc[0][2]);
+  const float v3 = limbs_to_f32(acc[2][3], acc[1][3], acc[0][3]);
+  yacc[0][0] += dg * fmaf(sg0, v0, sg1 * v1) - dmg * fmaf(mg0, X.x, mg1 * X.y);
+  yacc[1][0] += dh * fmaf(sh0, v2, sh1 * v3) - dmh * fmaf(mh0, X.x, mh1 * X.y);
 }
 
 // ---------------------------------------------------------------- the kernel
@@ -930,6 +994,42 @@ __global__ void __launch_bounds__((kMaxWarps + 1) * 32, 1) warpmma_kernel(const 
       return;
     }
   }
+  // The same for Q4_K (144-byte blocks: every block starts on a 16-byte boundary, one loop):
+  // the block's table bases and sums of x are constants of the warp.
+  if constexpr (QT == 4 && I8) {
+    if (a.fixed_blocks) {
+      const uint32_t kb = warp;
+      const float u0 = ublk[kb];
+      const uint32_t tc = table_s + (kb * 32 + 8 * c) * 24;
+      const uint32_t b0 = g == 2 * c ? tc : zero_s;
+      const uint32_t b1 = g == 2 * c + 1 ? tc + 4 * 24 : zero_s;
+      const float2 X = *reinterpret_cast<const float2*>(
+          reinterpret_cast<const uint8_t*>(base) + a.mtable_off + (kb * 8 + 2 * c) * 4);
+      const uint32_t off_g = pg_rb + kb * kBlk, off_h = ph_rb + kb * kBlk;
+      uint32_t s = 0, phase = 0, bi = 0;
+      for (uint32_t band = 0; band < nbands; ++band) {
+        bool ok = !*reinterpret_cast<volatile int*>(&s_failed);
+        if (ok && !mbar_wait(full_bar(s), phase)) {
+          ok = false;
+          s_failed = 1;
+          report_error(a.err, kErrWaitFull);
+        }
+        if (!__any_sync(0xffffffffu, !ok)) {
+          const uint32_t slot = ring_s + s * a.slot_bytes;
+          q4i8_block(slot + off_g, slot + off_h, c, b0, b1, k28, sel_sc, m_lo, m_hi, sh_m, X, u0,
+                     yacc);
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(empty_bar(s));
+        if (++s == a.ring) {
+          s = 0;
+          phase ^= 1;
+        }
+        band_end(band, bi);
+      }
+      return;
+    }
+  }
 
   // Unit j (super-block kc0 + j) of a tile goes to warp (rot + j) mod nw, rot advancing by the
   // tile's super-block count, so the warps take turns when there are more warps than blocks.
@@ -972,66 +1072,12 @@ __global__ void __launch_bounds__((kMaxWarps + 1) * 32, 1) warpmma_kernel(const 
         // three limbs of the same 8 elements of x, read by the 4 lanes of the column's group.
         const float u0 = ublk[kb];
         if constexpr (QT == 4) {
-          // Thread c owns qs chunk c (sub-blocks 2c: low nibbles, 2c+1: high). 8 steps (o, i):
-          // nibble o of bytes 8i..8i+7 of the chunk, i.e. elements 64c + 32o + 8i .. +7, whose x
-          // limbs are table chunk 8c + 4o + i; the lanes of MMA column n = 2c + o read them (two
-          // bases per thread, one per nibble, constant offsets per step), the others zeros.
-          int acc[3][4];
-          const uint4 hg = lds_v4(ag), hh = lds_v4(ah);
-          uint32_t Wg[8], Wh[8];
-          {
-            const uint4 g0 = lds_v4(ag + 16 + 32 * c), g1 = lds_v4(ag + 32 + 32 * c);
-            const uint4 h0 = lds_v4(ah + 16 + 32 * c), h1 = lds_v4(ah + 32 + 32 * c);
-            Wg[0] = g0.x; Wg[1] = g0.y; Wg[2] = g0.z; Wg[3] = g0.w;
-            Wg[4] = g1.x; Wg[5] = g1.y; Wg[6] = g1.z; Wg[7] = g1.w;
-            Wh[0] = h0.x; Wh[1] = h0.y; Wh[2] = h0.z; Wh[3] = h0.w;
-            Wh[4] = h1.x; Wh[5] = h1.y; Wh[6] = h1.z; Wh[7] = h1.w;
-          }
           const uint32_t tc = table_s + (kb * 32 + 8 * c) * 24;
           const uint32_t b0 = g == 2 * c ? tc : zero_s;
           const uint32_t b1 = g == 2 * c + 1 ? tc + 4 * 24 : zero_s;
-#pragma unroll
-          for (int o = 0; o < 2; ++o)
-#pragma unroll
-            for (int i = 0; i < 4; ++i) {
-              const uint32_t a0 = (o ? mulhi(Wg[2 * i], k28) : Wg[2 * i]) & 0x0F0F0F0Fu;
-              const uint32_t a1 = (o ? mulhi(Wh[2 * i], k28) : Wh[2 * i]) & 0x0F0F0F0Fu;
-              const uint32_t a2 = (o ? mulhi(Wg[2 * i + 1], k28) : Wg[2 * i + 1]) & 0x0F0F0F0Fu;
-              const uint32_t a3 = (o ? mulhi(Wh[2 * i + 1], k28) : Wh[2 * i + 1]) & 0x0F0F0F0Fu;
-              const uint32_t bb = (o ? b1 : b0) + 24 * i;
-#pragma unroll
-              for (int l = 0; l < 3; ++l) {
-                const uint2 bf = lds_v2(bb + 8 * l);
-                if (o == 0 && i == 0)
-                  imma16832_c(acc[l], a0, a1, a2, a3, bf.x, bf.y, 0u, 0u, 0u, 0u);
-                else
-                  imma16832(acc[l], a0, a1, a2, a3, bf.x, bf.y);
-              }
-            }
-          // scales and mins of sub-blocks 2c, 2c+1 (the thread's columns) as floats
-          auto scm = [&](const uint4& hd, float& s0, float& s1, float& m0, float& m1) {
-            const uint32_t ts = __byte_perm(hd.w, hd.y, sel_sc);
-            const uint32_t sc16 = (ts & m_lo) | ((ts >> 10) & m_hi);
-            const uint32_t tm = __byte_perm(hd.w, hd.z, sel_sc);
-            const uint32_t m16 = ((tm >> sh_m) & m_lo) | ((tm >> 10) & m_hi);
-            s0 = u16_to_f32<0>(sc16);
-            s1 = u16_to_f32<1>(sc16);
-            m0 = u16_to_f32<0>(m16);
-            m1 = u16_to_f32<1>(m16);
-          };
-          float sg0, sg1, mg0, mg1, sh0, sh1, mh0, mh1;
-          scm(hg, sg0, sg1, mg0, mg1);
-          scm(hh, sh0, sh1, mh0, mh1);
           const float2 X = *reinterpret_cast<const float2*>(
               reinterpret_cast<const uint8_t*>(base) + a.mtable_off + (kb * 8 + 2 * c) * 4);
-          const float dg = u0 * h2f(hg.x & 0xffffu), dmg = u0 * h2f(hg.x >> 16);
-          const float dh = u0 * h2f(hh.x & 0xffffu), dmh = u0 * h2f(hh.x >> 16);
-          const float v0 = limbs_to_f32(acc[2][0], acc[1][0], acc[0][0]);
-          const float v1 = limbs_to_f32(acc[2][1], acc[1][1], acc[0][1]);
-          const float v2 = limbs_to_f32(acc[2][2], acc[1][2], acc[0][2]);
-          const float v3 = limbs_to_f32(acc[2][3], acc[1][3], acc[0][3]);
-          yacc[0][0] += dg * fmaf(sg0, v0, sg1 * v1) - dmg * fmaf(mg0, X.x, mg1 * X.y);
-          yacc[1][0] += dh * fmaf(sh0, v2, sh1 * v3) - dmh * fmaf(mh0, X.x, mh1 * X.y);
+          q4i8_block(ag, ah, c, b0, b1, k28, sel_sc, m_lo, m_hi, sh_m, X, u0, yacc);
         } else {
           // Q6_K: per half, 4 steps: s < 2 the low-nibble group (sub-block c, words 2(s&1),
           // 2(s&1)+1 of the thread's 16 ql bytes), s >= 2 the high-nibble group (sub-block c+4)
@@ -1336,12 +1382,14 @@ int warpmma_matvec(kq_ctx* ctx, const kq_matvec_desc& d, uint64_t ldx, uint64_t 
     slot = slot_for(nwc, seg);
   }
   // Consumer warps: kMaxWarps (the warps taking turns over a tile's blocks), or one per block of
-  // the widest K-tile. Measured on B200: turns are 3% faster for Q4_K up to batch 4 (more warps
-  // hide more latency), 2% slower at batch 8 (the two-tile MMAs' registers), and 3% slower for
-  // Q6_K rows on 16-byte boundaries, where a warp fixed to one block keeps one load form (the
-  // block's alignment) instead of cycling through all of them.
+  // the widest K-tile. Measured on B200: a warp fixed to one block of whole-row tiles on 16-byte
+  // boundaries runs the integer path's fixed-block loop (every per-block constant hoisted; for
+  // Q6_K one load form per block alignment): 7% faster than turns for Q4_K, 3% for Q6_K. Else
+  // turns are 3% faster for Q4_K up to batch 4 (more warps hide more latency), 2% slower at
+  // batch 8 (the two-tile MMAs' registers).
   const bool rows16 = rb % 16 == 0;
-  const bool turns = q4 ? d.batch <= 4 : !rows16;
+  const bool fixed_ok = (mode == 4 || mode == 5) && nkt == 1 && seg == 0 && rows16;
+  const bool turns = fixed_ok ? false : q4 ? d.batch <= 4 : !rows16;
   const bool per_block = !turns != ((d.flags & kFlagWarpPerBlock) != 0);
   const uint32_t nw = per_block ? nwc : kMaxWarps;
   const uint32_t rb128 = static_cast<uint32_t>(rb % 128);
@@ -1386,7 +1434,7 @@ int warpmma_matvec(kq_ctx* ctx, const kq_matvec_desc& d, uint64_t ldx, uint64_t 
   args.zero = 0;
   args.row_perm = row_perm;
   args.split_tile = (seg == 0 && split) ? 1u : 0u;
-  args.fixed_blocks = (mode == 5 && nkt == 1 && seg == 0 && rows16 && nw == nwc) ? 1u : 0u;
+  args.fixed_blocks = (fixed_ok && nw == nwc) ? 1u : 0u;
   args.bars_off = args.red_off + red_bytes;
   args.ncol = ncol;
   args.fb = fb;
