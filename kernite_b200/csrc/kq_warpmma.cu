@@ -875,6 +875,103 @@ __global__ void __launch_bounds__((kMaxWarps + 1) * 32, 1) warpmma_kernel(const 
   // When every row starts on a 16-byte boundary, a block's offset within 16 bytes is the same
   // for all rows of a warp: (kb * block bytes) mod 16.
   const bool rows16 = (rb32 & 15u) == 0;
+  // One Q4_K super-block on the f16 path (rows g and g+8 of the tile at ag, ah): tab_t, bm_at:
+  // this thread's B-fragment and min-term addresses of the block (or the zero region); u0, u1:
+  // the block's 2^-shift of x for the thread's vectors.
+  auto q4f16_block = [&](uint32_t ag, uint32_t ah, const uint32_t (&tab_t)[NT],
+                         const uint32_t (&bm_at)[NT], float u0, float u1) {
+    const uint4 hg = lds_v4(ag), hh = lds_v4(ah);
+    const uint4 qg0 = lds_v4(ag + 16 + 32 * c), qg1 = lds_v4(ag + 32 + 32 * c);
+    const uint4 qh0 = lds_v4(ah + 16 + 32 * c), qh1 = lds_v4(ah + 32 + 32 * c);
+    // scales -> S = (sc_lo, sc_hi/16), Z = (-1024 sc_lo, -64 sc_hi), their swaps, mins
+    uint32_t Sg, Zg, S2g, Z2g, Amg, Sh, Zh, S2h, Z2h, Amh;
+    auto prep = [&](const uint4& hd, uint32_t& S, uint32_t& Z, uint32_t& S2, uint32_t& Z2,
+                    uint32_t& Am) {
+      const uint32_t ts = __byte_perm(hd.w, hd.y, sel_sc);
+      const uint32_t M = lop_and_or(ts, m_lo, lop_and_or(ts >> 10, m_hi, kMagic));
+      S = hfma2(M, f16x2_const(kH1, kH16th), f16x2_const(kHm1024, kHm64));
+      Z = hmul2(S, f16x2_const(kHm1024, kHm1024));
+      S2 = __byte_perm(S, 0, 0x1032);
+      Z2 = __byte_perm(Z, 0, 0x1032);
+      const uint32_t tm = __byte_perm(hd.w, hd.z, sel_sc);
+      const uint32_t Mm = lop_and_or(tm >> sh_m, m_lo, lop_and_or(tm >> 10, m_hi, kMagic));
+      Am = hadd2(Mm, f16x2_const(kHm1024, kHm1024));
+    };
+    prep(hg, Sg, Zg, S2g, Z2g, Amg);
+    prep(hh, Sh, Zh, S2h, Z2h, Amh);
+    const uint32_t qg[8] = {qg0.x, qg0.y, qg0.z, qg0.w, qg1.x, qg1.y, qg1.z, qg1.w};
+    const uint32_t qh[8] = {qh0.x, qh0.y, qh0.z, qh0.w, qh1.x, qh1.y, qh1.z, qh1.w};
+    float acc0[NT][4], acc1[NT][4], accm[NT][4];
+#pragma unroll
+    for (int tt = 0; tt < NT; ++tt)
+#pragma unroll
+      for (int j = 0; j < 4; ++j) acc0[tt][j] = acc1[tt][j] = accm[tt][j] = 0.f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+#pragma unroll
+      for (int o = 0; o < 2; ++o) {
+        const uint32_t wg = o ? mulhi(qg[i], k24) : qg[i];
+        const uint32_t wh = o ? mulhi(qh[i], k24) : qh[i];
+        const uint32_t a0 = hfma2(lop_and_or(wg, 0x00F0000Fu, kMagic), Sg, Zg);
+        const uint32_t a1 = hfma2(lop_and_or(wh, 0x00F0000Fu, kMagic), Sh, Zh);
+        const uint32_t a2 = hfma2(lop_and_or(wg, 0x000F00F0u, kMagic), S2g, Z2g);
+        const uint32_t a3 = hfma2(lop_and_or(wh, 0x000F00F0u, kMagic), S2h, Z2h);
+        const uint32_t m = 2 * i + o;
+#pragma unroll
+        for (int tt = 0; tt < NT; ++tt) {
+          const uint2 bf = lds_v2(tab_t[tt] + 32 * m);
+          if (o == 0)
+            mma16816(acc0[tt], a0, a1, a2, a3, bf.x, bf.y);
+          else
+            mma16816(acc1[tt], a0, a1, a2, a3, bf.x, bf.y);
+        }
+      }
+    }
+    // the min term: A = (m_2c, m_2c+1) in slots 2c, 2c+1 of rows g, g+8
+#pragma unroll
+    for (int tt = 0; tt < NT; ++tt) {
+      const uint32_t bm = lds_u32(bm_at[tt]);
+      mma16816(accm[tt], Amg, Amh, 0u, 0u, bm, 0u);
+    }
+    const float dg = h2f(hg.x & 0xffffu), dmg = h2f(hg.x >> 16);
+    const float dh = h2f(hh.x & 0xffffu), dmh = h2f(hh.x >> 16);
+    if constexpr (HILO && NT == 1) {
+      // columns 2c (hi) and 2c+1 (lo) are vector c
+      const float Dg = (acc0[0][0] + acc1[0][0]) + (acc0[0][1] + acc1[0][1]);
+      const float Dh = (acc0[0][2] + acc1[0][2]) + (acc0[0][3] + acc1[0][3]);
+      yacc[0][0] += u0 * (dg * Dg - dmg * (accm[0][0] + accm[0][1]));
+      yacc[1][0] += u0 * (dh * Dh - dmh * (accm[0][2] + accm[0][3]));
+    } else if constexpr (HILO) {
+      // tile 0 hi, tile 1 lo; columns 2c, 2c+1 are vectors 2c, 2c+1
+#pragma unroll
+      for (int j = 0; j < 2; ++j) {
+        const float uj = j ? u1 : u0;
+        const float Dg = (acc0[0][j] + acc1[0][j]) + (acc0[1][j] + acc1[1][j]);
+        const float Dh = (acc0[0][2 + j] + acc1[0][2 + j]) + (acc0[1][2 + j] + acc1[1][2 + j]);
+        yacc[0][j] += uj * (dg * Dg - dmg * (accm[0][j] + accm[1][j]));
+        yacc[1][j] += uj * (dh * Dh - dmh * (accm[0][2 + j] + accm[1][2 + j]));
+      }
+    } else {
+#pragma unroll
+      for (int j = 0; j < 2; ++j) {
+        const float uj = j ? u1 : u0;
+        yacc[0][j] += uj * (dg * (acc0[0][j] + acc1[0][j]) - dmg * accm[0][j]);
+        yacc[1][j] += uj * (dh * (acc0[0][2 + j] + acc1[0][2 + j]) - dmh * accm[0][2 + j]);
+      }
+    }
+  };
+  // per-block constants of the f16 path
+  auto q4f16_consts = [&](uint32_t kb, uint32_t (&tab_t)[NT], uint32_t (&bm_at)[NT], float& u0,
+                          float& u1) {
+#pragma unroll
+    for (int tt = 0; tt < NT; ++tt) {
+      tab_t[tt] = tab_on ? table_s + (kb * NT + tt) * a.ncol * kNStride + tab_lane : zero_s;
+      bm_at[tt] = tab_on ? mtable_s + ((kb * NT + tt) * a.ncol + g) * 16 + 4 * c : zero_s;
+    }
+    u0 = ublk[vb0c * a.nb + kb];
+    u1 = ublk[vb1 * a.nb + kb];
+  };
+
   // The band is done: this warp's partial rows go to the reduction buffer; every fb bands (and
   // after the last) the warps meet and sum them in a fixed order into y.
   auto band_end = [&](uint32_t band, uint32_t& bi) {
@@ -949,7 +1046,6 @@ __global__ void __launch_bounds__((kMaxWarps + 1) * 32, 1) warpmma_kernel(const 
         const uint32_t bA = g == c ? tkb : zero_s;
         const uint32_t bB = g == c + 4 ? tkb + 8 * 24 : zero_s;
         const uint32_t mkb = mtable_s + (kb * 48 + 2 * c) * 4;
-        const uint32_t rb32 = static_cast<uint32_t>(RB);
         const uint32_t off_g = pg_rb + kb * kBlk, off_h = ph_rb + kb * kBlk;
         uint32_t s = 0, phase = 0, bi = 0;
         for (uint32_t band = 0; band < nbands; ++band) {
@@ -995,16 +1091,23 @@ __global__ void __launch_bounds__((kMaxWarps + 1) * 32, 1) warpmma_kernel(const 
     }
   }
   // The same for Q4_K (144-byte blocks: every block starts on a 16-byte boundary, one loop):
-  // the block's table bases and sums of x are constants of the warp.
-  if constexpr (QT == 4 && I8) {
+  // the block's table addresses, scale of x and (integer path) sums of x are warp constants.
+  if constexpr (QT == 4) {
     if (a.fixed_blocks) {
       const uint32_t kb = warp;
-      const float u0 = ublk[kb];
-      const uint32_t tc = table_s + (kb * 32 + 8 * c) * 24;
-      const uint32_t b0 = g == 2 * c ? tc : zero_s;
-      const uint32_t b1 = g == 2 * c + 1 ? tc + 4 * 24 : zero_s;
-      const float2 X = *reinterpret_cast<const float2*>(
-          reinterpret_cast<const uint8_t*>(base) + a.mtable_off + (kb * 8 + 2 * c) * 4);
+      float u0, u1 = 0.f;
+      uint32_t b0 = 0, b1 = 0, tab_t[NT], bm_at[NT];
+      float2 X = make_float2(0.f, 0.f);
+      if constexpr (I8) {
+        u0 = ublk[kb];
+        const uint32_t tc = table_s + (kb * 32 + 8 * c) * 24;
+        b0 = g == 2 * c ? tc : zero_s;
+        b1 = g == 2 * c + 1 ? tc + 4 * 24 : zero_s;
+        X = *reinterpret_cast<const float2*>(reinterpret_cast<const uint8_t*>(base) +
+                                             a.mtable_off + (kb * 8 + 2 * c) * 4);
+      } else {
+        q4f16_consts(kb, tab_t, bm_at, u0, u1);
+      }
       const uint32_t off_g = pg_rb + kb * kBlk, off_h = ph_rb + kb * kBlk;
       uint32_t s = 0, phase = 0, bi = 0;
       for (uint32_t band = 0; band < nbands; ++band) {
@@ -1016,8 +1119,11 @@ __global__ void __launch_bounds__((kMaxWarps + 1) * 32, 1) warpmma_kernel(const 
         }
         if (!__any_sync(0xffffffffu, !ok)) {
           const uint32_t slot = ring_s + s * a.slot_bytes;
-          q4i8_block(slot + off_g, slot + off_h, c, b0, b1, k28, sel_sc, m_lo, m_hi, sh_m, X, u0,
-                     yacc);
+          if constexpr (I8)
+            q4i8_block(slot + off_g, slot + off_h, c, b0, b1, k28, sel_sc, m_lo, m_hi, sh_m, X, u0,
+                       yacc);
+          else
+            q4f16_block(slot + off_g, slot + off_h, tab_t, bm_at, u0, u1);
         }
         __syncwarp();
         if (lane == 0) mbar_arrive(empty_bar(s));
@@ -1142,91 +1248,10 @@ __global__ void __launch_bounds__((kMaxWarps + 1) * 32, 1) warpmma_kernel(const 
           }
         }
       } else if constexpr (QT == 4) {
-        const uint4 hg = lds_v4(ag), hh = lds_v4(ah);
-        const uint4 qg0 = lds_v4(ag + 16 + 32 * c), qg1 = lds_v4(ag + 32 + 32 * c);
-        const uint4 qh0 = lds_v4(ah + 16 + 32 * c), qh1 = lds_v4(ah + 32 + 32 * c);
-        // scales -> S = (sc_lo, sc_hi/16), Z = (-1024 sc_lo, -64 sc_hi), their swaps, mins
-        uint32_t Sg, Zg, S2g, Z2g, Amg, Sh, Zh, S2h, Z2h, Amh;
-        auto prep = [&](const uint4& hd, uint32_t& S, uint32_t& Z, uint32_t& S2, uint32_t& Z2,
-                        uint32_t& Am) {
-          const uint32_t ts = __byte_perm(hd.w, hd.y, sel_sc);
-          const uint32_t M = lop_and_or(ts, m_lo, lop_and_or(ts >> 10, m_hi, kMagic));
-          S = hfma2(M, f16x2_const(kH1, kH16th), f16x2_const(kHm1024, kHm64));
-          Z = hmul2(S, f16x2_const(kHm1024, kHm1024));
-          S2 = __byte_perm(S, 0, 0x1032);
-          Z2 = __byte_perm(Z, 0, 0x1032);
-          const uint32_t tm = __byte_perm(hd.w, hd.z, sel_sc);
-          const uint32_t Mm = lop_and_or(tm >> sh_m, m_lo, lop_and_or(tm >> 10, m_hi, kMagic));
-          Am = hadd2(Mm, f16x2_const(kHm1024, kHm1024));
-        };
-        prep(hg, Sg, Zg, S2g, Z2g, Amg);
-        prep(hh, Sh, Zh, S2h, Z2h, Amh);
-        const uint32_t qg[8] = {qg0.x, qg0.y, qg0.z, qg0.w, qg1.x, qg1.y, qg1.z, qg1.w};
-        const uint32_t qh[8] = {qh0.x, qh0.y, qh0.z, qh0.w, qh1.x, qh1.y, qh1.z, qh1.w};
-        float acc0[NT][4], acc1[NT][4], accm[NT][4];
-#pragma unroll
-        for (int tt = 0; tt < NT; ++tt)
-#pragma unroll
-          for (int j = 0; j < 4; ++j) acc0[tt][j] = acc1[tt][j] = accm[tt][j] = 0.f;
-        uint32_t tab_t[NT];
-#pragma unroll
-        for (int tt = 0; tt < NT; ++tt)
-          tab_t[tt] = tab_on ? table_s + (kb * NT + tt) * a.ncol * kNStride + tab_lane : zero_s;
-#pragma unroll
-        for (int i = 0; i < 8; ++i) {
-#pragma unroll
-          for (int o = 0; o < 2; ++o) {
-            const uint32_t wg = o ? mulhi(qg[i], k24) : qg[i];
-            const uint32_t wh = o ? mulhi(qh[i], k24) : qh[i];
-            const uint32_t a0 = hfma2(lop_and_or(wg, 0x00F0000Fu, kMagic), Sg, Zg);
-            const uint32_t a1 = hfma2(lop_and_or(wh, 0x00F0000Fu, kMagic), Sh, Zh);
-            const uint32_t a2 = hfma2(lop_and_or(wg, 0x000F00F0u, kMagic), S2g, Z2g);
-            const uint32_t a3 = hfma2(lop_and_or(wh, 0x000F00F0u, kMagic), S2h, Z2h);
-            const uint32_t m = 2 * i + o;
-#pragma unroll
-            for (int tt = 0; tt < NT; ++tt) {
-              const uint2 bf = lds_v2(tab_t[tt] + 32 * m);
-              if (o == 0)
-                mma16816(acc0[tt], a0, a1, a2, a3, bf.x, bf.y);
-              else
-                mma16816(acc1[tt], a0, a1, a2, a3, bf.x, bf.y);
-            }
-          }
-        }
-        // the min term: A = (m_2c, m_2c+1) in slots 2c, 2c+1 of rows g, g+8
-#pragma unroll
-        for (int tt = 0; tt < NT; ++tt) {
-          const uint32_t bm =
-              lds_u32(tab_on ? mtable_s + ((kb * NT + tt) * a.ncol + g) * 16 + 4 * c : zero_s);
-          mma16816(accm[tt], Amg, Amh, 0u, 0u, bm, 0u);
-        }
-        const float dg = h2f(hg.x & 0xffffu), dmg = h2f(hg.x >> 16);
-        const float dh = h2f(hh.x & 0xffffu), dmh = h2f(hh.x >> 16);
-        const float u0 = ublk[vb0c * a.nb + kb], u1 = ublk[vb1 * a.nb + kb];
-        if constexpr (HILO && NT == 1) {
-          // columns 2c (hi) and 2c+1 (lo) are vector c
-          const float Dg = (acc0[0][0] + acc1[0][0]) + (acc0[0][1] + acc1[0][1]);
-          const float Dh = (acc0[0][2] + acc1[0][2]) + (acc0[0][3] + acc1[0][3]);
-          yacc[0][0] += u0 * (dg * Dg - dmg * (accm[0][0] + accm[0][1]));
-          yacc[1][0] += u0 * (dh * Dh - dmh * (accm[0][2] + accm[0][3]));
-        } else if constexpr (HILO) {
-          // tile 0 hi, tile 1 lo; columns 2c, 2c+1 are vectors 2c, 2c+1
-#pragma unroll
-          for (int j = 0; j < 2; ++j) {
-            const float uj = j ? u1 : u0;
-            const float Dg = (acc0[0][j] + acc1[0][j]) + (acc0[1][j] + acc1[1][j]);
-            const float Dh = (acc0[0][2 + j] + acc1[0][2 + j]) + (acc0[1][2 + j] + acc1[1][2 + j]);
-            yacc[0][j] += uj * (dg * Dg - dmg * (accm[0][j] + accm[1][j]));
-            yacc[1][j] += uj * (dh * Dh - dmh * (accm[0][2 + j] + accm[1][2 + j]));
-          }
-        } else {
-#pragma unroll
-          for (int j = 0; j < 2; ++j) {
-            const float uj = j ? u1 : u0;
-            yacc[0][j] += uj * (dg * (acc0[0][j] + acc1[0][j]) - dmg * accm[0][j]);
-            yacc[1][j] += uj * (dh * (acc0[0][2 + j] + acc1[0][2 + j]) - dmh * accm[0][2 + j]);
-          }
-        }
+        uint32_t tab_t[NT], bm_at[NT];
+        float u0, u1;
+        q4f16_consts(kb, tab_t, bm_at, u0, u1);
+        q4f16_block(ag, ah, tab_t, bm_at, u0, u1);
       } else {
         // Q6_K, batch 1: thread (g, c) owns sub-blocks c and c+4 of each half of the block
         const float u0 = ublk[kb];
@@ -1388,7 +1413,7 @@ int warpmma_matvec(kq_ctx* ctx, const kq_matvec_desc& d, uint64_t ldx, uint64_t 
   // turns are 3% faster for Q4_K up to batch 4 (more warps hide more latency), 2% slower at
   // batch 8 (the two-tile MMAs' registers).
   const bool rows16 = rb % 16 == 0;
-  const bool fixed_ok = (mode == 4 || mode == 5) && nkt == 1 && seg == 0 && rows16;
+  const bool fixed_ok = (q4 || mode == 5) && nkt == 1 && seg == 0 && rows16;
   const bool turns = fixed_ok ? false : q4 ? d.batch <= 4 : !rows16;
   const bool per_block = !turns != ((d.flags & kFlagWarpPerBlock) != 0);
   const uint32_t nw = per_block ? nwc : kMaxWarps;
