@@ -65,8 +65,6 @@ constexpr uint32_t kRedBudget = 16384;  // bytes of shared memory for partial ro
 // Q4_K table: bytes per (block, n-tile, column): 16 MMAs x 4 threads x 8 bytes, plus 32 bytes
 // of padding so that the columns' rows start on different banks.
 constexpr uint32_t kNStride = 16 * 32 + 32;
-// Q6_K integer path: load a whole super-block's quants before the MMAs (else half by half).
-constexpr bool kQ6WholeBlock = false;
 constexpr uint32_t kZeroBytes = 1024 + 64;
 // The gap before rows 8..15 of a split tile: a Q4_K thread reads 16 bytes at 32-byte strides
 // (16 + 32c), which fill half the banks; a row 16 bytes (mod 32) further fills the other half.
@@ -1202,49 +1200,26 @@ __global__ void __launch_bounds__((kMaxWarps + 1) * 32, 1) warpmma_kernel(const 
           auto half = [&](uint32_t hf, const uint32_t (&L)[2][4], const uint32_t (&Q)[2][4]) {
             q6i8_half(hf, L, Q, ag, ah, c, mkb, bA, bB, k16, k28, sHi, dg, dh, yacc);
           };
-          if constexpr (kQ6WholeBlock) {
-            // both halves' quants in registers at once, so their work interleaves
-            uint32_t L[2][2][4], Q[2][2][4];
-            if (!same)
-              q6_load<-2>(ag, ah, c, 0, L, Q);
-            else if (o0 == 0)
-              q6_load<-1>(ag, ah, c, fs, L, Q);
-            else if (o0 == 8)
-              q6_load<8>(ag, ah, c, fs, L, Q);
-            else if ((o0 & 3u) == 0)
-              q6_load<4>(ag, ah, c, fs, L, Q);
-            else if (o0 < 4)
-              q6_load<0>(ag, ah, c, fs, L, Q);
-            else if (o0 < 8)
-              q6_load<1>(ag, ah, c, fs, L, Q);
-            else if (o0 < 12)
-              q6_load<2>(ag, ah, c, fs, L, Q);
-            else
-              q6_load<3>(ag, ah, c, fs, L, Q);
-            half(0, L[0], Q[0]);
-            half(1, L[1], Q[1]);
-          } else {
 #pragma unroll 1
-            for (uint32_t hf = 0; hf < 2; ++hf) {
-              uint32_t L[2][4], Q[2][4];
-              if (!same)
-                q6_load_half<-2>(ag, ah, c, hf, 0, L, Q);
-              else if (o0 == 0)
-                q6_load_half<-1>(ag, ah, c, hf, fs, L, Q);
-              else if (o0 == 8)
-                q6_load_half<8>(ag, ah, c, hf, fs, L, Q);
-              else if ((o0 & 3u) == 0)
-                q6_load_half<4>(ag, ah, c, hf, fs, L, Q);
-              else if (o0 < 4)
-                q6_load_half<0>(ag, ah, c, hf, fs, L, Q);
-              else if (o0 < 8)
-                q6_load_half<1>(ag, ah, c, hf, fs, L, Q);
-              else if (o0 < 12)
-                q6_load_half<2>(ag, ah, c, hf, fs, L, Q);
-              else
-                q6_load_half<3>(ag, ah, c, hf, fs, L, Q);
-              half(hf, L, Q);
-            }
+          for (uint32_t hf = 0; hf < 2; ++hf) {
+            uint32_t L[2][4], Q[2][4];
+            if (!same)
+              q6_load_half<-2>(ag, ah, c, hf, 0, L, Q);
+            else if (o0 == 0)
+              q6_load_half<-1>(ag, ah, c, hf, fs, L, Q);
+            else if (o0 == 8)
+              q6_load_half<8>(ag, ah, c, hf, fs, L, Q);
+            else if ((o0 & 3u) == 0)
+              q6_load_half<4>(ag, ah, c, hf, fs, L, Q);
+            else if (o0 < 4)
+              q6_load_half<0>(ag, ah, c, hf, fs, L, Q);
+            else if (o0 < 8)
+              q6_load_half<1>(ag, ah, c, hf, fs, L, Q);
+            else if (o0 < 12)
+              q6_load_half<2>(ag, ah, c, hf, fs, L, Q);
+            else
+              q6_load_half<3>(ag, ah, c, hf, fs, L, Q);
+            half(hf, L, Q);
           }
         }
       } else if constexpr (QT == 4) {
