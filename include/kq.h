@@ -153,6 +153,33 @@ int kq_fill_q6k(kq_ctx* ctx, uint64_t w, uint64_t block0, uint64_t nblocks, uint
 /* The stream key of tensor `tensor` under `seed` (host function; the same as the oracle's). */
 uint64_t kq_stream_key(uint64_t seed, uint64_t tensor);
 
+/* ---- GGUF model files (host only: no GPU, no context) ---------------------------------------
+ * The GGML project's model file format, the on-disk source of k-quant weights (kernite has no
+ * file loader; this is the data format on the input side of kq_matvec). A GGUF tensor stores a
+ * matrix exactly as kq_matvec takes it: dims[0] = k elements per row, dims[1] = rows, rows back
+ * to back; its `type` is the GGML type number, KQ_TYPE_Q4_K / KQ_TYPE_Q6_K for the two this
+ * library multiplies. kq_gguf_open maps the file read-only and checks every length in it
+ * against the file's size (a malformed file is KQ_E_INVALID with the reason, never a crash);
+ * tensor data are read in place, valid until kq_gguf_close. GGUF versions 2 and 3. */
+typedef struct kq_gguf kq_gguf;
+typedef struct kq_gguf_tensor {
+    const char* name;   /* NUL-terminated, owned by the kq_gguf */
+    uint32_t type;      /* GGML type number */
+    uint32_t n_dims;    /* 1..4 */
+    uint64_t dims[4];   /* dims[0] innermost (elements per row); unused ones are 1 */
+    uint64_t offset;    /* byte offset of the data in the file */
+    uint64_t nbytes;    /* data bytes; 0 when the type's block size is not known to the reader */
+    const void* data;   /* host address of the data in the mapping */
+} kq_gguf_tensor;
+int kq_gguf_open(const char* path, kq_gguf** out);
+int kq_gguf_close(kq_gguf* g);
+uint64_t kq_gguf_tensor_count(const kq_gguf* g);
+int kq_gguf_tensor_at(const kq_gguf* g, uint64_t index, kq_gguf_tensor* out);
+int kq_gguf_find(const kq_gguf* g, const char* name, kq_gguf_tensor* out);
+/* Metadata: an integer-typed (or bool) value, sign-extended; a string value (owned by g). */
+int kq_gguf_meta_int(const kq_gguf* g, const char* key, int64_t* out);
+int kq_gguf_meta_str(const kq_gguf* g, const char* key, const char** out);
+
 /* ---- Row-sharded stacks: a matvec whose epilogue also pushes its outputs to other GPUs ----
  *
  * With the rows of a matrix split over N GPUs, every GPU needs the whole output vector for the

@@ -54,6 +54,8 @@ EXPORTS = (
     "kq_matvec_q4k", "kq_matvec_q6k", "kq_matvec", "kq_dequant_q4k", "kq_dequant_q6k",
     "kq_fill_q4k", "kq_fill_q6k", "kq_stream_key", "kq_matvec_q4k_noalloc",
     "kq_matvec_push", "kq_wait_counter", "kq_peer_alloc", "kq_peer_open", "kq_peer_close", "kq_peer_free",
+    "kq_gguf_open", "kq_gguf_close", "kq_gguf_tensor_count", "kq_gguf_tensor_at", "kq_gguf_find",
+    "kq_gguf_meta_int", "kq_gguf_meta_str",
 )
 
 
@@ -75,6 +77,14 @@ class KqMatvecDesc(ctypes.Structure):
         ("x", ctypes.c_uint64), ("ldx", ctypes.c_uint64), ("ldy", ctypes.c_uint64),
         ("prologue", ctypes.c_uint32), ("epilogue", ctypes.c_uint32), ("eps", ctypes.c_float),
         ("pair_scale", ctypes.c_float), ("flags", ctypes.c_uint32), ("reserved", ctypes.c_uint32),
+    ]
+
+
+class KqGgufTensor(ctypes.Structure):
+    _fields_ = [
+        ("name", ctypes.c_char_p), ("type", ctypes.c_uint32), ("n_dims", ctypes.c_uint32),
+        ("dims", ctypes.c_uint64 * 4), ("offset", ctypes.c_uint64), ("nbytes", ctypes.c_uint64),
+        ("data", ctypes.c_void_p),
     ]
 
 
@@ -124,9 +134,17 @@ def lib() -> ctypes.CDLL:
     L.kq_peer_open.argtypes = [vp, ctypes.c_char_p, ctypes.POINTER(u64)]
     L.kq_peer_close.argtypes = [vp, u64]
     L.kq_peer_free.argtypes = [vp, u64]
+    L.kq_gguf_open.argtypes = [ctypes.c_char_p, ctypes.POINTER(vp)]
+    L.kq_gguf_close.argtypes = [vp]
+    L.kq_gguf_tensor_count.argtypes = [vp]
+    L.kq_gguf_tensor_count.restype = u64
+    L.kq_gguf_tensor_at.argtypes = [vp, u64, ctypes.POINTER(KqGgufTensor)]
+    L.kq_gguf_find.argtypes = [vp, ctypes.c_char_p, ctypes.POINTER(KqGgufTensor)]
+    L.kq_gguf_meta_int.argtypes = [vp, ctypes.c_char_p, ctypes.POINTER(ctypes.c_int64)]
+    L.kq_gguf_meta_str.argtypes = [vp, ctypes.c_char_p, ctypes.POINTER(ctypes.c_char_p)]
     for name in EXPORTS:
         fn = getattr(L, name)
-        if name not in ("kq_last_error", "kq_stream_key"):
+        if name not in ("kq_last_error", "kq_stream_key", "kq_gguf_tensor_count"):
             fn.restype = i32
     _lib = L
     return L
