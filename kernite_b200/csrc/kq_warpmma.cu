@@ -1,5 +1,8 @@
 // kq_warpmma.cu -- the Q4_K / Q6_K matvec for batch 1..8 with the multiply-adds on the tensor
-// cores through warp-level MMA (mma.sync m16n8k16: f16 operands from registers, f32 accumulate).
+// cores through warp-level MMA: at batch 1 (the default) integer MMAs (mma.sync m16n8k32, the
+// raw quants as u8 A operands, x as three signed byte limbs, s32 accumulate), at batch 2..8 f16
+// MMAs (m16n8k16, f16 operands from registers, f32 accumulate). The notes below describe the
+// f16 variant; the integer variant's are at q6i8_half and q4i8_block.
 //
 // y[b, r] = sum_k W[r, k] * x[b, k], W in GGML k-quant blocks (144-byte Q4_K, 210-byte Q6_K).
 //
@@ -16,7 +19,8 @@
 //    row segment. An mbarrier per slot counts the bytes in; Q6_K blocks at any even offset need
 //    nothing special (readers use the byte offset from the aligned copy).
 //  * A consumer warp takes one super-block of a tile: 16 MMAs (K = 16 each) over the tile's
-//    16 rows (warp w takes block w, or, with more warps than blocks, the warps take turns).
+//    16 rows (warp w takes block w, in a loop with the block's constants hoisted when the tiles
+//    are whole rows on 16-byte boundaries; else 19 warps take turns over a tile's blocks).
 //    The 16 rows are the MMA's M, x (with the batch) is its N. Thread (g, c) of the
 //    warp builds the A registers of rows g and g+8 from the bytes of its quarter of the block
 //    (Q4_K: qs chunk c = sub-blocks 2c, 2c+1; Q6_K: sub-blocks c and c+4 of each half).
