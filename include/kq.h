@@ -73,6 +73,9 @@ enum {
      * Without a path flag the library chooses: warp-MMA where it serves the request, the
      * tensor-core kernel above batch 8, the CUDA-core kernel otherwise. */
     KQ_FLAG_WARP_MMA = 1u << 4
+    /* Bits 29 and 30 are reserved for the library's tests and A/B timing: on the warp-MMA path
+     * they select its other operand variant at batch 1 (f16 instead of integer) and its other
+     * warp arrangement. Results stay within the same tolerance; callers leave them clear. */
 };
 
 typedef struct kq_ctx kq_ctx;
