@@ -386,23 +386,19 @@ def main(argv=None):
 
 
 def run_e2e(kernels, kb, torch, qtype, Ws, rows, K, batch, steps, dist):
-    """The same matvec through kernite_b200's public API with host buffers: each step copies its
-    x from pinned host memory, launches, and reads y back into pinned host memory."""
+    """The same matvec through kernite_b200's public API with host buffers (kq_matvec_host): each
+    step copies its x from pinned host memory, launches, reads y back into pinned host memory
+    and waits for it."""
     import numpy as np
 
     copies = len(Ws)
     xh = torch.from_numpy(np.random.default_rng(1).standard_normal((batch, K), dtype=np.float32)).pin_memory()
     yh = torch.empty(batch, rows).pin_memory()
-    xd = torch.empty(batch, K, device="cuda")
-    yd = torch.empty(batch, rows, device="cuda")
     s = torch.cuda.Stream()
-    fn = kernels.matvec_q4k if qtype == 4 else kernels.matvec_q6k
 
     def step(i):
-        with torch.cuda.stream(s):
-            xd.copy_(xh, non_blocking=True)
-            fn(yd, Ws[i % copies], xd, rows, K, batch, stream=s)
-            yh.copy_(yd, non_blocking=True)
+        # one library call: x to the device, the matvec, y back (kq_matvec_host), then the wait
+        kernels.matvec_host(qtype, yh, Ws[i % copies], xh, rows, K, batch, stream=s)
         s.synchronize()
 
     for i in range(20):

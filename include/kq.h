@@ -135,6 +135,17 @@ typedef struct kq_matvec_desc {
  * (examples/matmul/src/gpu.rs:360-391) made from the descriptor. */
 int kq_matvec(kq_ctx* ctx, const kq_matvec_desc* desc, kq_stream stream);
 
+/* kq_matvec with x and y in host memory, for callers that hold their vectors on the host (as a
+ * kernite caller does around Buffer::copy_from_host / copy_to_host, crates/cuda/src/lib.rs):
+ * copies x (batch rows of ldx floats) into the context's device staging buffer, runs the matvec
+ * with desc->w on the device, and copies y (batch rows of the output, ldy floats apart) back,
+ * all on `stream`; synchronise the stream before reading y. desc->x and desc->y are ignored.
+ * Page-locked host memory makes the copies asynchronous. The staging buffer grows on demand
+ * (cudaMalloc: not inside a stream capture); calls that may overlap on the GPU need separate
+ * contexts. */
+int kq_matvec_host(kq_ctx* ctx, const kq_matvec_desc* desc, float* y_host, const float* x_host,
+                   kq_stream stream);
+
 /* out[256*i + e] = weight e of block i, for nblocks blocks at w, in the canonical order
  * w = (f32(d)*f32(sc))*f32(q) - f32(dmin)*f32(m) (Q4_K) / (f32(d)*f32(scale))*f32(q-32) (Q6_K),
  * each operation rounded to f32: bit-exact with the CPU decode. A verification kernel. No

@@ -51,7 +51,7 @@ QK = 256
 # Every symbol include/kq.h declares (tests check the library exports each).
 EXPORTS = (
     "kq_ctx_create", "kq_ctx_destroy", "kq_last_error", "kq_ctx_info", "kq_device_error",
-    "kq_matvec_q4k", "kq_matvec_q6k", "kq_matvec", "kq_dequant_q4k", "kq_dequant_q6k",
+    "kq_matvec_q4k", "kq_matvec_q6k", "kq_matvec", "kq_matvec_host", "kq_dequant_q4k", "kq_dequant_q6k",
     "kq_fill_q4k", "kq_fill_q6k", "kq_stream_key", "kq_matvec_q4k_noalloc",
     "kq_matvec_push", "kq_wait_counter", "kq_peer_alloc", "kq_peer_open", "kq_peer_close", "kq_peer_free",
     "kq_gguf_open", "kq_gguf_close", "kq_gguf_tensor_count", "kq_gguf_tensor_at", "kq_gguf_find",
@@ -121,6 +121,7 @@ def lib() -> ctypes.CDLL:
     for name in ("kq_matvec_q4k", "kq_matvec_q6k"):
         getattr(L, name).argtypes = [vp, u64, u64, u64, u32, u32, u32, vp]
     L.kq_matvec.argtypes = [vp, ctypes.POINTER(KqMatvecDesc), vp]
+    L.kq_matvec_host.argtypes = [vp, ctypes.POINTER(KqMatvecDesc), vp, vp, vp]
     for name in ("kq_dequant_q4k", "kq_dequant_q6k"):
         getattr(L, name).argtypes = [vp, u64, u64, u64, vp]
     for name in ("kq_fill_q4k", "kq_fill_q6k"):
@@ -175,6 +176,19 @@ def _addr(p: Any) -> int:
             raise Error("kernite_b200", "a tensor given as a device pointer is on the CPU")
         return int(p.data_ptr())
     raise TypeError(f"not a device pointer: {type(p)!r}")
+
+
+def _host_addr(p: Any) -> int:
+    """The address of a host array (a CPU torch tensor or a C-contiguous numpy array)."""
+    if hasattr(p, "data_ptr"):
+        if getattr(p, "is_cuda", False):
+            raise Error("kernite_b200", "a host array was expected, got a CUDA tensor")
+        return int(p.data_ptr())
+    if hasattr(p, "ctypes"):
+        if not p.flags["C_CONTIGUOUS"]:
+            raise Error("kernite_b200", "host arrays must be C-contiguous")
+        return int(p.ctypes.data)
+    raise TypeError(f"not a host array: {type(p)!r}")
 
 
 def _stream(s: Any) -> int | None:
@@ -266,6 +280,19 @@ class Kernels:
                          ldx=ldx, ldy=ldy, prologue=prologue, epilogue=epilogue, eps=eps,
                          pair_scale=pair_scale, flags=flags, reserved=0)
         _check(lib().kq_matvec(self._ctx, ctypes.byref(d), _stream(stream)), "kq_matvec")
+
+    def matvec_host(self, qtype: int, y, w, x, rows: int, k: int, batch: int = 1, *,
+                    ldx: int = 0, ldy: int = 0, prologue: int = PROLOGUE_NONE,
+                    epilogue: int = EPILOGUE_NONE, eps: float = 0.0, pair_scale: float = 1.0,
+                    flags: int = 0, stream=None) -> None:
+        """``kq_matvec_host``: x and y are host arrays (torch CPU tensors, pinned for asynchronous
+        copies, or numpy arrays), w is on the device; synchronise ``stream`` before reading y."""
+        t = {4: TYPE_Q4_K, 6: TYPE_Q6_K}.get(qtype, qtype)
+        d = KqMatvecDesc(type=t, rows=rows, k=k, batch=batch, y=0, w=_addr(w), x=0, ldx=ldx,
+                         ldy=ldy, prologue=prologue, epilogue=epilogue, eps=eps,
+                         pair_scale=pair_scale, flags=flags, reserved=0)
+        _check(lib().kq_matvec_host(self._ctx, ctypes.byref(d), _host_addr(y), _host_addr(x),
+                                    _stream(stream)), "kq_matvec_host")
 
     def dequant(self, qtype: int, out, w, nblocks: int, stream=None) -> None:
         """Bit-exact decode of ``nblocks`` blocks into f32 (verification kernel)."""

@@ -121,9 +121,10 @@ int kq_ctx_create(int device, kq_ctx** out) {
 
 int kq_ctx_destroy(kq_ctx* ctx) {
   if (!ctx) return KQ_OK;
-  if (ctx->scratch) {
+  if (ctx->scratch || ctx->stage) {
     kq::enter(ctx);
-    cudaFree(ctx->scratch);  // waits for the device, so no launch still reads it
+    if (ctx->scratch) cudaFree(ctx->scratch);  // waits for the device: no launch still reads it
+    if (ctx->stage) cudaFree(ctx->stage);
   }
   delete ctx;
   return KQ_OK;
@@ -197,6 +198,51 @@ int kq_matvec(kq_ctx* ctx, const kq_matvec_desc* desc, kq_stream stream) {
   int rc = kq::enter(ctx);
   if (rc) return rc;
   return kq::matvec(ctx, *desc, static_cast<cudaStream_t>(stream));
+}
+
+int kq_matvec_host(kq_ctx* ctx, const kq_matvec_desc* desc, float* y_host, const float* x_host,
+                   kq_stream stream) {
+  const char* call = "kq_matvec_host";
+  if (!ctx || !desc || !y_host || !x_host) return fail(KQ_E_INVALID, call, "null argument");
+  int rc = kq::enter(ctx);
+  if (rc) return rc;
+  kq_matvec_desc d = *desc;
+  if (d.batch == 0 || d.rows == 0 || d.k == 0)
+    return fail(KQ_E_INVALID, call, "rows, k and batch must be positive");
+  const bool pair = d.epilogue == KQ_EPILOGUE_PAIR_PRODUCT;
+  const uint64_t ldx = d.ldx ? d.ldx : d.k;
+  const uint64_t out_rows = pair ? d.rows / 2 : d.rows;
+  const uint64_t ldy = d.ldy ? d.ldy : out_rows;
+  if (ldx < d.k || ldy < out_rows)
+    return fail(KQ_E_INVALID, call, "ldx must be >= k and ldy >= the output rows");
+  // staging: x (batch rows of ldx floats, 256-byte aligned start of y after it), y (batch x ldy)
+  const uint64_t xb = (uint64_t(d.batch) * ldx * 4 + 255) / 256 * 256;
+  const uint64_t need = xb + uint64_t(d.batch) * ldy * 4;
+  if (need > ctx->stage_bytes) {
+    if (ctx->stage) {
+      cudaError_t e = cudaFree(ctx->stage);  // waits for the device: no launch still uses it
+      ctx->stage = nullptr;
+      ctx->stage_bytes = 0;
+      if (e != cudaSuccess) return cuda_fail(e, "cudaFree", "host-call staging");
+    }
+    const cudaError_t e = cudaMalloc(&ctx->stage, need);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaMalloc", "host-call staging");
+    ctx->stage_bytes = need;
+  }
+  const cudaStream_t s = static_cast<cudaStream_t>(stream);
+  uint8_t* xs = static_cast<uint8_t*>(ctx->stage);
+  float* ys = reinterpret_cast<float*>(xs + xb);
+  cudaError_t e = cudaMemcpyAsync(xs, x_host, uint64_t(d.batch) * ldx * 4, cudaMemcpyHostToDevice, s);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaMemcpyAsync", "x to the device");
+  d.x = reinterpret_cast<uint64_t>(xs);
+  d.y = reinterpret_cast<uint64_t>(ys);
+  d.ldx = ldx;
+  d.ldy = ldy;
+  rc = kq::matvec(ctx, d, s);
+  if (rc) return rc;
+  e = cudaMemcpy2DAsync(y_host, ldy * 4, ys, ldy * 4, out_rows * 4, d.batch, cudaMemcpyDeviceToHost, s);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaMemcpy2DAsync", "y to the host");
+  return KQ_OK;
 }
 
 int kq_dequant_q4k(kq_ctx* ctx, uint64_t out, uint64_t w, uint64_t nblocks, kq_stream stream) {

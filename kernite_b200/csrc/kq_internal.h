@@ -16,6 +16,9 @@ struct kq_ctx {
   // Scratch the tensor-core path converts X into (allocated once, at creation).
   void* scratch = nullptr;
   uint64_t scratch_bytes = 0;
+  // Device staging for kq_matvec_host's x and y (grown on demand).
+  void* stage = nullptr;
+  uint64_t stage_bytes = 0;
 };
 
 namespace kq {

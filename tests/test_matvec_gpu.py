@@ -355,3 +355,36 @@ def test_rmsnorm_prologue_any_magnitude(kernels, mag):
     xn = x64 / np.sqrt(np.mean(x64 ** 2) + eps)
     y_ref, bound = oracle.matvec_ref(4, W.cpu().numpy(), xn.astype(np.float32), K, 0, rows)
     check(y, y_ref, bound, f"rmsnorm x~{mag}")
+
+
+@pytest.mark.parametrize("qtype,rows,K,batch,pad", [(6, 1000, 4096, 1, 0), (4, 300, 2048, 4, 8),
+                                                    (4, 64, 1024, 8, 0), (6, 77, 11008, 1, 4)])
+def test_matvec_host_buffers_match_the_device_path(kernels, qtype, rows, K, batch, pad):
+    # kq_matvec_host: x and y in host memory (pinned torch and plain numpy), strided, equal bit
+    # for bit to the same matvec on device buffers
+    W = torch.empty(kb.matrix_bytes(qtype, rows, K), dtype=torch.uint8, device="cuda")
+    kernels.fill(qtype, W, 0, rows * K // 256, kb.stream_key(95, qtype))
+    ldx, ldy = K + 4 * pad, rows + pad
+    x = np.random.default_rng(95).standard_normal((batch, ldx), dtype=np.float32)
+    yd = torch.zeros((batch, ldy), dtype=torch.float32, device="cuda")
+    kernels.matvec(qtype, yd, W, torch.from_numpy(x).cuda(), rows, K, batch, ldx=ldx, ldy=ldy)
+    torch.cuda.synchronize()
+    want = yd.cpu().numpy()
+    for pinned in (True, False):
+        if pinned:
+            xh = torch.from_numpy(x).pin_memory()
+            yh = torch.full((batch, ldy), -7.0, dtype=torch.float32).pin_memory()
+        else:
+            xh = x.copy()
+            yh = np.full((batch, ldy), -7.0, dtype=np.float32)
+        kernels.matvec_host(qtype, yh, W, xh, rows, K, batch, ldx=ldx, ldy=ldy)
+        torch.cuda.synchronize()
+        got = yh.numpy() if pinned else yh
+        assert np.array_equal(got[:, :rows], want[:, :rows])
+        assert (got[:, rows:] == -7.0).all()  # the gaps between rows of y stay untouched
+
+
+def test_matvec_host_rejects_device_arrays(kernels):
+    W = torch.empty(kb.matrix_bytes(4, 16, 256), dtype=torch.uint8, device="cuda")
+    with pytest.raises(kb.Error):
+        kernels.matvec_host(4, torch.zeros(16, device="cuda"), W, np.zeros(256, np.float32), 16, 256)
