@@ -55,7 +55,7 @@ enum { KQ_TYPE_Q4_K = 12, KQ_TYPE_Q6_K = 14 };
 
 /* What a matvec does to x before the product, and to each output after it. */
 enum { KQ_PROLOGUE_NONE = 0, KQ_PROLOGUE_RMSNORM = 1 };
-enum { KQ_EPILOGUE_NONE = 0, KQ_EPILOGUE_PAIR_PRODUCT = 1 };
+enum { KQ_EPILOGUE_NONE = 0, KQ_EPILOGUE_PAIR_PRODUCT = 1, KQ_EPILOGUE_SILU_PRODUCT = 2 };
 
 /* Flags for kq_matvec_desc.flags. */
 enum {
@@ -121,10 +121,13 @@ typedef struct kq_matvec_desc {
     uint32_t batch;    /* vectors: 1..64 for Q4_K, 1..8 for Q6_K */
     uint64_t y, w, x;  /* device addresses */
     uint64_t ldx;      /* floats between vectors of x (>= k, multiple of 4); 0 = k */
-    uint64_t ldy;      /* floats between vectors of y; 0 = rows (or rows/2 for PAIR_PRODUCT) */
+    uint64_t ldy;      /* floats between vectors of y; 0 = rows (or rows/2 for the products) */
     uint32_t prologue; /* KQ_PROLOGUE_*: RMSNORM uses x / sqrt(mean(x^2) + eps) */
     uint32_t epilogue; /* KQ_EPILOGUE_*: PAIR_PRODUCT writes y[r/2] = v(r) * v(r+1) * pair_scale
-                          for even r (rows must be even) */
+                          for even r (rows must be even); SILU_PRODUCT writes
+                          y[r/2] = silu(v(r)) * v(r+1) * pair_scale, silu(z) = z / (1 + e^-z):
+                          a gated FFN's gate and up rows interleaved, as Llama's SiLU(W_gate x)
+                          * (W_up x) */
     float eps;
     float pair_scale;
     uint32_t flags;    /* KQ_FLAG_* */

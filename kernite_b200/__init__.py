@@ -38,6 +38,7 @@ PROLOGUE_NONE = 0
 PROLOGUE_RMSNORM = 1
 EPILOGUE_NONE = 0
 EPILOGUE_PAIR_PRODUCT = 1
+EPILOGUE_SILU_PRODUCT = 2
 FLAG_WEIGHTS_STATIC = 1
 FLAG_NO_PDL = 2
 FLAG_TENSOR_CORES = 4

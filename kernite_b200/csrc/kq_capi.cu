@@ -209,7 +209,7 @@ int kq_matvec_host(kq_ctx* ctx, const kq_matvec_desc* desc, float* y_host, const
   kq_matvec_desc d = *desc;
   if (d.batch == 0 || d.rows == 0 || d.k == 0)
     return fail(KQ_E_INVALID, call, "rows, k and batch must be positive");
-  const bool pair = d.epilogue == KQ_EPILOGUE_PAIR_PRODUCT;
+  const bool pair = d.epilogue != KQ_EPILOGUE_NONE;
   const uint64_t ldx = d.ldx ? d.ldx : d.k;
   const uint64_t out_rows = pair ? d.rows / 2 : d.rows;
   const uint64_t ldy = d.ldy ? d.ldy : out_rows;

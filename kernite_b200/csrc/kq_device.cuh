@@ -5,6 +5,8 @@
 #include <cstdint>
 #include <cuda_fp16.h>
 
+#include "kq.h"
+
 namespace kq {
 
 constexpr int kQK = 256;
@@ -186,6 +188,15 @@ __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;"
 // Lets the next kernel on the stream launch (its CTAs then wait in pdl_wait()).
 __device__ __forceinline__ void pdl_launch_dependents() {
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
+// ---------------------------------------------------------------- epilogues
+
+// The product epilogues of a row pair (v0: the gate row, v1: the up row): v0 v1 s, or
+// silu(v0) v1 s with silu(z) = z / (1 + e^-z) (expf: CUDA's accurate exponential).
+__device__ __forceinline__ float pair_value(float v0, float v1, uint32_t epilogue, float s) {
+  if (epilogue == KQ_EPILOGUE_SILU_PRODUCT) v0 = v0 / (1.f + expf(-v0));
+  return v0 * v1 * s;
 }
 
 // ---------------------------------------------------------------- misc

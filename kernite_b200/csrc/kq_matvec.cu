@@ -495,7 +495,7 @@ __global__ void __launch_bounds__(Geo<B>::kMaxThreads, 1) matvec_kernel(const Ma
               } else if ((u & 1) == 0) {
                 held[b] = acc[b];
               } else {
-                a.y[b * a.ldy + row / 2] = held[b] * acc[b] * a.pair_scale;
+                a.y[b * a.ldy + row / 2] = pair_value(held[b], acc[b], a.epilogue, a.pair_scale);
               }
             }
           }
@@ -531,7 +531,7 @@ __global__ void __launch_bounds__(Geo<B>::kMaxThreads, 1) matvec_kernel(const Ma
               float v1 = 0.f;
               for (uint32_t w = 0; w < a.team_warps; ++w)
                 v1 += tb[((u0 + 1) * a.team_warps + w) * B + b];
-              a.y[b * a.ldy + row / 2] = v0 * v1 * a.pair_scale;
+              a.y[b * a.ldy + row / 2] = pair_value(v0, v1, a.epilogue, a.pair_scale);
             }
           }
         }
@@ -634,9 +634,9 @@ int matvec(kq_ctx* ctx, const kq_matvec_desc& d, cudaStream_t stream, const kq_p
   if (!d.w || !d.x || !d.y) return fail(KQ_E_INVALID, call, "null pointer");
   if (d.w % 16 || d.x % 16 || d.y % 4)
     return fail(KQ_E_INVALID, call, "w and x must be 16-byte aligned, y 4-byte aligned");
-  if (d.prologue > KQ_PROLOGUE_RMSNORM || d.epilogue > KQ_EPILOGUE_PAIR_PRODUCT)
+  if (d.prologue > KQ_PROLOGUE_RMSNORM || d.epilogue > KQ_EPILOGUE_SILU_PRODUCT)
     return fail(KQ_E_INVALID, call, "unknown prologue or epilogue");
-  const bool pair = d.epilogue == KQ_EPILOGUE_PAIR_PRODUCT;
+  const bool pair = d.epilogue != KQ_EPILOGUE_NONE;  // the products take rows in pairs
   if (pair && d.rows % 2) return fail(KQ_E_INVALID, call, "pair product needs an even row count");
   const uint64_t ldx = d.ldx ? d.ldx : d.k;
   const uint64_t out_rows = pair ? d.rows / 2 : d.rows;

@@ -1024,7 +1024,7 @@ __global__ void __launch_bounds__((kMaxWarps + 1) * 32, 1) warpmma_kernel(const 
           const float* rq = rp + nw * B;
           for (uint32_t w = 0; w < nw; ++w) v1 += rq[w * B];
           v1 *= s_ns[b];
-          a.y[b * a.ldy + row / 2] = v0 * v1 * a.pair_scale;
+          a.y[b * a.ldy + row / 2] = pair_value(v0, v1, a.epilogue, a.pair_scale);
         }
       }
       named_barrier(1, nthr);
@@ -1442,7 +1442,7 @@ int warpmma_matvec(kq_ctx* ctx, const kq_matvec_desc& d, uint64_t ldx, uint64_t 
   args.bars_off = args.red_off + red_bytes;
   args.ncol = ncol;
   args.fb = fb;
-  args.row_unit = d.epilogue == KQ_EPILOGUE_PAIR_PRODUCT ? 2 : 1;
+  args.row_unit = d.epilogue != KQ_EPILOGUE_NONE ? 2 : 1;
   args.prologue = d.prologue;
   args.epilogue = d.epilogue;
   args.flags = d.flags;

@@ -208,6 +208,30 @@ def test_pair_product_epilogue(kernels, qtype):
     assert np.isnan(yh[rows // 2:]).all()
 
 
+@pytest.mark.parametrize("qtype,K", [(4, 4096), (6, 4096), (6, 11008)])
+@pytest.mark.parametrize("path", ["auto", "cuda_cores"])
+def test_silu_product_epilogue(kernels, qtype, K, path):
+    # y[r/2] = silu(v(r)) * v(r+1) * scale: a gated FFN's interleaved gate and up rows. silu has
+    # slope in [-0.1, 1.1], so the gate's error bound passes through it scaled by at most 1.1.
+    rows, scale = 2 * 211, 0.25
+    W = dev_weights(kernels, qtype, rows, K, kb.stream_key(15, qtype))
+    x = np.random.default_rng(8).standard_normal((1, K), dtype=np.float32)
+    y = torch.full((rows // 2 + 8,), float("nan"), device="cuda")
+    flags = kb.FLAG_CUDA_CORES if path == "cuda_cores" else 0
+    kernels.matvec(qtype, y, W, torch.from_numpy(x).cuda(), rows, K, 1,
+                   epilogue=kb.EPILOGUE_SILU_PRODUCT, pair_scale=scale, flags=flags)
+    torch.cuda.synchronize()
+    yh = y.cpu().numpy().astype(np.float64)
+    r, b = oracle.matvec_ref(qtype, W.cpu().numpy(), x, K, 0, rows)
+    v0, v1, b0, b1 = r[0, 0::2], r[0, 1::2], b[0, 0::2], b[0, 1::2]
+    s0 = v0 / (1.0 + np.exp(-v0))
+    want = s0 * v1 * scale
+    tol = (TOL * (1.1 * b0 * np.abs(v1) + b1 * np.abs(s0) + 1.1 * TOL * b0 * b1) * scale
+           + 1e-6 * np.abs(want))
+    assert (np.abs(yh[: rows // 2] - want) <= tol).all()
+    assert np.isnan(yh[rows // 2:]).all()
+
+
 def test_invalid_arguments_are_rejected_before_launch(kernels):
     W = torch.empty(144 * 64, dtype=torch.uint8, device="cuda")
     x = torch.zeros(4096 * 9, device="cuda")
