@@ -23,6 +23,7 @@ LIB_PATH = os.path.join(HERE, "liboracle.so")
 
 Q4K_BYTES = 144
 Q6K_BYTES = 210
+Q5K_BYTES = 176
 QK = 256
 
 _lib = None
@@ -50,7 +51,7 @@ def lib() -> ctypes.CDLL:
         L.kqo_f32_to_fp16.restype = ctypes.c_uint16
         L.kqo_q4k_scale_min.argtypes = [u8p, ctypes.c_int, u8p, u8p]
         L.kqo_q4k_scale_min.restype = None
-        for name in ("kqo_dequant_q4k", "kqo_dequant_q6k"):
+        for name in ("kqo_dequant_q4k", "kqo_dequant_q5k", "kqo_dequant_q6k"):
             fn = getattr(L, name)
             fn.argtypes = [u8p, ctypes.c_size_t, f32p]
             fn.restype = None
@@ -59,7 +60,7 @@ def lib() -> ctypes.CDLL:
             ctypes.c_uint32, ctypes.c_uint64, ctypes.c_uint64, f64p, f64p,
         ]
         L.kqo_matvec_ref.restype = None
-        for name in ("kqo_fill_q4k", "kqo_fill_q6k"):
+        for name in ("kqo_fill_q4k", "kqo_fill_q5k", "kqo_fill_q6k"):
             fn = getattr(L, name)
             fn.argtypes = [u8p, ctypes.c_uint64, ctypes.c_uint64, ctypes.c_uint64]
             fn.restype = None
@@ -92,7 +93,7 @@ def _f64(a: np.ndarray):
 
 
 def block_bytes(qtype: int) -> int:
-    return {4: Q4K_BYTES, 6: Q6K_BYTES}[qtype]
+    return {4: Q4K_BYTES, 5: Q5K_BYTES, 6: Q6K_BYTES}[qtype]
 
 
 def fp16_to_f32(h: int) -> float:
@@ -117,7 +118,7 @@ def dequant(qtype: int, blocks: np.ndarray) -> np.ndarray:
     n = blocks.size // block_bytes(qtype)
     assert n * block_bytes(qtype) == blocks.size
     out = np.empty(n * QK, dtype=np.float32)
-    fn = lib().kqo_dequant_q4k if qtype == 4 else lib().kqo_dequant_q6k
+    fn = {4: lib().kqo_dequant_q4k, 5: lib().kqo_dequant_q5k, 6: lib().kqo_dequant_q6k}[qtype]
     fn(_u8(blocks), n, _f32(out))
     return out
 
@@ -133,7 +134,7 @@ def splitmix_at(key: int, i: int) -> int:
 def fill(qtype: int, key: int, b0: int, n: int) -> np.ndarray:
     """Blocks [b0, b0+n) of the synthetic tensor with stream key `key`, as raw bytes."""
     out = np.empty(n * block_bytes(qtype), dtype=np.uint8)
-    fn = lib().kqo_fill_q4k if qtype == 4 else lib().kqo_fill_q6k
+    fn = {4: lib().kqo_fill_q4k, 5: lib().kqo_fill_q5k, 6: lib().kqo_fill_q6k}[qtype]
     fn(_u8(out), key, b0, n)
     return out
 

@@ -153,13 +153,43 @@ void kqo_dequant_q6k(const uint8_t* blocks, size_t n, float* out) {
     }
 }
 
+/* ---------------------------------------------------------------- Q5_K */
+
+/* As Q4_K (qs at byte 48 instead of 16), with the fifth bit of element 32g + l in bit g of
+ * qh[l]: chunk c's low nibbles are group 2c, its high nibbles group 2c + 1. */
+void kqo_dequant_q5k(const uint8_t* blocks, size_t n, float* out) {
+    for (size_t b = 0; b < n; ++b) {
+        const uint8_t* blk = blocks + b * KQ_Q5K_BYTES;
+        float d = kqo_fp16_to_f32(rd16(blk));
+        float dmin = kqo_fp16_to_f32(rd16(blk + 2));
+        const uint8_t* scales = blk + 4;
+        const uint8_t* qh = blk + 16;
+        const uint8_t* qs = blk + 48;
+        float* o = out + b * KQ_QK;
+        for (int j = 0; j < 8; ++j) {
+            uint8_t sc, m;
+            kqo_q4k_scale_min(scales, j, &sc, &m);
+            float ds = d * (float)sc;
+            float dm = dmin * (float)m;
+            int c = j >> 1, hi = j & 1;
+            for (int l = 0; l < 32; ++l) {
+                uint8_t nib = hi ? (uint8_t)(qs[32 * c + l] >> 4) : (uint8_t)(qs[32 * c + l] & 15u);
+                uint8_t q = (uint8_t)(nib | (((qh[l] >> j) & 1u) << 4));
+                float t = ds * (float)q;
+                o[32 * j + l] = t - dm;
+            }
+        }
+    }
+}
+
 /* ---------------------------------------------------------------- reference matvec */
 
 void kqo_matvec_ref(int type, const uint8_t* W, const float* x, uint32_t K, uint32_t r0,
                     uint32_t r1, uint32_t batch, uint64_t ldx, uint64_t ldy, double* y,
                     double* bound) {
     const uint32_t nb = K / KQ_QK;
-    const size_t blk_bytes = type == 4 ? KQ_Q4K_BYTES : KQ_Q6K_BYTES;
+    const size_t blk_bytes =
+        type == 4 ? KQ_Q4K_BYTES : type == 5 ? KQ_Q5K_BYTES : KQ_Q6K_BYTES;
     float w[KQ_QK];
     for (uint32_t r = r0; r < r1; ++r) {
         for (uint32_t b = 0; b < batch; ++b) {
@@ -170,6 +200,8 @@ void kqo_matvec_ref(int type, const uint8_t* W, const float* x, uint32_t K, uint
             const uint8_t* blk = W + ((size_t)r * nb + kb) * blk_bytes;
             if (type == 4)
                 kqo_dequant_q4k(blk, 1, w);
+            else if (type == 5)
+                kqo_dequant_q5k(blk, 1, w);
             else
                 kqo_dequant_q6k(blk, 1, w);
             for (uint32_t b = 0; b < batch; ++b) {
@@ -248,5 +280,21 @@ void kqo_fill_q6k(uint8_t* out, uint64_t key, uint64_t b0, uint64_t n) {
         uint16_t d = uniform_fp16(kqo_splitmix_at(key, 28 * b + 27), 0x1p-12f, 15.0f * 0x1p-12f);
         blk[208] = (uint8_t)d;
         blk[209] = (uint8_t)(d >> 8);
+    }
+}
+
+/* Block b draws counters [24b, 24b+24): words 0-21 are its 176 bytes (bytes 0-3 then
+ * overwritten), word 22 gives d and word 23 gives dmin. */
+void kqo_fill_q5k(uint8_t* out, uint64_t key, uint64_t b0, uint64_t n) {
+    for (uint64_t i = 0; i < n; ++i) {
+        uint64_t b = b0 + i;
+        uint8_t* blk = out + i * KQ_Q5K_BYTES;
+        put_bytes(blk, key, 24 * b, KQ_Q5K_BYTES);
+        uint16_t d = uniform_fp16(kqo_splitmix_at(key, 24 * b + 22), 0x1p-11f, 15.0f * 0x1p-11f);
+        uint16_t m = uniform_fp16(kqo_splitmix_at(key, 24 * b + 23), 0x1p-11f, 15.0f * 0x1p-11f);
+        blk[0] = (uint8_t)d;
+        blk[1] = (uint8_t)(d >> 8);
+        blk[2] = (uint8_t)m;
+        blk[3] = (uint8_t)(m >> 8);
     }
 }

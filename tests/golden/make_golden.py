@@ -1,8 +1,8 @@
-"""Generate the committed golden fixtures that pin the CPU oracle's Q4_K / Q6_K decode.
+"""Generate the committed golden fixtures that pin the CPU oracle's Q4_K / Q5_K / Q6_K decode.
 
 The k-quant format is third-party (GGML); fxeqxmulfx/kernite has no implementation of it. The
 owner's published Python package gguf-py (version 0.19.0, ``gguf/quants.py``,
-``Q4_K.dequantize_blocks`` / ``Q6_K.dequantize_blocks``) is imported here, in the development
+``Q4_K``, ``Q5_K`` and ``Q6_K.dequantize_blocks``) is imported here, in the development
 container, to dequantise a fixed set of blocks. Its float32 outputs are stored bit for bit in
 ``kquant_golden.npz`` and the tests compare the oracle (and, on the GPU, the device decode)
 against them. The GPU box does not need gguf: only the .npz travels.
@@ -75,6 +75,32 @@ def pack_q4k_scales(sc: np.ndarray, mn: np.ndarray) -> np.ndarray:
     return s.astype(np.uint8)
 
 
+def kat_q5k() -> np.ndarray:
+    blocks = []
+    # one scale set to 1 (d = 1, dmin = 0), nibble and fifth-bit patterns covering q = 0..31
+    for j in range(8):
+        b = np.zeros(176, dtype=np.uint8)
+        b[0:2] = np.array([fp16_bits(1.0)], dtype=np.uint16).view(np.uint8)
+        sc = np.zeros(8, dtype=np.int64)
+        sc[j] = 1
+        b[4:16] = pack_q4k_scales(sc, np.zeros(8, dtype=np.int64))
+        b[16:48] = np.array([(37 * i + 11 * j) % 256 for i in range(32)], dtype=np.uint8)
+        b[48:] = np.array([(i % 16) | (((i + 5) % 16) << 4) for i in range(128)], dtype=np.uint8)
+        blocks.append(b)
+    # every 6-bit value of every scale slot and min slot, d = dmin = 1, all fifth bits set
+    for v in range(64):
+        b = np.zeros(176, dtype=np.uint8)
+        b[0:2] = np.array([fp16_bits(1.0)], dtype=np.uint16).view(np.uint8)
+        b[2:4] = np.array([fp16_bits(1.0)], dtype=np.uint16).view(np.uint8)
+        sc = np.array([(v + 7 * j) % 64 for j in range(8)])
+        mn = np.array([(63 - v + 3 * j) % 64 for j in range(8)])
+        b[4:16] = pack_q4k_scales(sc, mn)
+        b[16:48] = np.uint8(0xFF)
+        b[48:] = np.uint8(0x5A)
+        blocks.append(b)
+    return np.concatenate(blocks)
+
+
 def kat_q6k() -> np.ndarray:
     blocks = []
     for sgn in (1, -1):
@@ -107,7 +133,7 @@ def kat_q6k() -> np.ndarray:
 def gguf_dequant(qtype: int, raw: np.ndarray) -> np.ndarray:
     bb = oracle.block_bytes(qtype)
     arr = raw.reshape(-1, bb)
-    out = dequantize(arr, T.Q4_K if qtype == 4 else T.Q6_K)
+    out = dequantize(arr, {4: T.Q4_K, 5: T.Q5_K, 6: T.Q6_K}[qtype])
     return np.ascontiguousarray(out, dtype=np.float32).reshape(-1)
 
 
@@ -116,11 +142,11 @@ def main() -> None:
     rng = np.random.default_rng(20261201)
     data = {"gguf_version": np.array(gguf.__version__ if hasattr(gguf, "__version__") else "0.19.0")}
     key = oracle.stream_key(1234, 7)
-    for qtype in (4, 6):
+    for qtype in (4, 6, 5):  # Q5_K last: the Q4_K/Q6_K draws stay as they were
         bb = oracle.block_bytes(qtype)
         gen = oracle.fill(qtype, key, 0, 64)
         raw = rng.integers(0, 256, size=64 * bb, dtype=np.uint8)
-        kat = kat_q4k() if qtype == 4 else kat_q6k()
+        kat = {4: kat_q4k, 5: kat_q5k, 6: kat_q6k}[qtype]()
         for name, blocks in (("gen", gen), ("raw", raw), ("kat", kat)):
             ref = gguf_dequant(qtype, blocks)
             data[f"q{qtype}k_{name}_blocks"] = blocks

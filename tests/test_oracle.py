@@ -62,7 +62,7 @@ def test_f32_to_fp16_matches_numpy_rounding():
     assert np.array_equal(got, want)
 
 
-@pytest.mark.parametrize("qtype", [4, 6])
+@pytest.mark.parametrize("qtype", [4, 5, 6])
 @pytest.mark.parametrize("which", ["gen", "raw", "kat"])
 def test_dequant_matches_gguf_bit_for_bit(golden, qtype, which):
     blocks = golden[f"q{qtype}k_{which}_blocks"]
@@ -74,7 +74,7 @@ def test_dequant_matches_gguf_bit_for_bit(golden, qtype, which):
     assert np.array_equal(got[~nan], want[~nan])
 
 
-@pytest.mark.parametrize("qtype", [4, 6])
+@pytest.mark.parametrize("qtype", [4, 5, 6])
 def test_matvec_ref_matches_golden(golden, qtype):
     W = golden[f"q{qtype}k_mv_W"]
     x = golden[f"q{qtype}k_mv_x"]
