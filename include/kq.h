@@ -51,7 +51,7 @@ enum {
 };
 
 /* Quantisation types, GGML's type numbers. */
-enum { KQ_TYPE_Q4_K = 12, KQ_TYPE_Q6_K = 14 };
+enum { KQ_TYPE_Q4_K = 12, KQ_TYPE_Q5_K = 13, KQ_TYPE_Q6_K = 14 };
 
 /* What a matvec does to x before the product, and to each output after it. */
 enum { KQ_PROLOGUE_NONE = 0, KQ_PROLOGUE_RMSNORM = 1 };
@@ -156,6 +156,10 @@ int kq_matvec_host(kq_ctx* ctx, const kq_matvec_desc* desc, float* y_host, const
  * examples/matmul/src/reference.rs:1-10. */
 int kq_dequant_q4k(kq_ctx* ctx, uint64_t out, uint64_t w, uint64_t nblocks, kq_stream stream);
 int kq_dequant_q6k(kq_ctx* ctx, uint64_t out, uint64_t w, uint64_t nblocks, kq_stream stream);
+/* Q5_K (176-byte blocks {fp16 d, fp16 dmin, u8 scales[12], u8 qh[32], u8 qs[128]}, 16-byte
+ * aligned w): Q4_K's decode with q = nibble | fifth bit << 4, the fifth bit of element 32g + l
+ * in bit g of qh[l]. */
+int kq_dequant_q5k(kq_ctx* ctx, uint64_t out, uint64_t w, uint64_t nblocks, kq_stream stream);
 
 /* Writes synthetic blocks [block0, block0 + nblocks) of the tensor whose stream key is `key`
  * at w (w points at block0): counter-based splitmix64, so any range is reproducible on the CPU.
@@ -165,6 +169,9 @@ int kq_dequant_q6k(kq_ctx* ctx, uint64_t out, uint64_t w, uint64_t nblocks, kq_s
 int kq_fill_q4k(kq_ctx* ctx, uint64_t w, uint64_t block0, uint64_t nblocks, uint64_t key,
                 kq_stream stream);
 int kq_fill_q6k(kq_ctx* ctx, uint64_t w, uint64_t block0, uint64_t nblocks, uint64_t key,
+                kq_stream stream);
+/* Q5_K: scale/qh/quant bytes uniform, d and dmin = fp16(uniform[2^-11, 2^-7]). */
+int kq_fill_q5k(kq_ctx* ctx, uint64_t w, uint64_t block0, uint64_t nblocks, uint64_t key,
                 kq_stream stream);
 
 /* The stream key of tensor `tensor` under `seed` (host function; the same as the oracle's). */

@@ -33,6 +33,7 @@ KQ_E_DEVICE = 1003
 KQ_E_COMM = 1004
 
 TYPE_Q4_K = 12
+TYPE_Q5_K = 13
 TYPE_Q6_K = 14
 PROLOGUE_NONE = 0
 PROLOGUE_RMSNORM = 1
@@ -47,13 +48,14 @@ FLAG_WARP_MMA = 16
 
 Q4K_BYTES = 144
 Q6K_BYTES = 210
+Q5K_BYTES = 176
 QK = 256
 
 # Every symbol include/kq.h declares (tests check the library exports each).
 EXPORTS = (
     "kq_ctx_create", "kq_ctx_destroy", "kq_last_error", "kq_ctx_info", "kq_device_error",
     "kq_matvec_q4k", "kq_matvec_q6k", "kq_matvec", "kq_matvec_host", "kq_dequant_q4k", "kq_dequant_q6k",
-    "kq_fill_q4k", "kq_fill_q6k", "kq_stream_key", "kq_matvec_q4k_noalloc",
+    "kq_fill_q4k", "kq_fill_q6k", "kq_dequant_q5k", "kq_fill_q5k", "kq_stream_key", "kq_matvec_q4k_noalloc",
     "kq_matvec_push", "kq_wait_counter", "kq_peer_alloc", "kq_peer_open", "kq_peer_close", "kq_peer_free",
     "kq_gguf_open", "kq_gguf_close", "kq_gguf_tensor_count", "kq_gguf_tensor_at", "kq_gguf_find",
     "kq_gguf_meta_int", "kq_gguf_meta_str",
@@ -123,9 +125,9 @@ def lib() -> ctypes.CDLL:
         getattr(L, name).argtypes = [vp, u64, u64, u64, u32, u32, u32, vp]
     L.kq_matvec.argtypes = [vp, ctypes.POINTER(KqMatvecDesc), vp]
     L.kq_matvec_host.argtypes = [vp, ctypes.POINTER(KqMatvecDesc), vp, vp, vp]
-    for name in ("kq_dequant_q4k", "kq_dequant_q6k"):
+    for name in ("kq_dequant_q4k", "kq_dequant_q5k", "kq_dequant_q6k"):
         getattr(L, name).argtypes = [vp, u64, u64, u64, vp]
-    for name in ("kq_fill_q4k", "kq_fill_q6k"):
+    for name in ("kq_fill_q4k", "kq_fill_q5k", "kq_fill_q6k"):
         getattr(L, name).argtypes = [vp, u64, u64, u64, u64, vp]
     L.kq_stream_key.argtypes = [u64, u64]
     L.kq_stream_key.restype = u64
@@ -276,7 +278,7 @@ class Kernels:
                ldy: int = 0, prologue: int = PROLOGUE_NONE, epilogue: int = EPILOGUE_NONE,
                eps: float = 0.0, pair_scale: float = 1.0, flags: int = 0, stream=None) -> None:
         """The general matvec (``kq_matvec``); qtype is 4/6 or TYPE_Q4_K/TYPE_Q6_K."""
-        t = {4: TYPE_Q4_K, 6: TYPE_Q6_K}.get(qtype, qtype)
+        t = {4: TYPE_Q4_K, 5: TYPE_Q5_K, 6: TYPE_Q6_K}.get(qtype, qtype)
         d = KqMatvecDesc(type=t, rows=rows, k=k, batch=batch, y=_addr(y), w=_addr(w), x=_addr(x),
                          ldx=ldx, ldy=ldy, prologue=prologue, epilogue=epilogue, eps=eps,
                          pair_scale=pair_scale, flags=flags, reserved=0)
@@ -288,7 +290,7 @@ class Kernels:
                     flags: int = 0, stream=None) -> None:
         """``kq_matvec_host``: x and y are host arrays (torch CPU tensors, pinned for asynchronous
         copies, or numpy arrays), w is on the device; synchronise ``stream`` before reading y."""
-        t = {4: TYPE_Q4_K, 6: TYPE_Q6_K}.get(qtype, qtype)
+        t = {4: TYPE_Q4_K, 5: TYPE_Q5_K, 6: TYPE_Q6_K}.get(qtype, qtype)
         d = KqMatvecDesc(type=t, rows=rows, k=k, batch=batch, y=0, w=_addr(w), x=0, ldx=ldx,
                          ldy=ldy, prologue=prologue, epilogue=epilogue, eps=eps,
                          pair_scale=pair_scale, flags=flags, reserved=0)
@@ -297,12 +299,12 @@ class Kernels:
 
     def dequant(self, qtype: int, out, w, nblocks: int, stream=None) -> None:
         """Bit-exact decode of ``nblocks`` blocks into f32 (verification kernel)."""
-        fn = lib().kq_dequant_q4k if qtype in (4, TYPE_Q4_K) else lib().kq_dequant_q6k
+        fn = {4: lib().kq_dequant_q4k, 5: lib().kq_dequant_q5k, 6: lib().kq_dequant_q6k}[_qt(qtype)]
         _check(fn(self._ctx, _addr(out), _addr(w), nblocks, _stream(stream)), "kq_dequant")
 
     def fill(self, qtype: int, w, block0: int, nblocks: int, key: int, stream=None) -> None:
         """Synthetic blocks [block0, block0 + nblocks) of the keyed tensor, written at w."""
-        fn = lib().kq_fill_q4k if qtype in (4, TYPE_Q4_K) else lib().kq_fill_q6k
+        fn = {4: lib().kq_fill_q4k, 5: lib().kq_fill_q5k, 6: lib().kq_fill_q6k}[_qt(qtype)]
         _check(fn(self._ctx, _addr(w), block0, nblocks, key & (2**64 - 1), _stream(stream)), "kq_fill")
 
     def matvec_q4k_noalloc(self, y, w, x, rows: int, k: int, batch: int = 1, stream=None) -> None:
@@ -316,7 +318,7 @@ class Kernels:
                     pair_scale: float = 1.0, flags: int = 0, stream=None) -> None:
         """Batch-1 matvec whose epilogue also stores rows [0, push.push_rows) into every rank's
         full vector and counts them there (``kq_matvec_push``)."""
-        t = {4: TYPE_Q4_K, 6: TYPE_Q6_K}.get(qtype, qtype)
+        t = {4: TYPE_Q4_K, 5: TYPE_Q5_K, 6: TYPE_Q6_K}.get(qtype, qtype)
         d = KqMatvecDesc(type=t, rows=rows, k=k, batch=1, y=_addr(y), w=_addr(w), x=_addr(x),
                          ldx=0, ldy=0, prologue=prologue, epilogue=epilogue, eps=eps,
                          pair_scale=pair_scale, flags=flags, reserved=0)
@@ -360,8 +362,13 @@ class DeviceArray:
                                          "version": 3, "strides": None, "stream": None}
 
 
+def _qt(qtype: int) -> int:
+    """4, 5 or 6 for a type given as 4/5/6 or as its GGML number."""
+    return {TYPE_Q4_K: 4, TYPE_Q5_K: 5, TYPE_Q6_K: 6}.get(qtype, qtype)
+
+
 def block_bytes(qtype: int) -> int:
-    return Q4K_BYTES if qtype in (4, TYPE_Q4_K) else Q6K_BYTES
+    return {4: Q4K_BYTES, 5: Q5K_BYTES, 6: Q6K_BYTES}[_qt(qtype)]
 
 
 def matrix_bytes(qtype: int, rows: int, k: int) -> int:

@@ -4,10 +4,12 @@
 // The dequantiser computes every weight in the canonical order of the CPU decode,
 //   Q4_K: w = (f32(d) * f32(sc)) * f32(q) - f32(dmin) * f32(m)
 //   Q6_K: w = (f32(d) * f32(scale)) * f32(q - 32)
+//   Q5_K: as Q4_K, q = nibble | (fifth bit << 4), the fifth bit of element 32g + l in bit g of
+//         qh[l]
 // with __fmul_rn / __fsub_rn so that nothing contracts into an FMA, the discipline of
 // fxeqxmulfx/kernite's scalar references (examples/matmul/src/reference.rs:1-10).
 //
-// The generator reproduces the oracle's kqo_fill_q4k / kqo_fill_q6k byte for byte: splitmix64
+// The generator reproduces the oracle's kqo_fill_q4k / q5k / q6k byte for byte: splitmix64
 // output number i of the tensor's keyed stream, integer work plus one binary32 multiply, one
 // add and a round-to-nearest-even narrowing to fp16 per scale.
 #include <cuda_runtime.h>
@@ -84,6 +86,25 @@ __global__ void fill_q6k_kernel(uint8_t* w, uint64_t b0, uint64_t n, uint64_t ke
   }
 }
 
+__global__ void fill_q5k_kernel(uint8_t* w, uint64_t b0, uint64_t n, uint64_t key) {
+  for (uint64_t i = blockIdx.x * uint64_t(blockDim.x) + threadIdx.x; i < n;
+       i += uint64_t(gridDim.x) * blockDim.x) {
+    const uint64_t b = b0 + i;
+    uint64_t words[22];
+#pragma unroll
+    for (int t = 0; t < 22; ++t) words[t] = splitmix_at(key, 24 * b + t);
+    const uint32_t d = uniform_fp16(splitmix_at(key, 24 * b + 22), 0x1p-11f, 15.0f * 0x1p-11f);
+    const uint32_t m = uniform_fp16(splitmix_at(key, 24 * b + 23), 0x1p-11f, 15.0f * 0x1p-11f);
+    words[0] = (words[0] & ~0xffffffffull) | d | (uint64_t(m) << 16);
+    uint4* out = reinterpret_cast<uint4*>(w + i * kQ5KBytes);  // 176 = 11 x 16, w 16-aligned
+#pragma unroll
+    for (int t = 0; t < 11; ++t) {
+      out[t] = make_uint4(static_cast<uint32_t>(words[2 * t]), static_cast<uint32_t>(words[2 * t] >> 32),
+                          static_cast<uint32_t>(words[2 * t + 1]),
+                          static_cast<uint32_t>(words[2 * t + 1] >> 32));
+    }
+  }
+}
 
 // One thread per weight.
 __global__ void dequant_q4k_kernel(float* out, const uint8_t* w, uint64_t nblocks) {
@@ -134,6 +155,32 @@ __global__ void dequant_q6k_kernel(float* out, const uint8_t* w, uint64_t nblock
   }
 }
 
+__global__ void dequant_q5k_kernel(float* out, const uint8_t* w, uint64_t nblocks) {
+  const uint64_t total = nblocks * kQK;
+  for (uint64_t t = blockIdx.x * uint64_t(blockDim.x) + threadIdx.x; t < total;
+       t += uint64_t(gridDim.x) * blockDim.x) {
+    const uint8_t* blk = w + (t / kQK) * kQ5KBytes;
+    const uint32_t e = static_cast<uint32_t>(t % kQK);
+    const uint32_t j = e / 32, c = e / 64, l = e % 32;
+    const uint8_t* s = blk + 4;
+    uint32_t sc, m;
+    if (j < 4) {
+      sc = s[j] & 63u;
+      m = s[j + 4] & 63u;
+    } else {
+      sc = (s[j + 4] & 15u) | ((s[j - 4] >> 6) << 4);
+      m = (s[j + 4] >> 4) | ((s[j] >> 6) << 4);
+    }
+    const uint32_t byte = blk[48 + 32 * c + l];
+    const uint32_t q = ((j & 1) ? (byte >> 4) : (byte & 15u)) | (((blk[16 + l] >> j) & 1u) << 4);
+    const float d = h2f(blk[0] | (blk[1] << 8));
+    const float dmin = h2f(blk[2] | (blk[3] << 8));
+    const float ds = __fmul_rn(d, static_cast<float>(sc));
+    const float dm = __fmul_rn(dmin, static_cast<float>(m));
+    out[t] = __fsub_rn(__fmul_rn(ds, static_cast<float>(q)), dm);
+  }
+}
+
 uint32_t grid_for(uint64_t work, uint32_t threads, int sm_count) {
   const uint64_t want = (work + threads - 1) / threads;
   const uint64_t cap = uint64_t(sm_count) * 16;
@@ -166,7 +213,7 @@ int wait_counter(kq_ctx* ctx, uint64_t counter, uint64_t epoch, uint64_t mul, ui
 }
 
 int dequant(kq_ctx* ctx, int type, uint64_t out, uint64_t w, uint64_t nblocks, cudaStream_t s) {
-  const char* call = type == 4 ? "kq_dequant_q4k" : "kq_dequant_q6k";
+  const char* call = type == 4 ? "kq_dequant_q4k" : type == 5 ? "kq_dequant_q5k" : "kq_dequant_q6k";
   if (nblocks == 0) return KQ_OK;
   if (!out || !w) return fail(KQ_E_INVALID, call, "null pointer");
   if (out % 4 || w % 2) return fail(KQ_E_INVALID, call, "out must be 4-byte and w 2-byte aligned");
@@ -174,6 +221,9 @@ int dequant(kq_ctx* ctx, int type, uint64_t out, uint64_t w, uint64_t nblocks, c
   const uint32_t grid = grid_for(nblocks * kQK, threads, ctx->sm_count);
   if (type == 4)
     dequant_q4k_kernel<<<grid, threads, 0, s>>>(reinterpret_cast<float*>(out),
+                                                 reinterpret_cast<const uint8_t*>(w), nblocks);
+  else if (type == 5)
+    dequant_q5k_kernel<<<grid, threads, 0, s>>>(reinterpret_cast<float*>(out),
                                                  reinterpret_cast<const uint8_t*>(w), nblocks);
   else
     dequant_q6k_kernel<<<grid, threads, 0, s>>>(reinterpret_cast<float*>(out),
@@ -185,15 +235,17 @@ int dequant(kq_ctx* ctx, int type, uint64_t out, uint64_t w, uint64_t nblocks, c
 
 int fill(kq_ctx* ctx, int type, uint64_t w, uint64_t block0, uint64_t nblocks, uint64_t key,
          cudaStream_t s) {
-  const char* call = type == 4 ? "kq_fill_q4k" : "kq_fill_q6k";
+  const char* call = type == 4 ? "kq_fill_q4k" : type == 5 ? "kq_fill_q5k" : "kq_fill_q6k";
   if (nblocks == 0) return KQ_OK;
   if (!w) return fail(KQ_E_INVALID, call, "null pointer");
-  if (type == 4 && w % 16) return fail(KQ_E_INVALID, call, "w must be 16-byte aligned");
+  if (type != 6 && w % 16) return fail(KQ_E_INVALID, call, "w must be 16-byte aligned");
   if (type == 6 && w % 2) return fail(KQ_E_INVALID, call, "w must be 2-byte aligned");
   const uint32_t threads = 128;
   const uint32_t grid = grid_for(nblocks, threads, ctx->sm_count);
   if (type == 4)
     fill_q4k_kernel<<<grid, threads, 0, s>>>(reinterpret_cast<uint8_t*>(w), block0, nblocks, key);
+  else if (type == 5)
+    fill_q5k_kernel<<<grid, threads, 0, s>>>(reinterpret_cast<uint8_t*>(w), block0, nblocks, key);
   else
     fill_q6k_kernel<<<grid, threads, 0, s>>>(reinterpret_cast<uint8_t*>(w), block0, nblocks, key);
   const cudaError_t e = cudaGetLastError();

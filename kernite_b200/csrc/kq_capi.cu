@@ -259,6 +259,21 @@ int kq_dequant_q6k(kq_ctx* ctx, uint64_t out, uint64_t w, uint64_t nblocks, kq_s
   return kq::dequant(ctx, 6, out, w, nblocks, static_cast<cudaStream_t>(stream));
 }
 
+int kq_dequant_q5k(kq_ctx* ctx, uint64_t out, uint64_t w, uint64_t nblocks, kq_stream stream) {
+  if (!ctx) return fail(KQ_E_INVALID, "kq_dequant_q5k", "null ctx");
+  int rc = kq::enter(ctx);
+  if (rc) return rc;
+  return kq::dequant(ctx, 5, out, w, nblocks, static_cast<cudaStream_t>(stream));
+}
+
+int kq_fill_q5k(kq_ctx* ctx, uint64_t w, uint64_t block0, uint64_t nblocks, uint64_t key,
+                kq_stream stream) {
+  if (!ctx) return fail(KQ_E_INVALID, "kq_fill_q5k", "null ctx");
+  int rc = kq::enter(ctx);
+  if (rc) return rc;
+  return kq::fill(ctx, 5, w, block0, nblocks, key, static_cast<cudaStream_t>(stream));
+}
+
 int kq_fill_q4k(kq_ctx* ctx, uint64_t w, uint64_t block0, uint64_t nblocks, uint64_t key,
                 kq_stream stream) {
   if (!ctx) return fail(KQ_E_INVALID, "kq_fill_q4k", "null ctx");

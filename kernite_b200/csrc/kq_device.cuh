@@ -12,6 +12,7 @@ namespace kq {
 constexpr int kQK = 256;
 constexpr int kQ4KBytes = 144;  // fp16 d, fp16 dmin, u8 scales[12], u8 qs[128]
 constexpr int kQ6KBytes = 210;  // u8 ql[128], u8 qh[64], i8 scales[16], fp16 d
+constexpr int kQ5KBytes = 176;  // fp16 d, fp16 dmin, u8 scales[12], u8 qh[32], u8 qs[128]
 
 // Device error word codes: a bounded wait that gives up writes one (first writer wins) and its
 // kernel returns instead of hanging; kq_device_error() reads and clears it.

@@ -613,10 +613,13 @@ int matvec(kq_ctx* ctx, const kq_matvec_desc& d, cudaStream_t stream, const kq_p
   int qt;
   if (d.type == KQ_TYPE_Q4_K)
     qt = 4;
+  else if (d.type == KQ_TYPE_Q5_K)
+    qt = 5;
   else if (d.type == KQ_TYPE_Q6_K)
     qt = 6;
   else
-    return fail(KQ_E_INVALID, call, "type must be KQ_TYPE_Q4_K (12) or KQ_TYPE_Q6_K (14)");
+    return fail(KQ_E_INVALID, call,
+                "type must be KQ_TYPE_Q4_K (12), KQ_TYPE_Q5_K (13) or KQ_TYPE_Q6_K (14)");
   if (d.rows == 0 || d.k == 0 || d.k % kQK != 0)
     return fail(KQ_E_INVALID, call,
                 "rows must be > 0 and k a positive multiple of 256 (rows " +
@@ -654,6 +657,11 @@ int matvec(kq_ctx* ctx, const kq_matvec_desc& d, cudaStream_t stream, const kq_p
         return fail(KQ_E_INVALID, call, "push target " + std::to_string(p) + " is null or misaligned");
     if (push->wait_counter && (!push->epoch || push->wait_counter % 8 || push->epoch % 8))
       return fail(KQ_E_INVALID, call, "wait_counter needs an 8-byte aligned epoch and counter");
+  }
+  if (qt == 5) {  // Q5_K: the warp-MMA kernel's integer path only
+    if (push || d.batch != 1 || (d.flags & (KQ_FLAG_TENSOR_CORES | KQ_FLAG_CUDA_CORES)))
+      return fail(KQ_E_UNSUPPORTED, call, "Q5_K is served at batch 1 by the warp-MMA kernel");
+    return warpmma_matvec(ctx, d, ldx, ldy, stream);
   }
   if (d.flags & KQ_FLAG_WARP_MMA) {
     if (push || !warpmma_supports(d))

@@ -426,29 +426,53 @@ __device__ __forceinline__ void q6_block(uint32_t ag, uint32_t ah, uint32_t c, u
 // the zero region), so column n sums sub-block n. Then y += d sum sc_n D_n - dmin sum m_n X_n.
 //  sel_sc, m_lo, m_hi, sh_m: the thread's 6-bit scale/min unpack; X: the sums of x (limb units)
 //  over sub-blocks 2c, 2c+1; u0: the block's 2^-shift of x.
+// Q5K: the Q5_K block (176 bytes: qh[32] at 16, qs at 48), whose fifth bit of element 32g + l is
+// bit g of qh[l]: the thread's elements 64c + 32o + b take bit 2c + o of qh[b], and qh word j
+// holds the same byte positions b as qs word j of the chunk.
+template <bool Q5K = false>
 __device__ __forceinline__ void q4i8_block(uint32_t ag, uint32_t ah, uint32_t c, uint32_t b0,
                                            uint32_t b1, uint32_t k28, uint32_t sel_sc,
                                            uint32_t m_lo, uint32_t m_hi, uint32_t sh_m, float2 X,
                                            float u0, float (&yacc)[2][2]) {
+  constexpr uint32_t kQs = Q5K ? 48 : 16;
   int acc[3][4];
   const uint4 hg = lds_v4(ag), hh = lds_v4(ah);
   uint32_t Wg[8], Wh[8];
   {
-    const uint4 g0 = lds_v4(ag + 16 + 32 * c), g1 = lds_v4(ag + 32 + 32 * c);
-    const uint4 h0 = lds_v4(ah + 16 + 32 * c), h1 = lds_v4(ah + 32 + 32 * c);
+    const uint4 g0 = lds_v4(ag + kQs + 32 * c), g1 = lds_v4(ag + kQs + 16 + 32 * c);
+    const uint4 h0 = lds_v4(ah + kQs + 32 * c), h1 = lds_v4(ah + kQs + 16 + 32 * c);
     Wg[0] = g0.x; Wg[1] = g0.y; Wg[2] = g0.z; Wg[3] = g0.w;
     Wg[4] = g1.x; Wg[5] = g1.y; Wg[6] = g1.z; Wg[7] = g1.w;
     Wh[0] = h0.x; Wh[1] = h0.y; Wh[2] = h0.z; Wh[3] = h0.w;
     Wh[4] = h1.x; Wh[5] = h1.y; Wh[6] = h1.z; Wh[7] = h1.w;
   }
+  // Q5_K: the thread's two fifth bits of each byte position at bits 0 (o = 0) and 1 (o = 1)
+  uint32_t Vg[8], Vh[8];
+  if constexpr (Q5K) {
+    const uint4 p0 = lds_v4(ag + 16), p1 = lds_v4(ag + 32);
+    const uint4 q0 = lds_v4(ah + 16), q1 = lds_v4(ah + 32);
+    const uint32_t pg[8] = {p0.x, p0.y, p0.z, p0.w, p1.x, p1.y, p1.z, p1.w};
+    const uint32_t ph[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      Vg[j] = (pg[j] >> (2 * c)) & 0x03030303u;
+      Vh[j] = (ph[j] >> (2 * c)) & 0x03030303u;
+    }
+  }
+  // nibble o of word w, with (Q5_K) the fifth bit from v moved to bit 4 of each byte
+  auto quant = [&](uint32_t w, uint32_t v, int o) {
+    const uint32_t nib = (o ? mulhi(w, k28) : w) & 0x0F0F0F0Fu;
+    if constexpr (Q5K) return lop_and_or(o ? (v << 3) : (v << 4), 0x10101010u, nib);
+    return nib;
+  };
 #pragma unroll
   for (int o = 0; o < 2; ++o)
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
-      const uint32_t a0 = (o ? mulhi(Wg[2 * i], k28) : Wg[2 * i]) & 0x0F0F0F0Fu;
-      const uint32_t a1 = (o ? mulhi(Wh[2 * i], k28) : Wh[2 * i]) & 0x0F0F0F0Fu;
-      const uint32_t a2 = (o ? mulhi(Wg[2 * i + 1], k28) : Wg[2 * i + 1]) & 0x0F0F0F0Fu;
-      const uint32_t a3 = (o ? mulhi(Wh[2 * i + 1], k28) : Wh[2 * i + 1]) & 0x0F0F0F0Fu;
+      const uint32_t a0 = quant(Wg[2 * i], Q5K ? Vg[2 * i] : 0u, o);
+      const uint32_t a1 = quant(Wh[2 * i], Q5K ? Vh[2 * i] : 0u, o);
+      const uint32_t a2 = quant(Wg[2 * i + 1], Q5K ? Vg[2 * i + 1] : 0u, o);
+      const uint32_t a3 = quant(Wh[2 * i + 1], Q5K ? Vh[2 * i + 1] : 0u, o);
       const uint32_t bb = (o ? b1 : b0) + 24 * i;
 #pragma unroll
       for (int l = 0; l < 3; ++l) {
@@ -491,7 +515,7 @@ __device__ __forceinline__ void q4i8_block(uint32_t ag, uint32_t ah, uint32_t c,
 // columns separating sub-blocks.
 template <int QT, int NT, bool HILO, bool I8>
 __global__ void __launch_bounds__((kMaxWarps + 1) * 32, 1) warpmma_kernel(const WarpMmaArgs a) {
-  constexpr uint32_t kBlk = QT == 4 ? kQ4KBytes : kQ6KBytes;
+  constexpr uint32_t kBlk = QT == 4 ? kQ4KBytes : QT == 5 ? kQ5KBytes : kQ6KBytes;
   constexpr int kTarget = QT == 4 ? 10 : 14;  // x is scaled so that max |x| < 2^kTarget
 
   extern __shared__ __align__(128) uint8_t smem[];
@@ -844,7 +868,7 @@ __global__ void __launch_bounds__((kMaxWarps + 1) * 32, 1) warpmma_kernel(const 
   // B-fragment table offsets of this thread; lanes without a column read the zero region
   const bool tab_on = QT == 4 ? (g < a.ncol) : ((g & 3) == c);
   const uint32_t tab_lane = QT == 4 ? g * kNStride + c * 8 : (c * 2 + (g >> 2)) * 8;
-  const uint32_t zero_s = ring_s + a.zero_off + (QT == 4 ? c * 8 : 0);
+  const uint32_t zero_s = ring_s + a.zero_off + (QT != 6 ? c * 8 : 0);
   const uint32_t k24 = (1u << 24) << a.zero;              // >> 8
   const uint32_t k28 = (1u << 28) << a.zero;              // >> 4
   // I8 Q6_K: the shift of the thread's qh pairs (see q6i8_half), and 16 kept opaque
@@ -1094,7 +1118,7 @@ __global__ void __launch_bounds__((kMaxWarps + 1) * 32, 1) warpmma_kernel(const 
   }
   // The same for Q4_K (144-byte blocks: every block starts on a 16-byte boundary, one loop):
   // the block's table addresses, scale of x and (integer path) sums of x are warp constants.
-  if constexpr (QT == 4) {
+  if constexpr (QT == 4 || QT == 5) {
     if (a.fixed_blocks) {
       const uint32_t kb = warp;
       float u0, u1 = 0.f;
@@ -1122,7 +1146,7 @@ __global__ void __launch_bounds__((kMaxWarps + 1) * 32, 1) warpmma_kernel(const 
         if (!__any_sync(0xffffffffu, !ok)) {
           const uint32_t slot = ring_s + s * a.slot_bytes;
           if constexpr (I8)
-            q4i8_block(slot + off_g, slot + off_h, c, b0, b1, k28, sel_sc, m_lo, m_hi, sh_m, X, u0,
+            q4i8_block<QT == 5>(slot + off_g, slot + off_h, c, b0, b1, k28, sel_sc, m_lo, m_hi, sh_m, X, u0,
                        yacc);
           else
             q4f16_block(slot + off_g, slot + off_h, tab_t, bm_at, u0, u1);
@@ -1179,13 +1203,13 @@ __global__ void __launch_bounds__((kMaxWarps + 1) * 32, 1) warpmma_kernel(const 
         // hold 4 + 4 quants of one sub-block (8 consecutive elements of it per thread), B the
         // three limbs of the same 8 elements of x, read by the 4 lanes of the column's group.
         const float u0 = ublk[kb];
-        if constexpr (QT == 4) {
+        if constexpr (QT == 4 || QT == 5) {
           const uint32_t tc = table_s + (kb * 32 + 8 * c) * 24;
           const uint32_t b0 = g == 2 * c ? tc : zero_s;
           const uint32_t b1 = g == 2 * c + 1 ? tc + 4 * 24 : zero_s;
           const float2 X = *reinterpret_cast<const float2*>(
               reinterpret_cast<const uint8_t*>(base) + a.mtable_off + (kb * 8 + 2 * c) * 4);
-          q4i8_block(ag, ah, c, b0, b1, k28, sel_sc, m_lo, m_hi, sh_m, X, u0, yacc);
+          q4i8_block<QT == 5>(ag, ah, c, b0, b1, k28, sel_sc, m_lo, m_hi, sh_m, X, u0, yacc);
         } else {
           // Q6_K: per half, 4 steps: s < 2 the low-nibble group (sub-block c, words 2(s&1),
           // 2(s&1)+1 of the thread's 16 ql bytes), s >= 2 the high-nibble group (sub-block c+4)
@@ -1284,7 +1308,7 @@ Variant variant() {
 
 const Variant kVariants[] = {variant<4, 1, true>(), variant<4, 2, true>(), variant<4, 1, false>(),
                              variant<6, 1, false>(), variant<4, 1, false, true>(),
-                             variant<6, 1, false, true>()};
+                             variant<6, 1, false, true>(), variant<5, 1, false, true>()};
 
 }  // namespace
 
@@ -1299,7 +1323,7 @@ int warpmma_prepare(kq_ctx* ctx) {
 
 bool warpmma_supports(const kq_matvec_desc& d) {
   if (d.type == KQ_TYPE_Q4_K) return d.batch >= 1 && d.batch <= 8;
-  if (d.type == KQ_TYPE_Q6_K) return d.batch == 1;
+  if (d.type == KQ_TYPE_Q6_K || d.type == KQ_TYPE_Q5_K) return d.batch == 1;
   return false;
 }
 
@@ -1307,14 +1331,16 @@ int warpmma_matvec(kq_ctx* ctx, const kq_matvec_desc& d, uint64_t ldx, uint64_t 
                    cudaStream_t stream) {
   const char* call = "kq_matvec";
   const bool q4 = d.type == KQ_TYPE_Q4_K;
-  const uint32_t blk = q4 ? kQ4KBytes : kQ6KBytes;
+  const bool q5 = d.type == KQ_TYPE_Q5_K;  // Q4_K's layout plus qh: the Q4_K forms, integer only
+  const bool q45 = q4 || q5;
+  const uint32_t blk = q4 ? kQ4KBytes : q5 ? kQ5KBytes : kQ6KBytes;
   const uint32_t nb = d.k / kQK;
   const uint64_t rb = uint64_t(nb) * blk;
   // tile: 16 row segments of up to kc super-blocks (kc = the consumer warps), one bulk copy
   // each (the 16-byte-aligned superset, so up to 30 bytes more), at a pitch whose residue mod 128
   // makes the consumers' 16-byte loads free of bank conflicts: 16 for Q4_K (rows g, g+1
   // interleave their 32-byte strides), 64 for Q6_K (rows g, g+1 take the two halves of 128 B)
-  const uint32_t target = q4 ? 16u : 64u;
+  const uint32_t target = q45 ? 16u : 64u;
   auto slot_for = [&](uint32_t kc, uint32_t& seg_out) {
     uint32_t seg_ = ((kc * blk + 30 + 15) / 16) * 16;
     while (seg_ % 128 != target) seg_ += 16;
@@ -1348,13 +1374,16 @@ int warpmma_matvec(kq_ctx* ctx, const kq_matvec_desc& d, uint64_t ldx, uint64_t 
   // batch 1: the integer kernel, whose table is x's three byte limbs (3 bytes per element) plus
   // per-sub-block sums (Q6_K: the MMAs' C init, Q4_K: the min term's sums of x)
   const uint64_t i8_table = uint64_t(nb) * kQK * 3;
-  const uint64_t i8_mtable = q4 ? uint64_t(nb) * 8 * 4 : uint64_t(nb) * 2 * 3 * 8 * 4;
-  const bool want_i8 = (d.flags & kFlagAltBatch1) == 0;
+  const uint64_t i8_mtable = q45 ? uint64_t(nb) * 8 * 4 : uint64_t(nb) * 2 * 3 * 8 * 4;
+  const bool want_i8 = (d.flags & kFlagAltBatch1) == 0 || q5;
   if (d.batch == 1 && want_i8 &&
       i8_table + i8_mtable + fixed_min <= uint64_t(ctx->max_smem)) {
-    mode = q4 ? 4 : 5, ncol = 8;
+    mode = q4 ? 4 : q5 ? 6 : 5, ncol = 8;
     table_bytes = i8_table;
     mtable_bytes = i8_mtable;
+  } else if (q5) {
+    return fail(KQ_E_UNSUPPORTED, call,
+                "k " + std::to_string(d.k) + " does not fit the Q5_K warp-MMA kernel's shared memory");
   } else if (q4) {
     auto sizes = [&](uint32_t nt_, uint32_t ncol_) {
       table_bytes = uint64_t(nb) * nt_ * ncol_ * kNStride;
@@ -1392,8 +1421,8 @@ int warpmma_matvec(kq_ctx* ctx, const kq_matvec_desc& d, uint64_t ldx, uint64_t 
   // turns are 3% faster for Q4_K up to batch 4 (more warps hide more latency), 2% slower at
   // batch 8 (the two-tile MMAs' registers).
   const bool rows16 = rb % 16 == 0;
-  const bool fixed_ok = (q4 || mode == 5) && nkt == 1 && seg == 0 && rows16;
-  const bool turns = fixed_ok ? false : q4 ? d.batch <= 4 : !rows16;
+  const bool fixed_ok = (q45 || mode == 5) && nkt == 1 && seg == 0 && rows16;
+  const bool turns = fixed_ok ? false : q45 ? d.batch <= 4 : !rows16;
   const bool per_block = !turns != ((d.flags & kFlagWarpPerBlock) != 0);
   const uint32_t nw = per_block ? nwc : kMaxWarps;
   const uint32_t rb128 = static_cast<uint32_t>(rb % 128);

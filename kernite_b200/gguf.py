@@ -3,7 +3,7 @@
 
 A GGUF tensor stores a matrix exactly as ``kq_matvec`` takes it: ``shape`` is GGUF's dimension
 order (``shape[0]`` = k elements per row, ``shape[1]`` = rows) and the bytes are the rows back to
-back, so a Q4_K / Q6_K tensor goes to the device as it is::
+back, so a Q4_K / Q5_K / Q6_K tensor goes to the device as it is::
 
     with GGUFFile("model.gguf") as f:
         t = f.tensor("blk.0.attn_q.weight")
@@ -17,10 +17,10 @@ from dataclasses import dataclass
 
 import numpy as np
 
-from . import Error, KqGgufTensor, TYPE_Q4_K, TYPE_Q6_K, _check, lib
+from . import Error, KqGgufTensor, TYPE_Q4_K, TYPE_Q5_K, TYPE_Q6_K, _check, lib
 
 # GGML type numbers the library's matvec takes, by name
-QTYPES = {TYPE_Q4_K: 4, TYPE_Q6_K: 6}
+QTYPES = {TYPE_Q4_K: 4, TYPE_Q5_K: 5, TYPE_Q6_K: 6}
 
 
 @dataclass
@@ -29,16 +29,16 @@ class Tensor:
     the file is open)."""
 
     name: str
-    type: int          # GGML type number (12 = Q4_K, 14 = Q6_K, 0 = F32, ...)
+    type: int          # GGML type number (12 = Q4_K, 13 = Q5_K, 14 = Q6_K, 0 = F32, ...)
     shape: tuple       # GGUF order: shape[0] innermost
     offset: int        # byte offset of the data in the file
     data: np.ndarray   # uint8 view; empty when the reader does not know the type's block size
 
     @property
     def qtype(self) -> int:
-        """4 or 6 for a Q4_K / Q6_K tensor kq_matvec can multiply, else raises."""
+        """4, 5 or 6 for a Q4_K / Q5_K / Q6_K tensor kq_matvec can multiply, else raises."""
         if self.type not in QTYPES:
-            raise Error("gguf", f"tensor {self.name} has GGML type {self.type}, not Q4_K/Q6_K")
+            raise Error("gguf", f"tensor {self.name} has GGML type {self.type}, not Q4_K/Q5_K/Q6_K")
         return QTYPES[self.type]
 
     @property
