@@ -45,6 +45,7 @@ WORKLOADS = {
     "q6k_head": dict(qtype=6, rows=32000, k=4096, batch=1, source="BASELINE configs[1]"),
     "q4k": dict(qtype=4, rows=4096, k=4096, batch=1, source="BASELINE configs[0]"),
     "sweep": dict(qtype=4, rows=14336, k=4096, batch=None, source="BASELINE configs[3]"),
+    "q5k": dict(qtype=5, rows=14336, k=4096, batch=1, source="next k-quant type, sweep shape"),
 }
 
 
@@ -161,8 +162,7 @@ def cpu_matvec_timing(qtype, Wh, x, rows, K, seconds, threads):
     """Repeats the CPU matvec on a row sample until `seconds` pass; returns (GB/s, sample)."""
     import oracle
 
-    bb = 144 if qtype == 4 else 210
-    rb = (K // 256) * bb
+    rb = (K // 256) * oracle.block_bytes(qtype)
     t0 = time.perf_counter()
     oracle.matvec_cpu(qtype, Wh, x, rows, K, threads)
     one = time.perf_counter() - t0
@@ -193,8 +193,7 @@ def run_reference(args):
     w = workload_shape(args)
     qtype, rows, K, batch = w["qtype"], w["rows"], w["k"], w["batch"]
     threads = HOST_THREADS
-    bb = 144 if qtype == 4 else 210
-    rb = (K // 256) * bb
+    rb = (K // 256) * oracle.block_bytes(qtype)
     Wh = oracle.fill(qtype, oracle.stream_key(2026, qtype), 0, rows * K // 256)
     x = np.random.default_rng(0).standard_normal((batch, K), dtype=np.float32)
     t0 = time.perf_counter()

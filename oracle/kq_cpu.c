@@ -1,5 +1,5 @@
 /*
- * kq_cpu.c -- the CPU baseline: a multithreaded AVX2 + FMA (x86-64-v3) Q4_K / Q6_K matvec.
+ * kq_cpu.c -- the CPU baseline: a multithreaded AVX2 + FMA (x86-64-v3) Q4_K / Q5_K / Q6_K matvec.
  * TEST / BASELINE INFRASTRUCTURE ONLY (see kq_oracle.h): bench.py times it beside the GPU
  * numbers; the product never calls it.
  *
@@ -9,7 +9,7 @@
  * pinned to one core, as kernite_cpu's Grid::on places threads (GUIDE.md:512-523).
  *
  * Algebra per sub-block j of 32 (Q4_K) or 16 (Q6_K) weights:
- *   sum_k w_k x_k = d*sc_j * sum_k q_k x_k - dmin*m_j * sum_k x_k        (Q4_K)
+ *   sum_k w_k x_k = d*sc_j * sum_k q_k x_k - dmin*m_j * sum_k x_k        (Q4_K, Q5_K)
  *   sum_k w_k x_k = d*sc_j * (sum_k q_k x_k - 32 * sum_k x_k)             (Q6_K)
  * with the per-sub-block sums of x computed once per vector.
  */
@@ -46,19 +46,27 @@ static inline __m256 u8x8_to_f32(__m128i bytes8) {
     return _mm256_cvtepi32_ps(_mm256_cvtepu8_epi32(bytes8));
 }
 
-static float row_q4k(const uint8_t* row, const float* x, const float* xsum, uint32_t nb) {
+/* Q4_K, or (q5) Q5_K: the same block with qh[32] before qs, bit j of qh[l] the fifth bit of
+ * element 32 j + l */
+static float row_q45k(const uint8_t* row, const float* x, const float* xsum, uint32_t nb, int q5) {
     __m256 acc[4] = {_mm256_setzero_ps(), _mm256_setzero_ps(), _mm256_setzero_ps(),
                      _mm256_setzero_ps()};
     float tail = 0.0f;
-    const __m128i low = _mm_set1_epi8(0x0f);
+    const __m128i low = _mm_set1_epi8(0x0f), one = _mm_set1_epi8(1);
+    const size_t bb = q5 ? KQ_Q5K_BYTES : KQ_Q4K_BYTES;
     for (uint32_t kb = 0; kb < nb; ++kb) {
-        const uint8_t* blk = row + (size_t)kb * KQ_Q4K_BYTES;
+        const uint8_t* blk = row + (size_t)kb * bb;
         uint16_t dh, mh;
         memcpy(&dh, blk, 2);
         memcpy(&mh, blk + 2, 2);
         float d = _cvtsh_ss(dh), dmin = _cvtsh_ss(mh);
-        const uint8_t* qs = blk + 16;
+        const uint8_t* qs = blk + (q5 ? 48 : 16);
         const float* xb = x + (size_t)kb * KQ_QK;
+        __m128i qh0 = _mm_setzero_si128(), qh1 = _mm_setzero_si128();
+        if (q5) {
+            qh0 = _mm_loadu_si128((const __m128i*)(blk + 16));
+            qh1 = _mm_loadu_si128((const __m128i*)(blk + 32));
+        }
         for (int c = 0; c < 4; ++c) {
             uint8_t sc0, m0, sc1, m1;
             kqo_q4k_scale_min(blk + 4, 2 * c, &sc0, &m0);
@@ -68,6 +76,13 @@ static float row_q4k(const uint8_t* row, const float* x, const float* xsum, uint
             __m128i lo0 = _mm_and_si128(q0, low), lo1 = _mm_and_si128(q1, low);
             __m128i hi0 = _mm_and_si128(_mm_srli_epi16(q0, 4), low);
             __m128i hi1 = _mm_and_si128(_mm_srli_epi16(q1, 4), low);
+            if (q5) { /* bits 2c (sub-block 2c) and 2c + 1 (sub-block 2c + 1) of qh, to bit 4 */
+                const __m128i s0 = _mm_cvtsi32_si128(2 * c), s1 = _mm_cvtsi32_si128(2 * c + 1);
+                lo0 = _mm_or_si128(lo0, _mm_slli_epi16(_mm_and_si128(_mm_srl_epi16(qh0, s0), one), 4));
+                lo1 = _mm_or_si128(lo1, _mm_slli_epi16(_mm_and_si128(_mm_srl_epi16(qh1, s0), one), 4));
+                hi0 = _mm_or_si128(hi0, _mm_slli_epi16(_mm_and_si128(_mm_srl_epi16(qh0, s1), one), 4));
+                hi1 = _mm_or_si128(hi1, _mm_slli_epi16(_mm_and_si128(_mm_srl_epi16(qh1, s1), one), 4));
+            }
             __m256 s0 = _mm256_set1_ps(d * (float)sc0), s1 = _mm256_set1_ps(d * (float)sc1);
             const float* xa = xb + 64 * c;
             /* sub-block 2c: low nibbles, 32 elements, 4 accumulators */
@@ -142,15 +157,17 @@ static void* worker(void* arg) {
         pthread_setaffinity_np(pthread_self(), sizeof(set), &set);
     }
     const uint32_t nb = j->K / KQ_QK;
-    const size_t rb = (size_t)nb * (j->type == 4 ? KQ_Q4K_BYTES : KQ_Q6K_BYTES);
-    const uint32_t per = j->type == 4 ? 32 : 16;
+    const size_t rb = (size_t)nb * (j->type == 4   ? KQ_Q4K_BYTES
+                                    : j->type == 5 ? KQ_Q5K_BYTES
+                                                   : KQ_Q6K_BYTES);
+    const uint32_t per = j->type == 6 ? 16 : 32;
     /* rows outer, vectors inner: each weight row is read from memory once for all vectors */
     for (uint32_t r = j->r0; r < j->r1; ++r) {
         const uint8_t* row = j->W + (size_t)r * rb;
         for (uint32_t b = 0; b < j->batch; ++b) {
             const float* xb = j->x + (size_t)b * j->K;
             const float* sb = j->xsum + (size_t)b * (j->K / per);
-            float v = j->type == 4 ? row_q4k(row, xb, sb, nb) : row_q6k(row, xb, sb, nb);
+            float v = j->type == 6 ? row_q6k(row, xb, sb, nb) : row_q45k(row, xb, sb, nb, j->type == 5);
             j->y[(size_t)b * j->rows + r] = v;
         }
     }
@@ -159,8 +176,8 @@ static void* worker(void* arg) {
 
 int kqo_matvec_cpu(int type, const uint8_t* W, const float* x, uint32_t rows, uint32_t K,
                    uint32_t batch, float* y, int threads) {
-    if ((type != 4 && type != 6) || K % KQ_QK != 0 || threads < 1) return -1;
-    const uint32_t per = type == 4 ? 32 : 16;
+    if (type < 4 || type > 6 || K % KQ_QK != 0 || threads < 1) return -1;
+    const uint32_t per = type == 6 ? 16 : 32;
     const size_t nsub = (size_t)K / per;
     float* xsum = (float*)malloc(sizeof(float) * nsub * (batch ? batch : 1));
     if (!xsum) return -2;
