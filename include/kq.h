@@ -68,8 +68,9 @@ enum {
     KQ_FLAG_TENSOR_CORES = 1u << 2,
     /* Use the CUDA-core kernel (batch <= 8, f32 multiply-adds). */
     KQ_FLAG_CUDA_CORES = 1u << 3,
-    /* Use the warp-MMA kernel (Q4_K batch 1..8, Q6_K batch 1): dequantisation in registers into
-     * exact f16 operands, products on the tensor cores through mma.sync, f32 accumulation.
+    /* Use the warp-MMA kernel (Q4_K batch 1..8, Q5_K and Q6_K batch 1): dequantisation in
+     * registers into exact tensor-core operands (integer at batch 1, f16 above), products
+     * through mma.sync, f32 accumulation.
      * Without a path flag the library chooses: warp-MMA where it serves the request, the
      * tensor-core kernel above batch 8, the CUDA-core kernel otherwise. */
     KQ_FLAG_WARP_MMA = 1u << 4
@@ -116,7 +117,8 @@ int kq_matvec_q6k(kq_ctx* ctx, uint64_t y, uint64_t w, uint64_t x, uint32_t rows
 
 /* The general form: strides, fused prologue/epilogue, flags. */
 typedef struct kq_matvec_desc {
-    uint32_t type;     /* KQ_TYPE_Q4_K or KQ_TYPE_Q6_K */
+    uint32_t type;     /* KQ_TYPE_Q4_K, KQ_TYPE_Q6_K, or KQ_TYPE_Q5_K (batch 1, warp-MMA path
+                        * only: another path flag or batch > 1 gives KQ_E_UNSUPPORTED) */
     uint32_t rows, k;  /* W is rows x k; k % 256 == 0 */
     uint32_t batch;    /* vectors: 1..64 for Q4_K, 1..8 for Q6_K */
     uint64_t y, w, x;  /* device addresses */
