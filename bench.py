@@ -158,6 +158,20 @@ def workload_shape(args):
     return w
 
 
+def cpu_model():
+    """The host CPU's model name (/proc/cpuinfo), or the platform's processor string."""
+    try:
+        with open("/proc/cpuinfo") as f:
+            for line in f:
+                if line.startswith("model name"):
+                    return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    import platform
+
+    return platform.processor() or "unknown"
+
+
 def cpu_matvec_timing(qtype, Wh, x, rows, K, seconds, threads):
     """Repeats the CPU matvec on a row sample until `seconds` pass; returns (GB/s, sample)."""
     import oracle
@@ -218,7 +232,7 @@ def run_reference(args):
         "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
         "config": config_of(args, w, world),
         "cpu_baseline": {"value": round(gbs, 3), "unit": "GB/s", "cores": threads, "kind": "port",
-                         "sample": sample},
+                         "sample": sample, "cpu_model": cpu_model()},
         "e2e": {"value": round(gbs, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
         "gpu_launches": 0,
         "note": "fxeqxmulfx/kernite has no k-quant path and no Rust toolchain here; the CPU "
@@ -361,8 +375,11 @@ def main(argv=None):
         ok = bool((abs(y_cpu[:, :256] - y_ref) <= 1e-3 * bound).all()
                   and (abs(y.cpu().numpy()[:, :256] - y_ref) <= 1e-3 * bound).all())
         gbs, sample = cpu_matvec_timing(qtype, Wh, xh, rows, K, args.cpu_seconds, threads)
+        gbs1, sample1 = cpu_matvec_timing(qtype, Wh, xh, rows, K, args.cpu_seconds / 4, 1)
         cpu = {"value": round(gbs, 3), "unit": "GB/s", "cores": threads, "kind": "port",
-               "sample": sample, "checked_against_oracle": ok}
+               "sample": sample, "checked_against_oracle": ok,
+               "single_thread": {"value": round(gbs1, 3), "sample": sample1},
+               "cpu_model": cpu_model()}
 
     if rank == 0:
         cfg = config_of(args, w, world)
@@ -485,7 +502,7 @@ def run_stack(args):
                 "config": {"workload": f"{args.workload}: {cfg.name}", "layers": cfg.layers,
                            "hidden": cfg.hidden, "ffn": cfg.ffn, "kv": cfg.kv, "vocab": cfg.vocab},
                 "cpu_baseline": {"value": round(tps, 4), "unit": "tokens/s", "cores": HOST_THREADS,
-                                 "kind": "port", "sample": sample},
+                                 "kind": "port", "sample": sample, "cpu_model": cpu_model()},
                 "e2e": {"value": round(tps, 4), "unit": "tokens/s", "h2d_bytes_per_step": 0,
                         "d2h_bytes_per_step": 0},
                 "gpu_launches": 0}
@@ -592,7 +609,7 @@ def run_stack(args):
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         sec, sample = stack_cpu_seconds_per_token(cfg, HOST_THREADS)
         cpu = {"value": round(1.0 / sec, 4), "unit": "tokens/s", "cores": HOST_THREADS,
-               "kind": "port", "sample": sample}
+               "kind": "port", "sample": sample, "cpu_model": cpu_model()}
     if rank == 0:
         line = {
             "metric": "decode tokens/s", "value": round(tps, 3), "unit": "tokens/s",
