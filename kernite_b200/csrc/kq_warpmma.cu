@@ -435,7 +435,8 @@ __device__ __forceinline__ void q4i8_block(uint32_t ag, uint32_t ah, uint32_t c,
                                            uint32_t m_lo, uint32_t m_hi, uint32_t sh_m, float2 X,
                                            float u0, float (&yacc)[2][2]) {
   constexpr uint32_t kQs = Q5K ? 48 : 16;
-  int acc[3][4];
+  // one accumulator set per nibble (o): two independent chains of four MMAs per limb
+  int acc[2][3][4];
   const uint4 hg = lds_v4(ag), hh = lds_v4(ah);
   uint32_t Wg[8], Wh[8];
   {
@@ -466,9 +467,9 @@ __device__ __forceinline__ void q4i8_block(uint32_t ag, uint32_t ah, uint32_t c,
     return nib;
   };
 #pragma unroll
-  for (int o = 0; o < 2; ++o)
+  for (int i = 0; i < 4; ++i)
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
+    for (int o = 0; o < 2; ++o) {
       const uint32_t a0 = quant(Wg[2 * i], Q5K ? Vg[2 * i] : 0u, o);
       const uint32_t a1 = quant(Wh[2 * i], Q5K ? Vh[2 * i] : 0u, o);
       const uint32_t a2 = quant(Wg[2 * i + 1], Q5K ? Vg[2 * i + 1] : 0u, o);
@@ -477,10 +478,10 @@ __device__ __forceinline__ void q4i8_block(uint32_t ag, uint32_t ah, uint32_t c,
 #pragma unroll
       for (int l = 0; l < 3; ++l) {
         const uint2 bf = lds_v2(bb + 8 * l);
-        if (o == 0 && i == 0)
-          imma16832_c(acc[l], a0, a1, a2, a3, bf.x, bf.y, 0u, 0u, 0u, 0u);
+        if (i == 0)
+          imma16832_c(acc[o][l], a0, a1, a2, a3, bf.x, bf.y, 0u, 0u, 0u, 0u);
         else
-          imma16832(acc[l], a0, a1, a2, a3, bf.x, bf.y);
+          imma16832(acc[o][l], a0, a1, a2, a3, bf.x, bf.y);
       }
     }
   // scales and mins of sub-blocks 2c, 2c+1 (the thread's columns) as floats
@@ -499,10 +500,11 @@ __device__ __forceinline__ void q4i8_block(uint32_t ag, uint32_t ah, uint32_t c,
   scm(hh, sh0, sh1, mh0, mh1);
   const float dg = u0 * h2f(hg.x & 0xffffu), dmg = u0 * h2f(hg.x >> 16);
   const float dh = u0 * h2f(hh.x & 0xffffu), dmh = u0 * h2f(hh.x >> 16);
-  const float v0 = limbs_to_f32(acc[2][0], acc[1][0], acc[0][0]);
-  const float v1 = limbs_to_f32(acc[2][1], acc[1][1], acc[0][1]);
-  const float v2 = limbs_to_f32(acc[2][2], acc[1][2], acc[0][2]);
-  const float v3 = limbs_to_f32(acc[2][3], acc[1][3], acc[0][3]);
+  // column 2c (sub-block 2c) is summed by the o = 0 MMAs alone, column 2c + 1 by the o = 1 ones
+  const float v0 = limbs_to_f32(acc[0][2][0], acc[0][1][0], acc[0][0][0]);
+  const float v1 = limbs_to_f32(acc[1][2][1], acc[1][1][1], acc[1][0][1]);
+  const float v2 = limbs_to_f32(acc[0][2][2], acc[0][1][2], acc[0][0][2]);
+  const float v3 = limbs_to_f32(acc[1][2][3], acc[1][1][3], acc[1][0][3]);
   yacc[0][0] += dg * fmaf(sg0, v0, sg1 * v1) - dmg * fmaf(mg0, X.x, mg1 * X.y);
   yacc[1][0] += dh * fmaf(sh0, v2, sh1 * v3) - dmh * fmaf(mh0, X.x, mh1 * X.y);
 }
