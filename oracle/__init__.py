@@ -6,7 +6,8 @@ leg import this module, as the checker or as the timed CPU baseline; the product
 
 The k-quant path does not exist in fxeqxmulfx/kernite. The oracle restates the GGML k-quant
 format; it is pinned against gguf-py 0.19.0's numpy dequantizer (``gguf/quants.py``,
-``Q4_K.dequantize_blocks`` / ``Q6_K.dequantize_blocks``) through the fixtures in
+``Q2_K``, ``Q3_K``, ``Q4_K``, ``Q5_K``, ``Q6_K`` and ``Q8_0.dequantize_blocks``) through the
+fixtures in
 ``tests/golden/``, and its fp16 decode against kernite's table in
 ``crates/cuda/src/half.rs:165-180``.
 """
@@ -24,7 +25,15 @@ LIB_PATH = os.path.join(HERE, "liboracle.so")
 Q4K_BYTES = 144
 Q6K_BYTES = 210
 Q5K_BYTES = 176
+Q2K_BYTES = 84
+Q3K_BYTES = 110
+Q8_0_UNIT_BYTES = 272  # eight 34-byte Q8_0 blocks = 256 weights
 QK = 256
+# type numbers of the oracle: k-quants by their bit width, Q8_0 as 8
+UNIT_BYTES = {2: Q2K_BYTES, 3: Q3K_BYTES, 4: Q4K_BYTES, 5: Q5K_BYTES, 6: Q6K_BYTES,
+              8: Q8_0_UNIT_BYTES}
+# names of the fixture arrays' prefixes in tests/golden/kquant_golden.npz
+GOLDEN_PREFIX = {2: "q2k", 3: "q3k", 4: "q4k", 5: "q5k", 6: "q6k", 8: "q8_0"}
 
 _lib = None
 
@@ -51,16 +60,22 @@ def lib() -> ctypes.CDLL:
         L.kqo_f32_to_fp16.restype = ctypes.c_uint16
         L.kqo_q4k_scale_min.argtypes = [u8p, ctypes.c_int, u8p, u8p]
         L.kqo_q4k_scale_min.restype = None
-        for name in ("kqo_dequant_q4k", "kqo_dequant_q5k", "kqo_dequant_q6k"):
+        for name in ("kqo_dequant_q4k", "kqo_dequant_q5k", "kqo_dequant_q6k", "kqo_dequant_q2k",
+                     "kqo_dequant_q3k", "kqo_dequant_q8_0"):
             fn = getattr(L, name)
             fn.argtypes = [u8p, ctypes.c_size_t, f32p]
             fn.restype = None
+        L.kqo_dequant.argtypes = [ctypes.c_int, u8p, ctypes.c_size_t, f32p]
+        L.kqo_dequant.restype = ctypes.c_int
+        L.kqo_q3k_scale.argtypes = [u8p, ctypes.c_int]
+        L.kqo_q3k_scale.restype = ctypes.c_int
         L.kqo_matvec_ref.argtypes = [
             ctypes.c_int, u8p, f32p, ctypes.c_uint32, ctypes.c_uint32, ctypes.c_uint32,
             ctypes.c_uint32, ctypes.c_uint64, ctypes.c_uint64, f64p, f64p,
         ]
         L.kqo_matvec_ref.restype = None
-        for name in ("kqo_fill_q4k", "kqo_fill_q5k", "kqo_fill_q6k"):
+        for name in ("kqo_fill_q4k", "kqo_fill_q5k", "kqo_fill_q6k", "kqo_fill_q2k", "kqo_fill_q3k",
+                     "kqo_fill_q8_0"):
             fn = getattr(L, name)
             fn.argtypes = [u8p, ctypes.c_uint64, ctypes.c_uint64, ctypes.c_uint64]
             fn.restype = None
@@ -93,7 +108,8 @@ def _f64(a: np.ndarray):
 
 
 def block_bytes(qtype: int) -> int:
-    return {4: Q4K_BYTES, 5: Q5K_BYTES, 6: Q6K_BYTES}[qtype]
+    """Bytes per 256 weights (one super-block; for Q8_0, eight blocks)."""
+    return UNIT_BYTES[qtype]
 
 
 def fp16_to_f32(h: int) -> float:
@@ -102,6 +118,12 @@ def fp16_to_f32(h: int) -> float:
 
 def f32_to_fp16(x: float) -> int:
     return lib().kqo_f32_to_fp16(x)
+
+
+def q3k_scale(scales12: bytes, i: int) -> int:
+    """Scale i (0..15) of a Q3_K block's 12 packed scale bytes, minus 32."""
+    buf = np.frombuffer(bytes(scales12), dtype=np.uint8).copy()
+    return lib().kqo_q3k_scale(_u8(buf), i)
 
 
 def q4k_scale_min(scales12: bytes, j: int) -> tuple[int, int]:
@@ -118,8 +140,8 @@ def dequant(qtype: int, blocks: np.ndarray) -> np.ndarray:
     n = blocks.size // block_bytes(qtype)
     assert n * block_bytes(qtype) == blocks.size
     out = np.empty(n * QK, dtype=np.float32)
-    fn = {4: lib().kqo_dequant_q4k, 5: lib().kqo_dequant_q5k, 6: lib().kqo_dequant_q6k}[qtype]
-    fn(_u8(blocks), n, _f32(out))
+    if lib().kqo_dequant(qtype, _u8(blocks), n, _f32(out)) != 0:
+        raise ValueError(f"unknown type {qtype}")
     return out
 
 
@@ -134,7 +156,8 @@ def splitmix_at(key: int, i: int) -> int:
 def fill(qtype: int, key: int, b0: int, n: int) -> np.ndarray:
     """Blocks [b0, b0+n) of the synthetic tensor with stream key `key`, as raw bytes."""
     out = np.empty(n * block_bytes(qtype), dtype=np.uint8)
-    fn = {4: lib().kqo_fill_q4k, 5: lib().kqo_fill_q5k, 6: lib().kqo_fill_q6k}[qtype]
+    fn = {2: lib().kqo_fill_q2k, 3: lib().kqo_fill_q3k, 4: lib().kqo_fill_q4k,
+          5: lib().kqo_fill_q5k, 6: lib().kqo_fill_q6k, 8: lib().kqo_fill_q8_0}[qtype]
     fn(_u8(out), key, b0, n)
     return out
 

@@ -1,6 +1,7 @@
 /*
- * kq_oracle.c -- CPU restatement of the Q4_K / Q6_K decode, the f64 reference matvec and the
- * counter-based synthetic generator. TEST INFRASTRUCTURE ONLY (see kq_oracle.h).
+ * kq_oracle.c -- CPU restatement of the GGML Q2_K / Q3_K / Q4_K / Q5_K / Q6_K / Q8_0 decode, the
+ * f64 reference matvec and the counter-based synthetic generator. TEST INFRASTRUCTURE ONLY (see
+ * kq_oracle.h).
  *
  * Compiled with -ffp-contract=off: every float operation below is one IEEE binary32 (or
  * binary64) operation, rounded to nearest even, in the order written.
@@ -182,15 +183,114 @@ void kqo_dequant_q5k(const uint8_t* blocks, size_t n, float* out) {
     }
 }
 
+/* ---------------------------------------------------------------- Q2_K */
+
+/* scales[16] at 0 (low nibble: scale, high nibble: min of 16-element sub-block i), qs[64] at 16,
+ * d at 80, dmin at 82. Element 128h + 32s + l (h 0..1, s 0..3, l 0..31) is bits 2s..2s+1 of
+ * qs[32h + l]; its sub-block is element / 16. w = (d*f32(sc))*f32(q) - dmin*f32(m), the product
+ * of d and the scale rounded first (gguf-py/gguf/quants.py Q2_K.dequantize_blocks). */
+void kqo_dequant_q2k(const uint8_t* blocks, size_t n, float* out) {
+    for (size_t b = 0; b < n; ++b) {
+        const uint8_t* blk = blocks + b * KQ_Q2K_BYTES;
+        const uint8_t* sc = blk;
+        const uint8_t* qs = blk + 16;
+        float d = kqo_fp16_to_f32(rd16(blk + 80));
+        float dmin = kqo_fp16_to_f32(rd16(blk + 82));
+        float* o = out + b * KQ_QK;
+        for (int e = 0; e < KQ_QK; ++e) {
+            int h = e >> 7, s4 = (e >> 5) & 3, l = e & 31;
+            uint8_t q = (uint8_t)((qs[32 * h + l] >> (2 * s4)) & 3u);
+            uint8_t si = sc[e >> 4];
+            float dl = d * (float)(si & 15u);
+            float ml = dmin * (float)(si >> 4);
+            float t = dl * (float)q;
+            o[e] = t - ml;
+        }
+    }
+}
+
+/* ---------------------------------------------------------------- Q3_K */
+
+/* The 6-bit scale i (0..15) of a Q3_K block, as the signed value scale - 32: low 4 bits from
+ * nibble i / 8 of byte i % 8, high 2 bits from bits 2 (i / 4).. of byte 8 + i % 4. */
+int kqo_q3k_scale(const uint8_t s[12], int i) {
+    int lo = (s[i % 8] >> (4 * (i / 8))) & 15;
+    int hi = (s[8 + i % 4] >> (2 * (i / 4))) & 3;
+    return (lo | (hi << 4)) - 32;
+}
+
+/* hmask[32] at 0, qs[64] at 32, scales[12] at 96, d at 108. Element 128h + 32s + l has low bits
+ * 2s..2s+1 of qs[32h + l] and high bit k = 4h + s of hmask[l]; q = low - 4 when that bit is
+ * clear, low when it is set. Sub-block element / 16. w = (d*f32(scale - 32))*f32(q)
+ * (gguf-py/gguf/quants.py Q3_K.dequantize_blocks). */
+void kqo_dequant_q3k(const uint8_t* blocks, size_t n, float* out) {
+    for (size_t b = 0; b < n; ++b) {
+        const uint8_t* blk = blocks + b * KQ_Q3K_BYTES;
+        const uint8_t* hm = blk;
+        const uint8_t* qs = blk + 32;
+        const uint8_t* sc = blk + 96;
+        float d = kqo_fp16_to_f32(rd16(blk + 108));
+        float* o = out + b * KQ_QK;
+        for (int e = 0; e < KQ_QK; ++e) {
+            int h = e >> 7, s4 = (e >> 5) & 3, l = e & 31;
+            int low = (qs[32 * h + l] >> (2 * s4)) & 3;
+            int high = (hm[l] >> (4 * h + s4)) & 1;
+            int q = low - (high ? 0 : 4);
+            float dl = d * (float)kqo_q3k_scale(sc, e >> 4);
+            o[e] = dl * (float)q;
+        }
+    }
+}
+
+/* ---------------------------------------------------------------- Q8_0 */
+
+/* Eight consecutive 32-element Q8_0 blocks (34 bytes each: f16 d, then int8 qs[32]) make one
+ * 256-element unit of 272 bytes, so that rows of K (a multiple of 256) elements are whole units.
+ * w = f32(q) * d (gguf-py/gguf/quants.py Q8_0.dequantize_blocks). */
+void kqo_dequant_q8_0(const uint8_t* units, size_t n, float* out) {
+    for (size_t u = 0; u < n * 8; ++u) {
+        const uint8_t* blk = units + u * KQ_Q8_0_BLOCK_BYTES;
+        float d = kqo_fp16_to_f32(rd16(blk));
+        const int8_t* q = (const int8_t*)(blk + 2);
+        for (int l = 0; l < 32; ++l) out[u * 32 + l] = (float)q[l] * d;
+    }
+}
+
+/* Bytes per 256 weights of `type` (2, 3, 4, 5, 6, 8), 0 for an unknown type. */
+size_t kqo_unit_bytes(int type) {
+    switch (type) {
+        case 2: return KQ_Q2K_BYTES;
+        case 3: return KQ_Q3K_BYTES;
+        case 4: return KQ_Q4K_BYTES;
+        case 5: return KQ_Q5K_BYTES;
+        case 6: return KQ_Q6K_BYTES;
+        case 8: return KQ_Q8_0_UNIT_BYTES;
+        default: return 0;
+    }
+}
+
+/* Decode n 256-weight units of `type`; returns -1 for an unknown type. */
+int kqo_dequant(int type, const uint8_t* units, size_t n, float* out) {
+    switch (type) {
+        case 2: kqo_dequant_q2k(units, n, out); return 0;
+        case 3: kqo_dequant_q3k(units, n, out); return 0;
+        case 4: kqo_dequant_q4k(units, n, out); return 0;
+        case 5: kqo_dequant_q5k(units, n, out); return 0;
+        case 6: kqo_dequant_q6k(units, n, out); return 0;
+        case 8: kqo_dequant_q8_0(units, n, out); return 0;
+        default: return -1;
+    }
+}
+
 /* ---------------------------------------------------------------- reference matvec */
 
 void kqo_matvec_ref(int type, const uint8_t* W, const float* x, uint32_t K, uint32_t r0,
                     uint32_t r1, uint32_t batch, uint64_t ldx, uint64_t ldy, double* y,
                     double* bound) {
     const uint32_t nb = K / KQ_QK;
-    const size_t blk_bytes =
-        type == 4 ? KQ_Q4K_BYTES : type == 5 ? KQ_Q5K_BYTES : KQ_Q6K_BYTES;
+    const size_t blk_bytes = kqo_unit_bytes(type);
     float w[KQ_QK];
+    if (blk_bytes == 0) return;
     for (uint32_t r = r0; r < r1; ++r) {
         for (uint32_t b = 0; b < batch; ++b) {
             y[b * ldy + r] = 0.0;
@@ -198,12 +298,7 @@ void kqo_matvec_ref(int type, const uint8_t* W, const float* x, uint32_t K, uint
         }
         for (uint32_t kb = 0; kb < nb; ++kb) {
             const uint8_t* blk = W + ((size_t)r * nb + kb) * blk_bytes;
-            if (type == 4)
-                kqo_dequant_q4k(blk, 1, w);
-            else if (type == 5)
-                kqo_dequant_q5k(blk, 1, w);
-            else
-                kqo_dequant_q6k(blk, 1, w);
+            kqo_dequant(type, blk, 1, w);
             for (uint32_t b = 0; b < batch; ++b) {
                 const float* xb = x + b * ldx + (size_t)kb * KQ_QK;
                 double acc = 0.0, mag = 0.0;
@@ -296,5 +391,47 @@ void kqo_fill_q5k(uint8_t* out, uint64_t key, uint64_t b0, uint64_t n) {
         blk[1] = (uint8_t)(d >> 8);
         blk[2] = (uint8_t)m;
         blk[3] = (uint8_t)(m >> 8);
+    }
+}
+
+/* Block b draws counters [13b, 13b+13): words 0-10 give its 84 bytes (bytes 80-83 then
+ * overwritten), word 11 gives d and word 12 gives dmin, both fp16(uniform [2^-9, 2^-5]). */
+void kqo_fill_q2k(uint8_t* out, uint64_t key, uint64_t b0, uint64_t n) {
+    for (uint64_t i = 0; i < n; ++i) {
+        uint64_t b = b0 + i;
+        uint8_t* blk = out + i * KQ_Q2K_BYTES;
+        put_bytes(blk, key, 13 * b, KQ_Q2K_BYTES);
+        uint16_t d = uniform_fp16(kqo_splitmix_at(key, 13 * b + 11), 0x1p-9f, 15.0f * 0x1p-9f);
+        uint16_t m = uniform_fp16(kqo_splitmix_at(key, 13 * b + 12), 0x1p-9f, 15.0f * 0x1p-9f);
+        blk[80] = (uint8_t)d;
+        blk[81] = (uint8_t)(d >> 8);
+        blk[82] = (uint8_t)m;
+        blk[83] = (uint8_t)(m >> 8);
+    }
+}
+
+/* Block b draws counters [15b, 15b+15): words 0-13 give its 110 bytes (bytes 108-109 then
+ * overwritten), word 14 gives d = fp16(uniform [2^-11, 2^-7]). */
+void kqo_fill_q3k(uint8_t* out, uint64_t key, uint64_t b0, uint64_t n) {
+    for (uint64_t i = 0; i < n; ++i) {
+        uint64_t b = b0 + i;
+        uint8_t* blk = out + i * KQ_Q3K_BYTES;
+        put_bytes(blk, key, 15 * b, KQ_Q3K_BYTES);
+        uint16_t d = uniform_fp16(kqo_splitmix_at(key, 15 * b + 14), 0x1p-11f, 15.0f * 0x1p-11f);
+        blk[108] = (uint8_t)d;
+        blk[109] = (uint8_t)(d >> 8);
+    }
+}
+
+/* Units [b0, b0+n) of 8 blocks; Q8_0 block j = 8u + v draws counters [6j, 6j+6): words 0-4
+ * give its 34 bytes (bytes 0-1 then overwritten), word 5 gives d = fp16(uniform [2^-12, 2^-8]). */
+void kqo_fill_q8_0(uint8_t* out, uint64_t key, uint64_t b0, uint64_t n) {
+    for (uint64_t i = 0; i < n * 8; ++i) {
+        uint64_t j = b0 * 8 + i;
+        uint8_t* blk = out + i * KQ_Q8_0_BLOCK_BYTES;
+        put_bytes(blk, key, 6 * j, KQ_Q8_0_BLOCK_BYTES);
+        uint16_t d = uniform_fp16(kqo_splitmix_at(key, 6 * j + 5), 0x1p-12f, 15.0f * 0x1p-12f);
+        blk[0] = (uint8_t)d;
+        blk[1] = (uint8_t)(d >> 8);
     }
 }

@@ -1,8 +1,9 @@
-"""Generate the committed golden fixtures that pin the CPU oracle's Q4_K / Q5_K / Q6_K decode.
+"""Generate the committed golden fixtures that pin the CPU oracle's Q2_K / Q3_K / Q4_K / Q5_K /
+Q6_K / Q8_0 decode.
 
 The k-quant format is third-party (GGML); fxeqxmulfx/kernite has no implementation of it. The
-owner's published Python package gguf-py (version 0.19.0, ``gguf/quants.py``,
-``Q4_K``, ``Q5_K`` and ``Q6_K.dequantize_blocks``) is imported here, in the development
+owner's published Python package gguf-py (version 0.19.0, ``gguf/quants.py``, ``Q2_K``, ``Q3_K``,
+``Q4_K``, ``Q5_K``, ``Q6_K`` and ``Q8_0.dequantize_blocks``) is imported here, in the development
 container, to dequantise a fixed set of blocks. Its float32 outputs are stored bit for bit in
 ``kquant_golden.npz`` and the tests compare the oracle (and, on the GPU, the device decode)
 against them. The GPU box does not need gguf: only the .npz travels.
@@ -12,7 +13,10 @@ Block sets per type:
     tensor 7), the distribution every bench and parity test uses;
   * ``raw``: 64 blocks of uniformly random bytes (any fp16 d/dmin: subnormal, inf, NaN);
   * ``kat``: hand-built known-answer blocks: d = 1.0, dmin = 0, one scale set, quant
-    patterns 0..15 / 0..63, every 6-bit scale and min value through the Q4_K packing.
+    patterns 0..15 / 0..63, every 6-bit scale and min value through the Q4_K packing, every
+    4-bit scale and min (Q2_K), every 6-bit Q3_K scale and hmask pattern, every int8 (Q8_0).
+Array names start with the type: q2k, q3k, q4k, q5k, q6k, q8_0 (Q8_0 counted in units of eight
+34-byte blocks, 256 weights).
 Plus a small matvec case (rows 8, K 512, batch 3) with its float64 reference outputs computed
 from gguf's float32 weights.
 
@@ -130,27 +134,98 @@ def kat_q6k() -> np.ndarray:
     return np.concatenate(blocks)
 
 
+def kat_q2k() -> np.ndarray:
+    blocks = []
+    # every 4-bit scale / min pair across the 16 slots, d = dmin = 1, each crumb pattern
+    for base in range(0, 256, 16):
+        b = np.zeros(84, dtype=np.uint8)
+        b[0:16] = np.array([(base + 17 * i) % 256 for i in range(16)], dtype=np.uint8)
+        b[16:80] = np.array([(i * 0x1B) % 256 for i in range(64)], dtype=np.uint8)
+        b[80:82] = np.array([fp16_bits(1.0)], dtype=np.uint16).view(np.uint8)
+        b[82:84] = np.array([fp16_bits(1.0)], dtype=np.uint16).view(np.uint8)
+        blocks.append(b)
+    # one scale set to 1 (min 0), quants 0..3 along the block, d = 0.5
+    for i in range(16):
+        b = np.zeros(84, dtype=np.uint8)
+        b[i] = 1
+        b[16:80] = np.uint8(0b11100100)
+        b[80:82] = np.array([fp16_bits(0.5)], dtype=np.uint16).view(np.uint8)
+        blocks.append(b)
+    return np.concatenate(blocks)
+
+
+def pack_q3k_scales(sc: np.ndarray) -> np.ndarray:
+    """GGML's 12-byte packing of sixteen 6-bit Q3_K scales (values 0..63, stored + 32)."""
+    s = np.zeros(12, dtype=np.int64)
+    for i in range(16):
+        s[i % 8] |= (sc[i] & 15) << (4 * (i // 8))
+        s[8 + i % 4] |= ((sc[i] >> 4) & 3) << (2 * (i // 4))
+    return s.astype(np.uint8)
+
+
+def kat_q3k() -> np.ndarray:
+    blocks = []
+    # every 6-bit stored scale value through the packing, d = 1, alternating hmask bits
+    for v in range(0, 64, 4):
+        b = np.zeros(110, dtype=np.uint8)
+        b[0:32] = np.array([0x55 if i % 2 else 0xAA for i in range(32)], dtype=np.uint8)
+        b[32:96] = np.array([(i * 0x2D) % 256 for i in range(64)], dtype=np.uint8)
+        b[96:108] = pack_q3k_scales(np.array([(v + i) % 64 for i in range(16)]))
+        b[108:110] = np.array([fp16_bits(1.0)], dtype=np.uint16).view(np.uint8)
+        blocks.append(b)
+    # one sub-block scaled by +1 (stored 33), all q values -4..3 via hmask all-0 and all-1
+    for i in range(16):
+        for hm in (0x00, 0xFF):
+            b = np.zeros(110, dtype=np.uint8)
+            b[0:32] = np.uint8(hm)
+            b[32:96] = np.uint8(0b11100100)
+            sc = np.full(16, 32)
+            sc[i] = 33
+            b[96:108] = pack_q3k_scales(sc)
+            b[108:110] = np.array([fp16_bits(1.0)], dtype=np.uint16).view(np.uint8)
+            blocks.append(b)
+    return np.concatenate(blocks)
+
+
+def kat_q8_0() -> np.ndarray:
+    blocks = []
+    # every int8 value (eight per 32-byte block), d = 1, 0.5, -2 and a subnormal
+    for d in (1.0, 0.5, -2.0, 2.0 ** -20):
+        for base in range(0, 256, 32):
+            b = np.zeros(34, dtype=np.uint8)
+            b[0:2] = np.array([fp16_bits(d)], dtype=np.uint16).view(np.uint8)
+            b[2:34] = np.arange(base, base + 32, dtype=np.int64).astype(np.uint8)
+            blocks.append(b)
+    return np.concatenate(blocks)  # 32 blocks = 4 units
+
+
+GGUF_TYPES = {2: T.Q2_K, 3: T.Q3_K, 4: T.Q4_K, 5: T.Q5_K, 6: T.Q6_K, 8: T.Q8_0}
+GGUF_BLOCK_BYTES = {2: 84, 3: 110, 4: 144, 5: 176, 6: 210, 8: 34}
+
+
 def gguf_dequant(qtype: int, raw: np.ndarray) -> np.ndarray:
-    bb = oracle.block_bytes(qtype)
-    arr = raw.reshape(-1, bb)
-    out = dequantize(arr, {4: T.Q4_K, 5: T.Q5_K, 6: T.Q6_K}[qtype])
+    arr = raw.reshape(-1, GGUF_BLOCK_BYTES[qtype])
+    out = dequantize(arr, GGUF_TYPES[qtype])
     return np.ascontiguousarray(out, dtype=np.float32).reshape(-1)
 
 
 def main() -> None:
-    oracle.build()
+    oracle.build(force=True)  # make: rebuilds the library if a source is newer
     rng = np.random.default_rng(20261201)
     data = {"gguf_version": np.array(gguf.__version__ if hasattr(gguf, "__version__") else "0.19.0")}
     key = oracle.stream_key(1234, 7)
-    for qtype in (4, 6, 5):  # Q5_K last: the Q4_K/Q6_K draws stay as they were
+    # types in the order they were added: each type's random draws follow the earlier ones', so
+    # adding a type leaves every existing array as it was
+    for qtype in (4, 6, 5, 2, 3, 8):
+        pre = oracle.GOLDEN_PREFIX[qtype]
         bb = oracle.block_bytes(qtype)
         gen = oracle.fill(qtype, key, 0, 64)
         raw = rng.integers(0, 256, size=64 * bb, dtype=np.uint8)
-        kat = {4: kat_q4k, 5: kat_q5k, 6: kat_q6k}[qtype]()
+        kat = {2: kat_q2k, 3: kat_q3k, 4: kat_q4k, 5: kat_q5k, 6: kat_q6k, 8: kat_q8_0}[qtype]()
         for name, blocks in (("gen", gen), ("raw", raw), ("kat", kat)):
             ref = gguf_dequant(qtype, blocks)
-            data[f"q{qtype}k_{name}_blocks"] = blocks
-            data[f"q{qtype}k_{name}_f32bits"] = ref.view(np.uint32)
+            data[f"{pre}_{name}_blocks"] = blocks
+            data[f"{pre}_{name}_f32bits"] = ref.view(np.uint32)
         # small matvec case from generated blocks
         rows, K, batch = 8, 512, 3
         W = oracle.fill(qtype, oracle.stream_key(99, qtype), 0, rows * K // 256)
@@ -158,10 +233,10 @@ def main() -> None:
         w = gguf_dequant(qtype, W).reshape(rows, K).astype(np.float64)
         y = x.astype(np.float64) @ w.T
         bound = np.abs(x.astype(np.float64)[:, None, :] * w[None, :, :]).sum(-1)
-        data[f"q{qtype}k_mv_W"] = W
-        data[f"q{qtype}k_mv_x"] = x
-        data[f"q{qtype}k_mv_y"] = y
-        data[f"q{qtype}k_mv_bound"] = bound
+        data[f"{pre}_mv_W"] = W
+        data[f"{pre}_mv_x"] = x
+        data[f"{pre}_mv_y"] = y
+        data[f"{pre}_mv_bound"] = bound
     out = os.path.join(HERE, "kquant_golden.npz")
     np.savez_compressed(out, **data)
     print("wrote", out, os.path.getsize(out), "bytes")

@@ -62,11 +62,15 @@ def test_f32_to_fp16_matches_numpy_rounding():
     assert np.array_equal(got, want)
 
 
-@pytest.mark.parametrize("qtype", [4, 5, 6])
+ALL_TYPES = [2, 3, 4, 5, 6, 8]  # Q2_K .. Q6_K, Q8_0
+
+
+@pytest.mark.parametrize("qtype", ALL_TYPES)
 @pytest.mark.parametrize("which", ["gen", "raw", "kat"])
 def test_dequant_matches_gguf_bit_for_bit(golden, qtype, which):
-    blocks = golden[f"q{qtype}k_{which}_blocks"]
-    want = golden[f"q{qtype}k_{which}_f32bits"]
+    pre = oracle.GOLDEN_PREFIX[qtype]
+    blocks = golden[f"{pre}_{which}_blocks"]
+    want = golden[f"{pre}_{which}_f32bits"]
     got = oracle.dequant(qtype, blocks).view(np.uint32)
     wf, gf = want.view(np.float32), got.view(np.float32)
     nan = np.isnan(wf)
@@ -74,13 +78,14 @@ def test_dequant_matches_gguf_bit_for_bit(golden, qtype, which):
     assert np.array_equal(got[~nan], want[~nan])
 
 
-@pytest.mark.parametrize("qtype", [4, 5, 6])
+@pytest.mark.parametrize("qtype", ALL_TYPES)
 def test_matvec_ref_matches_golden(golden, qtype):
-    W = golden[f"q{qtype}k_mv_W"]
-    x = golden[f"q{qtype}k_mv_x"]
+    pre = oracle.GOLDEN_PREFIX[qtype]
+    W = golden[f"{pre}_mv_W"]
+    x = golden[f"{pre}_mv_x"]
     y, bound = oracle.matvec_ref(qtype, W, x, 512, 0, 8)
-    np.testing.assert_allclose(y, golden[f"q{qtype}k_mv_y"], rtol=0, atol=1e-12)
-    np.testing.assert_allclose(bound, golden[f"q{qtype}k_mv_bound"], rtol=1e-12)
+    np.testing.assert_allclose(y, golden[f"{pre}_mv_y"], rtol=0, atol=1e-12)
+    np.testing.assert_allclose(bound, golden[f"{pre}_mv_bound"], rtol=1e-12)
 
 
 def test_q4k_scale_packing_every_value():
@@ -166,3 +171,82 @@ def test_cpu_baseline_within_tolerance(qtype, K):
     y_ref, bound = oracle.matvec_ref(qtype, W, x, K, 0, rows)
     y = oracle.matvec_cpu(qtype, W, x, rows, K, threads=3)
     assert (np.abs(y - y_ref) <= 1e-3 * bound).all()
+
+
+def test_q3k_scale_packing_every_value():
+    # sixteen 6-bit scales packed as GGML does (low nibbles in bytes 0-7, high pairs in 8-11)
+    for v in range(64):
+        sc = [(v + 5 * i) % 64 for i in range(16)]
+        s = [0] * 12
+        for i in range(16):
+            s[i % 8] |= (sc[i] & 15) << (4 * (i // 8))
+            s[8 + i % 4] |= ((sc[i] >> 4) & 3) << (2 * (i // 4))
+        for i in range(16):
+            assert oracle.q3k_scale(bytes(s), i) == sc[i] - 32
+
+
+def test_q2k_q3k_known_answer_element_order():
+    # Q2_K: d = 1, dmin = 0, only sub-block i scaled by 1: its weights are the crumbs of qs in
+    # GGML order (element 128h + 32s + l = bits 2s.. of qs[32h + l])
+    rng = np.random.default_rng(3)
+    qs = rng.integers(0, 256, size=64, dtype=np.uint8)
+    hm = rng.integers(0, 256, size=32, dtype=np.uint8)
+    want_q2 = np.array([(qs[32 * (e // 128) + e % 32] >> (2 * ((e // 32) % 4))) & 3
+                        for e in range(256)], dtype=np.float32)
+    for i in range(16):
+        b = np.zeros(84, dtype=np.uint8)
+        b[i] = 1
+        b[16:80] = qs
+        b[80:82] = np.array([0x3C00], dtype=np.uint16).view(np.uint8)
+        w = oracle.dequant(2, b)
+        want = np.zeros(256, dtype=np.float32)
+        want[16 * i:16 * i + 16] = want_q2[16 * i:16 * i + 16]
+        assert np.array_equal(w, want), i
+    # Q3_K: every stored scale 33 (scale +1), d = 1: w = low crumb - 4 * (1 - hmask bit)
+    b = np.zeros(110, dtype=np.uint8)
+    b[0:32] = hm
+    b[32:96] = qs
+    s = [0] * 12
+    for i in range(16):
+        s[i % 8] |= (33 & 15) << (4 * (i // 8))
+        s[8 + i % 4] |= ((33 >> 4) & 3) << (2 * (i // 4))
+    b[96:108] = s
+    b[108:110] = np.array([0x3C00], dtype=np.uint16).view(np.uint8)
+    hbit = np.array([(hm[e % 32] >> (e // 32)) & 1 for e in range(256)])
+    assert np.array_equal(oracle.dequant(3, b), (want_q2 - 4 * (1 - hbit)).astype(np.float32))
+
+
+def test_q8_0_units_are_eight_blocks():
+    # a unit of 272 bytes is eight 34-byte blocks, each w = q * d with its own d
+    key = oracle.stream_key(5, 8)
+    u = oracle.fill(8, key, 0, 3)
+    assert u.size == 3 * 272
+    blocks = u.reshape(24, 34)
+    d = blocks[:, 0:2].copy().view(np.float16).astype(np.float32)
+    q = blocks[:, 2:].view(np.int8).astype(np.float32)
+    assert np.array_equal(oracle.dequant(8, u), (q * d).reshape(-1))
+    assert (d >= 2.0 ** -12).all() and (d <= 2.0 ** -8).all()
+    # counter-based: units 1..2 on their own are the same bytes
+    assert np.array_equal(oracle.fill(8, key, 1, 2), u[272:])
+
+
+@pytest.mark.parametrize("qtype", [2, 3])
+def test_new_generators_are_counter_based(qtype):
+    key = oracle.stream_key(42, qtype)
+    bb = oracle.block_bytes(qtype)
+    whole = oracle.fill(qtype, key, 0, 30)
+    assert np.array_equal(whole[11 * bb:16 * bb], oracle.fill(qtype, key, 11, 5))
+    blocks = whole.reshape(30, bb)
+    at = 80 if qtype == 2 else 108
+    d = blocks[:, at:at + 2].copy().view(np.float16).astype(np.float32)
+    lo, hi = (2.0 ** -9, 2.0 ** -5) if qtype == 2 else (2.0 ** -11, 2.0 ** -7)
+    assert (d >= lo).all() and (d <= hi).all()
+
+
+@pytest.mark.parametrize("qtype", ALL_TYPES)
+def test_golden_generated_blocks_are_the_generator_output(golden, qtype):
+    # the fixtures' "gen" blocks are the generator's stream (seed 1234, tensor 7), so the
+    # generator itself is pinned as well as the decode
+    key = oracle.stream_key(1234, 7)
+    pre = oracle.GOLDEN_PREFIX[qtype]
+    assert np.array_equal(golden[f"{pre}_gen_blocks"], oracle.fill(qtype, key, 0, 64))
