@@ -163,7 +163,8 @@ def test_generator_is_counter_based_and_in_range():
     assert oracle.stream_key(42, 3) != oracle.stream_key(42, 4)
 
 
-@pytest.mark.parametrize("qtype,K", [(4, 4096), (5, 4096), (5, 11008), (6, 4096), (6, 11008)])
+@pytest.mark.parametrize("qtype,K", [(2, 4096), (2, 11008), (3, 4096), (3, 11008), (4, 4096), (5, 4096),
+                                     (5, 11008), (6, 4096), (6, 11008), (8, 4096), (8, 11008)])
 def test_cpu_baseline_within_tolerance(qtype, K):
     rows = 64
     W = oracle.fill(qtype, oracle.stream_key(7, qtype), 0, rows * K // 256)
