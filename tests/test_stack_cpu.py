@@ -1,5 +1,5 @@
-"""Host-side logic of the row-sharded decode stack on CPU: shard plans, and world-size-2 gloo
-ranks running the stack on an oracle backend, against the unsharded reference."""
+"""Host-side logic of the row-sharded decode stack on CPU: shard plans, and world-size-2 and -4
+gloo ranks running the stack on an oracle backend, against the unsharded reference."""
 import math
 import os
 import sys
@@ -88,23 +88,24 @@ def _rank(rank, world, port, q):
 
 
 @pytest.mark.timeout(300)
-def test_two_gloo_ranks_match_unsharded_reference():
+@pytest.mark.parametrize("world", [2, 4])
+def test_gloo_ranks_match_unsharded_reference(world):
     cfg = st.CONFIGS["tiny"]
     x = np.random.default_rng(0).standard_normal(cfg.hidden).astype(np.float32)
     ref = st.reference_logits(cfg, x)
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
-    port = 29500 + os.getpid() % 1000
-    procs = [ctx.Process(target=_rank, args=(r, 2, port, q)) for r in range(2)]
+    port = 29500 + os.getpid() % 1000 + 7 * world
+    procs = [ctx.Process(target=_rank, args=(r, world, port, q)) for r in range(world)]
     for p in procs:
         p.start()
     out = dict(q.get(timeout=240) for _ in procs)
     for p in procs:
         p.join(timeout=60)
         assert p.exitcode == 0
-    for r in (0, 1):
+    for r in range(world):
         np.testing.assert_allclose(out[r], ref, rtol=1e-4, atol=1e-4 * np.abs(ref).max())
-    np.testing.assert_array_equal(out[0], out[1])
+        np.testing.assert_array_equal(out[0], out[r])
 
 
 def test_single_rank_oracle_backend_matches_reference():
