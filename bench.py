@@ -452,9 +452,10 @@ def _init_dist(torch, world, local):
     return dist
 
 
-def stack_cpu_seconds_per_token(cfg, threads):
+def stack_cpu_seconds_per_token(cfg, threads, also_single=False):
     """CPU baseline for a stack: one layer's matvecs and the head timed with the AVX2 port,
-    scaled to the stack's layer count. Returns (seconds per token, sample)."""
+    scaled to the stack's layer count. Returns (seconds per token, sample), and with
+    `also_single` the seconds per token on one thread as well (same matrices, timed after)."""
     import numpy as np
 
     import oracle
@@ -462,23 +463,28 @@ def stack_cpu_seconds_per_token(cfg, threads):
     from kernite_b200 import stack as st
 
     rng = np.random.default_rng(0)
-    t_layer = 0.0
+    counts = [threads, 1] if also_single else [threads]
+    t = {n: 0.0 for n in counts}
+
+    def timed(qtype, W, x, rows, k, scale):
+        for n in counts:
+            if n == threads:
+                oracle.matvec_cpu(qtype, W, x, rows, k, n)  # warm
+            t0 = time.perf_counter()
+            oracle.matvec_cpu(qtype, W, x, rows, k, n)
+            t[n] += scale * (time.perf_counter() - t0)
+
     for name, qtype, rows, k in cfg.matrices():
         W = oracle.fill(qtype, oracle.stream_key(cfg.seed, cfg.tensor_id(0, name)), 0, rows * k // st.QK)
-        x = rng.standard_normal((1, k), dtype=np.float32)
-        oracle.matvec_cpu(qtype, W, x, rows, k, threads)  # warm
-        t0 = time.perf_counter()
-        oracle.matvec_cpu(qtype, W, x, rows, k, threads)
-        t_layer += time.perf_counter() - t0
+        timed(qtype, W, rng.standard_normal((1, k), dtype=np.float32), rows, k, cfg.layers)
         del W
     H = oracle.fill(6, oracle.stream_key(cfg.seed, cfg.tensor_id(cfg.layers, "head")), 0,
                     cfg.vocab * cfg.hidden // st.QK)
-    xh = rng.standard_normal((1, cfg.hidden), dtype=np.float32)
-    t0 = time.perf_counter()
-    oracle.matvec_cpu(6, H, xh, cfg.vocab, cfg.hidden, threads)
-    t_head = time.perf_counter() - t0
-    sec = cfg.layers * t_layer + t_head
-    return sec, f"layer 0 (4 matvecs) and the head timed once each, scaled to {cfg.layers} layers"
+    timed(6, H, rng.standard_normal((1, cfg.hidden), dtype=np.float32), cfg.vocab, cfg.hidden, 1)
+    sample = f"layer 0 (4 matvecs) and the head timed once each, scaled to {cfg.layers} layers"
+    if also_single:
+        return t[threads], sample, t[1]
+    return t[threads], sample
 
 
 def run_stack(args):
@@ -607,9 +613,10 @@ def run_stack(args):
                 "note": "achieved = the stack's weight bytes per GPU per token / token time"}
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        sec, sample = stack_cpu_seconds_per_token(cfg, HOST_THREADS)
+        sec, sample, sec1 = stack_cpu_seconds_per_token(cfg, HOST_THREADS, also_single=True)
         cpu = {"value": round(1.0 / sec, 4), "unit": "tokens/s", "cores": HOST_THREADS,
-               "kind": "port", "sample": sample, "cpu_model": cpu_model()}
+               "kind": "port", "sample": sample, "cpu_model": cpu_model(),
+               "single_thread": {"value": round(1.0 / sec1, 4), "sample": sample}}
     if rank == 0:
         line = {
             "metric": "decode tokens/s", "value": round(tps, 3), "unit": "tokens/s",
