@@ -52,6 +52,9 @@ enum {
 
 /* Quantisation types, GGML's type numbers. */
 enum { KQ_TYPE_Q4_K = 12, KQ_TYPE_Q5_K = 13, KQ_TYPE_Q6_K = 14 };
+/* Types the library decodes and generates but does not multiply yet (kq_dequant_* / kq_fill_*
+ * only; kq_matvec answers KQ_E_INVALID). */
+enum { KQ_TYPE_Q8_0 = 8, KQ_TYPE_Q2_K = 10, KQ_TYPE_Q3_K = 11 };
 
 /* What a matvec does to x before the product, and to each output after it. */
 enum { KQ_PROLOGUE_NONE = 0, KQ_PROLOGUE_RMSNORM = 1 };
@@ -162,6 +165,17 @@ int kq_dequant_q6k(kq_ctx* ctx, uint64_t out, uint64_t w, uint64_t nblocks, kq_s
  * aligned w): Q4_K's decode with q = nibble | fifth bit << 4, the fifth bit of element 32g + l
  * in bit g of qh[l]. */
 int kq_dequant_q5k(kq_ctx* ctx, uint64_t out, uint64_t w, uint64_t nblocks, kq_stream stream);
+/* Q2_K (84-byte blocks {u8 scales[16], u8 qs[64], fp16 d, fp16 dmin}): element 128h + 32s + l
+ * is bits 2s..2s+1 of qs[32h + l], sub-block e/16 has scale (low nibble) and min (high nibble)
+ * scales[e/16]; w = (f32(d)*f32(sc))*f32(q) - f32(dmin)*f32(m). */
+int kq_dequant_q2k(kq_ctx* ctx, uint64_t out, uint64_t w, uint64_t nblocks, kq_stream stream);
+/* Q3_K (110-byte blocks {u8 hmask[32], u8 qs[64], u8 scales[12], fp16 d}): q = bits 2s..2s+1
+ * of qs[32h + l], minus 4 unless bit 4h + s of hmask[l] is set; sixteen 6-bit scales stored + 32;
+ * w = (f32(d)*f32(scale))*f32(q). */
+int kq_dequant_q3k(kq_ctx* ctx, uint64_t out, uint64_t w, uint64_t nblocks, kq_stream stream);
+/* Q8_0, counted in units of eight 34-byte blocks {fp16 d, i8 qs[32]} (256 weights, 272 bytes):
+ * w = f32(q) * f32(d). nblocks = units. */
+int kq_dequant_q8_0(kq_ctx* ctx, uint64_t out, uint64_t w, uint64_t nblocks, kq_stream stream);
 
 /* Writes synthetic blocks [block0, block0 + nblocks) of the tensor whose stream key is `key`
  * at w (w points at block0): counter-based splitmix64, so any range is reproducible on the CPU.
@@ -175,6 +189,15 @@ int kq_fill_q6k(kq_ctx* ctx, uint64_t w, uint64_t block0, uint64_t nblocks, uint
 /* Q5_K: scale/qh/quant bytes uniform, d and dmin = fp16(uniform[2^-11, 2^-7]). */
 int kq_fill_q5k(kq_ctx* ctx, uint64_t w, uint64_t block0, uint64_t nblocks, uint64_t key,
                 kq_stream stream);
+/* Q2_K: scale/quant bytes uniform, d and dmin = fp16(uniform[2^-9, 2^-5]). Q3_K: hmask, quant
+ * and scale bytes uniform, d = fp16(uniform[2^-11, 2^-7]). Q8_0 (block0 and nblocks in units of
+ * eight blocks): quants uniform, d = fp16(uniform[2^-12, 2^-8]). Any alignment of w. */
+int kq_fill_q2k(kq_ctx* ctx, uint64_t w, uint64_t block0, uint64_t nblocks, uint64_t key,
+                kq_stream stream);
+int kq_fill_q3k(kq_ctx* ctx, uint64_t w, uint64_t block0, uint64_t nblocks, uint64_t key,
+                kq_stream stream);
+int kq_fill_q8_0(kq_ctx* ctx, uint64_t w, uint64_t block0, uint64_t nblocks, uint64_t key,
+                 kq_stream stream);
 
 /* The stream key of tensor `tensor` under `seed` (host function; the same as the oracle's). */
 uint64_t kq_stream_key(uint64_t seed, uint64_t tensor);

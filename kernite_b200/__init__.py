@@ -35,6 +35,9 @@ KQ_E_COMM = 1004
 TYPE_Q4_K = 12
 TYPE_Q5_K = 13
 TYPE_Q6_K = 14
+TYPE_Q8_0 = 8   # decode and generator only (no matvec yet)
+TYPE_Q2_K = 10  # decode and generator only
+TYPE_Q3_K = 11  # decode and generator only
 PROLOGUE_NONE = 0
 PROLOGUE_RMSNORM = 1
 EPILOGUE_NONE = 0
@@ -49,13 +52,17 @@ FLAG_WARP_MMA = 16
 Q4K_BYTES = 144
 Q6K_BYTES = 210
 Q5K_BYTES = 176
+Q2K_BYTES = 84
+Q3K_BYTES = 110
+Q8_0_UNIT_BYTES = 272  # eight 34-byte Q8_0 blocks = 256 weights
 QK = 256
 
 # Every symbol include/kq.h declares (tests check the library exports each).
 EXPORTS = (
     "kq_ctx_create", "kq_ctx_destroy", "kq_last_error", "kq_ctx_info", "kq_device_error",
     "kq_matvec_q4k", "kq_matvec_q6k", "kq_matvec", "kq_matvec_host", "kq_dequant_q4k", "kq_dequant_q6k",
-    "kq_fill_q4k", "kq_fill_q6k", "kq_dequant_q5k", "kq_fill_q5k", "kq_stream_key", "kq_matvec_q4k_noalloc",
+    "kq_fill_q4k", "kq_fill_q6k", "kq_dequant_q5k", "kq_fill_q5k", "kq_dequant_q2k", "kq_dequant_q3k",
+    "kq_dequant_q8_0", "kq_fill_q2k", "kq_fill_q3k", "kq_fill_q8_0", "kq_stream_key", "kq_matvec_q4k_noalloc",
     "kq_matvec_push", "kq_wait_counter", "kq_peer_alloc", "kq_peer_open", "kq_peer_close", "kq_peer_free",
     "kq_gguf_open", "kq_gguf_close", "kq_gguf_tensor_count", "kq_gguf_tensor_at", "kq_gguf_find",
     "kq_gguf_meta_int", "kq_gguf_meta_str",
@@ -125,9 +132,11 @@ def lib() -> ctypes.CDLL:
         getattr(L, name).argtypes = [vp, u64, u64, u64, u32, u32, u32, vp]
     L.kq_matvec.argtypes = [vp, ctypes.POINTER(KqMatvecDesc), vp]
     L.kq_matvec_host.argtypes = [vp, ctypes.POINTER(KqMatvecDesc), vp, vp, vp]
-    for name in ("kq_dequant_q4k", "kq_dequant_q5k", "kq_dequant_q6k"):
+    for name in ("kq_dequant_q4k", "kq_dequant_q5k", "kq_dequant_q6k", "kq_dequant_q2k",
+                 "kq_dequant_q3k", "kq_dequant_q8_0"):
         getattr(L, name).argtypes = [vp, u64, u64, u64, vp]
-    for name in ("kq_fill_q4k", "kq_fill_q5k", "kq_fill_q6k"):
+    for name in ("kq_fill_q4k", "kq_fill_q5k", "kq_fill_q6k", "kq_fill_q2k", "kq_fill_q3k",
+                 "kq_fill_q8_0"):
         getattr(L, name).argtypes = [vp, u64, u64, u64, u64, vp]
     L.kq_stream_key.argtypes = [u64, u64]
     L.kq_stream_key.restype = u64
@@ -298,13 +307,18 @@ class Kernels:
                                     _stream(stream)), "kq_matvec_host")
 
     def dequant(self, qtype: int, out, w, nblocks: int, stream=None) -> None:
-        """Bit-exact decode of ``nblocks`` blocks into f32 (verification kernel)."""
-        fn = {4: lib().kq_dequant_q4k, 5: lib().kq_dequant_q5k, 6: lib().kq_dequant_q6k}[_qt(qtype)]
+        """Bit-exact decode of ``nblocks`` blocks (units of 256 weights) into f32 (verification
+        kernel)."""
+        L = lib()
+        fn = {2: L.kq_dequant_q2k, 3: L.kq_dequant_q3k, 4: L.kq_dequant_q4k, 5: L.kq_dequant_q5k,
+              6: L.kq_dequant_q6k, 8: L.kq_dequant_q8_0}[_qt(qtype)]
         _check(fn(self._ctx, _addr(out), _addr(w), nblocks, _stream(stream)), "kq_dequant")
 
     def fill(self, qtype: int, w, block0: int, nblocks: int, key: int, stream=None) -> None:
         """Synthetic blocks [block0, block0 + nblocks) of the keyed tensor, written at w."""
-        fn = {4: lib().kq_fill_q4k, 5: lib().kq_fill_q5k, 6: lib().kq_fill_q6k}[_qt(qtype)]
+        L = lib()
+        fn = {2: L.kq_fill_q2k, 3: L.kq_fill_q3k, 4: L.kq_fill_q4k, 5: L.kq_fill_q5k,
+              6: L.kq_fill_q6k, 8: L.kq_fill_q8_0}[_qt(qtype)]
         _check(fn(self._ctx, _addr(w), block0, nblocks, key & (2**64 - 1), _stream(stream)), "kq_fill")
 
     def matvec_q4k_noalloc(self, y, w, x, rows: int, k: int, batch: int = 1, stream=None) -> None:
@@ -363,12 +377,15 @@ class DeviceArray:
 
 
 def _qt(qtype: int) -> int:
-    """4, 5 or 6 for a type given as 4/5/6 or as its GGML number."""
-    return {TYPE_Q4_K: 4, TYPE_Q5_K: 5, TYPE_Q6_K: 6}.get(qtype, qtype)
+    """The type's bit width (2..6; 8 for Q8_0) for a type given that way or by its GGML number
+    (10..14, 8)."""
+    return {TYPE_Q2_K: 2, TYPE_Q3_K: 3, TYPE_Q4_K: 4, TYPE_Q5_K: 5, TYPE_Q6_K: 6}.get(qtype, qtype)
 
 
 def block_bytes(qtype: int) -> int:
-    return {4: Q4K_BYTES, 5: Q5K_BYTES, 6: Q6K_BYTES}[_qt(qtype)]
+    """Bytes per 256 weights (a super-block; for Q8_0 eight blocks)."""
+    return {2: Q2K_BYTES, 3: Q3K_BYTES, 4: Q4K_BYTES, 5: Q5K_BYTES, 6: Q6K_BYTES,
+            8: Q8_0_UNIT_BYTES}[_qt(qtype)]
 
 
 def matrix_bytes(qtype: int, rows: int, k: int) -> int:

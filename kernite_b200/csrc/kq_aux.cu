@@ -12,8 +12,12 @@
 // The generator reproduces the oracle's kqo_fill_q4k / q5k / q6k byte for byte: splitmix64
 // output number i of the tensor's keyed stream, integer work plus one binary32 multiply, one
 // add and a round-to-nearest-even narrowing to fp16 per scale.
+//
+// Q2_K, Q3_K and Q8_0 (units of 256 weights; a Q8_0 unit is eight 34-byte blocks) decode and
+// generate through the __host__ __device__ functions of kq_decode.cuh.
 #include <cuda_runtime.h>
 
+#include "kq_decode.cuh"
 #include "kq_device.cuh"
 #include "kq_internal.h"
 
@@ -181,6 +185,25 @@ __global__ void dequant_q5k_kernel(float* out, const uint8_t* w, uint64_t nblock
   }
 }
 
+// Q2_K / Q3_K / Q8_0: one thread per weight
+template <int T>
+__global__ void dequant_unit_kernel(float* out, const uint8_t* w, uint64_t nunits) {
+  constexpr uint32_t kUnit = T == 2 ? dec::kQ2KBytes : T == 3 ? dec::kQ3KBytes : dec::kQ8Unit;
+  const uint64_t total = nunits * kQK;
+  for (uint64_t t = blockIdx.x * uint64_t(blockDim.x) + threadIdx.x; t < total;
+       t += uint64_t(gridDim.x) * blockDim.x)
+    out[t] = dec::weight(T, w + (t / kQK) * kUnit, static_cast<uint32_t>(t % kQK));
+}
+
+// Q2_K / Q3_K / Q8_0: one thread per unit, units [b0, b0 + n) of the tensor at w (w = unit b0)
+template <int T>
+__global__ void fill_unit_kernel(uint8_t* w, uint64_t b0, uint64_t n, uint64_t key) {
+  constexpr uint32_t kUnit = T == 2 ? dec::kQ2KBytes : T == 3 ? dec::kQ3KBytes : dec::kQ8Unit;
+  for (uint64_t i = blockIdx.x * uint64_t(blockDim.x) + threadIdx.x; i < n;
+       i += uint64_t(gridDim.x) * blockDim.x)
+    dec::fill_unit(T, w + i * kUnit, key, b0 + i);
+}
+
 uint32_t grid_for(uint64_t work, uint32_t threads, int sm_count) {
   const uint64_t want = (work + threads - 1) / threads;
   const uint64_t cap = uint64_t(sm_count) * 16;
@@ -212,14 +235,34 @@ int wait_counter(kq_ctx* ctx, uint64_t counter, uint64_t epoch, uint64_t mul, ui
   return KQ_OK;
 }
 
+namespace {
+const char* type_call(const char* verb, int type) {
+  static const char* const names[2][9] = {
+      {"", "", "kq_dequant_q2k", "kq_dequant_q3k", "kq_dequant_q4k", "kq_dequant_q5k",
+       "kq_dequant_q6k", "", "kq_dequant_q8_0"},
+      {"", "", "kq_fill_q2k", "kq_fill_q3k", "kq_fill_q4k", "kq_fill_q5k", "kq_fill_q6k", "",
+       "kq_fill_q8_0"}};
+  return (type >= 2 && type <= 8) ? names[verb[0] == 'f'][type] : "kq_dequant";
+}
+}  // namespace
+
 int dequant(kq_ctx* ctx, int type, uint64_t out, uint64_t w, uint64_t nblocks, cudaStream_t s) {
-  const char* call = type == 4 ? "kq_dequant_q4k" : type == 5 ? "kq_dequant_q5k" : "kq_dequant_q6k";
+  const char* call = type_call("dequant", type);
   if (nblocks == 0) return KQ_OK;
   if (!out || !w) return fail(KQ_E_INVALID, call, "null pointer");
   if (out % 4 || w % 2) return fail(KQ_E_INVALID, call, "out must be 4-byte and w 2-byte aligned");
   const uint32_t threads = 256;
   const uint32_t grid = grid_for(nblocks * kQK, threads, ctx->sm_count);
-  if (type == 4)
+  if (type == 2)
+    dequant_unit_kernel<2><<<grid, threads, 0, s>>>(reinterpret_cast<float*>(out),
+                                                    reinterpret_cast<const uint8_t*>(w), nblocks);
+  else if (type == 3)
+    dequant_unit_kernel<3><<<grid, threads, 0, s>>>(reinterpret_cast<float*>(out),
+                                                    reinterpret_cast<const uint8_t*>(w), nblocks);
+  else if (type == 8)
+    dequant_unit_kernel<8><<<grid, threads, 0, s>>>(reinterpret_cast<float*>(out),
+                                                    reinterpret_cast<const uint8_t*>(w), nblocks);
+  else if (type == 4)
     dequant_q4k_kernel<<<grid, threads, 0, s>>>(reinterpret_cast<float*>(out),
                                                  reinterpret_cast<const uint8_t*>(w), nblocks);
   else if (type == 5)
@@ -235,14 +278,20 @@ int dequant(kq_ctx* ctx, int type, uint64_t out, uint64_t w, uint64_t nblocks, c
 
 int fill(kq_ctx* ctx, int type, uint64_t w, uint64_t block0, uint64_t nblocks, uint64_t key,
          cudaStream_t s) {
-  const char* call = type == 4 ? "kq_fill_q4k" : type == 5 ? "kq_fill_q5k" : "kq_fill_q6k";
+  const char* call = type_call("fill", type);
   if (nblocks == 0) return KQ_OK;
   if (!w) return fail(KQ_E_INVALID, call, "null pointer");
-  if (type != 6 && w % 16) return fail(KQ_E_INVALID, call, "w must be 16-byte aligned");
+  if ((type == 4 || type == 5) && w % 16) return fail(KQ_E_INVALID, call, "w must be 16-byte aligned");
   if (type == 6 && w % 2) return fail(KQ_E_INVALID, call, "w must be 2-byte aligned");
   const uint32_t threads = 128;
   const uint32_t grid = grid_for(nblocks, threads, ctx->sm_count);
-  if (type == 4)
+  if (type == 2)
+    fill_unit_kernel<2><<<grid, threads, 0, s>>>(reinterpret_cast<uint8_t*>(w), block0, nblocks, key);
+  else if (type == 3)
+    fill_unit_kernel<3><<<grid, threads, 0, s>>>(reinterpret_cast<uint8_t*>(w), block0, nblocks, key);
+  else if (type == 8)
+    fill_unit_kernel<8><<<grid, threads, 0, s>>>(reinterpret_cast<uint8_t*>(w), block0, nblocks, key);
+  else if (type == 4)
     fill_q4k_kernel<<<grid, threads, 0, s>>>(reinterpret_cast<uint8_t*>(w), block0, nblocks, key);
   else if (type == 5)
     fill_q5k_kernel<<<grid, threads, 0, s>>>(reinterpret_cast<uint8_t*>(w), block0, nblocks, key);
