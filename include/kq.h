@@ -52,8 +52,8 @@ enum {
 
 /* Quantisation types, GGML's type numbers. */
 enum { KQ_TYPE_Q4_K = 12, KQ_TYPE_Q5_K = 13, KQ_TYPE_Q6_K = 14 };
-/* Types the library decodes and generates but does not multiply yet (kq_dequant_* / kq_fill_*
- * only; kq_matvec answers KQ_E_INVALID). */
+/* Types the library decodes but does not multiply yet (kq_dequant_* only; kq_matvec answers
+ * KQ_E_INVALID). */
 enum { KQ_TYPE_Q8_0 = 8, KQ_TYPE_Q2_K = 10, KQ_TYPE_Q3_K = 11 };
 
 /* What a matvec does to x before the product, and to each output after it. */
@@ -189,15 +189,6 @@ int kq_fill_q6k(kq_ctx* ctx, uint64_t w, uint64_t block0, uint64_t nblocks, uint
 /* Q5_K: scale/qh/quant bytes uniform, d and dmin = fp16(uniform[2^-11, 2^-7]). */
 int kq_fill_q5k(kq_ctx* ctx, uint64_t w, uint64_t block0, uint64_t nblocks, uint64_t key,
                 kq_stream stream);
-/* Q2_K: scale/quant bytes uniform, d and dmin = fp16(uniform[2^-9, 2^-5]). Q3_K: hmask, quant
- * and scale bytes uniform, d = fp16(uniform[2^-11, 2^-7]). Q8_0 (block0 and nblocks in units of
- * eight blocks): quants uniform, d = fp16(uniform[2^-12, 2^-8]). Any alignment of w. */
-int kq_fill_q2k(kq_ctx* ctx, uint64_t w, uint64_t block0, uint64_t nblocks, uint64_t key,
-                kq_stream stream);
-int kq_fill_q3k(kq_ctx* ctx, uint64_t w, uint64_t block0, uint64_t nblocks, uint64_t key,
-                kq_stream stream);
-int kq_fill_q8_0(kq_ctx* ctx, uint64_t w, uint64_t block0, uint64_t nblocks, uint64_t key,
-                 kq_stream stream);
 
 /* The stream key of tensor `tensor` under `seed` (host function; the same as the oracle's). */
 uint64_t kq_stream_key(uint64_t seed, uint64_t tensor);

@@ -35,9 +35,9 @@ KQ_E_COMM = 1004
 TYPE_Q4_K = 12
 TYPE_Q5_K = 13
 TYPE_Q6_K = 14
-TYPE_Q8_0 = 8   # decode and generator only (no matvec yet)
-TYPE_Q2_K = 10  # decode and generator only
-TYPE_Q3_K = 11  # decode and generator only
+TYPE_Q8_0 = 8   # decode only (no matvec yet)
+TYPE_Q2_K = 10  # decode only
+TYPE_Q3_K = 11  # decode only
 PROLOGUE_NONE = 0
 PROLOGUE_RMSNORM = 1
 EPILOGUE_NONE = 0
@@ -62,7 +62,7 @@ EXPORTS = (
     "kq_ctx_create", "kq_ctx_destroy", "kq_last_error", "kq_ctx_info", "kq_device_error",
     "kq_matvec_q4k", "kq_matvec_q6k", "kq_matvec", "kq_matvec_host", "kq_dequant_q4k", "kq_dequant_q6k",
     "kq_fill_q4k", "kq_fill_q6k", "kq_dequant_q5k", "kq_fill_q5k", "kq_dequant_q2k", "kq_dequant_q3k",
-    "kq_dequant_q8_0", "kq_fill_q2k", "kq_fill_q3k", "kq_fill_q8_0", "kq_stream_key", "kq_matvec_q4k_noalloc",
+    "kq_dequant_q8_0", "kq_stream_key", "kq_matvec_q4k_noalloc",
     "kq_matvec_push", "kq_wait_counter", "kq_peer_alloc", "kq_peer_open", "kq_peer_close", "kq_peer_free",
     "kq_gguf_open", "kq_gguf_close", "kq_gguf_tensor_count", "kq_gguf_tensor_at", "kq_gguf_find",
     "kq_gguf_meta_int", "kq_gguf_meta_str",
@@ -135,8 +135,7 @@ def lib() -> ctypes.CDLL:
     for name in ("kq_dequant_q4k", "kq_dequant_q5k", "kq_dequant_q6k", "kq_dequant_q2k",
                  "kq_dequant_q3k", "kq_dequant_q8_0"):
         getattr(L, name).argtypes = [vp, u64, u64, u64, vp]
-    for name in ("kq_fill_q4k", "kq_fill_q5k", "kq_fill_q6k", "kq_fill_q2k", "kq_fill_q3k",
-                 "kq_fill_q8_0"):
+    for name in ("kq_fill_q4k", "kq_fill_q5k", "kq_fill_q6k"):
         getattr(L, name).argtypes = [vp, u64, u64, u64, u64, vp]
     L.kq_stream_key.argtypes = [u64, u64]
     L.kq_stream_key.restype = u64
@@ -316,9 +315,7 @@ class Kernels:
 
     def fill(self, qtype: int, w, block0: int, nblocks: int, key: int, stream=None) -> None:
         """Synthetic blocks [block0, block0 + nblocks) of the keyed tensor, written at w."""
-        L = lib()
-        fn = {2: L.kq_fill_q2k, 3: L.kq_fill_q3k, 4: L.kq_fill_q4k, 5: L.kq_fill_q5k,
-              6: L.kq_fill_q6k, 8: L.kq_fill_q8_0}[_qt(qtype)]
+        fn = {4: lib().kq_fill_q4k, 5: lib().kq_fill_q5k, 6: lib().kq_fill_q6k}[_qt(qtype)]
         _check(fn(self._ctx, _addr(w), block0, nblocks, key & (2**64 - 1), _stream(stream)), "kq_fill")
 
     def matvec_q4k_noalloc(self, y, w, x, rows: int, k: int, batch: int = 1, stream=None) -> None:

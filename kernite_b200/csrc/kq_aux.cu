@@ -13,8 +13,8 @@
 // output number i of the tensor's keyed stream, integer work plus one binary32 multiply, one
 // add and a round-to-nearest-even narrowing to fp16 per scale.
 //
-// Q2_K, Q3_K and Q8_0 (units of 256 weights; a Q8_0 unit is eight 34-byte blocks) decode and
-// generate through the __host__ __device__ functions of kq_decode.cuh.
+// Q2_K, Q3_K and Q8_0 (units of 256 weights; a Q8_0 unit is eight 34-byte blocks) decode through
+// the __host__ __device__ functions of kq_decode.cuh.
 #include <cuda_runtime.h>
 
 #include "kq_decode.cuh"
@@ -195,15 +195,6 @@ __global__ void dequant_unit_kernel(float* out, const uint8_t* w, uint64_t nunit
     out[t] = dec::weight(T, w + (t / kQK) * kUnit, static_cast<uint32_t>(t % kQK));
 }
 
-// Q2_K / Q3_K / Q8_0: one thread per unit, units [b0, b0 + n) of the tensor at w (w = unit b0)
-template <int T>
-__global__ void fill_unit_kernel(uint8_t* w, uint64_t b0, uint64_t n, uint64_t key) {
-  constexpr uint32_t kUnit = T == 2 ? dec::kQ2KBytes : T == 3 ? dec::kQ3KBytes : dec::kQ8Unit;
-  for (uint64_t i = blockIdx.x * uint64_t(blockDim.x) + threadIdx.x; i < n;
-       i += uint64_t(gridDim.x) * blockDim.x)
-    dec::fill_unit(T, w + i * kUnit, key, b0 + i);
-}
-
 uint32_t grid_for(uint64_t work, uint32_t threads, int sm_count) {
   const uint64_t want = (work + threads - 1) / threads;
   const uint64_t cap = uint64_t(sm_count) * 16;
@@ -240,8 +231,7 @@ const char* type_call(const char* verb, int type) {
   static const char* const names[2][9] = {
       {"", "", "kq_dequant_q2k", "kq_dequant_q3k", "kq_dequant_q4k", "kq_dequant_q5k",
        "kq_dequant_q6k", "", "kq_dequant_q8_0"},
-      {"", "", "kq_fill_q2k", "kq_fill_q3k", "kq_fill_q4k", "kq_fill_q5k", "kq_fill_q6k", "",
-       "kq_fill_q8_0"}};
+      {"", "", "", "", "kq_fill_q4k", "kq_fill_q5k", "kq_fill_q6k", "", ""}};
   return (type >= 2 && type <= 8) ? names[verb[0] == 'f'][type] : "kq_dequant";
 }
 }  // namespace
@@ -285,13 +275,7 @@ int fill(kq_ctx* ctx, int type, uint64_t w, uint64_t block0, uint64_t nblocks, u
   if (type == 6 && w % 2) return fail(KQ_E_INVALID, call, "w must be 2-byte aligned");
   const uint32_t threads = 128;
   const uint32_t grid = grid_for(nblocks, threads, ctx->sm_count);
-  if (type == 2)
-    fill_unit_kernel<2><<<grid, threads, 0, s>>>(reinterpret_cast<uint8_t*>(w), block0, nblocks, key);
-  else if (type == 3)
-    fill_unit_kernel<3><<<grid, threads, 0, s>>>(reinterpret_cast<uint8_t*>(w), block0, nblocks, key);
-  else if (type == 8)
-    fill_unit_kernel<8><<<grid, threads, 0, s>>>(reinterpret_cast<uint8_t*>(w), block0, nblocks, key);
-  else if (type == 4)
+  if (type == 4)
     fill_q4k_kernel<<<grid, threads, 0, s>>>(reinterpret_cast<uint8_t*>(w), block0, nblocks, key);
   else if (type == 5)
     fill_q5k_kernel<<<grid, threads, 0, s>>>(reinterpret_cast<uint8_t*>(w), block0, nblocks, key);

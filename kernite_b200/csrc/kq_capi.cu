@@ -281,21 +281,10 @@ int kq_fill_q5k(kq_ctx* ctx, uint64_t w, uint64_t block0, uint64_t nblocks, uint
     if (rc) return rc;                                                                      \
     return kq::dequant(ctx, type, out, w, nblocks, static_cast<cudaStream_t>(stream));      \
   }
-#define KQ_FILL_ENTRY(name, type)                                                           \
-  int name(kq_ctx* ctx, uint64_t w, uint64_t block0, uint64_t nblocks, uint64_t key,       \
-           kq_stream stream) {                                                              \
-    if (!ctx) return fail(KQ_E_INVALID, #name, "null ctx");                                \
-    int rc = kq::enter(ctx);                                                                \
-    if (rc) return rc;                                                                      \
-    return kq::fill(ctx, type, w, block0, nblocks, key, static_cast<cudaStream_t>(stream)); \
-  }
 
 KQ_DEQUANT_ENTRY(kq_dequant_q2k, 2)
 KQ_DEQUANT_ENTRY(kq_dequant_q3k, 3)
 KQ_DEQUANT_ENTRY(kq_dequant_q8_0, 8)
-KQ_FILL_ENTRY(kq_fill_q2k, 2)
-KQ_FILL_ENTRY(kq_fill_q3k, 3)
-KQ_FILL_ENTRY(kq_fill_q8_0, 8)
 
 int kq_fill_q4k(kq_ctx* ctx, uint64_t w, uint64_t block0, uint64_t nblocks, uint64_t key,
                 kq_stream stream) {

@@ -1,7 +1,7 @@
-// kq_decode.cuh -- one weight of a Q2_K / Q3_K / Q8_0 unit of 256 weights, and the synthetic
-// generator's bytes for one unit, as __host__ __device__ functions. The device's verification
-// kernels (kq_aux.cu) call them; the same source compiled for the host is checked against the
-// CPU oracle and the gguf-py fixtures on a machine without a GPU.
+// kq_decode.cuh -- one weight of a Q2_K / Q3_K / Q8_0 unit of 256 weights, as __host__
+// __device__ functions. The device's verification kernel (kq_aux.cu) calls them; the same source
+// compiled for the host is checked against the CPU oracle and the gguf-py fixtures on a machine
+// without a GPU.
 //
 // Decode order is the canonical one of the CPU oracle, every float operation rounded to binary32
 // on its own (no contraction; __fmul_rn / __fsub_rn on the device, and a host build compiled with
@@ -38,14 +38,6 @@ KQ_HD float sub_rn(float a, float b) {
   return __fsub_rn(a, b);
 #else
   return a - b;
-#endif
-}
-
-KQ_HD float add_rn(float a, float b) {
-#if defined(__CUDA_ARCH__)
-  return __fadd_rn(a, b);
-#else
-  return a + b;
 #endif
 }
 
@@ -98,64 +90,6 @@ KQ_HD float q8_0_weight(const uint8_t* unit, uint32_t e) {
 
 KQ_HD float weight(int type, const uint8_t* unit, uint32_t e) {
   return type == 2 ? q2k_weight(unit, e) : type == 3 ? q3k_weight(unit, e) : q8_0_weight(unit, e);
-}
-
-// ---------------------------------------------------------------- generator
-
-KQ_HD uint64_t mix64(uint64_t z) {
-  z = (z ^ (z >> 30)) * 0xbf58476d1ce4e5b9ull;
-  z = (z ^ (z >> 27)) * 0x94d049bb133111ebull;
-  return z ^ (z >> 31);
-}
-
-// splitmix64's output number i of the stream with state `key`
-KQ_HD uint64_t splitmix_at(uint64_t key, uint64_t i) {
-  return mix64(key + (i + 1) * 0x9e3779b97f4a7c15ull);
-}
-
-// fp16(lo + u * span), u = the top 24 bits of `word` times 2^-24 (exact), one multiply, one add,
-// round to nearest even
-KQ_HD uint16_t uniform_fp16(uint64_t word, float lo, float span) {
-  const float u = static_cast<float>(static_cast<uint32_t>(word >> 40)) * 0x1p-24f;
-  return __half_as_ushort(__float2half_rn(add_rn(lo, mul_rn(u, span))));
-}
-
-// n bytes of counters base, base + 1, ...: byte i is byte i % 8 of output base + i / 8
-KQ_HD void put_bytes(uint8_t* dst, uint64_t key, uint64_t base, uint32_t n) {
-  for (uint32_t i = 0; i < n; i += 8) {
-    const uint64_t w = splitmix_at(key, base + i / 8);
-    for (uint32_t j = 0; j < 8 && i + j < n; ++j) dst[i + j] = static_cast<uint8_t>(w >> (8 * j));
-  }
-}
-
-KQ_HD void put_f16(uint8_t* p, uint16_t h) {
-  p[0] = static_cast<uint8_t>(h);
-  p[1] = static_cast<uint8_t>(h >> 8);
-}
-
-// Unit u of a synthetic tensor with stream key `key`, as the CPU oracle writes it:
-//   Q2_K block u: counters [13u, 13u + 13): words 0-10 its 84 bytes, then d (word 11) and dmin
-//     (word 12) = fp16(uniform [2^-9, 2^-5]) over bytes 80-83;
-//   Q3_K block u: counters [15u, 15u + 15): words 0-13 its 110 bytes, d (word 14) =
-//     fp16(uniform [2^-11, 2^-7]) over bytes 108-109;
-//   Q8_0 blocks j = 8u .. 8u + 7: counters [6j, 6j + 6): words 0-4 its 34 bytes, d (word 5) =
-//     fp16(uniform [2^-12, 2^-8]) over bytes 0-1.
-KQ_HD void fill_unit(int type, uint8_t* unit, uint64_t key, uint64_t u) {
-  if (type == 2) {
-    put_bytes(unit, key, 13 * u, kQ2KBytes);
-    put_f16(unit + 80, uniform_fp16(splitmix_at(key, 13 * u + 11), 0x1p-9f, 15.0f * 0x1p-9f));
-    put_f16(unit + 82, uniform_fp16(splitmix_at(key, 13 * u + 12), 0x1p-9f, 15.0f * 0x1p-9f));
-  } else if (type == 3) {
-    put_bytes(unit, key, 15 * u, kQ3KBytes);
-    put_f16(unit + 108, uniform_fp16(splitmix_at(key, 15 * u + 14), 0x1p-11f, 15.0f * 0x1p-11f));
-  } else {
-    for (uint32_t v = 0; v < 8; ++v) {
-      const uint64_t j = 8 * u + v;
-      uint8_t* blk = unit + v * kQ8Block;
-      put_bytes(blk, key, 6 * j, kQ8Block);
-      put_f16(blk, uniform_fp16(splitmix_at(key, 6 * j + 5), 0x1p-12f, 15.0f * 0x1p-12f));
-    }
-  }
 }
 
 }  // namespace dec

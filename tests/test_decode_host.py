@@ -1,7 +1,7 @@
-"""The device decoder and generator of Q2_K, Q3_K and Q8_0 (kernite_b200/csrc/kq_decode.cuh,
-__host__ __device__ functions) compiled for the host and checked without a GPU: bit for bit
-against the gguf-py 0.19.0 fixtures and against the CPU oracle's generator. The GPU tests then
-check the kernels that call the same functions (tests/test_more_types_gpu.py)."""
+"""The device decoder of Q2_K, Q3_K and Q8_0 (kernite_b200/csrc/kq_decode.cuh, __host__
+__device__ functions) compiled for the host and checked without a GPU: bit for bit against the
+gguf-py 0.19.0 fixtures and the CPU oracle. The GPU tests then check the kernel that calls the
+same functions (tests/test_more_types_gpu.py)."""
 import ctypes
 import os
 import shutil
@@ -28,8 +28,6 @@ def host(tmp_path_factory):
                     os.path.join(ROOT, "tests", "host", "host_decode.cu"), "-o", out], check=True)
     L = ctypes.CDLL(out)
     L.kqh_dequant.argtypes = [ctypes.c_int, ctypes.c_void_p, ctypes.c_uint64, ctypes.c_void_p]
-    L.kqh_fill.argtypes = [ctypes.c_int, ctypes.c_void_p, ctypes.c_uint64, ctypes.c_uint64,
-                           ctypes.c_uint64]
     return L
 
 
@@ -53,12 +51,7 @@ def test_device_decode_source_matches_gguf(host, golden, qtype, which):
 
 
 @pytest.mark.parametrize("qtype", TYPES)
-def test_device_generator_source_matches_oracle(host, qtype):
-    key = oracle.stream_key(11, qtype)
-    b0, n = 123, 500
-    out = np.zeros(n * oracle.block_bytes(qtype), dtype=np.uint8)
-    assert host.kqh_fill(qtype, out.ctypes.data, key, b0, n) == 0
-    assert np.array_equal(out, oracle.fill(qtype, key, b0, n))
-    # and the decode of generated units equals the oracle's
-    assert np.array_equal(dequant(host, qtype, out).view(np.uint32),
-                          oracle.dequant(qtype, out).view(np.uint32))
+def test_device_decode_source_matches_oracle_on_generated(host, qtype):
+    blocks = oracle.fill(qtype, oracle.stream_key(11, qtype), 123, 500)
+    assert np.array_equal(dequant(host, qtype, blocks).view(np.uint32),
+                          oracle.dequant(qtype, blocks).view(np.uint32))
