@@ -53,7 +53,11 @@ def test_ctx_create_rejects_null_out():
 def test_entry_points_reject_null_ctx():
     L = kb.lib()
     assert L.kq_matvec_q4k(None, 0, 0, 0, 1, 256, 1, None) == kb.KQ_E_INVALID
-    assert L.kq_dequant_q6k(None, 0, 0, 1, None) == kb.KQ_E_INVALID
+    for name in ("kq_dequant_q4k", "kq_dequant_q5k", "kq_dequant_q6k", "kq_dequant_q2k",
+                 "kq_dequant_q3k", "kq_dequant_q8_0"):
+        assert getattr(L, name)(None, 0, 0, 1, None) == kb.KQ_E_INVALID, name
+    for name in ("kq_fill_q5k", "kq_fill_q6k"):
+        assert getattr(L, name)(None, 0, 0, 1, 0, None) == kb.KQ_E_INVALID, name
     assert L.kq_fill_q4k(None, 0, 0, 1, 0, None) == kb.KQ_E_INVALID
     d = kb.KqMatvecDesc()
     assert L.kq_matvec(None, ctypes.byref(d), None) == kb.KQ_E_INVALID
