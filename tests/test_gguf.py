@@ -39,6 +39,10 @@ def write_model(path, alignment=None):
     tensors = {
         "blk.0.attn_q.weight": (T.Q4_K, quant_bytes(4, 48, 512, 11)),
         "blk.0.ffn_down.weight": (T.Q6_K, quant_bytes(6, 40, 768, 12)),
+        "blk.0.ffn_up.weight": (T.Q5_K, quant_bytes(5, 32, 512, 13)),
+        "blk.1.attn_k.weight": (T.Q8_0, quant_bytes(8, 16, 512, 14)),
+        "blk.1.attn_v.weight": (T.Q2_K, quant_bytes(2, 16, 256, 15)),
+        "blk.1.ffn_gate.weight": (T.Q3_K, quant_bytes(3, 24, 512, 16)),
         "token_embd.weight": (None, np.arange(15, dtype=np.float32).reshape(3, 5)),
         "output_norm.weight": (None, np.linspace(-1, 1, 7).astype(np.float16)),
     }
@@ -75,6 +79,15 @@ def test_reader_agrees_with_gguf_py(tmp_path, alignment):
         assert (q.qtype, q.rows, q.k) == (4, 48, 512)
         d = f.tensor("blk.0.ffn_down.weight")
         assert (d.qtype, d.rows, d.k) == (6, 40, 768)
+        u = f.tensor("blk.0.ffn_up.weight")
+        assert (u.qtype, u.rows, u.k) == (5, 32, 512)
+        for name, ggml_type, rows, k in (("blk.1.attn_k.weight", 8, 16, 512),
+                                         ("blk.1.attn_v.weight", 10, 16, 256),
+                                         ("blk.1.ffn_gate.weight", 11, 24, 512)):
+            t = f.tensor(name)
+            assert (t.type, t.rows, t.k) == (ggml_type, rows, k), name
+            with pytest.raises(kb.Error):  # decoded, not multiplied
+                t.qtype
         assert f.meta_int("llama.block_count") == 2
         assert f.meta_int("test.negative") == -5
         assert f.meta_int("test.flag") == 1
@@ -123,7 +136,7 @@ def test_gguf_weights_multiply_like_the_oracle_and_gguf_py(tmp_path):
     write_model(path)
     kernels = kb.Kernels.load(0)
     with GGUFFile(path) as f:
-        for name in ("blk.0.attn_q.weight", "blk.0.ffn_down.weight"):
+        for name in ("blk.0.attn_q.weight", "blk.0.ffn_down.weight", "blk.0.ffn_up.weight"):
             t = f.tensor(name)
             W = t.to_device()
             x = np.random.default_rng(5).standard_normal((1, t.k), dtype=np.float32)
@@ -137,3 +150,23 @@ def test_gguf_weights_multiply_like_the_oracle_and_gguf_py(tmp_path):
             wf = gguf.quants.dequantize(np.array(t.data).reshape(t.rows, -1), T(t.type))
             y_gg = wf.astype(np.float64) @ x[0].astype(np.float64)
             assert (np.abs(y[0] - y_gg) <= 1e-3 * bound[0]).all(), name
+
+
+@pytest.mark.gpu
+def test_gguf_weights_decode_like_gguf_py(tmp_path):
+    import torch
+
+    path = tmp_path / "m.gguf"
+    write_model(path)
+    kernels = kb.Kernels.load(0)
+    with GGUFFile(path) as f:
+        for name in ("blk.0.attn_q.weight", "blk.0.ffn_down.weight", "blk.0.ffn_up.weight",
+                     "blk.1.attn_k.weight", "blk.1.attn_v.weight", "blk.1.ffn_gate.weight"):
+            t = f.tensor(name)
+            n = t.rows * t.k // 256
+            out = torch.empty(n * 256, dtype=torch.float32, device="cuda")
+            kernels.dequant(t.type, out, t.to_device(), n)
+            torch.cuda.synchronize()
+            want = gguf.quants.dequantize(np.array(t.data).reshape(t.rows, -1), T(t.type))
+            want = np.ascontiguousarray(want, dtype=np.float32).reshape(-1)
+            assert np.array_equal(out.cpu().numpy().view(np.uint32), want.view(np.uint32)), name
