@@ -1,4 +1,4 @@
-"""kernite_b200 -- a B200-native Q4_K / Q6_K matvec behind kernite-cuda's call surface.
+"""kernite_b200 -- a B200-native Q4_K / Q5_K / Q6_K matvec behind kernite-cuda's call surface.
 
 The product is ``libkq.so`` (hand-written CUDA for sm_100a behind the C ABI in
 ``include/kq.h``). This module is the host-side mirror of fxeqxmulfx/kernite's interface for the
@@ -285,7 +285,8 @@ class Kernels:
     def matvec(self, qtype: int, y, w, x, rows: int, k: int, batch: int = 1, *, ldx: int = 0,
                ldy: int = 0, prologue: int = PROLOGUE_NONE, epilogue: int = EPILOGUE_NONE,
                eps: float = 0.0, pair_scale: float = 1.0, flags: int = 0, stream=None) -> None:
-        """The general matvec (``kq_matvec``); qtype is 4/6 or TYPE_Q4_K/TYPE_Q6_K."""
+        """The general matvec (``kq_matvec``); qtype is 4/5/6 or TYPE_Q4_K/TYPE_Q5_K/TYPE_Q6_K
+        (Q5_K at batch 1 only)."""
         t = {4: TYPE_Q4_K, 5: TYPE_Q5_K, 6: TYPE_Q6_K}.get(qtype, qtype)
         d = KqMatvecDesc(type=t, rows=rows, k=k, batch=batch, y=_addr(y), w=_addr(w), x=_addr(x),
                          ldx=ldx, ldy=ldy, prologue=prologue, epilogue=epilogue, eps=eps,
