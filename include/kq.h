@@ -6,7 +6,7 @@
  * (crates/macros/src/gpu.rs:276-328) on a `Kernels` struct that `Kernels::load(&Cuda)` fills by
  * loading a module (crates/macros/src/gpu.rs:74-98, crates/cuda/src/lib.rs:945-1016), and
  * launches with `cuLaunchKernel` (crates/cuda/src/lib.rs:1045-1054). Each entry point below
- * replaces one piece of that, as its comment says; INTEGRATION.md shows the Rust binding.
+ * replaces one piece of that, as its comment says.
  *
  * Conventions (kernite-cuda's, kept):
  *  - Device pointers are plain 64-bit addresses, exactly what `kernite_cuda::Ptr::addr()`
@@ -19,7 +19,11 @@
  *  - Launches are asynchronous on the given stream (NULL = the legacy default stream, on which
  *    kernite launches everything, crates/cuda/src/lib.rs:1051).
  *  - A kq_ctx is for the thread and GPU that made it, as a kernite `Cuda` is
- *    (crates/cuda/src/lib.rs:27-35). Entry points make the ctx's device current if it is not.
+ *    (crates/cuda/src/lib.rs:27-35). kq_ctx_create leaves its device current, as Cuda::on makes
+ *    its context current; every other entry point makes the ctx's device current for the call
+ *    if it is not, and makes the caller's device current again before it returns.
+ *  - Each kq_ctx has its own device error word: errors recorded by one ctx's launches are read
+ *    and cleared by kq_device_error on that ctx only.
  *
  * Safety contract (kernite's launcher contract, crates/cuda/src/lib.rs:1035-1044): every pointer
  * must be device memory of the ctx's GPU, valid until the launch completes; the host must not

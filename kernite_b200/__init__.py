@@ -22,9 +22,8 @@ import os
 from typing import Any
 
 HERE = os.path.dirname(os.path.abspath(__file__))
-# KQ_LIBRARY names another build of the same ABI (an A/B build of the kernels); by default the
-# in-tree libkq.so.
-LIB_PATH = os.environ.get("KQ_LIBRARY") or os.path.join(HERE, "libkq.so")
+# The in-tree build of the library (kernite_b200/build.py writes it).
+LIB_PATH = os.path.join(HERE, "libkq.so")
 
 KQ_OK = 0
 KQ_E_INVALID = 1001

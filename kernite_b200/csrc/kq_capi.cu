@@ -12,9 +12,9 @@
 #include "kq_device.cuh"
 #include "kq_internal.h"
 
-// The device error word that bounded waits write instead of hanging. A file-scope device
-// variable: every GPU that loads the library has its own copy; host code takes its address with
-// cudaGetSymbolAddress per device in kq_ctx_create.
+// The device error word of kq_matvec_q4k_noalloc, which has no context to hold one: a file-scope
+// device variable (zero at load; every GPU that loads the library has its own copy), whose
+// address host code takes with cudaGetSymbolAddress per device. A kq_ctx has its own word.
 __device__ unsigned g_kq_error_word;
 
 namespace kq {
@@ -45,15 +45,20 @@ int error_word_address(unsigned** out) {
   return KQ_OK;
 }
 
-int enter(const kq_ctx* ctx) {
+int DeviceScope::enter(const kq_ctx* ctx) {
   int cur = -1;
   cudaError_t e = cudaGetDevice(&cur);
   if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
   if (cur != ctx->device) {
     e = cudaSetDevice(ctx->device);
     if (e != cudaSuccess) return cuda_fail(e, "cudaSetDevice");
+    restore_ = cur;
   }
   return KQ_OK;
+}
+
+DeviceScope::~DeviceScope() {
+  if (restore_ >= 0) cudaSetDevice(restore_);
 }
 
 }  // namespace kq
@@ -76,32 +81,36 @@ int kq_ctx_create(int device, kq_ctx** out) {
   e = cudaSetDevice(device);
   if (e != cudaSuccess) return cuda_fail(e, "cudaSetDevice");
   int major = 0, minor = 0;
-  cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, device);
-  cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, device);
+  e = cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, device);
+  if (e == cudaSuccess) e = cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, device);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaDeviceGetAttribute", "compute capability");
   if (major != 10 || minor != 0)
     return fail(KQ_E_UNSUPPORTED, "kq_ctx_create",
                 "this library is built for sm_100a (B200); GPU " + std::to_string(device) +
                     " is sm_" + std::to_string(major) + std::to_string(minor));
   kq_ctx* ctx = new kq_ctx();
   ctx->device = device;
-  cudaDeviceGetAttribute(&ctx->sm_count, cudaDevAttrMultiProcessorCount, device);
-  cudaDeviceGetAttribute(&ctx->max_smem, cudaDevAttrMaxSharedMemoryPerBlockOptin, device);
+  e = cudaDeviceGetAttribute(&ctx->sm_count, cudaDevAttrMultiProcessorCount, device);
+  if (e == cudaSuccess)
+    e = cudaDeviceGetAttribute(&ctx->max_smem, cudaDevAttrMaxSharedMemoryPerBlockOptin, device);
+  if (e != cudaSuccess) {
+    delete ctx;
+    return cuda_fail(e, "cudaDeviceGetAttribute", "SM count / shared memory per block");
+  }
   // Leave room for the kernels' static shared memory.
   ctx->max_smem -= 2048;
-  void* p = nullptr;
-  e = cudaGetSymbolAddress(&p, g_kq_error_word);
+  // The ctx's own error word (in its own 256 bytes, zeroed here and by kq_device_error only), so
+  // that no other ctx on the GPU can clear an error this one's launches recorded.
+  e = cudaMalloc(reinterpret_cast<void**>(&ctx->err), 256);
+  if (e == cudaSuccess) e = cudaMemset(ctx->err, 0, 256);
   if (e != cudaSuccess) {
+    if (ctx->err) cudaFree(ctx->err);
     delete ctx;
-    return cuda_fail(e, "cudaGetSymbolAddress", "device error word");
-  }
-  ctx->err = static_cast<unsigned*>(p);
-  e = cudaMemset(ctx->err, 0, sizeof(unsigned));
-  if (e != cudaSuccess) {
-    delete ctx;
-    return cuda_fail(e, "cudaMemset", "device error word");
+    return cuda_fail(e, "cudaMalloc", "device error word");
   }
   e = cudaMalloc(&ctx->scratch, kq::kCtxScratchBytes);
   if (e != cudaSuccess) {
+    cudaFree(ctx->err);
     delete ctx;
     return cuda_fail(e, "cudaMalloc", "context scratch");
   }
@@ -112,6 +121,7 @@ int kq_ctx_create(int device, kq_ctx** out) {
   if (rc == KQ_OK) rc = kq::aux_prepare(ctx);
   if (rc != KQ_OK) {
     cudaFree(ctx->scratch);
+    cudaFree(ctx->err);
     delete ctx;
     return rc;
   }
@@ -121,10 +131,13 @@ int kq_ctx_create(int device, kq_ctx** out) {
 
 int kq_ctx_destroy(kq_ctx* ctx) {
   if (!ctx) return KQ_OK;
-  if (ctx->scratch || ctx->stage) {
-    kq::enter(ctx);
-    if (ctx->scratch) cudaFree(ctx->scratch);  // waits for the device: no launch still reads it
+  {
+    kq::DeviceScope scope;
+    scope.enter(ctx);
+    // cudaFree waits for the device: no launch still reads what it frees
+    if (ctx->scratch) cudaFree(ctx->scratch);
     if (ctx->stage) cudaFree(ctx->stage);
+    if (ctx->err) cudaFree(ctx->err);
   }
   delete ctx;
   return KQ_OK;
@@ -150,7 +163,8 @@ int kq_ctx_info(const kq_ctx* ctx, int* device, int* sm_count, int* max_smem_per
 
 int kq_device_error(kq_ctx* ctx) {
   if (!ctx) return fail(KQ_E_INVALID, "kq_device_error", "null ctx");
-  int rc = kq::enter(ctx);
+  kq::DeviceScope scope;
+  int rc = scope.enter(ctx);
   if (rc) return rc;
   cudaError_t e = cudaDeviceSynchronize();
   if (e != cudaSuccess) return cuda_fail(e, "cudaDeviceSynchronize");
@@ -178,7 +192,8 @@ static int matvec_simple(kq_ctx* ctx, uint32_t type, uint64_t y, uint64_t w, uin
   d.y = y;
   d.w = w;
   d.x = x;
-  int rc = kq::enter(ctx);
+  kq::DeviceScope scope;
+  int rc = scope.enter(ctx);
   if (rc) return rc;
   return kq::matvec(ctx, d, static_cast<cudaStream_t>(stream));
 }
@@ -195,7 +210,8 @@ int kq_matvec_q6k(kq_ctx* ctx, uint64_t y, uint64_t w, uint64_t x, uint32_t rows
 
 int kq_matvec(kq_ctx* ctx, const kq_matvec_desc* desc, kq_stream stream) {
   if (!ctx || !desc) return fail(KQ_E_INVALID, "kq_matvec", "null ctx or descriptor");
-  int rc = kq::enter(ctx);
+  kq::DeviceScope scope;
+  int rc = scope.enter(ctx);
   if (rc) return rc;
   return kq::matvec(ctx, *desc, static_cast<cudaStream_t>(stream));
 }
@@ -204,7 +220,8 @@ int kq_matvec_host(kq_ctx* ctx, const kq_matvec_desc* desc, float* y_host, const
                    kq_stream stream) {
   const char* call = "kq_matvec_host";
   if (!ctx || !desc || !y_host || !x_host) return fail(KQ_E_INVALID, call, "null argument");
-  int rc = kq::enter(ctx);
+  kq::DeviceScope scope;
+  int rc = scope.enter(ctx);
   if (rc) return rc;
   kq_matvec_desc d = *desc;
   if (d.batch == 0 || d.rows == 0 || d.k == 0)
@@ -247,21 +264,24 @@ int kq_matvec_host(kq_ctx* ctx, const kq_matvec_desc* desc, float* y_host, const
 
 int kq_dequant_q4k(kq_ctx* ctx, uint64_t out, uint64_t w, uint64_t nblocks, kq_stream stream) {
   if (!ctx) return fail(KQ_E_INVALID, "kq_dequant_q4k", "null ctx");
-  int rc = kq::enter(ctx);
+  kq::DeviceScope scope;
+  int rc = scope.enter(ctx);
   if (rc) return rc;
   return kq::dequant(ctx, 4, out, w, nblocks, static_cast<cudaStream_t>(stream));
 }
 
 int kq_dequant_q6k(kq_ctx* ctx, uint64_t out, uint64_t w, uint64_t nblocks, kq_stream stream) {
   if (!ctx) return fail(KQ_E_INVALID, "kq_dequant_q6k", "null ctx");
-  int rc = kq::enter(ctx);
+  kq::DeviceScope scope;
+  int rc = scope.enter(ctx);
   if (rc) return rc;
   return kq::dequant(ctx, 6, out, w, nblocks, static_cast<cudaStream_t>(stream));
 }
 
 int kq_dequant_q5k(kq_ctx* ctx, uint64_t out, uint64_t w, uint64_t nblocks, kq_stream stream) {
   if (!ctx) return fail(KQ_E_INVALID, "kq_dequant_q5k", "null ctx");
-  int rc = kq::enter(ctx);
+  kq::DeviceScope scope;
+  int rc = scope.enter(ctx);
   if (rc) return rc;
   return kq::dequant(ctx, 5, out, w, nblocks, static_cast<cudaStream_t>(stream));
 }
@@ -269,7 +289,8 @@ int kq_dequant_q5k(kq_ctx* ctx, uint64_t out, uint64_t w, uint64_t nblocks, kq_s
 int kq_fill_q5k(kq_ctx* ctx, uint64_t w, uint64_t block0, uint64_t nblocks, uint64_t key,
                 kq_stream stream) {
   if (!ctx) return fail(KQ_E_INVALID, "kq_fill_q5k", "null ctx");
-  int rc = kq::enter(ctx);
+  kq::DeviceScope scope;
+  int rc = scope.enter(ctx);
   if (rc) return rc;
   return kq::fill(ctx, 5, w, block0, nblocks, key, static_cast<cudaStream_t>(stream));
 }
@@ -277,7 +298,8 @@ int kq_fill_q5k(kq_ctx* ctx, uint64_t w, uint64_t block0, uint64_t nblocks, uint
 #define KQ_DEQUANT_ENTRY(name, type)                                                        \
   int name(kq_ctx* ctx, uint64_t out, uint64_t w, uint64_t nblocks, kq_stream stream) {     \
     if (!ctx) return fail(KQ_E_INVALID, #name, "null ctx");                                \
-    int rc = kq::enter(ctx);                                                                \
+    kq::DeviceScope scope;                                                                  \
+    int rc = scope.enter(ctx);                                                              \
     if (rc) return rc;                                                                      \
     return kq::dequant(ctx, type, out, w, nblocks, static_cast<cudaStream_t>(stream));      \
   }
@@ -289,7 +311,8 @@ KQ_DEQUANT_ENTRY(kq_dequant_q8_0, 8)
 int kq_fill_q4k(kq_ctx* ctx, uint64_t w, uint64_t block0, uint64_t nblocks, uint64_t key,
                 kq_stream stream) {
   if (!ctx) return fail(KQ_E_INVALID, "kq_fill_q4k", "null ctx");
-  int rc = kq::enter(ctx);
+  kq::DeviceScope scope;
+  int rc = scope.enter(ctx);
   if (rc) return rc;
   return kq::fill(ctx, 4, w, block0, nblocks, key, static_cast<cudaStream_t>(stream));
 }
@@ -297,7 +320,8 @@ int kq_fill_q4k(kq_ctx* ctx, uint64_t w, uint64_t block0, uint64_t nblocks, uint
 int kq_fill_q6k(kq_ctx* ctx, uint64_t w, uint64_t block0, uint64_t nblocks, uint64_t key,
                 kq_stream stream) {
   if (!ctx) return fail(KQ_E_INVALID, "kq_fill_q6k", "null ctx");
-  int rc = kq::enter(ctx);
+  kq::DeviceScope scope;
+  int rc = scope.enter(ctx);
   if (rc) return rc;
   return kq::fill(ctx, 6, w, block0, nblocks, key, static_cast<cudaStream_t>(stream));
 }
@@ -307,7 +331,8 @@ uint64_t kq_stream_key(uint64_t seed, uint64_t tensor) { return kq::stream_key(s
 int kq_matvec_push(kq_ctx* ctx, const kq_matvec_desc* desc, const kq_push_desc* push,
                    kq_stream stream) {
   if (!ctx || !desc || !push) return fail(KQ_E_INVALID, "kq_matvec_push", "null ctx, descriptor or push");
-  int rc = kq::enter(ctx);
+  kq::DeviceScope scope;
+  int rc = scope.enter(ctx);
   if (rc) return rc;
   return kq::matvec(ctx, *desc, static_cast<cudaStream_t>(stream), push);
 }
@@ -315,14 +340,16 @@ int kq_matvec_push(kq_ctx* ctx, const kq_matvec_desc* desc, const kq_push_desc* 
 int kq_wait_counter(kq_ctx* ctx, uint64_t counter, uint64_t epoch, uint64_t wait_mul,
                     uint64_t wait_add, kq_stream stream) {
   if (!ctx) return fail(KQ_E_INVALID, "kq_wait_counter", "null ctx");
-  int rc = kq::enter(ctx);
+  kq::DeviceScope scope;
+  int rc = scope.enter(ctx);
   if (rc) return rc;
   return kq::wait_counter(ctx, counter, epoch, wait_mul, wait_add, static_cast<cudaStream_t>(stream));
 }
 
 int kq_peer_alloc(kq_ctx* ctx, uint64_t bytes, uint64_t* ptr, void* ipc_handle) {
   if (!ctx || !ptr || !ipc_handle || !bytes) return fail(KQ_E_INVALID, "kq_peer_alloc", "null argument or zero size");
-  int rc = kq::enter(ctx);
+  kq::DeviceScope scope;
+  int rc = scope.enter(ctx);
   if (rc) return rc;
   void* p = nullptr;
   cudaError_t e = cudaMalloc(&p, bytes);
@@ -345,7 +372,8 @@ int kq_peer_alloc(kq_ctx* ctx, uint64_t bytes, uint64_t* ptr, void* ipc_handle) 
 
 int kq_peer_open(kq_ctx* ctx, const void* ipc_handle, uint64_t* ptr) {
   if (!ctx || !ipc_handle || !ptr) return fail(KQ_E_INVALID, "kq_peer_open", "null argument");
-  int rc = kq::enter(ctx);
+  kq::DeviceScope scope;
+  int rc = scope.enter(ctx);
   if (rc) return rc;
   cudaIpcMemHandle_t h;
   std::memcpy(&h, ipc_handle, sizeof(h));
@@ -358,7 +386,8 @@ int kq_peer_open(kq_ctx* ctx, const void* ipc_handle, uint64_t* ptr) {
 
 int kq_peer_close(kq_ctx* ctx, uint64_t ptr) {
   if (!ctx || !ptr) return fail(KQ_E_INVALID, "kq_peer_close", "null argument");
-  int rc = kq::enter(ctx);
+  kq::DeviceScope scope;
+  int rc = scope.enter(ctx);
   if (rc) return rc;
   const cudaError_t e = cudaIpcCloseMemHandle(reinterpret_cast<void*>(ptr));
   if (e != cudaSuccess) return cuda_fail(e, "cudaIpcCloseMemHandle");
@@ -367,7 +396,8 @@ int kq_peer_close(kq_ctx* ctx, uint64_t ptr) {
 
 int kq_peer_free(kq_ctx* ctx, uint64_t ptr) {
   if (!ctx || !ptr) return fail(KQ_E_INVALID, "kq_peer_free", "null argument");
-  int rc = kq::enter(ctx);
+  kq::DeviceScope scope;
+  int rc = scope.enter(ctx);
   if (rc) return rc;
   const cudaError_t e = cudaFree(reinterpret_cast<void*>(ptr));
   if (e != cudaSuccess) return cuda_fail(e, "cudaFree", "peer memory");

@@ -12,7 +12,7 @@ struct kq_ctx {
   int device = 0;
   int sm_count = 0;
   int max_smem = 0;       // opt-in dynamic shared memory per block
-  unsigned* err = nullptr;  // the device error word (a file-scope __device__ variable)
+  unsigned* err = nullptr;  // the ctx's device error word (its own allocation)
   // Scratch the tensor-core path converts X into (allocated once, at creation).
   void* scratch = nullptr;
   uint64_t scratch_bytes = 0;
@@ -32,8 +32,20 @@ int fail(int code, const char* call, const std::string& detail);
 int cuda_fail(cudaError_t e, const char* call, const std::string& detail = std::string());
 // The current device's address of the library's device error word.
 int error_word_address(unsigned** out);
-// Makes the ctx's device current if it is not.
-int enter(const kq_ctx* ctx);
+// An entry point's hold on the ctx's device: enter() makes it current if it is not, and the
+// destructor makes the caller's device current again, so no entry point leaves the thread on
+// another GPU than the one it found.
+class DeviceScope {
+ public:
+  DeviceScope() = default;
+  DeviceScope(const DeviceScope&) = delete;
+  DeviceScope& operator=(const DeviceScope&) = delete;
+  ~DeviceScope();
+  int enter(const kq_ctx* ctx);
+
+ private:
+  int restore_ = -1;
+};
 
 int matvec_prepare(kq_ctx* ctx);
 int mma_prepare(kq_ctx* ctx);

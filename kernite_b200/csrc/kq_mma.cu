@@ -461,11 +461,12 @@ int noalloc_setup(int dev, NoAllocDevice** out) {
   NoAllocDevice& d = g_noalloc_devices[dev];
   if (!d.ready) {
     int major = 0, minor = 0;
-    cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev);
-    cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, dev);
+    cudaError_t e = cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev);
+    if (e == cudaSuccess) e = cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, dev);
+    if (e != cudaSuccess) return kq::cuda_fail(e, "cudaDeviceGetAttribute", "compute capability");
     if (major != 10 || minor != 0)
       return kq::fail(KQ_E_UNSUPPORTED, "kq_matvec_q4k_noalloc", "this library is built for sm_100a (B200)");
-    cudaError_t e = cudaDeviceGetAttribute(&d.sm_count, cudaDevAttrMultiProcessorCount, dev);
+    e = cudaDeviceGetAttribute(&d.sm_count, cudaDevAttrMultiProcessorCount, dev);
     if (e != cudaSuccess) return kq::cuda_fail(e, "cudaDeviceGetAttribute");
     for (uint32_t n : {16u, 32u, 64u}) {
       const void* fn = n == 16 ? kq::mma_fn<16>() : n == 32 ? kq::mma_fn<32>() : kq::mma_fn<64>();

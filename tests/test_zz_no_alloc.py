@@ -1,10 +1,10 @@
 """kq_matvec_q4k_noalloc: the tensor-core Q4_K matvec for callers that cannot allocate device
 memory (graph-capture regions, servers whose pools already hold the GPU, latency-critical paths).
 Its scratch is a static device array shared by all calls, so this file runs last (a failure here
-leaves every other test already run) and checks two calls in a row against the allocating entry
-point; it passes alone in a fresh process too."""
-import ctypes
-
+leaves every other test already run). Each case runs two calls in a row and checks both against
+the oracle (|y - y_ref| <= 1e-3 * sum|w x|) and against the allocating entry point, at every
+scratch width (batch padded to 16, 32 and 64) and at the two shapes that fill the 1 MiB scratch
+exactly (k = 8192 at batch 40, k = 32768 at batch 16). It passes alone in a fresh process too."""
 import numpy as np
 import pytest
 import torch
@@ -18,15 +18,19 @@ pytestmark = pytest.mark.gpu
 TOL = 1e-3
 
 
-def test_noalloc_matches_the_allocating_entry_point_twice(kernels):
+@pytest.mark.parametrize("rows,K,batches", [
+    (1500, 4096, (3, 20)),     # npad 16, then 32
+    (640, 8192, (40, 40)),     # npad 64: k * 64 * 2 = 1 MiB, the whole scratch
+    (300, 32768, (16, 9)),     # npad 16: k * 16 * 2 = 1 MiB
+])
+def test_noalloc_matches_the_oracle_and_the_allocating_entry_point_twice(kernels, rows, K, batches):
     L = kb.lib()
-    rows, K = 1500, 4096
     n = rows * K // 256
     W = torch.empty(n * 144, dtype=torch.uint8, device="cuda")
-    kernels.fill(4, W, 0, n, kb.stream_key(404, 4))
+    kernels.fill(4, W, 0, n, kb.stream_key(404 + K, 4))
     Wh = W.cpu().numpy()
-    for call, batch in enumerate((3, 20)):
-        x = np.random.default_rng(call).standard_normal((batch, K), dtype=np.float32)
+    for call, batch in enumerate(batches):
+        x = np.random.default_rng(call + K).standard_normal((batch, K), dtype=np.float32)
         xd = torch.from_numpy(x).cuda()
         y_new = torch.full((batch, rows), float("nan"), device="cuda")
         y_old = torch.full((batch, rows), float("nan"), device="cuda")
@@ -35,10 +39,11 @@ def test_noalloc_matches_the_allocating_entry_point_twice(kernels):
         assert rc == 0, kb.last_error()
         kernels.matvec(4, y_old, W, xd, rows, K, batch, flags=kb.FLAG_TENSOR_CORES)
         torch.cuda.synchronize()
-        a, b = y_new.cpu().numpy(), y_old.cpu().numpy()
-        _, bound = oracle.matvec_ref(4, Wh, x, K, 0, rows)
+        a, b = y_new.cpu().numpy().astype(np.float64), y_old.cpu().numpy().astype(np.float64)
+        y_ref, bound = oracle.matvec_ref(4, Wh, x, K, 0, rows)
         assert np.isfinite(a).all()
-        assert (np.abs(a - b) <= TOL * bound).all(), f"call {call}"
+        assert (np.abs(a - y_ref) <= TOL * bound).all(), f"call {call}: worst {(np.abs(a - y_ref) / bound).max():.3e}"
+        assert (np.abs(a - b) <= TOL * bound).all(), f"call {call} vs the allocating path"
     kernels.device_error()
 
 
