@@ -64,8 +64,10 @@ def parse_args(argv=None):
     ap.add_argument("--extra-flags", type=lambda v: int(v, 0), default=0,
                     help="more descriptor flag bits OR-ed into every timed launch (A/B tests)")
     ap.add_argument("--impl", default="kq", choices=["kq", "reference"])
-    ap.add_argument("--exchange", default="nccl", choices=["nccl", "push"],
-                    help="sharded stacks: NCCL all-gathers, or the matvec's own push to peer memory")
+    ap.add_argument("--exchange", default="nccl", choices=["nccl", "push", "chain"],
+                    help="stacks: NCCL all-gathers after one launch per projection, the CUDA-core "
+                         "matvec's own push to peer memory, or chains of the warp-MMA kernel (up to "
+                         "three projections a launch, outputs pushed to peer memory at N > 1)")
     ap.add_argument("--e2e-steps", type=int, default=2000, help="steps of the end-to-end leg")
     ap.add_argument("--cpu-seconds", type=float, default=12.0, help="CPU-baseline time budget")
     ap.add_argument("--no-cpu-baseline", action="store_true")
@@ -524,7 +526,8 @@ def run_stack(args):
     kernels = kb.Kernels.load(local)
     stream = torch.cuda.Stream()
     push = args.exchange == "push" and world > 1
-    stack = st.make_cuda_stack(cfg, kernels, rank, world, stream=stream, push=push)
+    chain = args.exchange == "chain"
+    stack = st.make_cuda_stack(cfg, kernels, rank, world, stream=stream, push=push, chain=chain)
     x = torch.from_numpy(np.random.default_rng(0).standard_normal(cfg.hidden).astype(np.float32))
     stack.buf["x"].copy_(x.cuda())
     torch.cuda.synchronize()
@@ -625,8 +628,9 @@ def run_stack(args):
             "vs_baseline": None, "dtype": "f32", "data": "synthetic",
             "config": {"workload": f"{args.workload}: {cfg.name}", "layers": cfg.layers,
                        "hidden": cfg.hidden, "ffn": cfg.ffn, "kv": cfg.kv, "vocab": cfg.vocab,
-                       "parallelism": (f"rows sharded x{world}, " + ("push to peer memory" if push else
-                                       "NCCL all-gather")) if world > 1 else "single",
+                       "parallelism": (f"rows sharded x{world}, " + (
+                           "chains, push to peer memory" if chain else "push to peer memory" if push else
+                           "NCCL all-gather")) if world > 1 else ("single, chains" if chain else "single"),
                        "graph": graph is not None, "batch": 1,
                        "l2": f"{wbytes / world / 1e9:.1f} GB of weights per GPU per token > L2"},
             "weight_gbs": round(wbytes * tps / 1e9, 2),
@@ -640,7 +644,7 @@ def run_stack(args):
     if graph is not None:
         graph.reset()
     graph = None
-    if push:
+    if push or (chain and world > 1):
         stack.be.close()
     if dist:
         dist.barrier()

@@ -255,6 +255,49 @@ int kq_matvec_push(kq_ctx* ctx, const kq_matvec_desc* desc, const kq_push_desc* 
 int kq_wait_counter(kq_ctx* ctx, uint64_t counter, uint64_t epoch, uint64_t wait_mul,
                     uint64_t wait_add, kq_stream stream);
 
+/* ---- Chains: several matvecs in one launch, with the exchange of a row-sharded stack ---------
+ *
+ * A decode step is a chain of matvecs, each reading the previous one's output. kq_matvec_chain
+ * runs up to 8 of them (batch 1, one type, one k: e.g. a layer's q|k|v, o and gate|up
+ * projections) in one launch of the warp-MMA integer kernel, one CTA per SM: each CTA streams its
+ * share of the rows of every matrix in turn, the next matrix's weights already in flight while
+ * it finishes one. What a kernel boundary did between two matvecs, counters do: once a CTA's
+ * outputs of a job are stored, it adds their count to the job's counter (release); a job with a
+ * wait_counter reads x only once that counter reaches (*epoch) * wait_target (bounded wait,
+ * acquire), i.e. once every CTA (of every rank) has stored its part of x in this step. Counters
+ * only grow; *epoch, advanced once per step (kq_epoch_advance), keeps each step's targets apart,
+ * so counters and epoch start at zero and are never reset.
+ *
+ * Row-sharded over N GPUs (one process each): each rank runs the same chain on its rows; a job
+ * with npush > 0 also stores its outputs [0, push_rows) into every rank's full vector (push_y[p],
+ * this rank's slice in rank p's memory, mapped with kq_peer_open; this rank's own included) and
+ * adds the count to counter[p] on each rank (system scope), so the next job's wait on this
+ * rank's counter (target N * push_rows per step) is the all-gather. A wait that gives up sets the
+ * ctx's device error word and the chain runs on without waiting, so a missing rank costs one
+ * wait budget (about 2 s), not a hang. No reference counterpart: kernite launches one kernel at a
+ * time and has no collective; its only inter-GPU operation is Buffer::copy_from over
+ * cuMemcpyPeer (crates/cuda/src/lib.rs:405-439). */
+typedef struct kq_chain_job {
+    kq_matvec_desc mv;     /* batch 1; y receives every output of the job on this GPU */
+    uint64_t wait_counter; /* 0, or a u64 counter on this GPU that x waits for */
+    uint64_t wait_target;  /* the count wait_counter gains per step */
+    uint32_t npush;        /* 0, or the ranks (<= 8) whose full vectors receive pushed outputs */
+    uint32_t push_rows;    /* outputs [0, push_rows) are pushed */
+    uint64_t push_y[8];    /* per rank: where this rank's pushed outputs go in that rank's memory */
+    uint64_t counter[8];   /* npush == 0: counter[0] (0 = none) on this GPU gains the output
+                            * count; npush > 0: counter[p] on rank p gains the pushed count */
+} kq_chain_job;
+
+/* Runs jobs[0..njobs) (1..8) in one launch on `stream`; epoch is the address of this GPU's u64
+ * step counter. Every job has the first one's type (Q4_K, Q5_K or Q6_K) and k and must fit the
+ * integer kernel's shared memory (KQ_E_UNSUPPORTED otherwise). The first job also waits for the
+ * previous kernel on the stream, as every matvec does. */
+int kq_matvec_chain(kq_ctx* ctx, const kq_chain_job* jobs, uint32_t njobs, uint64_t epoch,
+                    kq_stream stream);
+
+/* *epoch += 1 on `stream` (one thread): the start of a step for the chains that follow. */
+int kq_epoch_advance(kq_ctx* ctx, uint64_t epoch, kq_stream stream);
+
 /* Device memory other GPUs can map: cudaMalloc'd, zeroed, with its CUDA IPC handle (64 bytes)
  * written to ipc_handle. Replaces the peer side of Buffer::copy_from (crates/cuda/src/lib.rs:
  * 405-439), which copies through cuMemcpyPeer instead of mapping. */

@@ -62,7 +62,7 @@ EXPORTS = (
     "kq_matvec_q4k", "kq_matvec_q6k", "kq_matvec", "kq_matvec_host", "kq_dequant_q4k", "kq_dequant_q6k",
     "kq_fill_q4k", "kq_fill_q6k", "kq_dequant_q5k", "kq_fill_q5k", "kq_dequant_q2k", "kq_dequant_q3k",
     "kq_dequant_q8_0", "kq_stream_key", "kq_matvec_q4k_noalloc",
-    "kq_matvec_push", "kq_wait_counter", "kq_peer_alloc", "kq_peer_open", "kq_peer_close", "kq_peer_free",
+    "kq_matvec_push", "kq_wait_counter", "kq_matvec_chain", "kq_epoch_advance", "kq_peer_alloc", "kq_peer_open", "kq_peer_close", "kq_peer_free",
     "kq_gguf_open", "kq_gguf_close", "kq_gguf_tensor_count", "kq_gguf_tensor_at", "kq_gguf_find",
     "kq_gguf_meta_int", "kq_gguf_meta_str",
 )
@@ -106,6 +106,17 @@ class KqPushDesc(ctypes.Structure):
     ]
 
 
+class KqChainJob(ctypes.Structure):
+    """``kq_chain_job`` (include/kq.h): one matvec of a chain launch."""
+    _fields_ = [
+        ("mv", KqMatvecDesc), ("wait_counter", ctypes.c_uint64), ("wait_target", ctypes.c_uint64),
+        ("npush", ctypes.c_uint32), ("push_rows", ctypes.c_uint32),
+        ("push_y", ctypes.c_uint64 * 8), ("counter", ctypes.c_uint64 * 8),
+    ]
+
+
+CHAIN_MAX_JOBS = 8
+
 IPC_HANDLE_BYTES = 64
 
 _lib: ctypes.CDLL | None = None
@@ -141,6 +152,8 @@ def lib() -> ctypes.CDLL:
     L.kq_matvec_q4k_noalloc.argtypes = [u64, u64, u64, u32, u32, u32, vp]
     L.kq_matvec_push.argtypes = [vp, ctypes.POINTER(KqMatvecDesc), ctypes.POINTER(KqPushDesc), vp]
     L.kq_wait_counter.argtypes = [vp, u64, u64, u64, u64, vp]
+    L.kq_matvec_chain.argtypes = [vp, ctypes.POINTER(KqChainJob), u32, u64, vp]
+    L.kq_epoch_advance.argtypes = [vp, u64, vp]
     L.kq_peer_alloc.argtypes = [vp, u64, ctypes.POINTER(u64), ctypes.c_char_p]
     L.kq_peer_open.argtypes = [vp, ctypes.c_char_p, ctypes.POINTER(u64)]
     L.kq_peer_close.argtypes = [vp, u64]
@@ -340,6 +353,22 @@ class Kernels:
         """Stream-ordered bounded wait until *counter >= (*epoch - 1) * wait_mul + wait_add."""
         _check(lib().kq_wait_counter(self._ctx, counter, epoch, wait_mul, wait_add, _stream(stream)),
                "kq_wait_counter")
+
+    def matvec_chain(self, jobs, epoch: int, stream=None) -> None:
+        """``kq_matvec_chain``: up to 8 batch-1 matvecs of one type and k in one launch, each
+        waiting for its counter before it reads x (see include/kq.h). ``jobs`` is a sequence of
+        :class:`KqChainJob` or a ctypes array of them; ``epoch`` the address of this GPU's u64
+        step counter."""
+        if not isinstance(jobs, ctypes.Array):
+            arr = (KqChainJob * len(jobs))(*jobs)
+        else:
+            arr = jobs
+        _check(lib().kq_matvec_chain(self._ctx, arr, len(arr), epoch, _stream(stream)),
+               "kq_matvec_chain")
+
+    def epoch_advance(self, epoch: int, stream=None) -> None:
+        """``*epoch += 1`` on the stream: the start of a step for the chains after it."""
+        _check(lib().kq_epoch_advance(self._ctx, epoch, _stream(stream)), "kq_epoch_advance")
 
     def peer_alloc(self, nbytes: int) -> tuple[int, bytes]:
         """Zeroed device memory other GPUs can map; returns (address, 64-byte IPC handle)."""

@@ -212,7 +212,18 @@ __global__ void wait_counter_kernel(unsigned* err, const unsigned long long* cnt
   wait_count(err, cnt, epoch, mul, add);
 }
 
+__global__ void epoch_advance_kernel(unsigned long long* epoch) { *epoch += 1ull; }
+
 int aux_prepare(kq_ctx*) { return KQ_OK; }
+
+int epoch_advance(kq_ctx*, uint64_t epoch, cudaStream_t s) {
+  if (!epoch || epoch % 8)
+    return fail(KQ_E_INVALID, "kq_epoch_advance", "epoch must be a non-null 8-byte aligned address");
+  epoch_advance_kernel<<<1, 1, 0, s>>>(reinterpret_cast<unsigned long long*>(epoch));
+  const cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "cudaLaunchKernel", "kq_epoch_advance");
+  return KQ_OK;
+}
 
 int wait_counter(kq_ctx* ctx, uint64_t counter, uint64_t epoch, uint64_t mul, uint64_t add,
                  cudaStream_t s) {

@@ -337,6 +337,23 @@ int kq_matvec_push(kq_ctx* ctx, const kq_matvec_desc* desc, const kq_push_desc* 
   return kq::matvec(ctx, *desc, static_cast<cudaStream_t>(stream), push);
 }
 
+int kq_matvec_chain(kq_ctx* ctx, const kq_chain_job* jobs, uint32_t njobs, uint64_t epoch,
+                    kq_stream stream) {
+  if (!ctx || !jobs) return fail(KQ_E_INVALID, "kq_matvec_chain", "null ctx or jobs");
+  kq::DeviceScope scope;
+  int rc = scope.enter(ctx);
+  if (rc) return rc;
+  return kq::warpmma_chain(ctx, jobs, njobs, epoch, static_cast<cudaStream_t>(stream));
+}
+
+int kq_epoch_advance(kq_ctx* ctx, uint64_t epoch, kq_stream stream) {
+  if (!ctx) return fail(KQ_E_INVALID, "kq_epoch_advance", "null ctx");
+  kq::DeviceScope scope;
+  int rc = scope.enter(ctx);
+  if (rc) return rc;
+  return kq::epoch_advance(ctx, epoch, static_cast<cudaStream_t>(stream));
+}
+
 int kq_wait_counter(kq_ctx* ctx, uint64_t counter, uint64_t epoch, uint64_t wait_mul,
                     uint64_t wait_add, kq_stream stream) {
   if (!ctx) return fail(KQ_E_INVALID, "kq_wait_counter", "null ctx");

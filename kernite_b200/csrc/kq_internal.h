@@ -55,11 +55,16 @@ int mma_matvec(kq_ctx* ctx, const kq_matvec_desc& d, uint64_t ldx, uint64_t ldy,
 uint64_t mma_scratch_bytes(uint32_t k, uint32_t batch);
 int matvec(kq_ctx* ctx, const kq_matvec_desc& d, cudaStream_t stream,
            const kq_push_desc* push = nullptr);
+// The argument checks every matvec entry point makes before a launch (KQ_E_INVALID on failure).
+int check_desc(const kq_matvec_desc& d, const char* call);
 
 int warpmma_prepare(kq_ctx* ctx);
 bool warpmma_supports(const kq_matvec_desc& d);
 int warpmma_matvec(kq_ctx* ctx, const kq_matvec_desc& d, uint64_t ldx, uint64_t ldy,
                    cudaStream_t stream);
+int warpmma_chain(kq_ctx* ctx, const kq_chain_job* jobs, uint32_t njobs, uint64_t epoch,
+                  cudaStream_t stream);
+int epoch_advance(kq_ctx* ctx, uint64_t epoch, cudaStream_t stream);
 
 int aux_prepare(kq_ctx* ctx);
 int wait_counter(kq_ctx* ctx, uint64_t counter, uint64_t epoch, uint64_t mul, uint64_t add,

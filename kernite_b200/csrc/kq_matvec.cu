@@ -608,8 +608,7 @@ int matvec_prepare(kq_ctx* ctx) {
   return KQ_OK;
 }
 
-int matvec(kq_ctx* ctx, const kq_matvec_desc& d, cudaStream_t stream, const kq_push_desc* push) {
-  const char* call = push ? "kq_matvec_push" : "kq_matvec";
+int check_desc(const kq_matvec_desc& d, const char* call) {
   int qt;
   if (d.type == KQ_TYPE_Q4_K)
     qt = 4;
@@ -646,6 +645,17 @@ int matvec(kq_ctx* ctx, const kq_matvec_desc& d, cudaStream_t stream, const kq_p
   const uint64_t ldy = d.ldy ? d.ldy : out_rows;
   if (ldx < d.k || ldx % 4) return fail(KQ_E_INVALID, call, "ldx must be >= k and a multiple of 4");
   if (ldy < out_rows) return fail(KQ_E_INVALID, call, "ldy must be >= the output rows");
+  return KQ_OK;
+}
+
+int matvec(kq_ctx* ctx, const kq_matvec_desc& d, cudaStream_t stream, const kq_push_desc* push) {
+  const char* call = push ? "kq_matvec_push" : "kq_matvec";
+  const int rc = check_desc(d, call);
+  if (rc) return rc;
+  const int qt = d.type == KQ_TYPE_Q4_K ? 4 : d.type == KQ_TYPE_Q5_K ? 5 : 6;
+  const bool pair = d.epilogue != KQ_EPILOGUE_NONE;
+  const uint64_t ldx = d.ldx ? d.ldx : d.k;
+  const uint64_t ldy = d.ldy ? d.ldy : (pair ? d.rows / 2 : d.rows);
 
   // Path: the tensor cores above batch 8 (and when asked), the CUDA cores otherwise.
   if (push) {

@@ -83,6 +83,11 @@ constexpr uint32_t kFlagAltBatch1 = 1u << 30;
 // or kMaxWarps taking turns) for A/B timing.
 constexpr uint32_t kFlagWarpPerBlock = 1u << 29;
 
+// A chain launch: at most this many jobs (their parameters travel in the launch), and pushes to
+// at most this many GPUs.
+constexpr uint32_t kChainMaxJobs = 8;
+constexpr uint32_t kChainMaxRanks = 8;
+
 constexpr uint32_t kMagic = 0x64006400u;  // f16x2 (1024, 1024): OR a 10-bit field in = 1024 + v
 
 struct WarpMmaArgs {
@@ -105,6 +110,36 @@ struct WarpMmaArgs {
   uint32_t fb;           // bands of partial rows kept before a flush
   uint32_t row_unit, prologue, epilogue, flags;
   float eps, pair_scale;
+};
+
+// A matvec that is one job of a chain (one launch running several matvecs of one type and k in
+// turn, each reading the previous one's output): the wait before its x is read, where its outputs
+// go on the other GPUs of a row-sharded stack, and the counters that tell their readers the
+// outputs are complete.
+struct ChainSync {
+  // null, or a counter on this GPU that must reach *epoch * wait_target before x is read
+  const unsigned long long* wait_cnt;
+  uint64_t wait_target;
+  // outputs [0, push_rows) also go to push_y[p][o] for p < npush (0: they stay on this GPU)
+  uint32_t npush, push_rows;
+  float* push_y[kChainMaxRanks];
+  // after its outputs are stored, each CTA adds its output count (pushed outputs when npush > 0)
+  // to counter[p] for p < max(npush, 1); null counter[0]: no count
+  unsigned long long* counter[kChainMaxRanks];
+};
+
+struct ChainParams {
+  const unsigned long long* epoch;  // this GPU's token counter
+  uint32_t njobs;
+  WarpMmaArgs job[kChainMaxJobs];
+  ChainSync sync[kChainMaxJobs];
+};
+
+// The parts of shared memory that are not in the dynamic layout.
+struct WarpMmaShared {
+  int failed;
+  double sq[kMaxWarps][8];  // [consumer warp][vector] sums of squares of x
+  float ns[8];              // per vector: the RMS-norm factor (1 without norm)
 };
 
 // ---------------------------------------------------------------- register-level helpers
@@ -509,23 +544,152 @@ __device__ __forceinline__ void q4i8_block(uint32_t ag, uint32_t ah, uint32_t c,
   yacc[1][0] += dh * fmaf(sh0, v2, sh1 * v3) - dmh * fmaf(mh0, X.x, mh1 * X.y);
 }
 
-// ---------------------------------------------------------------- the kernel
+// ---------------------------------------------------------------- the kernels' parts
 
-// QT: 4 or 6. NT: n8 tiles per MMA step (2 when batch 5..8 takes hi and lo in separate tiles).
-// HILO: x enters as hi + lo (else hi only). I8 (batch 1): integer MMAs, A = the raw quants as
-// bytes, x as three signed byte limbs (24-bit fixed point per 256-element block), the eight MMA
-// columns separating sub-blocks.
+// The rows [r_begin, r_end) of a matvec that this CTA streams and multiplies: a contiguous share
+// of whole output units (pairs of rows for the product epilogues).
+__device__ __forceinline__ void cta_rows(const WarpMmaArgs& a, uint32_t& r_begin, uint32_t& r_end) {
+  const uint64_t units = a.rows / a.row_unit;
+  r_begin = static_cast<uint32_t>(units * blockIdx.x / gridDim.x) * a.row_unit;
+  r_end = static_cast<uint32_t>(units * (blockIdx.x + 1) / gridDim.x) * a.row_unit;
+}
+
+// The 128-byte aligned start of the dynamic shared memory.
+__device__ __forceinline__ uint8_t* smem_base(uint8_t* smem) {
+  return smem + ((128u - (smem_u32(smem) & 127u)) & 127u);
+}
+
+// Thread 0 sets up the ring's mbarriers (a full and an empty one per slot); the CTA then meets.
+__device__ __forceinline__ void init_ring(const WarpMmaArgs& a, uint8_t* base, WarpMmaShared& sh) {
+  uint64_t* bars = reinterpret_cast<uint64_t*>(base + a.bars_off);
+  if (threadIdx.x == 0) {
+    sh.failed = 0;
+    for (uint32_t s = 0; s < a.ring; ++s) {
+      mbar_init(smem_u32(&bars[s]), 1);
+      mbar_init(smem_u32(&bars[a.ring + s]), a.nw);
+    }
+    fence_mbar_init();
+  }
+  __syncthreads();
+}
+
+// The producer warp's part of one matvec: the tiles of this CTA's rows, each into the next ring
+// slot once the consumers have freed it. Lane r of the warp copies row r of a tile (16 rows, one
+// bulk copy each, at the padded pitch), or lane 0 the tile's rows in one copy; lane 0 posts the
+// tile's byte count on its slot's mbarrier. s, phase: the ring position, carried from one matvec
+// of a launch to the next; issued: the tiles this warp issued before in the launch (the first
+// `ring` of them need no free slot). Returns false once a wait gave up.
+template <int QT>
+__device__ __forceinline__ bool produce_job(const WarpMmaArgs& a, uint8_t* base, WarpMmaShared& sh,
+                                            uint32_t& s, uint32_t& phase, uint32_t& issued) {
+  constexpr uint32_t kBlk = QT == 4 ? kQ4KBytes : QT == 5 ? kQ5KBytes : kQ6KBytes;
+  int& s_failed = sh.failed;
+  const uint32_t ring_s = smem_u32(base);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(base + a.bars_off);
+  auto full_bar = [&](uint32_t s) { return smem_u32(&bars[s]); };
+  auto empty_bar = [&](uint32_t s) { return smem_u32(&bars[a.ring + s]); };
+  const uint32_t lane = threadIdx.x & 31;
+  const uint64_t RB = a.row_bytes;
+  uint32_t r_begin, r_end;
+  cta_rows(a, r_begin, r_end);
+  const uint32_t nbands = (r_end - r_begin + kTileRows - 1) / kTileRows;
+  const uint32_t ntiles = nbands * a.nkt;
+  const uint64_t pol = policy_evict_first();
+  const uint64_t end_floor = a.total_bytes & ~uint64_t(15);
+  for (uint32_t t = 0; t < ntiles; ++t) {
+    if (issued >= a.ring) {
+      int ok = 1;
+      if (lane == 0) {
+        if (*reinterpret_cast<volatile int*>(&s_failed)) {
+          ok = 0;
+        } else if (!mbar_wait_sleep(empty_bar(s), phase ^ 1)) {
+          s_failed = 1;
+          report_error(a.err, kErrWaitEmpty);
+          ok = 0;
+        }
+      }
+      if (!__shfl_sync(0xffffffffu, ok, 0)) return false;
+    }
+    const uint32_t band = t / a.nkt, kt = t % a.nkt;
+    const uint32_t r0 = r_begin + band * kTileRows;
+    const uint32_t r1 = min(r0 + kTileRows, r_end);
+    const uint32_t slot = ring_s + s * a.slot_bytes;
+    // K-tile kt: super-blocks [kc0, kc1), kq + (kt < kr) of them (the consumers' split)
+    const uint32_t kq = a.nb / a.nkt, kr = a.nb % a.nkt;
+    const uint32_t kc0 = kt * kq + min(kt, kr), kc1 = kc0 + kq + (kt < kr ? 1u : 0u);
+    const uint32_t r = r0 + lane;
+    uint64_t a0 = 0, a1 = 0;
+    if (a.seg_bytes == 0) {
+      // whole rows: one copy of the tile's 16-byte-aligned superset, by lane 0
+      if (lane == 0) {
+        a0 = (uint64_t(r0) * RB) & ~uint64_t(15);
+        a1 = (uint64_t(r1) * RB + 15) & ~uint64_t(15);
+        if (a1 > end_floor) {
+          for (uint64_t i = end_floor; i < a.total_bytes; i += 2)
+            sts_u16(slot + static_cast<uint32_t>(i - a0),
+                    __ldg(reinterpret_cast<const unsigned short*>(a.W + i)));
+          a1 = end_floor;
+        }
+        if (a1 < a0) a1 = a0;
+      }
+    } else if (lane < kTileRows && r < r1) {
+      const uint64_t b0 = uint64_t(r) * RB + uint64_t(kc0) * kBlk;
+      const uint64_t b1 = uint64_t(r) * RB + uint64_t(kc1) * kBlk;
+      a0 = b0 & ~uint64_t(15);
+      a1 = (b1 + 15) & ~uint64_t(15);
+      if (a1 > end_floor) {
+        // the end of W is off a 16-byte boundary: its last bytes (an even count, < 16) are
+        // read with plain loads
+        const uint32_t dst = slot + lane * a.seg_bytes;
+        for (uint64_t i = end_floor; i < a.total_bytes; i += 2)
+          sts_u16(dst + static_cast<uint32_t>(i - a0),
+                  __ldg(reinterpret_cast<const unsigned short*>(a.W + i)));
+        a1 = end_floor;
+      }
+      if (a1 < a0) a1 = a0;
+    }
+    uint32_t bytes = static_cast<uint32_t>(a1 - a0), total = bytes;
+#pragma unroll
+    for (int o = 16; o; o >>= 1) total += __shfl_xor_sync(0xffffffffu, total, o);
+    __syncwarp();
+    if (lane == 0) mbar_arrive_expect_tx(full_bar(s), total);
+    __syncwarp();
+    if (a.split_tile) {
+      // rows r0..r0+7 at the slot, rows r0+8.. kSplitGap bytes past where they would follow
+      // (rows are whole and start on 16-byte boundaries here, so a1 - a0 = (r1 - r0) * RB)
+      if (lane == 0 && bytes) {
+        const uint32_t first = static_cast<uint32_t>(std::min<uint64_t>(bytes, 8 * RB));
+        bulk_g2s(slot, a.W + a0, first, full_bar(s), pol);
+        if (bytes > first)
+          bulk_g2s(slot + first + kSplitGap, a.W + a0 + first, bytes - first, full_bar(s), pol);
+      }
+    } else if (bytes) {
+      bulk_g2s(slot + lane * a.seg_bytes, a.W + a0, bytes, full_bar(s), pol);
+    }
+    // (whole-row tiles: only lane 0 has bytes, and its destination is the slot itself)
+    ++issued;
+    if (++s == a.ring) {
+      s = 0;
+      phase ^= 1;
+    }
+  }
+  return true;
+}
+
+// The consumer warps' part of one matvec: x into the B-fragment table (with the RMS-norm sums),
+// then every tile of this CTA's rows from the ring, MMAs, and the outputs. s, phase: the ring
+// position, carried from one matvec of a launch to the next. sync: null for a lone matvec; for a
+// job of a chain, where its outputs are also pushed.
 template <int QT, int NT, bool HILO, bool I8>
-__global__ void __launch_bounds__((kMaxWarps + 1) * 32, 1) warpmma_kernel(const WarpMmaArgs a) {
+__device__ __forceinline__ void consume_job(const WarpMmaArgs& a, const ChainSync* sync,
+                                            uint8_t* base, WarpMmaShared& sh, uint32_t& s,
+                                            uint32_t& phase) {
   constexpr uint32_t kBlk = QT == 4 ? kQ4KBytes : QT == 5 ? kQ5KBytes : kQ6KBytes;
   constexpr int kTarget = QT == 4 ? 10 : 14;  // x is scaled so that max |x| < 2^kTarget
+  int& s_failed = sh.failed;
+  double (&s_sq)[kMaxWarps][8] = sh.sq;
+  float (&s_ns)[8] = sh.ns;
 
-  extern __shared__ __align__(128) uint8_t smem[];
-  __shared__ int s_failed;
-  __shared__ double s_sq[kMaxWarps][8];  // [consumer warp][vector] sums of squares of x
-  __shared__ float s_ns[8];                // per vector: the RMS-norm factor (1 without norm)
-
-  uint8_t* base = smem + ((128u - (smem_u32(smem) & 127u)) & 127u);
   const uint32_t ring_s = smem_u32(base);
   const uint32_t table_s = ring_s + a.table_off;
   const uint32_t mtable_s = ring_s + a.mtable_off;
@@ -539,117 +703,13 @@ __global__ void __launch_bounds__((kMaxWarps + 1) * 32, 1) warpmma_kernel(const 
   const uint32_t nthr = nw * 32;
   const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const uint64_t RB = a.row_bytes;
-
-  const uint64_t units = a.rows / a.row_unit;
-  const uint32_t r_begin = static_cast<uint32_t>(units * blockIdx.x / gridDim.x) * a.row_unit;
-  const uint32_t r_end = static_cast<uint32_t>(units * (blockIdx.x + 1) / gridDim.x) * a.row_unit;
+  uint32_t r_begin, r_end;
+  cta_rows(a, r_begin, r_end);
   const uint32_t nbands = (r_end - r_begin + kTileRows - 1) / kTileRows;
-  const uint32_t ntiles = nbands * a.nkt;
 
-  if (threadIdx.x == 0) {
-    s_failed = 0;
-    for (uint32_t s = 0; s < a.ring; ++s) {
-      mbar_init(full_bar(s), 1);
-      mbar_init(empty_bar(s), nw);
-    }
-    fence_mbar_init();
-  }
-  __syncthreads();
-  pdl_launch_dependents();
-
-  // ------------------------------------------------------------------ producer warp
-  // Lane r of the producer warp copies row r of each tile (16 rows, one bulk copy each, at the
-  // padded pitch); lane 0 posts the tile's byte count on its slot's mbarrier.
-  if (warp == nw) {
-    if (!(a.flags & KQ_FLAG_WEIGHTS_STATIC)) pdl_wait();
-    const uint64_t pol = policy_evict_first();
-    const uint64_t end_floor = a.total_bytes & ~uint64_t(15);
-    uint32_t s = 0, phase = 0;
-    for (uint32_t t = 0; t < ntiles; ++t) {
-      if (t >= a.ring) {
-        int ok = 1;
-        if (lane == 0) {
-          if (s_failed) {
-            ok = 0;
-          } else if (!mbar_wait_sleep(empty_bar(s), phase ^ 1)) {
-            s_failed = 1;
-            report_error(a.err, kErrWaitEmpty);
-            ok = 0;
-          }
-        }
-        if (!__shfl_sync(0xffffffffu, ok, 0)) break;
-      }
-      const uint32_t band = t / a.nkt, kt = t % a.nkt;
-      const uint32_t r0 = r_begin + band * kTileRows;
-      const uint32_t r1 = min(r0 + kTileRows, r_end);
-      const uint32_t slot = ring_s + s * a.slot_bytes;
-      // K-tile kt: super-blocks [kc0, kc1), kq + (kt < kr) of them (the consumers' split)
-      const uint32_t kq = a.nb / a.nkt, kr = a.nb % a.nkt;
-      const uint32_t kc0 = kt * kq + min(kt, kr), kc1 = kc0 + kq + (kt < kr ? 1u : 0u);
-      const uint32_t r = r0 + lane;
-      uint64_t a0 = 0, a1 = 0;
-      if (a.seg_bytes == 0) {
-        // whole rows: one copy of the tile's 16-byte-aligned superset, by lane 0
-        if (lane == 0) {
-          a0 = (uint64_t(r0) * RB) & ~uint64_t(15);
-          a1 = (uint64_t(r1) * RB + 15) & ~uint64_t(15);
-          if (a1 > end_floor) {
-            for (uint64_t i = end_floor; i < a.total_bytes; i += 2)
-              sts_u16(slot + static_cast<uint32_t>(i - a0),
-                      __ldg(reinterpret_cast<const unsigned short*>(a.W + i)));
-            a1 = end_floor;
-          }
-          if (a1 < a0) a1 = a0;
-        }
-      } else if (lane < kTileRows && r < r1) {
-        const uint64_t b0 = uint64_t(r) * RB + uint64_t(kc0) * kBlk;
-        const uint64_t b1 = uint64_t(r) * RB + uint64_t(kc1) * kBlk;
-        a0 = b0 & ~uint64_t(15);
-        a1 = (b1 + 15) & ~uint64_t(15);
-        if (a1 > end_floor) {
-          // the end of W is off a 16-byte boundary: its last bytes (an even count, < 16) are
-          // read with plain loads
-          const uint32_t dst = slot + lane * a.seg_bytes;
-          for (uint64_t i = end_floor; i < a.total_bytes; i += 2)
-            sts_u16(dst + static_cast<uint32_t>(i - a0),
-                    __ldg(reinterpret_cast<const unsigned short*>(a.W + i)));
-          a1 = end_floor;
-        }
-        if (a1 < a0) a1 = a0;
-      }
-      uint32_t bytes = static_cast<uint32_t>(a1 - a0), total = bytes;
-#pragma unroll
-      for (int o = 16; o; o >>= 1) total += __shfl_xor_sync(0xffffffffu, total, o);
-      __syncwarp();
-      if (lane == 0) mbar_arrive_expect_tx(full_bar(s), total);
-      __syncwarp();
-      if (a.split_tile) {
-        // rows r0..r0+7 at the slot, rows r0+8.. kSplitGap bytes past where they would follow
-        // (rows are whole and start on 16-byte boundaries here, so a1 - a0 = (r1 - r0) * RB)
-        if (lane == 0 && bytes) {
-          const uint32_t first = static_cast<uint32_t>(std::min<uint64_t>(bytes, 8 * RB));
-          bulk_g2s(slot, a.W + a0, first, full_bar(s), pol);
-          if (bytes > first)
-            bulk_g2s(slot + first + kSplitGap, a.W + a0 + first, bytes - first, full_bar(s), pol);
-        }
-      } else if (bytes) {
-        bulk_g2s(slot + lane * a.seg_bytes, a.W + a0, bytes, full_bar(s), pol);
-      }
-      // (whole-row tiles: only lane 0 has bytes, and its destination is the slot itself)
-      if (++s == a.ring) {
-        s = 0;
-        phase ^= 1;
-      }
-    }
-    return;
-  }
-
-  // ------------------------------------------------------------------ consumers
   const uint32_t tid = threadIdx.x;  // 0 .. nthr-1
   const uint32_t g = lane >> 2, c = lane & 3;
   const uint32_t B = a.batch;
-
-  pdl_wait();  // x may be the previous kernel's output
 
   // ---- x prologue, one pass. Each warp takes 256-element blocks of x (one super-block of one
   // vector: an "x-block"), four at a time with all 32 loads of a lane in flight. Per x-block:
@@ -674,7 +734,7 @@ __global__ void __launch_bounds__((kMaxWarps + 1) * 32, 1) warpmma_kernel(const 
           const uint32_t b = xb / a.nb, kb = xb - b * a.nb;
           const float* src = a.x + b * a.ldx + kb * kQK + lane;
 #pragma unroll
-          for (int r = 0; r < 8; ++r) v[j][r] = src[32 * r];
+          for (int r = 0; r < 8; ++r) v[j][r] = __ldcg(src + 32 * r);
         }
       }
 #pragma unroll
@@ -1043,15 +1103,19 @@ __global__ void __launch_bounds__((kMaxWarps + 1) * 32, 1) warpmma_kernel(const 
         const float* rp = red + ((bj * kTileRows + row16) * nw) * B + b;
         for (uint32_t w = 0; w < nw; ++w) v0 += rp[w * B];
         v0 *= s_ns[b];
-        if (R == 1) {
-          a.y[b * a.ldy + row] = v0;
-        } else {
+        uint32_t out = row;
+        if (R != 1) {
           float v1 = 0.f;
           const float* rq = rp + nw * B;
           for (uint32_t w = 0; w < nw; ++w) v1 += rq[w * B];
           v1 *= s_ns[b];
-          a.y[b * a.ldy + row / 2] = pair_value(v0, v1, a.epilogue, a.pair_scale);
+          v0 = pair_value(v0, v1, a.epilogue, a.pair_scale);
+          out = row / 2;
         }
+        a.y[b * a.ldy + out] = v0;
+        // a chain job's pushed outputs also go to every rank's full vector (batch 1)
+        if (sync && out < sync->push_rows)
+          for (uint32_t rk = 0; rk < sync->npush; ++rk) sync->push_y[rk][out] = v0;
       }
       named_barrier(1, nthr);
       bi = 0;
@@ -1075,7 +1139,7 @@ __global__ void __launch_bounds__((kMaxWarps + 1) * 32, 1) warpmma_kernel(const 
         const uint32_t bB = g == c + 4 ? tkb + 8 * 24 : zero_s;
         const uint32_t mkb = mtable_s + (kb * 48 + 2 * c) * 4;
         const uint32_t off_g = pg_rb + kb * kBlk, off_h = ph_rb + kb * kBlk;
-        uint32_t s = 0, phase = 0, bi = 0;
+        uint32_t bi = 0;
         for (uint32_t band = 0; band < nbands; ++band) {
           bool ok = !*reinterpret_cast<volatile int*>(&s_failed);
           if (ok && !mbar_wait(full_bar(s), phase)) {
@@ -1137,7 +1201,7 @@ __global__ void __launch_bounds__((kMaxWarps + 1) * 32, 1) warpmma_kernel(const 
         q4f16_consts(kb, tab_t, bm_at, u0, u1);
       }
       const uint32_t off_g = pg_rb + kb * kBlk, off_h = ph_rb + kb * kBlk;
-      uint32_t s = 0, phase = 0, bi = 0;
+      uint32_t bi = 0;
       for (uint32_t band = 0; band < nbands; ++band) {
         bool ok = !*reinterpret_cast<volatile int*>(&s_failed);
         if (ok && !mbar_wait(full_bar(s), phase)) {
@@ -1167,7 +1231,7 @@ __global__ void __launch_bounds__((kMaxWarps + 1) * 32, 1) warpmma_kernel(const 
 
   // Unit j (super-block kc0 + j) of a tile goes to warp (rot + j) mod nw, rot advancing by the
   // tile's super-block count, so the warps take turns when there are more warps than blocks.
-  uint32_t s = 0, phase = 0, bi = 0, rot = 0;
+  uint32_t bi = 0, rot = 0;
   for (uint32_t band = 0; band < nbands; ++band) {
   const uint32_t r0 = r_begin + band * kTileRows;
   uint32_t kc0 = 0;
@@ -1297,6 +1361,122 @@ __global__ void __launch_bounds__((kMaxWarps + 1) * 32, 1) warpmma_kernel(const 
   }  // bands
 }
 
+// ---------------------------------------------------------------- the kernels
+
+// QT: 4, 5 or 6. NT: n8 tiles per MMA step (2 when batch 5..8 takes hi and lo in separate tiles).
+// HILO: x enters as hi + lo (else hi only). I8 (batch 1): integer MMAs, A = the raw quants as
+// bytes, x as three signed byte limbs (24-bit fixed point per 256-element block), the eight MMA
+// columns separating sub-blocks.
+template <int QT, int NT, bool HILO, bool I8>
+__global__ void __launch_bounds__((kMaxWarps + 1) * 32, 1) warpmma_kernel(const WarpMmaArgs a) {
+  extern __shared__ __align__(128) uint8_t smem[];
+  __shared__ WarpMmaShared sh;
+  uint8_t* base = smem_base(smem);
+  init_ring(a, base, sh);
+  pdl_launch_dependents();
+  uint32_t s = 0, phase = 0;
+  if ((threadIdx.x >> 5) == a.nw) {
+    if (!(a.flags & KQ_FLAG_WEIGHTS_STATIC)) pdl_wait();
+    uint32_t issued = 0;
+    produce_job<QT>(a, base, sh, s, phase, issued);
+    return;
+  }
+  pdl_wait();  // x may be the previous kernel's output
+  consume_job<QT, NT, HILO, I8>(a, nullptr, base, sh, s, phase);
+}
+
+// Bounded wait (acquire, system scope) by one thread until *cnt >= target; on giving up it
+// records kErrWaitPeer and returns false (at once when the CTA already failed).
+__device__ __forceinline__ bool wait_at_least(unsigned* err, const unsigned long long* cnt,
+                                              unsigned long long target, const int* failed) {
+  if (ld_acquire_sys(cnt) >= target) return true;
+  if (*reinterpret_cast<const volatile int*>(failed) || (err && *reinterpret_cast<volatile unsigned*>(err)))
+    return false;
+  const uint64_t t0 = globaltimer();
+  while (ld_acquire_sys(cnt) < target) {
+    if (globaltimer() - t0 > kWaitBudgetNs) {
+      report_error(err, kErrWaitPeer);
+      return false;
+    }
+    __nanosleep(32);
+  }
+  return true;
+}
+
+// A chain: the batch-1 integer matvecs p.job[0..njobs) of one type and k in one launch, each
+// reading the previous one's output. The producer streams the jobs' tiles back to back, so the
+// next matrix's weights are in flight while the consumers finish a matrix and wait for its
+// output. Between jobs, instead of a kernel boundary: every CTA, once its outputs of job j are
+// stored (on this GPU, and with a push on every rank's), adds its output count to job j's
+// counter(s) (release; system scope when pushing to other GPUs); job j + 1's consumers wait
+// (bounded, acquire) until their counter reaches *epoch * wait_target, i.e. until every CTA of
+// every rank has stored its part of x for this token. The counters only grow: *epoch, which the
+// caller advances once per token, makes each token's targets its own. All CTAs of the grid wait
+// on one another, so the grid is one CTA per SM and the CTAs must all be resident: nothing else
+// may hold an SM for good while a chain runs (kernels before it in the stream finish on their
+// own; kernels after it start only as its CTAs exit).
+template <int QT>
+__global__ void __launch_bounds__((kMaxWarps + 1) * 32, 1)
+    warpmma_chain_kernel(const __grid_constant__ ChainParams p) {
+  extern __shared__ __align__(128) uint8_t smem[];
+  __shared__ WarpMmaShared sh;
+  uint8_t* base = smem_base(smem);
+  const WarpMmaArgs& a0 = p.job[0];
+  init_ring(a0, base, sh);
+  pdl_launch_dependents();
+  const uint32_t nw = a0.nw, nthr = nw * 32;
+  uint32_t s = 0, phase = 0;
+  if ((threadIdx.x >> 5) == nw) {
+    if (!(a0.flags & KQ_FLAG_WEIGHTS_STATIC)) pdl_wait();
+    uint32_t issued = 0;
+    bool ok = true;
+    for (uint32_t j = 0; j < p.njobs && ok; ++j) ok = produce_job<QT>(p.job[j], base, sh, s, phase, issued);
+    if (!ok && (threadIdx.x & 31) == 0) {
+      // a wait gave up: before the CTA ends, let the copies still in flight into its ring land
+      // (each slot's last phase; bounded like every wait)
+      const uint32_t n = min(issued, a0.ring);
+      uint64_t* bars = reinterpret_cast<uint64_t*>(base + a0.bars_off);
+      uint32_t ss = s, ph = phase;
+      for (uint32_t i = 0; i < n; ++i) {
+        if (ss == 0) {
+          ss = a0.ring;
+          ph ^= 1;
+        }
+        --ss;
+        mbar_wait_sleep(smem_u32(&bars[ss]), ph);
+      }
+    }
+    return;
+  }
+  pdl_wait();  // the first job's x may be the previous kernel's output
+  unsigned long long epoch = 0;
+  if (threadIdx.x == 0) epoch = ld_acquire_sys(p.epoch);
+  for (uint32_t j = 0; j < p.njobs; ++j) {
+    const WarpMmaArgs& a = p.job[j];
+    const ChainSync& y = p.sync[j];
+    if (y.wait_cnt) {
+      if (threadIdx.x == 0 && !wait_at_least(a.err, y.wait_cnt, epoch * y.wait_target, &sh.failed))
+        sh.failed = 1;
+      named_barrier(1, nthr);
+    }
+    consume_job<QT, 1, false, true>(a, &y, base, sh, s, phase);
+    named_barrier(1, nthr);  // every consumer's outputs of job j are stored
+    if (threadIdx.x == 0 && y.counter[0]) {
+      uint32_t r_begin, r_end;
+      cta_rows(a, r_begin, r_end);
+      const uint32_t o0 = r_begin / a.row_unit, o1 = r_end / a.row_unit;
+      if (y.npush) {
+        const uint32_t pushed = o1 > y.push_rows ? (o0 < y.push_rows ? y.push_rows - o0 : 0u) : o1 - o0;
+        __threadfence_system();
+        for (uint32_t rk = 0; rk < y.npush; ++rk) atomicAdd_system(y.counter[rk], static_cast<unsigned long long>(pushed));
+      } else {
+        __threadfence();
+        atomicAdd(y.counter[0], static_cast<unsigned long long>(o1 - o0));
+      }
+    }
+  }
+}
+
 struct Variant {
   const void* fn;
   int qt, nt;
@@ -1312,6 +1492,13 @@ const Variant kVariants[] = {variant<4, 1, true>(), variant<4, 2, true>(), varia
                              variant<6, 1, false>(), variant<4, 1, false, true>(),
                              variant<6, 1, false, true>(), variant<5, 1, false, true>()};
 
+// The chain kernel of a type (Q4_K, Q5_K or Q6_K).
+const void* chain_fn(uint32_t type) {
+  return type == KQ_TYPE_Q4_K   ? reinterpret_cast<const void*>(&warpmma_chain_kernel<4>)
+         : type == KQ_TYPE_Q5_K ? reinterpret_cast<const void*>(&warpmma_chain_kernel<5>)
+                                : reinterpret_cast<const void*>(&warpmma_chain_kernel<6>);
+}
+
 }  // namespace
 
 int warpmma_prepare(kq_ctx* ctx) {
@@ -1319,6 +1506,11 @@ int warpmma_prepare(kq_ctx* ctx) {
     const cudaError_t e =
         cudaFuncSetAttribute(v.fn, cudaFuncAttributeMaxDynamicSharedMemorySize, ctx->max_smem);
     if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute", "warp-MMA matvec kernel");
+  }
+  for (uint32_t t : {uint32_t(KQ_TYPE_Q4_K), uint32_t(KQ_TYPE_Q5_K), uint32_t(KQ_TYPE_Q6_K)}) {
+    const cudaError_t e =
+        cudaFuncSetAttribute(chain_fn(t), cudaFuncAttributeMaxDynamicSharedMemorySize, ctx->max_smem);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute", "warp-MMA chain kernel");
   }
   return KQ_OK;
 }
@@ -1329,9 +1521,19 @@ bool warpmma_supports(const kq_matvec_desc& d) {
   return false;
 }
 
-int warpmma_matvec(kq_ctx* ctx, const kq_matvec_desc& d, uint64_t ldx, uint64_t ldy,
-                   cudaStream_t stream) {
-  const char* call = "kq_matvec";
+namespace {
+
+// A planned warp-MMA launch: the kernel's arguments, the variant, and the launch shape.
+struct WarpMmaPlan {
+  WarpMmaArgs args;
+  int mode;  // index into kVariants
+  uint32_t smem, grid, block;
+};
+
+// Chooses the variant, the tiles and the shared-memory layout of one matvec (arguments already
+// checked by the caller), as the standalone launch uses them.
+int warpmma_plan(kq_ctx* ctx, const kq_matvec_desc& d, uint64_t ldx, uint64_t ldy, const char* call,
+                 WarpMmaPlan& plan) {
   const bool q4 = d.type == KQ_TYPE_Q4_K;
   const bool q5 = d.type == KQ_TYPE_Q5_K;  // Q4_K's layout plus qh: the Q4_K forms, integer only
   const bool q45 = q4 || q5;
@@ -1482,25 +1684,120 @@ int warpmma_matvec(kq_ctx* ctx, const kq_matvec_desc& d, uint64_t ldx, uint64_t 
   const uint32_t smem = args.bars_off + 2 * 8 * 8 + 128;
 
   const uint64_t units = d.rows / args.row_unit;
-  const uint32_t grid = static_cast<uint32_t>(std::min<uint64_t>(ctx->sm_count, units));
+  plan.args = args;
+  plan.mode = mode;
+  plan.smem = smem;
+  plan.grid = static_cast<uint32_t>(std::min<uint64_t>(ctx->sm_count, units));
+  plan.block = (nw + 1) * 32;
+  return KQ_OK;
+}
 
+cudaError_t launch(const void* fn, uint32_t grid, uint32_t block, uint32_t smem, bool pdl,
+                   cudaStream_t stream, void* arg) {
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(grid);
-  cfg.blockDim = dim3((nw + 1) * 32);
+  cfg.blockDim = dim3(block);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = stream;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = (d.flags & KQ_FLAG_NO_PDL) ? 0 : 1;
-  void* params[] = {&args};
-  const cudaError_t e = cudaLaunchKernelExC(&cfg, kVariants[mode].fn, params);
+  cfg.numAttrs = pdl ? 1 : 0;
+  void* params[] = {arg};
+  return cudaLaunchKernelExC(&cfg, fn, params);
+}
+
+std::string shape(uint32_t grid, uint32_t block, uint32_t smem) {
+  return "grid " + std::to_string(grid) + " x " + std::to_string(block) + " threads, " +
+         std::to_string(smem) + " B shared";
+}
+
+// Does the layout of b match a's (ring, tiles, shared-memory regions, warps)?
+bool same_layout(const WarpMmaArgs& a, const WarpMmaArgs& b) {
+  return a.row_bytes == b.row_bytes && a.nb == b.nb && a.nkt == b.nkt && a.nw == b.nw &&
+         a.ring == b.ring && a.slot_bytes == b.slot_bytes && a.seg_bytes == b.seg_bytes &&
+         a.table_off == b.table_off && a.mtable_off == b.mtable_off && a.ublk_off == b.ublk_off &&
+         a.zero_off == b.zero_off && a.red_off == b.red_off && a.bars_off == b.bars_off &&
+         a.row_perm == b.row_perm && a.split_tile == b.split_tile &&
+         a.fixed_blocks == b.fixed_blocks && a.ncol == b.ncol && a.fb == b.fb;
+}
+
+}  // namespace
+
+int warpmma_matvec(kq_ctx* ctx, const kq_matvec_desc& d, uint64_t ldx, uint64_t ldy,
+                   cudaStream_t stream) {
+  WarpMmaPlan plan;
+  int rc = warpmma_plan(ctx, d, ldx, ldy, "kq_matvec", plan);
+  if (rc) return rc;
+  const cudaError_t e = launch(kVariants[plan.mode].fn, plan.grid, plan.block, plan.smem,
+                               !(d.flags & KQ_FLAG_NO_PDL), stream, &plan.args);
   if (e != cudaSuccess)
-    return cuda_fail(e, "cudaLaunchKernelExC",
-                     "warp-MMA matvec grid " + std::to_string(grid) + " x " +
-                         std::to_string((nw + 1) * 32) + " threads, " + std::to_string(smem) +
-                         " B shared");
+    return cuda_fail(e, "cudaLaunchKernelExC", "warp-MMA matvec " + shape(plan.grid, plan.block, plan.smem));
+  return KQ_OK;
+}
+
+int warpmma_chain(kq_ctx* ctx, const kq_chain_job* jobs, uint32_t njobs, uint64_t epoch,
+                  cudaStream_t stream) {
+  const char* call = "kq_matvec_chain";
+  if (!jobs || njobs == 0 || njobs > kChainMaxJobs)
+    return fail(KQ_E_INVALID, call, "1.." + std::to_string(kChainMaxJobs) + " jobs");
+  if (!epoch || epoch % 8) return fail(KQ_E_INVALID, call, "epoch must be a non-null 8-byte aligned address");
+  ChainParams p = {};
+  p.epoch = reinterpret_cast<const unsigned long long*>(epoch);
+  p.njobs = njobs;
+  uint32_t smem = 0, block = 0;
+  for (uint32_t j = 0; j < njobs; ++j) {
+    const kq_chain_job& job = jobs[j];
+    const kq_matvec_desc& d = job.mv;
+    const std::string at = "job " + std::to_string(j) + ": ";
+    int rc = check_desc(d, call);
+    if (rc) return rc;
+    if (d.type != jobs[0].mv.type || d.k != jobs[0].mv.k)
+      return fail(KQ_E_INVALID, call, at + "every job of a chain has the first job's type and k");
+    if (d.batch != 1 || (d.type != KQ_TYPE_Q4_K && d.type != KQ_TYPE_Q5_K && d.type != KQ_TYPE_Q6_K))
+      return fail(KQ_E_INVALID, call, at + "chains take batch-1 Q4_K, Q5_K or Q6_K matvecs");
+    if (d.ldx > d.k || d.ldy > (d.epilogue != KQ_EPILOGUE_NONE ? d.rows / 2 : d.rows))
+      return fail(KQ_E_INVALID, call, at + "batch 1 has no strides");
+    if (d.flags & (KQ_FLAG_TENSOR_CORES | KQ_FLAG_CUDA_CORES | kFlagAltBatch1 | kFlagWarpPerBlock))
+      return fail(KQ_E_INVALID, call, at + "chains run the warp-MMA integer kernel only");
+    if (job.npush > kChainMaxRanks) return fail(KQ_E_INVALID, call, at + "npush above 8");
+    const uint32_t outs = d.epilogue != KQ_EPILOGUE_NONE ? d.rows / 2 : d.rows;
+    if (job.npush && (job.push_rows == 0 || job.push_rows > outs))
+      return fail(KQ_E_INVALID, call, at + "push_rows must be 1..the job's outputs");
+    for (uint32_t r = 0; r < job.npush; ++r)
+      if (!job.push_y[r] || job.push_y[r] % 4 || !job.counter[r] || job.counter[r] % 8)
+        return fail(KQ_E_INVALID, call, at + "push_y must be 4-byte and counter 8-byte aligned, non-null");
+    if (!job.npush && job.counter[0] % 8) return fail(KQ_E_INVALID, call, at + "counter must be 8-byte aligned");
+    if (job.wait_counter % 8) return fail(KQ_E_INVALID, call, at + "wait_counter must be 8-byte aligned");
+    WarpMmaPlan plan;
+    rc = warpmma_plan(ctx, d, d.k, outs, call, plan);
+    if (rc) return rc;
+    if (plan.mode != (d.type == KQ_TYPE_Q4_K ? 4 : d.type == KQ_TYPE_Q5_K ? 6 : 5))
+      return fail(KQ_E_UNSUPPORTED, call, at + "k " + std::to_string(d.k) + " does not fit the integer kernel");
+    if (j && !same_layout(p.job[0], plan.args))
+      return fail(KQ_E_UNSUPPORTED, call, at + "its tiles differ from the first job's");
+    p.job[j] = plan.args;
+    smem = plan.smem;
+    block = plan.block;
+    ChainSync& y = p.sync[j];
+    y.wait_cnt = reinterpret_cast<const unsigned long long*>(job.wait_counter);
+    y.wait_target = job.wait_target;
+    y.npush = job.npush;
+    y.push_rows = job.npush ? job.push_rows : 0;
+    for (uint32_t r = 0; r < kChainMaxRanks; ++r) {
+      y.push_y[r] = r < job.npush ? reinterpret_cast<float*>(job.push_y[r]) : nullptr;
+      y.counter[r] = (r < job.npush || (r == 0 && !job.npush))
+                         ? reinterpret_cast<unsigned long long*>(job.counter[r])
+                         : nullptr;
+    }
+  }
+  // one CTA per SM for every job: the CTAs wait on one another between jobs
+  const uint32_t grid = static_cast<uint32_t>(ctx->sm_count);
+  const cudaError_t e = launch(chain_fn(jobs[0].mv.type), grid, block, smem,
+                               !(jobs[0].mv.flags & KQ_FLAG_NO_PDL), stream, &p);
+  if (e != cudaSuccess)
+    return cuda_fail(e, "cudaLaunchKernelExC", "warp-MMA chain " + shape(grid, block, smem));
   return KQ_OK;
 }
 

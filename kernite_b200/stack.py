@@ -139,6 +139,80 @@ def push_target(cfg: StackConfig, key: str, occurrence: int) -> tuple[int, int]:
     return per_token, occurrence * n
 
 
+@dataclass(frozen=True)
+class ChainJob:
+    """One matvec of a token as a chain job (kq_matvec_chain): what it reads and writes, and the
+    counters that order it. Buffer names are full vectors ("x", "q", "o", "a", "xd", "logits",
+    read or pushed) or local outputs ("qkv", "o_loc", "a_loc", "x_loc", "l_loc")."""
+    name: str
+    layer: int
+    qtype: int
+    rows: int           # this rank's rows of the matrix
+    k: int
+    x: str              # the full vector it reads
+    y: str              # the local buffer that gets every output
+    push: str | None    # the full vector its outputs [0, push_rows) go to on every rank (world > 1)
+    push_rows: int
+    rmsnorm: bool
+    pair_scale: float | None
+    counter: int        # the counter its CTAs add to (index into the token's counters)
+    wait: int | None    # the counter x waits for, or None (the token's input)
+    wait_target: int    # what `wait` gains per token
+    outputs: int        # outputs on this rank (rows, or rows / 2 for the pair product)
+
+
+def chain_plan(cfg: StackConfig, rank: int, world: int) -> tuple[list[ChainJob], list[list[int]]]:
+    """A token of the stack as chain jobs, and how they group into launches (runs of jobs with
+    one type and k, at most 8: per layer q|k|v, o, gate|up in one launch and down in another,
+    then the head). Job i adds to counter i: with one rank every output it stores, with N ranks
+    the outputs it pushes to every rank's full vector (N * push_rows per token on each rank), and
+    the job that reads that vector waits for exactly that count."""
+    sh = plan(cfg, rank, world)
+    h, f = cfg.hidden, cfg.ffn
+    jobs: list[ChainJob] = []
+
+    def add(name, layer, x, y, push, push_rows, rmsnorm=False, pair_scale=None):
+        shard = sh[name]
+        outputs = shard.rows // 2 if pair_scale is not None else shard.rows
+        prev = jobs[-1] if jobs else None
+        if prev is None:
+            wait, target = None, 0
+        else:
+            wait = prev.counter
+            target = prev.outputs if world == 1 else world * prev.push_rows
+        jobs.append(ChainJob(name, layer, shard.qtype, shard.rows, shard.k, x, y,
+                             push if world > 1 else None, push_rows if world > 1 else 0, rmsnorm,
+                             pair_scale, len(jobs), wait, target, outputs))
+
+    for layer in range(cfg.layers):
+        add("qkv", layer, "x" if layer == 0 else "xd", "qkv", "q", h // world, rmsnorm=layer > 0)
+        add("o", layer, "q", "o_loc", "o", h // world)
+        add("gate_up", layer, "o", "a_loc", "a", f // world, pair_scale=1.0 / math.sqrt(f))
+        add("down", layer, "a", "x_loc", "xd", h // world)
+    add("head", cfg.layers, "xd" if cfg.layers else "x", "l_loc", "logits", cfg.vocab // world,
+        rmsnorm=True)
+    launches: list[list[int]] = []
+    for i, j in enumerate(jobs):
+        cur = launches[-1] if launches else None
+        if cur and len(cur) < 8 and (jobs[cur[0]].qtype, jobs[cur[0]].k) == (j.qtype, j.k):
+            cur.append(i)
+        else:
+            launches.append([i])
+    return jobs, launches
+
+
+def chain_layout(cfg: StackConfig, njobs: int) -> tuple[dict[str, int], int]:
+    """Byte offsets in a rank's region for chains (identical on every rank): the step counter
+    ("epoch") and one u64 counter per job of the token ("counters"), then the full vectors, each
+    256-byte aligned. Returns (offsets, total bytes)."""
+    off = {"epoch": 0, "counters": 8}
+    pos = (8 + 8 * njobs + 255) // 256 * 256
+    for k, n in full_sizes(cfg).items():
+        off[k] = pos
+        pos += (n * 4 + 255) // 256 * 256
+    return off, pos
+
+
 class DecodeStack:
     """One rank's part of a decode stack on a backend. `forward(x)` runs one token."""
 
@@ -170,12 +244,17 @@ class DecodeStack:
             b["q"], b["o"], b["a"], b["xd"], b["logits"] = b["qkv"], b["o_loc"], b["a_loc"], b["x_loc"], b["l_loc"]
 
     def launches_per_token(self) -> int:
-        """This library's kernels per token: the matvecs, plus the closing wait of the push
-        exchange."""
+        """This library's kernels per token: the matvecs (chains: the step counter's advance and
+        one launch per run of jobs), plus the closing wait of an exchange between GPUs."""
+        if getattr(self.be, "chain", False):
+            return 1 + len(self.be.chain_launches) + (1 if self.world > 1 else 0)
         return 4 * self.cfg.layers + 1 + (1 if getattr(self.be, "push", False) else 0)
 
     def forward(self) -> None:
         """One token: reads buf['x'], writes buf['logits'] (on every rank)."""
+        if getattr(self.be, "chain", False):
+            self.be.chain_token(self)
+            return
         cfg, be, b, sh = self.cfg, self.be, self.buf, self.shards
         begin = getattr(be, "begin_token", None)
         if begin:
@@ -211,7 +290,7 @@ class CudaBackend:
     counts them there, and the next matvec waits for the count (kq_matvec_push)."""
 
     def __init__(self, kernels, stream=None, group=None, world: int = 1, flags: int = 0,
-                 push: bool = False, rank: int = 0):
+                 push: bool = False, rank: int = 0, chain: bool = False):
         import torch
 
         import kernite_b200 as kb
@@ -222,28 +301,107 @@ class CudaBackend:
         self.world = world
         self.rank = rank
         self.flags = flags
-        self.push = push and world > 1
+        self.chain = chain
+        self.push = push and world > 1 and not chain
         self.launches = 0
         self.region = None
         self.peers: list[int] = []
 
     # ---------------------------------------------------------------- push exchange set-up
-    def full_vectors(self, cfg: StackConfig, rank: int, world: int):
-        torch, kb = self.torch, self.kb
-        if not self.push:
-            return {k: self.vector(n) for k, n in full_sizes(cfg).items()}
+    def _map_region(self, nbytes: int, rank: int, world: int) -> None:
+        """This rank's exchange region (zeroed, IPC-shareable) and every peer's, mapped."""
         import torch.distributed as dist
 
-        self.cfg = cfg
-        self.off, nbytes = push_layout(cfg)
         ptr, handle = self.k.peer_alloc(nbytes)
         self.region = ptr
         handles = [None] * world
         dist.all_gather_object(handles, handle, group=self.group)
         self.peers = [ptr if p == rank else self.k.peer_open(handles[p]) for p in range(world)]
+
+    def full_vectors(self, cfg: StackConfig, rank: int, world: int):
+        torch, kb = self.torch, self.kb
+        if self.chain:
+            return self._chain_vectors(cfg, rank, world)
+        if not self.push:
+            return {k: self.vector(n) for k, n in full_sizes(cfg).items()}
+        self.cfg = cfg
+        self.off, nbytes = push_layout(cfg)
+        self._map_region(nbytes, rank, world)
+        ptr = self.region
         view = lambda off, n, t="<f4": torch.as_tensor(kb.DeviceArray(ptr + off, n, t), device="cuda")
         self.epoch = view(self.off["epoch"], 1, "<i8")
         return {k: view(self.off[k], n) for k, n in full_sizes(cfg).items()}
+
+    # ---------------------------------------------------------------- chains
+    def _chain_vectors(self, cfg: StackConfig, rank: int, world: int):
+        """Chains: the token's jobs, the step counter and job counters, and the full vectors (in
+        the exchange region every rank maps when world > 1)."""
+        torch, kb = self.torch, self.kb
+        self.cfg = cfg
+        self.chain_jobs, self.chain_launches = chain_plan(cfg, rank, world)
+        off, nbytes = chain_layout(cfg, len(self.chain_jobs))
+        self.coff = off
+        if world == 1:
+            self._counter_mem = torch.zeros(1 + len(self.chain_jobs), dtype=torch.int64, device="cuda")
+            base = self._counter_mem.data_ptr()
+            self.epoch_addr, self.counter_base = base, base + 8
+            return {k: self.vector(n) for k, n in full_sizes(cfg).items()}
+        self._map_region(nbytes, rank, world)
+        self.epoch_addr = self.region + off["epoch"]
+        self.counter_base = self.region + off["counters"]
+        view = lambda o, n: torch.as_tensor(kb.DeviceArray(self.region + o, n), device="cuda")
+        return {k: view(off[k], n) for k, n in full_sizes(cfg).items()}
+
+    def build_chains(self, stack: "DecodeStack") -> None:
+        """The kq_chain_job arrays of every launch of a token (addresses fixed from here on)."""
+        kb = self.kb
+        b = stack.buf
+        self.chain_arrays = []
+        for launch in self.chain_launches:
+            arr = (kb.KqChainJob * len(launch))()
+            for slot, i in enumerate(launch):
+                j = self.chain_jobs[i]
+                if j.layer < stack.cfg.layers:
+                    W = stack.weights[j.layer][j.name]
+                else:
+                    W = stack.head
+                d = arr[slot]
+                d.mv = kb.KqMatvecDesc(
+                    type={4: kb.TYPE_Q4_K, 6: kb.TYPE_Q6_K}[j.qtype], rows=j.rows, k=j.k, batch=1,
+                    y=b[j.y].data_ptr(), w=W.data_ptr(), x=b[j.x].data_ptr(), ldx=0, ldy=0,
+                    prologue=kb.PROLOGUE_RMSNORM if j.rmsnorm else kb.PROLOGUE_NONE,
+                    epilogue=kb.EPILOGUE_PAIR_PRODUCT if j.pair_scale is not None else kb.EPILOGUE_NONE,
+                    eps=stack.cfg.eps, pair_scale=j.pair_scale if j.pair_scale is not None else 1.0,
+                    flags=kb.FLAG_WEIGHTS_STATIC | self.flags, reserved=0)
+                if j.wait is not None:
+                    d.wait_counter = self.counter_base + 8 * j.wait
+                    d.wait_target = j.wait_target
+                if self.world == 1:
+                    d.npush = 0
+                    d.counter[0] = self.counter_base + 8 * j.counter
+                else:
+                    d.npush = self.world
+                    d.push_rows = j.push_rows
+                    for p, base in enumerate(self.peers):
+                        d.push_y[p] = base + self.coff[j.push] + 4 * self.rank * j.push_rows
+                        d.counter[p] = base + self.coff["counters"] + 8 * j.counter
+            self.chain_arrays.append(arr)
+
+    def chain_token(self, stack: "DecodeStack") -> None:
+        """One token as chains: advance the step counter, launch every run of jobs, and (world
+        > 1) wait until every rank's logits have arrived."""
+        if not hasattr(self, "chain_arrays"):
+            self.build_chains(stack)
+        self.k.epoch_advance(self.epoch_addr, stream=self.stream)
+        for arr in self.chain_arrays:
+            self.k.matvec_chain(arr, self.epoch_addr, stream=self.stream)
+        self.launches += 1 + len(self.chain_arrays)
+        if self.world > 1:
+            head = self.chain_jobs[-1]
+            n = self.world * head.push_rows
+            self.k.wait_counter(self.counter_base + 8 * head.counter, self.epoch_addr, n, n,
+                                stream=self.stream)
+            self.launches += 1
 
     def begin_token(self) -> None:
         if self.push:
@@ -261,7 +419,7 @@ class CudaBackend:
         """Unmaps the peers' regions and frees this rank's, once every rank is done with them
         (a collective step: all ranks call it)."""
         self.torch.cuda.synchronize()
-        if self.push:
+        if self.peers:
             import torch.distributed as dist
 
             dist.barrier(group=self.group)
@@ -332,9 +490,13 @@ class _null:
 
 
 def make_cuda_stack(cfg: StackConfig, kernels, rank: int = 0, world: int = 1, group=None,
-                    stream=None, flags: int = 0, push: bool = False) -> DecodeStack:
+                    stream=None, flags: int = 0, push: bool = False, chain: bool = False) -> DecodeStack:
+    """One rank's stack on libkq.so. The exchange between ranks (and the launches): NCCL
+    all-gathers after one matvec launch per projection (default), the matvec's own push to peer
+    memory (push=True, the CUDA-core kernel), or chains (chain=True: the warp-MMA kernel, up to
+    three projections per launch, outputs pushed to peer memory and ordered by counters)."""
     return DecodeStack(cfg, CudaBackend(kernels, stream=stream, group=group, world=world, flags=flags,
-                                        push=push, rank=rank), rank, world)
+                                        push=push, rank=rank, chain=chain), rank, world)
 
 
 # ---------------------------------------------------------------- reference (for tests)

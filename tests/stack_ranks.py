@@ -1,6 +1,7 @@
 """One rank of the sharded decode stack on the GPU (launched by tests/test_stack_multigpu.py
-under torchrun): runs the tiny and a 2-layer 70B-shaped stack with both exchanges (NCCL
-all-gathers, and the matvec's own push over peer mappings), one token eagerly and two more
+under torchrun): runs the tiny and a 2-layer 70B-shaped stack with each exchange (NCCL
+all-gathers; the CUDA-core matvec's own push over peer mappings; chains of the warp-MMA kernel
+pushing to peer memory, ordered by counters), one token eagerly and two more
 replayed from a CUDA graph, each token on new input, and checks the logits on every rank
 against the unsharded CPU reference."""
 import dataclasses
@@ -26,14 +27,15 @@ def main():
     kernels = kb.Kernels.load(local)
     ok = True
     refs = {}
-    for exchange in ("nccl", "push"):
+    for exchange in ("nccl", "push", "chain"):
         for name, cfg in (("tiny", st.CONFIGS["tiny"]), ("70b-2", dataclasses.replace(st.CONFIGS["70b"], layers=2))):
             xs = [np.random.default_rng(3 + t).standard_normal(cfg.hidden).astype(np.float32) for t in range(3)]
             for t, x in enumerate(xs):
                 if (name, t) not in refs:
                     refs[name, t] = st.reference_logits(cfg, x)
             stream = torch.cuda.Stream()
-            s = st.make_cuda_stack(cfg, kernels, rank, world, stream=stream, push=exchange == "push")
+            s = st.make_cuda_stack(cfg, kernels, rank, world, stream=stream, push=exchange == "push",
+                                   chain=exchange == "chain")
             s.buf["x"].copy_(torch.from_numpy(xs[0]).cuda())
             torch.cuda.synchronize()
             with torch.cuda.stream(stream):
@@ -56,7 +58,7 @@ def main():
             except kb.Error as e:  # keep taking the collective steps; fail at the end
                 print(f"rank {rank}: {e}", flush=True)
                 ok = False
-            if exchange == "push":
+            if exchange != "nccl":
                 s.be.close()
             for t, y in enumerate(out):
                 ref = refs[name, t]
