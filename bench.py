@@ -1,21 +1,34 @@
-"""Benchmark of the B200 Q4_K / Q6_K matvec (BASELINE.json metric: weight GB/s and % of HBM peak).
+"""Benchmark of the B200 k-quant path (BASELINE.json metric: weight GB/s and % of HBM peak for the
+Q4_K / Q6_K matvec; decode tokens/s).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--workload NAME] [--impl kq|reference]
 
-One JSON line on rank 0. A step is one matvec over one weight matrix in HBM (the workload's
-shape), its weights rotating over enough copies that their total exceeds twice the 126 MB L2,
-so every step streams from DRAM. Workloads:
+One JSON line on rank 0. Workloads:
 
-  q6k_head   configs[1]  Q6_K 32000 x 4096, batch 1   (default; the metric's config)
+  stack70b   configs[4]  Llama-70B-shaped decode matvec stack, rows sharded over the N GPUs
+                         (default): a step is one decode token
+  stack7b    configs[2]  Llama-7B-shaped decode matvec stack, a step is one token
+  q6k_head   configs[1]  Q6_K 32000 x 4096, batch 1: a step is one matvec
   q4k        configs[0]  Q4_K 4096 x 4096, batch 1
   sweep      configs[3]  Q4_K 14336 x 4096, batch --batch (1..64)
-  stack7b    configs[2]  Llama-7B-shaped decode matvec stack, decode tokens/s
-  stack70b   configs[4]  Llama-70B-shaped stack, rows sharded over the N GPUs (NCCL all-gathers)
+  q5k                    Q5_K 14336 x 4096, batch 1 (the next k-quant type)
 
-With N GPUs (torchrun) every rank runs its own replica: the single matvec does not shard
-("replicas only"), so `scaling` is "weak" and `value` sums the ranks' bytes over the slowest
-rank's time. `--impl reference` times the CPU implementation of the path (the oracle's AVX2 C
-port, all host threads) on the same workload; under torchrun only rank 0 runs it.
+Stacks: one token is one replay of a CUDA graph of the token's launches; by default chains of
+the warp-MMA kernel (per layer one launch for q|k|v, o and gate|up, one for down; the head),
+whose outputs, with N GPUs, are pushed into every rank's full vectors inside those launches
+(`--exchange nccl` times one launch per projection with NCCL all-gathers instead). `scaling` is
+"strong" (the model is fixed, its rows split over the N GPUs). Before timing, a 2-layer copy of
+the stack, sharded and exchanged the same way, is checked on every rank against the unsharded
+CPU reference ("parity" in the line); rank 0 at N=1 also times the Q6_K head matvec alone
+(configs[1], "matvec_q6k_head") and the CPU baseline.
+
+Single matvecs: a step is one launch over one weight matrix, its weights rotating over enough
+copies that their total exceeds twice the 126 MB L2, so every step streams from DRAM. With N GPUs
+every rank runs its own replica ("replicas only": `scaling` "weak", `value` sums the ranks'
+bytes over the slowest rank's time).
+
+`--impl reference` times the CPU implementation of the path (the oracle's AVX2 C port, all host
+threads) on the same workload; under torchrun only rank 0 runs it.
 """
 from __future__ import annotations
 
@@ -55,23 +68,33 @@ STACKS = {"stack7b": "7b", "stack70b": "70b"}
 def parse_args(argv=None):
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20000)
-    ap.add_argument("--warmup", type=int, default=200)
-    ap.add_argument("--workload", default="q6k_head", choices=sorted(WORKLOADS) + sorted(STACKS))
+    ap.add_argument("--steps", type=int, default=None,
+                    help="timed steps (default 200 tokens for stacks, 20000 launches for a matvec)")
+    ap.add_argument("--warmup", type=int, default=None, help="untimed steps (default 5 / 200)")
+    ap.add_argument("--workload", default="stack70b", choices=sorted(WORKLOADS) + sorted(STACKS))
     ap.add_argument("--batch", type=int, default=1)
     ap.add_argument("--path", default="auto", choices=["auto", "tc", "cc", "wm"],
                     help="tensor cores (tcgen05), CUDA cores, warp-level MMA, or the library's choice")
     ap.add_argument("--extra-flags", type=lambda v: int(v, 0), default=0,
                     help="more descriptor flag bits OR-ed into every timed launch (A/B tests)")
     ap.add_argument("--impl", default="kq", choices=["kq", "reference"])
-    ap.add_argument("--exchange", default="nccl", choices=["nccl", "push", "chain"],
+    ap.add_argument("--exchange", default="chain", choices=["nccl", "push", "chain"],
                     help="stacks: NCCL all-gathers after one launch per projection, the CUDA-core "
                          "matvec's own push to peer memory, or chains of the warp-MMA kernel (up to "
                          "three projections a launch, outputs pushed to peer memory at N > 1)")
     ap.add_argument("--e2e-steps", type=int, default=2000, help="steps of the end-to-end leg")
     ap.add_argument("--cpu-seconds", type=float, default=12.0, help="CPU-baseline time budget")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    return ap.parse_args(argv)
+    ap.add_argument("--layers", type=int, default=None,
+                    help="stacks: run only the first N layers (smaller cases for profiling; the "
+                         "line's config says so); default: the config's layer count")
+    args = ap.parse_args(argv)
+    stack = args.workload in STACKS
+    if args.steps is None:
+        args.steps = 200 if stack else 20000
+    if args.warmup is None:
+        args.warmup = 5 if stack else 200
+    return args
 
 
 def measured_peak():
@@ -244,12 +267,23 @@ def run_reference(args):
     return 0
 
 
+def rotation_copies(wbytes: int) -> int:
+    """Weight copies a single-matvec run rotates over: their total exceeds twice the L2."""
+    return max(2, -(-2 * L2_BYTES // wbytes) + 1)
+
+
 def config_of(args, w, world):
+    """The workload description of a single-matvec run, the same in both arms."""
+    import oracle
+
+    wbytes = w["rows"] * (w["k"] // 256) * oracle.block_bytes(w["qtype"])
+    copies = rotation_copies(wbytes)
     return {
         "workload": f"{args.workload}: Q{w['qtype']}_K {w['rows']}x{w['k']} batch {w['batch']} ({w['source']})",
         "qtype": f"Q{w['qtype']}_K", "rows": w["rows"], "k": w["k"], "batch": w["batch"],
         "path": args.path,
         "parallelism": f"replicas x{world}" if world > 1 else "single",
+        "l2": f"weights rotate over {copies} copies ({copies * wbytes / 1e6:.0f} MB > 2x L2)",
     }
 
 
@@ -280,7 +314,7 @@ def main(argv=None):
     qtype, rows, K, batch = w["qtype"], w["rows"], w["k"], w["batch"]
     wbytes = kb.matrix_bytes(qtype, rows, K)
     algo_bytes = wbytes + batch * K * 4 + batch * rows * 4
-    copies = max(2, -(-2 * L2_BYTES // wbytes) + 1)
+    copies = rotation_copies(wbytes)
     nblk = rows * K // 256
     Ws = []
     for c in range(copies):
@@ -385,7 +419,6 @@ def main(argv=None):
 
     if rank == 0:
         cfg = config_of(args, w, world)
-        cfg["l2"] = f"weights rotate over {copies} copies ({copies * wbytes / 1e6:.0f} MB > 2x L2)"
         line = {
             "metric": "weight GB/s", "value": round(value, 2), "unit": "GB/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_step, 6),
@@ -454,8 +487,9 @@ def _init_dist(torch, world, local):
     return dist
 
 
-def stack_cpu_seconds_per_token(cfg, threads, also_single=False):
-    """CPU baseline for a stack: one layer's matvecs and the head timed with the AVX2 port,
+def stack_cpu_seconds_per_token(cfg, threads, also_single=False, layers_timed=3):
+    """CPU baseline for a stack: the matvecs of the first `layers_timed` layers (each matrix its
+    own weights, timed once after a warm-up call) and the head, with the AVX2 port, the layers
     scaled to the stack's layer count. Returns (seconds per token, sample), and with
     `also_single` the seconds per token on one thread as well (same matrices, timed after)."""
     import numpy as np
@@ -467,6 +501,7 @@ def stack_cpu_seconds_per_token(cfg, threads, also_single=False):
     rng = np.random.default_rng(0)
     counts = [threads, 1] if also_single else [threads]
     t = {n: 0.0 for n in counts}
+    nl = max(1, min(layers_timed, cfg.layers))
 
     def timed(qtype, W, x, rows, k, scale):
         for n in counts:
@@ -476,28 +511,147 @@ def stack_cpu_seconds_per_token(cfg, threads, also_single=False):
             oracle.matvec_cpu(qtype, W, x, rows, k, n)
             t[n] += scale * (time.perf_counter() - t0)
 
-    for name, qtype, rows, k in cfg.matrices():
-        W = oracle.fill(qtype, oracle.stream_key(cfg.seed, cfg.tensor_id(0, name)), 0, rows * k // st.QK)
-        timed(qtype, W, rng.standard_normal((1, k), dtype=np.float32), rows, k, cfg.layers)
-        del W
+    for layer in range(nl):
+        for name, qtype, rows, k in cfg.matrices():
+            W = oracle.fill(qtype, oracle.stream_key(cfg.seed, cfg.tensor_id(layer, name)), 0, rows * k // st.QK)
+            timed(qtype, W, rng.standard_normal((1, k), dtype=np.float32), rows, k, cfg.layers / nl)
+            del W
     H = oracle.fill(6, oracle.stream_key(cfg.seed, cfg.tensor_id(cfg.layers, "head")), 0,
                     cfg.vocab * cfg.hidden // st.QK)
     timed(6, H, rng.standard_normal((1, cfg.hidden), dtype=np.float32), cfg.vocab, cfg.hidden, 1)
-    sample = f"layer 0 (4 matvecs) and the head timed once each, scaled to {cfg.layers} layers"
+    sample = (f"layers 0..{nl - 1} (4 matvecs each, own weights) and the head, each timed once after "
+              f"a warm-up call; layers scaled to {cfg.layers}")
     if also_single:
         return t[threads], sample, t[1]
     return t[threads], sample
 
 
+def stack_config(args, cfg, world, chain):
+    """The workload description of a stack run, the same in both arms."""
+    return {"workload": f"{args.workload}: {cfg.name}", "layers": cfg.layers, "hidden": cfg.hidden,
+            "ffn": cfg.ffn, "kv": cfg.kv, "vocab": cfg.vocab, "batch": 1,
+            "parallelism": (f"rows sharded x{world}, " + (
+                "chains, push to peer memory" if chain else "push to peer memory"
+                if args.exchange == "push" else "NCCL all-gather")) if world > 1 else
+            ("single, chains" if chain else "single"),
+            "graph": True,
+            "l2": f"{cfg.weight_bytes() / world / 1e9:.1f} GB of weights per GPU per token > L2"}
+
+
+def stack_parity(cfg, kernels, rank, world, chain, push, dist):
+    """On-run parity of the stack exactly as timed (same sharding, exchange and kernels) on its
+    first two layers: every rank runs one token of a 2-layer copy (same seed, shapes and shards)
+    on seeded input; every rank's logits must be identical (checked by an all-reduce of max and
+    min), and rank 0 checks them against the unsharded f64 CPU reference within
+    1e-3 * sum_k |w_head x_k| per logit (x = the reference's normalised head input)."""
+    import dataclasses
+
+    import numpy as np
+    import torch
+
+    import oracle
+
+    from kernite_b200 import stack as st
+
+    c2 = dataclasses.replace(cfg, layers=min(2, cfg.layers))
+    stream = torch.cuda.Stream()
+    s = st.make_cuda_stack(c2, kernels, rank, world, stream=stream, push=push, chain=chain)
+    x = np.random.default_rng(31).standard_normal(c2.hidden).astype(np.float32)
+    s.buf["x"].copy_(torch.from_numpy(x).cuda())
+    torch.cuda.synchronize()
+    with torch.cuda.stream(stream):
+        s.forward()
+    torch.cuda.synchronize()
+    kernels.device_error()
+    got = s.buf["logits"].clone()
+    same = True
+    if dist:
+        hi, lo = got.clone(), got.clone()
+        dist.all_reduce(hi, op=dist.ReduceOp.MAX)
+        dist.all_reduce(lo, op=dist.ReduceOp.MIN)
+        same = bool(torch.equal(hi, lo))
+    if s.be.peers:
+        s.be.close()
+    del s
+    if rank != 0:
+        return None
+    ref, bound = st.reference_logits(c2, x, with_bound=True)
+    err = np.abs(got.cpu().numpy().astype(np.float64) - ref)
+    ratio = float((err / (1e-3 * bound)).max())
+    return {"parity_ok": bool(same and ratio <= 1.0), "worst_error_ratio": round(ratio, 5),
+            "ranks_identical": same,
+            "checked": f"2-layer copy of the stack, one token, {world} rank(s), against the f64 CPU "
+                       "reference: |logit - ref| <= 1e-3 * sum|w_head x|"}
+
+
+def time_lone_matvec(kernels, qtype, rows, K, steps=2000):
+    """The Q6_K head-shaped single matvec timed as the q6k_head workload
+    is, for the stack line's extra keys: weights rotating over copies totalling > 2x L2, graph-
+    replayed launches, CUDA events on the launching stream."""
+    import numpy as np
+    import torch
+
+    import kernite_b200 as kb
+
+    wbytes = kb.matrix_bytes(qtype, rows, K)
+    copies = rotation_copies(wbytes)
+    Ws = []
+    for c in range(copies):
+        W = torch.empty(wbytes, dtype=torch.uint8, device="cuda")
+        kernels.fill(qtype, W, 0, rows * K // 256, kb.stream_key(2026 + c, qtype))
+        Ws.append(W)
+    x = torch.from_numpy(np.random.default_rng(0).standard_normal((1, K), dtype=np.float32)).cuda()
+    y = torch.empty(1, rows, device="cuda")
+    stream = torch.cuda.Stream()
+    G = copies * max(1, 64 // copies)
+    with torch.cuda.stream(stream):
+        for i in range(3 * G):
+            kernels.matvec(qtype, y, Ws[i % copies], x, rows, K, 1, flags=kb.FLAG_WEIGHTS_STATIC, stream=stream)
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=stream):
+        for i in range(G):
+            kernels.matvec(qtype, y, Ws[i % copies], x, rows, K, 1, flags=kb.FLAG_WEIGHTS_STATIC, stream=stream)
+    reps = max(1, steps // G)
+    with torch.cuda.stream(stream):
+        g.replay()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(stream):
+        e0.record(stream)
+        for _ in range(reps):
+            g.replay()
+        e1.record(stream)
+    torch.cuda.synchronize()
+    kernels.device_error()
+    ms = e0.elapsed_time(e1) / (reps * G)
+    algo = wbytes + K * 4 + rows * 4
+    peak, kind = measured_peak()
+    del g
+    return {"workload": f"Q{qtype}_K {rows}x{K} batch 1 (BASELINE configs[1])", "launches": reps * G,
+            "us_per_launch": round(ms * 1e3, 3), "weight_gbs": round(wbytes / (ms / 1e3) / 1e9, 2),
+            "roofline": {"bound": "hbm", "achieved": round(algo / (ms / 1e3) / 1e9, 2), "peak": peak,
+                         "unit": "GB/s", "frac": round(algo / (ms / 1e3) / 1e9 / peak, 4),
+                         "peak_source": kind, "traffic": profiled_traffic("q6k_head"),
+                         "algorithmic_bytes_per_launch": algo}}
+
+
 def run_stack(args):
     """Decode tokens/s of a Llama-shaped matvec stack: one token = one replay of a CUDA graph
-    holding every layer's launches (and, for N > 1, the NCCL all-gathers)."""
+    holding every launch of the token (chains by default: per layer one launch for q|k|v, o and
+    gate|up and one for down, then the head; for N > 1 the outputs pushed to every rank's full
+    vectors inside those launches)."""
     import numpy as np
 
     from kernite_b200 import stack as st
 
     cfg = st.CONFIGS[STACKS[args.workload]]
+    if args.layers is not None:
+        import dataclasses
+
+        cfg = dataclasses.replace(cfg, layers=args.layers, name=f"{cfg.name}, first {args.layers} layers")
     world, rank, local = dist_setup()
+    chain = args.exchange == "chain"
     if args.impl == "reference":
         if rank != 0:
             return 0
@@ -507,13 +661,15 @@ def run_stack(args):
                 "unit": "tokens/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
                 "ms_per_step": round(sec * 1e3, 3), "higher_is_better": True, "scaling": "strong",
                 "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-                "config": {"workload": f"{args.workload}: {cfg.name}", "layers": cfg.layers,
-                           "hidden": cfg.hidden, "ffn": cfg.ffn, "kv": cfg.kv, "vocab": cfg.vocab},
+                "config": stack_config(args, cfg, world, chain),
                 "cpu_baseline": {"value": round(tps, 4), "unit": "tokens/s", "cores": HOST_THREADS,
                                  "kind": "port", "sample": sample, "cpu_model": cpu_model()},
                 "e2e": {"value": round(tps, 4), "unit": "tokens/s", "h2d_bytes_per_step": 0,
                         "d2h_bytes_per_step": 0},
-                "gpu_launches": 0}
+                "gpu_launches": 0,
+                "note": "fxeqxmulfx/kernite has no k-quant path and no Rust toolchain here; the CPU "
+                        "implementation timed is this repo's AVX2+FMA C port (oracle/kq_cpu.c) on the "
+                        "host's cores, one process whatever the GPU count"}
         print(json.dumps(line), flush=True)
         return 0
 
@@ -524,9 +680,9 @@ def run_stack(args):
     torch.cuda.set_device(local)
     dist = _init_dist(torch, world, local)
     kernels = kb.Kernels.load(local)
-    stream = torch.cuda.Stream()
     push = args.exchange == "push" and world > 1
-    chain = args.exchange == "chain"
+    parity = stack_parity(cfg, kernels, rank, world, chain, push, dist)
+    stream = torch.cuda.Stream()
     stack = st.make_cuda_stack(cfg, kernels, rank, world, stream=stream, push=push, chain=chain)
     x = torch.from_numpy(np.random.default_rng(0).standard_normal(cfg.hidden).astype(np.float32))
     stack.buf["x"].copy_(x.cuda())
@@ -537,24 +693,12 @@ def run_stack(args):
     torch.cuda.synchronize()
     kernels.device_error()
     graph = torch.cuda.CUDAGraph()
-    try:
-        with torch.cuda.graph(graph, stream=stream):
-            stack.forward()
-    except Exception as e:  # noqa: BLE001 - report and run eagerly
-        if rank == 0:
-            print(f"[bench] graph capture failed ({e}); timing eager launches", file=sys.stderr)
-        torch.cuda.synchronize()
-        graph = None
-
-    def token():
-        if graph is not None:
-            graph.replay()
-        else:
-            stack.forward()
+    with torch.cuda.graph(graph, stream=stream):
+        stack.forward()
 
     with torch.cuda.stream(stream):
         for _ in range(3):
-            token()
+            graph.replay()
     torch.cuda.synchronize()
     sampler = ClockSampler(local)
     sampler.start()
@@ -565,7 +709,7 @@ def run_stack(args):
     with torch.cuda.stream(stream):
         e0.record(stream)
         for _ in range(args.steps):
-            token()
+            graph.replay()
         e1.record(stream)
     torch.cuda.synchronize()
     if dist:
@@ -593,7 +737,7 @@ def run_stack(args):
         f0.record(stream)
         for _ in range(e2e_steps):
             stack.buf["x"].copy_(xh, non_blocking=True)
-            token()
+            graph.replay()
             lh.copy_(stack.buf["logits"], non_blocking=True)
             stream.synchronize()
         f1.record(stream)
@@ -614,37 +758,35 @@ def run_stack(args):
                 "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)" if peak_kind == "measured"
                 else "fallback 6650 GB/s",
                 "note": "achieved = the stack's weight bytes per GPU per token / token time"}
+    # A graph holding NCCL calls must be released before the process group goes, or the
+    # teardown waits for good.
+    torch.cuda.synchronize()
+    graph.reset()
+    graph = None
+    lone = None
     cpu = None
-    if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        sec, sample, sec1 = stack_cpu_seconds_per_token(cfg, HOST_THREADS, also_single=True)
-        cpu = {"value": round(1.0 / sec, 4), "unit": "tokens/s", "cores": HOST_THREADS,
-               "kind": "port", "sample": sample, "cpu_model": cpu_model(),
-               "single_thread": {"value": round(1.0 / sec1, 4), "sample": sample}}
+    if rank == 0 and world == 1:
+        lone = time_lone_matvec(kernels, 6, 32000, 4096)
+        if not args.no_cpu_baseline:
+            sec, sample, sec1 = stack_cpu_seconds_per_token(cfg, HOST_THREADS, also_single=True)
+            cpu = {"value": round(1.0 / sec, 4), "unit": "tokens/s", "cores": HOST_THREADS,
+                   "kind": "port", "sample": sample, "cpu_model": cpu_model(),
+                   "single_thread": {"value": round(1.0 / sec1, 4), "sample": sample}}
     if rank == 0:
         line = {
             "metric": "decode tokens/s", "value": round(tps, 3), "unit": "tokens/s",
             "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": round(ms_tok, 5), "higher_is_better": True, "scaling": "strong",
             "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-            "config": {"workload": f"{args.workload}: {cfg.name}", "layers": cfg.layers,
-                       "hidden": cfg.hidden, "ffn": cfg.ffn, "kv": cfg.kv, "vocab": cfg.vocab,
-                       "parallelism": (f"rows sharded x{world}, " + (
-                           "chains, push to peer memory" if chain else "push to peer memory" if push else
-                           "NCCL all-gather")) if world > 1 else ("single, chains" if chain else "single"),
-                       "graph": graph is not None, "batch": 1,
-                       "l2": f"{wbytes / world / 1e9:.1f} GB of weights per GPU per token > L2"},
+            "config": stack_config(args, cfg, world, chain),
             "weight_gbs": round(wbytes * tps / 1e9, 2),
-            "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e,
+            "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e, "parity": parity,
             "gpu_launches": args.steps * stack.launches_per_token(), "clocks": clocks,
         }
+        if lone is not None:
+            line["matvec_q6k_head"] = lone
         print(json.dumps(line), flush=True)
-    # A graph holding NCCL calls must be released before the process group goes, or the
-    # teardown waits for good.
-    torch.cuda.synchronize()
-    if graph is not None:
-        graph.reset()
-    graph = None
-    if push or (chain and world > 1):
+    if stack.be.peers:
         stack.be.close()
     if dist:
         dist.barrier()

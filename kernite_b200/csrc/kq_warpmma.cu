@@ -128,10 +128,22 @@ struct ChainSync {
   unsigned long long* counter[kChainMaxRanks];
 };
 
+// What one matvec has of its own when several share a launch's layout: its matrix, vectors and
+// fused glue. (A lone launch takes these from its WarpMmaArgs.)
+struct JobArgs {
+  const uint8_t* W;
+  const float* x;
+  float* y;
+  uint64_t total_bytes;
+  uint32_t rows, row_unit, prologue, epilogue;
+  float eps, pair_scale;
+};
+
 struct ChainParams {
+  WarpMmaArgs lay;                  // the layout every job shares (its per-job fields unused)
   const unsigned long long* epoch;  // this GPU's token counter
   uint32_t njobs;
-  WarpMmaArgs job[kChainMaxJobs];
+  JobArgs job[kChainMaxJobs];
   ChainSync sync[kChainMaxJobs];
 };
 
@@ -548,10 +560,16 @@ __device__ __forceinline__ void q4i8_block(uint32_t ag, uint32_t ah, uint32_t c,
 
 // The rows [r_begin, r_end) of a matvec that this CTA streams and multiplies: a contiguous share
 // of whole output units (pairs of rows for the product epilogues).
-__device__ __forceinline__ void cta_rows(const WarpMmaArgs& a, uint32_t& r_begin, uint32_t& r_end) {
-  const uint64_t units = a.rows / a.row_unit;
-  r_begin = static_cast<uint32_t>(units * blockIdx.x / gridDim.x) * a.row_unit;
-  r_end = static_cast<uint32_t>(units * (blockIdx.x + 1) / gridDim.x) * a.row_unit;
+__device__ __forceinline__ void cta_rows(const JobArgs& v, uint32_t& r_begin, uint32_t& r_end) {
+  const uint64_t units = v.rows / v.row_unit;
+  r_begin = static_cast<uint32_t>(units * blockIdx.x / gridDim.x) * v.row_unit;
+  r_end = static_cast<uint32_t>(units * (blockIdx.x + 1) / gridDim.x) * v.row_unit;
+}
+
+// A lone launch's per-matvec fields.
+__device__ __forceinline__ JobArgs job_of(const WarpMmaArgs& a) {
+  return JobArgs{a.W, a.x, a.y, a.total_bytes, a.rows, a.row_unit, a.prologue, a.epilogue, a.eps,
+                 a.pair_scale};
 }
 
 // The 128-byte aligned start of the dynamic shared memory.
@@ -580,8 +598,9 @@ __device__ __forceinline__ void init_ring(const WarpMmaArgs& a, uint8_t* base, W
 // of a launch to the next; issued: the tiles this warp issued before in the launch (the first
 // `ring` of them need no free slot). Returns false once a wait gave up.
 template <int QT>
-__device__ __forceinline__ bool produce_job(const WarpMmaArgs& a, uint8_t* base, WarpMmaShared& sh,
-                                            uint32_t& s, uint32_t& phase, uint32_t& issued) {
+__device__ __forceinline__ bool produce_job(const WarpMmaArgs& a, const JobArgs& v, uint8_t* base,
+                                            WarpMmaShared& sh, uint32_t& s, uint32_t& phase,
+                                            uint32_t& issued) {
   constexpr uint32_t kBlk = QT == 4 ? kQ4KBytes : QT == 5 ? kQ5KBytes : kQ6KBytes;
   int& s_failed = sh.failed;
   const uint32_t ring_s = smem_u32(base);
@@ -591,11 +610,11 @@ __device__ __forceinline__ bool produce_job(const WarpMmaArgs& a, uint8_t* base,
   const uint32_t lane = threadIdx.x & 31;
   const uint64_t RB = a.row_bytes;
   uint32_t r_begin, r_end;
-  cta_rows(a, r_begin, r_end);
+  cta_rows(v, r_begin, r_end);
   const uint32_t nbands = (r_end - r_begin + kTileRows - 1) / kTileRows;
   const uint32_t ntiles = nbands * a.nkt;
   const uint64_t pol = policy_evict_first();
-  const uint64_t end_floor = a.total_bytes & ~uint64_t(15);
+  const uint64_t end_floor = v.total_bytes & ~uint64_t(15);
   for (uint32_t t = 0; t < ntiles; ++t) {
     if (issued >= a.ring) {
       int ok = 1;
@@ -625,9 +644,9 @@ __device__ __forceinline__ bool produce_job(const WarpMmaArgs& a, uint8_t* base,
         a0 = (uint64_t(r0) * RB) & ~uint64_t(15);
         a1 = (uint64_t(r1) * RB + 15) & ~uint64_t(15);
         if (a1 > end_floor) {
-          for (uint64_t i = end_floor; i < a.total_bytes; i += 2)
+          for (uint64_t i = end_floor; i < v.total_bytes; i += 2)
             sts_u16(slot + static_cast<uint32_t>(i - a0),
-                    __ldg(reinterpret_cast<const unsigned short*>(a.W + i)));
+                    __ldg(reinterpret_cast<const unsigned short*>(v.W + i)));
           a1 = end_floor;
         }
         if (a1 < a0) a1 = a0;
@@ -641,9 +660,9 @@ __device__ __forceinline__ bool produce_job(const WarpMmaArgs& a, uint8_t* base,
         // the end of W is off a 16-byte boundary: its last bytes (an even count, < 16) are
         // read with plain loads
         const uint32_t dst = slot + lane * a.seg_bytes;
-        for (uint64_t i = end_floor; i < a.total_bytes; i += 2)
+        for (uint64_t i = end_floor; i < v.total_bytes; i += 2)
           sts_u16(dst + static_cast<uint32_t>(i - a0),
-                  __ldg(reinterpret_cast<const unsigned short*>(a.W + i)));
+                  __ldg(reinterpret_cast<const unsigned short*>(v.W + i)));
         a1 = end_floor;
       }
       if (a1 < a0) a1 = a0;
@@ -659,12 +678,12 @@ __device__ __forceinline__ bool produce_job(const WarpMmaArgs& a, uint8_t* base,
       // (rows are whole and start on 16-byte boundaries here, so a1 - a0 = (r1 - r0) * RB)
       if (lane == 0 && bytes) {
         const uint32_t first = static_cast<uint32_t>(std::min<uint64_t>(bytes, 8 * RB));
-        bulk_g2s(slot, a.W + a0, first, full_bar(s), pol);
+        bulk_g2s(slot, v.W + a0, first, full_bar(s), pol);
         if (bytes > first)
-          bulk_g2s(slot + first + kSplitGap, a.W + a0 + first, bytes - first, full_bar(s), pol);
+          bulk_g2s(slot + first + kSplitGap, v.W + a0 + first, bytes - first, full_bar(s), pol);
       }
     } else if (bytes) {
-      bulk_g2s(slot + lane * a.seg_bytes, a.W + a0, bytes, full_bar(s), pol);
+      bulk_g2s(slot + lane * a.seg_bytes, v.W + a0, bytes, full_bar(s), pol);
     }
     // (whole-row tiles: only lane 0 has bytes, and its destination is the slot itself)
     ++issued;
@@ -681,9 +700,9 @@ __device__ __forceinline__ bool produce_job(const WarpMmaArgs& a, uint8_t* base,
 // position, carried from one matvec of a launch to the next. sync: null for a lone matvec; for a
 // job of a chain, where its outputs are also pushed.
 template <int QT, int NT, bool HILO, bool I8>
-__device__ __forceinline__ void consume_job(const WarpMmaArgs& a, const ChainSync* sync,
-                                            uint8_t* base, WarpMmaShared& sh, uint32_t& s,
-                                            uint32_t& phase) {
+__device__ __forceinline__ void consume_job(const WarpMmaArgs& a, const JobArgs& mj,
+                                            const ChainSync* sync, uint8_t* base,
+                                            WarpMmaShared& sh, uint32_t& s, uint32_t& phase) {
   constexpr uint32_t kBlk = QT == 4 ? kQ4KBytes : QT == 5 ? kQ5KBytes : kQ6KBytes;
   constexpr int kTarget = QT == 4 ? 10 : 14;  // x is scaled so that max |x| < 2^kTarget
   int& s_failed = sh.failed;
@@ -704,7 +723,7 @@ __device__ __forceinline__ void consume_job(const WarpMmaArgs& a, const ChainSyn
   const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const uint64_t RB = a.row_bytes;
   uint32_t r_begin, r_end;
-  cta_rows(a, r_begin, r_end);
+  cta_rows(mj, r_begin, r_end);
   const uint32_t nbands = (r_end - r_begin + kTileRows - 1) / kTileRows;
 
   const uint32_t tid = threadIdx.x;  // 0 .. nthr-1
@@ -732,7 +751,7 @@ __device__ __forceinline__ void consume_job(const WarpMmaArgs& a, const ChainSyn
         const uint32_t xb = xb0 + j * nw;
         if (xb < nxb) {
           const uint32_t b = xb / a.nb, kb = xb - b * a.nb;
-          const float* src = a.x + b * a.ldx + kb * kQK + lane;
+          const float* src = mj.x + b * a.ldx + kb * kQK + lane;
 #pragma unroll
           for (int r = 0; r < 8; ++r) v[j][r] = __ldcg(src + 32 * r);
         }
@@ -748,7 +767,7 @@ __device__ __forceinline__ void consume_job(const WarpMmaArgs& a, const ChainSyn
         for (int r = 0; r < 8; ++r) mx = fmaxf(mx, fabsf(v[j][r]));
 #pragma unroll
         for (int o = 16; o; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-        if (a.prologue == KQ_PROLOGUE_RMSNORM) {
+        if (mj.prologue == KQ_PROLOGUE_RMSNORM) {
 #pragma unroll
           for (int r = 0; r < 8; ++r)
             sq = fma(static_cast<double>(v[j][r]), static_cast<double>(v[j][r]), sq);
@@ -906,11 +925,11 @@ __device__ __forceinline__ void consume_job(const WarpMmaArgs& a, const ChainSyn
     named_barrier(1, nthr);
     if (tid < B) {
       float ns = 1.f;
-      if (a.prologue == KQ_PROLOGUE_RMSNORM) {
+      if (mj.prologue == KQ_PROLOGUE_RMSNORM) {
         double t = 0.0;
         for (uint32_t w = 0; w < nw; ++w) t += s_sq[w][tid];
         ns = static_cast<float>(
-            1.0 / sqrt(t / (static_cast<double>(a.nb) * kQK) + static_cast<double>(a.eps)));
+            1.0 / sqrt(t / (static_cast<double>(a.nb) * kQK) + static_cast<double>(mj.eps)));
       }
       s_ns[tid] = ns;  // read at the flushes, which start with a barrier
     }
@@ -1090,7 +1109,7 @@ __device__ __forceinline__ void consume_job(const WarpMmaArgs& a, const ChainSyn
       // Flush: sum every warp's partial of each row in a fixed order and write y.
       named_barrier(1, nthr);
       const uint32_t band0 = band - bi;
-      const uint32_t R = a.row_unit;
+      const uint32_t R = mj.row_unit;
       const uint32_t nout = (bi + 1) * (kTileRows / R) * B;
       for (uint32_t o = tid; o < nout; o += nthr) {
         const uint32_t b = o % B;
@@ -1109,10 +1128,10 @@ __device__ __forceinline__ void consume_job(const WarpMmaArgs& a, const ChainSyn
           const float* rq = rp + nw * B;
           for (uint32_t w = 0; w < nw; ++w) v1 += rq[w * B];
           v1 *= s_ns[b];
-          v0 = pair_value(v0, v1, a.epilogue, a.pair_scale);
+          v0 = pair_value(v0, v1, mj.epilogue, mj.pair_scale);
           out = row / 2;
         }
-        a.y[b * a.ldy + out] = v0;
+        mj.y[b * a.ldy + out] = v0;
         // a chain job's pushed outputs also go to every rank's full vector (batch 1)
         if (sync && out < sync->push_rows)
           for (uint32_t rk = 0; rk < sync->npush; ++rk) sync->push_y[rk][out] = v0;
@@ -1375,14 +1394,15 @@ __global__ void __launch_bounds__((kMaxWarps + 1) * 32, 1) warpmma_kernel(const 
   init_ring(a, base, sh);
   pdl_launch_dependents();
   uint32_t s = 0, phase = 0;
+  const JobArgs v = job_of(a);
   if ((threadIdx.x >> 5) == a.nw) {
     if (!(a.flags & KQ_FLAG_WEIGHTS_STATIC)) pdl_wait();
     uint32_t issued = 0;
-    produce_job<QT>(a, base, sh, s, phase, issued);
+    produce_job<QT>(a, v, base, sh, s, phase, issued);
     return;
   }
   pdl_wait();  // x may be the previous kernel's output
-  consume_job<QT, NT, HILO, I8>(a, nullptr, base, sh, s, phase);
+  consume_job<QT, NT, HILO, I8>(a, v, nullptr, base, sh, s, phase);
 }
 
 // Bounded wait (acquire, system scope) by one thread until *cnt >= target; on giving up it
@@ -1421,25 +1441,27 @@ __global__ void __launch_bounds__((kMaxWarps + 1) * 32, 1)
   extern __shared__ __align__(128) uint8_t smem[];
   __shared__ WarpMmaShared sh;
   uint8_t* base = smem_base(smem);
-  const WarpMmaArgs& a0 = p.job[0];
-  init_ring(a0, base, sh);
+  // the layout (ring, tiles, shared-memory regions) is the same for every job: its fields are read
+  // at fixed parameter offsets, as a lone launch reads them; only each job's own fields vary
+  const WarpMmaArgs& a = p.lay;
+  init_ring(a, base, sh);
   pdl_launch_dependents();
-  const uint32_t nw = a0.nw, nthr = nw * 32;
+  const uint32_t nw = a.nw, nthr = nw * 32;
   uint32_t s = 0, phase = 0;
   if ((threadIdx.x >> 5) == nw) {
-    if (!(a0.flags & KQ_FLAG_WEIGHTS_STATIC)) pdl_wait();
+    if (!(a.flags & KQ_FLAG_WEIGHTS_STATIC)) pdl_wait();
     uint32_t issued = 0;
     bool ok = true;
-    for (uint32_t j = 0; j < p.njobs && ok; ++j) ok = produce_job<QT>(p.job[j], base, sh, s, phase, issued);
+    for (uint32_t j = 0; j < p.njobs && ok; ++j) ok = produce_job<QT>(a, p.job[j], base, sh, s, phase, issued);
     if (!ok && (threadIdx.x & 31) == 0) {
       // a wait gave up: before the CTA ends, let the copies still in flight into its ring land
       // (each slot's last phase; bounded like every wait)
-      const uint32_t n = min(issued, a0.ring);
-      uint64_t* bars = reinterpret_cast<uint64_t*>(base + a0.bars_off);
+      const uint32_t n = min(issued, a.ring);
+      uint64_t* bars = reinterpret_cast<uint64_t*>(base + a.bars_off);
       uint32_t ss = s, ph = phase;
       for (uint32_t i = 0; i < n; ++i) {
         if (ss == 0) {
-          ss = a0.ring;
+          ss = a.ring;
           ph ^= 1;
         }
         --ss;
@@ -1449,22 +1471,22 @@ __global__ void __launch_bounds__((kMaxWarps + 1) * 32, 1)
     return;
   }
   pdl_wait();  // the first job's x may be the previous kernel's output
-  unsigned long long epoch = 0;
-  if (threadIdx.x == 0) epoch = ld_acquire_sys(p.epoch);
+  __shared__ unsigned long long s_epoch;  // (kept out of registers: the tile loops need them all)
+  if (threadIdx.x == 0) s_epoch = ld_acquire_sys(p.epoch);
   for (uint32_t j = 0; j < p.njobs; ++j) {
-    const WarpMmaArgs& a = p.job[j];
+    const JobArgs& v = p.job[j];
     const ChainSync& y = p.sync[j];
     if (y.wait_cnt) {
-      if (threadIdx.x == 0 && !wait_at_least(a.err, y.wait_cnt, epoch * y.wait_target, &sh.failed))
+      if (threadIdx.x == 0 && !wait_at_least(a.err, y.wait_cnt, s_epoch * y.wait_target, &sh.failed))
         sh.failed = 1;
       named_barrier(1, nthr);
     }
-    consume_job<QT, 1, false, true>(a, &y, base, sh, s, phase);
+    consume_job<QT, 1, false, true>(a, v, &y, base, sh, s, phase);
     named_barrier(1, nthr);  // every consumer's outputs of job j are stored
     if (threadIdx.x == 0 && y.counter[0]) {
       uint32_t r_begin, r_end;
-      cta_rows(a, r_begin, r_end);
-      const uint32_t o0 = r_begin / a.row_unit, o1 = r_end / a.row_unit;
+      cta_rows(v, r_begin, r_end);
+      const uint32_t o0 = r_begin / v.row_unit, o1 = r_end / v.row_unit;
       if (y.npush) {
         const uint32_t pushed = o1 > y.push_rows ? (o0 < y.push_rows ? y.push_rows - o0 : 0u) : o1 - o0;
         __threadfence_system();
@@ -1775,9 +1797,13 @@ int warpmma_chain(kq_ctx* ctx, const kq_chain_job* jobs, uint32_t njobs, uint64_
     if (rc) return rc;
     if (plan.mode != (d.type == KQ_TYPE_Q4_K ? 4 : d.type == KQ_TYPE_Q5_K ? 6 : 5))
       return fail(KQ_E_UNSUPPORTED, call, at + "k " + std::to_string(d.k) + " does not fit the integer kernel");
-    if (j && !same_layout(p.job[0], plan.args))
+    if (j == 0)
+      p.lay = plan.args;
+    else if (!same_layout(p.lay, plan.args))
       return fail(KQ_E_UNSUPPORTED, call, at + "its tiles differ from the first job's");
-    p.job[j] = plan.args;
+    const WarpMmaArgs& g = plan.args;
+    p.job[j] = JobArgs{g.W, g.x, g.y, g.total_bytes, g.rows, g.row_unit, g.prologue, g.epilogue,
+                       g.eps, g.pair_scale};
     smem = plan.smem;
     block = plan.block;
     ChainSync& y = p.sync[j];

@@ -501,9 +501,10 @@ def make_cuda_stack(cfg: StackConfig, kernels, rank: int = 0, world: int = 1, gr
 
 # ---------------------------------------------------------------- reference (for tests)
 
-def reference_logits(cfg: StackConfig, x, layers: int | None = None):
-    """The unsharded stack on the CPU oracle, in f64 from the f32-dequantised weights. Test
-    infrastructure only."""
+def reference_logits(cfg: StackConfig, x, layers: int | None = None, with_bound: bool = False):
+    """The unsharded stack on the CPU oracle, in f64 from the f32-dequantised weights; with
+    `with_bound` also sum_k |w_head[r, k] x_k| per logit (x the normalised head input), the scale
+    of the 1e-3 tolerance. Test and bench-check infrastructure only."""
     import numpy as np
 
     import oracle
@@ -512,9 +513,9 @@ def reference_logits(cfg: StackConfig, x, layers: int | None = None):
         return oracle.fill(qtype, oracle.stream_key(cfg.seed, cfg.tensor_id(layer, name)), 0,
                            rows * k // QK)
 
-    def mv(qtype, W, v, rows, k):
-        y, _ = oracle.matvec_ref(qtype, W, np.asarray(v, dtype=np.float32)[None, :], k, 0, rows)
-        return y[0]
+    def mv(qtype, W, v, rows, k, bound=False):
+        y, b = oracle.matvec_ref(qtype, W, np.asarray(v, dtype=np.float32)[None, :], k, 0, rows)
+        return (y[0], b[0]) if bound else y[0]
 
     def norm(v):
         v = np.asarray(v, dtype=np.float64)
@@ -533,4 +534,5 @@ def reference_logits(cfg: StackConfig, x, layers: int | None = None):
         x = mv(6, weights("down", layer, 6, h, f), a, h, f)
     head = oracle.fill(6, oracle.stream_key(cfg.seed, cfg.tensor_id(cfg.layers, "head")), 0,
                        cfg.vocab * h // QK)
-    return mv(6, head, norm(x), cfg.vocab, h)
+    logits, bound = mv(6, head, norm(x), cfg.vocab, h, bound=True)
+    return (logits, bound) if with_bound else logits

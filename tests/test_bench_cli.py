@@ -37,3 +37,22 @@ def test_reference_arm_other_ranks_are_silent():
     out = run(["--impl", "reference", "--workload", "q4k", "--steps", "3", "--warmup", "3"],
               env={"RANK": "1", "LOCAL_RANK": "1", "WORLD_SIZE": "2"})
     assert out.strip() == ""
+
+
+def test_stack_reference_arm_has_the_gpu_arms_config():
+    out = run(["--impl", "reference", "--steps", "3", "--warmup", "3"])  # the default workload
+    d = json.loads([ln for ln in out.splitlines() if ln.strip()][0])
+    assert d["metric"] == "decode tokens/s" and d["unit"] == "tokens/s" and d["value"] > 0
+    assert d["config"]["workload"].startswith("stack70b")
+    import bench
+    from kernite_b200 import stack as st
+
+    args = bench.parse_args(["--steps", "3"])
+    assert d["config"] == bench.stack_config(args, st.CONFIGS["70b"], 1, True)
+    assert "l2" in d["config"] and d["cpu_baseline"]["cores"] >= 1
+
+
+def test_matvec_reference_arm_config_has_the_l2_rotation():
+    out = run(["--impl", "reference", "--workload", "q6k_head", "--steps", "3", "--warmup", "3"])
+    d = json.loads([ln for ln in out.splitlines() if ln.strip()][0])
+    assert "l2" in d["config"] and "copies" in d["config"]["l2"]

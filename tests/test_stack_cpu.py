@@ -130,3 +130,83 @@ def test_push_layout_and_targets():
     mul, add = st.push_target(cfg, "q", 3)
     assert mul == cfg.layers * cfg.hidden and add == 3 * cfg.hidden
     assert st.push_target(cfg, "logits", 1) == (cfg.vocab, cfg.vocab)
+
+
+# ---------------------------------------------------------------- chains (host logic)
+
+ALIAS_ONE_RANK = {"q": "qkv", "o": "o_loc", "a": "a_loc", "xd": "x_loc", "logits": "l_loc"}
+
+
+def _simulate_chain(cfg, world, tokens=3):
+    """Runs the token's chain jobs on `world` simulated ranks, job after job, tagging every
+    element each job stores (local output, pushes into every rank's full vectors) and adding to
+    the counters as the kernel does; before a job reads x on a rank, its wait must already be
+    met and every element of x must hold this token's output of the job it waits for."""
+    plans = [st.chain_plan(cfg, r, world) for r in range(world)]
+    jobs0, launches = plans[0]
+    sizes = st.full_sizes(cfg)
+    for r in range(world):
+        assert [(j.name, j.layer, j.counter, j.wait, j.wait_target) for j in plans[r][0]] == \
+               [(j.name, j.layer, j.counter, j.wait, j.wait_target) for j in jobs0]
+    counters = [np.zeros(len(jobs0), dtype=np.int64) for _ in range(world)]
+    full = [{k: np.full(n, -1, dtype=np.int64) for k, n in sizes.items()} for _ in range(world)]
+    local = [{} for _ in range(world)]
+    for t in range(1, tokens + 1):
+        tag = lambda i: t * 100000 + i
+        for r in range(world):
+            full[r]["x"] = np.full(cfg.hidden, tag(-1))  # the token's input, on every rank
+        for i, j0 in enumerate(jobs0):
+            for r in range(world):
+                j = plans[r][0][i]
+                if j.wait is not None:
+                    assert counters[r][j.wait] >= t * j.wait_target, (t, j.name, j.layer, r)
+                    want = tag(j.wait)
+                else:
+                    want = tag(-1)
+                if world == 1 and j.x in ALIAS_ONE_RANK:
+                    src = local[r][ALIAS_ONE_RANK[j.x]][: sizes[j.x]]
+                else:
+                    src = full[r][j.x]
+                assert src.size >= j.k and (src[: j.k] == want).all(), (t, j.name, j.layer, r)
+            for r in range(world):
+                j = plans[r][0][i]
+                local[r][j.y] = np.full(j.outputs, tag(i))
+                if world == 1:
+                    counters[r][j.counter] += j.outputs
+                else:
+                    assert j.push_rows <= j.outputs
+                    for p in range(world):
+                        dst = full[p][j.push][r * j.push_rows:(r + 1) * j.push_rows]
+                        assert dst.size == j.push_rows
+                        dst[:] = tag(i)
+                        counters[p][j.counter] += j.push_rows
+        head = len(jobs0) - 1
+        for r in range(world):
+            logits = local[r]["l_loc"] if world == 1 else full[r]["logits"]
+            assert (logits == tag(head)).all()
+    return jobs0, launches
+
+
+@pytest.mark.parametrize("name,world", [("tiny", 1), ("tiny", 2), ("tiny", 4), ("7b", 1), ("7b", 2),
+                                        ("7b", 8), ("70b", 1), ("70b", 8)])
+def test_chain_plan_orders_every_read_after_its_writes(name, world):
+    cfg = st.CONFIGS[name]
+    if name != "tiny":
+        cfg = __import__("dataclasses").replace(cfg, layers=3)
+    jobs, launches = _simulate_chain(cfg, world)
+    assert sorted(i for l in launches for i in l) == list(range(len(jobs)))
+    for l in launches:
+        assert 1 <= len(l) <= 8 and l == list(range(l[0], l[0] + len(l)))
+        assert len({(jobs[i].qtype, jobs[i].k) for i in l}) == 1
+    # per layer: q|k|v, o, gate|up in one launch, down in another; then the head
+    assert [len(l) for l in launches] == [3, 1] * cfg.layers + [1]
+
+
+def test_chain_layout_fits_counters_and_vectors():
+    for name, cfg in st.CONFIGS.items():
+        n = len(st.chain_plan(cfg, 0, 1)[0])
+        off, total = st.chain_layout(cfg, n)
+        assert off["counters"] == 8 and off["epoch"] == 0
+        ends = sorted((off[k], off[k] + 4 * v) for k, v in st.full_sizes(cfg).items())
+        assert ends[0][0] >= 8 + 8 * n and all(a % 256 == 0 for a, _ in ends)
+        assert all(ends[i][1] <= ends[i + 1][0] for i in range(len(ends) - 1)) and ends[-1][1] <= total
