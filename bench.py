@@ -79,9 +79,10 @@ def parse_args(argv=None):
                     help="more descriptor flag bits OR-ed into every timed launch (A/B tests)")
     ap.add_argument("--impl", default="kq", choices=["kq", "reference"])
     ap.add_argument("--exchange", default="chain", choices=["nccl", "push", "chain"],
-                    help="stacks: NCCL all-gathers after one launch per projection, the CUDA-core "
-                         "matvec's own push to peer memory, or chains of the warp-MMA kernel (up to "
-                         "three projections a launch, outputs pushed to peer memory at N > 1)")
+                    help="stacks: NCCL all-gathers after one launch per projection, the warp-MMA "
+                         "matvec's own push to peer memory (one launch per projection), or chains of "
+                         "the warp-MMA kernel (up to three projections a launch, outputs pushed to "
+                         "peer memory at N > 1)")
     ap.add_argument("--e2e-steps", type=int, default=2000, help="steps of the end-to-end leg")
     ap.add_argument("--cpu-seconds", type=float, default=12.0, help="CPU-baseline time budget")
     ap.add_argument("--no-cpu-baseline", action="store_true")

@@ -232,9 +232,11 @@ int kq_gguf_meta_str(const kq_gguf* g, const char* key, const char** out);
  * ranks, this one included, mapped with kq_peer_open), and each CTA, once its rows are stored
  * everywhere, adds its row count to counter[p] with a system-scope fence before it. A launch
  * whose x is such a full vector first waits (bounded, acquire) until its rank's counter
- * wait_counter reaches (*epoch - 1) * wait_mul + wait_add, then reads x through L2. Batch 1,
- * CUDA-core kernel. No reference counterpart: kernite has no collective; its only inter-GPU
- * operation is Buffer::copy_from over cuMemcpyPeer (crates/cuda/src/lib.rs:405-439). */
+ * wait_counter reaches (*epoch - 1) * wait_mul + wait_add, then reads x through L2. Batch 1:
+ * the warp-MMA integer kernel (Q4_K, Q5_K, Q6_K; the weights streaming while the wait runs), or
+ * the CUDA-core kernel with KQ_FLAG_CUDA_CORES (Q4_K, Q6_K). No reference counterpart: kernite
+ * has no collective; its only inter-GPU operation is Buffer::copy_from over cuMemcpyPeer
+ * (crates/cuda/src/lib.rs:405-439). */
 typedef struct kq_push_desc {
     uint32_t npush;        /* ranks to store to (0..8) */
     uint32_t push_rows;    /* output rows (in output units) that are pushed: rows [0, push_rows) */

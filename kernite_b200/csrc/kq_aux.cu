@@ -212,16 +212,33 @@ __global__ void wait_counter_kernel(unsigned* err, const unsigned long long* cnt
   wait_count(err, cnt, epoch, mul, add);
 }
 
-__global__ void epoch_advance_kernel(unsigned long long* epoch) { *epoch += 1ull; }
+// *epoch += 1 once the kernels before it on the stream are done (a chain of the previous step may
+// still read the old value as its CTAs start), launched with programmatic dependent launch so
+// that it waits on the device instead of breaking the chains' overlap with a launch gap.
+__global__ void epoch_advance_kernel(unsigned long long* epoch) {
+  pdl_wait();
+  *epoch += 1ull;
+  __threadfence();
+  pdl_launch_dependents();
+}
 
 int aux_prepare(kq_ctx*) { return KQ_OK; }
 
 int epoch_advance(kq_ctx*, uint64_t epoch, cudaStream_t s) {
   if (!epoch || epoch % 8)
     return fail(KQ_E_INVALID, "kq_epoch_advance", "epoch must be a non-null 8-byte aligned address");
-  epoch_advance_kernel<<<1, 1, 0, s>>>(reinterpret_cast<unsigned long long*>(epoch));
-  const cudaError_t e = cudaGetLastError();
-  if (e != cudaSuccess) return cuda_fail(e, "cudaLaunchKernel", "kq_epoch_advance");
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(1);
+  cfg.blockDim = dim3(1);
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  const cudaError_t e =
+      cudaLaunchKernelEx(&cfg, epoch_advance_kernel, reinterpret_cast<unsigned long long*>(epoch));
+  if (e != cudaSuccess) return cuda_fail(e, "cudaLaunchKernelEx", "kq_epoch_advance");
   return KQ_OK;
 }
 

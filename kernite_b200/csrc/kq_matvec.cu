@@ -660,7 +660,8 @@ int matvec(kq_ctx* ctx, const kq_matvec_desc& d, cudaStream_t stream, const kq_p
   // Path: the tensor cores above batch 8 (and when asked), the CUDA cores otherwise.
   if (push) {
     if (d.batch != 1 || (d.flags & KQ_FLAG_TENSOR_CORES))
-      return fail(KQ_E_INVALID, call, "the push exchange serves batch 1 on the CUDA-core kernel");
+      return fail(KQ_E_INVALID, call,
+                  "the push exchange serves batch 1 on the warp-MMA or CUDA-core kernel");
     if (push->npush > 8) return fail(KQ_E_INVALID, call, "npush must be 0..8");
     for (uint32_t p = 0; p < push->npush; ++p)
       if (!push->y[p] || !push->counter[p] || push->y[p] % 4 || push->counter[p] % 8)
@@ -668,6 +669,8 @@ int matvec(kq_ctx* ctx, const kq_matvec_desc& d, cudaStream_t stream, const kq_p
     if (push->wait_counter && (!push->epoch || push->wait_counter % 8 || push->epoch % 8))
       return fail(KQ_E_INVALID, call, "wait_counter needs an 8-byte aligned epoch and counter");
   }
+  // The push exchange: the warp-MMA kernel's integer path unless the CUDA cores are asked for.
+  if (push && !(d.flags & KQ_FLAG_CUDA_CORES)) return warpmma_push(ctx, d, *push, ldx, ldy, stream);
   if (qt == 5) {  // Q5_K: the warp-MMA kernel's integer path only
     if (push || d.batch != 1 || (d.flags & (KQ_FLAG_TENSOR_CORES | KQ_FLAG_CUDA_CORES)))
       return fail(KQ_E_UNSUPPORTED, call, "Q5_K is served at batch 1 by the warp-MMA kernel");

@@ -147,6 +147,15 @@ struct ChainParams {
   ChainSync sync[kChainMaxJobs];
 };
 
+// A lone matvec of a row-sharded stack (kq_matvec_push on the warp-MMA kernel): the push of its
+// outputs to every rank and the counters, as a chain job has them, and its wait, whose target is
+// (*epoch - 1) * wait_mul + wait_add.
+struct PushArgs {
+  ChainSync y;
+  const unsigned long long* epoch;
+  uint64_t wait_mul, wait_add;
+};
+
 // The parts of shared memory that are not in the dynamic layout.
 struct WarpMmaShared {
   int failed;
@@ -702,7 +711,8 @@ __device__ __forceinline__ bool produce_job(const WarpMmaArgs& a, const JobArgs&
 template <int QT, int NT, bool HILO, bool I8>
 __device__ __forceinline__ void consume_job(const WarpMmaArgs& a, const JobArgs& mj,
                                             const ChainSync* sync, uint8_t* base,
-                                            WarpMmaShared& sh, uint32_t& s, uint32_t& phase) {
+                                            WarpMmaShared& sh, uint32_t& s, uint32_t& phase,
+                                            uint32_t opq = 0) {
   constexpr uint32_t kBlk = QT == 4 ? kQ4KBytes : QT == 5 ? kQ5KBytes : kQ6KBytes;
   constexpr int kTarget = QT == 4 ? 10 : 14;  // x is scaled so that max |x| < 2^kTarget
   int& s_failed = sh.failed;
@@ -720,13 +730,16 @@ __device__ __forceinline__ void consume_job(const WarpMmaArgs& a, const JobArgs&
 
   const uint32_t nw = a.nw;
   const uint32_t nthr = nw * 32;
-  const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  // opq: 0, read anew for each job of a chain, so that nothing derived from the thread index is
+  // hoisted out of the chain's job loop (held in registers through the x prologue)
+  const uint32_t tx = threadIdx.x + opq;
+  const uint32_t warp = tx >> 5, lane = tx & 31;
   const uint64_t RB = a.row_bytes;
   uint32_t r_begin, r_end;
   cta_rows(mj, r_begin, r_end);
   const uint32_t nbands = (r_end - r_begin + kTileRows - 1) / kTileRows;
 
-  const uint32_t tid = threadIdx.x;  // 0 .. nthr-1
+  const uint32_t tid = tx;  // 0 .. nthr-1
   const uint32_t g = lane >> 2, c = lane & 3;
   const uint32_t B = a.batch;
 
@@ -1405,22 +1418,82 @@ __global__ void __launch_bounds__((kMaxWarps + 1) * 32, 1) warpmma_kernel(const 
   consume_job<QT, NT, HILO, I8>(a, v, nullptr, base, sh, s, phase);
 }
 
-// Bounded wait (acquire, system scope) by one thread until *cnt >= target; on giving up it
-// records kErrWaitPeer and returns false (at once when the CTA already failed).
+__device__ __forceinline__ unsigned long long ld_acquire_gpu(const unsigned long long* p) {
+  unsigned long long v;
+  asm volatile("ld.acquire.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+
+// Adds n to *cnt with release semantics: every store this CTA made before (ordered by the barrier
+// its consumers met first) is visible, at the scope, before the count is.
+__device__ __forceinline__ void red_release_gpu(unsigned long long* cnt, uint32_t n) {
+  asm volatile("red.release.gpu.global.add.u64 [%0], %1;" ::"l"(cnt), "l"(static_cast<unsigned long long>(n))
+               : "memory");
+}
+__device__ __forceinline__ void red_release_sys(unsigned long long* cnt, uint32_t n) {
+  asm volatile("red.release.sys.global.add.u64 [%0], %1;" ::"l"(cnt), "l"(static_cast<unsigned long long>(n))
+               : "memory");
+}
+
+// Bounded wait (acquire; system scope when other GPUs add to the counter, else GPU scope) by one
+// thread until *cnt >= target; on giving up it records kErrWaitPeer and returns false (at once
+// when the CTA or an earlier wait already failed).
 __device__ __forceinline__ bool wait_at_least(unsigned* err, const unsigned long long* cnt,
-                                              unsigned long long target, const int* failed) {
-  if (ld_acquire_sys(cnt) >= target) return true;
+                                              unsigned long long target, bool sys, const int* failed) {
+  auto load = [&]() { return sys ? ld_acquire_sys(cnt) : ld_acquire_gpu(cnt); };
+  if (load() >= target) return true;
   if (*reinterpret_cast<const volatile int*>(failed) || (err && *reinterpret_cast<volatile unsigned*>(err)))
     return false;
   const uint64_t t0 = globaltimer();
-  while (ld_acquire_sys(cnt) < target) {
+  while (load() < target) {
     if (globaltimer() - t0 > kWaitBudgetNs) {
       report_error(err, kErrWaitPeer);
       return false;
     }
-    __nanosleep(32);
   }
   return true;
+}
+
+// A lone batch-1 integer matvec that also does a row-sharded stack's exchange: before its
+// consumers read x (a full vector other GPUs push into), one thread waits (bounded, acquire,
+// system scope) until this rank's counter for x reaches this step's target; its flushes store the
+// outputs below push_rows into every rank's full vector; once they are stored, the CTA adds their
+// count to every rank's counter (release, system scope). The producer streams the weights from
+// the start, the wait overlapping the first tiles' copies.
+template <int QT>
+__global__ void __launch_bounds__((kMaxWarps + 1) * 32, 1)
+    warpmma_push_kernel(const WarpMmaArgs a, const __grid_constant__ PushArgs q) {
+  extern __shared__ __align__(128) uint8_t smem[];
+  __shared__ WarpMmaShared sh;
+  uint8_t* base = smem_base(smem);
+  init_ring(a, base, sh);
+  pdl_launch_dependents();
+  uint32_t s = 0, phase = 0;
+  const JobArgs v = job_of(a);
+  if ((threadIdx.x >> 5) == a.nw) {
+    if (!(a.flags & KQ_FLAG_WEIGHTS_STATIC)) pdl_wait();
+    uint32_t issued = 0;
+    produce_job<QT>(a, v, base, sh, s, phase, issued);
+    return;
+  }
+  pdl_wait();
+  const uint32_t nthr = a.nw * 32;
+  if (q.y.wait_cnt) {
+    if (threadIdx.x == 0) {
+      const unsigned long long target = (ld_acquire_sys(q.epoch) - 1ull) * q.wait_mul + q.wait_add;
+      if (!wait_at_least(a.err, q.y.wait_cnt, target, true, &sh.failed)) sh.failed = 1;
+    }
+    named_barrier(1, nthr);
+  }
+  consume_job<QT, 1, false, true>(a, v, &q.y, base, sh, s, phase);
+  named_barrier(1, nthr);  // every consumer's outputs are stored
+  if (threadIdx.x == 0 && q.y.npush) {
+    uint32_t r_begin, r_end;
+    cta_rows(v, r_begin, r_end);
+    const uint32_t o0 = r_begin / v.row_unit, o1 = r_end / v.row_unit, pr = q.y.push_rows;
+    const uint32_t pushed = o1 > pr ? (o0 < pr ? pr - o0 : 0u) : o1 - o0;
+    for (uint32_t rk = 0; rk < q.y.npush; ++rk) red_release_sys(q.y.counter[rk], pushed);
+  }
 }
 
 // A chain: the batch-1 integer matvecs p.job[0..njobs) of one type and k in one launch, each
@@ -1471,29 +1544,48 @@ __global__ void __launch_bounds__((kMaxWarps + 1) * 32, 1)
     return;
   }
   pdl_wait();  // the first job's x may be the previous kernel's output
-  __shared__ unsigned long long s_epoch;  // (kept out of registers: the tile loops need them all)
-  if (threadIdx.x == 0) s_epoch = ld_acquire_sys(p.epoch);
+  // The current job's own fields live in shared memory: the tile loops then hold no register for
+  // them (they are read where used, at the prologue and the flushes), as a lone launch reads its
+  // fields from the parameter bank.
+  __shared__ JobArgs s_job;
+  __shared__ ChainSync s_sync;
+  __shared__ unsigned long long s_epoch;
+  __shared__ uint32_t s_zero;
+  if (threadIdx.x == 0) {
+    s_epoch = p.sync[0].wait_cnt || p.njobs > 1 ? ld_acquire_sys(p.epoch) : 0ull;
+    s_zero = 0;
+  }
   for (uint32_t j = 0; j < p.njobs; ++j) {
-    const JobArgs& v = p.job[j];
-    const ChainSync& y = p.sync[j];
-    if (y.wait_cnt) {
-      if (threadIdx.x == 0 && !wait_at_least(a.err, y.wait_cnt, s_epoch * y.wait_target, &sh.failed))
-        sh.failed = 1;
-      named_barrier(1, nthr);
+    // the job's fields into shared memory, a word per consumer thread
+    static_assert(sizeof(JobArgs) % 4 == 0 && sizeof(ChainSync) % 4 == 0, "word copies");
+    constexpr uint32_t kJobWords = sizeof(JobArgs) / 4, kSyncWords = sizeof(ChainSync) / 4;
+    for (uint32_t i = threadIdx.x; i < kJobWords + kSyncWords; i += nthr) {
+      if (i < kJobWords)
+        reinterpret_cast<uint32_t*>(&s_job)[i] = reinterpret_cast<const uint32_t*>(&p.job[j])[i];
+      else
+        reinterpret_cast<uint32_t*>(&s_sync)[i - kJobWords] =
+            reinterpret_cast<const uint32_t*>(&p.sync[j])[i - kJobWords];
     }
-    consume_job<QT, 1, false, true>(a, v, &y, base, sh, s, phase);
+    if (threadIdx.x == 0) {
+      // x is complete once the counter of the job that wrote it reaches this step's target
+      const ChainSync& y = p.sync[j];
+      if (y.wait_cnt && !wait_at_least(a.err, y.wait_cnt, s_epoch * y.wait_target, y.npush != 0, &sh.failed))
+        sh.failed = 1;
+    }
+    named_barrier(1, nthr);
+    consume_job<QT, 1, false, true>(a, s_job, &s_sync, base, sh, s, phase,
+                                    *reinterpret_cast<volatile uint32_t*>(&s_zero));
     named_barrier(1, nthr);  // every consumer's outputs of job j are stored
-    if (threadIdx.x == 0 && y.counter[0]) {
+    if (threadIdx.x == 0 && s_sync.counter[0]) {
       uint32_t r_begin, r_end;
-      cta_rows(v, r_begin, r_end);
-      const uint32_t o0 = r_begin / v.row_unit, o1 = r_end / v.row_unit;
-      if (y.npush) {
-        const uint32_t pushed = o1 > y.push_rows ? (o0 < y.push_rows ? y.push_rows - o0 : 0u) : o1 - o0;
-        __threadfence_system();
-        for (uint32_t rk = 0; rk < y.npush; ++rk) atomicAdd_system(y.counter[rk], static_cast<unsigned long long>(pushed));
+      cta_rows(s_job, r_begin, r_end);
+      const uint32_t o0 = r_begin / s_job.row_unit, o1 = r_end / s_job.row_unit;
+      const uint32_t pr = s_sync.push_rows;
+      if (s_sync.npush) {
+        const uint32_t pushed = o1 > pr ? (o0 < pr ? pr - o0 : 0u) : o1 - o0;
+        for (uint32_t rk = 0; rk < s_sync.npush; ++rk) red_release_sys(s_sync.counter[rk], pushed);
       } else {
-        __threadfence();
-        atomicAdd(y.counter[0], static_cast<unsigned long long>(o1 - o0));
+        red_release_gpu(s_sync.counter[0], o1 - o0);
       }
     }
   }
@@ -1514,6 +1606,13 @@ const Variant kVariants[] = {variant<4, 1, true>(), variant<4, 2, true>(), varia
                              variant<6, 1, false>(), variant<4, 1, false, true>(),
                              variant<6, 1, false, true>(), variant<5, 1, false, true>()};
 
+// The push kernel of a type (Q4_K, Q5_K or Q6_K).
+const void* push_fn(uint32_t type) {
+  return type == KQ_TYPE_Q4_K   ? reinterpret_cast<const void*>(&warpmma_push_kernel<4>)
+         : type == KQ_TYPE_Q5_K ? reinterpret_cast<const void*>(&warpmma_push_kernel<5>)
+                                : reinterpret_cast<const void*>(&warpmma_push_kernel<6>);
+}
+
 // The chain kernel of a type (Q4_K, Q5_K or Q6_K).
 const void* chain_fn(uint32_t type) {
   return type == KQ_TYPE_Q4_K   ? reinterpret_cast<const void*>(&warpmma_chain_kernel<4>)
@@ -1530,9 +1629,11 @@ int warpmma_prepare(kq_ctx* ctx) {
     if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute", "warp-MMA matvec kernel");
   }
   for (uint32_t t : {uint32_t(KQ_TYPE_Q4_K), uint32_t(KQ_TYPE_Q5_K), uint32_t(KQ_TYPE_Q6_K)}) {
-    const cudaError_t e =
+    cudaError_t e =
         cudaFuncSetAttribute(chain_fn(t), cudaFuncAttributeMaxDynamicSharedMemorySize, ctx->max_smem);
     if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute", "warp-MMA chain kernel");
+    e = cudaFuncSetAttribute(push_fn(t), cudaFuncAttributeMaxDynamicSharedMemorySize, ctx->max_smem);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute", "warp-MMA push kernel");
   }
   return KQ_OK;
 }
@@ -1756,6 +1857,42 @@ int warpmma_matvec(kq_ctx* ctx, const kq_matvec_desc& d, uint64_t ldx, uint64_t 
                                !(d.flags & KQ_FLAG_NO_PDL), stream, &plan.args);
   if (e != cudaSuccess)
     return cuda_fail(e, "cudaLaunchKernelExC", "warp-MMA matvec " + shape(plan.grid, plan.block, plan.smem));
+  return KQ_OK;
+}
+
+int warpmma_push(kq_ctx* ctx, const kq_matvec_desc& d, const kq_push_desc& push, uint64_t ldx,
+                 uint64_t ldy, cudaStream_t stream) {
+  const char* call = "kq_matvec_push";
+  WarpMmaPlan plan;
+  int rc = warpmma_plan(ctx, d, ldx, ldy, call, plan);
+  if (rc) return rc;
+  if (plan.mode != (d.type == KQ_TYPE_Q4_K ? 4 : d.type == KQ_TYPE_Q5_K ? 6 : 5))
+    return fail(KQ_E_UNSUPPORTED, call, "k " + std::to_string(d.k) + " does not fit the integer kernel");
+  PushArgs q = {};
+  q.y.wait_cnt = reinterpret_cast<const unsigned long long*>(push.wait_counter);
+  q.y.npush = push.npush;
+  q.y.push_rows = push.npush ? push.push_rows : 0;
+  for (uint32_t r = 0; r < kChainMaxRanks; ++r) {
+    q.y.push_y[r] = r < push.npush ? reinterpret_cast<float*>(push.y[r]) : nullptr;
+    q.y.counter[r] = r < push.npush ? reinterpret_cast<unsigned long long*>(push.counter[r]) : nullptr;
+  }
+  q.epoch = reinterpret_cast<const unsigned long long*>(push.epoch);
+  q.wait_mul = push.wait_mul;
+  q.wait_add = push.wait_add;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(plan.grid);
+  cfg.blockDim = dim3(plan.block);
+  cfg.dynamicSmemBytes = plan.smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = (d.flags & KQ_FLAG_NO_PDL) ? 0 : 1;
+  void* params[] = {&plan.args, &q};
+  const cudaError_t e = cudaLaunchKernelExC(&cfg, push_fn(d.type), params);
+  if (e != cudaSuccess)
+    return cuda_fail(e, "cudaLaunchKernelExC", "warp-MMA push " + shape(plan.grid, plan.block, plan.smem));
   return KQ_OK;
 }
 

@@ -287,7 +287,8 @@ class CudaBackend:
     """libkq.so kernels on one GPU. With world > 1 the exchange after each projection is either
     an NCCL all-gather (torch.distributed), or -- push=True -- done by the matvec itself: its
     epilogue stores its rows into every rank's full vector over CUDA IPC peer mappings and
-    counts them there, and the next matvec waits for the count (kq_matvec_push)."""
+    counts them there, and the next matvec waits for the count (kq_matvec_push), or -- chain=True
+    -- the same inside chains of several matvecs per launch (kq_matvec_chain)."""
 
     def __init__(self, kernels, stream=None, group=None, world: int = 1, flags: int = 0,
                  push: bool = False, rank: int = 0, chain: bool = False):
@@ -493,7 +494,7 @@ def make_cuda_stack(cfg: StackConfig, kernels, rank: int = 0, world: int = 1, gr
                     stream=None, flags: int = 0, push: bool = False, chain: bool = False) -> DecodeStack:
     """One rank's stack on libkq.so. The exchange between ranks (and the launches): NCCL
     all-gathers after one matvec launch per projection (default), the matvec's own push to peer
-    memory (push=True, the CUDA-core kernel), or chains (chain=True: the warp-MMA kernel, up to
+    memory (push=True, the warp-MMA kernel's push variant), or chains (chain=True: up to
     three projections per launch, outputs pushed to peer memory and ordered by counters)."""
     return DecodeStack(cfg, CudaBackend(kernels, stream=stream, group=group, world=world, flags=flags,
                                         push=push, rank=rank, chain=chain), rank, world)

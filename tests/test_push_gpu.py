@@ -1,0 +1,93 @@
+"""kq_matvec_push on one GPU, pushing to its own full vector (npush 1): the warp-MMA push kernel's
+outputs equal the lone launch's bit for bit, both in y and in the full vector; the counter gains
+the pushed count; a second launch waits for that count before it reads x; and the CUDA-core push
+(KQ_FLAG_CUDA_CORES) agrees within the bound. The exchange between GPUs is covered by
+tests/test_stack_multigpu.py."""
+import numpy as np
+import pytest
+import torch
+
+import oracle
+
+import kernite_b200 as kb
+
+pytestmark = pytest.mark.gpu
+
+
+def _w(kernels, qtype, rows, k, t):
+    n = rows * k // 256
+    W = torch.empty(n * kb.block_bytes(qtype), dtype=torch.uint8, device="cuda")
+    kernels.fill(qtype, W, 0, n, kb.stream_key(55, t))
+    return W
+
+
+def _desc(npush, push_rows, full, counter, wait=0, epoch=0, mul=0, add=0):
+    d = kb.KqPushDesc()
+    d.npush, d.push_rows = npush, push_rows
+    d.y[0] = full
+    d.counter[0] = counter
+    d.wait_counter, d.epoch, d.wait_mul, d.wait_add = wait, epoch, mul, add
+    return d
+
+
+@pytest.mark.parametrize("qtype,rows,k,pair", [(4, 4096, 4096, False), (6, 32000, 4096, False),
+                                               (4, 2048, 8192, True), (6, 300, 11008, False),
+                                               (5, 1024, 4096, False)])
+def test_push_kernel_equals_lone_kernel(kernels, qtype, rows, k, pair):
+    W = _w(kernels, qtype, rows, k, rows)
+    x = torch.from_numpy(np.random.default_rng(rows).standard_normal(k).astype(np.float32)).cuda()
+    outs = rows // 2 if pair else rows
+    kw = dict(epilogue=kb.EPILOGUE_PAIR_PRODUCT if pair else kb.EPILOGUE_NONE, pair_scale=0.03)
+    y0 = torch.full((outs,), float("nan"), device="cuda")
+    y1 = torch.full((outs,), float("nan"), device="cuda")
+    full = torch.full((outs + 7,), float("nan"), device="cuda")
+    mem = torch.zeros(2, dtype=torch.int64, device="cuda")
+    push_rows = outs - 5 if outs > 5 else outs
+    kernels.matvec(qtype, y0, W, x, rows, k, 1, **kw)
+    kernels.matvec_push(qtype, y1, W, x, rows, k, _desc(1, push_rows, full.data_ptr() + 8, mem.data_ptr()), **kw)
+    torch.cuda.synchronize()
+    kernels.device_error()
+    assert torch.equal(y0, y1)
+    assert torch.equal(full[2:2 + push_rows], y0[:push_rows])
+    assert torch.isnan(full[:2]).all() and torch.isnan(full[2 + push_rows:]).all()
+    assert int(mem[0]) == push_rows
+
+
+def test_push_waits_for_the_count_before_reading_x(kernels):
+    """Two pushes in a row over three steps: the second reads the first's full vector after its
+    counter reaches step * rows ((epoch - 1) * mul + add)."""
+    h = 4096
+    W1, W2 = _w(kernels, 4, h, h, 1), _w(kernels, 4, h, h, 2)
+    mem = torch.zeros(3, dtype=torch.int64, device="cuda")  # epoch, counter 1, counter 2
+    ep, c1, c2 = mem.data_ptr(), mem.data_ptr() + 8, mem.data_ptr() + 16
+    x = torch.zeros(h, device="cuda")
+    y1, y2, full1, full2 = (torch.zeros(h, device="cuda") for _ in range(4))
+    r1, r2 = torch.zeros(h, device="cuda"), torch.zeros(h, device="cuda")
+    for step in range(1, 4):
+        x.copy_(torch.from_numpy(np.random.default_rng(step).standard_normal(h).astype(np.float32)))
+        mem[0] += 1
+        kernels.matvec_push(4, y1, W1, x, h, h, _desc(1, h, full1.data_ptr(), c1))
+        kernels.matvec_push(4, y2, W2, full1, h, h, _desc(1, h, full2.data_ptr(), c2, wait=c1, epoch=ep,
+                                                          mul=h, add=h))
+        kernels.matvec(4, r1, W1, x, h, h, 1)
+        kernels.matvec(4, r2, W2, r1, h, h, 1)
+        torch.cuda.synchronize()
+        kernels.device_error()
+        assert torch.equal(full2, r2), step
+    assert mem.tolist() == [3, 3 * h, 3 * h]
+
+
+def test_cuda_core_push_agrees_within_the_bound(kernels):
+    rows, k = 1024, 4096
+    W = _w(kernels, 6, rows, k, 3)
+    xh = np.random.default_rng(4).standard_normal(k).astype(np.float32)
+    x = torch.from_numpy(xh).cuda()
+    y, full = torch.zeros(rows, device="cuda"), torch.zeros(rows, device="cuda")
+    mem = torch.zeros(1, dtype=torch.int64, device="cuda")
+    kernels.matvec_push(6, y, W, x, rows, k, _desc(1, rows, full.data_ptr(), mem.data_ptr()),
+                        flags=kb.FLAG_CUDA_CORES)
+    torch.cuda.synchronize()
+    kernels.device_error()
+    ref, bound = oracle.matvec_ref(6, W.cpu().numpy(), xh[None, :], k, 0, rows)
+    assert (np.abs(full.cpu().numpy() - ref[0]) <= 1e-3 * bound[0]).all()
+    assert torch.equal(full, y) and int(mem[0]) == rows
