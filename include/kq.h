@@ -310,6 +310,38 @@ int kq_peer_open(kq_ctx* ctx, const void* ipc_handle, uint64_t* ptr);
 int kq_peer_close(kq_ctx* ctx, uint64_t ptr);
 int kq_peer_free(kq_ctx* ctx, uint64_t ptr);
 
+/* ---- The kernels as a module image, for a caller that loads and launches them itself -------
+ *
+ * kernite loads a module (Module::load, crates/cuda/src/lib.rs:945-1016, which takes PTX text only,
+ * :952-953) and launches its functions with cuLaunchKernel from a macro launcher
+ * (crates/macros/src/gpu.rs:276-328, crates/cuda/src/lib.rs:1045-1054). The pair below lets it do
+ * the same with this library's warp-MMA kernels: kq_module_image hands over the sm_100a cubin
+ * (tcgen05 and the other sm_100a-only instructions need the architecture-specific target, so the
+ * image is a cubin, not PTX; a Module::load_image(&Cuda, &[u8], names) addition to kernite-cuda
+ * loads it), and kq_matvec_plan says which function of it to launch, and how. */
+
+/* The image: ELF bytes inside libkq.so, valid for the life of the process. No GPU needed. */
+int kq_module_image(const void** image, size_t* bytes);
+
+/* One planned launch of a function of that image. */
+typedef struct kq_launch {
+    char kernel[256];      /* its name in the image (cuModuleGetFunction) */
+    uint32_t grid[3];
+    uint32_t block[3];
+    uint32_t shared_bytes; /* dynamic shared memory; set the function's
+                            * CU_FUNC_ATTRIBUTE_MAX_DYNAMIC_SHARED_SIZE_BYTES to at least this */
+    uint32_t param_bytes;  /* the function takes one parameter: these bytes, by value */
+    uint8_t params[512];
+} kq_launch;
+
+/* Plans kq_matvec(ctx, desc) on the warp-MMA kernel without launching anything: the function,
+ * the grid, the block, the shared memory and the parameter bytes. Launched with
+ * cuLaunchKernel(f, grid, block, shared_bytes, stream, {params}, NULL) in the primary context of
+ * the ctx's GPU (the one kernite retains), it computes what kq_matvec computes, bit for bit; its
+ * bounded waits record into the ctx's device error word (kq_device_error). Requests the warp-MMA
+ * kernel does not serve (batch above 8, tensor-core or CUDA-core flags) are KQ_E_UNSUPPORTED. */
+int kq_matvec_plan(kq_ctx* ctx, const kq_matvec_desc* desc, kq_launch* out);
+
 /* The tensor-core Q4_K matvec of kq_matvec_q4k (batch 1..64) for callers that cannot allocate
  * device memory: code running while a CUDA graph is being captured, a serving process whose
  * memory pool has already reserved the GPU, or a latency-critical path where a cudaMalloc

@@ -64,7 +64,7 @@ EXPORTS = (
     "kq_dequant_q8_0", "kq_stream_key", "kq_matvec_q4k_noalloc",
     "kq_matvec_push", "kq_wait_counter", "kq_matvec_chain", "kq_epoch_advance", "kq_peer_alloc", "kq_peer_open", "kq_peer_close", "kq_peer_free",
     "kq_gguf_open", "kq_gguf_close", "kq_gguf_tensor_count", "kq_gguf_tensor_at", "kq_gguf_find",
-    "kq_gguf_meta_int", "kq_gguf_meta_str",
+    "kq_gguf_meta_int", "kq_gguf_meta_str", "kq_module_image", "kq_matvec_plan",
 )
 
 
@@ -103,6 +103,15 @@ class KqPushDesc(ctypes.Structure):
         ("y", ctypes.c_uint64 * 8), ("counter", ctypes.c_uint64 * 8),
         ("wait_counter", ctypes.c_uint64), ("epoch", ctypes.c_uint64),
         ("wait_mul", ctypes.c_uint64), ("wait_add", ctypes.c_uint64),
+    ]
+
+
+class KqLaunch(ctypes.Structure):
+    """``kq_launch`` (include/kq.h): one planned launch of a function of the module image."""
+    _fields_ = [
+        ("kernel", ctypes.c_char * 256), ("grid", ctypes.c_uint32 * 3), ("block", ctypes.c_uint32 * 3),
+        ("shared_bytes", ctypes.c_uint32), ("param_bytes", ctypes.c_uint32),
+        ("params", ctypes.c_uint8 * 512),
     ]
 
 
@@ -153,6 +162,8 @@ def lib() -> ctypes.CDLL:
     L.kq_matvec_push.argtypes = [vp, ctypes.POINTER(KqMatvecDesc), ctypes.POINTER(KqPushDesc), vp]
     L.kq_wait_counter.argtypes = [vp, u64, u64, u64, u64, vp]
     L.kq_matvec_chain.argtypes = [vp, ctypes.POINTER(KqChainJob), u32, u64, vp]
+    L.kq_module_image.argtypes = [ctypes.POINTER(vp), ctypes.POINTER(ctypes.c_size_t)]
+    L.kq_matvec_plan.argtypes = [vp, ctypes.POINTER(KqMatvecDesc), ctypes.POINTER(KqLaunch)]
     L.kq_epoch_advance.argtypes = [vp, u64, vp]
     L.kq_peer_alloc.argtypes = [vp, u64, ctypes.POINTER(u64), ctypes.c_char_p]
     L.kq_peer_open.argtypes = [vp, ctypes.c_char_p, ctypes.POINTER(u64)]
@@ -222,6 +233,14 @@ def _stream(s: Any) -> int | None:
     if hasattr(s, "cuda_stream"):
         return int(s.cuda_stream) or None
     raise TypeError(f"not a stream: {type(s)!r}")
+
+
+def module_image() -> bytes:
+    """The warp-MMA kernels' sm_100a cubin (``kq_module_image``), for a caller that loads the
+    module itself (cuModuleLoadData) and launches what :meth:`Kernels.matvec_plan` plans."""
+    p, n = ctypes.c_void_p(), ctypes.c_size_t()
+    _check(lib().kq_module_image(ctypes.byref(p), ctypes.byref(n)), "kq_module_image")
+    return ctypes.string_at(p.value, n.value)
 
 
 def stream_key(seed: int, tensor: int) -> int:
@@ -353,6 +372,19 @@ class Kernels:
         """Stream-ordered bounded wait until *counter >= (*epoch - 1) * wait_mul + wait_add."""
         _check(lib().kq_wait_counter(self._ctx, counter, epoch, wait_mul, wait_add, _stream(stream)),
                "kq_wait_counter")
+
+    def matvec_plan(self, qtype: int, y, w, x, rows: int, k: int, batch: int = 1, *,
+                    prologue: int = PROLOGUE_NONE, epilogue: int = EPILOGUE_NONE, eps: float = 0.0,
+                    pair_scale: float = 1.0, flags: int = 0) -> "KqLaunch":
+        """``kq_matvec_plan``: the warp-MMA launch of this matvec, unlaunched (a function of
+        :func:`module_image`, its grid, block, shared memory and parameter bytes)."""
+        t = {4: TYPE_Q4_K, 5: TYPE_Q5_K, 6: TYPE_Q6_K}.get(qtype, qtype)
+        d = KqMatvecDesc(type=t, rows=rows, k=k, batch=batch, y=_addr(y), w=_addr(w), x=_addr(x),
+                         ldx=0, ldy=0, prologue=prologue, epilogue=epilogue, eps=eps,
+                         pair_scale=pair_scale, flags=flags, reserved=0)
+        out = KqLaunch()
+        _check(lib().kq_matvec_plan(self._ctx, ctypes.byref(d), ctypes.byref(out)), "kq_matvec_plan")
+        return out
 
     def matvec_chain(self, jobs, epoch: int, stream=None) -> None:
         """``kq_matvec_chain``: up to 8 batch-1 matvecs of one type and k in one launch, each

@@ -46,17 +46,47 @@ def needs_build() -> bool:
     return any(os.path.getmtime(p) > t for p in deps)
 
 
+# The sources whose kernels also ship as a module image inside the library (kq_module_image):
+# compiled a second time to an sm_100a cubin and embedded as read-only data.
+IMAGE_SOURCES = {"kq_warpmma.cu": "kq_image_warpmma"}
+
+
+def _image_asm(symbol: str, cubin: str) -> str:
+    return (f"\t.section .rodata\n\t.balign 64\n\t.global {symbol}\n\t.type {symbol}, @object\n"
+            f"{symbol}:\n\t.incbin \"{cubin}\"\n\t.global {symbol}_end\n{symbol}_end:\n"
+            f"\t.section .note.GNU-stack,\"\",@progbits\n")
+
+
 def build(verbose: bool = False, force: bool = False) -> str:
     if not force and not needs_build():
         return LIB
+    from concurrent.futures import ThreadPoolExecutor
+
     os.makedirs(BUILD, exist_ok=True)
-    objs = []
+    jobs, objs = [], []
     for src in sources():
         obj = os.path.join(BUILD, os.path.basename(src) + ".o")
         cmd = [nvcc(), *ARCH, *FLAGS, "-I", INCLUDE, "-I", CSRC, "-c", src, "-o", obj]
         if verbose:
             cmd.insert(1, "-Xptxas=-v")
-        subprocess.run(cmd, check=True)
+        jobs.append(cmd)
+        objs.append(obj)
+        sym = IMAGE_SOURCES.get(os.path.basename(src))
+        if sym:
+            cubin = os.path.join(BUILD, os.path.basename(src) + ".cubin")
+            jobs.append([nvcc(), *ARCH, "-O3", "-std=c++17", "--expt-relaxed-constexpr",
+                         "-I", INCLUDE, "-I", CSRC, "-cubin", src, "-o", cubin])
+    with ThreadPoolExecutor(max_workers=min(8, os.cpu_count() or 1)) as pool:
+        for r in pool.map(lambda c: subprocess.run(c, capture_output=not verbose, text=True), jobs):
+            if r.returncode:
+                raise RuntimeError(f"{' '.join(r.args)}\n{r.stdout or ''}{r.stderr or ''}")
+    for src, sym in IMAGE_SOURCES.items():
+        cubin = os.path.join(BUILD, src + ".cubin")
+        asm = os.path.join(BUILD, sym + ".S")
+        with open(asm, "w") as f:
+            f.write(_image_asm(sym, cubin))
+        obj = os.path.join(BUILD, sym + ".o")
+        subprocess.run(["gcc", "-c", asm, "-o", obj], check=True)
         objs.append(obj)
     tmp = LIB + ".tmp"
     subprocess.run([nvcc(), *ARCH, "-shared", "-cudart", "static", "-o", tmp, *objs], check=True)

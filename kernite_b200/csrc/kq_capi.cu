@@ -337,6 +337,25 @@ int kq_matvec_push(kq_ctx* ctx, const kq_matvec_desc* desc, const kq_push_desc* 
   return kq::matvec(ctx, *desc, static_cast<cudaStream_t>(stream), push);
 }
 
+// The warp-MMA kernels' cubin, embedded at build time (kernite_b200/build.py).
+extern "C" const unsigned char kq_image_warpmma[];
+extern "C" const unsigned char kq_image_warpmma_end[];
+
+int kq_module_image(const void** image, size_t* bytes) {
+  if (!image || !bytes) return fail(KQ_E_INVALID, "kq_module_image", "null argument");
+  *image = kq_image_warpmma;
+  *bytes = static_cast<size_t>(kq_image_warpmma_end - kq_image_warpmma);
+  return KQ_OK;
+}
+
+int kq_matvec_plan(kq_ctx* ctx, const kq_matvec_desc* desc, kq_launch* out) {
+  if (!ctx || !desc || !out) return fail(KQ_E_INVALID, "kq_matvec_plan", "null ctx, descriptor or out");
+  kq::DeviceScope scope;
+  int rc = scope.enter(ctx);
+  if (rc) return rc;
+  return kq::warpmma_plan_launch(ctx, *desc, *out);
+}
+
 int kq_matvec_chain(kq_ctx* ctx, const kq_chain_job* jobs, uint32_t njobs, uint64_t epoch,
                     kq_stream stream) {
   if (!ctx || !jobs) return fail(KQ_E_INVALID, "kq_matvec_chain", "null ctx or jobs");

@@ -47,8 +47,11 @@
 // The GGML block layouts and the decode follow the public format (the CPU restatement in
 // oracle/kq_oracle.c); the pattern "one output row per group of lanes, FMA chain over k" is the
 // matvec of fxeqxmulfx/kernite's examples/microgpt/src/gpu.rs:100-131, re-shaped for HBM.
+#include <cuda.h>
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
+
+#include <cstring>
 
 #include <algorithm>
 #include <string>
@@ -58,7 +61,9 @@
 #include "kq_internal.h"
 
 namespace kq {
-namespace {
+// Device code and kernels in a named namespace: their mangled names are the same in this build
+// and in the separately compiled module image (kq_module_image), where a caller looks them up.
+namespace wm {
 
 // Consumer warps: 19 + the producer = 5 warps per scheduler, which leaves 96 registers a thread
 // (each scheduler's register file holds 16K: 5 x 32 x 96 <= 16384; 6 warps would leave 80).
@@ -1620,7 +1625,9 @@ const void* chain_fn(uint32_t type) {
                                 : reinterpret_cast<const void*>(&warpmma_chain_kernel<6>);
 }
 
-}  // namespace
+}  // namespace wm
+
+using namespace wm;
 
 int warpmma_prepare(kq_ctx* ctx) {
   for (const Variant& v : kVariants) {
@@ -1857,6 +1864,45 @@ int warpmma_matvec(kq_ctx* ctx, const kq_matvec_desc& d, uint64_t ldx, uint64_t 
                                !(d.flags & KQ_FLAG_NO_PDL), stream, &plan.args);
   if (e != cudaSuccess)
     return cuda_fail(e, "cudaLaunchKernelExC", "warp-MMA matvec " + shape(plan.grid, plan.block, plan.smem));
+  return KQ_OK;
+}
+
+int warpmma_plan_launch(kq_ctx* ctx, const kq_matvec_desc& d, kq_launch& out) {
+  const char* call = "kq_matvec_plan";
+  int rc = check_desc(d, call);
+  if (rc) return rc;
+  if (!warpmma_supports(d) || (d.flags & (KQ_FLAG_TENSOR_CORES | KQ_FLAG_CUDA_CORES)))
+    return fail(KQ_E_UNSUPPORTED, call, "the warp-MMA kernel serves Q4_K batch 1..8 and Q5_K, Q6_K batch 1");
+  const bool pair = d.epilogue != KQ_EPILOGUE_NONE;
+  const uint64_t ldx = d.ldx ? d.ldx : d.k;
+  const uint64_t ldy = d.ldy ? d.ldy : (pair ? d.rows / 2 : d.rows);
+  WarpMmaPlan plan;
+  rc = warpmma_plan(ctx, d, ldx, ldy, call, plan);
+  if (rc) return rc;
+  // the function's name, as the driver has it (the image is the same source, compiled alike)
+  cudaFunction_t f = nullptr;
+  cudaError_t e = cudaGetFuncBySymbol(&f, kVariants[plan.mode].fn);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaGetFuncBySymbol", call);
+  using GetName = CUresult (*)(const char**, CUfunction);
+  void* fp = nullptr;
+  cudaDriverEntryPointQueryResult q;
+  e = cudaGetDriverEntryPoint("cuFuncGetName", &fp, cudaEnableDefault, &q);
+  if (e != cudaSuccess || q != cudaDriverEntryPointSuccess || !fp)
+    return fail(KQ_E_UNSUPPORTED, call, "the driver has no cuFuncGetName");
+  const char* name = nullptr;
+  const CUresult r = reinterpret_cast<GetName>(fp)(&name, reinterpret_cast<CUfunction>(f));
+  if (r != CUDA_SUCCESS || !name || std::strlen(name) >= sizeof(out.kernel))
+    return fail(KQ_E_UNSUPPORTED, call, "cuFuncGetName gave no usable name");
+  static_assert(sizeof(WarpMmaArgs) <= sizeof(out.params), "kq_launch params too small");
+  std::memset(&out, 0, sizeof(out));
+  std::strcpy(out.kernel, name);
+  out.grid[0] = plan.grid;
+  out.grid[1] = out.grid[2] = 1;
+  out.block[0] = plan.block;
+  out.block[1] = out.block[2] = 1;
+  out.shared_bytes = plan.smem;
+  out.param_bytes = sizeof(WarpMmaArgs);
+  std::memcpy(out.params, &plan.args, sizeof(WarpMmaArgs));
   return KQ_OK;
 }
 

@@ -76,3 +76,28 @@ def test_desc_layout_matches_header(tmp_path):
     got = [int(v) for v in subprocess.run([str(exe)], capture_output=True, text=True, check=True).stdout.split()]
     D = kb.KqMatvecDesc
     assert got == [ctypes.sizeof(D), D.y.offset, D.prologue.offset, D.eps.offset, D.flags.offset]
+
+
+def test_module_image_is_an_sm100a_cubin():
+    import struct
+
+    img = kb.module_image()
+    assert img[:4] == b"\x7fELF" and len(img) > 100_000
+    # ELF64 header: e_machine at 18 is EM_CUDA (190); the CUDA ELF's e_flags hold the SM (100)
+    assert img[4] == 2 and struct.unpack_from("<H", img, 18)[0] == 190
+    flags = struct.unpack_from("<I", img, 48)[0]
+    assert (flags & 0xFF) == 100 or ((flags >> 8) & 0xFF) == 100, hex(flags)
+
+
+def test_launch_struct_layout_matches_header(tmp_path):
+    src = tmp_path / "launch.c"
+    src.write_text(
+        '#include <stdio.h>\n#include <stddef.h>\n#include "kq.h"\n'
+        'int main(void){printf("%zu %zu %zu %zu %zu\\n", sizeof(kq_launch), offsetof(kq_launch, grid),'
+        ' offsetof(kq_launch, shared_bytes), offsetof(kq_launch, params), sizeof(kq_chain_job));return 0;}\n')
+    exe = tmp_path / "launch"
+    subprocess.run(["gcc", "-I", os.path.join(ROOT, "include"), str(src), "-o", str(exe)], check=True)
+    got = [int(v) for v in subprocess.run([str(exe)], capture_output=True, text=True, check=True).stdout.split()]
+    L = kb.KqLaunch
+    assert got == [ctypes.sizeof(L), L.grid.offset, L.shared_bytes.offset, L.params.offset,
+                   ctypes.sizeof(kb.KqChainJob)]
