@@ -224,6 +224,36 @@ int kq_gguf_find(const kq_gguf* g, const char* name, kq_gguf_tensor* out);
 int kq_gguf_meta_int(const kq_gguf* g, const char* key, int64_t* out);
 int kq_gguf_meta_str(const kq_gguf* g, const char* key, const char** out);
 
+/* ---- A decode step's attention: rotary embedding, the key/value cache, GQA attention -------
+ *
+ * Between a layer's q|k|v matvec and its output projection a Llama decode step rotates the query
+ * and key heads by their position (RoPE), appends the key and value heads to a cache, and lets
+ * each query head attend over every cached position of its key/value head (grouped-query
+ * attention: n_heads / n_kv query heads share one). The functional model is kernite's microgpt
+ * attention (examples/microgpt/src/gpu.rs:130-230: per head the logits q.k scaled, their maximum,
+ * exponentials and sum, the weights and the values they weigh); kernite has no cache, no RoPE and
+ * no GQA. Caches are f16, row p = position p, n_kv * head_dim values (head-major); activations
+ * are f32. */
+
+/* qkv = the step's q (n_heads * head_dim), k and v (n_kv * head_dim each), back to back, as a
+ * q|k|v matvec writes them. q_out <- q with element pairs (2i, 2i+1) of each head rotated by the
+ * angle pos * base^(-2i / head_dim) (GGML's "norm" rotary mode; base 10000 for Llama 2, 500000 for
+ * Llama 3); row pos of k_cache <- k rotated the same way, row pos of v_cache <- v, as f16. */
+int kq_rope_append(kq_ctx* ctx, uint64_t qkv, uint64_t q_out, uint64_t k_cache, uint64_t v_cache,
+                   uint32_t n_heads, uint32_t n_kv, uint32_t head_dim, uint32_t pos, double base,
+                   kq_stream stream);
+
+/* out[h * head_dim + j] = sum_p w_hp v_p[g(h) * head_dim + j] over the cache's first len rows,
+ * w_h = softmax_p(q_h . k_p[g(h)] / sqrt(head_dim)), g(h) = h / (n_heads / n_kv). Split over
+ * positions across CTAs, combined in a second launch; workspace (device, 16-byte aligned, not
+ * read before written) holds the splits: kq_attention_workspace gives its size. n_heads / n_kv
+ * 1..16, head_dim a multiple of 8 up to 256. */
+int kq_attention_decode(kq_ctx* ctx, uint64_t out, uint64_t q, uint64_t k_cache, uint64_t v_cache,
+                        uint32_t n_heads, uint32_t n_kv, uint32_t head_dim, uint32_t len,
+                        uint64_t workspace, uint64_t workspace_bytes, kq_stream stream);
+uint64_t kq_attention_workspace(kq_ctx* ctx, uint32_t n_heads, uint32_t n_kv, uint32_t head_dim,
+                                uint32_t len);
+
 /* ---- Row-sharded stacks: a matvec whose epilogue also pushes its outputs to other GPUs ----
  *
  * With the rows of a matrix split over N GPUs, every GPU needs the whole output vector for the

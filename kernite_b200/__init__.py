@@ -65,6 +65,7 @@ EXPORTS = (
     "kq_matvec_push", "kq_wait_counter", "kq_matvec_chain", "kq_epoch_advance", "kq_peer_alloc", "kq_peer_open", "kq_peer_close", "kq_peer_free",
     "kq_gguf_open", "kq_gguf_close", "kq_gguf_tensor_count", "kq_gguf_tensor_at", "kq_gguf_find",
     "kq_gguf_meta_int", "kq_gguf_meta_str", "kq_module_image", "kq_matvec_plan",
+    "kq_rope_append", "kq_attention_decode", "kq_attention_workspace",
 )
 
 
@@ -163,6 +164,10 @@ def lib() -> ctypes.CDLL:
     L.kq_wait_counter.argtypes = [vp, u64, u64, u64, u64, vp]
     L.kq_matvec_chain.argtypes = [vp, ctypes.POINTER(KqChainJob), u32, u64, vp]
     L.kq_module_image.argtypes = [ctypes.POINTER(vp), ctypes.POINTER(ctypes.c_size_t)]
+    L.kq_rope_append.argtypes = [vp, u64, u64, u64, u64, u32, u32, u32, u32, ctypes.c_double, vp]
+    L.kq_attention_decode.argtypes = [vp, u64, u64, u64, u64, u32, u32, u32, u32, u64, u64, vp]
+    L.kq_attention_workspace.argtypes = [vp, u32, u32, u32, u32]
+    L.kq_attention_workspace.restype = u64
     L.kq_matvec_plan.argtypes = [vp, ctypes.POINTER(KqMatvecDesc), ctypes.POINTER(KqLaunch)]
     L.kq_epoch_advance.argtypes = [vp, u64, vp]
     L.kq_peer_alloc.argtypes = [vp, u64, ctypes.POINTER(u64), ctypes.c_char_p]
@@ -179,7 +184,7 @@ def lib() -> ctypes.CDLL:
     L.kq_gguf_meta_str.argtypes = [vp, ctypes.c_char_p, ctypes.POINTER(ctypes.c_char_p)]
     for name in EXPORTS:
         fn = getattr(L, name)
-        if name not in ("kq_last_error", "kq_stream_key", "kq_gguf_tensor_count"):
+        if name not in ("kq_last_error", "kq_stream_key", "kq_gguf_tensor_count", "kq_attention_workspace"):
             fn.restype = i32
     _lib = L
     return L
@@ -385,6 +390,24 @@ class Kernels:
         out = KqLaunch()
         _check(lib().kq_matvec_plan(self._ctx, ctypes.byref(d), ctypes.byref(out)), "kq_matvec_plan")
         return out
+
+    def rope_append(self, qkv, q_out, k_cache, v_cache, n_heads: int, n_kv: int, head_dim: int,
+                    pos: int, base: float = 10000.0, stream=None) -> None:
+        """``kq_rope_append``: q rotated into q_out; k rotated and v into row ``pos`` of the f16
+        caches."""
+        _check(lib().kq_rope_append(self._ctx, _addr(qkv), _addr(q_out), _addr(k_cache), _addr(v_cache),
+                                    n_heads, n_kv, head_dim, pos, base, _stream(stream)), "kq_rope_append")
+
+    def attention_workspace(self, n_heads: int, n_kv: int, head_dim: int, length: int) -> int:
+        return int(lib().kq_attention_workspace(self._ctx, n_heads, n_kv, head_dim, length))
+
+    def attention(self, out, q, k_cache, v_cache, n_heads: int, n_kv: int, head_dim: int,
+                  length: int, workspace, workspace_bytes: int, stream=None) -> None:
+        """``kq_attention_decode``: one step's grouped-query attention over the caches' first
+        ``length`` positions."""
+        _check(lib().kq_attention_decode(self._ctx, _addr(out), _addr(q), _addr(k_cache), _addr(v_cache),
+                                         n_heads, n_kv, head_dim, length, _addr(workspace),
+                                         workspace_bytes, _stream(stream)), "kq_attention_decode")
 
     def matvec_chain(self, jobs, epoch: int, stream=None) -> None:
         """``kq_matvec_chain``: up to 8 batch-1 matvecs of one type and k in one launch, each

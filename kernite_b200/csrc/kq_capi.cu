@@ -337,6 +337,34 @@ int kq_matvec_push(kq_ctx* ctx, const kq_matvec_desc* desc, const kq_push_desc* 
   return kq::matvec(ctx, *desc, static_cast<cudaStream_t>(stream), push);
 }
 
+int kq_rope_append(kq_ctx* ctx, uint64_t qkv, uint64_t q_out, uint64_t k_cache, uint64_t v_cache,
+                   uint32_t n_heads, uint32_t n_kv, uint32_t head_dim, uint32_t pos, double base,
+                   kq_stream stream) {
+  if (!ctx) return fail(KQ_E_INVALID, "kq_rope_append", "null ctx");
+  kq::DeviceScope scope;
+  int rc = scope.enter(ctx);
+  if (rc) return rc;
+  return kq::rope_append(ctx, qkv, q_out, k_cache, v_cache, n_heads, n_kv, head_dim, pos, base,
+                         static_cast<cudaStream_t>(stream));
+}
+
+int kq_attention_decode(kq_ctx* ctx, uint64_t out, uint64_t q, uint64_t k_cache, uint64_t v_cache,
+                        uint32_t n_heads, uint32_t n_kv, uint32_t head_dim, uint32_t len,
+                        uint64_t workspace, uint64_t workspace_bytes, kq_stream stream) {
+  if (!ctx) return fail(KQ_E_INVALID, "kq_attention_decode", "null ctx");
+  kq::DeviceScope scope;
+  int rc = scope.enter(ctx);
+  if (rc) return rc;
+  return kq::attention_decode(ctx, out, q, k_cache, v_cache, n_heads, n_kv, head_dim, len,
+                              workspace, workspace_bytes, static_cast<cudaStream_t>(stream));
+}
+
+uint64_t kq_attention_workspace(kq_ctx* ctx, uint32_t n_heads, uint32_t n_kv, uint32_t head_dim,
+                                uint32_t len) {
+  if (!ctx || !n_kv) return 0;
+  return kq::attention_workspace_bytes(ctx, n_heads, n_kv, head_dim, len ? len : 1);
+}
+
 // The warp-MMA kernels' cubin, embedded at build time (kernite_b200/build.py).
 extern "C" const unsigned char kq_image_warpmma[];
 extern "C" const unsigned char kq_image_warpmma_end[];

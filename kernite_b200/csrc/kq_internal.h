@@ -78,4 +78,11 @@ int fill(kq_ctx* ctx, int type, uint64_t w, uint64_t block0, uint64_t nblocks, u
 
 uint64_t stream_key(uint64_t seed, uint64_t tensor);
 
+int rope_append(kq_ctx* ctx, uint64_t qkv, uint64_t q_out, uint64_t k_cache, uint64_t v_cache,
+                uint32_t nh, uint32_t nkv, uint32_t d, uint32_t pos, double base, cudaStream_t s);
+uint64_t attention_workspace_bytes(kq_ctx* ctx, uint32_t nh, uint32_t nkv, uint32_t d, uint32_t len);
+int attention_decode(kq_ctx* ctx, uint64_t out, uint64_t q, uint64_t k_cache, uint64_t v_cache,
+                     uint32_t nh, uint32_t nkv, uint32_t d, uint32_t len, uint64_t workspace,
+                     uint64_t workspace_bytes, cudaStream_t s);
+
 }  // namespace kq

@@ -46,6 +46,21 @@ class StackConfig:
     vocab: int
     eps: float = 1e-6
     seed: int = 2026
+    # A real decode step's attention between q|k|v and o (off for BASELINE's matvec stacks):
+    # the q and k heads rotated at the step's position (RoPE), k and v appended to a per-layer
+    # f16 cache of `max_pos` positions, and o = W_o . attention(q, cache) instead of W_o . q.
+    attention: bool = False
+    head_dim: int = 128
+    rope_base: float = 10000.0
+    max_pos: int = 64
+
+    @property
+    def n_heads(self) -> int:
+        return self.hidden // self.head_dim
+
+    @property
+    def n_kv(self) -> int:
+        return self.kv // self.head_dim
 
     def matrices(self):
         """(name, qtype, rows, k) of one layer's matrices, then the head."""
@@ -237,11 +252,21 @@ class DecodeStack:
             "x_loc": backend.vector(sh["down"].rows), "xd": fv["xd"],
             "l_loc": backend.vector(sh["head"].rows), "logits": fv["logits"],
         }
+        self.pos = 0
+        if cfg.attention:
+            if (cfg.n_heads % world or cfg.n_kv % world or cfg.n_heads % cfg.n_kv
+                    or cfg.hidden % cfg.head_dim or cfg.kv % cfg.head_dim):
+                raise ValueError("attention needs whole heads on every rank and whole query groups")
+            nq = sh["qkv"].gathered[1]  # this rank's query rows = its heads' attention outputs
+            self.buf["q_rot"] = backend.vector(nq)
+            self.buf["att"] = backend.vector(nq)
+            self.caches = [backend.kv_cache(cfg, world) for _ in range(cfg.layers)]
         if world == 1:
             # one rank: each "gathered" vector is the local output itself (q is the first h
-            # entries of the q|k|v output), so the gathers vanish
+            # entries of the q|k|v output, or the attention output), so the gathers vanish
             b = self.buf
-            b["q"], b["o"], b["a"], b["xd"], b["logits"] = b["qkv"], b["o_loc"], b["a_loc"], b["x_loc"], b["l_loc"]
+            b["q"] = b["att"] if cfg.attention else b["qkv"]
+            b["o"], b["a"], b["xd"], b["logits"] = b["o_loc"], b["a_loc"], b["x_loc"], b["l_loc"]
 
     def launches_per_token(self) -> int:
         """This library's kernels per token: the matvecs (chains: the step counter's advance and
@@ -260,10 +285,18 @@ class DecodeStack:
         if begin:
             begin()
         x = b["x"]
+        if cfg.attention and self.pos >= cfg.max_pos:
+            raise ValueError(f"the key/value caches hold {cfg.max_pos} positions")
         for layer, lw in enumerate(self.weights):
             be.matvec(lw["qkv"], sh["qkv"], b["qkv"], x, rmsnorm=layer > 0, eps=cfg.eps,
                       out=("q", sh["qkv"].gathered), src=("xd", layer) if layer > 0 else None)
-            be.gather(b["q"], b["qkv"], sh["qkv"].gathered)
+            if cfg.attention:
+                # this rank's heads: rotate, append to the layer's cache, attend; o's input is
+                # every rank's attention output
+                be.attend(self, layer, self.pos)
+                be.gather(b["q"], b["att"], (0, sh["qkv"].gathered[1]))
+            else:
+                be.gather(b["q"], b["qkv"], sh["qkv"].gathered)
             be.matvec(lw["o"], sh["o"], b["o_loc"], b["q"], out=("o", sh["o"].gathered), src=("q", layer + 1))
             be.gather(b["o"], b["o_loc"], sh["o"].gathered)
             be.matvec(lw["gate_up"], sh["gate_up"], b["a_loc"], b["o"], pair_scale=1.0 / math.sqrt(cfg.ffn),
@@ -279,6 +312,7 @@ class DecodeStack:
         end = getattr(be, "end_token", None)
         if end:
             end()
+        self.pos += 1
 
 
 # ---------------------------------------------------------------- the CUDA backend (product)
@@ -448,6 +482,27 @@ class CudaBackend:
     def vector(self, n: int):
         return self.torch.zeros(n, dtype=self.torch.float32, device="cuda")
 
+    def kv_cache(self, cfg: StackConfig, world: int):
+        """One layer's f16 key and value caches for this rank's key/value heads."""
+        n = cfg.max_pos * (cfg.n_kv // world) * cfg.head_dim
+        torch = self.torch
+        return (torch.zeros(n, dtype=torch.float16, device="cuda"),
+                torch.zeros(n, dtype=torch.float16, device="cuda"))
+
+    def attend(self, stack: "DecodeStack", layer: int, pos: int) -> None:
+        """This rank's heads of one layer's attention at position pos: q and k rotated, k and v
+        appended to the layer's cache, buf['att'] = attention over positions 0..pos."""
+        cfg, b, w = stack.cfg, stack.buf, self.world
+        nh, nkv, d = cfg.n_heads // w, cfg.n_kv // w, cfg.head_dim
+        kc, vc = stack.caches[layer]
+        if not hasattr(self, "_att_ws"):
+            nbytes = self.k.attention_workspace(nh, nkv, d, cfg.max_pos)
+            self._att_ws = self.torch.empty(nbytes // 4 + 4, dtype=self.torch.float32, device="cuda")
+        self.k.rope_append(b["qkv"], b["q_rot"], kc, vc, nh, nkv, d, pos, cfg.rope_base, stream=self.stream)
+        self.k.attention(b["att"], b["q_rot"], kc, vc, nh, nkv, d, pos + 1, self._att_ws,
+                         self._att_ws.numel() * 4, stream=self.stream)
+        self.launches += 3
+
     def matvec(self, W, shard: Shard, y, x, rmsnorm: bool = False, eps: float = 0.0,
                pair_scale: float | None = None, out=None, src=None) -> None:
         kb = self.kb
@@ -492,6 +547,8 @@ class _null:
 
 def make_cuda_stack(cfg: StackConfig, kernels, rank: int = 0, world: int = 1, group=None,
                     stream=None, flags: int = 0, push: bool = False, chain: bool = False) -> DecodeStack:
+    if cfg.attention and (push or chain):
+        raise ValueError("a stack with attention runs one launch per projection (NCCL or one rank)")
     """One rank's stack on libkq.so. The exchange between ranks (and the launches): NCCL
     all-gathers after one matvec launch per projection (default), the matvec's own push to peer
     memory (push=True, the warp-MMA kernel's push variant), or chains (chain=True: up to
@@ -502,10 +559,31 @@ def make_cuda_stack(cfg: StackConfig, kernels, rank: int = 0, world: int = 1, gr
 
 # ---------------------------------------------------------------- reference (for tests)
 
-def reference_logits(cfg: StackConfig, x, layers: int | None = None, with_bound: bool = False):
+def _reference_attend(cfg: StackConfig, layer: int, qkv, cache: dict):
+    """One layer's attention step of the reference: rotate q and k at the next position, append
+    k and v (rounded to f16, as the GPU's caches hold them), attend over every position so far."""
+    import numpy as np
+
+    import oracle
+
+    nh, nkv, d = cfg.n_heads, cfg.n_kv, cfg.head_dim
+    pos = cache.setdefault("pos", 0)
+    q, k, v = oracle.rope_ref(qkv, nh, nkv, d, pos, cfg.rope_base)
+    K, V = cache.setdefault(layer, ([], []))
+    K.append(k.astype(np.float32).astype(np.float16))
+    V.append(v.astype(np.float32).astype(np.float16))
+    att, _ = oracle.attention_ref(q.astype(np.float32), np.stack(K), np.stack(V), nh, nkv, d, pos + 1)
+    return att.reshape(-1)
+
+
+def reference_logits(cfg: StackConfig, x, layers: int | None = None, with_bound: bool = False,
+                     cache: dict | None = None):
     """The unsharded stack on the CPU oracle, in f64 from the f32-dequantised weights; with
     `with_bound` also sum_k |w_head[r, k] x_k| per logit (x the normalised head input), the scale
-    of the 1e-3 tolerance. Test and bench-check infrastructure only."""
+    of the 1e-3 tolerance. With attention, `cache` carries the key/value caches and the position
+    from one call (token) to the next. Test and bench-check infrastructure only."""
+    if cache is None:
+        cache = {}
     import numpy as np
 
     import oracle
@@ -529,6 +607,8 @@ def reference_logits(cfg: StackConfig, x, layers: int | None = None, with_bound:
         xin = norm(x) if layer > 0 else x
         qkv = mv(4, weights("qkv", layer, 4, h + 2 * kv, h), xin, h + 2 * kv, h)
         q = qkv[:h]
+        if cfg.attention:
+            q = _reference_attend(cfg, layer, qkv, cache)
         o = mv(4, weights("o", layer, 4, h, h), q, h, h)
         gu = mv(4, weights("gate_up", layer, 4, 2 * f, h), o, 2 * f, h)
         a = gu[0::2] * gu[1::2] / math.sqrt(f)
@@ -536,4 +616,6 @@ def reference_logits(cfg: StackConfig, x, layers: int | None = None, with_bound:
     head = oracle.fill(6, oracle.stream_key(cfg.seed, cfg.tensor_id(cfg.layers, "head")), 0,
                        cfg.vocab * h // QK)
     logits, bound = mv(6, head, norm(x), cfg.vocab, h, bound=True)
+    if cfg.attention:
+        cache["pos"] += 1
     return (logits, bound) if with_bound else logits

@@ -199,3 +199,50 @@ def cpu_threads() -> int:
         return len(os.sched_getaffinity(0))
     except AttributeError:  # pragma: no cover
         return os.cpu_count() or 1
+
+
+# ---------------------------------------------------------------- a decode step's attention
+
+def rope_ref(qkv: np.ndarray, nh: int, nkv: int, d: int, pos: int, base: float):
+    """The step's q and k heads rotated by position `pos` (element pairs (2i, 2i+1) by the angle
+    pos * base^(-2i/d), GGML's "norm" rotary mode), and v, in f64: (q (nh, d), k (nkv, d),
+    v (nkv, d)). kernite has no RoPE; this is the published rotary embedding (Su et al., RoFormer)
+    in the pairing GGML's Llama uses."""
+    x = np.asarray(qkv, dtype=np.float64)
+    q = x[: nh * d].reshape(nh, d)
+    k = x[nh * d:(nh + nkv) * d].reshape(nkv, d)
+    v = x[(nh + nkv) * d:(nh + 2 * nkv) * d].reshape(nkv, d)
+    ang = pos * base ** (-2.0 * np.arange(d // 2) / d)
+    c, s = np.cos(ang), np.sin(ang)
+
+    def rot(a):
+        out = np.empty_like(a)
+        out[:, 0::2] = a[:, 0::2] * c - a[:, 1::2] * s
+        out[:, 1::2] = a[:, 0::2] * s + a[:, 1::2] * c
+        return out
+
+    return rot(q), rot(k), v
+
+
+def attention_ref(q: np.ndarray, k_cache: np.ndarray, v_cache: np.ndarray, nh: int, nkv: int,
+                  d: int, length: int):
+    """Grouped-query attention of one step's queries q (nh, d) over the first `length` positions
+    of the caches (positions, nkv, d), in f64; query head h reads key/value head h // (nh / nkv).
+    Returns (out (nh, d), bound (nh, d) = sum_p w_hp |v_p|, the scale of the tolerance). Follows
+    kernite's microgpt attention (examples/microgpt/src/gpu.rs:130-230): logits q.k scaled, their
+    maximum, exponentials and sum, the weights, the values they weigh."""
+    q = np.asarray(q, dtype=np.float64).reshape(nh, d)
+    K = np.asarray(k_cache, dtype=np.float64)[:length]
+    V = np.asarray(v_cache, dtype=np.float64)[:length]
+    grp = nh // nkv
+    out = np.zeros((nh, d))
+    bound = np.zeros((nh, d))
+    for h in range(nh):
+        g = h // grp
+        logits = K[:, g, :] @ q[h] / np.sqrt(d)
+        w = np.exp(logits - logits.max())
+        w /= w.sum()
+        out[h] = w @ V[:, g, :]
+        bound[h] = w @ np.abs(V[:, g, :])
+    return out, bound
+

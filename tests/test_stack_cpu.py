@@ -43,6 +43,19 @@ class OracleBackend:
             r = r[0::2] * r[1::2] * pair_scale
         y[: r.size] = torch.from_numpy(r.astype(np.float32))
 
+    def kv_cache(self, cfg, world):
+        return ([], [])
+
+    def attend(self, stack, layer, pos):
+        cfg, b, w = stack.cfg, stack.buf, self.world
+        nh, nkv, d = cfg.n_heads // w, cfg.n_kv // w, cfg.head_dim
+        q, k, v = oracle.rope_ref(b["qkv"].numpy(), nh, nkv, d, pos, cfg.rope_base)
+        K, V = stack.caches[layer]
+        K.append(k.astype(np.float32).astype(np.float16))
+        V.append(v.astype(np.float32).astype(np.float16))
+        att, _ = oracle.attention_ref(q.astype(np.float32), np.stack(K), np.stack(V), nh, nkv, d, pos + 1)
+        b["att"][:] = torch.from_numpy(att.reshape(-1).astype(np.float32))
+
     def gather(self, out, loc, part):
         a, b = part
         if self.world == 1:
@@ -72,31 +85,40 @@ def test_weight_bytes_match_baseline():
     assert st.CONFIGS["70b"].weight_bytes() == 43_563_171_840
 
 
-def _rank(rank, world, port, q):
+ATT_TINY = __import__("dataclasses").replace(st.CONFIGS["tiny"], attention=True, max_pos=8)
+
+
+def _rank(rank, world, port, q, attention=False):
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
     dist.init_process_group("gloo", rank=rank, world_size=world)
     try:
-        cfg = st.CONFIGS["tiny"]
+        cfg = ATT_TINY if attention else st.CONFIGS["tiny"]
         s = st.DecodeStack(cfg, OracleBackend(world), rank, world)
-        x = np.random.default_rng(0).standard_normal(cfg.hidden).astype(np.float32)
-        s.buf["x"].copy_(torch.from_numpy(x))
-        s.forward()
-        q.put((rank, s.buf["logits"].numpy().copy()))
+        outs = []
+        for t in range(3 if attention else 1):
+            x = np.random.default_rng(t).standard_normal(cfg.hidden).astype(np.float32)
+            s.buf["x"].copy_(torch.from_numpy(x))
+            s.forward()
+            outs.append(s.buf["logits"].numpy().copy())
+        q.put((rank, outs))
     finally:
         dist.destroy_process_group()
 
 
 @pytest.mark.timeout(300)
-@pytest.mark.parametrize("world", [2, 4])
-def test_gloo_ranks_match_unsharded_reference(world):
-    cfg = st.CONFIGS["tiny"]
-    x = np.random.default_rng(0).standard_normal(cfg.hidden).astype(np.float32)
-    ref = st.reference_logits(cfg, x)
+@pytest.mark.parametrize("world,attention", [(2, False), (4, False), (2, True)])
+def test_gloo_ranks_match_unsharded_reference(world, attention):
+    """Sharded ranks against the unsharded reference; with attention, three tokens in a row
+    (each rank attends over its own heads' caches, the attention outputs gathered for o)."""
+    cfg = ATT_TINY if attention else st.CONFIGS["tiny"]
+    cache = {}
+    refs = [st.reference_logits(cfg, np.random.default_rng(t).standard_normal(cfg.hidden).astype(np.float32),
+                                cache=cache) for t in range(3 if attention else 1)]
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
-    port = 29500 + os.getpid() % 1000 + 7 * world
-    procs = [ctx.Process(target=_rank, args=(r, world, port, q)) for r in range(world)]
+    port = 29500 + os.getpid() % 1000 + 7 * world + (3 if attention else 0)
+    procs = [ctx.Process(target=_rank, args=(r, world, port, q, attention)) for r in range(world)]
     for p in procs:
         p.start()
     out = dict(q.get(timeout=240) for _ in procs)
@@ -104,8 +126,9 @@ def test_gloo_ranks_match_unsharded_reference(world):
         p.join(timeout=60)
         assert p.exitcode == 0
     for r in range(world):
-        np.testing.assert_allclose(out[r], ref, rtol=1e-4, atol=1e-4 * np.abs(ref).max())
-        np.testing.assert_array_equal(out[0], out[r])
+        for t, ref in enumerate(refs):
+            np.testing.assert_allclose(out[r][t], ref, rtol=1e-4, atol=1e-4 * np.abs(ref).max())
+            np.testing.assert_array_equal(out[0][t], out[r][t])
 
 
 def test_single_rank_oracle_backend_matches_reference():
