@@ -1561,6 +1561,9 @@ __global__ void __launch_bounds__((kMaxWarps + 1) * 32, 1)
     s_zero = 0;
   }
   for (uint32_t j = 0; j < p.njobs; ++j) {
+    // thread 0 has read the previous job's counters from s_sync for its signal before anyone
+    // overwrites them
+    if (j) named_barrier(1, nthr);
     // the job's fields into shared memory, a word per consumer thread
     static_assert(sizeof(JobArgs) % 4 == 0 && sizeof(ChainSync) % 4 == 0, "word copies");
     constexpr uint32_t kJobWords = sizeof(JobArgs) / 4, kSyncWords = sizeof(ChainSync) / 4;

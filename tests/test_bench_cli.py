@@ -48,7 +48,7 @@ def test_stack_reference_arm_has_the_gpu_arms_config():
     from kernite_b200 import stack as st
 
     args = bench.parse_args(["--steps", "3"])
-    assert d["config"] == bench.stack_config(args, st.CONFIGS["70b"], 1, True)
+    assert d["config"] == bench.stack_config(args, st.CONFIGS["70b"], 1, args.exchange == "chain")
     assert "l2" in d["config"] and d["cpu_baseline"]["cores"] >= 1
 
 

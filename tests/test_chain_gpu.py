@@ -165,3 +165,36 @@ def test_chain_rejects_mixed_types_and_bad_arguments(kernels):
     j.npush, j.push_rows = 2, 16  # push targets missing
     with pytest.raises(kb.Error):
         kernels.matvec_chain([j], mem.data_ptr())
+
+
+def test_chain_pushing_to_its_own_full_vectors_over_steps(kernels):
+    """The exchange form of a chain on one GPU (npush 1: outputs pushed to this GPU's own full
+    vectors, counted with system-scope releases, waited for with system-scope acquires), three
+    jobs a launch over four steps, against lone launches."""
+    h, f = 4096, 11008
+    Wqkv, Wo, Wgu = _weights(kernels, 4, 3 * h, h, 11), _weights(kernels, 4, h, h, 12), _weights(kernels, 4, 2 * f, h, 13)
+    mem = torch.zeros(4, dtype=torch.int64, device="cuda")
+    ep, c = mem.data_ptr(), mem.data_ptr() + 8
+    loc = [torch.zeros(n, device="cuda") for n in (3 * h, h, f)]
+    full = [torch.zeros(n, device="cuda") for n in (h, h, f)]
+    r = [torch.zeros(n, device="cuda") for n in (3 * h, h, f)]
+    x = torch.zeros(h, device="cuda")
+    s = 1.0 / math.sqrt(f)
+    jobs = [_job(4, loc[0], Wqkv, x, 3 * h, h, rmsnorm=True),
+            _job(4, loc[1], Wo, full[0], h, h, wait=c, target=h),
+            _job(4, loc[2], Wgu, full[1], 2 * f, h, wait=c + 8, target=h, pair_scale=s)]
+    for i, (j, n) in enumerate(zip(jobs, (h, h, f))):
+        j.npush, j.push_rows = 1, n
+        j.push_y[0] = full[i].data_ptr()
+        j.counter[0] = c + 8 * i
+    for step in range(4):
+        x.copy_(torch.from_numpy(np.random.default_rng(50 + step).standard_normal(h).astype(np.float32)))
+        kernels.epoch_advance(ep)
+        kernels.matvec_chain(jobs, ep)
+        kernels.matvec(4, r[0], Wqkv, x, 3 * h, h, prologue=kb.PROLOGUE_RMSNORM, eps=1e-6)
+        kernels.matvec(4, r[1], Wo, r[0], h, h)
+        kernels.matvec(4, r[2], Wgu, r[1], 2 * f, h, epilogue=kb.EPILOGUE_PAIR_PRODUCT, pair_scale=s)
+        torch.cuda.synchronize()
+        kernels.device_error()
+        assert torch.equal(full[0], r[0][:h]) and torch.equal(full[1], r[1]) and torch.equal(full[2], r[2]), step
+    assert mem.tolist() == [4, 4 * h, 4 * h, 4 * f]
