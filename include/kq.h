@@ -56,8 +56,10 @@ enum {
 
 /* Quantisation types, GGML's type numbers. */
 enum { KQ_TYPE_Q4_K = 12, KQ_TYPE_Q5_K = 13, KQ_TYPE_Q6_K = 14 };
-/* Types the library decodes but does not multiply yet (kq_dequant_* only; kq_matvec answers
- * KQ_E_INVALID). */
+/* More types: decoded (kq_dequant_*) and multiplied by kq_matvec at batch 1 without prologue or
+ * epilogue, on the CUDA cores (k * 4 bytes of x must fit in shared memory). Q2_K: 84-byte blocks
+ * of 256; Q3_K: 110-byte blocks of 256 (rows 2-byte aligned); Q8_0: 34-byte blocks of 32 (a row
+ * of k weights is k / 32 blocks, k a multiple of 256). W 16-byte aligned for all. */
 enum { KQ_TYPE_Q8_0 = 8, KQ_TYPE_Q2_K = 10, KQ_TYPE_Q3_K = 11 };
 
 /* What a matvec does to x before the product, and to each output after it. */

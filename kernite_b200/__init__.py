@@ -34,9 +34,9 @@ KQ_E_COMM = 1004
 TYPE_Q4_K = 12
 TYPE_Q5_K = 13
 TYPE_Q6_K = 14
-TYPE_Q8_0 = 8   # decode only (no matvec yet)
-TYPE_Q2_K = 10  # decode only
-TYPE_Q3_K = 11  # decode only
+TYPE_Q8_0 = 8   # batch-1 matvec on the CUDA cores
+TYPE_Q2_K = 10  # batch-1 matvec on the CUDA cores
+TYPE_Q3_K = 11  # batch-1 matvec on the CUDA cores
 PROLOGUE_NONE = 0
 PROLOGUE_RMSNORM = 1
 EPILOGUE_NONE = 0
@@ -323,7 +323,7 @@ class Kernels:
                eps: float = 0.0, pair_scale: float = 1.0, flags: int = 0, stream=None) -> None:
         """The general matvec (``kq_matvec``); qtype is 4/5/6 or TYPE_Q4_K/TYPE_Q5_K/TYPE_Q6_K
         (Q5_K at batch 1 only)."""
-        t = {4: TYPE_Q4_K, 5: TYPE_Q5_K, 6: TYPE_Q6_K}.get(qtype, qtype)
+        t = {2: TYPE_Q2_K, 3: TYPE_Q3_K, 4: TYPE_Q4_K, 5: TYPE_Q5_K, 6: TYPE_Q6_K, 8: TYPE_Q8_0}.get(qtype, qtype)
         d = KqMatvecDesc(type=t, rows=rows, k=k, batch=batch, y=_addr(y), w=_addr(w), x=_addr(x),
                          ldx=ldx, ldy=ldy, prologue=prologue, epilogue=epilogue, eps=eps,
                          pair_scale=pair_scale, flags=flags, reserved=0)
@@ -335,7 +335,7 @@ class Kernels:
                     flags: int = 0, stream=None) -> None:
         """``kq_matvec_host``: x and y are host arrays (torch CPU tensors, pinned for asynchronous
         copies, or numpy arrays), w is on the device; synchronise ``stream`` before reading y."""
-        t = {4: TYPE_Q4_K, 5: TYPE_Q5_K, 6: TYPE_Q6_K}.get(qtype, qtype)
+        t = {2: TYPE_Q2_K, 3: TYPE_Q3_K, 4: TYPE_Q4_K, 5: TYPE_Q5_K, 6: TYPE_Q6_K, 8: TYPE_Q8_0}.get(qtype, qtype)
         d = KqMatvecDesc(type=t, rows=rows, k=k, batch=batch, y=0, w=_addr(w), x=0, ldx=ldx,
                          ldy=ldy, prologue=prologue, epilogue=epilogue, eps=eps,
                          pair_scale=pair_scale, flags=flags, reserved=0)
@@ -366,7 +366,7 @@ class Kernels:
                     pair_scale: float = 1.0, flags: int = 0, stream=None) -> None:
         """Batch-1 matvec whose epilogue also stores rows [0, push.push_rows) into every rank's
         full vector and counts them there (``kq_matvec_push``)."""
-        t = {4: TYPE_Q4_K, 5: TYPE_Q5_K, 6: TYPE_Q6_K}.get(qtype, qtype)
+        t = {2: TYPE_Q2_K, 3: TYPE_Q3_K, 4: TYPE_Q4_K, 5: TYPE_Q5_K, 6: TYPE_Q6_K, 8: TYPE_Q8_0}.get(qtype, qtype)
         d = KqMatvecDesc(type=t, rows=rows, k=k, batch=1, y=_addr(y), w=_addr(w), x=_addr(x),
                          ldx=0, ldy=0, prologue=prologue, epilogue=epilogue, eps=eps,
                          pair_scale=pair_scale, flags=flags, reserved=0)
@@ -383,7 +383,7 @@ class Kernels:
                     pair_scale: float = 1.0, flags: int = 0) -> "KqLaunch":
         """``kq_matvec_plan``: the warp-MMA launch of this matvec, unlaunched (a function of
         :func:`module_image`, its grid, block, shared memory and parameter bytes)."""
-        t = {4: TYPE_Q4_K, 5: TYPE_Q5_K, 6: TYPE_Q6_K}.get(qtype, qtype)
+        t = {2: TYPE_Q2_K, 3: TYPE_Q3_K, 4: TYPE_Q4_K, 5: TYPE_Q5_K, 6: TYPE_Q6_K, 8: TYPE_Q8_0}.get(qtype, qtype)
         d = KqMatvecDesc(type=t, rows=rows, k=k, batch=batch, y=_addr(y), w=_addr(w), x=_addr(x),
                          ldx=0, ldy=0, prologue=prologue, epilogue=epilogue, eps=eps,
                          pair_scale=pair_scale, flags=flags, reserved=0)

@@ -119,6 +119,7 @@ int kq_ctx_create(int device, kq_ctx** out) {
   if (rc == KQ_OK) rc = kq::mma_prepare(ctx);
   if (rc == KQ_OK) rc = kq::warpmma_prepare(ctx);
   if (rc == KQ_OK) rc = kq::aux_prepare(ctx);
+  if (rc == KQ_OK) rc = kq::types_prepare(ctx);
   if (rc != KQ_OK) {
     cudaFree(ctx->scratch);
     cudaFree(ctx->err);

@@ -70,6 +70,8 @@ int warpmma_chain(kq_ctx* ctx, const kq_chain_job* jobs, uint32_t njobs, uint64_
 int epoch_advance(kq_ctx* ctx, uint64_t epoch, cudaStream_t stream);
 
 int aux_prepare(kq_ctx* ctx);
+int types_prepare(kq_ctx* ctx);
+int types_matvec(kq_ctx* ctx, const kq_matvec_desc& d, cudaStream_t stream);
 int wait_counter(kq_ctx* ctx, uint64_t counter, uint64_t epoch, uint64_t mul, uint64_t add,
                  cudaStream_t s);
 int dequant(kq_ctx* ctx, int type, uint64_t out, uint64_t w, uint64_t nblocks, cudaStream_t s);

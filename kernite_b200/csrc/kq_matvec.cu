@@ -650,6 +650,10 @@ int check_desc(const kq_matvec_desc& d, const char* call) {
 
 int matvec(kq_ctx* ctx, const kq_matvec_desc& d, cudaStream_t stream, const kq_push_desc* push) {
   const char* call = push ? "kq_matvec_push" : "kq_matvec";
+  if (d.type == KQ_TYPE_Q2_K || d.type == KQ_TYPE_Q3_K || d.type == KQ_TYPE_Q8_0) {
+    if (push) return fail(KQ_E_UNSUPPORTED, call, "the push exchange serves Q4_K, Q5_K and Q6_K");
+    return types_matvec(ctx, d, stream);
+  }
   const int rc = check_desc(d, call);
   if (rc) return rc;
   const int qt = d.type == KQ_TYPE_Q4_K ? 4 : d.type == KQ_TYPE_Q5_K ? 5 : 6;
