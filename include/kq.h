@@ -277,10 +277,28 @@ typedef struct kq_push_desc {
     uint64_t wait_counter; /* 0, or this rank's counter for x (u64) */
     uint64_t epoch;        /* address of this rank's token counter (u64), read on the device */
     uint64_t wait_mul, wait_add;
+    /* KQ_PUSH_TAGGED (warp-MMA kernel): full vectors are tagged, 8 bytes an element (the f32
+     * value in the low word, a u32 tag in the high word, stored together in one 8-byte store), so
+     * a reader needs no counter and no fence: it reads x (when wait_counter is nonzero, or always
+     * with KQ_PUSH_TAGGED_X) waiting, bounded, on each element until its tag equals
+     * (*epoch - 1) * wait_mul + wait_add (mod 2^32), and the outputs go to y[p] (tagged, element
+     * index = output index) with the tag (*epoch - 1) * push_mul + push_add; counter[] unused.
+     * Tags of 0 never match (they are what zeroed memory holds): make every tag at least 1. */
+    uint32_t flags;
+    uint32_t reserved;
+    uint64_t push_mul, push_add;
 } kq_push_desc;
+enum { KQ_PUSH_TAGGED = 1u << 0, KQ_PUSH_TAGGED_X = 1u << 1 };
 
 int kq_matvec_push(kq_ctx* ctx, const kq_matvec_desc* desc, const kq_push_desc* push,
                    kq_stream stream);
+
+/* dst[i] = the value of tagged element i of src (0 <= i < n), once its tag equals
+ * (*epoch - 1) * wait_mul + wait_add (mod 2^32): bounded waits, stream-ordered; the last vector of
+ * a step (the logits) into plain f32 for the caller. A wait that gives up sets the device error
+ * word and the element is copied as it is. */
+int kq_tagged_unpack(kq_ctx* ctx, uint64_t dst, uint64_t src, uint64_t n, uint64_t epoch,
+                     uint64_t wait_mul, uint64_t wait_add, kq_stream stream);
 
 /* Stream-ordered wait (one thread, bounded, acquire) until *counter >= (*epoch - 1) * wait_mul +
  * wait_add, for a caller that reads a pushed full vector with its own code (the last one of a

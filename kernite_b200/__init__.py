@@ -65,7 +65,7 @@ EXPORTS = (
     "kq_matvec_push", "kq_wait_counter", "kq_matvec_chain", "kq_epoch_advance", "kq_peer_alloc", "kq_peer_open", "kq_peer_close", "kq_peer_free",
     "kq_gguf_open", "kq_gguf_close", "kq_gguf_tensor_count", "kq_gguf_tensor_at", "kq_gguf_find",
     "kq_gguf_meta_int", "kq_gguf_meta_str", "kq_module_image", "kq_matvec_plan",
-    "kq_rope_append", "kq_attention_decode", "kq_attention_workspace",
+    "kq_rope_append", "kq_attention_decode", "kq_attention_workspace", "kq_tagged_unpack",
 )
 
 
@@ -104,7 +104,13 @@ class KqPushDesc(ctypes.Structure):
         ("y", ctypes.c_uint64 * 8), ("counter", ctypes.c_uint64 * 8),
         ("wait_counter", ctypes.c_uint64), ("epoch", ctypes.c_uint64),
         ("wait_mul", ctypes.c_uint64), ("wait_add", ctypes.c_uint64),
+        ("flags", ctypes.c_uint32), ("reserved", ctypes.c_uint32),
+        ("push_mul", ctypes.c_uint64), ("push_add", ctypes.c_uint64),
     ]
+
+
+PUSH_TAGGED = 1
+PUSH_TAGGED_X = 2
 
 
 class KqLaunch(ctypes.Structure):
@@ -162,6 +168,7 @@ def lib() -> ctypes.CDLL:
     L.kq_matvec_q4k_noalloc.argtypes = [u64, u64, u64, u32, u32, u32, vp]
     L.kq_matvec_push.argtypes = [vp, ctypes.POINTER(KqMatvecDesc), ctypes.POINTER(KqPushDesc), vp]
     L.kq_wait_counter.argtypes = [vp, u64, u64, u64, u64, vp]
+    L.kq_tagged_unpack.argtypes = [vp, u64, u64, u64, u64, u64, u64, vp]
     L.kq_matvec_chain.argtypes = [vp, ctypes.POINTER(KqChainJob), u32, u64, vp]
     L.kq_module_image.argtypes = [ctypes.POINTER(vp), ctypes.POINTER(ctypes.c_size_t)]
     L.kq_rope_append.argtypes = [vp, u64, u64, u64, u64, u32, u32, u32, u32, ctypes.c_double, vp]
@@ -424,6 +431,12 @@ class Kernels:
     def epoch_advance(self, epoch: int, stream=None) -> None:
         """``*epoch += 1`` on the stream: the start of a step for the chains after it."""
         _check(lib().kq_epoch_advance(self._ctx, epoch, _stream(stream)), "kq_epoch_advance")
+
+    def tagged_unpack(self, dst, src, n: int, epoch: int, wait_mul: int, wait_add: int, stream=None) -> None:
+        """``kq_tagged_unpack``: the values of a tagged full vector into plain f32, once every
+        element carries this step's tag."""
+        _check(lib().kq_tagged_unpack(self._ctx, _addr(dst), _addr(src), n, epoch, wait_mul, wait_add,
+                                      _stream(stream)), "kq_tagged_unpack")
 
     def peer_alloc(self, nbytes: int) -> tuple[int, bytes]:
         """Zeroed device memory other GPUs can map; returns (address, 64-byte IPC handle)."""

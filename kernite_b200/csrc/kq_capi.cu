@@ -402,6 +402,15 @@ int kq_epoch_advance(kq_ctx* ctx, uint64_t epoch, kq_stream stream) {
   return kq::epoch_advance(ctx, epoch, static_cast<cudaStream_t>(stream));
 }
 
+int kq_tagged_unpack(kq_ctx* ctx, uint64_t dst, uint64_t src, uint64_t n, uint64_t epoch,
+                     uint64_t wait_mul, uint64_t wait_add, kq_stream stream) {
+  if (!ctx) return fail(KQ_E_INVALID, "kq_tagged_unpack", "null ctx");
+  kq::DeviceScope scope;
+  int rc = scope.enter(ctx);
+  if (rc) return rc;
+  return kq::tagged_unpack(ctx, dst, src, n, epoch, wait_mul, wait_add, static_cast<cudaStream_t>(stream));
+}
+
 int kq_wait_counter(kq_ctx* ctx, uint64_t counter, uint64_t epoch, uint64_t wait_mul,
                     uint64_t wait_add, kq_stream stream) {
   if (!ctx) return fail(KQ_E_INVALID, "kq_wait_counter", "null ctx");

@@ -46,6 +46,15 @@ __device__ __forceinline__ unsigned long long ld_acquire_sys(const unsigned long
   return v;
 }
 
+// This GPU's step counter, written by an earlier kernel on the stream: after pdl_wait() (or a
+// kernel boundary) its value is visible, so a relaxed GPU-scope load will do (an acquire at
+// system scope costs microseconds on the critical path of every CTA).
+__device__ __forceinline__ unsigned long long ld_epoch(const unsigned long long* p) {
+  unsigned long long v;
+  asm volatile("ld.relaxed.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+
 // Waits (acquire, system scope) until *cnt >= (*epoch - 1) * mul + add: the arrival count other
 // GPUs add to after storing into this GPU's memory. Gives up after kWaitBudgetNs, at once when
 // an earlier wait already failed (so one missing rank costs one budget, not one per launch), and
@@ -53,7 +62,7 @@ __device__ __forceinline__ unsigned long long ld_acquire_sys(const unsigned long
 __device__ __forceinline__ bool wait_count(unsigned* err, const unsigned long long* cnt,
                                            const unsigned long long* epoch, uint64_t mul,
                                            uint64_t add) {
-  const unsigned long long target = (ld_acquire_sys(epoch) - 1ull) * mul + add;
+  const unsigned long long target = (ld_epoch(epoch) - 1ull) * mul + add;
   if (ld_acquire_sys(cnt) >= target) return true;
   bool ok = false;
   if (!(err && *reinterpret_cast<volatile unsigned*>(err))) {

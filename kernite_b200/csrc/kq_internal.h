@@ -62,6 +62,8 @@ int warpmma_prepare(kq_ctx* ctx);
 bool warpmma_supports(const kq_matvec_desc& d);
 int warpmma_matvec(kq_ctx* ctx, const kq_matvec_desc& d, uint64_t ldx, uint64_t ldy,
                    cudaStream_t stream);
+int tagged_unpack(kq_ctx* ctx, uint64_t dst, uint64_t src, uint64_t n, uint64_t epoch, uint64_t mul,
+                  uint64_t add, cudaStream_t stream);
 int warpmma_plan_launch(kq_ctx* ctx, const kq_matvec_desc& d, kq_launch& out);
 int warpmma_push(kq_ctx* ctx, const kq_matvec_desc& d, const kq_push_desc& push, uint64_t ldx,
                  uint64_t ldy, cudaStream_t stream);

@@ -667,8 +667,15 @@ int matvec(kq_ctx* ctx, const kq_matvec_desc& d, cudaStream_t stream, const kq_p
       return fail(KQ_E_INVALID, call,
                   "the push exchange serves batch 1 on the warp-MMA or CUDA-core kernel");
     if (push->npush > 8) return fail(KQ_E_INVALID, call, "npush must be 0..8");
+    const bool tagged = (push->flags & KQ_PUSH_TAGGED) != 0;
+    if (push->flags & ~uint32_t(KQ_PUSH_TAGGED | KQ_PUSH_TAGGED_X))
+      return fail(KQ_E_INVALID, call, "unknown push flags");
+    if ((push->flags & KQ_PUSH_TAGGED_X) && !tagged)
+      return fail(KQ_E_INVALID, call, "KQ_PUSH_TAGGED_X goes with KQ_PUSH_TAGGED");
+    if (tagged && (d.flags & KQ_FLAG_CUDA_CORES))
+      return fail(KQ_E_UNSUPPORTED, call, "tagged pushes run on the warp-MMA kernel");
     for (uint32_t p = 0; p < push->npush; ++p)
-      if (!push->y[p] || !push->counter[p] || push->y[p] % 4 || push->counter[p] % 8)
+      if (!push->y[p] || (tagged ? push->y[p] % 8 : (!push->counter[p] || push->y[p] % 4 || push->counter[p] % 8)))
         return fail(KQ_E_INVALID, call, "push target " + std::to_string(p) + " is null or misaligned");
     if (push->wait_counter && (!push->epoch || push->wait_counter % 8 || push->epoch % 8))
       return fail(KQ_E_INVALID, call, "wait_counter needs an 8-byte aligned epoch and counter");

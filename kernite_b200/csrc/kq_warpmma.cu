@@ -131,6 +131,10 @@ struct ChainSync {
   // after its outputs are stored, each CTA adds its output count (pushed outputs when npush > 0)
   // to counter[p] for p < max(npush, 1); null counter[0]: no count
   unsigned long long* counter[kChainMaxRanks];
+  // 1: push_y[p] are tagged vectors (8 bytes an element: the f32 value, then the tag of this
+  // launch's outputs, WarpMmaShared::tag_out) and no counter is added to
+  uint32_t tagged;
+  uint32_t reserved;
 };
 
 // What one matvec has of its own when several share a launch's layout: its matrix, vectors and
@@ -158,7 +162,8 @@ struct ChainParams {
 struct PushArgs {
   ChainSync y;
   const unsigned long long* epoch;
-  uint64_t wait_mul, wait_add;
+  uint64_t wait_mul, wait_add;  // the counter's target, or with tagged x the tag x carries
+  uint64_t push_mul, push_add;  // the tag of the outputs (tagged pushes)
 };
 
 // The parts of shared memory that are not in the dynamic layout.
@@ -166,7 +171,23 @@ struct WarpMmaShared {
   int failed;
   double sq[kMaxWarps][8];  // [consumer warp][vector] sums of squares of x
   float ns[8];              // per vector: the RMS-norm factor (1 without norm)
+  uint32_t tag_x, tag_out;  // tagged exchange: the tag x's elements must carry; the outputs' tag
 };
+
+// 8 bytes of a tagged vector: the f32 value (low word) and its tag (high word), one aligned 8-byte
+// load (so value and tag come from the same store), cached in L2 only: other GPUs' stores into
+// this GPU's memory land in its L2, so a repeated load sees them, and the L1 (not coherent) is
+// bypassed. (A system-scope load takes a slower path; the tag, not the load's scope, is what
+// says the value is this step's.)
+__device__ __forceinline__ unsigned long long ld_tagged(const unsigned long long* p) {
+  unsigned long long v;
+  asm volatile("ld.global.cg.u64 %0, [%1];" : "=l"(v) : "l"(p));
+  return v;
+}
+
+__device__ __forceinline__ void st_tagged(float* p, float v, uint32_t tag) {
+  asm volatile("st.global.v2.u32 [%0], {%1, %2};" ::"l"(p), "r"(__float_as_uint(v)), "r"(tag) : "memory");
+}
 
 // ---------------------------------------------------------------- register-level helpers
 
@@ -713,7 +734,7 @@ __device__ __forceinline__ bool produce_job(const WarpMmaArgs& a, const JobArgs&
 // then every tile of this CTA's rows from the ring, MMAs, and the outputs. s, phase: the ring
 // position, carried from one matvec of a launch to the next. sync: null for a lone matvec; for a
 // job of a chain, where its outputs are also pushed.
-template <int QT, int NT, bool HILO, bool I8>
+template <int QT, int NT, bool HILO, bool I8, bool TX = false>
 __device__ __forceinline__ void consume_job(const WarpMmaArgs& a, const JobArgs& mj,
                                             const ChainSync* sync, uint8_t* base,
                                             WarpMmaShared& sh, uint32_t& s, uint32_t& phase,
@@ -764,14 +785,61 @@ __device__ __forceinline__ void consume_job(const WarpMmaArgs& a, const JobArgs&
     const uint32_t nxb = a.nb * B;
     for (uint32_t xb0 = warp; xb0 < nxb; xb0 += 4 * nw) {
       float v[4][8];
+      bool tags_ok = true;
+      const uint32_t want_tag = TX ? sh.tag_x : 0u;
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
         const uint32_t xb = xb0 + j * nw;
         if (xb < nxb) {
           const uint32_t b = xb / a.nb, kb = xb - b * a.nb;
-          const float* src = mj.x + b * a.ldx + kb * kQK + lane;
+          if constexpr (TX) {
+            // a tagged vector (batch 1): the values, and whether every tag is this step's; the
+            // loads of all four x-blocks are in flight together, the stale ones reloaded after
+            const unsigned long long* src =
+                reinterpret_cast<const unsigned long long*>(mj.x) + kb * kQK + lane;
 #pragma unroll
-          for (int r = 0; r < 8; ++r) v[j][r] = __ldcg(src + 32 * r);
+            for (int r = 0; r < 8; ++r) {
+              const unsigned long long w = ld_tagged(src + 32 * r);
+              v[j][r] = __uint_as_float(static_cast<uint32_t>(w));
+              tags_ok &= static_cast<uint32_t>(w >> 32) == want_tag;
+            }
+          } else {
+            const float* src = mj.x + b * a.ldx + kb * kQK + lane;
+#pragma unroll
+            for (int r = 0; r < 8; ++r) v[j][r] = __ldcg(src + 32 * r);
+          }
+        }
+      }
+      if constexpr (TX) {
+        if (!tags_ok) {
+          // some element is not this step's yet: wait for each, bounded (at once when this CTA
+          // or an earlier launch already gave up)
+          // (unrolled, so that v stays in registers; the code is cold)
+          uint64_t t0 = 0;
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            const uint32_t xb = xb0 + j * nw;
+            if (xb >= nxb) break;
+            const unsigned long long* src =
+                reinterpret_cast<const unsigned long long*>(mj.x) + (xb % a.nb) * kQK + lane;
+#pragma unroll
+            for (int r = 0; r < 8; ++r) {
+              unsigned long long w = ld_tagged(src + 32 * r);
+              while (static_cast<uint32_t>(w >> 32) != want_tag) {
+                if (*reinterpret_cast<volatile int*>(&s_failed) ||
+                    (a.err && *reinterpret_cast<volatile unsigned*>(a.err)))
+                  break;
+                if (t0 == 0) t0 = globaltimer();
+                if (globaltimer() - t0 > kWaitBudgetNs) {
+                  report_error(a.err, kErrWaitPeer);
+                  s_failed = 1;
+                  break;
+                }
+                w = ld_tagged(src + 32 * r);
+              }
+              v[j][r] = __uint_as_float(static_cast<uint32_t>(w));
+            }
+          }
         }
       }
 #pragma unroll
@@ -1151,8 +1219,14 @@ __device__ __forceinline__ void consume_job(const WarpMmaArgs& a, const JobArgs&
         }
         mj.y[b * a.ldy + out] = v0;
         // a chain job's pushed outputs also go to every rank's full vector (batch 1)
-        if (sync && out < sync->push_rows)
-          for (uint32_t rk = 0; rk < sync->npush; ++rk) sync->push_y[rk][out] = v0;
+        if (sync && out < sync->push_rows) {
+          if (sync->tagged) {
+            const uint32_t tag = sh.tag_out;
+            for (uint32_t rk = 0; rk < sync->npush; ++rk) st_tagged(sync->push_y[rk] + 2 * out, v0, tag);
+          } else {
+            for (uint32_t rk = 0; rk < sync->npush; ++rk) sync->push_y[rk][out] = v0;
+          }
+        }
       }
       named_barrier(1, nthr);
       bi = 0;
@@ -1459,13 +1533,16 @@ __device__ __forceinline__ bool wait_at_least(unsigned* err, const unsigned long
   return true;
 }
 
-// A lone batch-1 integer matvec that also does a row-sharded stack's exchange: before its
-// consumers read x (a full vector other GPUs push into), one thread waits (bounded, acquire,
-// system scope) until this rank's counter for x reaches this step's target; its flushes store the
-// outputs below push_rows into every rank's full vector; once they are stored, the CTA adds their
-// count to every rank's counter (release, system scope). The producer streams the weights from
+// A lone batch-1 integer matvec that also does a row-sharded stack's exchange. Counted form
+// (TX false, q.y.tagged 0): before its consumers read x (a full vector other GPUs push into), one
+// thread waits (bounded, acquire, system scope) until this rank's counter for x reaches this
+// step's target; its flushes store the outputs below push_rows into every rank's full vector; once
+// they are stored, the CTA adds their count to every rank's counter (release, system scope).
+// Tagged form (q.y.tagged 1; TX: x is tagged too): the outputs go out as 8-byte (value, tag)
+// stores and x's elements are each waited for until they carry this step's tag, so there is no
+// fence, no counter and no round trip on the critical path. The producer streams the weights from
 // the start, the wait overlapping the first tiles' copies.
-template <int QT>
+template <int QT, bool TX>
 __global__ void __launch_bounds__((kMaxWarps + 1) * 32, 1)
     warpmma_push_kernel(const WarpMmaArgs a, const __grid_constant__ PushArgs q) {
   extern __shared__ __align__(128) uint8_t smem[];
@@ -1483,14 +1560,20 @@ __global__ void __launch_bounds__((kMaxWarps + 1) * 32, 1)
   }
   pdl_wait();
   const uint32_t nthr = a.nw * 32;
-  if (q.y.wait_cnt) {
-    if (threadIdx.x == 0) {
-      const unsigned long long target = (ld_acquire_sys(q.epoch) - 1ull) * q.wait_mul + q.wait_add;
+  if (threadIdx.x == 0) {
+    if (q.y.tagged || TX) {
+      const unsigned long long e = ld_epoch(q.epoch) - 1ull;
+      sh.tag_x = static_cast<uint32_t>(e * q.wait_mul + q.wait_add);
+      sh.tag_out = static_cast<uint32_t>(e * q.push_mul + q.push_add);
+    }
+    if (!TX && q.y.wait_cnt) {
+      const unsigned long long target = (ld_epoch(q.epoch) - 1ull) * q.wait_mul + q.wait_add;
       if (!wait_at_least(a.err, q.y.wait_cnt, target, true, &sh.failed)) sh.failed = 1;
     }
-    named_barrier(1, nthr);
   }
-  consume_job<QT, 1, false, true>(a, v, &q.y, base, sh, s, phase);
+  named_barrier(1, nthr);
+  consume_job<QT, 1, false, true, TX>(a, v, &q.y, base, sh, s, phase);
+  if (q.y.tagged) return;  // no counts
   named_barrier(1, nthr);  // every consumer's outputs are stored
   if (threadIdx.x == 0 && q.y.npush) {
     uint32_t r_begin, r_end;
@@ -1498,6 +1581,27 @@ __global__ void __launch_bounds__((kMaxWarps + 1) * 32, 1)
     const uint32_t o0 = r_begin / v.row_unit, o1 = r_end / v.row_unit, pr = q.y.push_rows;
     const uint32_t pushed = o1 > pr ? (o0 < pr ? pr - o0 : 0u) : o1 - o0;
     for (uint32_t rk = 0; rk < q.y.npush; ++rk) red_release_sys(q.y.counter[rk], pushed);
+  }
+}
+
+// dst[i] = the value of tagged element i of src once it carries the tag (bounded waits).
+__global__ void tagged_unpack_kernel(float* dst, const unsigned long long* src, uint64_t n,
+                                     const unsigned long long* epoch, uint64_t mul, uint64_t add,
+                                     unsigned* err) {
+  const uint32_t want = static_cast<uint32_t>((ld_epoch(epoch) - 1ull) * mul + add);
+  for (uint64_t i = blockIdx.x * uint64_t(blockDim.x) + threadIdx.x; i < n; i += uint64_t(gridDim.x) * blockDim.x) {
+    unsigned long long w = ld_tagged(src + i);
+    if (static_cast<uint32_t>(w >> 32) != want) {
+      const uint64_t t0 = globaltimer();
+      while (static_cast<uint32_t>(w >> 32) != want) {
+        if ((err && *reinterpret_cast<volatile unsigned*>(err)) || globaltimer() - t0 > kWaitBudgetNs) {
+          report_error(err, kErrWaitPeer);
+          break;
+        }
+        w = ld_tagged(src + i);
+      }
+    }
+    dst[i] = __uint_as_float(static_cast<uint32_t>(w));
   }
 }
 
@@ -1557,7 +1661,7 @@ __global__ void __launch_bounds__((kMaxWarps + 1) * 32, 1)
   __shared__ unsigned long long s_epoch;
   __shared__ uint32_t s_zero;
   if (threadIdx.x == 0) {
-    s_epoch = p.sync[0].wait_cnt || p.njobs > 1 ? ld_acquire_sys(p.epoch) : 0ull;
+    s_epoch = p.sync[0].wait_cnt || p.njobs > 1 ? ld_epoch(p.epoch) : 0ull;
     s_zero = 0;
   }
   for (uint32_t j = 0; j < p.njobs; ++j) {
@@ -1614,11 +1718,15 @@ const Variant kVariants[] = {variant<4, 1, true>(), variant<4, 2, true>(), varia
                              variant<6, 1, false>(), variant<4, 1, false, true>(),
                              variant<6, 1, false, true>(), variant<5, 1, false, true>()};
 
-// The push kernel of a type (Q4_K, Q5_K or Q6_K).
-const void* push_fn(uint32_t type) {
-  return type == KQ_TYPE_Q4_K   ? reinterpret_cast<const void*>(&warpmma_push_kernel<4>)
-         : type == KQ_TYPE_Q5_K ? reinterpret_cast<const void*>(&warpmma_push_kernel<5>)
-                                : reinterpret_cast<const void*>(&warpmma_push_kernel<6>);
+// The push kernel of a type (Q4_K, Q5_K or Q6_K), x plain or tagged.
+const void* push_fn(uint32_t type, bool tx) {
+  if (tx)
+    return type == KQ_TYPE_Q4_K   ? reinterpret_cast<const void*>(&warpmma_push_kernel<4, true>)
+           : type == KQ_TYPE_Q5_K ? reinterpret_cast<const void*>(&warpmma_push_kernel<5, true>)
+                                  : reinterpret_cast<const void*>(&warpmma_push_kernel<6, true>);
+  return type == KQ_TYPE_Q4_K   ? reinterpret_cast<const void*>(&warpmma_push_kernel<4, false>)
+         : type == KQ_TYPE_Q5_K ? reinterpret_cast<const void*>(&warpmma_push_kernel<5, false>)
+                                : reinterpret_cast<const void*>(&warpmma_push_kernel<6, false>);
 }
 
 // The chain kernel of a type (Q4_K, Q5_K or Q6_K).
@@ -1642,8 +1750,10 @@ int warpmma_prepare(kq_ctx* ctx) {
     cudaError_t e =
         cudaFuncSetAttribute(chain_fn(t), cudaFuncAttributeMaxDynamicSharedMemorySize, ctx->max_smem);
     if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute", "warp-MMA chain kernel");
-    e = cudaFuncSetAttribute(push_fn(t), cudaFuncAttributeMaxDynamicSharedMemorySize, ctx->max_smem);
-    if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute", "warp-MMA push kernel");
+    for (bool tx : {false, true}) {
+      e = cudaFuncSetAttribute(push_fn(t, tx), cudaFuncAttributeMaxDynamicSharedMemorySize, ctx->max_smem);
+      if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute", "warp-MMA push kernel");
+    }
   }
   return KQ_OK;
 }
@@ -1909,6 +2019,22 @@ int warpmma_plan_launch(kq_ctx* ctx, const kq_matvec_desc& d, kq_launch& out) {
   return KQ_OK;
 }
 
+int tagged_unpack(kq_ctx* ctx, uint64_t dst, uint64_t src, uint64_t n, uint64_t epoch, uint64_t mul,
+                  uint64_t add, cudaStream_t stream) {
+  const char* call = "kq_tagged_unpack";
+  if (!dst || !src || !epoch || dst % 4 || src % 8 || epoch % 8)
+    return fail(KQ_E_INVALID, call, "dst 4-byte, src and epoch 8-byte aligned, non-null");
+  if (n == 0) return KQ_OK;
+  const uint32_t grid = static_cast<uint32_t>(std::min<uint64_t>((n + 255) / 256, uint64_t(ctx->sm_count) * 2));
+  tagged_unpack_kernel<<<grid, 256, 0, stream>>>(reinterpret_cast<float*>(dst),
+                                                 reinterpret_cast<const unsigned long long*>(src), n,
+                                                 reinterpret_cast<const unsigned long long*>(epoch),
+                                                 mul, add, ctx->err);
+  const cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "cudaLaunchKernel", call);
+  return KQ_OK;
+}
+
 int warpmma_push(kq_ctx* ctx, const kq_matvec_desc& d, const kq_push_desc& push, uint64_t ldx,
                  uint64_t ldy, cudaStream_t stream) {
   const char* call = "kq_matvec_push";
@@ -1928,6 +2054,21 @@ int warpmma_push(kq_ctx* ctx, const kq_matvec_desc& d, const kq_push_desc& push,
   q.epoch = reinterpret_cast<const unsigned long long*>(push.epoch);
   q.wait_mul = push.wait_mul;
   q.wait_add = push.wait_add;
+  const bool tagged = (push.flags & KQ_PUSH_TAGGED) != 0;
+  const bool tx = tagged && (push.wait_counter || (push.flags & KQ_PUSH_TAGGED_X));
+  q.y.tagged = tagged ? 1u : 0u;
+  q.push_mul = push.push_mul;
+  q.push_add = push.push_add;
+  if (tagged) {
+    q.y.wait_cnt = nullptr;
+    for (uint32_t r = 0; r < kChainMaxRanks; ++r) q.y.counter[r] = nullptr;
+    if (!push.epoch || push.epoch % 8)
+      return fail(KQ_E_INVALID, call, "tagged pushes need an 8-byte aligned epoch");
+    for (uint32_t r = 0; r < push.npush; ++r)
+      if (push.y[r] % 8) return fail(KQ_E_INVALID, call, "tagged vectors must be 8-byte aligned");
+    if (tx && (d.x % 16 || d.ldx > d.k))
+      return fail(KQ_E_INVALID, call, "a tagged x must be 16-byte aligned, batch 1");
+  }
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(plan.grid);
   cfg.blockDim = dim3(plan.block);
@@ -1939,7 +2080,7 @@ int warpmma_push(kq_ctx* ctx, const kq_matvec_desc& d, const kq_push_desc& push,
   cfg.attrs = attr;
   cfg.numAttrs = (d.flags & KQ_FLAG_NO_PDL) ? 0 : 1;
   void* params[] = {&plan.args, &q};
-  const cudaError_t e = cudaLaunchKernelExC(&cfg, push_fn(d.type), params);
+  const cudaError_t e = cudaLaunchKernelExC(&cfg, push_fn(d.type, tx), params);
   if (e != cudaSuccess)
     return cuda_fail(e, "cudaLaunchKernelExC", "warp-MMA push " + shape(plan.grid, plan.block, plan.smem));
   return KQ_OK;

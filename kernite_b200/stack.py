@@ -133,25 +133,23 @@ def full_sizes(cfg: StackConfig) -> dict[str, int]:
 
 
 def push_layout(cfg: StackConfig) -> tuple[dict[str, int], int]:
-    """Byte offsets in a rank's exchange region (identical on every rank): one u64 arrival
-    counter per full vector and the token counter ("epoch") in the first 256 bytes, then the
-    full vectors, each 256-byte aligned. Returns (offsets, total bytes)."""
-    off = {f"cnt_{k}": 8 * i for i, k in enumerate(FULL_KEYS)}
-    off["epoch"] = 8 * len(FULL_KEYS)
+    """Byte offsets in a rank's exchange region (identical on every rank): the token counter
+    ("epoch") in the first 256 bytes, then the tagged full vectors (8 bytes an element: the f32
+    value and its tag), each 256-byte aligned. Returns (offsets, total bytes)."""
+    off = {"epoch": 0}
     pos = 256
     for k, n in full_sizes(cfg).items():
         off[k] = pos
-        pos += (n * 4 + 255) // 256 * 256
+        pos += (n * 8 + 255) // 256 * 256
     return off, pos
 
 
-def push_target(cfg: StackConfig, key: str, occurrence: int) -> tuple[int, int]:
-    """(wait_mul, wait_add) for reading full vector `key` after its occurrence-th write of a
-    token (1-based): every write adds the vector's length to its counter, so before token t's
-    occurrence o the counter must reach (t - 1) * writes_per_token * len + o * len."""
-    n = full_sizes(cfg)[key]
-    per_token = (1 if key == "logits" else cfg.layers) * n
-    return per_token, occurrence * n
+def push_tag(cfg: StackConfig, key: str, occurrence: int) -> tuple[int, int]:
+    """(mul, add) of the tag of full vector `key`'s occurrence-th write of a token (1-based): the
+    tag is (t - 1) * writes_per_token + occurrence in token t, so every write of a vector carries
+    a tag no earlier write carried, and no tag is 0 (zeroed memory's)."""
+    per_token = 1 if key == "logits" else cfg.layers
+    return per_token, occurrence
 
 
 @dataclass(frozen=True)
@@ -289,7 +287,7 @@ class DecodeStack:
             raise ValueError(f"the key/value caches hold {cfg.max_pos} positions")
         for layer, lw in enumerate(self.weights):
             be.matvec(lw["qkv"], sh["qkv"], b["qkv"], x, rmsnorm=layer > 0, eps=cfg.eps,
-                      out=("q", sh["qkv"].gathered), src=("xd", layer) if layer > 0 else None)
+                      out=("q", sh["qkv"].gathered, layer + 1), src=("xd", layer) if layer > 0 else None)
             if cfg.attention:
                 # this rank's heads: rotate, append to the layer's cache, attend; o's input is
                 # every rank's attention output
@@ -297,21 +295,22 @@ class DecodeStack:
                 be.gather(b["q"], b["att"], (0, sh["qkv"].gathered[1]))
             else:
                 be.gather(b["q"], b["qkv"], sh["qkv"].gathered)
-            be.matvec(lw["o"], sh["o"], b["o_loc"], b["q"], out=("o", sh["o"].gathered), src=("q", layer + 1))
+            be.matvec(lw["o"], sh["o"], b["o_loc"], b["q"], out=("o", sh["o"].gathered, layer + 1),
+                      src=("q", layer + 1))
             be.gather(b["o"], b["o_loc"], sh["o"].gathered)
             be.matvec(lw["gate_up"], sh["gate_up"], b["a_loc"], b["o"], pair_scale=1.0 / math.sqrt(cfg.ffn),
-                      out=("a", sh["gate_up"].gathered), src=("o", layer + 1))
+                      out=("a", sh["gate_up"].gathered, layer + 1), src=("o", layer + 1))
             be.gather(b["a"], b["a_loc"], sh["gate_up"].gathered)
-            be.matvec(lw["down"], sh["down"], b["x_loc"], b["a"], out=("xd", sh["down"].gathered),
+            be.matvec(lw["down"], sh["down"], b["x_loc"], b["a"], out=("xd", sh["down"].gathered, layer + 1),
                       src=("a", layer + 1))
             be.gather(b["xd"], b["x_loc"], sh["down"].gathered)
             x = b["xd"]
         be.matvec(self.head, sh["head"], b["l_loc"], x, rmsnorm=True, eps=cfg.eps,
-                  out=("logits", sh["head"].gathered), src=("xd", cfg.layers) if self.cfg.layers else None)
+                  out=("logits", sh["head"].gathered, 1), src=("xd", cfg.layers) if self.cfg.layers else None)
         be.gather(b["logits"], b["l_loc"], sh["head"].gathered)
         end = getattr(be, "end_token", None)
         if end:
-            end()
+            end(self)
         self.pos += 1
 
 
@@ -359,13 +358,13 @@ class CudaBackend:
             return self._chain_vectors(cfg, rank, world)
         if not self.push:
             return {k: self.vector(n) for k, n in full_sizes(cfg).items()}
+        # the exchange's full vectors are tagged, in the region every rank maps; the host-side
+        # vectors are plain ones (the logits unpacked into buf['logits'] at the end of a token)
         self.cfg = cfg
         self.off, nbytes = push_layout(cfg)
         self._map_region(nbytes, rank, world)
-        ptr = self.region
-        view = lambda off, n, t="<f4": torch.as_tensor(kb.DeviceArray(ptr + off, n, t), device="cuda")
-        self.epoch = view(self.off["epoch"], 1, "<i8")
-        return {k: view(self.off[k], n) for k, n in full_sizes(cfg).items()}
+        self.epoch = torch.as_tensor(kb.DeviceArray(self.region + self.off["epoch"], 1, "<i8"), device="cuda")
+        return {k: self.vector(n) for k, n in full_sizes(cfg).items()}
 
     # ---------------------------------------------------------------- chains
     def _chain_vectors(self, cfg: StackConfig, rank: int, world: int):
@@ -443,11 +442,13 @@ class CudaBackend:
             with self.torch.cuda.stream(self.stream) if self.stream is not None else _null():
                 self.epoch.add_(1)
 
-    def end_token(self) -> None:
-        # the other ranks' logits rows are the one push no later launch waits for
+    def end_token(self, stack: "DecodeStack" = None) -> None:
+        # the logits are the one pushed vector no later launch reads: wait for every rank's rows
+        # and unpack them into the plain logits
         if self.push:
-            self.k.wait_counter(self.region + self.off["cnt_logits"], self.region + self.off["epoch"],
-                                *push_target(self.cfg, "logits", 1), stream=self.stream)
+            self.k.tagged_unpack(stack.buf["logits"], self.region + self.off["logits"], self.cfg.vocab,
+                                 self.region + self.off["epoch"], *push_tag(self.cfg, "logits", 1),
+                                 stream=self.stream)
             self.launches += 1
 
     def close(self) -> None:
@@ -511,18 +512,21 @@ class CudaBackend:
                   pair_scale=pair_scale if pair_scale is not None else 1.0,
                   flags=kb.FLAG_WEIGHTS_STATIC | self.flags, stream=self.stream)
         if self.push and out is not None:
-            key, (a, b) = out
+            key, (a, b), occ_out = out
             d = kb.KqPushDesc()
             d.npush = self.world
             d.push_rows = b - a
+            d.flags = kb.PUSH_TAGGED
+            d.epoch = self.region + self.off["epoch"]
+            d.push_mul, d.push_add = push_tag(self.cfg, key, occ_out)
             for p, base in enumerate(self.peers):
-                d.y[p] = base + self.off[key] + 4 * self.rank * (b - a)
-                d.counter[p] = base + self.off[f"cnt_{key}"]
+                d.y[p] = base + self.off[key] + 8 * self.rank * (b - a)
             if src is not None:
+                # x is this rank's tagged copy of the full vector
                 skey, occ = src
-                d.wait_counter = self.region + self.off[f"cnt_{skey}"]
-                d.epoch = self.region + self.off["epoch"]
-                d.wait_mul, d.wait_add = push_target(self.cfg, skey, occ)
+                d.flags |= kb.PUSH_TAGGED_X
+                d.wait_mul, d.wait_add = push_tag(self.cfg, skey, occ)
+                x = self.region + self.off[skey]
             self.k.matvec_push(shard.qtype, y, W, x, shard.rows, shard.k, d, **kw)
         else:
             self.k.matvec(shard.qtype, y, W, x, shard.rows, shard.k, 1, **kw)

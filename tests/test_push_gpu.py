@@ -91,3 +91,57 @@ def test_cuda_core_push_agrees_within_the_bound(kernels):
     ref, bound = oracle.matvec_ref(6, W.cpu().numpy(), xh[None, :], k, 0, rows)
     assert (np.abs(full.cpu().numpy() - ref[0]) <= 1e-3 * bound[0]).all()
     assert torch.equal(full, y) and int(mem[0]) == rows
+
+
+def test_tagged_push_chain_of_two_over_steps(kernels):
+    """The tagged exchange on one GPU: the first launch pushes its outputs as (value, tag) pairs
+    into a tagged full vector, the second reads that vector waiting on each element's tag and
+    pushes its own; kq_tagged_unpack gives the plain values. Three steps: the tags advance with
+    the epoch, so a step never reads the previous step's elements."""
+    h = 4096
+    W1, W2 = _w(kernels, 4, h, h, 21), _w(kernels, 6, h, h, 22)
+    mem = torch.zeros(1, dtype=torch.int64, device="cuda")  # epoch
+    ep = mem.data_ptr()
+    x = torch.zeros(h, device="cuda")
+    y1, y2 = torch.zeros(h, device="cuda"), torch.zeros(h, device="cuda")
+    t1 = torch.zeros(2 * h, device="cuda")  # tagged: 8 bytes an element
+    t2 = torch.zeros(2 * h, device="cuda")
+    plain = torch.full((h,), float("nan"), device="cuda")
+    r1, r2 = torch.zeros(h, device="cuda"), torch.zeros(h, device="cuda")
+    for step in range(1, 4):
+        x.copy_(torch.from_numpy(np.random.default_rng(step).standard_normal(h).astype(np.float32)))
+        mem[0] += 1
+        d1 = _desc(1, h, t1.data_ptr(), 0, epoch=ep)
+        d1.flags, d1.push_mul, d1.push_add = kb.PUSH_TAGGED, 1, 1
+        kernels.matvec_push(4, y1, W1, x, h, h, d1)
+        d2 = _desc(1, h, t2.data_ptr(), 0, epoch=ep, mul=1, add=1)
+        d2.flags, d2.push_mul, d2.push_add = kb.PUSH_TAGGED | kb.PUSH_TAGGED_X, 1, 1
+        kernels.matvec_push(6, y2, W2, t1, h, h, d2, prologue=kb.PROLOGUE_RMSNORM, eps=1e-6)
+        kernels.tagged_unpack(plain, t2, h, ep, 1, 1)
+        kernels.matvec(4, r1, W1, x, h, h, 1)
+        kernels.matvec(6, r2, W2, r1, h, h, 1, prologue=kb.PROLOGUE_RMSNORM, eps=1e-6)
+        torch.cuda.synchronize()
+        kernels.device_error()
+        assert torch.equal(y1, r1) and torch.equal(y2, r2) and torch.equal(plain, r2), step
+        tags = t2.view(torch.int32)[1::2]
+        assert (tags == step).all()
+
+
+def test_tagged_read_of_a_stale_vector_gives_up(kernels):
+    """x whose elements carry an old tag: the bounded wait runs out (about 2 s), the error word
+    says so, and the context keeps working."""
+    h = 1024
+    W = _w(kernels, 4, 256, h, 23)
+    mem = torch.ones(1, dtype=torch.int64, device="cuda")
+    stale = torch.zeros(2 * h, device="cuda")  # tags 0: never this step's
+    y = torch.zeros(256, device="cuda")
+    d = _desc(1, 256, torch.zeros(512, device="cuda").data_ptr(), 0, epoch=mem.data_ptr(), mul=1, add=1)
+    d.flags, d.push_mul, d.push_add = kb.PUSH_TAGGED | kb.PUSH_TAGGED_X, 1, 1
+    kernels.matvec_push(4, y, W, stale, 256, h, d)
+    torch.cuda.synchronize()
+    with pytest.raises(kb.Error) as e:
+        kernels.device_error()
+    assert e.value.code == kb.KQ_E_DEVICE
+    kernels.matvec(4, y, W, torch.zeros(h, device="cuda"), 256, h, 1)
+    torch.cuda.synchronize()
+    kernels.device_error()

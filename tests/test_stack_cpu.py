@@ -143,16 +143,22 @@ def test_single_rank_oracle_backend_matches_reference():
     assert math.isfinite(float(np.abs(ref).max()))
 
 
-def test_push_layout_and_targets():
+def test_push_layout_and_tags():
     cfg = st.CONFIGS["70b"]
     off, total = st.push_layout(cfg)
-    assert off["epoch"] == 40 and all(off[k] % 256 == 0 for k in st.FULL_KEYS)
-    assert total >= off["logits"] + 4 * cfg.vocab
-    # q is written once per layer: before token t's layer-L read the counter holds
-    # (t-1) * layers * h from earlier tokens and (L+1) * h from this one
-    mul, add = st.push_target(cfg, "q", 3)
-    assert mul == cfg.layers * cfg.hidden and add == 3 * cfg.hidden
-    assert st.push_target(cfg, "logits", 1) == (cfg.vocab, cfg.vocab)
+    assert off["epoch"] == 0 and all(off[k] % 256 == 0 and off[k] >= 256 for k in st.FULL_KEYS)
+    ends = sorted((off[k], off[k] + 8 * n) for k, n in st.full_sizes(cfg).items())
+    assert all(ends[i][1] <= ends[i + 1][0] for i in range(len(ends) - 1)) and ends[-1][1] <= total
+    # every write of a vector over several tokens carries its own tag, never 0, and the reader of
+    # each write expects exactly the writer's tag
+    for key in st.FULL_KEYS:
+        writes = 1 if key == "logits" else cfg.layers
+        tags = []
+        for t in range(1, 4):
+            for occ in range(1, writes + 1):
+                mul, add = st.push_tag(cfg, key, occ)
+                tags.append((t - 1) * mul + add)
+        assert len(set(tags)) == len(tags) and min(tags) >= 1
 
 
 # ---------------------------------------------------------------- chains (host logic)
