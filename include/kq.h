@@ -287,6 +287,14 @@ typedef struct kq_push_desc {
     uint32_t flags;
     uint32_t reserved;
     uint64_t push_mul, push_add;
+    /* Tagged pushes only. ksplit (0 or 1: none; 2, 4, 8): the CTAs share each row range ksplit
+     * ways, each multiplying its share of the row's K-tiles (at most the tiles a row has), and
+     * push their partial sums into slot (CTA mod ksplit) of the destination vectors, slots
+     * npush * push_rows elements apart (no product epilogue; y is not written). x_slots (0 or 1:
+     * none; up to 8): x is such a vector, its slots k elements apart, and every element of x is
+     * the sum of its slots, added in slot order. For row-sharded stacks whose shards are too
+     * short to give every CTA a row range of its own. */
+    uint32_t ksplit, x_slots;
 } kq_push_desc;
 enum { KQ_PUSH_TAGGED = 1u << 0, KQ_PUSH_TAGGED_X = 1u << 1 };
 

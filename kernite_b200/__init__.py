@@ -106,6 +106,7 @@ class KqPushDesc(ctypes.Structure):
         ("wait_mul", ctypes.c_uint64), ("wait_add", ctypes.c_uint64),
         ("flags", ctypes.c_uint32), ("reserved", ctypes.c_uint32),
         ("push_mul", ctypes.c_uint64), ("push_add", ctypes.c_uint64),
+        ("ksplit", ctypes.c_uint32), ("x_slots", ctypes.c_uint32),
     ]
 
 

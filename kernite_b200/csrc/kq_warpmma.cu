@@ -113,6 +113,7 @@ struct WarpMmaArgs {
   uint32_t fixed_blocks; // 1: integer path with warp w fixed to block w (whole 16-byte rows)
   uint32_t ncol;         // B columns in use per n-tile
   uint32_t fb;           // bands of partial rows kept before a flush
+  uint32_t ksplit;       // CTAs sharing each row range, each its 1/ksplit of the K-tiles (1: none)
   uint32_t row_unit, prologue, epilogue, flags;
   float eps, pair_scale;
 };
@@ -134,7 +135,7 @@ struct ChainSync {
   // 1: push_y[p] are tagged vectors (8 bytes an element: the f32 value, then the tag of this
   // launch's outputs, WarpMmaShared::tag_out) and no counter is added to
   uint32_t tagged;
-  uint32_t reserved;
+  uint32_t out_slot;  // tagged, split K: elements between the slots of the push_y vectors
 };
 
 // What one matvec has of its own when several share a launch's layout: its matrix, vectors and
@@ -164,6 +165,8 @@ struct PushArgs {
   const unsigned long long* epoch;
   uint64_t wait_mul, wait_add;  // the counter's target, or with tagged x the tag x carries
   uint64_t push_mul, push_add;  // the tag of the outputs (tagged pushes)
+  uint32_t x_slots;             // tagged x: its split-K slots (1: none)
+  uint32_t reserved;
 };
 
 // The parts of shared memory that are not in the dynamic layout.
@@ -172,6 +175,7 @@ struct WarpMmaShared {
   double sq[kMaxWarps][8];  // [consumer warp][vector] sums of squares of x
   float ns[8];              // per vector: the RMS-norm factor (1 without norm)
   uint32_t tag_x, tag_out;  // tagged exchange: the tag x's elements must carry; the outputs' tag
+  uint32_t x_slots;         // tagged x: the slots (split-K parts, K elements apart) summed per element
 };
 
 // 8 bytes of a tagged vector: the f32 value (low word) and its tag (high word), one aligned 8-byte
@@ -595,10 +599,21 @@ __device__ __forceinline__ void q4i8_block(uint32_t ag, uint32_t ah, uint32_t c,
 
 // The rows [r_begin, r_end) of a matvec that this CTA streams and multiplies: a contiguous share
 // of whole output units (pairs of rows for the product epilogues).
-__device__ __forceinline__ void cta_rows(const JobArgs& v, uint32_t& r_begin, uint32_t& r_end) {
+// With split K (ksplit > 1), CTAs ksplit * g .. ksplit * g + ksplit - 1 share row range g.
+__device__ __forceinline__ void cta_rows(const JobArgs& v, uint32_t ksplit, uint32_t& r_begin,
+                                         uint32_t& r_end) {
   const uint64_t units = v.rows / v.row_unit;
-  r_begin = static_cast<uint32_t>(units * blockIdx.x / gridDim.x) * v.row_unit;
-  r_end = static_cast<uint32_t>(units * (blockIdx.x + 1) / gridDim.x) * v.row_unit;
+  const uint32_t groups = gridDim.x / ksplit, g = blockIdx.x / ksplit;
+  r_begin = static_cast<uint32_t>(units * g / groups) * v.row_unit;
+  r_end = static_cast<uint32_t>(units * (g + 1) / groups) * v.row_unit;
+}
+
+// The K-tiles [kt_lo, kt_hi) of each band that this CTA takes: all, or with split K its share.
+__device__ __forceinline__ void cta_ktiles(uint32_t nkt, uint32_t ksplit, uint32_t& kt_lo,
+                                           uint32_t& kt_hi) {
+  const uint32_t part = blockIdx.x % ksplit;
+  kt_lo = part * nkt / ksplit;
+  kt_hi = (part + 1) * nkt / ksplit;
 }
 
 // A lone launch's per-matvec fields.
@@ -645,9 +660,12 @@ __device__ __forceinline__ bool produce_job(const WarpMmaArgs& a, const JobArgs&
   const uint32_t lane = threadIdx.x & 31;
   const uint64_t RB = a.row_bytes;
   uint32_t r_begin, r_end;
-  cta_rows(v, r_begin, r_end);
+  cta_rows(v, a.ksplit, r_begin, r_end);
   const uint32_t nbands = (r_end - r_begin + kTileRows - 1) / kTileRows;
-  const uint32_t ntiles = nbands * a.nkt;
+  uint32_t kt_lo, kt_hi;
+  cta_ktiles(a.nkt, a.ksplit, kt_lo, kt_hi);
+  const uint32_t nktc = kt_hi - kt_lo;
+  const uint32_t ntiles = nbands * nktc;
   const uint64_t pol = policy_evict_first();
   const uint64_t end_floor = v.total_bytes & ~uint64_t(15);
   for (uint32_t t = 0; t < ntiles; ++t) {
@@ -664,7 +682,7 @@ __device__ __forceinline__ bool produce_job(const WarpMmaArgs& a, const JobArgs&
       }
       if (!__shfl_sync(0xffffffffu, ok, 0)) return false;
     }
-    const uint32_t band = t / a.nkt, kt = t % a.nkt;
+    const uint32_t band = t / nktc, kt = kt_lo + t % nktc;
     const uint32_t r0 = r_begin + band * kTileRows;
     const uint32_t r1 = min(r0 + kTileRows, r_end);
     const uint32_t slot = ring_s + s * a.slot_bytes;
@@ -734,13 +752,15 @@ __device__ __forceinline__ bool produce_job(const WarpMmaArgs& a, const JobArgs&
 // then every tile of this CTA's rows from the ring, MMAs, and the outputs. s, phase: the ring
 // position, carried from one matvec of a launch to the next. sync: null for a lone matvec; for a
 // job of a chain, where its outputs are also pushed.
-template <int QT, int NT, bool HILO, bool I8, bool TX = false>
+template <int QT, int NT, bool HILO, bool I8, int TXS = 0>
 __device__ __forceinline__ void consume_job(const WarpMmaArgs& a, const JobArgs& mj,
                                             const ChainSync* sync, uint8_t* base,
                                             WarpMmaShared& sh, uint32_t& s, uint32_t& phase,
                                             uint32_t opq = 0) {
   constexpr uint32_t kBlk = QT == 4 ? kQ4KBytes : QT == 5 ? kQ5KBytes : kQ6KBytes;
   constexpr int kTarget = QT == 4 ? 10 : 14;  // x is scaled so that max |x| < 2^kTarget
+  // x: plain f32 (TXS 0), a tagged vector (1), or a tagged vector of several split-K slots (2)
+  constexpr bool TX = TXS > 0;
   int& s_failed = sh.failed;
   double (&s_sq)[kMaxWarps][8] = sh.sq;
   float (&s_ns)[8] = sh.ns;
@@ -762,7 +782,7 @@ __device__ __forceinline__ void consume_job(const WarpMmaArgs& a, const JobArgs&
   const uint32_t warp = tx >> 5, lane = tx & 31;
   const uint64_t RB = a.row_bytes;
   uint32_t r_begin, r_end;
-  cta_rows(mj, r_begin, r_end);
+  cta_rows(mj, a.ksplit, r_begin, r_end);
   const uint32_t nbands = (r_end - r_begin + kTileRows - 1) / kTileRows;
 
   const uint32_t tid = tx;  // 0 .. nthr-1
@@ -787,6 +807,8 @@ __device__ __forceinline__ void consume_job(const WarpMmaArgs& a, const JobArgs&
       float v[4][8];
       bool tags_ok = true;
       const uint32_t want_tag = TX ? sh.tag_x : 0u;
+      const uint32_t x_slots = TXS == 2 ? sh.x_slots : 1u;
+      const uint64_t kx = uint64_t(a.nb) * kQK;  // elements between x's slots
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
         const uint32_t xb = xb0 + j * nw;
@@ -802,6 +824,16 @@ __device__ __forceinline__ void consume_job(const WarpMmaArgs& a, const JobArgs&
               const unsigned long long w = ld_tagged(src + 32 * r);
               v[j][r] = __uint_as_float(static_cast<uint32_t>(w));
               tags_ok &= static_cast<uint32_t>(w >> 32) == want_tag;
+            }
+            // split-K slots 1.. of the writer: added in slot order (the same sum on every rank)
+            if constexpr (TXS == 2)
+            for (uint32_t sl = 1; sl < x_slots; ++sl) {
+#pragma unroll
+              for (int r = 0; r < 8; ++r) {
+                const unsigned long long w = ld_tagged(src + uint64_t(sl) * kx + 32 * r);
+                v[j][r] += __uint_as_float(static_cast<uint32_t>(w));
+                tags_ok &= static_cast<uint32_t>(w >> 32) == want_tag;
+              }
             }
           } else {
             const float* src = mj.x + b * a.ldx + kb * kQK + lane;
@@ -824,20 +856,25 @@ __device__ __forceinline__ void consume_job(const WarpMmaArgs& a, const JobArgs&
                 reinterpret_cast<const unsigned long long*>(mj.x) + (xb % a.nb) * kQK + lane;
 #pragma unroll
             for (int r = 0; r < 8; ++r) {
-              unsigned long long w = ld_tagged(src + 32 * r);
-              while (static_cast<uint32_t>(w >> 32) != want_tag) {
-                if (*reinterpret_cast<volatile int*>(&s_failed) ||
-                    (a.err && *reinterpret_cast<volatile unsigned*>(a.err)))
-                  break;
-                if (t0 == 0) t0 = globaltimer();
-                if (globaltimer() - t0 > kWaitBudgetNs) {
-                  report_error(a.err, kErrWaitPeer);
-                  s_failed = 1;
-                  break;
+              float sum = 0.f;
+              for (uint32_t sl = 0; sl < x_slots; ++sl) {
+                const unsigned long long* at = src + uint64_t(sl) * kx + 32 * r;
+                unsigned long long w = ld_tagged(at);
+                while (static_cast<uint32_t>(w >> 32) != want_tag) {
+                  if (*reinterpret_cast<volatile int*>(&s_failed) ||
+                      (a.err && *reinterpret_cast<volatile unsigned*>(a.err)))
+                    break;
+                  if (t0 == 0) t0 = globaltimer();
+                  if (globaltimer() - t0 > kWaitBudgetNs) {
+                    report_error(a.err, kErrWaitPeer);
+                    s_failed = 1;
+                    break;
+                  }
+                  w = ld_tagged(at);
                 }
-                w = ld_tagged(src + 32 * r);
+                sum = sl ? sum + __uint_as_float(static_cast<uint32_t>(w)) : __uint_as_float(static_cast<uint32_t>(w));
               }
-              v[j][r] = __uint_as_float(static_cast<uint32_t>(w));
+              v[j][r] = sum;
             }
           }
         }
@@ -1217,12 +1254,15 @@ __device__ __forceinline__ void consume_job(const WarpMmaArgs& a, const JobArgs&
           v0 = pair_value(v0, v1, mj.epilogue, mj.pair_scale);
           out = row / 2;
         }
-        mj.y[b * a.ldy + out] = v0;
+        // (with split K, v0 is this CTA's part of the sum over K: it goes to its own slot of
+        // every rank's tagged vector only, where the reader adds the slots up)
+        if (a.ksplit == 1) mj.y[b * a.ldy + out] = v0;
         // a chain job's pushed outputs also go to every rank's full vector (batch 1)
         if (sync && out < sync->push_rows) {
           if (sync->tagged) {
             const uint32_t tag = sh.tag_out;
-            for (uint32_t rk = 0; rk < sync->npush; ++rk) st_tagged(sync->push_y[rk] + 2 * out, v0, tag);
+            const uint32_t at = (blockIdx.x % a.ksplit) * sync->out_slot + out;
+            for (uint32_t rk = 0; rk < sync->npush; ++rk) st_tagged(sync->push_y[rk] + 2 * at, v0, tag);
           } else {
             for (uint32_t rk = 0; rk < sync->npush; ++rk) sync->push_y[rk][out] = v0;
           }
@@ -1343,10 +1383,12 @@ __device__ __forceinline__ void consume_job(const WarpMmaArgs& a, const JobArgs&
   // Unit j (super-block kc0 + j) of a tile goes to warp (rot + j) mod nw, rot advancing by the
   // tile's super-block count, so the warps take turns when there are more warps than blocks.
   uint32_t bi = 0, rot = 0;
+  uint32_t kt_lo, kt_hi;
+  cta_ktiles(nkt, a.ksplit, kt_lo, kt_hi);
   for (uint32_t band = 0; band < nbands; ++band) {
   const uint32_t r0 = r_begin + band * kTileRows;
-  uint32_t kc0 = 0;
-  for (uint32_t kt = 0; kt < nkt; ++kt) {
+  uint32_t kc0 = kt_lo * kq + min(kt_lo, kr);
+  for (uint32_t kt = kt_lo; kt < kt_hi; ++kt) {
     const uint32_t kc1 = kc0 + kq + (kt < kr ? 1u : 0u);
     bool ok = !*reinterpret_cast<volatile int*>(&s_failed);
     if (ok && !mbar_wait(full_bar(s), phase)) {
@@ -1542,9 +1584,10 @@ __device__ __forceinline__ bool wait_at_least(unsigned* err, const unsigned long
 // stores and x's elements are each waited for until they carry this step's tag, so there is no
 // fence, no counter and no round trip on the critical path. The producer streams the weights from
 // the start, the wait overlapping the first tiles' copies.
-template <int QT, bool TX>
+template <int QT, int TXS>
 __global__ void __launch_bounds__((kMaxWarps + 1) * 32, 1)
     warpmma_push_kernel(const WarpMmaArgs a, const __grid_constant__ PushArgs q) {
+  constexpr bool TX = TXS > 0;
   extern __shared__ __align__(128) uint8_t smem[];
   __shared__ WarpMmaShared sh;
   uint8_t* base = smem_base(smem);
@@ -1565,6 +1608,7 @@ __global__ void __launch_bounds__((kMaxWarps + 1) * 32, 1)
       const unsigned long long e = ld_epoch(q.epoch) - 1ull;
       sh.tag_x = static_cast<uint32_t>(e * q.wait_mul + q.wait_add);
       sh.tag_out = static_cast<uint32_t>(e * q.push_mul + q.push_add);
+      sh.x_slots = q.x_slots;
     }
     if (!TX && q.y.wait_cnt) {
       const unsigned long long target = (ld_epoch(q.epoch) - 1ull) * q.wait_mul + q.wait_add;
@@ -1572,12 +1616,12 @@ __global__ void __launch_bounds__((kMaxWarps + 1) * 32, 1)
     }
   }
   named_barrier(1, nthr);
-  consume_job<QT, 1, false, true, TX>(a, v, &q.y, base, sh, s, phase);
+  consume_job<QT, 1, false, true, TXS>(a, v, &q.y, base, sh, s, phase);
   if (q.y.tagged) return;  // no counts
   named_barrier(1, nthr);  // every consumer's outputs are stored
   if (threadIdx.x == 0 && q.y.npush) {
     uint32_t r_begin, r_end;
-    cta_rows(v, r_begin, r_end);
+    cta_rows(v, a.ksplit, r_begin, r_end);
     const uint32_t o0 = r_begin / v.row_unit, o1 = r_end / v.row_unit, pr = q.y.push_rows;
     const uint32_t pushed = o1 > pr ? (o0 < pr ? pr - o0 : 0u) : o1 - o0;
     for (uint32_t rk = 0; rk < q.y.npush; ++rk) red_release_sys(q.y.counter[rk], pushed);
@@ -1690,7 +1734,7 @@ __global__ void __launch_bounds__((kMaxWarps + 1) * 32, 1)
     named_barrier(1, nthr);  // every consumer's outputs of job j are stored
     if (threadIdx.x == 0 && s_sync.counter[0]) {
       uint32_t r_begin, r_end;
-      cta_rows(s_job, r_begin, r_end);
+      cta_rows(s_job, a.ksplit, r_begin, r_end);
       const uint32_t o0 = r_begin / s_job.row_unit, o1 = r_end / s_job.row_unit;
       const uint32_t pr = s_sync.push_rows;
       if (s_sync.npush) {
@@ -1718,15 +1762,16 @@ const Variant kVariants[] = {variant<4, 1, true>(), variant<4, 2, true>(), varia
                              variant<6, 1, false>(), variant<4, 1, false, true>(),
                              variant<6, 1, false, true>(), variant<5, 1, false, true>()};
 
-// The push kernel of a type (Q4_K, Q5_K or Q6_K), x plain or tagged.
-const void* push_fn(uint32_t type, bool tx) {
-  if (tx)
-    return type == KQ_TYPE_Q4_K   ? reinterpret_cast<const void*>(&warpmma_push_kernel<4, true>)
-           : type == KQ_TYPE_Q5_K ? reinterpret_cast<const void*>(&warpmma_push_kernel<5, true>)
-                                  : reinterpret_cast<const void*>(&warpmma_push_kernel<6, true>);
-  return type == KQ_TYPE_Q4_K   ? reinterpret_cast<const void*>(&warpmma_push_kernel<4, false>)
-         : type == KQ_TYPE_Q5_K ? reinterpret_cast<const void*>(&warpmma_push_kernel<5, false>)
-                                : reinterpret_cast<const void*>(&warpmma_push_kernel<6, false>);
+// The push kernel of a type (Q4_K, Q5_K or Q6_K) for x plain (txs 0), tagged (1), or tagged
+// with several split-K slots (2).
+template <int TXS>
+const void* push_fn_t(uint32_t type) {
+  return type == KQ_TYPE_Q4_K   ? reinterpret_cast<const void*>(&warpmma_push_kernel<4, TXS>)
+         : type == KQ_TYPE_Q5_K ? reinterpret_cast<const void*>(&warpmma_push_kernel<5, TXS>)
+                                : reinterpret_cast<const void*>(&warpmma_push_kernel<6, TXS>);
+}
+const void* push_fn(uint32_t type, int txs) {
+  return txs == 0 ? push_fn_t<0>(type) : txs == 1 ? push_fn_t<1>(type) : push_fn_t<2>(type);
 }
 
 // The chain kernel of a type (Q4_K, Q5_K or Q6_K).
@@ -1750,8 +1795,8 @@ int warpmma_prepare(kq_ctx* ctx) {
     cudaError_t e =
         cudaFuncSetAttribute(chain_fn(t), cudaFuncAttributeMaxDynamicSharedMemorySize, ctx->max_smem);
     if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute", "warp-MMA chain kernel");
-    for (bool tx : {false, true}) {
-      e = cudaFuncSetAttribute(push_fn(t, tx), cudaFuncAttributeMaxDynamicSharedMemorySize, ctx->max_smem);
+    for (int txs : {0, 1, 2}) {
+      e = cudaFuncSetAttribute(push_fn(t, txs), cudaFuncAttributeMaxDynamicSharedMemorySize, ctx->max_smem);
       if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute", "warp-MMA push kernel");
     }
   }
@@ -1918,6 +1963,7 @@ int warpmma_plan(kq_ctx* ctx, const kq_matvec_desc& d, uint64_t ldx, uint64_t ld
   args.bars_off = args.red_off + red_bytes;
   args.ncol = ncol;
   args.fb = fb;
+  args.ksplit = 1;
   args.row_unit = d.epilogue != KQ_EPILOGUE_NONE ? 2 : 1;
   args.prologue = d.prologue;
   args.epilogue = d.epilogue;
@@ -1963,7 +2009,8 @@ bool same_layout(const WarpMmaArgs& a, const WarpMmaArgs& b) {
          a.table_off == b.table_off && a.mtable_off == b.mtable_off && a.ublk_off == b.ublk_off &&
          a.zero_off == b.zero_off && a.red_off == b.red_off && a.bars_off == b.bars_off &&
          a.row_perm == b.row_perm && a.split_tile == b.split_tile &&
-         a.fixed_blocks == b.fixed_blocks && a.ncol == b.ncol && a.fb == b.fb;
+         a.fixed_blocks == b.fixed_blocks && a.ncol == b.ncol && a.fb == b.fb &&
+         a.ksplit == b.ksplit;
 }
 
 }  // namespace
@@ -2059,6 +2106,26 @@ int warpmma_push(kq_ctx* ctx, const kq_matvec_desc& d, const kq_push_desc& push,
   q.y.tagged = tagged ? 1u : 0u;
   q.push_mul = push.push_mul;
   q.push_add = push.push_add;
+  q.x_slots = push.x_slots ? push.x_slots : 1u;
+  const uint32_t ksplit = push.ksplit ? push.ksplit : 1u;
+  if (ksplit > 1 || q.x_slots > 1) {
+    if (!tagged) return fail(KQ_E_INVALID, call, "split K and x slots go with tagged pushes");
+    if (q.x_slots > 8 || ksplit > 8 || (ksplit & (ksplit - 1)))
+      return fail(KQ_E_INVALID, call, "ksplit must be 1, 2, 4 or 8 and x_slots 1..8");
+    if (q.x_slots > 1 && !tx) return fail(KQ_E_INVALID, call, "x slots need a tagged x");
+    if (ksplit > plan.args.nkt)
+      return fail(KQ_E_INVALID, call, "ksplit " + std::to_string(ksplit) + " above the " +
+                                          std::to_string(plan.args.nkt) + " K-tiles of a row");
+    if (ksplit > 1 && d.epilogue != KQ_EPILOGUE_NONE)
+      return fail(KQ_E_INVALID, call, "split K sums its parts in the reader: no product epilogue");
+  }
+  plan.args.ksplit = ksplit;
+  q.y.out_slot = push.npush * push.push_rows;  // a slot is a whole full vector
+  if (ksplit > 1) {
+    // every row range is shared by ksplit CTAs: whole groups of them
+    const uint64_t units = d.epilogue != KQ_EPILOGUE_NONE ? d.rows / 2 : d.rows;
+    plan.grid = static_cast<uint32_t>(std::min<uint64_t>(ctx->sm_count / ksplit, units)) * ksplit;
+  }
   if (tagged) {
     q.y.wait_cnt = nullptr;
     for (uint32_t r = 0; r < kChainMaxRanks; ++r) q.y.counter[r] = nullptr;
@@ -2080,7 +2147,7 @@ int warpmma_push(kq_ctx* ctx, const kq_matvec_desc& d, const kq_push_desc& push,
   cfg.attrs = attr;
   cfg.numAttrs = (d.flags & KQ_FLAG_NO_PDL) ? 0 : 1;
   void* params[] = {&plan.args, &q};
-  const cudaError_t e = cudaLaunchKernelExC(&cfg, push_fn(d.type, tx), params);
+  const cudaError_t e = cudaLaunchKernelExC(&cfg, push_fn(d.type, !tx ? 0 : q.x_slots > 1 ? 2 : 1), params);
   if (e != cudaSuccess)
     return cuda_fail(e, "cudaLaunchKernelExC", "warp-MMA push " + shape(plan.grid, plan.block, plan.smem));
   return KQ_OK;

@@ -132,15 +132,31 @@ def full_sizes(cfg: StackConfig) -> dict[str, int]:
     return {"q": cfg.hidden, "o": cfg.hidden, "a": cfg.ffn, "xd": cfg.hidden, "logits": cfg.vocab}
 
 
-def push_layout(cfg: StackConfig) -> tuple[dict[str, int], int]:
+def push_splits(cfg: StackConfig, world: int, sm_count: int) -> dict[str, int]:
+    """Split K per pushed vector (by the vector its matvec writes): 2 where the shard has so few
+    16-row bands that half the CTAs would hold one (a CTA's time is its tiles, so two CTAs taking
+    half a band's K-tiles each halve it), the rows have two K-tiles or more (more than 16
+    super-blocks) and the outputs are plain sums (not the gate/up product); else 1."""
+    h, f = cfg.hidden, cfg.ffn
+    rows_k = {"q": (h + 2 * cfg.kv, h), "o": (h, h), "xd": (h, f)}
+    out = {}
+    for key, (rows, k) in rows_k.items():
+        bands = -(-(rows // world) // 16)
+        out[key] = 2 if world > 1 and 2 * bands <= sm_count and k // QK > 16 else 1
+    return out
+
+
+def push_layout(cfg: StackConfig, splits: dict[str, int] | None = None) -> tuple[dict[str, int], int]:
     """Byte offsets in a rank's exchange region (identical on every rank): the token counter
     ("epoch") in the first 256 bytes, then the tagged full vectors (8 bytes an element: the f32
-    value and its tag), each 256-byte aligned. Returns (offsets, total bytes)."""
+    value and its tag; a vector written with split K has that many slots of it), each 256-byte
+    aligned. Returns (offsets, total bytes)."""
+    splits = splits or {}
     off = {"epoch": 0}
     pos = 256
     for k, n in full_sizes(cfg).items():
         off[k] = pos
-        pos += (n * 8 + 255) // 256 * 256
+        pos += (splits.get(k, 1) * n * 8 + 255) // 256 * 256
     return off, pos
 
 
@@ -324,7 +340,7 @@ class CudaBackend:
     -- the same inside chains of several matvecs per launch (kq_matvec_chain)."""
 
     def __init__(self, kernels, stream=None, group=None, world: int = 1, flags: int = 0,
-                 push: bool = False, rank: int = 0, chain: bool = False):
+                 push: bool = False, rank: int = 0, chain: bool = False, split_k: bool = False):
         import torch
 
         import kernite_b200 as kb
@@ -336,6 +352,7 @@ class CudaBackend:
         self.rank = rank
         self.flags = flags
         self.chain = chain
+        self.split_k = split_k
         self.push = push and world > 1 and not chain
         self.launches = 0
         self.region = None
@@ -361,7 +378,11 @@ class CudaBackend:
         # the exchange's full vectors are tagged, in the region every rank maps; the host-side
         # vectors are plain ones (the logits unpacked into buf['logits'] at the end of a token)
         self.cfg = cfg
-        self.off, nbytes = push_layout(cfg)
+        # split K for short shards (push_splits) measured no faster on a B200 at 8-way shards
+        # (62.1 vs 62.4 us a 70B layer: the readers' two-slot loads cost what the halved tiles
+        # save), so the stack pushes unsplit; the library keeps the option (KqPushDesc.ksplit)
+        self.ksplit = push_splits(cfg, world, self.k.sm_count) if self.split_k else {}
+        self.off, nbytes = push_layout(cfg, self.ksplit)
         self._map_region(nbytes, rank, world)
         self.epoch = torch.as_tensor(kb.DeviceArray(self.region + self.off["epoch"], 1, "<i8"), device="cuda")
         return {k: self.vector(n) for k, n in full_sizes(cfg).items()}
@@ -519,13 +540,15 @@ class CudaBackend:
             d.flags = kb.PUSH_TAGGED
             d.epoch = self.region + self.off["epoch"]
             d.push_mul, d.push_add = push_tag(self.cfg, key, occ_out)
+            d.ksplit = self.ksplit.get(key, 1) if pair_scale is None else 1
             for p, base in enumerate(self.peers):
                 d.y[p] = base + self.off[key] + 8 * self.rank * (b - a)
             if src is not None:
-                # x is this rank's tagged copy of the full vector
+                # x is this rank's tagged copy of the full vector (the sum of its split-K slots)
                 skey, occ = src
                 d.flags |= kb.PUSH_TAGGED_X
                 d.wait_mul, d.wait_add = push_tag(self.cfg, skey, occ)
+                d.x_slots = self.ksplit.get(skey, 1)
                 x = self.region + self.off[skey]
             self.k.matvec_push(shard.qtype, y, W, x, shard.rows, shard.k, d, **kw)
         else:
@@ -550,7 +573,8 @@ class _null:
 
 
 def make_cuda_stack(cfg: StackConfig, kernels, rank: int = 0, world: int = 1, group=None,
-                    stream=None, flags: int = 0, push: bool = False, chain: bool = False) -> DecodeStack:
+                    stream=None, flags: int = 0, push: bool = False, chain: bool = False,
+                    split_k: bool = False) -> DecodeStack:
     if cfg.attention and (push or chain):
         raise ValueError("a stack with attention runs one launch per projection (NCCL or one rank)")
     """One rank's stack on libkq.so. The exchange between ranks (and the launches): NCCL
@@ -558,7 +582,7 @@ def make_cuda_stack(cfg: StackConfig, kernels, rank: int = 0, world: int = 1, gr
     memory (push=True, the warp-MMA kernel's push variant), or chains (chain=True: up to
     three projections per launch, outputs pushed to peer memory and ordered by counters)."""
     return DecodeStack(cfg, CudaBackend(kernels, stream=stream, group=group, world=world, flags=flags,
-                                        push=push, rank=rank, chain=chain), rank, world)
+                                        push=push, rank=rank, chain=chain, split_k=split_k), rank, world)
 
 
 # ---------------------------------------------------------------- reference (for tests)

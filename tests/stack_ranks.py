@@ -27,15 +27,15 @@ def main():
     kernels = kb.Kernels.load(local)
     ok = True
     refs = {}
-    for exchange in ("nccl", "push", "chain"):
+    for exchange in ("nccl", "push", "push-split", "chain"):
         for name, cfg in (("tiny", st.CONFIGS["tiny"]), ("70b-2", dataclasses.replace(st.CONFIGS["70b"], layers=2))):
             xs = [np.random.default_rng(3 + t).standard_normal(cfg.hidden).astype(np.float32) for t in range(3)]
             for t, x in enumerate(xs):
                 if (name, t) not in refs:
                     refs[name, t] = st.reference_logits(cfg, x)
             stream = torch.cuda.Stream()
-            s = st.make_cuda_stack(cfg, kernels, rank, world, stream=stream, push=exchange == "push",
-                                   chain=exchange == "chain")
+            s = st.make_cuda_stack(cfg, kernels, rank, world, stream=stream, push=exchange.startswith("push"),
+                                   chain=exchange == "chain", split_k=exchange == "push-split")
             s.buf["x"].copy_(torch.from_numpy(xs[0]).cuda())
             torch.cuda.synchronize()
             with torch.cuda.stream(stream):

@@ -145,3 +145,38 @@ def test_tagged_read_of_a_stale_vector_gives_up(kernels):
     kernels.matvec(4, y, W, torch.zeros(h, device="cuda"), 256, h, 1)
     torch.cuda.synchronize()
     kernels.device_error()
+
+
+def test_split_k_pushes_slots_the_reader_adds_up(kernels):
+    """Split K (ksplit 2): CTA pairs each multiply half of a row's K-tiles and push their partial
+    sums into their own slot of the tagged vector; the next launch (x_slots 2) reads every element
+    as the sum of its two slots. The slots add up to the unsplit matvec within the bound, the
+    reader's outputs are the matvec of that sum, and a second run gives the same bits."""
+    rows1, k1, rows2 = 2048, 8192, 1024
+    W1, W2 = _w(kernels, 4, rows1, k1, 31), _w(kernels, 6, rows2, rows1, 32)
+    mem = torch.ones(1, dtype=torch.int64, device="cuda")
+    ep = mem.data_ptr()
+    xh = np.random.default_rng(9).standard_normal(k1).astype(np.float32)
+    x = torch.from_numpy(xh).cuda()
+    outs = []
+    for run in range(2):
+        t1 = torch.zeros(2 * 2 * rows1, device="cuda")  # 2 slots, 8 bytes an element
+        t2 = torch.zeros(2 * rows2, device="cuda")
+        d1 = _desc(1, rows1, t1.data_ptr(), 0, epoch=ep)
+        d1.flags, d1.push_mul, d1.push_add, d1.ksplit = kb.PUSH_TAGGED, 1, 1, 2
+        kernels.matvec_push(4, torch.zeros(rows1, device="cuda"), W1, x, rows1, k1, d1)
+        d2 = _desc(1, rows2, t2.data_ptr(), 0, epoch=ep, mul=1, add=1)
+        d2.flags, d2.push_mul, d2.push_add, d2.x_slots = kb.PUSH_TAGGED | kb.PUSH_TAGGED_X, 1, 1, 2
+        y2 = torch.zeros(rows2, device="cuda")
+        kernels.matvec_push(6, y2, W2, t1, rows2, rows1, d2)
+        torch.cuda.synchronize()
+        kernels.device_error()
+        slots = t1.view(2, rows1, 2)[:, :, 0].cpu().numpy().astype(np.float64)
+        assert (t1.view(torch.int32)[1::2] == 1).all()
+        outs.append((slots.sum(0), y2.cpu().numpy()))
+    ref1, b1 = oracle.matvec_ref(4, W1.cpu().numpy(), xh[None, :], k1, 0, rows1)
+    assert (np.abs(outs[0][0] - ref1[0]) <= 1e-3 * b1[0]).all()
+    x2 = outs[0][0].astype(np.float32)
+    ref2, b2 = oracle.matvec_ref(6, W2.cpu().numpy(), x2[None, :], rows1, 0, rows2)
+    assert (np.abs(outs[0][1] - ref2[0]) <= 1e-3 * b2[0]).all()
+    assert np.array_equal(outs[0][0], outs[1][0]) and np.array_equal(outs[0][1], outs[1][1])

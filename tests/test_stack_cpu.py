@@ -143,6 +143,16 @@ def test_single_rank_oracle_backend_matches_reference():
     assert math.isfinite(float(np.abs(ref).max()))
 
 
+def test_push_splits_only_short_shards_with_several_k_tiles():
+    c70, c7 = st.CONFIGS["70b"], st.CONFIGS["7b"]
+    assert st.push_splits(c70, 1, 148) == {"q": 1, "o": 1, "xd": 1}
+    assert st.push_splits(c70, 2, 148) == {"q": 1, "o": 1, "xd": 1}
+    assert st.push_splits(c70, 8, 148) == {"q": 1, "o": 2, "xd": 2}
+    assert st.push_splits(c7, 8, 148)["o"] == 1  # k = 4096: one K-tile a row, nothing to split
+    off, total = st.push_layout(c70, st.push_splits(c70, 8, 148))
+    assert off["a"] - off["o"] >= 2 * c70.hidden * 8 and off["o"] - off["q"] >= c70.hidden * 8
+
+
 def test_push_layout_and_tags():
     cfg = st.CONFIGS["70b"]
     off, total = st.push_layout(cfg)
