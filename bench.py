@@ -113,15 +113,15 @@ def measured_peak():
         return FALLBACK_HBM_GBS, "fallback"
 
 
-def profiled_traffic(name: str):
-    """Per-launch DRAM bytes (read + write) of the dominant kernel from the committed ncu
-    summary for this workload, or None."""
+def profiled_traffic(name: str, unit: str = "launch"):
+    """DRAM bytes (read + write) per launch of the dominant kernel (per token for a stack) from
+    the committed ncu summary for this workload, or None."""
     path = os.path.join(ROOT, "profiles", f"{name}.md")
     try:
         text = open(path).read()
     except OSError:
         return None
-    m = re.search(r"traffic_bytes_per_launch:\s*([0-9]+)", text)
+    m = re.search(r"traffic_bytes_per_" + unit + r":\s*([0-9]+)", text)
     return int(m.group(1)) if m else None
 
 
@@ -760,7 +760,10 @@ def run_stack(args):
     peak, peak_kind = measured_peak()
     per_gpu_gbs = wbytes / world / (ms_tok / 1e3) / 1e9
     roofline = {"bound": "hbm", "achieved": round(per_gpu_gbs, 2), "peak": peak, "unit": "GB/s",
-                "frac": round(per_gpu_gbs / peak, 4), "traffic": profiled_traffic(args.workload),
+                "frac": round(per_gpu_gbs / peak, 4),
+                "traffic": profiled_traffic(args.workload, "token") if world == 1 and args.layers is None else None,
+                "traffic_note": "DRAM bytes per token on one GPU: 80 layers at the per-layer bytes of a "
+                                "2-layer ncu capture, plus the head (profiles/stack70b.md)",
                 "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)" if peak_kind == "measured"
                 else "fallback 6650 GB/s",
                 "note": "achieved = the stack's weight bytes per GPU per token / token time"}
