@@ -769,6 +769,9 @@ __device__ __forceinline__ void consume_job(const WarpMmaArgs& a, const JobArgs&
   const uint32_t table_s = ring_s + a.table_off;
   const uint32_t mtable_s = ring_s + a.mtable_off;
   float* ublk = reinterpret_cast<float*>(base + a.ublk_off);  // [vector][block]: 2^-shift of x
+  const uint32_t ublk_s = ring_s + a.ublk_off;
+  // (the tile loops read it, and the sums of x, with explicit shared-memory loads)
+  auto ublk_at = [&](uint32_t i) { return __uint_as_float(lds_u32(ublk_s + 4 * i)); };
   float* red = reinterpret_cast<float*>(base + a.red_off);
   uint64_t* bars = reinterpret_cast<uint64_t*>(base + a.bars_off);
   auto full_bar = [&](uint32_t s) { return smem_u32(&bars[s]); };
@@ -1198,8 +1201,8 @@ __device__ __forceinline__ void consume_job(const WarpMmaArgs& a, const JobArgs&
       tab_t[tt] = tab_on ? table_s + (kb * NT + tt) * a.ncol * kNStride + tab_lane : zero_s;
       bm_at[tt] = tab_on ? mtable_s + ((kb * NT + tt) * a.ncol + g) * 16 + 4 * c : zero_s;
     }
-    u0 = ublk[vb0c * a.nb + kb];
-    u1 = ublk[vb1 * a.nb + kb];
+    u0 = ublk_at(vb0c * a.nb + kb);
+    u1 = ublk_at(vb1 * a.nb + kb);
   };
 
   // The band is done: this warp's partial rows go to the reduction buffer; every fb bands (and
@@ -1284,7 +1287,7 @@ __device__ __forceinline__ void consume_job(const WarpMmaArgs& a, const JobArgs&
       auto fixed_loop = [&](auto cls) {
         constexpr int F = decltype(cls)::value;
         const uint32_t kb = fkb;
-        const float u0 = ublk[kb];
+        const float u0 = ublk_at(kb);
         const uint32_t tkb = table_s + (kb * 32 + 2 * c) * 24;
         const uint32_t bA = g == c ? tkb : zero_s;
         const uint32_t bB = g == c + 4 ? tkb + 8 * 24 : zero_s;
@@ -1342,12 +1345,14 @@ __device__ __forceinline__ void consume_job(const WarpMmaArgs& a, const JobArgs&
       uint32_t b0 = 0, b1 = 0, tab_t[NT], bm_at[NT];
       float2 X = make_float2(0.f, 0.f);
       if constexpr (I8) {
-        u0 = ublk[kb];
+        u0 = ublk_at(kb);
         const uint32_t tc = table_s + (kb * 32 + 8 * c) * 24;
         b0 = g == 2 * c ? tc : zero_s;
         b1 = g == 2 * c + 1 ? tc + 4 * 24 : zero_s;
-        X = *reinterpret_cast<const float2*>(reinterpret_cast<const uint8_t*>(base) +
-                                             a.mtable_off + (kb * 8 + 2 * c) * 4);
+        {
+          const uint2 xs = lds_v2(mtable_s + (kb * 8 + 2 * c) * 4);
+          X = make_float2(__uint_as_float(xs.x), __uint_as_float(xs.y));
+        }
       } else {
         q4f16_consts(kb, tab_t, bm_at, u0, u1);
       }
@@ -1421,13 +1426,13 @@ __device__ __forceinline__ void consume_job(const WarpMmaArgs& a, const JobArgs&
         // Integer MMAs (batch 1). Column n of the MMA is sub-block n; the A registers of a step
         // hold 4 + 4 quants of one sub-block (8 consecutive elements of it per thread), B the
         // three limbs of the same 8 elements of x, read by the 4 lanes of the column's group.
-        const float u0 = ublk[kb];
+        const float u0 = ublk_at(kb);
         if constexpr (QT == 4 || QT == 5) {
           const uint32_t tc = table_s + (kb * 32 + 8 * c) * 24;
           const uint32_t b0 = g == 2 * c ? tc : zero_s;
           const uint32_t b1 = g == 2 * c + 1 ? tc + 4 * 24 : zero_s;
-          const float2 X = *reinterpret_cast<const float2*>(
-              reinterpret_cast<const uint8_t*>(base) + a.mtable_off + (kb * 8 + 2 * c) * 4);
+          const uint2 xs = lds_v2(mtable_s + (kb * 8 + 2 * c) * 4);
+          const float2 X = make_float2(__uint_as_float(xs.x), __uint_as_float(xs.y));
           q4i8_block<QT == 5>(ag, ah, c, b0, b1, k28, sel_sc, m_lo, m_hi, sh_m, X, u0, yacc);
         } else {
           // Q6_K: per half, 4 steps: s < 2 the low-nibble group (sub-block c, words 2(s&1),
@@ -1476,7 +1481,7 @@ __device__ __forceinline__ void consume_job(const WarpMmaArgs& a, const JobArgs&
         q4f16_block(ag, ah, tab_t, bm_at, u0, u1);
       } else {
         // Q6_K, batch 1: thread (g, c) owns sub-blocks c and c+4 of each half of the block
-        const float u0 = ublk[kb];
+        const float u0 = ublk_at(kb);
         const float dg = u0 * h2f(lds_u16(ag + 208)), dh = u0 * h2f(lds_u16(ah + 208));
         const uint32_t tab_kb = tab_on ? table_s + kb * 1024 + tab_lane : zero_s;
         // the block's quants, loaded in the form the rows' common alignment allows
