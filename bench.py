@@ -182,6 +182,13 @@ def dist_setup():
     return world, rank, local
 
 
+def matvec_launches(qtype, batch, path):
+    """Kernels one matvec call launches: the tensor-core path (Q4_K/Q5_K above batch 8, or when
+    asked) runs an X pre-pass before the matmul; the other paths are one kernel."""
+    tc = path == "tc" or (path == "auto" and batch > 8 and qtype in (4, 5))
+    return 2 if tc else 1
+
+
 def workload_shape(args):
     w = dict(WORKLOADS[args.workload])
     if w["batch"] is None:
@@ -432,7 +439,7 @@ def main(argv=None):
             "data": "synthetic", "config": cfg,
             "hbm_frac": round(achieved / peak, 4),
             "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e,
-            "gpu_launches": args.steps, "clocks": clocks,
+            "gpu_launches": args.steps * matvec_launches(qtype, batch, args.path), "clocks": clocks,
         }
         print(json.dumps(line), flush=True)
     kernels.close()

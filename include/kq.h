@@ -73,7 +73,7 @@ enum {
     KQ_FLAG_WEIGHTS_STATIC = 1u << 0,
     /* Launch without the programmatic-dependent-launch attribute. */
     KQ_FLAG_NO_PDL = 1u << 1,
-    /* Use the tensor-core (tcgen05) kernel; Q4_K only. */
+    /* Use the tensor-core (tcgen05) kernel; Q4_K and Q5_K. */
     KQ_FLAG_TENSOR_CORES = 1u << 2,
     /* Use the CUDA-core kernel (batch <= 8, f32 multiply-adds). */
     KQ_FLAG_CUDA_CORES = 1u << 3,
@@ -81,7 +81,7 @@ enum {
      * registers into exact tensor-core operands (integer at batch 1, f16 above), products
      * through mma.sync, f32 accumulation.
      * Without a path flag the library chooses: warp-MMA where it serves the request, the
-     * tensor-core kernel above batch 8, the CUDA-core kernel otherwise. */
+     * tensor-core kernel above batch 8 (Q5_K: above batch 1), the CUDA-core kernel otherwise. */
     KQ_FLAG_WARP_MMA = 1u << 4
     /* Bits 29 and 30 are reserved for the library's tests and A/B timing: on the warp-MMA path
      * they select its other operand variant at batch 1 (f16 instead of integer) and its other
@@ -126,10 +126,11 @@ int kq_matvec_q6k(kq_ctx* ctx, uint64_t y, uint64_t w, uint64_t x, uint32_t rows
 
 /* The general form: strides, fused prologue/epilogue, flags. */
 typedef struct kq_matvec_desc {
-    uint32_t type;     /* KQ_TYPE_Q4_K, KQ_TYPE_Q6_K, or KQ_TYPE_Q5_K (batch 1, warp-MMA path
-                        * only: another path flag or batch > 1 gives KQ_E_UNSUPPORTED) */
+    uint32_t type;     /* KQ_TYPE_Q4_K, KQ_TYPE_Q5_K, KQ_TYPE_Q6_K (or Q2_K, Q3_K, Q8_0 below);
+                        * Q5_K: batch 1 on the warp-MMA kernel, 2..64 on the tensor cores, no
+                        * CUDA-core kernel */
     uint32_t rows, k;  /* W is rows x k; k % 256 == 0 */
-    uint32_t batch;    /* vectors: 1..64 for Q4_K, 1..8 for Q6_K */
+    uint32_t batch;    /* vectors: 1..64 for Q4_K and Q5_K, 1..8 for Q6_K */
     uint64_t y, w, x;  /* device addresses */
     uint64_t ldx;      /* floats between vectors of x (>= k, multiple of 4); 0 = k */
     uint64_t ldy;      /* floats between vectors of y; 0 = rows (or rows/2 for the products) */

@@ -623,7 +623,7 @@ int check_desc(const kq_matvec_desc& d, const char* call) {
     return fail(KQ_E_INVALID, call,
                 "rows must be > 0 and k a positive multiple of 256 (rows " +
                     std::to_string(d.rows) + ", k " + std::to_string(d.k) + ")");
-  const uint32_t max_batch = qt == 4 ? 64 : 8;
+  const uint32_t max_batch = qt == 6 ? 8 : 64;
   if (d.batch < 1 || d.batch > max_batch)
     return fail(KQ_E_INVALID, call,
                 "batch must be 1.." + std::to_string(max_batch) + " (got " + std::to_string(d.batch) + ")");
@@ -682,10 +682,15 @@ int matvec(kq_ctx* ctx, const kq_matvec_desc& d, cudaStream_t stream, const kq_p
   }
   // The push exchange: the warp-MMA kernel's integer path unless the CUDA cores are asked for.
   if (push && !(d.flags & KQ_FLAG_CUDA_CORES)) return warpmma_push(ctx, d, *push, ldx, ldy, stream);
-  if (qt == 5) {  // Q5_K: the warp-MMA kernel's integer path only
-    if (push || d.batch != 1 || (d.flags & (KQ_FLAG_TENSOR_CORES | KQ_FLAG_CUDA_CORES)))
-      return fail(KQ_E_UNSUPPORTED, call, "Q5_K is served at batch 1 by the warp-MMA kernel");
-    return warpmma_matvec(ctx, d, ldx, ldy, stream);
+  if (qt == 5) {  // Q5_K: batch 1 on the warp-MMA kernel, batch 2..64 (or when asked) on the tensor cores
+    if (d.flags & KQ_FLAG_CUDA_CORES)
+      return fail(KQ_E_UNSUPPORTED, call, "Q5_K has no CUDA-core kernel");
+    if (d.batch == 1 && !(d.flags & KQ_FLAG_TENSOR_CORES)) return warpmma_matvec(ctx, d, ldx, ldy, stream);
+    if ((d.flags & KQ_FLAG_WARP_MMA) || !mma_supports(d))
+      return fail(KQ_E_UNSUPPORTED, call,
+                  "Q5_K above batch 1 is served by the tensor-core kernel, batch 2..64 without "
+                  "prologue or epilogue");
+    return mma_matvec(ctx, d, ldx, ldy, stream);
   }
   if (d.flags & KQ_FLAG_WARP_MMA) {
     if (push || !warpmma_supports(d))
@@ -701,7 +706,7 @@ int matvec(kq_ctx* ctx, const kq_matvec_desc& d, cudaStream_t stream, const kq_p
   if (want_tc) {
     if (!mma_supports(d))
       return fail(KQ_E_UNSUPPORTED, call,
-                  "the tensor-core kernel serves Q4_K without prologue/epilogue, batch 1..64");
+                  "the tensor-core kernel serves Q4_K and Q5_K without prologue/epilogue, batch 1..64");
     return mma_matvec(ctx, d, ldx, ldy, stream);
   }
   if (d.batch > 8)

@@ -1,21 +1,29 @@
-// kq_mma.cu -- the Q4_K matvec / small-batch matmul on the 5th-generation tensor cores.
+// kq_mma.cu -- the Q4_K / Q5_K small-batch matmul (batch 2..64) on the 5th-generation tensor cores.
 //
-// Y[b, r] = sum_k W[r, k] X[b, k] as D = A * B^T per tile of 128 weight rows:
-//   A (128 rows x 256 K per super-block, f16) is written by the dequantising threads straight
-//     into tensor memory: thread = weight row = TMEM lane, so there is no shared-memory A tile;
+// Y[b, r] = sum_k W[r, k] X[b, k] as D = A * B^T per tile of TM <= 128 weight rows:
+//   raw W: one 2-D TMA copy per super-block column of the tile (TM rows x 144 bytes: a box of a
+//     tensor map over W viewed as rows x row-bytes), into a ring of kRaw shared-memory stages.
+//     The rows land 144 bytes apart, so eight consecutive rows read at one offset hit eight
+//     different bank groups (144 / 16 = 9 is odd): the dequantisers' loads do not conflict;
+//   A (128 lanes x 256 K per super-block, f16) is written by the dequantising threads straight
+//     into tensor memory (tcgen05.st): no shared-memory A tile, whose write and read by the tensor
+//     core (512 bytes per row and super-block, 3.5x the raw bytes) would bound the kernel at these
+//     batch sizes;
 //   B (N = batch padded to 16/32/64, K-major f16) is X, converted once per call by a small
 //     pre-pass into the exact shared-memory layout of the B operand (kept in the context's
 //     scratch buffer), and fetched per super-block with one bulk copy;
 //   D (128 lanes x N f32 columns) accumulates in tensor memory over the whole row; four epilogue
 //     warps read it back with tcgen05.ld and write Y.
-// One persistent CTA per SM owns a contiguous range of rows. Warp roles:
+// A warp may only reach the tensor-memory lanes of its quadrant (warp % 4), which is also its
+// scheduler, so a tile's rows are spread evenly over the four quadrants: row q * nq + t of the
+// tile (nq = TM / 4 rounded up) is lane 32 q + t. Every scheduler then dequantises the same
+// number of rows whatever TM is. The rows are cut into tiles of equal height TM (the last one
+// shorter), tile t going to CTA t % grid. Warp roles:
 //   0       tensor-memory owner and MMA issuer: 16 tcgen05.mma (K = 16) per super-block, then
 //           tcgen05.commit to free the A and B slots, and at the end of a tile to publish D;
-//   1       B loader: one cp.async.bulk of the super-block's B tile into a ring of slots;
-//   2..9    dequantisers: TMEM lane quadrant w % 4, half (w - 2) / 4 of each super-block. Each
-//           thread streams its own row with 16-byte cp.async copies into a private ring of
-//           shared memory several super-blocks deep (weights never pass through the TMA unit,
-//           whose per-request cost would bound a copy per row);
+//   1       loader: the raw W copies, up to kRaw super-blocks ahead, and the B copies;
+//   2..9    dequantisers: lane quadrant w % 4, half (w - 2) / 4 of each super-block; thread t
+//           holds row q * nq + t (threads past the quadrant's rows store don't-care lanes);
 //   10..13  epilogue.
 // The dequantiser keeps the canonical weight w = d*sc*q - dmin*m to one f16 rounding: q comes
 // out of the 1024 + q magic exactly (one LOP3 per two weights and one HSUB2), then one HFMA2
@@ -24,7 +32,9 @@
 // permutes X alike, so the contraction is unchanged.
 //
 // Every wait is bounded (kq_device.cuh): a wait that gives up records an error word, and all
-// roles then run to the end without waiting, so the CTA frees its tensor memory and exits.
+// roles then run to the end without waiting; the loader then waits (bounded) for its copies in
+// flight, and the CTA frees its tensor memory and exits.
+#include <cuda.h>
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
@@ -39,31 +49,37 @@
 namespace kq {
 namespace {
 
-constexpr int kTileM = 128;
-constexpr int kASlots = 3;            // A slots in TMEM, one super-block (128 columns) each
-constexpr int kDQ = 4;                // depth of each dequantiser's private copy ring (blocks)
-constexpr int kDqThreads = 256;
-constexpr int kDqBytes = 80;          // bytes a dequantiser copies per block: header + 64 B of qs
-constexpr uint32_t kDqRing = kDQ * kDqThreads * kDqBytes;
+constexpr int kTileM = 128;           // MMA M = tensor-memory lanes; a tile holds TM <= 128 rows
+// raw W stages (super-blocks in flight per CTA): fewer for Q5_K's 176-byte blocks
+template <int QT>
+constexpr int kRawStages = QT == 4 ? 8 : 6;
+template <int QT>
+constexpr uint32_t kBlockBytes = QT == 4 ? kQ4KBytes : kQ5KBytes;
+constexpr int kASlots = 3;            // A slots in tensor memory, one super-block (128 columns) each
 constexpr int kThreads = 14 * 32;
 constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kDCol = kASlots * 128;  // first D column
 
 struct MmaArgs {
-  const uint8_t* W;
   const uint8_t* xp;  // X in B-operand layout: per block 32 k-groups x NPAD rows x 16 B
   float* y;
   unsigned* err;
   uint64_t ldy;
   uint32_t rows, nb, batch, flags;
+  uint32_t tm;          // rows per tile
+  uint32_t nq;          // rows per lane quadrant: ceil(tm / 4)
+  uint32_t ntiles;      // tiles of the matrix
+  uint32_t raw_stride;  // bytes per raw stage (tm * 144 rounded up to 1024)
 };
 
-template <int NPAD>
-struct MmaGeo {
-  static constexpr int kBSlots = NPAD <= 32 ? 8 : 4;
-  static constexpr uint32_t kBSlotBytes = 32 * NPAD * 16;
-  static constexpr uint32_t kSmem = kDqRing + kBSlots * kBSlotBytes + 1024 + 1024;
-};
+// B slots: one super-block of X each (NPAD x 512 bytes), as many as leave room for the raw ring.
+__host__ __device__ constexpr uint32_t b_slots(uint32_t npad) { return npad <= 16 ? 4 : npad <= 32 ? 3 : 2; }
+__host__ __device__ constexpr uint32_t b_slot_bytes(uint32_t npad) { return npad * 512; }
+
+template <int QT>
+__host__ __device__ constexpr uint32_t smem_bytes(uint32_t npad, uint32_t raw_stride) {
+  return 1024 + kRawStages<QT> * raw_stride + b_slots(npad) * b_slot_bytes(npad) + 512;  // + barriers
+}
 
 // Waits on `bar` for `parity` as one warp: lane 0 polls, every lane gets the outcome.
 __device__ __forceinline__ bool warp_wait(uint32_t bar, uint32_t parity, int* failed,
@@ -83,6 +99,16 @@ __device__ __forceinline__ bool warp_wait(uint32_t bar, uint32_t parity, int* fa
 
 __device__ __forceinline__ uint32_t h2_bits(__half2 h) { return *reinterpret_cast<uint32_t*>(&h); }
 __device__ __forceinline__ __half2 bits_h2(uint32_t u) { return *reinterpret_cast<__half2*>(&u); }
+
+// 2-D tiled TMA load of box (x, y) of `tmap` into shared `dst`, completing on `bar`; no multicast.
+__device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* tmap, uint32_t x,
+                                            uint32_t y, uint32_t bar, uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes.L2::cache_hint"
+      " [%0], [%1, {%2, %3}], [%4], %5;" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(tmap)), "r"(x), "r"(y), "r"(bar), "l"(policy)
+      : "memory");
+}
 
 // X (f32, batch vectors of stride ldx) -> B-operand layout in f16: for block kb, k-group
 // j = 8c + ww and row n, 16 bytes at ((kb*32 + j) * NPAD + n) * 16 holding x[e+0], x[e+2],
@@ -110,37 +136,45 @@ __global__ void xperm_kernel(uint4* xp, const float* x, uint64_t ldx, uint32_t n
   }
 }
 
-template <int NPAD>
-__global__ void __launch_bounds__(kThreads, 1) mma_q4k_kernel(const MmaArgs a) {
-  using G = MmaGeo<NPAD>;
-  constexpr int BS = G::kBSlots;
+template <int QT, int NPAD>
+__global__ void __launch_bounds__(kThreads, 1)
+    mma_kernel(const __grid_constant__ CUtensorMap wmap, const MmaArgs a) {
+  constexpr uint32_t BS = b_slots(NPAD), kB = b_slot_bytes(NPAD);
+  constexpr int kRaw = kRawStages<QT>;
+  constexpr uint32_t kBlk = kBlockBytes<QT>;
+  constexpr uint32_t kQs = QT == 4 ? 16 : 48;  // offset of qs in a block (Q5_K: qh[32] before it)
   extern __shared__ __align__(1024) uint8_t smem_raw[];
-  uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
-  uint8_t* dq = smem;                  // [kDQ][256 threads][80 B]
-  uint8_t* bring = smem + kDqRing;     // [BS][B tile]
-  uint64_t* bars = reinterpret_cast<uint64_t*>(bring + BS * G::kBSlotBytes);
-  uint64_t* a_full = bars;                 // [3]  dequantisers -> MMA
-  uint64_t* a_empty = a_full + kASlots;    // [3]  MMA commit -> dequantisers
-  uint64_t* b_full = a_empty + kASlots;    // [BS] B loader (tx bytes) -> MMA
-  uint64_t* b_empty = b_full + BS;         // [BS] MMA commit -> B loader
-  uint64_t* d_full = b_empty + BS;         // [2]  MMA commit -> epilogue
-  uint64_t* d_empty = d_full + 2;          // [2]  epilogue -> MMA
+  const uint32_t base = (smem_u32(smem_raw) + 1023u) & ~1023u;
+  const uint32_t raw_s = base;                        // [kRaw][raw_stride]
+  const uint32_t b_s = raw_s + kRaw * a.raw_stride;   // [BS][kB]
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem_raw + (b_s + BS * kB - smem_u32(smem_raw)));
+  uint64_t* raw_full = bars;                 // [kRaw]    loader (tx bytes) -> dequantisers
+  uint64_t* raw_empty = raw_full + kRaw;     // [kRaw]    dequantisers -> loader
+  uint64_t* a_full = raw_empty + kRaw;       // [kASlots] dequantisers -> MMA
+  uint64_t* a_empty = a_full + kASlots;      // [kASlots] MMA commit -> dequantisers
+  uint64_t* b_full = a_empty + kASlots;      // [BS]      loader (tx bytes) -> MMA
+  uint64_t* b_empty = b_full + BS;           // [BS]      MMA commit -> loader
+  uint64_t* d_full = b_empty + BS;           // [2]       MMA commit -> epilogue
+  uint64_t* d_empty = d_full + 2;            // [2]       epilogue -> MMA
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(d_empty + 2);
   int* failed = reinterpret_cast<int*>(tmem_holder + 1);
 
   const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const uint32_t RB = a.nb * kQ4KBytes;
-  const uint32_t r_begin = static_cast<uint32_t>(uint64_t(a.rows) * blockIdx.x / gridDim.x);
-  const uint32_t r_end = static_cast<uint32_t>(uint64_t(a.rows) * (blockIdx.x + 1) / gridDim.x);
-  const uint32_t ntiles = (r_end - r_begin + kTileM - 1) / kTileM;
+  // tiles blockIdx.x, blockIdx.x + gridDim.x, ...
+  const uint32_t ntiles = (a.ntiles - blockIdx.x + gridDim.x - 1) / gridDim.x;
+  const uint32_t total = ntiles * a.nb;  // super-blocks this CTA streams
 
   if (threadIdx.x == 0) {
     *failed = 0;
+    for (int i = 0; i < kRaw; ++i) {
+      mbar_init(smem_u32(&raw_full[i]), 1);
+      mbar_init(smem_u32(&raw_empty[i]), 8);
+    }
     for (int i = 0; i < kASlots; ++i) {
       mbar_init(smem_u32(&a_full[i]), 8);
       mbar_init(smem_u32(&a_empty[i]), 1);
     }
-    for (int i = 0; i < BS; ++i) {
+    for (uint32_t i = 0; i < BS; ++i) {
       mbar_init(smem_u32(&b_full[i]), 1);
       mbar_init(smem_u32(&b_empty[i]), 1);
     }
@@ -162,7 +196,7 @@ __global__ void __launch_bounds__(kThreads, 1) mma_q4k_kernel(const MmaArgs a) {
 
   if (warp == 0) {
     // ---------------------------------------------------------------- MMA issuer
-    const uint32_t idesc = idesc_f16_f32(kTileM, NPAD);
+    constexpr uint32_t idesc = idesc_f16_f32(kTileM, NPAD);
     uint32_t g = 0;
     for (uint32_t T = 0; T < ntiles; ++T) {
       const uint32_t dbuf = T & 1;
@@ -176,7 +210,7 @@ __global__ void __launch_bounds__(kThreads, 1) mma_q4k_kernel(const MmaArgs a) {
         tc_fence_after();
         if (lane == 0) {
           if (ok) {
-            const uint32_t bslot = smem_u32(bring) + bs * G::kBSlotBytes;
+            const uint32_t bslot = b_s + bs * kB;
 #pragma unroll
             for (uint32_t s = 0; s < 16; ++s) {
               const uint64_t bdesc = smem_desc(bslot + s * 2 * NPAD * 16, NPAD * 16, 128);
@@ -192,122 +226,132 @@ __global__ void __launch_bounds__(kThreads, 1) mma_q4k_kernel(const MmaArgs a) {
       __syncwarp();
     }
   } else if (warp == 1) {
-    // ---------------------------------------------------------------- B loader
-    pdl_wait();  // the B tiles come from the pre-pass just before this kernel
-    const uint32_t tile_bytes = G::kBSlotBytes;
-    uint32_t g = 0;
-    for (uint32_t T = 0; T < ntiles; ++T) {
-      for (uint32_t kb = 0; kb < a.nb; ++kb, ++g) {
-        const uint32_t bs = g % BS;
-        if (g >= BS) warp_wait(smem_u32(&b_empty[bs]), ((g / BS) - 1) & 1, failed, a.err, kErrWaitEmpty);
+    // ---------------------------------------------------------------- loader
+    const uint64_t pol = policy_evict_first();
+    const uint32_t raw_bytes = a.tm * kBlk;
+    constexpr uint32_t kLag = kRaw / 2;  // the B copies trail the raw copies by this many blocks
+    if (!(a.flags & KQ_FLAG_WEIGHTS_STATIC)) pdl_wait();  // W may be the previous kernel's output
+    for (uint32_t step = 0; step < total + kLag; ++step) {
+      if (step < total) {
+        const uint32_t g = step, rs = g % kRaw;
+        if (g >= kRaw) warp_wait(smem_u32(&raw_empty[rs]), ((g / kRaw) - 1) & 1, failed, a.err, kErrWaitEmpty);
+        if (lane == 0) {
+          const uint32_t T = g / a.nb, kb = g - T * a.nb;
+          const uint32_t row0 = (blockIdx.x + T * gridDim.x) * a.tm;
+          const uint32_t full = smem_u32(&raw_full[rs]);
+          mbar_arrive_expect_tx(full, raw_bytes);
+          tma_load_2d(raw_s + rs * a.raw_stride, &wmap, kb * kBlk, row0, full, pol);
+        }
+        __syncwarp();
+      }
+      if (step >= kLag) {
+        if (step == kLag) pdl_wait();  // the B tiles come from the pre-pass just before this kernel
+        const uint32_t gb = step - kLag, kb = gb % a.nb, bs = gb % BS;
+        if (gb >= BS) warp_wait(smem_u32(&b_empty[bs]), ((gb / BS) - 1) & 1, failed, a.err, kErrWaitEmpty);
         if (lane == 0) {
           const uint32_t full = smem_u32(&b_full[bs]);
-          mbar_arrive_expect_tx(full, tile_bytes);
-          bulk_g2s(smem_u32(bring) + bs * tile_bytes, a.xp + uint64_t(kb) * tile_bytes, tile_bytes,
-                   full);
+          mbar_arrive_expect_tx(full, kB);
+          bulk_g2s(b_s + bs * kB, a.xp + uint64_t(kb) * kB, kB, full);
         }
         __syncwarp();
       }
     }
+    // every copy must have landed before the CTA exits, also when a wait gave up
+    if (lane == 0 && *reinterpret_cast<volatile int*>(failed)) {
+      for (uint32_t g = total > kRaw ? total - kRaw : 0; g < total; ++g)
+        mbar_wait(smem_u32(&raw_full[g % kRaw]), (g / kRaw) & 1);
+      for (uint32_t g = total > BS ? total - BS : 0; g < total; ++g)
+        mbar_wait(smem_u32(&b_full[g % BS]), (g / BS) & 1);
+    }
+    __syncwarp();
   } else if (warp < 10) {
     // ---------------------------------------------------------------- dequantisers
-    const uint32_t quad = warp & 3;              // TMEM lanes 32*quad .. +31
-    const uint32_t part = (warp - 2) >> 2;       // chunks 2*part, 2*part+1 of each block
-    const uint32_t t = (warp - 2) * 32 + lane;   // private ring column
-    const uint32_t lrow = quad * 32 + lane;      // row within the tile
-    const uint32_t my_ring = smem_u32(dq) + t * kDqBytes;
+    const uint32_t quad = warp & 3;         // tensor-memory lanes 32 quad .. +31
+    const uint32_t part = (warp - 2) >> 2;  // chunks 2 part, 2 part + 1 of each block
+    const uint32_t trow = quad * a.nq + lane;  // this thread's row of the tile
+    const bool valid = lane < a.nq && trow < a.tm;
+    const uint32_t src_row = (valid ? trow : 0) * kBlk;
     const uint32_t lane_base = tmem + ((quad * 32) << 16) + part * 64;
-    const uint32_t total = ntiles * a.nb;
-    if (!(a.flags & KQ_FLAG_WEIGHTS_STATIC)) pdl_wait();  // W may be the previous kernel's output
-    // issue position (tile, block) of the next copy
-    uint32_t iT = 0, ikb = 0, issued = 0;
-    auto issue = [&]() {
-      if (issued < total) {
-        const uint32_t row = r_begin + iT * kTileM + lrow;
-        if (row < r_end) {
-          const uint8_t* src = a.W + uint64_t(row) * RB + uint64_t(ikb) * kQ4KBytes;
-          const uint32_t dst = my_ring + (issued % kDQ) * (kDqThreads * kDqBytes);
-          cp_async16(dst, src);                    // d, dmin, scales
-          const uint8_t* qs = src + 16 + 64 * part;
+    const __half2 magic = __half2half2(__ushort_as_half(0x6400));  // 1024
+    for (uint32_t g = 0; g < total; ++g) {
+      const uint32_t rs = g % kRaw, as = g % kASlots;
+      const bool ok = warp_wait(smem_u32(&raw_full[rs]), (g / kRaw) & 1, failed, a.err, kErrWaitFull);
+      if (g >= kASlots) warp_wait(smem_u32(&a_empty[as]), ((g / kASlots) - 1) & 1, failed, a.err, kErrWaitEmpty);
+      tc_fence_after();
+      const uint32_t src = raw_s + rs * a.raw_stride + src_row;
+      const uint4 hdr = ok ? lds_v4(src) : make_uint4(0, 0, 0, 0);
+      const float d = h2f(hdr.x & 0xffffu), dmin = h2f(hdr.x >> 16);
+      // Q5_K: the fifth bits of chunk c's byte l are bits 2c (low nibble) and 2c+1 (high nibble)
+      // of qh[l]; the 16 qh bytes of half hh serve both of this thread's chunks
+      uint4 qh[2] = {make_uint4(0, 0, 0, 0), make_uint4(0, 0, 0, 0)};
+      if (QT == 5 && ok) {
+        qh[0] = lds_v4(src + 16);
+        qh[1] = lds_v4(src + 32);
+      }
+      const uint32_t taddr = lane_base + as * 128;
 #pragma unroll
-          for (int i = 0; i < 4; ++i) cp_async16(dst + 16 + 16 * i, qs + 16 * i);
+      for (int cc = 0; cc < 2; ++cc) {
+        uint32_t sc0, m0, sc1, m1;  // sub-blocks 2c (low nibbles) and 2c+1 (high nibbles)
+        if (part == 0) {
+          sc0 = (hdr.y >> (16 * cc)) & 63u;
+          m0 = (hdr.z >> (16 * cc)) & 63u;
+          sc1 = (hdr.y >> (16 * cc + 8)) & 63u;
+          m1 = (hdr.z >> (16 * cc + 8)) & 63u;
+        } else {
+          const uint32_t s0 = 16 * cc, s1 = 16 * cc + 8;
+          sc0 = ((hdr.w >> s0) & 15u) | (((hdr.y >> (s0 + 6)) & 3u) << 4);
+          m0 = ((hdr.w >> (s0 + 4)) & 15u) | (((hdr.z >> (s0 + 6)) & 3u) << 4);
+          sc1 = ((hdr.w >> s1) & 15u) | (((hdr.y >> (s1 + 6)) & 3u) << 4);
+          m1 = ((hdr.w >> (s1 + 4)) & 15u) | (((hdr.z >> (s1 + 6)) & 3u) << 4);
         }
-        if (++ikb == a.nb) {
-          ikb = 0;
-          ++iT;
+        // low nibbles: q * s0 - m0; high nibbles hold 16 q: 16q * (s1 / 16) - m1
+        const __half2 s_lo = __half2half2(__float2half_rn(d * static_cast<float>(sc0)));
+        const __half2 mn_lo = __half2half2(__float2half_rn(-dmin * static_cast<float>(m0)));
+        const __half2 s_hi = __half2half2(__float2half_rn(d * static_cast<float>(sc1) * 0.0625f));
+        const __half2 mn_hi = __half2half2(__float2half_rn(-dmin * static_cast<float>(m1)));
+#pragma unroll
+        for (int hh = 0; hh < 2; ++hh) {  // 16 bytes of qs -> 16 tensor-memory columns
+          const uint4 q = ok ? lds_v4(src + kQs + 64 * part + 32 * cc + 16 * hh) : make_uint4(0, 0, 0, 0);
+          const uint32_t words[4] = {q.x, q.y, q.z, q.w};
+          const uint32_t hwords[4] = {qh[hh].x, qh[hh].y, qh[hh].z, qh[hh].w};
+          uint32_t v[16];
+#pragma unroll
+          for (int ww = 0; ww < 4; ++ww) {
+            const uint32_t w = words[ww], w8 = w >> 8;
+            uint32_t la0 = (w & 0x000F000Fu) | 0x64006400u, la1 = (w8 & 0x000F000Fu) | 0x64006400u;
+            uint32_t lb0 = (w & 0x00F000F0u) | 0x64006400u, lb1 = (w8 & 0x00F000F0u) | 0x64006400u;
+            if (QT == 5) {  // 1024 + q + 16 h and 1024 + 16 (q + 16 h)
+              const uint32_t h = hwords[ww] >> (2 * (2 * part + cc));
+              la0 |= (h << 4) & 0x00100010u;  // bytes 0, 2, bit 2c
+              la1 |= (h >> 4) & 0x00100010u;  // bytes 1, 3, bit 2c
+              lb0 |= (h << 7) & 0x01000100u;  // bytes 0, 2, bit 2c+1
+              lb1 |= (h >> 1) & 0x01000100u;  // bytes 1, 3, bit 2c+1
+            }
+            const __half2 a0 = __hsub2(bits_h2(la0), magic);
+            const __half2 a1 = __hsub2(bits_h2(la1), magic);
+            const __half2 b0 = __hsub2(bits_h2(lb0), magic);
+            const __half2 b1 = __hsub2(bits_h2(lb1), magic);
+            v[4 * ww + 0] = h2_bits(__hfma2(a0, s_lo, mn_lo));
+            v[4 * ww + 1] = h2_bits(__hfma2(a1, s_lo, mn_lo));
+            v[4 * ww + 2] = h2_bits(__hfma2(b0, s_hi, mn_hi));
+            v[4 * ww + 3] = h2_bits(__hfma2(b1, s_hi, mn_hi));
+          }
+          tmem_st16(taddr + 32 * cc + 16 * hh, v);
         }
       }
-      cp_async_commit();  // possibly empty: keeps one group per block
-      ++issued;
-    };
-#pragma unroll 1
-    for (int i = 0; i < kDQ - 1; ++i) issue();
-    const __half2 magic = __half2half2(__ushort_as_half(0x6400));  // 1024
-    uint32_t g = 0;
-    for (uint32_t T = 0; T < ntiles; ++T) {
-      const bool valid = lrow < r_end - (r_begin + T * kTileM);
-      for (uint32_t kb = 0; kb < a.nb; ++kb, ++g) {
-        issue();
-        cp_async_wait<kDQ - 1>();  // this thread's copy of block g has landed
-        const uint32_t as = g % kASlots;
-        if (g >= kASlots)
-          warp_wait(smem_u32(&a_empty[as]), ((g / kASlots) - 1) & 1, failed, a.err, kErrWaitEmpty);
-        tc_fence_after();
-        const uint32_t src = my_ring + (g % kDQ) * (kDqThreads * kDqBytes);
-        const uint4 hdr = valid ? lds_v4(src) : make_uint4(0, 0, 0, 0);
-        const float d = h2f(hdr.x & 0xffffu), dmin = h2f(hdr.x >> 16);
-        const uint32_t taddr = lane_base + as * 128;
-#pragma unroll
-        for (int cc = 0; cc < 2; ++cc) {
-          uint32_t sc0, m0, sc1, m1;  // sub-blocks 2c (low nibbles) and 2c+1 (high nibbles)
-          if (part == 0) {
-            sc0 = (hdr.y >> (16 * cc)) & 63u;
-            m0 = (hdr.z >> (16 * cc)) & 63u;
-            sc1 = (hdr.y >> (16 * cc + 8)) & 63u;
-            m1 = (hdr.z >> (16 * cc + 8)) & 63u;
-          } else {
-            const uint32_t s0 = 16 * cc, s1 = 16 * cc + 8;
-            sc0 = ((hdr.w >> s0) & 15u) | (((hdr.y >> (s0 + 6)) & 3u) << 4);
-            m0 = ((hdr.w >> (s0 + 4)) & 15u) | (((hdr.z >> (s0 + 6)) & 3u) << 4);
-            sc1 = ((hdr.w >> s1) & 15u) | (((hdr.y >> (s1 + 6)) & 3u) << 4);
-            m1 = ((hdr.w >> (s1 + 4)) & 15u) | (((hdr.z >> (s1 + 6)) & 3u) << 4);
-          }
-          // low nibbles: q * s0 - m0; high nibbles hold 16 q: 16q * (s1 / 16) - m1
-          const __half2 s_lo = __half2half2(__float2half_rn(d * static_cast<float>(sc0)));
-          const __half2 mn_lo = __half2half2(__float2half_rn(-dmin * static_cast<float>(m0)));
-          const __half2 s_hi = __half2half2(__float2half_rn(d * static_cast<float>(sc1) * 0.0625f));
-          const __half2 mn_hi = __half2half2(__float2half_rn(-dmin * static_cast<float>(m1)));
-#pragma unroll
-          for (int hh = 0; hh < 2; ++hh) {  // 16 bytes of qs -> 16 TMEM columns
-            const uint4 q = valid ? lds_v4(src + 16 + 32 * cc + 16 * hh) : make_uint4(0, 0, 0, 0);
-            const uint32_t words[4] = {q.x, q.y, q.z, q.w};
-            uint32_t v[16];
-#pragma unroll
-            for (int ww = 0; ww < 4; ++ww) {
-              const uint32_t w = words[ww], w8 = w >> 8;
-              const __half2 a0 = __hsub2(bits_h2((w & 0x000F000Fu) | 0x64006400u), magic);
-              const __half2 a1 = __hsub2(bits_h2((w8 & 0x000F000Fu) | 0x64006400u), magic);
-              const __half2 b0 = __hsub2(bits_h2((w & 0x00F000F0u) | 0x64006400u), magic);
-              const __half2 b1 = __hsub2(bits_h2((w8 & 0x00F000F0u) | 0x64006400u), magic);
-              v[4 * ww + 0] = h2_bits(__hfma2(a0, s_lo, mn_lo));
-              v[4 * ww + 1] = h2_bits(__hfma2(a1, s_lo, mn_lo));
-              v[4 * ww + 2] = h2_bits(__hfma2(b0, s_hi, mn_hi));
-              v[4 * ww + 3] = h2_bits(__hfma2(b1, s_hi, mn_hi));
-            }
-            tmem_st16(taddr + 32 * cc + 16 * hh, v);
-          }
-        }
-        tmem_wait_st();
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(smem_u32(&a_full[as]));
+      tmem_wait_st();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) {
+        mbar_arrive(smem_u32(&a_full[as]));
+        mbar_arrive(smem_u32(&raw_empty[rs]));
       }
     }
-    cp_async_wait<0>();
   } else {
     // ---------------------------------------------------------------- epilogue
     pdl_wait();
     const uint32_t quad = warp & 3;
+    const uint32_t trow = quad * a.nq + lane;
     for (uint32_t T = 0; T < ntiles; ++T) {
       const uint32_t dbuf = T & 1;
       const bool ok = warp_wait(smem_u32(&d_full[dbuf]), (T / 2) & 1, failed, a.err, kErrWaitFull);
@@ -324,8 +368,8 @@ __global__ void __launch_bounds__(kThreads, 1) mma_q4k_kernel(const MmaArgs a) {
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(smem_u32(&d_empty[dbuf]));
-      const uint32_t row = r_begin + T * kTileM + quad * 32 + lane;
-      if (ok && row < r_end) {
+      const uint32_t row = (blockIdx.x + T * gridDim.x) * a.tm + trow;
+      if (ok && lane < a.nq && trow < a.tm && row < a.rows) {
 #pragma unroll
         for (int n = 0; n < NPAD; ++n)
           if (n < static_cast<int>(a.batch)) a.y[n * a.ldy + row] = __uint_as_float(v[n]);
@@ -341,26 +385,134 @@ __global__ void __launch_bounds__(kThreads, 1) mma_q4k_kernel(const MmaArgs a) {
   }
 }
 
-template <int NPAD>
-const void* mma_fn() {
-  return reinterpret_cast<const void*>(&mma_q4k_kernel<NPAD>);
+template <int QT>
+const void* mma_fn(uint32_t npad) {
+  return npad == 16   ? reinterpret_cast<const void*>(&mma_kernel<QT, 16>)
+         : npad == 32 ? reinterpret_cast<const void*>(&mma_kernel<QT, 32>)
+                      : reinterpret_cast<const void*>(&mma_kernel<QT, 64>);
 }
+
+const void* mma_fn_for(int qt, uint32_t npad) { return qt == 4 ? mma_fn<4>(npad) : mma_fn<5>(npad); }
 
 uint32_t npad_for(uint32_t batch) { return batch <= 16 ? 16 : batch <= 32 ? 32 : 64; }
 
-int smem_for(uint32_t npad) {
-  return npad == 16 ? MmaGeo<16>::kSmem : npad == 32 ? MmaGeo<32>::kSmem : MmaGeo<64>::kSmem;
+uint32_t raw_stride_for(int qt, uint32_t tm) {
+  return (tm * (qt == 4 ? kBlockBytes<4> : kBlockBytes<5>) + 1023u) & ~1023u;
+}
+
+uint32_t smem_for(int qt, uint32_t npad, uint32_t raw_stride) {
+  return qt == 4 ? smem_bytes<4>(npad, raw_stride) : smem_bytes<5>(npad, raw_stride);
+}
+
+// The opt-in shared memory the kernel for (qt, npad) is given: enough for 128-row tiles.
+int smem_limit(int qt, uint32_t npad) { return static_cast<int>(smem_for(qt, npad, raw_stride_for(qt, kTileM))); }
+
+// Sets every instance's shared-memory limit (with the device the kernels run on current).
+cudaError_t set_smem_limits() {
+  for (int qt : {4, 5})
+    for (uint32_t n : {16u, 32u, 64u}) {
+      const cudaError_t e =
+          cudaFuncSetAttribute(mma_fn_for(qt, n), cudaFuncAttributeMaxDynamicSharedMemorySize, smem_limit(qt, n));
+      if (e != cudaSuccess) return e;
+    }
+  return cudaSuccess;
+}
+
+using EncodeTiled = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                 const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                 CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+// cuTensorMapEncodeTiled through the runtime's driver entry point (the library links only the
+// runtime); null when the driver has none.
+EncodeTiled encode_tiled() {
+  static const EncodeTiled fn = []() -> EncodeTiled {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess)
+      return nullptr;
+    return reinterpret_cast<EncodeTiled>(p);
+  }();
+  return fn;
+}
+
+// One call of the pre-pass and the kernel on `stream`: tiles of equal height (rows / SMs rounded
+// up, at most 128, at least 16 or all rows), the tensor map over W with one tile's super-block
+// column as its box.
+int mma_launch(const char* call, int sm_count, int qt, uint64_t w, uint64_t x, uint64_t ldx, uint64_t y,
+               uint64_t ldy, uint32_t rows, uint32_t k, uint32_t batch, uint32_t flags, void* scratch,
+               unsigned* err, cudaStream_t stream) {
+  const uint32_t npad = npad_for(batch);
+  const uint32_t blk = qt == 4 ? kBlockBytes<4> : kBlockBytes<5>;
+  const uint32_t nb = k / kQK;
+  const uint32_t sms = static_cast<uint32_t>(std::max(sm_count, 1));
+  const uint32_t per_cta = (rows + sms * kTileM - 1) / (sms * kTileM);  // tiles per CTA
+  uint32_t tm = (rows + sms * per_cta - 1) / (sms * per_cta);
+  tm = std::min<uint32_t>(kTileM, std::max<uint32_t>(tm, std::min<uint32_t>(rows, 16)));
+  const uint32_t ntiles = (rows + tm - 1) / tm;
+
+  const EncodeTiled encode = encode_tiled();
+  if (!encode) return fail(KQ_E_UNSUPPORTED, call, "the driver has no cuTensorMapEncodeTiled");
+  CUtensorMap map;
+  const cuuint64_t dims[2] = {uint64_t(nb) * blk, rows};
+  const cuuint64_t strides[1] = {uint64_t(nb) * blk};
+  const cuuint32_t box[2] = {blk, tm};
+  const cuuint32_t estr[2] = {1, 1};
+  const CUresult r = encode(&map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, reinterpret_cast<void*>(w), dims, strides,
+                            box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS)
+    return fail(KQ_E_INVALID, call, "cuTensorMapEncodeTiled refused W (error " + std::to_string(int(r)) + ")");
+
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  const unsigned nattr = (flags & KQ_FLAG_NO_PDL) ? 0 : 1;
+  {  // pre-pass: X -> B-operand layout
+    const uint32_t total = nb * 32 * npad;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(std::min<uint32_t>((total + 255) / 256, sms * 4));
+    cfg.blockDim = dim3(256);
+    cfg.stream = stream;
+    cfg.attrs = attr;
+    cfg.numAttrs = nattr;
+    const cudaError_t e = cudaLaunchKernelEx(&cfg, xperm_kernel, reinterpret_cast<uint4*>(scratch),
+                                             reinterpret_cast<const float*>(x), ldx, nb, batch, npad);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaLaunchKernelEx", "X pre-pass");
+  }
+  MmaArgs args;
+  args.xp = static_cast<const uint8_t*>(scratch);
+  args.y = reinterpret_cast<float*>(y);
+  args.err = err;
+  args.ldy = ldy;
+  args.rows = rows;
+  args.nb = nb;
+  args.batch = batch;
+  args.flags = flags;
+  args.tm = tm;
+  args.ntiles = ntiles;
+  args.nq = (tm + 3) / 4;
+  args.raw_stride = raw_stride_for(qt, tm);
+  const uint32_t grid = std::min<uint32_t>(sms, ntiles);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = smem_for(qt, npad, args.raw_stride);
+  cfg.stream = stream;
+  cfg.attrs = attr;
+  cfg.numAttrs = nattr;
+  void* params[] = {&map, &args};
+  const cudaError_t e = cudaLaunchKernelExC(&cfg, mma_fn_for(qt, npad), params);
+  if (e != cudaSuccess)
+    return cuda_fail(e, "cudaLaunchKernelExC", "tensor-core matvec grid " + std::to_string(grid));
+  return KQ_OK;
 }
 
 }  // namespace
 
 int mma_prepare(kq_ctx* ctx) {
-  for (uint32_t n : {16u, 32u, 64u}) {
-    const void* fn = n == 16 ? mma_fn<16>() : n == 32 ? mma_fn<32>() : mma_fn<64>();
-    const cudaError_t e =
-        cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_for(n));
-    if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute", "tensor-core matvec kernel");
-  }
+  const cudaError_t e = set_smem_limits();
+  if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute", "tensor-core matvec kernel");
   return KQ_OK;
 }
 
@@ -369,62 +521,20 @@ uint64_t mma_scratch_bytes(uint32_t k, uint32_t batch) {
 }
 
 bool mma_supports(const kq_matvec_desc& d) {
-  return d.type == KQ_TYPE_Q4_K && d.batch >= 1 && d.batch <= 64 &&
+  return (d.type == KQ_TYPE_Q4_K || d.type == KQ_TYPE_Q5_K) && d.batch >= 1 && d.batch <= 64 &&
          d.prologue == KQ_PROLOGUE_NONE && d.epilogue == KQ_EPILOGUE_NONE;
 }
 
 int mma_matvec(kq_ctx* ctx, const kq_matvec_desc& d, uint64_t ldx, uint64_t ldy,
                cudaStream_t stream) {
-  const uint32_t npad = npad_for(d.batch);
-  const uint32_t nb = d.k / kQK;
   const uint64_t need = mma_scratch_bytes(d.k, d.batch);
   if (need > ctx->scratch_bytes)
     return fail(KQ_E_UNSUPPORTED, "kq_matvec",
                 "the tensor-core path needs " + std::to_string(need) + " bytes of scratch for k " +
                     std::to_string(d.k) + ", batch " + std::to_string(d.batch) + "; the context has " +
                     std::to_string(ctx->scratch_bytes));
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[0].val.programmaticStreamSerializationAllowed = 1;
-  const unsigned nattr = (d.flags & KQ_FLAG_NO_PDL) ? 0 : 1;
-
-  // pre-pass: X -> B-operand layout
-  {
-    const uint32_t total = nb * 32 * npad;
-    cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(std::min<uint32_t>((total + 255) / 256, ctx->sm_count * 4));
-    cfg.blockDim = dim3(256);
-    cfg.stream = stream;
-    cfg.attrs = attr;
-    cfg.numAttrs = nattr;
-    const cudaError_t e = cudaLaunchKernelEx(&cfg, xperm_kernel, reinterpret_cast<uint4*>(ctx->scratch),
-                                             reinterpret_cast<const float*>(d.x), ldx, nb, d.batch, npad);
-    if (e != cudaSuccess) return cuda_fail(e, "cudaLaunchKernelEx", "X pre-pass");
-  }
-  MmaArgs args;
-  args.W = reinterpret_cast<const uint8_t*>(d.w);
-  args.xp = static_cast<const uint8_t*>(ctx->scratch);
-  args.y = reinterpret_cast<float*>(d.y);
-  args.err = ctx->err;
-  args.ldy = ldy;
-  args.rows = d.rows;
-  args.nb = nb;
-  args.batch = d.batch;
-  args.flags = d.flags;
-  const void* fn = npad == 16 ? mma_fn<16>() : npad == 32 ? mma_fn<32>() : mma_fn<64>();
-  const uint32_t grid = std::min<uint32_t>(ctx->sm_count, d.rows);
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(grid);
-  cfg.blockDim = dim3(kThreads);
-  cfg.dynamicSmemBytes = smem_for(npad);
-  cfg.stream = stream;
-  cfg.attrs = attr;
-  cfg.numAttrs = nattr;
-  void* params[] = {&args};
-  const cudaError_t e = cudaLaunchKernelExC(&cfg, fn, params);
-  if (e != cudaSuccess)
-    return cuda_fail(e, "cudaLaunchKernelExC", "tensor-core matvec grid " + std::to_string(grid));
-  return KQ_OK;
+  return mma_launch("kq_matvec", ctx->sm_count, d.type == KQ_TYPE_Q4_K ? 4 : 5, d.w, d.x, ldx, d.y, ldy,
+                    d.rows, d.k, d.batch, d.flags, ctx->scratch, ctx->err, stream);
 }
 
 }  // namespace kq
@@ -468,11 +578,8 @@ int noalloc_setup(int dev, NoAllocDevice** out) {
       return kq::fail(KQ_E_UNSUPPORTED, "kq_matvec_q4k_noalloc", "this library is built for sm_100a (B200)");
     e = cudaDeviceGetAttribute(&d.sm_count, cudaDevAttrMultiProcessorCount, dev);
     if (e != cudaSuccess) return kq::cuda_fail(e, "cudaDeviceGetAttribute");
-    for (uint32_t n : {16u, 32u, 64u}) {
-      const void* fn = n == 16 ? kq::mma_fn<16>() : n == 32 ? kq::mma_fn<32>() : kq::mma_fn<64>();
-      e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, kq::smem_for(n));
-      if (e != cudaSuccess) return kq::cuda_fail(e, "cudaFuncSetAttribute", "tensor-core matvec kernel");
-    }
+    e = kq::set_smem_limits();
+    if (e != cudaSuccess) return kq::cuda_fail(e, "cudaFuncSetAttribute", "tensor-core matvec kernel");
     void* p = nullptr;
     e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
     if (e != cudaSuccess) return kq::cuda_fail(e, "cudaGetSymbolAddress", "static scratch");
@@ -508,47 +615,8 @@ extern "C" int kq_matvec_q4k_noalloc(uint64_t y, uint64_t w, uint64_t x, uint32_
   if (e != cudaSuccess) return kq::cuda_fail(e, "cudaGetDevice");
   if (dev < 0 || dev >= kMaxDevices) return kq::fail(KQ_E_UNSUPPORTED, call, "device ordinal past 63");
   NoAllocDevice* d = nullptr;
-  int rc = noalloc_setup(dev, &d);
+  const int rc = noalloc_setup(dev, &d);
   if (rc) return rc;
-
-  const uint32_t npad = kq::npad_for(batch);
-  const uint32_t nb = k / kq::kQK;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[0].val.programmaticStreamSerializationAllowed = 1;
-  const cudaStream_t s = static_cast<cudaStream_t>(stream);
-  {
-    const uint32_t total = nb * 32 * npad;
-    cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(std::min<uint32_t>((total + 255) / 256, d->sm_count * 4));
-    cfg.blockDim = dim3(256);
-    cfg.stream = s;
-    cfg.attrs = attr;
-    cfg.numAttrs = 1;
-    e = cudaLaunchKernelEx(&cfg, kq::xperm_kernel, reinterpret_cast<uint4*>(d->scratch),
-                           reinterpret_cast<const float*>(x), uint64_t(k), nb, batch, npad);
-    if (e != cudaSuccess) return kq::cuda_fail(e, "cudaLaunchKernelEx", "X pre-pass");
-  }
-  kq::MmaArgs args;
-  args.W = reinterpret_cast<const uint8_t*>(w);
-  args.xp = static_cast<const uint8_t*>(d->scratch);
-  args.y = reinterpret_cast<float*>(y);
-  args.err = d->err;
-  args.ldy = rows;
-  args.rows = rows;
-  args.nb = nb;
-  args.batch = batch;
-  args.flags = 0;
-  const void* fn = npad == 16 ? kq::mma_fn<16>() : npad == 32 ? kq::mma_fn<32>() : kq::mma_fn<64>();
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(std::min<uint32_t>(d->sm_count, rows));
-  cfg.blockDim = dim3(kq::kThreads);
-  cfg.dynamicSmemBytes = kq::smem_for(npad);
-  cfg.stream = s;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
-  void* params[] = {&args};
-  e = cudaLaunchKernelExC(&cfg, fn, params);
-  if (e != cudaSuccess) return kq::cuda_fail(e, "cudaLaunchKernelExC", "tensor-core matvec");
-  return KQ_OK;
+  return kq::mma_launch(call, d->sm_count, 4, w, x, k, y, rows, rows, k, batch, 0, d->scratch, d->err,
+                        static_cast<cudaStream_t>(stream));
 }

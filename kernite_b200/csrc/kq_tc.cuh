@@ -1,5 +1,5 @@
 // kq_tc.cuh -- tcgen05 (5th-generation tensor core) building blocks for sm_100a: tensor memory
-// allocation, loads/stores, the f16 MMA with A in tensor memory and B in shared memory, commit,
+// allocation, loads/stores, the f16 MMA (A in tensor or shared memory, B in shared memory), commit,
 // fences, and the shared-memory matrix / instruction descriptors.
 //
 // Descriptor layouts (PTX ISA, tcgen05 "shared memory descriptor" and "instruction descriptor
@@ -86,6 +86,17 @@ __device__ __forceinline__ void mma_f16_ts(uint32_t d_tmem, uint32_t a_tmem, uin
       "setp.ne.b32 p, %4, 0;\n\t"
       "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
       "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// D[tmem] (+)= A[smem] * B[smem]^T, f16 inputs, f32 accumulate. One thread issues.
+__device__ __forceinline__ void mma_f16_ss(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
+                                           uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
       : "memory");
 }
 

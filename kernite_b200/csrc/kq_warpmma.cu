@@ -1826,7 +1826,7 @@ struct WarpMmaPlan {
 // Chooses the variant, the tiles and the shared-memory layout of one matvec (arguments already
 // checked by the caller), as the standalone launch uses them.
 int warpmma_plan(kq_ctx* ctx, const kq_matvec_desc& d, uint64_t ldx, uint64_t ldy, const char* call,
-                 WarpMmaPlan& plan) {
+                 WarpMmaPlan& plan, uint32_t ksplit = 1, bool compact = true) {
   const bool q4 = d.type == KQ_TYPE_Q4_K;
   const bool q5 = d.type == KQ_TYPE_Q5_K;  // Q4_K's layout plus qh: the Q4_K forms, integer only
   const bool q45 = q4 || q5;
@@ -1928,6 +1928,21 @@ int warpmma_plan(kq_ctx* ctx, const kq_matvec_desc& d, uint64_t ldx, uint64_t ld
     return fail(KQ_E_UNSUPPORTED, call,
                 "k " + std::to_string(d.k) + " with batch " + std::to_string(d.batch) +
                     " does not fit the warp-MMA kernel's shared memory");
+  // A CTA with fewer rows than a tile's 16 (short matrices, row shards): its slots hold only the
+  // rows it has, so that more slots, and more tiles in flight, fit beside the table. The
+  // consumers still read 16 rows of a slot; the rows it lacks lie past it, in the next slot or,
+  // from the last slot, in the table that follows the ring, and feed outputs nobody stores.
+  // (Segmented tiles only, whose rows each have their own copy; chains keep full slots, so that
+  // every job of a launch has one layout.)
+  if (compact && seg != 0) {
+    const uint32_t ru = d.epilogue != KQ_EPILOGUE_NONE ? 2 : 1;
+    const uint64_t units = d.rows / ru;
+    const uint64_t groups =
+        std::max<uint64_t>(1, std::min<uint64_t>(ctx->sm_count / std::max<uint32_t>(ksplit, 1), units));
+    const uint64_t rpc = (units + groups - 1) / groups * ru;  // rows of the fullest CTA
+    const uint32_t cslot = static_cast<uint32_t>(((rpc * seg + 127) / 128) * 128);
+    if (rpc < kTileRows && kTileRows * seg - cslot <= table_bytes + mtable_bytes) slot = cslot;
+  }
   // partial rows of up to 16 bands between flushes, in what two ring slots leave
   const uint32_t band_red = kTileRows * nw * d.batch * 4;
   const uint64_t base_need = need_for(slot) - uint64_t(kTileRows) * kMaxWarps * d.batch * 4;
@@ -2091,7 +2106,8 @@ int warpmma_push(kq_ctx* ctx, const kq_matvec_desc& d, const kq_push_desc& push,
                  uint64_t ldy, cudaStream_t stream) {
   const char* call = "kq_matvec_push";
   WarpMmaPlan plan;
-  int rc = warpmma_plan(ctx, d, ldx, ldy, call, plan);
+  // (the plan sizes its slots for the rows a CTA gets, which split K multiplies)
+  int rc = warpmma_plan(ctx, d, ldx, ldy, call, plan, std::min<uint32_t>(std::max<uint32_t>(push.ksplit, 1), 8));
   if (rc) return rc;
   if (plan.mode != (d.type == KQ_TYPE_Q4_K ? 4 : d.type == KQ_TYPE_Q5_K ? 6 : 5))
     return fail(KQ_E_UNSUPPORTED, call, "k " + std::to_string(d.k) + " does not fit the integer kernel");
@@ -2192,7 +2208,7 @@ int warpmma_chain(kq_ctx* ctx, const kq_chain_job* jobs, uint32_t njobs, uint64_
     if (!job.npush && job.counter[0] % 8) return fail(KQ_E_INVALID, call, at + "counter must be 8-byte aligned");
     if (job.wait_counter % 8) return fail(KQ_E_INVALID, call, at + "wait_counter must be 8-byte aligned");
     WarpMmaPlan plan;
-    rc = warpmma_plan(ctx, d, d.k, outs, call, plan);
+    rc = warpmma_plan(ctx, d, d.k, outs, call, plan, 1, false);
     if (rc) return rc;
     if (plan.mode != (d.type == KQ_TYPE_Q4_K ? 4 : d.type == KQ_TYPE_Q5_K ? 6 : 5))
       return fail(KQ_E_UNSUPPORTED, call, at + "k " + std::to_string(d.k) + " does not fit the integer kernel");

@@ -302,6 +302,8 @@ TC_SHAPES = [
     (1, 256, 1), (100, 256, 1), (128, 512, 1), (129, 4096, 1), (300, 11008, 1), (4096, 4096, 1),
     (333, 4096, 2), (257, 4096, 8), (333, 4096, 17), (77, 8192, 33), (1000, 4096, 64),
     (14336, 4096, 16), (5000, 4096, 40),
+    # one- and two-row tiles; several tiles per CTA (rows past 148 x 128); the sweep shape at 32, 64
+    (2, 512, 12), (16, 256, 9), (20000, 2048, 16), (40000, 1024, 64), (14336, 4096, 32), (14336, 4096, 64),
 ]
 
 

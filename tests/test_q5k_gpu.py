@@ -1,6 +1,6 @@
 """Q5_K on the GPU, through the C ABI: the device generator and decoder bit for bit against the
-CPU oracle and the gguf-py fixtures, and the matvec (the warp-MMA kernel's integer path, batch 1)
-against the oracle's f64 reference.
+CPU oracle and the gguf-py fixtures, and the matvec (the warp-MMA kernel's integer path at batch 1,
+the tensor-core kernel at batch 2..64) against the oracle's f64 reference.
 
 Q5_K is Q4_K's block (f16 d and dmin, twelve bytes of 6-bit sub-block scales and mins, 128 bytes of
 nibbles) with 32 more bytes, qh, whose bit g of byte l is the fifth bit of element 32 g + l
@@ -159,11 +159,70 @@ def test_q5k_matvec_is_deterministic(kernels):
 
 def test_q5k_matvec_rejects_what_it_does_not_serve(kernels):
     W = torch.zeros(kb.Q5K_BYTES * 16, dtype=torch.uint8, device="cuda")
-    x = torch.zeros(4096 * 4, device="cuda")
-    y = torch.zeros(4096 * 4, device="cuda")
-    with pytest.raises(kb.Error) as e:  # batch 1 only
-        kernels.matvec(5, y, W, x, 1, 256, 2)
-    assert e.value.code == kb.KQ_E_UNSUPPORTED
+    x = torch.zeros(4096 * 65, device="cuda")
+    y = torch.zeros(4096 * 65, device="cuda")
     with pytest.raises(kb.Error) as e:  # the CUDA-core kernel does not take Q5_K
         kernels.matvec(5, y, W, x, 1, 256, 1, flags=kb.FLAG_CUDA_CORES)
     assert e.value.code == kb.KQ_E_UNSUPPORTED
+    with pytest.raises(kb.Error) as e:  # the warp-MMA kernel serves Q5_K at batch 1 only
+        kernels.matvec(5, y, W, x, 1, 256, 2, flags=kb.FLAG_WARP_MMA)
+    assert e.value.code == kb.KQ_E_UNSUPPORTED
+    with pytest.raises(kb.Error) as e:  # no fused prologue above batch 1
+        kernels.matvec(5, y, W, x, 1, 256, 2, prologue=kb.PROLOGUE_RMSNORM, eps=1e-6)
+    assert e.value.code == kb.KQ_E_UNSUPPORTED
+    with pytest.raises(kb.Error):  # batch 65
+        kernels.matvec(5, y, W, x, 1, 256, 65)
+
+
+# ---------------------------------------------------------------- batch 2..64: the tensor-core kernel
+
+TC_SHAPES = [  # (rows, K, batch)
+    (1, 256, 2), (16, 512, 9), (100, 4096, 16), (300, 11008, 3), (333, 4096, 17), (77, 2816, 33),
+    (1000, 4096, 64), (14336, 4096, 16), (5000, 4352, 40), (20000, 2048, 24),
+]
+
+
+@pytest.mark.parametrize("rows,K,batch", TC_SHAPES)
+def test_q5k_tensor_core_matmul_matches_oracle(kernels, rows, K, batch):
+    W = dev_weights(kernels, rows, K, kb.stream_key(7000 + rows, K + batch))
+    x = np.random.default_rng(rows + K + batch).standard_normal((batch, K), dtype=np.float32)
+    y = run(kernels, W, x, rows, K)
+    y_ref, bound = oracle.matvec_ref(5, W.cpu().numpy(), x, K, 0, rows)
+    check(y, y_ref, bound, f"q5 tc {rows}x{K} b{batch}")
+
+
+def test_q5k_tensor_core_every_fifth_bit_counts(kernels):
+    rows, K, batch = 200, 2048, 12
+    base = oracle.fill(5, oracle.stream_key(91, 5), 0, rows * K // 256).reshape(-1, kb.Q5K_BYTES)
+    x = np.random.default_rng(91).standard_normal((batch, K), dtype=np.float32)
+    ys = []
+    for fill in (0x00, 0xFF, 0x5A):
+        blocks = base.copy()
+        blocks[:, 16:48] = fill
+        W = torch.from_numpy(blocks.reshape(-1).copy()).cuda()
+        y = run(kernels, W, x, rows, K)
+        y_ref, bound = oracle.matvec_ref(5, blocks.reshape(-1), x, K, 0, rows)
+        check(y, y_ref, bound, f"qh {fill:#x}")
+        ys.append(y)
+    assert not np.array_equal(ys[0], ys[1]) and not np.array_equal(ys[1], ys[2])
+
+
+def test_q5k_tensor_core_integer_inputs_are_exact(kernels):
+    rows, K, batch = 300, 1024, 5
+    blocks = oracle.fill(5, oracle.stream_key(92, 5), 0, rows * K // 256).reshape(-1, kb.Q5K_BYTES)
+    blocks[:, 0:2] = np.array([0x2400], dtype=np.uint16).view(np.uint8)  # d = 2^-6
+    blocks[:, 2:4] = np.array([0x2800], dtype=np.uint16).view(np.uint8)  # dmin = 2^-5
+    W = torch.from_numpy(blocks.reshape(-1).copy()).cuda()
+    x = np.random.default_rng(6).integers(-2, 3, size=(batch, K)).astype(np.float32)
+    y = run(kernels, W, x, rows, K)
+    y_ref, _ = oracle.matvec_ref(5, blocks.reshape(-1), x, K, 0, rows)
+    assert np.array_equal(y, y_ref.astype(np.float32))
+
+
+def test_q5k_batch_one_on_the_tensor_cores_when_asked(kernels):
+    rows, K = 700, 4096
+    W = dev_weights(kernels, rows, K, kb.stream_key(93, 5))
+    x = np.random.default_rng(93).standard_normal((1, K), dtype=np.float32)
+    y = run(kernels, W, x, rows, K, flags=kb.FLAG_TENSOR_CORES)
+    y_ref, bound = oracle.matvec_ref(5, W.cpu().numpy(), x, K, 0, rows)
+    check(y, y_ref, bound, "q5 tc batch 1")
