@@ -403,7 +403,10 @@ def main(argv=None):
 
     peak, peak_kind = measured_peak()
     achieved = algo_bytes / (ms_step / 1e3) / 1e9
-    traffic = profiled_traffic(args.workload if args.workload != "sweep" else f"sweep_b{batch}")
+    if args.workload == "sweep" and matvec_launches(qtype, batch, args.path) == 2:
+        traffic = profiled_traffic("sweep_tc", f"launch_b{batch}")  # the tensor-core kernel
+    else:
+        traffic = profiled_traffic(args.workload if args.workload != "sweep" else f"sweep_b{batch}")
     roofline = {"bound": "hbm", "achieved": round(achieved, 2), "peak": peak, "unit": "GB/s",
                 "frac": round(achieved / peak, 4), "traffic": traffic,
                 "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)" if peak_kind == "measured"
