@@ -189,6 +189,13 @@ __device__ __forceinline__ unsigned long long ld_tagged(const unsigned long long
   return v;
 }
 
+// Two consecutive tagged elements (16-byte aligned) in one load; each 8-byte element is read whole.
+__device__ __forceinline__ ulonglong2 ld_tagged2(const unsigned long long* p) {
+  ulonglong2 v;
+  asm volatile("ld.global.cg.v2.u64 {%0, %1}, [%2];" : "=l"(v.x), "=l"(v.y) : "l"(p));
+  return v;
+}
+
 __device__ __forceinline__ void st_tagged(float* p, float v, uint32_t tag) {
   asm volatile("st.global.v2.u32 [%0], {%1, %2};" ::"l"(p), "r"(__float_as_uint(v)), "r"(tag) : "memory");
 }
@@ -805,6 +812,168 @@ __device__ __forceinline__ void consume_job(const WarpMmaArgs& a, const JobArgs&
   {
     if (lane == 0)
       for (int b = 0; b < 8; ++b) s_sq[warp][b] = 0.0;
+    if constexpr (I8) {
+      // Batch 1, integer table. Lane l owns the 8 consecutive elements 8l .. 8l+7 of an x-block,
+      // which are chunk l of the block's table entry (the 8 bytes of each limb), so its loads
+      // are two 16-byte ones (four for a tagged x), its table writes three 8-byte ones, and the
+      // per-sub-block sums need two shuffles. kXG x-blocks per round, all loads in flight.
+      constexpr int kXG = TX ? 4 : 6;  // (more would spill: a tagged x doubles the live loads)
+      const uint32_t want_tag = TX ? sh.tag_x : 0u;
+      const uint32_t x_slots = TXS == 2 ? sh.x_slots : 1u;
+      const uint64_t kx = uint64_t(a.nb) * kQK;  // elements between x's slots
+      for (uint32_t xb0 = warp; xb0 < a.nb; xb0 += kXG * nw) {
+        float v[kXG][8];
+        bool tags_ok = true;
+#pragma unroll
+        for (int j = 0; j < kXG; ++j) {
+          const uint32_t kb = xb0 + j * nw;
+          if (kb < a.nb) {
+            if constexpr (TX) {
+              const unsigned long long* src =
+                  reinterpret_cast<const unsigned long long*>(mj.x) + kb * kQK + 8 * lane;
+#pragma unroll
+              for (int q = 0; q < 4; ++q) {
+                const ulonglong2 w = ld_tagged2(src + 2 * q);
+                v[j][2 * q] = __uint_as_float(static_cast<uint32_t>(w.x));
+                v[j][2 * q + 1] = __uint_as_float(static_cast<uint32_t>(w.y));
+                tags_ok &= static_cast<uint32_t>(w.x >> 32) == want_tag &&
+                           static_cast<uint32_t>(w.y >> 32) == want_tag;
+              }
+              // split-K slots 1.. of the writer: added in slot order (the same sum on every rank)
+              if constexpr (TXS == 2)
+              for (uint32_t sl = 1; sl < x_slots; ++sl) {
+#pragma unroll
+                for (int q = 0; q < 4; ++q) {
+                  const ulonglong2 w = ld_tagged2(src + uint64_t(sl) * kx + 2 * q);
+                  v[j][2 * q] += __uint_as_float(static_cast<uint32_t>(w.x));
+                  v[j][2 * q + 1] += __uint_as_float(static_cast<uint32_t>(w.y));
+                  tags_ok &= static_cast<uint32_t>(w.x >> 32) == want_tag &&
+                             static_cast<uint32_t>(w.y >> 32) == want_tag;
+                }
+              }
+            } else {
+              const float4* src = reinterpret_cast<const float4*>(mj.x + kb * kQK + 8 * lane);
+              const float4 p0 = __ldcg(src), p1 = __ldcg(src + 1);
+              v[j][0] = p0.x, v[j][1] = p0.y, v[j][2] = p0.z, v[j][3] = p0.w;
+              v[j][4] = p1.x, v[j][5] = p1.y, v[j][6] = p1.z, v[j][7] = p1.w;
+            }
+          }
+        }
+        if constexpr (TX) {
+          if (!tags_ok) {
+            // some element is not this step's yet: wait for each, bounded (at once when this CTA
+            // or an earlier launch already gave up); unrolled, so that v stays in registers
+            uint64_t t0 = 0;
+#pragma unroll
+            for (int j = 0; j < kXG; ++j) {
+              const uint32_t kb = xb0 + j * nw;
+              if (kb >= a.nb) break;
+              const unsigned long long* src =
+                  reinterpret_cast<const unsigned long long*>(mj.x) + kb * kQK + 8 * lane;
+#pragma unroll
+              for (int i = 0; i < 8; ++i) {
+                float sum = 0.f;
+                for (uint32_t sl = 0; sl < x_slots; ++sl) {
+                  const unsigned long long* at = src + uint64_t(sl) * kx + i;
+                  unsigned long long w = ld_tagged(at);
+                  while (static_cast<uint32_t>(w >> 32) != want_tag) {
+                    if (*reinterpret_cast<volatile int*>(&s_failed) ||
+                        (a.err && *reinterpret_cast<volatile unsigned*>(a.err)))
+                      break;
+                    if (t0 == 0) t0 = globaltimer();
+                    if (globaltimer() - t0 > kWaitBudgetNs) {
+                      report_error(a.err, kErrWaitPeer);
+                      s_failed = 1;
+                      break;
+                    }
+                    w = ld_tagged(at);
+                  }
+                  sum = sl ? sum + __uint_as_float(static_cast<uint32_t>(w))
+                           : __uint_as_float(static_cast<uint32_t>(w));
+                }
+                v[j][i] = sum;
+              }
+            }
+          }
+        }
+#pragma unroll
+        for (int j = 0; j < kXG; ++j) {
+          const uint32_t kb = xb0 + j * nw;
+          if (kb >= a.nb) break;
+          float mx = 0.f;
+#pragma unroll
+          for (int i = 0; i < 8; ++i) mx = fmaxf(mx, fabsf(v[j][i]));
+#pragma unroll
+          for (int o = 16; o; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+          double sq = 0.0;  // only the RMS norm needs it
+          if (mj.prologue == KQ_PROLOGUE_RMSNORM) {
+#pragma unroll
+            for (int i = 0; i < 8; ++i)
+              sq = fma(static_cast<double>(v[j][i]), static_cast<double>(v[j][i]), sq);
+#pragma unroll
+            for (int o = 16; o; o >>= 1) sq += __shfl_xor_sync(0xffffffffu, sq, o);
+          }
+          // 24-bit fixed point for the block: the power of two that brings max |x| into
+          // [2^21, 2^22), so that x = (L2 2^16 + L1 2^8 + L0) 2^-sh with signed byte limbs
+          // |L2| <= 64, |L1|, |L0| <= 128 (an integer-valued x stays exact).
+          int e = 1;
+          if (mx > 0.f && isfinite(mx)) frexpf(mx, &e);  // mx = f * 2^e, f in [0.5, 1)
+          const int shv = mx > 0.f ? max(-126, min(126, 22 - e)) : 0;
+          const float sc = ldexpf(1.f, shv);
+          if (lane == 0) {
+            s_sq[warp][0] += sq;
+            ublk[kb] = ldexpf(1.f, -shv);
+          }
+          uint32_t pk[3][2] = {{0u, 0u}, {0u, 0u}, {0u, 0u}};  // limb bytes, 4 to a word
+          int tl[3] = {0, 0, 0};                              // per-limb sums (Q6_K)
+          int tx = 0;                                         // sum of X (Q4_K, Q5_K)
+#pragma unroll
+          for (int i = 0; i < 8; ++i) {
+            const int X = __float2int_rn(v[j][i] * sc);
+            const int l0 = ((X + 128) & 255) - 128;
+            const int x1 = (X - l0) >> 8;
+            const int l1 = ((x1 + 128) & 255) - 128;
+            const int l2 = (x1 - l1) >> 8;
+            const uint32_t sft = 8 * (i & 3);
+            pk[0][i >> 2] |= (static_cast<uint32_t>(l0) & 0xffu) << sft;
+            pk[1][i >> 2] |= (static_cast<uint32_t>(l1) & 0xffu) << sft;
+            pk[2][i >> 2] |= (static_cast<uint32_t>(l2) & 0xffu) << sft;
+            tl[0] += l0, tl[1] += l1, tl[2] += l2;
+            tx += X;
+          }
+          // chunk `lane` of the block: 24 bytes, 8 of each limb
+          const uint32_t at = table_s + (kb * 32 + lane) * 24;
+#pragma unroll
+          for (int l = 0; l < 3; ++l)
+            asm volatile("st.shared.v2.u32 [%0], {%1, %2};" ::"r"(at + 8 * l), "r"(pk[l][0]), "r"(pk[l][1])
+                         : "memory");
+          if constexpr (QT == 6) {
+            // C init of the MMAs: -32 * (sum of each limb over each 16-element sub-block), so that
+            // A = q (unsigned) gives sum (q - 32) x exactly; sub-block sb is lanes 2 sb, 2 sb + 1.
+            // Entry ((kb * 2 + half) * 3 + l) * 8 + (sub-block within the half).
+            const uint32_t sb = lane >> 1;
+#pragma unroll
+            for (int l = 0; l < 3; ++l) {
+              const int t = tl[l] + __shfl_xor_sync(0xffffffffu, tl[l], 1);
+              if ((lane & 1) == 0)
+                asm volatile("st.shared.s32 [%0], %1;" ::"r"(
+                                 mtable_s + ((kb * 2 + (sb >> 3)) * 24 + l * 8 + (sb & 7)) * 4),
+                             "r"(-32 * t)
+                             : "memory");
+            }
+          } else {
+            // the sum of x (in limb units) over each 32-element sub-block, lanes 4 r .. 4 r + 3,
+            // for the min term
+            int t = tx + __shfl_xor_sync(0xffffffffu, tx, 1);
+            t += __shfl_xor_sync(0xffffffffu, t, 2);
+            if ((lane & 3) == 0)
+              asm volatile("st.shared.f32 [%0], %1;" ::"r"(mtable_s + (kb * 8 + (lane >> 2)) * 4),
+                           "f"(static_cast<float>(t))
+                           : "memory");
+          }
+        }
+      }
+    } else {
     const uint32_t nxb = a.nb * B;
     for (uint32_t xb0 = warp; xb0 < nxb; xb0 += 4 * nw) {
       float v[4][8];
@@ -900,73 +1069,7 @@ __device__ __forceinline__ void consume_job(const WarpMmaArgs& a, const JobArgs&
 #pragma unroll
           for (int o = 16; o; o >>= 1) sq += __shfl_xor_sync(0xffffffffu, sq, o);
         }
-        if constexpr (I8) {
-          // 24-bit fixed point for the block: the power of two that brings max |x| into
-          // [2^21, 2^22), so that x = (L2 2^16 + L1 2^8 + L0) 2^-sh with signed byte limbs
-          // |L2| <= 64, |L1|, |L0| <= 128 (an integer-valued x stays exact).
-          int e = 1;
-          if (mx > 0.f && isfinite(mx)) frexpf(mx, &e);  // mx = f * 2^e, f in [0.5, 1)
-          const int sh = mx > 0.f ? max(-126, min(126, 22 - e)) : 0;
-          const float sc = ldexpf(1.f, sh);
-          if (lane == 0) {
-            s_sq[warp][b] += sq;
-            ublk[b * a.nb + kb] = ldexpf(1.f, -sh);
-          }
-          int L[3][8];
-#pragma unroll
-          for (int r = 0; r < 8; ++r) {
-            const int X = __float2int_rn(v[j][r] * sc);
-            const int l0 = ((X + 128) & 255) - 128;
-            const int x1 = (X - l0) >> 8;
-            const int l1 = ((x1 + 128) & 255) - 128;
-            L[0][r] = l0;
-            L[1][r] = l1;
-            L[2][r] = (x1 - l1) >> 8;
-            // element 32 r + lane of the block: chunk 4 r + lane / 8 (24 bytes: 8 of each limb)
-            const uint32_t at = table_s + (kb * 32 + 4 * r + (lane >> 3)) * 24 + (lane & 7);
-#pragma unroll
-            for (int l = 0; l < 3; ++l)
-              asm volatile("st.shared.u8 [%0], %1;" ::"r"(at + 8 * l), "r"(L[l][r]) : "memory");
-          }
-          if constexpr (QT == 6) {
-            // C init of the MMAs: -32 * (sum of each limb over each 16-element sub-block), so
-            // that A = q (unsigned) gives sum (q - 32) x exactly. The 48 sums (3 limbs x 16
-            // sub-blocks) are read back from the table just written: sub-block sb of the block
-            // is chunks 2 sb and 2 sb + 1, limb l the 8 bytes at 8 l of each; one dp4a per 4
-            // bytes. Lane i takes sums i and i + 32.
-            __syncwarp();
-#pragma unroll
-            for (int pass = 0; pass < 2; ++pass) {
-              const uint32_t i = lane + 32 * pass;
-              if (i < 48) {
-                const uint32_t l = i >> 4, sb = i & 15;
-                const uint32_t at = table_s + (kb * 32 + 2 * sb) * 24 + 8 * l;
-                const uint2 w0 = lds_v2(at), w1 = lds_v2(at + 24);
-                int t = __dp4a(static_cast<int>(w0.x), 0x01010101, 0);
-                t = __dp4a(static_cast<int>(w0.y), 0x01010101, t);
-                t = __dp4a(static_cast<int>(w1.x), 0x01010101, t);
-                t = __dp4a(static_cast<int>(w1.y), 0x01010101, t);
-                // entry ((kb * 2 + half) * 3 + l) * 8 + (sub-block within the half)
-                asm volatile("st.shared.s32 [%0], %1;" ::"r"(
-                                 mtable_s + ((kb * 2 + (sb >> 3)) * 24 + l * 8 + (sb & 7)) * 4),
-                             "r"(-32 * t)
-                             : "memory");
-              }
-            }
-          } else {
-            // the sum of x (in limb units) over each 32-element sub-block r, for the min term
-#pragma unroll
-            for (int r = 0; r < 8; ++r) {
-              int t = (L[2][r] << 16) + (L[1][r] << 8) + L[0][r];
-#pragma unroll
-              for (int o = 16; o; o >>= 1) t += __shfl_xor_sync(0xffffffffu, t, o);
-              if (lane == 0)
-                asm volatile("st.shared.f32 [%0], %1;" ::"r"(mtable_s + (kb * 8 + r) * 4),
-                             "f"(static_cast<float>(t))
-                             : "memory");
-            }
-          }
-        } else {
+        {
           int e = 1;
           if (mx > 0.f && isfinite(mx)) frexpf(mx, &e);  // mx = f * 2^e, f in [0.5, 1)
           const int sh = (e > kTarget || e <= 0) ? max(-126, min(126, kTarget - e)) : 0;
@@ -1044,6 +1147,7 @@ __device__ __forceinline__ void consume_job(const WarpMmaArgs& a, const JobArgs&
 
         }
       }
+    }
     }
     // a zeroed region that lanes without a B column read their fragments from
     for (uint32_t i = tid; i < kZeroBytes / 4; i += nthr)
@@ -1216,16 +1320,16 @@ __device__ __forceinline__ void consume_job(const WarpMmaArgs& a, const JobArgs&
         yacc[r][0] += __shfl_xor_sync(0xffffffffu, yacc[r][0], 2);
       }
       if (c == 0) {
-        red[((bi * kTileRows + pg) * nw + warp) * B] = yacc[0][0];
-        red[((bi * kTileRows + ph) * nw + warp) * B] = yacc[1][0];
+        red[((bi * nw + warp) * kTileRows + pg) * B] = yacc[0][0];
+        red[((bi * nw + warp) * kTileRows + ph) * B] = yacc[1][0];
       }
     } else {
 #pragma unroll
       for (int j = 0; j < 2; ++j) {
         const uint32_t b = (HILO && NT == 1) ? (j == 0 ? c : 8u) : 2 * c + j;
         if (b < B) {
-          red[((bi * kTileRows + pg) * nw + warp) * B + b] = yacc[0][j];
-          red[((bi * kTileRows + ph) * nw + warp) * B + b] = yacc[1][j];
+          red[((bi * nw + warp) * kTileRows + pg) * B + b] = yacc[0][j];
+          red[((bi * nw + warp) * kTileRows + ph) * B + b] = yacc[1][j];
         }
       }
     }
@@ -1245,14 +1349,15 @@ __device__ __forceinline__ void consume_job(const WarpMmaArgs& a, const JobArgs&
         const uint32_t row = r_begin + (band0 + bj) * kTileRows + row16;
         if (row >= r_end) continue;
         float v0 = 0.f;
-        const float* rp = red + ((bj * kTileRows + row16) * nw) * B + b;
-        for (uint32_t w = 0; w < nw; ++w) v0 += rp[w * B];
+        // (band-major, then warp, then row: the threads of a warp read consecutive rows)
+        const float* rp = red + (bj * nw * kTileRows + row16) * B + b;
+        for (uint32_t w = 0; w < nw; ++w) v0 += rp[w * kTileRows * B];
         v0 *= s_ns[b];
         uint32_t out = row;
         if (R != 1) {
           float v1 = 0.f;
-          const float* rq = rp + nw * B;
-          for (uint32_t w = 0; w < nw; ++w) v1 += rq[w * B];
+          const float* rq = rp + B;
+          for (uint32_t w = 0; w < nw; ++w) v1 += rq[w * kTileRows * B];
           v1 *= s_ns[b];
           v0 = pair_value(v0, v1, mj.epilogue, mj.pair_scale);
           out = row / 2;
