@@ -178,6 +178,21 @@ struct WarpMmaShared {
   uint32_t x_slots;         // tagged x: the slots (split-K parts, K elements apart) summed per element
 };
 
+// Tiles the producer issues before it waits for the previous kernel to finish (when the consumers
+// start loading x), in a CTA with at most kHoldMaxTiles tiles: the rest of the ring would queue
+// ahead of those loads, and for a short matrix the x prologue is most of a launch's critical path.
+// A long matrix keeps its whole head start.
+constexpr uint32_t kHoldTiles = 2, kHoldMaxTiles = 16;
+
+// The exponent e of a positive finite float v = f * 2^e, f in [0.5, 1) (frexpf's, for a normal v;
+// for a subnormal v it gives -126, at or below which every caller clamps alike).
+__device__ __forceinline__ int exponent_of(float v) {
+  return static_cast<int>((__float_as_uint(v) >> 23) & 255u) - 126;
+}
+
+// 2^s as a float, s in [-126, 127].
+__device__ __forceinline__ float pow2f(int s) { return __uint_as_float(static_cast<uint32_t>(s + 127) << 23); }
+
 // 8 bytes of a tagged vector: the f32 value (low word) and its tag (high word), one aligned 8-byte
 // load (so value and tag come from the same store), cached in L2 only: other GPUs' stores into
 // this GPU's memory land in its L2, so a repeated load sees them, and the L1 (not coherent) is
@@ -676,6 +691,9 @@ __device__ __forceinline__ bool produce_job(const WarpMmaArgs& a, const JobArgs&
   const uint64_t pol = policy_evict_first();
   const uint64_t end_floor = v.total_bytes & ~uint64_t(15);
   for (uint32_t t = 0; t < ntiles; ++t) {
+    // hold until the previous kernel is done, when the consumers load x (a no-op when the
+    // weights are not static: the producer has waited for it already)
+    if (issued == kHoldTiles && issued < a.ring && ntiles <= kHoldMaxTiles) pdl_wait();
     if (issued >= a.ring) {
       int ok = 1;
       if (lane == 0) {
@@ -917,12 +935,12 @@ __device__ __forceinline__ void consume_job(const WarpMmaArgs& a, const JobArgs&
           // [2^21, 2^22), so that x = (L2 2^16 + L1 2^8 + L0) 2^-sh with signed byte limbs
           // |L2| <= 64, |L1|, |L0| <= 128 (an integer-valued x stays exact).
           int e = 1;
-          if (mx > 0.f && isfinite(mx)) frexpf(mx, &e);  // mx = f * 2^e, f in [0.5, 1)
+          if (mx > 0.f && isfinite(mx)) e = exponent_of(mx);  // mx = f * 2^e, f in [0.5, 1)
           const int shv = mx > 0.f ? max(-126, min(126, 22 - e)) : 0;
-          const float sc = ldexpf(1.f, shv);
+          const float sc = pow2f(shv);
           if (lane == 0) {
             s_sq[warp][0] += sq;
-            ublk[kb] = ldexpf(1.f, -shv);
+            ublk[kb] = pow2f(-shv);
           }
           uint32_t pk[3][2] = {{0u, 0u}, {0u, 0u}, {0u, 0u}};  // limb bytes, 4 to a word
           int tl[3] = {0, 0, 0};                              // per-limb sums (Q6_K)
@@ -1071,12 +1089,12 @@ __device__ __forceinline__ void consume_job(const WarpMmaArgs& a, const JobArgs&
         }
         {
           int e = 1;
-          if (mx > 0.f && isfinite(mx)) frexpf(mx, &e);  // mx = f * 2^e, f in [0.5, 1)
+          if (mx > 0.f && isfinite(mx)) e = exponent_of(mx);  // mx = f * 2^e, f in [0.5, 1)
           const int sh = (e > kTarget || e <= 0) ? max(-126, min(126, kTarget - e)) : 0;
-          const float sc = ldexpf(1.f, sh);
+          const float sc = pow2f(sh);
           if (lane == 0) {
             s_sq[warp][b] += sq;
-            ublk[b * a.nb + kb] = ldexpf(1.f, -sh);
+            ublk[b * a.nb + kb] = pow2f(-sh);
           }
   #pragma unroll
           for (int r = 0; r < 8; ++r) v[j][r] *= sc;
