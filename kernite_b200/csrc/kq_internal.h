@@ -1,6 +1,7 @@
 // kq_internal.h -- what the library's translation units share (host side).
 #pragma once
 
+#include <cuda.h>
 #include <cuda_runtime.h>
 
 #include <cstdint>
@@ -53,6 +54,13 @@ bool mma_supports(const kq_matvec_desc& d);
 int mma_matvec(kq_ctx* ctx, const kq_matvec_desc& d, uint64_t ldx, uint64_t ldy,
                cudaStream_t stream);
 uint64_t mma_scratch_bytes(uint32_t k, uint32_t batch);
+// cuTensorMapEncodeTiled (through the runtime's driver entry point; the library links only the
+// runtime) of a rank-`rank` tiled map over `base`: dims and box innermost first, strides in bytes
+// of dims 1.., no interleave, no swizzle, L2 promotion 256 B, zero fill. KQ_OK, or KQ_E_UNSUPPORTED
+// when the driver has no such call, KQ_E_INVALID when it refuses the map.
+int encode_tensor_map(CUtensorMap* map, CUtensorMapDataType type, uint32_t rank, const void* base,
+                      const uint64_t* dims, const uint64_t* strides, const uint32_t* box,
+                      const char* call);
 int matvec(kq_ctx* ctx, const kq_matvec_desc& d, cudaStream_t stream,
            const kq_push_desc* push = nullptr);
 // The argument checks every matvec entry point makes before a launch (KQ_E_INVALID on failure).

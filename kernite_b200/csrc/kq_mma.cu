@@ -451,18 +451,13 @@ int mma_launch(const char* call, int sm_count, int qt, uint64_t w, uint64_t x, u
   tm = std::min<uint32_t>(kTileM, std::max<uint32_t>(tm, std::min<uint32_t>(rows, 16)));
   const uint32_t ntiles = (rows + tm - 1) / tm;
 
-  const EncodeTiled encode = encode_tiled();
-  if (!encode) return fail(KQ_E_UNSUPPORTED, call, "the driver has no cuTensorMapEncodeTiled");
   CUtensorMap map;
-  const cuuint64_t dims[2] = {uint64_t(nb) * blk, rows};
-  const cuuint64_t strides[1] = {uint64_t(nb) * blk};
-  const cuuint32_t box[2] = {blk, tm};
-  const cuuint32_t estr[2] = {1, 1};
-  const CUresult r = encode(&map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, reinterpret_cast<void*>(w), dims, strides,
-                            box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
-                            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  if (r != CUDA_SUCCESS)
-    return fail(KQ_E_INVALID, call, "cuTensorMapEncodeTiled refused W (error " + std::to_string(int(r)) + ")");
+  const uint64_t dims[2] = {uint64_t(nb) * blk, rows};
+  const uint64_t strides[1] = {uint64_t(nb) * blk};
+  const uint32_t box[2] = {blk, tm};
+  const int erc = encode_tensor_map(&map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, reinterpret_cast<const void*>(w),
+                                    dims, strides, box, call);
+  if (erc) return erc;
 
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
@@ -509,6 +504,27 @@ int mma_launch(const char* call, int sm_count, int qt, uint64_t w, uint64_t x, u
 }
 
 }  // namespace
+
+int encode_tensor_map(CUtensorMap* map, CUtensorMapDataType type, uint32_t rank, const void* base,
+                      const uint64_t* dims, const uint64_t* strides, const uint32_t* box,
+                      const char* call) {
+  const EncodeTiled encode = encode_tiled();
+  if (!encode) return fail(KQ_E_UNSUPPORTED, call, "the driver has no cuTensorMapEncodeTiled");
+  cuuint64_t d[5], st[4];
+  cuuint32_t b[5], e[5];
+  for (uint32_t i = 0; i < rank; ++i) {
+    d[i] = dims[i];
+    b[i] = box[i];
+    e[i] = 1;
+    if (i + 1 < rank) st[i] = strides[i];
+  }
+  const CUresult r = encode(map, type, rank, const_cast<void*>(base), d, st, b, e, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                            CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS)
+    return fail(KQ_E_INVALID, call, "cuTensorMapEncodeTiled refused W (error " + std::to_string(int(r)) + ")");
+  return KQ_OK;
+}
 
 int mma_prepare(kq_ctx* ctx) {
   const cudaError_t e = set_smem_limits();

@@ -116,6 +116,11 @@ struct WarpMmaArgs {
   uint32_t ksplit;       // CTAs sharing each row range, each its 1/ksplit of the K-tiles (1: none)
   uint32_t row_unit, prologue, epilogue, flags;
   float eps, pair_scale;
+  // 1: the tiles of whole bands come in by the tensor map (one 3-D TMA copy of 16 rows), rows
+  // tile_pitch bytes apart; a CTA's last band of fewer than 16 rows still goes row by row, at the
+  // same pitch
+  uint32_t tmap_mode, tile_pitch;
+  CUtensorMap tmap;  // W as [rows][super-blocks][block bytes] (Q6_K: [rows][8-block groups][1680 B])
 };
 
 // A matvec that is one job of a chain (one launch running several matvecs of one type and k in
@@ -663,6 +668,17 @@ __device__ __forceinline__ void init_ring(const WarpMmaArgs& a, uint8_t* base, W
   __syncthreads();
 }
 
+// A 3-D tiled TMA copy of box (x, y, z) of `tmap` (a kernel parameter) into shared `dst`,
+// completing on `bar`; no multicast.
+__device__ __forceinline__ void tma_load_3d(uint32_t dst, const CUtensorMap* tmap, uint32_t x, uint32_t y,
+                                            uint32_t z, uint32_t bar, uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes.L2::cache_hint"
+      " [%0], [%1, {%2, %3, %4}], [%5], %6;" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(tmap)), "r"(x), "r"(y), "r"(z), "r"(bar), "l"(policy)
+      : "memory");
+}
+
 // The producer warp's part of one matvec: the tiles of this CTA's rows, each into the next ring
 // slot once the consumers have freed it. Lane r of the warp copies row r of a tile (16 rows, one
 // bulk copy each, at the padded pitch), or lane 0 the tile's rows in one copy; lane 0 posts the
@@ -714,6 +730,20 @@ __device__ __forceinline__ bool produce_job(const WarpMmaArgs& a, const JobArgs&
     // K-tile kt: super-blocks [kc0, kc1), kq + (kt < kr) of them (the consumers' split)
     const uint32_t kq = a.nb / a.nkt, kr = a.nb % a.nkt;
     const uint32_t kc0 = kt * kq + min(kt, kr), kc1 = kc0 + kq + (kt < kr ? 1u : 0u);
+    if (a.tmap_mode && r1 - r0 == kTileRows) {
+      // a whole band by the tensor map, one copy
+      if (lane == 0) {
+        mbar_arrive_expect_tx(full_bar(s), kTileRows * a.tile_pitch);
+        tma_load_3d(slot, &a.tmap, 0, QT == 6 ? kc0 / 8 : kc0, r0, full_bar(s), pol);  // Q6_K: groups
+      }
+      __syncwarp();
+      ++issued;
+      if (++s == a.ring) {
+        s = 0;
+        phase ^= 1;
+      }
+      continue;
+    }
     const uint32_t r = r0 + lane;
     uint64_t a0 = 0, a1 = 0;
     if (a.seg_bytes == 0) {
@@ -751,7 +781,11 @@ __device__ __forceinline__ bool produce_job(const WarpMmaArgs& a, const JobArgs&
     __syncwarp();
     if (lane == 0) mbar_arrive_expect_tx(full_bar(s), total);
     __syncwarp();
-    if (a.split_tile) {
+    if (a.tmap_mode) {
+      // a band of fewer than 16 rows: row by row at the tensor-map layout's pitch (the rows start
+      // on 16-byte boundaries, so each copy is exactly the row's K-tile)
+      if (bytes) bulk_g2s(slot + lane * a.tile_pitch, v.W + a0, bytes, full_bar(s), pol);
+    } else if (a.split_tile) {
       // rows r0..r0+7 at the slot, rows r0+8.. kSplitGap bytes past where they would follow
       // (rows are whole and start on 16-byte boundaries here, so a1 - a0 = (r1 - r0) * RB)
       if (lane == 0 && bytes) {
@@ -1224,9 +1258,11 @@ __device__ __forceinline__ void consume_job(const WarpMmaArgs& a, const JobArgs&
   // kq + (kt < kr) super-blocks (the producer splits the same way).
   const uint32_t nkt = a.nkt, kq = a.nb / nkt, kr = a.nb % nkt;
   const uint32_t rb32 = static_cast<uint32_t>(RB);
-  // byte offsets of tile rows pg and ph in a whole-row slot
-  const uint32_t pg_rb = pg * rb32 + (a.split_tile && pg >= 8 ? kSplitGap : 0u);
-  const uint32_t ph_rb = ph * rb32 + (a.split_tile && ph >= 8 ? kSplitGap : 0u);
+  // byte offsets of tile rows pg and ph in a whole-row slot (or a tensor-map slot, whose rows are
+  // tile_pitch bytes apart)
+  const uint32_t pitch = a.tmap_mode ? a.tile_pitch : rb32;
+  const uint32_t pg_rb = pg * pitch + (a.split_tile && pg >= 8 ? kSplitGap : 0u);
+  const uint32_t ph_rb = ph * pitch + (a.split_tile && ph >= 8 ? kSplitGap : 0u);
   // When every row starts on a 16-byte boundary, a block's offset within 16 bytes is the same
   // for all rows of a warp: (kb * block bytes) mod 16.
   const bool rows16 = (rb32 & 15u) == 0;
@@ -1532,9 +1568,10 @@ __device__ __forceinline__ void consume_job(const WarpMmaArgs& a, const JobArgs&
     if (kb < kc1 && !failed) {
       // shared-memory addresses of this block in rows g and g+8 of the tile
       uint32_t ag, ah;
-      if (a.seg_bytes == 0) {
-        // whole rows back to back from the tile's aligned start
-        const uint32_t delta = (r0 * rb32) & 15u;
+      if (a.seg_bytes == 0 || a.tmap_mode) {
+        // whole rows back to back from the tile's aligned start (tensor-map slots: rows on
+        // 16-byte boundaries, from the slot's start)
+        const uint32_t delta = a.tmap_mode ? 0u : (r0 * rb32) & 15u;
         ag = slot + delta + pg_rb + j * kBlk;
         ah = slot + delta + ph_rb + j * kBlk;
       } else {
@@ -1649,7 +1686,7 @@ __device__ __forceinline__ void consume_job(const WarpMmaArgs& a, const JobArgs&
 // bytes, x as three signed byte limbs (24-bit fixed point per 256-element block), the eight MMA
 // columns separating sub-blocks.
 template <int QT, int NT, bool HILO, bool I8>
-__global__ void __launch_bounds__((kMaxWarps + 1) * 32, 1) warpmma_kernel(const WarpMmaArgs a) {
+__global__ void __launch_bounds__((kMaxWarps + 1) * 32, 1) warpmma_kernel(const __grid_constant__ WarpMmaArgs a) {
   extern __shared__ __align__(128) uint8_t smem[];
   __shared__ WarpMmaShared sh;
   uint8_t* base = smem_base(smem);
@@ -1714,7 +1751,7 @@ __device__ __forceinline__ bool wait_at_least(unsigned* err, const unsigned long
 // the start, the wait overlapping the first tiles' copies.
 template <int QT, int TXS>
 __global__ void __launch_bounds__((kMaxWarps + 1) * 32, 1)
-    warpmma_push_kernel(const WarpMmaArgs a, const __grid_constant__ PushArgs q) {
+    warpmma_push_kernel(const __grid_constant__ WarpMmaArgs a, const __grid_constant__ PushArgs q) {
   constexpr bool TX = TXS > 0;
   extern __shared__ __align__(128) uint8_t smem[];
   __shared__ WarpMmaShared sh;
@@ -2057,12 +2094,56 @@ int warpmma_plan(kq_ctx* ctx, const kq_matvec_desc& d, uint64_t ldx, uint64_t ld
   // from the last slot, in the table that follows the ring, and feed outputs nobody stores.
   // (Segmented tiles only, whose rows each have their own copy; chains keep full slots, so that
   // every job of a launch has one layout.)
-  if (compact && seg != 0) {
-    const uint32_t ru = d.epilogue != KQ_EPILOGUE_NONE ? 2 : 1;
-    const uint64_t units = d.rows / ru;
-    const uint64_t groups =
-        std::max<uint64_t>(1, std::min<uint64_t>(ctx->sm_count / std::max<uint32_t>(ksplit, 1), units));
-    const uint64_t rpc = (units + groups - 1) / groups * ru;  // rows of the fullest CTA
+  //
+  // K-tiled rows (segmented tiles) of a CTA with three whole bands or more (with fewer, measured
+  // slower: 70B 2-way q|k|v 12.6 -> 13.7 us, o 9.9 -> 10.6 us): the whole bands come in
+  // by a 3-D tensor map, one TMA copy per tile (two for a split tile) instead of one bulk copy
+  // per row, whose per-copy cost capped the producer (measured on B200: one copy per tile made
+  // the 70B gate|up 20% faster). It needs equal K-tiles, rows and K-tiles on 16-byte boundaries
+  // (Q6_K: K-tiles of whole 8-block groups, 1680 bytes) and a row pitch the consumers' loads
+  // take without bank conflicts (the box lands in one piece, its rows back to back, so that its
+  // shared-memory start stays on 128 bytes): Q4_K and Q5_K rows 16 mod 32 bytes apart, the box
+  // one block wider than the K-tile when the K-tile alone is 0 mod 128 (the extra block is the
+  // next K-tile's first, read again from L2, or past the row's end, filled with zeros); Q6_K rows
+  // 64 mod 128 apart, or 32 / 96 with MMA rows paired two apart, as for whole-row tiles.
+  const uint32_t ru = d.epilogue != KQ_EPILOGUE_NONE ? 2 : 1;
+  const uint64_t units = d.rows / ru;
+  const uint64_t groups =
+      std::max<uint64_t>(1, std::min<uint64_t>(ctx->sm_count / std::max<uint32_t>(ksplit, 1), units));
+  const uint64_t rpc = (units + groups - 1) / groups * ru;  // rows of the fullest CTA
+  bool tmap = false, tperm = false;
+  uint32_t kbox = nwc;            // blocks in a box row
+  uint32_t tp = nwc * blk;        // the tensor-map layout's row pitch
+  if (compact && seg != 0 && rpc >= 3 * kTileRows && nb % nkt == 0 && rb % 16 == 0 &&
+      (q45 || (nb % 8 == 0 && nwc % 8 == 0))) {
+    if (q45) {
+      if (tp % 32 != 16) kbox = nwc + 1, tp = kbox * blk;
+      tmap = tp % 32 == 16;
+    } else {
+      const uint32_t res = tp % 128;
+      tperm = res == 32 || res == 96;
+      tmap = tperm || res == 64;
+    }
+  }
+  CUtensorMap tm_map;
+  if (tmap) {
+    std::memset(&tm_map, 0, sizeof(tm_map));
+    int erc;
+    if (q45) {
+      const uint64_t dims[3] = {blk, nb, d.rows}, strides[2] = {blk, rb};
+      const uint32_t box[3] = {blk, kbox, kTileRows};
+      erc = encode_tensor_map(&tm_map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, reinterpret_cast<const void*>(d.w),
+                              dims, strides, box, call);
+    } else {
+      const uint64_t dims[3] = {kQ6KBytes, nb / 8, d.rows}, strides[2] = {8 * kQ6KBytes, rb};
+      const uint32_t box[3] = {kQ6KBytes, nwc / 8, kTileRows};  // 8 blocks = 210 8-byte words
+      erc = encode_tensor_map(&tm_map, CU_TENSOR_MAP_DATA_TYPE_UINT64, 3, reinterpret_cast<const void*>(d.w),
+                              dims, strides, box, call);
+    }
+    if (erc) return erc;
+    seg = tp;
+    slot = static_cast<uint32_t>(((uint64_t(kTileRows) * tp + 127) / 128) * 128);
+  } else if (compact && seg != 0) {
     const uint32_t cslot = static_cast<uint32_t>(((rpc * seg + 127) / 128) * 128);
     if (rpc < kTileRows && kTileRows * seg - cslot <= table_bytes + mtable_bytes) slot = cslot;
   }
@@ -2100,8 +2181,12 @@ int warpmma_plan(kq_ctx* ctx, const kq_matvec_desc& d, uint64_t ldx, uint64_t ld
   args.zero_off = args.ublk_off + ublk_bytes;
   args.red_off = args.zero_off + kZeroBytes;
   args.zero = 0;
-  args.row_perm = row_perm;
-  args.split_tile = (seg == 0 && split) ? 1u : 0u;
+  args.row_perm = tmap ? (tperm ? 1u : 0u) : row_perm;
+  args.split_tile = tmap ? 0u : (seg == 0 && split) ? 1u : 0u;
+  args.tmap_mode = tmap ? 1u : 0u;
+  args.tile_pitch = tmap ? tp : 0u;
+  if (tmap) args.tmap = tm_map;
+  else std::memset(&args.tmap, 0, sizeof(args.tmap));
   args.fixed_blocks = (fixed_ok && nw == nwc) ? 1u : 0u;
   args.bars_off = args.red_off + red_bytes;
   args.ncol = ncol;
@@ -2115,7 +2200,6 @@ int warpmma_plan(kq_ctx* ctx, const kq_matvec_desc& d, uint64_t ldx, uint64_t ld
   args.pair_scale = d.pair_scale;
   const uint32_t smem = args.bars_off + 2 * 8 * 8 + 128;
 
-  const uint64_t units = d.rows / args.row_unit;
   plan.args = args;
   plan.mode = mode;
   plan.smem = smem;
@@ -2153,7 +2237,7 @@ bool same_layout(const WarpMmaArgs& a, const WarpMmaArgs& b) {
          a.zero_off == b.zero_off && a.red_off == b.red_off && a.bars_off == b.bars_off &&
          a.row_perm == b.row_perm && a.split_tile == b.split_tile &&
          a.fixed_blocks == b.fixed_blocks && a.ncol == b.ncol && a.fb == b.fb &&
-         a.ksplit == b.ksplit;
+         a.ksplit == b.ksplit && a.tmap_mode == b.tmap_mode && a.tile_pitch == b.tile_pitch;
 }
 
 }  // namespace

@@ -95,6 +95,9 @@ SHAPES = [
     (4, 500, 4096, 2), (4, 300, 4096, 3), (4, 301, 4096, 4), (4, 150, 4096, 5), (4, 200, 4096, 8),
     (6, 500, 4096, 2), (6, 299, 4096, 3), (6, 301, 4096, 4), (6, 151, 4096, 7), (6, 200, 4096, 8),
     (4, 100, 11008, 2), (6, 100, 11008, 2),
+    # K-tiled rows with whole 16-row bands (tensor-map tiles on the warp-MMA kernel) and a last
+    # band of a few rows
+    (4, 3000, 8192, 1), (6, 2400, 16384, 1), (4, 2400, 8192, 2), (4, 2600, 12288, 2),
 ]
 
 

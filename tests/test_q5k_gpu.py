@@ -81,6 +81,8 @@ def test_q5k_device_dequant_matches_oracle_on_generated(kernels):
 SHAPES = [  # (rows, K)
     (1, 256), (15, 256), (16, 512), (17, 4096), (148, 4096), (300, 4096), (4096, 4096),
     (1000, 4352), (257, 8192), (300, 11008), (3, 11008), (64, 28672), (77, 2816),
+    # K-tiled rows with whole 16-row bands (tensor-map tiles) and a last band of a few rows
+    (4096, 8192), (2500, 16384),
 ]
 
 
