@@ -2095,8 +2095,9 @@ int warpmma_plan(kq_ctx* ctx, const kq_matvec_desc& d, uint64_t ldx, uint64_t ld
   // (Segmented tiles only, whose rows each have their own copy; chains keep full slots, so that
   // every job of a launch has one layout.)
   //
-  // K-tiled rows (segmented tiles) of a CTA with three whole bands or more (with fewer, measured
-  // slower: 70B 2-way q|k|v 12.6 -> 13.7 us, o 9.9 -> 10.6 us): the whole bands come in
+  // K-tiled rows (segmented tiles) of a CTA with a whole band (Q4_K, Q5_K: three whole bands; with
+  // fewer, measured slower: 70B 2-way q|k|v 12.6 -> 13.7 us, o 9.9 -> 10.6 us, while the Q6_K
+  // down projection gained at any band count, 2-way 39.1 -> 35.5 us): the whole bands come in
   // by a 3-D tensor map, one TMA copy per tile (two for a split tile) instead of one bulk copy
   // per row, whose per-copy cost capped the producer (measured on B200: one copy per tile made
   // the 70B gate|up 20% faster). It needs equal K-tiles, rows and K-tiles on 16-byte boundaries
@@ -2114,7 +2115,7 @@ int warpmma_plan(kq_ctx* ctx, const kq_matvec_desc& d, uint64_t ldx, uint64_t ld
   bool tmap = false, tperm = false;
   uint32_t kbox = nwc;            // blocks in a box row
   uint32_t tp = nwc * blk;        // the tensor-map layout's row pitch
-  if (compact && seg != 0 && rpc >= 3 * kTileRows && nb % nkt == 0 && rb % 16 == 0 &&
+  if (compact && seg != 0 && rpc >= (q45 ? 3u : 1u) * kTileRows && nb % nkt == 0 && rb % 16 == 0 &&
       (q45 || (nb % 8 == 0 && nwc % 8 == 0))) {
     if (q45) {
       if (tp % 32 != 16) kbox = nwc + 1, tp = kbox * blk;
