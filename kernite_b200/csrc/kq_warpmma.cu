@@ -1497,6 +1497,47 @@ __device__ __forceinline__ void consume_job(const WarpMmaArgs& a, const JobArgs&
   }
   // The same for Q4_K (144-byte blocks: every block starts on a 16-byte boundary, one loop):
   // the block's table addresses, scale of x and (integer path) sums of x are warp constants.
+  if constexpr ((QT == 4 || QT == 5) && I8 && TXS == 0) {
+    if (a.fixed_blocks && a.tmap_mode) {
+      // Tensor-map tiles of K-tiled rows: warp w takes block w of every K-tile (all K-tiles have
+      // the same width); the row offsets are the same in every tile, the block's x constants
+      // (table addresses, scale, sums) change with the K-tile.
+      const uint32_t off_g = pg_rb + warp * kBlk, off_h = ph_rb + warp * kBlk;
+      uint32_t kt_lo, kt_hi;
+      cta_ktiles(nkt, a.ksplit, kt_lo, kt_hi);
+      uint32_t bi = 0;
+      for (uint32_t band = 0; band < nbands; ++band) {
+        for (uint32_t kt = kt_lo; kt < kt_hi; ++kt) {
+          const uint32_t kb = kt * kq + warp;
+          const float u0 = ublk_at(kb);
+          const uint32_t tc = table_s + (kb * 32 + 8 * c) * 24;
+          const uint32_t b0 = g == 2 * c ? tc : zero_s;
+          const uint32_t b1 = g == 2 * c + 1 ? tc + 4 * 24 : zero_s;
+          const uint2 xs = lds_v2(mtable_s + (kb * 8 + 2 * c) * 4);
+          const float2 X = make_float2(__uint_as_float(xs.x), __uint_as_float(xs.y));
+          bool ok = !*reinterpret_cast<volatile int*>(&s_failed);
+          if (ok && !mbar_wait(full_bar(s), phase)) {
+            ok = false;
+            s_failed = 1;
+            report_error(a.err, kErrWaitFull);
+          }
+          if (!__any_sync(0xffffffffu, !ok)) {
+            const uint32_t slot = ring_s + s * a.slot_bytes;
+            q4i8_block<QT == 5>(slot + off_g, slot + off_h, c, b0, b1, k28, sel_sc, m_lo, m_hi, sh_m, X, u0,
+                                yacc);
+          }
+          __syncwarp();
+          if (lane == 0) mbar_arrive(empty_bar(s));
+          if (++s == a.ring) {
+            s = 0;
+            phase ^= 1;
+          }
+        }
+        band_end(band, bi);
+      }
+      return;
+    }
+  }
   if constexpr (QT == 4 || QT == 5) {
     if (a.fixed_blocks) {
       const uint32_t kb = warp;
@@ -1986,7 +2027,7 @@ struct WarpMmaPlan {
 // Chooses the variant, the tiles and the shared-memory layout of one matvec (arguments already
 // checked by the caller), as the standalone launch uses them.
 int warpmma_plan(kq_ctx* ctx, const kq_matvec_desc& d, uint64_t ldx, uint64_t ldy, const char* call,
-                 WarpMmaPlan& plan, uint32_t ksplit = 1, bool compact = true) {
+                 WarpMmaPlan& plan, uint32_t ksplit = 1, bool compact = true, bool tmap_fixed = true) {
   const bool q4 = d.type == KQ_TYPE_Q4_K;
   const bool q5 = d.type == KQ_TYPE_Q5_K;  // Q4_K's layout plus qh: the Q4_K forms, integer only
   const bool q45 = q4 || q5;
@@ -2081,7 +2122,7 @@ int warpmma_plan(kq_ctx* ctx, const kq_matvec_desc& d, uint64_t ldx, uint64_t ld
   const bool fixed_ok = (q45 || mode == 5) && nkt == 1 && seg == 0 && rows16;
   const bool turns = fixed_ok ? false : q45 ? d.batch <= 4 : !rows16;
   const bool per_block = !turns != ((d.flags & kFlagWarpPerBlock) != 0);
-  const uint32_t nw = per_block ? nwc : kMaxWarps;
+  uint32_t nw = per_block ? nwc : kMaxWarps;
   const uint32_t rb128 = static_cast<uint32_t>(rb % 128);
   const uint32_t row_perm = (seg == 0 && (rb128 == 32 || rb128 == 96)) ? 1u : 0u;
   if (need_for(slot) > uint64_t(ctx->max_smem))
@@ -2144,6 +2185,8 @@ int warpmma_plan(kq_ctx* ctx, const kq_matvec_desc& d, uint64_t ldx, uint64_t ld
     if (erc) return erc;
     seg = tp;
     slot = static_cast<uint32_t>(((uint64_t(kTileRows) * tp + 127) / 128) * 128);
+    // Q4_K / Q5_K at batch 1: warp w fixed to block w of every K-tile, as for whole-row tiles
+    if (tmap_fixed && q45 && (mode == 4 || mode == 6) && !(d.flags & kFlagWarpPerBlock)) nw = nwc;
   } else if (compact && seg != 0) {
     const uint32_t cslot = static_cast<uint32_t>(((rpc * seg + 127) / 128) * 128);
     if (rpc < kTileRows && kTileRows * seg - cslot <= table_bytes + mtable_bytes) slot = cslot;
@@ -2188,7 +2231,7 @@ int warpmma_plan(kq_ctx* ctx, const kq_matvec_desc& d, uint64_t ldx, uint64_t ld
   args.tile_pitch = tmap ? tp : 0u;
   if (tmap) args.tmap = tm_map;
   else std::memset(&args.tmap, 0, sizeof(args.tmap));
-  args.fixed_blocks = (fixed_ok && nw == nwc) ? 1u : 0u;
+  args.fixed_blocks = ((fixed_ok || (tmap && tmap_fixed && q45)) && nw == nwc) ? 1u : 0u;
   args.bars_off = args.red_off + red_bytes;
   args.ncol = ncol;
   args.fb = fb;
@@ -2315,7 +2358,9 @@ int warpmma_push(kq_ctx* ctx, const kq_matvec_desc& d, const kq_push_desc& push,
   const char* call = "kq_matvec_push";
   WarpMmaPlan plan;
   // (the plan sizes its slots for the rows a CTA gets, which split K multiplies)
-  int rc = warpmma_plan(ctx, d, ldx, ldy, call, plan, std::min<uint32_t>(std::max<uint32_t>(push.ksplit, 1), 8));
+  // (no fixed-block loop on tensor-map tiles: the push kernels are compiled without it)
+  int rc = warpmma_plan(ctx, d, ldx, ldy, call, plan, std::min<uint32_t>(std::max<uint32_t>(push.ksplit, 1), 8),
+                        true, false);
   if (rc) return rc;
   if (plan.mode != (d.type == KQ_TYPE_Q4_K ? 4 : d.type == KQ_TYPE_Q5_K ? 6 : 5))
     return fail(KQ_E_UNSUPPORTED, call, "k " + std::to_string(d.k) + " does not fit the integer kernel");
