@@ -1440,6 +1440,67 @@ __device__ __forceinline__ void consume_job(const WarpMmaArgs& a, const JobArgs&
   // Q6_K integer path, tiles of whole rows on 16-byte boundaries, one warp per block: warp w
   // takes block w of every tile, so its block's offset within 16 bytes (2w mod 16) is fixed, and
   // the loop is compiled once per residue class, with every address but the slot's hoisted.
+  if constexpr (QT == 6 && I8 && TXS == 0) {
+    if (a.fixed_blocks && a.tmap_mode) {
+      // Tensor-map tiles of K-tiled rows: warp w takes block w of every K-tile (whose 16-byte
+      // residue, 2w mod 16, is the same in every tile); the x constants change with the K-tile.
+      const uint32_t fkb = warp;
+      const uint32_t off_g = pg_rb + fkb * kBlk, off_h = ph_rb + fkb * kBlk;
+      uint32_t kt_lo, kt_hi;
+      cta_ktiles(nkt, a.ksplit, kt_lo, kt_hi);
+      auto tmap_loop = [&](auto cls) {
+        constexpr int F = decltype(cls)::value;
+        uint32_t bi = 0;
+        for (uint32_t band = 0; band < nbands; ++band) {
+          for (uint32_t kt = kt_lo; kt < kt_hi; ++kt) {
+            const uint32_t kb = kt * kq + fkb;
+            const float u0 = ublk_at(kb);
+            const uint32_t tkb = table_s + (kb * 32 + 2 * c) * 24;
+            const uint32_t bA = g == c ? tkb : zero_s;
+            const uint32_t bB = g == c + 4 ? tkb + 8 * 24 : zero_s;
+            const uint32_t mkb = mtable_s + (kb * 48 + 2 * c) * 4;
+            bool ok = !*reinterpret_cast<volatile int*>(&s_failed);
+            if (ok && !mbar_wait(full_bar(s), phase)) {
+              ok = false;
+              s_failed = 1;
+              report_error(a.err, kErrWaitFull);
+            }
+            if (!__any_sync(0xffffffffu, !ok)) {
+              const uint32_t ag = ring_s + s * a.slot_bytes + off_g;
+              const uint32_t ah = ring_s + s * a.slot_bytes + off_h;
+              const float dg = u0 * h2f(lds_u16(ag + 208)), dh = u0 * h2f(lds_u16(ah + 208));
+#pragma unroll 1
+              for (uint32_t hf = 0; hf < 2; ++hf) {
+                uint32_t L[2][4], Q[2][4];
+#pragma unroll
+                for (int r = 0; r < 2; ++r) {
+                  const uint32_t base = r ? ah : ag;
+                  lds16_class<F>(base + 64 * hf + 16 * c, L[r]);
+                  lds16_class<F>(base + 128 + 32 * hf + 16 * (c & 1), Q[r]);
+                }
+                q6i8_half(hf, L, Q, ag, ah, c, mkb, bA, bB, k16, k28, sHi, dg, dh, yacc);
+              }
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(empty_bar(s));
+            if (++s == a.ring) {
+              s = 0;
+              phase ^= 1;
+            }
+          }
+          band_end(band, bi);
+        }
+      };
+      switch (residue_class(fkb * kBlk)) {
+        case 16: tmap_loop(std::integral_constant<int, 16>()); break;
+        case 8: tmap_loop(std::integral_constant<int, 8>()); break;
+        case 4: tmap_loop(std::integral_constant<int, 4>()); break;
+        case 2: tmap_loop(std::integral_constant<int, 2>()); break;
+        default: tmap_loop(std::integral_constant<int, 6>()); break;
+      }
+      return;
+    }
+  }
   if constexpr (QT == 6 && I8) {
     if (a.fixed_blocks) {
       const uint32_t fkb = warp;
@@ -2186,7 +2247,7 @@ int warpmma_plan(kq_ctx* ctx, const kq_matvec_desc& d, uint64_t ldx, uint64_t ld
     seg = tp;
     slot = static_cast<uint32_t>(((uint64_t(kTileRows) * tp + 127) / 128) * 128);
     // Q4_K / Q5_K at batch 1: warp w fixed to block w of every K-tile, as for whole-row tiles
-    if (tmap_fixed && q45 && (mode == 4 || mode == 6) && !(d.flags & kFlagWarpPerBlock)) nw = nwc;
+    if (tmap_fixed && (mode == 4 || mode == 5 || mode == 6) && !(d.flags & kFlagWarpPerBlock)) nw = nwc;
   } else if (compact && seg != 0) {
     const uint32_t cslot = static_cast<uint32_t>(((rpc * seg + 127) / 128) * 128);
     if (rpc < kTileRows && kTileRows * seg - cslot <= table_bytes + mtable_bytes) slot = cslot;
@@ -2231,7 +2292,7 @@ int warpmma_plan(kq_ctx* ctx, const kq_matvec_desc& d, uint64_t ldx, uint64_t ld
   args.tile_pitch = tmap ? tp : 0u;
   if (tmap) args.tmap = tm_map;
   else std::memset(&args.tmap, 0, sizeof(args.tmap));
-  args.fixed_blocks = ((fixed_ok || (tmap && tmap_fixed && q45)) && nw == nwc) ? 1u : 0u;
+  args.fixed_blocks = ((fixed_ok || (tmap && tmap_fixed)) && nw == nwc) ? 1u : 0u;
   args.bars_off = args.red_off + red_bytes;
   args.ncol = ncol;
   args.fb = fb;
