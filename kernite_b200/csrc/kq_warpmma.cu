@@ -1440,10 +1440,11 @@ __device__ __forceinline__ void consume_job(const WarpMmaArgs& a, const JobArgs&
   // Q6_K integer path, tiles of whole rows on 16-byte boundaries, one warp per block: warp w
   // takes block w of every tile, so its block's offset within 16 bytes (2w mod 16) is fixed, and
   // the loop is compiled once per residue class, with every address but the slot's hoisted.
-  if constexpr (QT == 6 && I8 && TXS == 0) {
+  if constexpr (QT == 6 && I8 && TXS <= 1) {
     if (a.fixed_blocks && a.tmap_mode) {
       // Tensor-map tiles of K-tiled rows: warp w takes block w of every K-tile (whose 16-byte
       // residue, 2w mod 16, is the same in every tile); the x constants change with the K-tile.
+      // (Compiled for lone launches and for push kernels whose tagged x has one slot.)
       const uint32_t fkb = warp;
       const uint32_t off_g = pg_rb + fkb * kBlk, off_h = ph_rb + fkb * kBlk;
       uint32_t kt_lo, kt_hi;
@@ -1502,7 +1503,7 @@ __device__ __forceinline__ void consume_job(const WarpMmaArgs& a, const JobArgs&
     }
   }
   if constexpr (QT == 6 && I8) {
-    if (a.fixed_blocks) {
+    if (a.fixed_blocks && !a.tmap_mode) {  // (tensor-map tiles without their loop take turns)
       const uint32_t fkb = warp;
       auto fixed_loop = [&](auto cls) {
         constexpr int F = decltype(cls)::value;
@@ -1600,7 +1601,7 @@ __device__ __forceinline__ void consume_job(const WarpMmaArgs& a, const JobArgs&
     }
   }
   if constexpr (QT == 4 || QT == 5) {
-    if (a.fixed_blocks) {
+    if (a.fixed_blocks && !a.tmap_mode) {
       const uint32_t kb = warp;
       float u0, u1 = 0.f;
       uint32_t b0 = 0, b1 = 0, tab_t[NT], bm_at[NT];
@@ -2419,9 +2420,11 @@ int warpmma_push(kq_ctx* ctx, const kq_matvec_desc& d, const kq_push_desc& push,
   const char* call = "kq_matvec_push";
   WarpMmaPlan plan;
   // (the plan sizes its slots for the rows a CTA gets, which split K multiplies)
-  // (no fixed-block loop on tensor-map tiles: the push kernels are compiled without it)
-  int rc = warpmma_plan(ctx, d, ldx, ldy, call, plan, std::min<uint32_t>(std::max<uint32_t>(push.ksplit, 1), 8),
-                        true, false);
+  // (the fixed-block loop on tensor-map tiles: Q6_K only, and not with split-K slots; the Q4_K
+  // and Q5_K push kernels are compiled without it, which cost them registers)
+  const uint32_t ks = std::min<uint32_t>(std::max<uint32_t>(push.ksplit, 1), 8);
+  int rc = warpmma_plan(ctx, d, ldx, ldy, call, plan, ks, true,
+                        d.type == KQ_TYPE_Q6_K && push.x_slots <= 1);
   if (rc) return rc;
   if (plan.mode != (d.type == KQ_TYPE_Q4_K ? 4 : d.type == KQ_TYPE_Q5_K ? 6 : 5))
     return fail(KQ_E_UNSUPPORTED, call, "k " + std::to_string(d.k) + " does not fit the integer kernel");
