@@ -15,12 +15,14 @@
 //
 // Shape (one persistent CTA per SM, contiguous rows per CTA):
 //  * A producer warp streams tiles of 16 rows x up to 16 super-blocks into a ring of shared
-//    memory slots with cp.async.bulk (TMA, 1-D): one copy for a tile of whole rows, else one per
-//    row segment. An mbarrier per slot counts the bytes in; Q6_K blocks at any even offset need
-//    nothing special (readers use the byte offset from the aligned copy).
+//    memory slots: one 1-D bulk copy for a tile of whole rows; for K-tiled rows one 3-D TMA copy
+//    of a tensor map over W per band of 16 whole rows (the tensor-map tiles), else one bulk copy
+//    per row segment. An mbarrier per slot counts the bytes in; Q6_K blocks at any even offset
+//    need nothing special (readers use the byte offset from the aligned copy).
 //  * A consumer warp takes one super-block of a tile: 16 MMAs (K = 16 each) over the tile's
-//    16 rows (warp w takes block w, in a loop with the block's constants hoisted when the tiles
-//    are whole rows on 16-byte boundaries; else 19 warps take turns over a tile's blocks).
+//    16 rows (warp w takes block w, in a loop with the block's constants hoisted, when the tiles
+//    are whole rows on 16-byte boundaries or tensor-map tiles; else 19 warps take turns over a
+//    tile's blocks).
 //    The 16 rows are the MMA's M, x (with the batch) is its N. Thread (g, c) of the
 //    warp builds the A registers of rows g and g+8 from the bytes of its quarter of the block
 //    (Q4_K: qs chunk c = sub-blocks 2c, 2c+1; Q6_K: sub-blocks c and c+4 of each half).
