@@ -122,6 +122,10 @@ struct WarpMmaArgs {
   // tile_pitch bytes apart; a CTA's last band of fewer than 16 rows still goes row by row, at the
   // same pitch
   uint32_t tmap_mode, tile_pitch;
+  // 0, or the first K-tile of x's second part: the x table holds the K-tiles [0, xpart) first,
+  // then [xpart, nkt), rebuilt in between (Q6_K tensor-map tiles whose whole table would leave
+  // room for only two ring slots); every band's partial rows are kept across the two parts
+  uint32_t xpart;
   CUtensorMap tmap;  // W as [rows][super-blocks][block bytes] (Q6_K: [rows][8-block groups][1680 B])
 };
 
@@ -687,7 +691,7 @@ __device__ __forceinline__ void tma_load_3d(uint32_t dst, const CUtensorMap* tma
 // tile's byte count on its slot's mbarrier. s, phase: the ring position, carried from one matvec
 // of a launch to the next; issued: the tiles this warp issued before in the launch (the first
 // `ring` of them need no free slot). Returns false once a wait gave up.
-template <int QT>
+template <int QT, bool XP = false>
 __device__ __forceinline__ bool produce_job(const WarpMmaArgs& a, const JobArgs& v, uint8_t* base,
                                             WarpMmaShared& sh, uint32_t& s, uint32_t& phase,
                                             uint32_t& issued) {
@@ -725,7 +729,17 @@ __device__ __forceinline__ bool produce_job(const WarpMmaArgs& a, const JobArgs&
       }
       if (!__shfl_sync(0xffffffffu, ok, 0)) return false;
     }
-    const uint32_t band = t / nktc, kt = kt_lo + t % nktc;
+    // band by band, K-tile by K-tile; with x in two parts, every band's K-tiles of the first
+    // part, then every band's of the second (the consumers' order)
+    uint32_t band, kt;
+    if constexpr (!XP) {
+      band = t / nktc, kt = kt_lo + t % nktc;
+    } else if (t < nbands * a.xpart) {
+      band = t / a.xpart, kt = t % a.xpart;
+    } else {
+      const uint32_t u = t - nbands * a.xpart, w = a.nkt - a.xpart;
+      band = u / w, kt = a.xpart + u % w;
+    }
     const uint32_t r0 = r_begin + band * kTileRows;
     const uint32_t r1 = min(r0 + kTileRows, r_end);
     const uint32_t slot = ring_s + s * a.slot_bytes;
@@ -809,11 +823,183 @@ __device__ __forceinline__ bool produce_job(const WarpMmaArgs& a, const JobArgs&
   return true;
 }
 
+// The integer x table (batch 1) of the x-blocks [kb_lo, kb_hi), at entries kb - kb_lo, and the
+// blocks' scales of x (ublk) at kb. Lane l owns the 8 consecutive elements 8l .. 8l+7 of an
+// x-block, which are chunk l of the block's table entry (the 8 bytes of each limb), so its loads
+// are two 16-byte ones (four for a tagged x), its table writes three 8-byte ones, and the
+// per-sub-block sums need two shuffles. kXG x-blocks a round, all loads in flight (fewer where
+// the caller holds more registers). (A function, not a lambda of the caller: a closure that
+// captures the caller's locals changed the register allocation of every kernel that has it.)
+template <int QT, int TXS, int kXG>
+__device__ __forceinline__ void x_table_i8(const WarpMmaArgs& a, const JobArgs& mj, WarpMmaShared& sh,
+                                           float* ublk, uint32_t table_s, uint32_t mtable_s,
+                                           uint32_t warp, uint32_t lane, uint32_t nw, uint32_t kb_lo,
+                                           uint32_t kb_hi) {
+  constexpr bool TX = TXS > 0;
+  int& s_failed = sh.failed;
+  double (&s_sq)[kMaxWarps][8] = sh.sq;
+  const uint32_t want_tag = TX ? sh.tag_x : 0u;
+  const uint32_t x_slots = TXS == 2 ? sh.x_slots : 1u;
+  const uint64_t kx = uint64_t(a.nb) * kQK;  // elements between x's slots
+  for (uint32_t xb0 = kb_lo + warp; xb0 < kb_hi; xb0 += kXG * nw) {
+    float v[kXG][8];
+    bool tags_ok = true;
+#pragma unroll
+    for (int j = 0; j < kXG; ++j) {
+      const uint32_t kb = xb0 + j * nw;
+      if (kb < kb_hi) {
+        if constexpr (TX) {
+          const unsigned long long* src =
+              reinterpret_cast<const unsigned long long*>(mj.x) + kb * kQK + 8 * lane;
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            const ulonglong2 w = ld_tagged2(src + 2 * q);
+            v[j][2 * q] = __uint_as_float(static_cast<uint32_t>(w.x));
+            v[j][2 * q + 1] = __uint_as_float(static_cast<uint32_t>(w.y));
+            tags_ok &= static_cast<uint32_t>(w.x >> 32) == want_tag &&
+                       static_cast<uint32_t>(w.y >> 32) == want_tag;
+          }
+          // split-K slots 1.. of the writer: added in slot order (the same sum on every rank;
+          // x_slots is 1 unless TXS == 2)
+          for (uint32_t sl = 1; sl < x_slots; ++sl) {
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+              const ulonglong2 w = ld_tagged2(src + uint64_t(sl) * kx + 2 * q);
+              v[j][2 * q] += __uint_as_float(static_cast<uint32_t>(w.x));
+              v[j][2 * q + 1] += __uint_as_float(static_cast<uint32_t>(w.y));
+              tags_ok &= static_cast<uint32_t>(w.x >> 32) == want_tag &&
+                         static_cast<uint32_t>(w.y >> 32) == want_tag;
+            }
+          }
+        } else {
+          const float4* src = reinterpret_cast<const float4*>(mj.x + kb * kQK + 8 * lane);
+          const float4 p0 = __ldcg(src), p1 = __ldcg(src + 1);
+          v[j][0] = p0.x, v[j][1] = p0.y, v[j][2] = p0.z, v[j][3] = p0.w;
+          v[j][4] = p1.x, v[j][5] = p1.y, v[j][6] = p1.z, v[j][7] = p1.w;
+        }
+      }
+    }
+    if constexpr (TX) {
+      if (!tags_ok) {
+        // some element is not this step's yet: wait for each, bounded (at once when this CTA
+        // or an earlier launch already gave up); unrolled, so that v stays in registers
+        uint64_t t0 = 0;
+#pragma unroll
+        for (int j = 0; j < kXG; ++j) {
+          const uint32_t kb = xb0 + j * nw;
+          if (kb >= kb_hi) break;
+          const unsigned long long* src =
+              reinterpret_cast<const unsigned long long*>(mj.x) + kb * kQK + 8 * lane;
+#pragma unroll
+          for (int i = 0; i < 8; ++i) {
+            float sum = 0.f;
+            for (uint32_t sl = 0; sl < x_slots; ++sl) {
+              const unsigned long long* at = src + uint64_t(sl) * kx + i;
+              unsigned long long w = ld_tagged(at);
+              while (static_cast<uint32_t>(w >> 32) != want_tag) {
+                if (*reinterpret_cast<volatile int*>(&s_failed) ||
+                    (a.err && *reinterpret_cast<volatile unsigned*>(a.err)))
+                  break;
+                if (t0 == 0) t0 = globaltimer();
+                if (globaltimer() - t0 > kWaitBudgetNs) {
+                  report_error(a.err, kErrWaitPeer);
+                  s_failed = 1;
+                  break;
+                }
+                w = ld_tagged(at);
+              }
+              sum = sl ? sum + __uint_as_float(static_cast<uint32_t>(w))
+                       : __uint_as_float(static_cast<uint32_t>(w));
+            }
+            v[j][i] = sum;
+          }
+        }
+      }
+    }
+#pragma unroll
+    for (int j = 0; j < kXG; ++j) {
+      const uint32_t kb = xb0 + j * nw;
+      if (kb >= kb_hi) break;
+      float mx = 0.f;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) mx = fmaxf(mx, fabsf(v[j][i]));
+#pragma unroll
+      for (int o = 16; o; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+      double sq = 0.0;  // only the RMS norm needs it
+      if (mj.prologue == KQ_PROLOGUE_RMSNORM) {
+#pragma unroll
+        for (int i = 0; i < 8; ++i)
+          sq = fma(static_cast<double>(v[j][i]), static_cast<double>(v[j][i]), sq);
+#pragma unroll
+        for (int o = 16; o; o >>= 1) sq += __shfl_xor_sync(0xffffffffu, sq, o);
+      }
+      // 24-bit fixed point for the block: the power of two that brings max |x| into
+      // [2^21, 2^22), so that x = (L2 2^16 + L1 2^8 + L0) 2^-sh with signed byte limbs
+      // |L2| <= 64, |L1|, |L0| <= 128 (an integer-valued x stays exact).
+      int e = 1;
+      if (mx > 0.f && isfinite(mx)) e = exponent_of(mx);  // mx = f * 2^e, f in [0.5, 1)
+      const int shv = mx > 0.f ? max(-126, min(126, 22 - e)) : 0;
+      const float sc = pow2f(shv);
+      if (lane == 0) {
+        s_sq[warp][0] += sq;
+        ublk[kb] = pow2f(-shv);
+      }
+      uint32_t pk[3][2] = {{0u, 0u}, {0u, 0u}, {0u, 0u}};  // limb bytes, 4 to a word
+      int tl[3] = {0, 0, 0};                              // per-limb sums (Q6_K)
+      int tx = 0;                                         // sum of X (Q4_K, Q5_K)
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const int X = __float2int_rn(v[j][i] * sc);
+        const int l0 = ((X + 128) & 255) - 128;
+        const int x1 = (X - l0) >> 8;
+        const int l1 = ((x1 + 128) & 255) - 128;
+        const int l2 = (x1 - l1) >> 8;
+        const uint32_t sft = 8 * (i & 3);
+        pk[0][i >> 2] |= (static_cast<uint32_t>(l0) & 0xffu) << sft;
+        pk[1][i >> 2] |= (static_cast<uint32_t>(l1) & 0xffu) << sft;
+        pk[2][i >> 2] |= (static_cast<uint32_t>(l2) & 0xffu) << sft;
+        tl[0] += l0, tl[1] += l1, tl[2] += l2;
+        tx += X;
+      }
+      // chunk `lane` of the block: 24 bytes, 8 of each limb
+      const uint32_t at = table_s + ((kb - kb_lo) * 32 + lane) * 24;
+#pragma unroll
+      for (int l = 0; l < 3; ++l)
+        asm volatile("st.shared.v2.u32 [%0], {%1, %2};" ::"r"(at + 8 * l), "r"(pk[l][0]), "r"(pk[l][1])
+                     : "memory");
+      if constexpr (QT == 6) {
+        // C init of the MMAs: -32 * (sum of each limb over each 16-element sub-block), so that
+        // A = q (unsigned) gives sum (q - 32) x exactly; sub-block sb is lanes 2 sb, 2 sb + 1.
+        // Entry ((kb' * 2 + half) * 3 + l) * 8 + (sub-block within the half), kb' = kb - kb_lo.
+        const uint32_t sb = lane >> 1;
+#pragma unroll
+        for (int l = 0; l < 3; ++l) {
+          const int t = tl[l] + __shfl_xor_sync(0xffffffffu, tl[l], 1);
+          if ((lane & 1) == 0)
+            asm volatile("st.shared.s32 [%0], %1;" ::"r"(
+                             mtable_s + (((kb - kb_lo) * 2 + (sb >> 3)) * 24 + l * 8 + (sb & 7)) * 4),
+                         "r"(-32 * t)
+                         : "memory");
+        }
+      } else {
+        // the sum of x (in limb units) over each 32-element sub-block, lanes 4 r .. 4 r + 3,
+        // for the min term
+        int t = tx + __shfl_xor_sync(0xffffffffu, tx, 1);
+        t += __shfl_xor_sync(0xffffffffu, t, 2);
+        if ((lane & 3) == 0)
+          asm volatile("st.shared.f32 [%0], %1;" ::"r"(mtable_s + ((kb - kb_lo) * 8 + (lane >> 2)) * 4),
+                       "f"(static_cast<float>(t))
+                       : "memory");
+      }
+    }
+  }
+}
+
 // The consumer warps' part of one matvec: x into the B-fragment table (with the RMS-norm sums),
 // then every tile of this CTA's rows from the ring, MMAs, and the outputs. s, phase: the ring
 // position, carried from one matvec of a launch to the next. sync: null for a lone matvec; for a
 // job of a chain, where its outputs are also pushed.
-template <int QT, int NT, bool HILO, bool I8, int TXS = 0>
+template <int QT, int NT, bool HILO, bool I8, int TXS = 0, bool XP = false>
 __device__ __forceinline__ void consume_job(const WarpMmaArgs& a, const JobArgs& mj,
                                             const ChainSync* sync, uint8_t* base,
                                             WarpMmaShared& sh, uint32_t& s, uint32_t& phase,
@@ -867,166 +1053,9 @@ __device__ __forceinline__ void consume_job(const WarpMmaArgs& a, const JobArgs&
     if (lane == 0)
       for (int b = 0; b < 8; ++b) s_sq[warp][b] = 0.0;
     if constexpr (I8) {
-      // Batch 1, integer table. Lane l owns the 8 consecutive elements 8l .. 8l+7 of an x-block,
-      // which are chunk l of the block's table entry (the 8 bytes of each limb), so its loads
-      // are two 16-byte ones (four for a tagged x), its table writes three 8-byte ones, and the
-      // per-sub-block sums need two shuffles. kXG x-blocks per round, all loads in flight.
-      constexpr int kXG = TX ? 4 : 6;  // (more would spill: a tagged x doubles the live loads)
-      const uint32_t want_tag = TX ? sh.tag_x : 0u;
-      const uint32_t x_slots = TXS == 2 ? sh.x_slots : 1u;
-      const uint64_t kx = uint64_t(a.nb) * kQK;  // elements between x's slots
-      for (uint32_t xb0 = warp; xb0 < a.nb; xb0 += kXG * nw) {
-        float v[kXG][8];
-        bool tags_ok = true;
-#pragma unroll
-        for (int j = 0; j < kXG; ++j) {
-          const uint32_t kb = xb0 + j * nw;
-          if (kb < a.nb) {
-            if constexpr (TX) {
-              const unsigned long long* src =
-                  reinterpret_cast<const unsigned long long*>(mj.x) + kb * kQK + 8 * lane;
-#pragma unroll
-              for (int q = 0; q < 4; ++q) {
-                const ulonglong2 w = ld_tagged2(src + 2 * q);
-                v[j][2 * q] = __uint_as_float(static_cast<uint32_t>(w.x));
-                v[j][2 * q + 1] = __uint_as_float(static_cast<uint32_t>(w.y));
-                tags_ok &= static_cast<uint32_t>(w.x >> 32) == want_tag &&
-                           static_cast<uint32_t>(w.y >> 32) == want_tag;
-              }
-              // split-K slots 1.. of the writer: added in slot order (the same sum on every rank)
-              if constexpr (TXS == 2)
-              for (uint32_t sl = 1; sl < x_slots; ++sl) {
-#pragma unroll
-                for (int q = 0; q < 4; ++q) {
-                  const ulonglong2 w = ld_tagged2(src + uint64_t(sl) * kx + 2 * q);
-                  v[j][2 * q] += __uint_as_float(static_cast<uint32_t>(w.x));
-                  v[j][2 * q + 1] += __uint_as_float(static_cast<uint32_t>(w.y));
-                  tags_ok &= static_cast<uint32_t>(w.x >> 32) == want_tag &&
-                             static_cast<uint32_t>(w.y >> 32) == want_tag;
-                }
-              }
-            } else {
-              const float4* src = reinterpret_cast<const float4*>(mj.x + kb * kQK + 8 * lane);
-              const float4 p0 = __ldcg(src), p1 = __ldcg(src + 1);
-              v[j][0] = p0.x, v[j][1] = p0.y, v[j][2] = p0.z, v[j][3] = p0.w;
-              v[j][4] = p1.x, v[j][5] = p1.y, v[j][6] = p1.z, v[j][7] = p1.w;
-            }
-          }
-        }
-        if constexpr (TX) {
-          if (!tags_ok) {
-            // some element is not this step's yet: wait for each, bounded (at once when this CTA
-            // or an earlier launch already gave up); unrolled, so that v stays in registers
-            uint64_t t0 = 0;
-#pragma unroll
-            for (int j = 0; j < kXG; ++j) {
-              const uint32_t kb = xb0 + j * nw;
-              if (kb >= a.nb) break;
-              const unsigned long long* src =
-                  reinterpret_cast<const unsigned long long*>(mj.x) + kb * kQK + 8 * lane;
-#pragma unroll
-              for (int i = 0; i < 8; ++i) {
-                float sum = 0.f;
-                for (uint32_t sl = 0; sl < x_slots; ++sl) {
-                  const unsigned long long* at = src + uint64_t(sl) * kx + i;
-                  unsigned long long w = ld_tagged(at);
-                  while (static_cast<uint32_t>(w >> 32) != want_tag) {
-                    if (*reinterpret_cast<volatile int*>(&s_failed) ||
-                        (a.err && *reinterpret_cast<volatile unsigned*>(a.err)))
-                      break;
-                    if (t0 == 0) t0 = globaltimer();
-                    if (globaltimer() - t0 > kWaitBudgetNs) {
-                      report_error(a.err, kErrWaitPeer);
-                      s_failed = 1;
-                      break;
-                    }
-                    w = ld_tagged(at);
-                  }
-                  sum = sl ? sum + __uint_as_float(static_cast<uint32_t>(w))
-                           : __uint_as_float(static_cast<uint32_t>(w));
-                }
-                v[j][i] = sum;
-              }
-            }
-          }
-        }
-#pragma unroll
-        for (int j = 0; j < kXG; ++j) {
-          const uint32_t kb = xb0 + j * nw;
-          if (kb >= a.nb) break;
-          float mx = 0.f;
-#pragma unroll
-          for (int i = 0; i < 8; ++i) mx = fmaxf(mx, fabsf(v[j][i]));
-#pragma unroll
-          for (int o = 16; o; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-          double sq = 0.0;  // only the RMS norm needs it
-          if (mj.prologue == KQ_PROLOGUE_RMSNORM) {
-#pragma unroll
-            for (int i = 0; i < 8; ++i)
-              sq = fma(static_cast<double>(v[j][i]), static_cast<double>(v[j][i]), sq);
-#pragma unroll
-            for (int o = 16; o; o >>= 1) sq += __shfl_xor_sync(0xffffffffu, sq, o);
-          }
-          // 24-bit fixed point for the block: the power of two that brings max |x| into
-          // [2^21, 2^22), so that x = (L2 2^16 + L1 2^8 + L0) 2^-sh with signed byte limbs
-          // |L2| <= 64, |L1|, |L0| <= 128 (an integer-valued x stays exact).
-          int e = 1;
-          if (mx > 0.f && isfinite(mx)) e = exponent_of(mx);  // mx = f * 2^e, f in [0.5, 1)
-          const int shv = mx > 0.f ? max(-126, min(126, 22 - e)) : 0;
-          const float sc = pow2f(shv);
-          if (lane == 0) {
-            s_sq[warp][0] += sq;
-            ublk[kb] = pow2f(-shv);
-          }
-          uint32_t pk[3][2] = {{0u, 0u}, {0u, 0u}, {0u, 0u}};  // limb bytes, 4 to a word
-          int tl[3] = {0, 0, 0};                              // per-limb sums (Q6_K)
-          int tx = 0;                                         // sum of X (Q4_K, Q5_K)
-#pragma unroll
-          for (int i = 0; i < 8; ++i) {
-            const int X = __float2int_rn(v[j][i] * sc);
-            const int l0 = ((X + 128) & 255) - 128;
-            const int x1 = (X - l0) >> 8;
-            const int l1 = ((x1 + 128) & 255) - 128;
-            const int l2 = (x1 - l1) >> 8;
-            const uint32_t sft = 8 * (i & 3);
-            pk[0][i >> 2] |= (static_cast<uint32_t>(l0) & 0xffu) << sft;
-            pk[1][i >> 2] |= (static_cast<uint32_t>(l1) & 0xffu) << sft;
-            pk[2][i >> 2] |= (static_cast<uint32_t>(l2) & 0xffu) << sft;
-            tl[0] += l0, tl[1] += l1, tl[2] += l2;
-            tx += X;
-          }
-          // chunk `lane` of the block: 24 bytes, 8 of each limb
-          const uint32_t at = table_s + (kb * 32 + lane) * 24;
-#pragma unroll
-          for (int l = 0; l < 3; ++l)
-            asm volatile("st.shared.v2.u32 [%0], {%1, %2};" ::"r"(at + 8 * l), "r"(pk[l][0]), "r"(pk[l][1])
-                         : "memory");
-          if constexpr (QT == 6) {
-            // C init of the MMAs: -32 * (sum of each limb over each 16-element sub-block), so that
-            // A = q (unsigned) gives sum (q - 32) x exactly; sub-block sb is lanes 2 sb, 2 sb + 1.
-            // Entry ((kb * 2 + half) * 3 + l) * 8 + (sub-block within the half).
-            const uint32_t sb = lane >> 1;
-#pragma unroll
-            for (int l = 0; l < 3; ++l) {
-              const int t = tl[l] + __shfl_xor_sync(0xffffffffu, tl[l], 1);
-              if ((lane & 1) == 0)
-                asm volatile("st.shared.s32 [%0], %1;" ::"r"(
-                                 mtable_s + ((kb * 2 + (sb >> 3)) * 24 + l * 8 + (sb & 7)) * 4),
-                             "r"(-32 * t)
-                             : "memory");
-            }
-          } else {
-            // the sum of x (in limb units) over each 32-element sub-block, lanes 4 r .. 4 r + 3,
-            // for the min term
-            int t = tx + __shfl_xor_sync(0xffffffffu, tx, 1);
-            t += __shfl_xor_sync(0xffffffffu, t, 2);
-            if ((lane & 3) == 0)
-              asm volatile("st.shared.f32 [%0], %1;" ::"r"(mtable_s + (kb * 8 + (lane >> 2)) * 4),
-                           "f"(static_cast<float>(t))
-                           : "memory");
-          }
-        }
-      }
+      // (more x-blocks a round would spill: a tagged x doubles the live loads)
+      x_table_i8<QT, TXS, TX ? 4 : 6>(a, mj, sh, ublk, table_s, mtable_s, warp, lane, nw, 0,
+                                       XP ? a.xpart * (a.nb / a.nkt) : a.nb);
     } else {
     const uint32_t nxb = a.nb * B;
     for (uint32_t xb0 = warp; xb0 < nxb; xb0 += 4 * nw) {
@@ -1366,8 +1395,9 @@ __device__ __forceinline__ void consume_job(const WarpMmaArgs& a, const JobArgs&
   };
 
   // The band is done: this warp's partial rows go to the reduction buffer; every fb bands (and
-  // after the last) the warps meet and sum them in a fixed order into y.
-  auto band_end = [&](uint32_t band, uint32_t& bi) {
+  // after the last) the warps meet and sum them in a fixed order into y. part: 0, or with x in
+  // two parts 1 (store the partial rows, no flush: fb covers every band) and 2 (add to them).
+  auto band_end = [&](uint32_t band, uint32_t& bi, uint32_t part = 0) {
     if constexpr (QT == 6 || I8) {
       // the four threads of a row hold different sub-blocks of vector 0
 #pragma unroll
@@ -1376,8 +1406,16 @@ __device__ __forceinline__ void consume_job(const WarpMmaArgs& a, const JobArgs&
         yacc[r][0] += __shfl_xor_sync(0xffffffffu, yacc[r][0], 2);
       }
       if (c == 0) {
-        red[((bi * nw + warp) * kTileRows + pg) * B] = yacc[0][0];
-        red[((bi * nw + warp) * kTileRows + ph) * B] = yacc[1][0];
+        float* rg = &red[((bi * nw + warp) * kTileRows + pg) * B];
+        float* rh = &red[((bi * nw + warp) * kTileRows + ph) * B];
+        if (XP && part == 2) {
+          // (the first part's partial of the same row, written by this thread)
+          *rg += yacc[0][0];
+          *rh += yacc[1][0];
+        } else {
+          *rg = yacc[0][0];
+          *rh = yacc[1][0];
+        }
       }
     } else {
 #pragma unroll
@@ -1391,7 +1429,7 @@ __device__ __forceinline__ void consume_job(const WarpMmaArgs& a, const JobArgs&
     }
     yacc[0][0] = yacc[0][1] = yacc[1][0] = yacc[1][1] = 0.f;
 
-    if (bi + 1 == a.fb || band + 1 == nbands) {
+    if ((!XP || part != 1) && (bi + 1 == a.fb || band + 1 == nbands)) {
       // Flush: sum every warp's partial of each row in a fixed order and write y.
       named_barrier(1, nthr);
       const uint32_t band0 = band - bi;
@@ -1451,17 +1489,19 @@ __device__ __forceinline__ void consume_job(const WarpMmaArgs& a, const JobArgs&
       const uint32_t off_g = pg_rb + fkb * kBlk, off_h = ph_rb + fkb * kBlk;
       uint32_t kt_lo, kt_hi;
       cta_ktiles(nkt, a.ksplit, kt_lo, kt_hi);
-      auto tmap_loop = [&](auto cls) {
+      // part: 0 (x whole), or 1 and 2 (x in two parts: the K-tiles [kt_a, kt_z) of every band,
+      // whose x-blocks are the table's from kb_base on)
+      auto tmap_loop = [&](auto cls, uint32_t kt_a, uint32_t kt_z, uint32_t kb_base, uint32_t part) {
         constexpr int F = decltype(cls)::value;
         uint32_t bi = 0;
         for (uint32_t band = 0; band < nbands; ++band) {
-          for (uint32_t kt = kt_lo; kt < kt_hi; ++kt) {
+          for (uint32_t kt = kt_a; kt < kt_z; ++kt) {
             const uint32_t kb = kt * kq + fkb;
             const float u0 = ublk_at(kb);
-            const uint32_t tkb = table_s + (kb * 32 + 2 * c) * 24;
+            const uint32_t tkb = table_s + ((kb - kb_base) * 32 + 2 * c) * 24;
             const uint32_t bA = g == c ? tkb : zero_s;
             const uint32_t bB = g == c + 4 ? tkb + 8 * 24 : zero_s;
-            const uint32_t mkb = mtable_s + (kb * 48 + 2 * c) * 4;
+            const uint32_t mkb = mtable_s + ((kb - kb_base) * 48 + 2 * c) * 4;
             bool ok = !*reinterpret_cast<volatile int*>(&s_failed);
             if (ok && !mbar_wait(full_bar(s), phase)) {
               ok = false;
@@ -1491,15 +1531,32 @@ __device__ __forceinline__ void consume_job(const WarpMmaArgs& a, const JobArgs&
               phase ^= 1;
             }
           }
-          band_end(band, bi);
+          band_end(band, bi, part);
         }
       };
-      switch (residue_class(fkb * kBlk)) {
-        case 16: tmap_loop(std::integral_constant<int, 16>()); break;
-        case 8: tmap_loop(std::integral_constant<int, 8>()); break;
-        case 4: tmap_loop(std::integral_constant<int, 4>()); break;
-        case 2: tmap_loop(std::integral_constant<int, 2>()); break;
-        default: tmap_loop(std::integral_constant<int, 6>()); break;
+      auto run = [&](uint32_t kt_a, uint32_t kt_z, uint32_t kb_base, uint32_t pm) {
+        switch (residue_class(fkb * kBlk)) {
+          case 16: tmap_loop(std::integral_constant<int, 16>(), kt_a, kt_z, kb_base, pm); break;
+          case 8: tmap_loop(std::integral_constant<int, 8>(), kt_a, kt_z, kb_base, pm); break;
+          case 4: tmap_loop(std::integral_constant<int, 4>(), kt_a, kt_z, kb_base, pm); break;
+          case 2: tmap_loop(std::integral_constant<int, 2>(), kt_a, kt_z, kb_base, pm); break;
+          default: tmap_loop(std::integral_constant<int, 6>(), kt_a, kt_z, kb_base, pm); break;
+        }
+      };
+      if constexpr (XP) {
+        // x in two parts (the kernel compiled for them): every band's first K-tiles, then, once
+        // every warp is done with the first part's table, the second's built over it
+        for (uint32_t part = 0; part < 2; ++part) {
+          if (part) {
+            named_barrier(1, nthr);
+            x_table_i8<QT, TXS, TX ? 1 : 2>(a, mj, sh, ublk, table_s, mtable_s, warp, lane, nw,
+                                            a.xpart * kq, a.nb);
+            named_barrier(1, nthr);
+          }
+          run(part ? a.xpart : 0u, part ? kt_hi : a.xpart, part ? a.xpart * kq : 0u, part + 1);
+        }
+      } else {
+        run(kt_lo, kt_hi, 0u, 0u);
       }
       return;
     }
@@ -1790,7 +1847,7 @@ __device__ __forceinline__ void consume_job(const WarpMmaArgs& a, const JobArgs&
 // HILO: x enters as hi + lo (else hi only). I8 (batch 1): integer MMAs, A = the raw quants as
 // bytes, x as three signed byte limbs (24-bit fixed point per 256-element block), the eight MMA
 // columns separating sub-blocks.
-template <int QT, int NT, bool HILO, bool I8>
+template <int QT, int NT, bool HILO, bool I8, bool XP = false>
 __global__ void __launch_bounds__((kMaxWarps + 1) * 32, 1) warpmma_kernel(const __grid_constant__ WarpMmaArgs a) {
   extern __shared__ __align__(128) uint8_t smem[];
   __shared__ WarpMmaShared sh;
@@ -1802,11 +1859,11 @@ __global__ void __launch_bounds__((kMaxWarps + 1) * 32, 1) warpmma_kernel(const 
   if ((threadIdx.x >> 5) == a.nw) {
     if (!(a.flags & KQ_FLAG_WEIGHTS_STATIC)) pdl_wait();
     uint32_t issued = 0;
-    produce_job<QT>(a, v, base, sh, s, phase, issued);
+    produce_job<QT, XP>(a, v, base, sh, s, phase, issued);
     return;
   }
   pdl_wait();  // x may be the previous kernel's output
-  consume_job<QT, NT, HILO, I8>(a, v, nullptr, base, sh, s, phase);
+  consume_job<QT, NT, HILO, I8, 0, XP>(a, v, nullptr, base, sh, s, phase);
 }
 
 __device__ __forceinline__ unsigned long long ld_acquire_gpu(const unsigned long long* p) {
@@ -1854,7 +1911,7 @@ __device__ __forceinline__ bool wait_at_least(unsigned* err, const unsigned long
 // stores and x's elements are each waited for until they carry this step's tag, so there is no
 // fence, no counter and no round trip on the critical path. The producer streams the weights from
 // the start, the wait overlapping the first tiles' copies.
-template <int QT, int TXS>
+template <int QT, int TXS, bool XP = false>
 __global__ void __launch_bounds__((kMaxWarps + 1) * 32, 1)
     warpmma_push_kernel(const __grid_constant__ WarpMmaArgs a, const __grid_constant__ PushArgs q) {
   constexpr bool TX = TXS > 0;
@@ -1868,7 +1925,7 @@ __global__ void __launch_bounds__((kMaxWarps + 1) * 32, 1)
   if ((threadIdx.x >> 5) == a.nw) {
     if (!(a.flags & KQ_FLAG_WEIGHTS_STATIC)) pdl_wait();
     uint32_t issued = 0;
-    produce_job<QT>(a, v, base, sh, s, phase, issued);
+    produce_job<QT, XP>(a, v, base, sh, s, phase, issued);
     return;
   }
   pdl_wait();
@@ -1886,7 +1943,7 @@ __global__ void __launch_bounds__((kMaxWarps + 1) * 32, 1)
     }
   }
   named_barrier(1, nthr);
-  consume_job<QT, 1, false, true, TXS>(a, v, &q.y, base, sh, s, phase);
+  consume_job<QT, 1, false, true, TXS, XP>(a, v, &q.y, base, sh, s, phase);
   if (q.y.tagged) return;  // no counts
   named_barrier(1, nthr);  // every consumer's outputs are stored
   if (threadIdx.x == 0 && q.y.npush) {
@@ -2023,14 +2080,18 @@ struct Variant {
   bool hilo;
 };
 
-template <int QT, int NT, bool HILO, bool I8 = false>
+template <int QT, int NT, bool HILO, bool I8 = false, bool XP = false>
 Variant variant() {
-  return Variant{reinterpret_cast<const void*>(&warpmma_kernel<QT, NT, HILO, I8>), QT, NT, HILO};
+  return Variant{reinterpret_cast<const void*>(&warpmma_kernel<QT, NT, HILO, I8, XP>), QT, NT, HILO};
 }
 
+// (the last: the Q6_K integer kernel compiled for x in two parts, which a plan with xpart takes
+// instead of mode 5's)
 const Variant kVariants[] = {variant<4, 1, true>(), variant<4, 2, true>(), variant<4, 1, false>(),
                              variant<6, 1, false>(), variant<4, 1, false, true>(),
-                             variant<6, 1, false, true>(), variant<5, 1, false, true>()};
+                             variant<6, 1, false, true>(), variant<5, 1, false, true>(),
+                             variant<6, 1, false, true, true>()};
+constexpr int kXPartVariant = 7;
 
 // The push kernel of a type (Q4_K, Q5_K or Q6_K) for x plain (txs 0), tagged (1), or tagged
 // with several split-K slots (2).
@@ -2040,7 +2101,11 @@ const void* push_fn_t(uint32_t type) {
          : type == KQ_TYPE_Q5_K ? reinterpret_cast<const void*>(&warpmma_push_kernel<5, TXS>)
                                 : reinterpret_cast<const void*>(&warpmma_push_kernel<6, TXS>);
 }
-const void* push_fn(uint32_t type, int txs) {
+// (xp: the Q6_K kernel compiled for x in two parts, plain or tagged x with one slot)
+const void* push_fn(uint32_t type, int txs, bool xp = false) {
+  if (xp && type == KQ_TYPE_Q6_K && txs < 2)
+    return txs == 0 ? reinterpret_cast<const void*>(&warpmma_push_kernel<6, 0, true>)
+                    : reinterpret_cast<const void*>(&warpmma_push_kernel<6, 1, true>);
   return txs == 0 ? push_fn_t<0>(type) : txs == 1 ? push_fn_t<1>(type) : push_fn_t<2>(type);
 }
 
@@ -2065,10 +2130,11 @@ int warpmma_prepare(kq_ctx* ctx) {
     cudaError_t e =
         cudaFuncSetAttribute(chain_fn(t), cudaFuncAttributeMaxDynamicSharedMemorySize, ctx->max_smem);
     if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute", "warp-MMA chain kernel");
-    for (int txs : {0, 1, 2}) {
-      e = cudaFuncSetAttribute(push_fn(t, txs), cudaFuncAttributeMaxDynamicSharedMemorySize, ctx->max_smem);
-      if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute", "warp-MMA push kernel");
-    }
+    for (int txs : {0, 1, 2})
+      for (bool xp : {false, true}) {
+        e = cudaFuncSetAttribute(push_fn(t, txs, xp), cudaFuncAttributeMaxDynamicSharedMemorySize, ctx->max_smem);
+        if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute", "warp-MMA push kernel");
+      }
   }
   return KQ_OK;
 }
@@ -2257,9 +2323,33 @@ int warpmma_plan(kq_ctx* ctx, const kq_matvec_desc& d, uint64_t ldx, uint64_t ld
   }
   // partial rows of up to 16 bands between flushes, in what two ring slots leave
   const uint32_t band_red = kTileRows * nw * d.batch * 4;
+  auto ring_for = [&](uint64_t table, uint32_t bands) {
+    const uint64_t tail_ = table + ublk_bytes + kZeroBytes + 16 + uint64_t(bands) * band_red + 2 * 8 * 8 + 128;
+    return tail_ < uint64_t(ctx->max_smem) ? (uint64_t(ctx->max_smem) - tail_) / slot : 0;
+  };
+  // x in two parts (Q6_K tensor-map tiles of a lone launch or a push with one x slot, warp w on
+  // block w, no prologue or epilogue): when the whole x table (3.75 bytes an element: K = 28672
+  // takes 105 KB) leaves room for only two ring slots, the table holds the first half of the
+  // K-tiles, then the second's, rebuilt once every band has had the first; every band's partial
+  // rows stay in shared memory in between. A third slot of 54 KB keeps more of the CTA's weights
+  // in flight.
+  uint32_t xpart = 0;
+  const uint32_t cta_bands = static_cast<uint32_t>((rpc + kTileRows - 1) / kTileRows);
+  if (tmap && mode == 5 && nw == nwc && tmap_fixed && !(d.flags & kFlagWarpPerBlock) && ksplit <= 1 &&
+      d.prologue == KQ_PROLOGUE_NONE && d.epilogue == KQ_EPILOGUE_NONE && nkt >= 2 &&
+      cta_bands <= 16 && ring_for(table_bytes + mtable_bytes, 16) < 3) {
+    const uint32_t kh = (nkt + 1) / 2, nbh = kh * (nb / nkt);
+    const uint64_t tb = uint64_t(nbh) * kQK * 3, mb = uint64_t(nbh) * 2 * 3 * 8 * 4;
+    if (ring_for(tb + mb, cta_bands) >= 3) {
+      xpart = kh;
+      table_bytes = tb;
+      mtable_bytes = mb;
+    }
+  }
   const uint64_t base_need = need_for(slot) - uint64_t(kTileRows) * kMaxWarps * d.batch * 4;
-  const uint32_t fb = static_cast<uint32_t>(std::min<uint64_t>(
-      16, std::min<uint64_t>(kRedBudget, uint64_t(ctx->max_smem) - base_need) / band_red));
+  const uint32_t fb = xpart ? cta_bands
+                            : static_cast<uint32_t>(std::min<uint64_t>(
+                                  16, std::min<uint64_t>(kRedBudget, uint64_t(ctx->max_smem) - base_need) / band_red));
   const uint32_t red_bytes = fb * band_red;
   const uint64_t tail =
       table_bytes + mtable_bytes + ublk_bytes + kZeroBytes + 16 + red_bytes + 2 * 8 * 8 + 128;
@@ -2293,6 +2383,7 @@ int warpmma_plan(kq_ctx* ctx, const kq_matvec_desc& d, uint64_t ldx, uint64_t ld
   args.split_tile = tmap ? 0u : (seg == 0 && split) ? 1u : 0u;
   args.tmap_mode = tmap ? 1u : 0u;
   args.tile_pitch = tmap ? tp : 0u;
+  args.xpart = xpart;
   if (tmap) args.tmap = tm_map;
   else std::memset(&args.tmap, 0, sizeof(args.tmap));
   args.fixed_blocks = ((fixed_ok || (tmap && tmap_fixed)) && nw == nwc) ? 1u : 0u;
@@ -2345,7 +2436,8 @@ bool same_layout(const WarpMmaArgs& a, const WarpMmaArgs& b) {
          a.zero_off == b.zero_off && a.red_off == b.red_off && a.bars_off == b.bars_off &&
          a.row_perm == b.row_perm && a.split_tile == b.split_tile &&
          a.fixed_blocks == b.fixed_blocks && a.ncol == b.ncol && a.fb == b.fb &&
-         a.ksplit == b.ksplit && a.tmap_mode == b.tmap_mode && a.tile_pitch == b.tile_pitch;
+         a.ksplit == b.ksplit && a.tmap_mode == b.tmap_mode && a.tile_pitch == b.tile_pitch &&
+         a.xpart == b.xpart;
 }
 
 }  // namespace
@@ -2355,7 +2447,7 @@ int warpmma_matvec(kq_ctx* ctx, const kq_matvec_desc& d, uint64_t ldx, uint64_t 
   WarpMmaPlan plan;
   int rc = warpmma_plan(ctx, d, ldx, ldy, "kq_matvec", plan);
   if (rc) return rc;
-  const cudaError_t e = launch(kVariants[plan.mode].fn, plan.grid, plan.block, plan.smem,
+  const cudaError_t e = launch(kVariants[plan.args.xpart ? kXPartVariant : plan.mode].fn, plan.grid, plan.block, plan.smem,
                                !(d.flags & KQ_FLAG_NO_PDL), stream, &plan.args);
   if (e != cudaSuccess)
     return cuda_fail(e, "cudaLaunchKernelExC", "warp-MMA matvec " + shape(plan.grid, plan.block, plan.smem));
@@ -2376,7 +2468,7 @@ int warpmma_plan_launch(kq_ctx* ctx, const kq_matvec_desc& d, kq_launch& out) {
   if (rc) return rc;
   // the function's name, as the driver has it (the image is the same source, compiled alike)
   cudaFunction_t f = nullptr;
-  cudaError_t e = cudaGetFuncBySymbol(&f, kVariants[plan.mode].fn);
+  cudaError_t e = cudaGetFuncBySymbol(&f, kVariants[plan.args.xpart ? kXPartVariant : plan.mode].fn);
   if (e != cudaSuccess) return cuda_fail(e, "cudaGetFuncBySymbol", call);
   using GetName = CUresult (*)(const char**, CUfunction);
   void* fp = nullptr;
@@ -2487,7 +2579,8 @@ int warpmma_push(kq_ctx* ctx, const kq_matvec_desc& d, const kq_push_desc& push,
   cfg.attrs = attr;
   cfg.numAttrs = (d.flags & KQ_FLAG_NO_PDL) ? 0 : 1;
   void* params[] = {&plan.args, &q};
-  const cudaError_t e = cudaLaunchKernelExC(&cfg, push_fn(d.type, !tx ? 0 : q.x_slots > 1 ? 2 : 1), params);
+  const cudaError_t e =
+      cudaLaunchKernelExC(&cfg, push_fn(d.type, !tx ? 0 : q.x_slots > 1 ? 2 : 1, plan.args.xpart != 0), params);
   if (e != cudaSuccess)
     return cuda_fail(e, "cudaLaunchKernelExC", "warp-MMA push " + shape(plan.grid, plan.block, plan.smem));
   return KQ_OK;

@@ -96,8 +96,9 @@ SHAPES = [
     (6, 500, 4096, 2), (6, 299, 4096, 3), (6, 301, 4096, 4), (6, 151, 4096, 7), (6, 200, 4096, 8),
     (4, 100, 11008, 2), (6, 100, 11008, 2),
     # K-tiled rows with whole 16-row bands (tensor-map tiles on the warp-MMA kernel) and a last
-    # band of a few rows
+    # band of a few rows; Q6_K at K = 16384 and 28672 takes x in two parts (two bands a CTA here)
     (4, 3000, 8192, 1), (6, 2400, 16384, 1), (4, 2400, 8192, 2), (4, 2600, 12288, 2),
+    (6, 4096, 28672, 1),
 ]
 
 

@@ -32,7 +32,7 @@ def _desc(npush, push_rows, full, counter, wait=0, epoch=0, mul=0, add=0):
 
 @pytest.mark.parametrize("qtype,rows,k,pair", [(4, 4096, 4096, False), (6, 32000, 4096, False),
                                                (4, 2048, 8192, True), (6, 300, 11008, False),
-                                               (5, 1024, 4096, False)])
+                                               (5, 1024, 4096, False), (6, 4096, 28672, False)])
 def test_push_kernel_equals_lone_kernel(kernels, qtype, rows, k, pair):
     W = _w(kernels, qtype, rows, k, rows)
     x = torch.from_numpy(np.random.default_rng(rows).standard_normal(k).astype(np.float32)).cuda()
@@ -125,6 +125,38 @@ def test_tagged_push_chain_of_two_over_steps(kernels):
         assert torch.equal(y1, r1) and torch.equal(y2, r2) and torch.equal(plain, r2), step
         tags = t2.view(torch.int32)[1::2]
         assert (tags == step).all()
+
+
+def test_tagged_push_into_a_long_k_matvec(kernels):
+    """A tagged vector of 28672 elements read by a Q6_K matvec of the 70B down projection's
+    2-way shard shape (4096 x 28672): its x table comes in two parts, the second built from the
+    tagged vector in the middle of the launch. Two steps, equal to the lone launches bit for bit."""
+    h, f = 4096, 28672
+    W1, W2 = _w(kernels, 4, f, h, 31), _w(kernels, 6, h, f, 32)
+    mem = torch.zeros(1, dtype=torch.int64, device="cuda")  # epoch
+    ep = mem.data_ptr()
+    x = torch.zeros(h, device="cuda")
+    y1, y2 = torch.zeros(f, device="cuda"), torch.zeros(h, device="cuda")
+    t1, t2 = torch.zeros(2 * f, device="cuda"), torch.zeros(2 * h, device="cuda")
+    plain = torch.full((h,), float("nan"), device="cuda")
+    r1, r2 = torch.zeros(f, device="cuda"), torch.zeros(h, device="cuda")
+    for step in range(1, 3):
+        x.copy_(torch.from_numpy(np.random.default_rng(40 + step).standard_normal(h).astype(np.float32)))
+        mem[0] += 1
+        d1 = _desc(1, f, t1.data_ptr(), 0, epoch=ep)
+        d1.flags, d1.push_mul, d1.push_add = kb.PUSH_TAGGED, 1, 1
+        kernels.matvec_push(4, y1, W1, x, f, h, d1)
+        d2 = _desc(1, h, t2.data_ptr(), 0, epoch=ep, mul=1, add=1)
+        d2.flags, d2.push_mul, d2.push_add = kb.PUSH_TAGGED | kb.PUSH_TAGGED_X, 1, 1
+        kernels.matvec_push(6, y2, W2, t1, h, f, d2)
+        kernels.tagged_unpack(plain, t2, h, ep, 1, 1)
+        kernels.matvec(4, r1, W1, x, f, h, 1)
+        kernels.matvec(6, r2, W2, r1, h, f, 1)
+        torch.cuda.synchronize()
+        kernels.device_error()
+        assert torch.equal(y1, r1) and torch.equal(y2, r2) and torch.equal(plain, r2), step
+    ref, bound = oracle.matvec_ref(6, W2.cpu().numpy(), r1.cpu().numpy()[None, :], f, 0, 64)
+    assert (np.abs(r2.cpu().numpy()[:64] - ref[0]) <= 1e-3 * bound[0]).all()
 
 
 def test_tagged_read_of_a_stale_vector_gives_up(kernels):
