@@ -123,8 +123,9 @@ struct WarpMmaArgs {
   // same pitch
   uint32_t tmap_mode, tile_pitch;
   // 0, or the first K-tile of x's second part: the x table holds the K-tiles [0, xpart) first,
-  // then [xpart, nkt), rebuilt in between (Q6_K tensor-map tiles whose whole table would leave
-  // room for only two ring slots); every band's partial rows are kept across the two parts
+  // then [xpart, nkt), rebuilt in between by each warp for its own block (Q6_K tensor-map tiles
+  // whose whole table would leave room for only two ring slots); every band's partial rows are
+  // kept across the two parts
   uint32_t xpart;
   CUtensorMap tmap;  // W as [rows][super-blocks][block bytes] (Q6_K: [rows][8-block groups][1680 B])
 };
@@ -1544,14 +1545,17 @@ __device__ __forceinline__ void consume_job(const WarpMmaArgs& a, const JobArgs&
         }
       };
       if constexpr (XP) {
-        // x in two parts (the kernel compiled for them): every band's first K-tiles, then, once
-        // every warp is done with the first part's table, the second's built over it
+        // x in two parts (the kernel compiled for them): every band's first K-tiles, then the
+        // second's. Warp w reads only the table entries of its own block of each K-tile, x-blocks
+        // w, w + nw, ... (nw = the K-tile's blocks), which are the ones the table builder gives
+        // warp w: each warp builds its share of the second part's table over its own entries as
+        // soon as it is done with the first, with no barrier.
         for (uint32_t part = 0; part < 2; ++part) {
           if (part) {
-            named_barrier(1, nthr);
+            __syncwarp();
             x_table_i8<QT, TXS, TX ? 1 : 2>(a, mj, sh, ublk, table_s, mtable_s, warp, lane, nw,
                                             a.xpart * kq, a.nb);
-            named_barrier(1, nthr);
+            __syncwarp();
           }
           run(part ? a.xpart : 0u, part ? kt_hi : a.xpart, part ? a.xpart * kq : 0u, part + 1);
         }
@@ -2330,9 +2334,9 @@ int warpmma_plan(kq_ctx* ctx, const kq_matvec_desc& d, uint64_t ldx, uint64_t ld
   // x in two parts (Q6_K tensor-map tiles of a lone launch or a push with one x slot, warp w on
   // block w, no prologue or epilogue): when the whole x table (3.75 bytes an element: K = 28672
   // takes 105 KB) leaves room for only two ring slots, the table holds the first half of the
-  // K-tiles, then the second's, rebuilt once every band has had the first; every band's partial
-  // rows stay in shared memory in between. A third slot of 54 KB keeps more of the CTA's weights
-  // in flight.
+  // K-tiles, then the second's (each warp rebuilds its own entries once every band has had its
+  // first part); every band's partial rows stay in shared memory in between. A third slot of
+  // 54 KB keeps more of the CTA's weights in flight.
   uint32_t xpart = 0;
   const uint32_t cta_bands = static_cast<uint32_t>((rpc + kTileRows - 1) / kTileRows);
   if (tmap && mode == 5 && nw == nwc && tmap_fixed && !(d.flags & kFlagWarpPerBlock) && ksplit <= 1 &&
