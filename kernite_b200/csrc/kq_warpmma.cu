@@ -824,183 +824,11 @@ __device__ __forceinline__ bool produce_job(const WarpMmaArgs& a, const JobArgs&
   return true;
 }
 
-// The integer x table (batch 1) of the x-blocks [kb_lo, kb_hi), at entries kb - kb_lo, and the
-// blocks' scales of x (ublk) at kb. Lane l owns the 8 consecutive elements 8l .. 8l+7 of an
-// x-block, which are chunk l of the block's table entry (the 8 bytes of each limb), so its loads
-// are two 16-byte ones (four for a tagged x), its table writes three 8-byte ones, and the
-// per-sub-block sums need two shuffles. kXG x-blocks a round, all loads in flight (fewer where
-// the caller holds more registers). (A function, not a lambda of the caller: a closure that
-// captures the caller's locals changed the register allocation of every kernel that has it.)
-template <int QT, int TXS, int kXG>
-__device__ __forceinline__ void x_table_i8(const WarpMmaArgs& a, const JobArgs& mj, WarpMmaShared& sh,
-                                           float* ublk, uint32_t table_s, uint32_t mtable_s,
-                                           uint32_t warp, uint32_t lane, uint32_t nw, uint32_t kb_lo,
-                                           uint32_t kb_hi) {
-  constexpr bool TX = TXS > 0;
-  int& s_failed = sh.failed;
-  double (&s_sq)[kMaxWarps][8] = sh.sq;
-  const uint32_t want_tag = TX ? sh.tag_x : 0u;
-  const uint32_t x_slots = TXS == 2 ? sh.x_slots : 1u;
-  const uint64_t kx = uint64_t(a.nb) * kQK;  // elements between x's slots
-  for (uint32_t xb0 = kb_lo + warp; xb0 < kb_hi; xb0 += kXG * nw) {
-    float v[kXG][8];
-    bool tags_ok = true;
-#pragma unroll
-    for (int j = 0; j < kXG; ++j) {
-      const uint32_t kb = xb0 + j * nw;
-      if (kb < kb_hi) {
-        if constexpr (TX) {
-          const unsigned long long* src =
-              reinterpret_cast<const unsigned long long*>(mj.x) + kb * kQK + 8 * lane;
-#pragma unroll
-          for (int q = 0; q < 4; ++q) {
-            const ulonglong2 w = ld_tagged2(src + 2 * q);
-            v[j][2 * q] = __uint_as_float(static_cast<uint32_t>(w.x));
-            v[j][2 * q + 1] = __uint_as_float(static_cast<uint32_t>(w.y));
-            tags_ok &= static_cast<uint32_t>(w.x >> 32) == want_tag &&
-                       static_cast<uint32_t>(w.y >> 32) == want_tag;
-          }
-          // split-K slots 1.. of the writer: added in slot order (the same sum on every rank;
-          // x_slots is 1 unless TXS == 2)
-          for (uint32_t sl = 1; sl < x_slots; ++sl) {
-#pragma unroll
-            for (int q = 0; q < 4; ++q) {
-              const ulonglong2 w = ld_tagged2(src + uint64_t(sl) * kx + 2 * q);
-              v[j][2 * q] += __uint_as_float(static_cast<uint32_t>(w.x));
-              v[j][2 * q + 1] += __uint_as_float(static_cast<uint32_t>(w.y));
-              tags_ok &= static_cast<uint32_t>(w.x >> 32) == want_tag &&
-                         static_cast<uint32_t>(w.y >> 32) == want_tag;
-            }
-          }
-        } else {
-          const float4* src = reinterpret_cast<const float4*>(mj.x + kb * kQK + 8 * lane);
-          const float4 p0 = __ldcg(src), p1 = __ldcg(src + 1);
-          v[j][0] = p0.x, v[j][1] = p0.y, v[j][2] = p0.z, v[j][3] = p0.w;
-          v[j][4] = p1.x, v[j][5] = p1.y, v[j][6] = p1.z, v[j][7] = p1.w;
-        }
-      }
-    }
-    if constexpr (TX) {
-      if (!tags_ok) {
-        // some element is not this step's yet: wait for each, bounded (at once when this CTA
-        // or an earlier launch already gave up); unrolled, so that v stays in registers
-        uint64_t t0 = 0;
-#pragma unroll
-        for (int j = 0; j < kXG; ++j) {
-          const uint32_t kb = xb0 + j * nw;
-          if (kb >= kb_hi) break;
-          const unsigned long long* src =
-              reinterpret_cast<const unsigned long long*>(mj.x) + kb * kQK + 8 * lane;
-#pragma unroll
-          for (int i = 0; i < 8; ++i) {
-            float sum = 0.f;
-            for (uint32_t sl = 0; sl < x_slots; ++sl) {
-              const unsigned long long* at = src + uint64_t(sl) * kx + i;
-              unsigned long long w = ld_tagged(at);
-              while (static_cast<uint32_t>(w >> 32) != want_tag) {
-                if (*reinterpret_cast<volatile int*>(&s_failed) ||
-                    (a.err && *reinterpret_cast<volatile unsigned*>(a.err)))
-                  break;
-                if (t0 == 0) t0 = globaltimer();
-                if (globaltimer() - t0 > kWaitBudgetNs) {
-                  report_error(a.err, kErrWaitPeer);
-                  s_failed = 1;
-                  break;
-                }
-                w = ld_tagged(at);
-              }
-              sum = sl ? sum + __uint_as_float(static_cast<uint32_t>(w))
-                       : __uint_as_float(static_cast<uint32_t>(w));
-            }
-            v[j][i] = sum;
-          }
-        }
-      }
-    }
-#pragma unroll
-    for (int j = 0; j < kXG; ++j) {
-      const uint32_t kb = xb0 + j * nw;
-      if (kb >= kb_hi) break;
-      float mx = 0.f;
-#pragma unroll
-      for (int i = 0; i < 8; ++i) mx = fmaxf(mx, fabsf(v[j][i]));
-#pragma unroll
-      for (int o = 16; o; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-      double sq = 0.0;  // only the RMS norm needs it
-      if (mj.prologue == KQ_PROLOGUE_RMSNORM) {
-#pragma unroll
-        for (int i = 0; i < 8; ++i)
-          sq = fma(static_cast<double>(v[j][i]), static_cast<double>(v[j][i]), sq);
-#pragma unroll
-        for (int o = 16; o; o >>= 1) sq += __shfl_xor_sync(0xffffffffu, sq, o);
-      }
-      // 24-bit fixed point for the block: the power of two that brings max |x| into
-      // [2^21, 2^22), so that x = (L2 2^16 + L1 2^8 + L0) 2^-sh with signed byte limbs
-      // |L2| <= 64, |L1|, |L0| <= 128 (an integer-valued x stays exact).
-      int e = 1;
-      if (mx > 0.f && isfinite(mx)) e = exponent_of(mx);  // mx = f * 2^e, f in [0.5, 1)
-      const int shv = mx > 0.f ? max(-126, min(126, 22 - e)) : 0;
-      const float sc = pow2f(shv);
-      if (lane == 0) {
-        s_sq[warp][0] += sq;
-        ublk[kb] = pow2f(-shv);
-      }
-      uint32_t pk[3][2] = {{0u, 0u}, {0u, 0u}, {0u, 0u}};  // limb bytes, 4 to a word
-      int tl[3] = {0, 0, 0};                              // per-limb sums (Q6_K)
-      int tx = 0;                                         // sum of X (Q4_K, Q5_K)
-#pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        const int X = __float2int_rn(v[j][i] * sc);
-        const int l0 = ((X + 128) & 255) - 128;
-        const int x1 = (X - l0) >> 8;
-        const int l1 = ((x1 + 128) & 255) - 128;
-        const int l2 = (x1 - l1) >> 8;
-        const uint32_t sft = 8 * (i & 3);
-        pk[0][i >> 2] |= (static_cast<uint32_t>(l0) & 0xffu) << sft;
-        pk[1][i >> 2] |= (static_cast<uint32_t>(l1) & 0xffu) << sft;
-        pk[2][i >> 2] |= (static_cast<uint32_t>(l2) & 0xffu) << sft;
-        tl[0] += l0, tl[1] += l1, tl[2] += l2;
-        tx += X;
-      }
-      // chunk `lane` of the block: 24 bytes, 8 of each limb
-      const uint32_t at = table_s + ((kb - kb_lo) * 32 + lane) * 24;
-#pragma unroll
-      for (int l = 0; l < 3; ++l)
-        asm volatile("st.shared.v2.u32 [%0], {%1, %2};" ::"r"(at + 8 * l), "r"(pk[l][0]), "r"(pk[l][1])
-                     : "memory");
-      if constexpr (QT == 6) {
-        // C init of the MMAs: -32 * (sum of each limb over each 16-element sub-block), so that
-        // A = q (unsigned) gives sum (q - 32) x exactly; sub-block sb is lanes 2 sb, 2 sb + 1.
-        // Entry ((kb' * 2 + half) * 3 + l) * 8 + (sub-block within the half), kb' = kb - kb_lo.
-        const uint32_t sb = lane >> 1;
-#pragma unroll
-        for (int l = 0; l < 3; ++l) {
-          const int t = tl[l] + __shfl_xor_sync(0xffffffffu, tl[l], 1);
-          if ((lane & 1) == 0)
-            asm volatile("st.shared.s32 [%0], %1;" ::"r"(
-                             mtable_s + (((kb - kb_lo) * 2 + (sb >> 3)) * 24 + l * 8 + (sb & 7)) * 4),
-                         "r"(-32 * t)
-                         : "memory");
-        }
-      } else {
-        // the sum of x (in limb units) over each 32-element sub-block, lanes 4 r .. 4 r + 3,
-        // for the min term
-        int t = tx + __shfl_xor_sync(0xffffffffu, tx, 1);
-        t += __shfl_xor_sync(0xffffffffu, t, 2);
-        if ((lane & 3) == 0)
-          asm volatile("st.shared.f32 [%0], %1;" ::"r"(mtable_s + ((kb - kb_lo) * 8 + (lane >> 2)) * 4),
-                       "f"(static_cast<float>(t))
-                       : "memory");
-      }
-    }
-  }
-}
-
 // The consumer warps' part of one matvec: x into the B-fragment table (with the RMS-norm sums),
 // then every tile of this CTA's rows from the ring, MMAs, and the outputs. s, phase: the ring
 // position, carried from one matvec of a launch to the next. sync: null for a lone matvec; for a
 // job of a chain, where its outputs are also pushed.
-template <int QT, int NT, bool HILO, bool I8, int TXS = 0, bool XP = false>
+template <int QT, int NT, bool HILO, bool I8, int TXS = 0, int PART = 0>
 __device__ __forceinline__ void consume_job(const WarpMmaArgs& a, const JobArgs& mj,
                                             const ChainSync* sync, uint8_t* base,
                                             WarpMmaShared& sh, uint32_t& s, uint32_t& phase,
@@ -1051,12 +879,175 @@ __device__ __forceinline__ void consume_job(const WarpMmaArgs& a, const JobArgs&
   //  * the scaled values, split into f16 parts, go to their places in the B-fragment table;
   //  * Q4_K: the sums of its eight 32-element sub-blocks (a reduce-scatter by shuffles).
   {
+    if constexpr (PART == 2) __syncwarp();  // (this warp's reads of its first-part entries first)
     if (lane == 0)
       for (int b = 0; b < 8; ++b) s_sq[warp][b] = 0.0;
     if constexpr (I8) {
-      // (more x-blocks a round would spill: a tagged x doubles the live loads)
-      x_table_i8<QT, TXS, TX ? 4 : 6>(a, mj, sh, ublk, table_s, mtable_s, warp, lane, nw, 0,
-                                       XP ? a.xpart * (a.nb / a.nkt) : a.nb);
+      // Batch 1, integer table, of the x-blocks [kb_lo, kb_hi) at entries kb - kb_lo (the scales
+      // of x, ublk, at kb). Lane l owns the 8 consecutive elements 8l .. 8l+7 of an x-block,
+      // which are chunk l of the block's table entry (the 8 bytes of each limb), so its loads
+      // are two 16-byte ones (four for a tagged x), its table writes three 8-byte ones, and the
+      // per-sub-block sums need two shuffles. kXG x-blocks per round, all loads in flight.
+      // PART 0: all of x; 1, 2: the first or second part (warp w builds x-blocks w, w + nw, ...,
+      // with nw the K-tile's blocks: the ones it reads in the fixed-block loop)
+      const uint32_t kb_lo = PART == 2 ? a.xpart * (a.nb / a.nkt) : 0u;
+      const uint32_t kb_hi = PART == 1 ? a.xpart * (a.nb / a.nkt) : a.nb;
+      constexpr int kXG = TX ? 4 : 6;  // (more would spill: a tagged x doubles the live loads)
+      const uint32_t want_tag = TX ? sh.tag_x : 0u;
+      const uint32_t x_slots = TXS == 2 ? sh.x_slots : 1u;
+      const uint64_t kx = uint64_t(a.nb) * kQK;  // elements between x's slots
+      for (uint32_t xb0 = kb_lo + warp; xb0 < kb_hi; xb0 += kXG * nw) {
+        float v[kXG][8];
+        bool tags_ok = true;
+#pragma unroll
+        for (int j = 0; j < kXG; ++j) {
+          const uint32_t kb = xb0 + j * nw;
+          if (kb < kb_hi) {
+            if constexpr (TX) {
+              const unsigned long long* src =
+                  reinterpret_cast<const unsigned long long*>(mj.x) + kb * kQK + 8 * lane;
+#pragma unroll
+              for (int q = 0; q < 4; ++q) {
+                const ulonglong2 w = ld_tagged2(src + 2 * q);
+                v[j][2 * q] = __uint_as_float(static_cast<uint32_t>(w.x));
+                v[j][2 * q + 1] = __uint_as_float(static_cast<uint32_t>(w.y));
+                tags_ok &= static_cast<uint32_t>(w.x >> 32) == want_tag &&
+                           static_cast<uint32_t>(w.y >> 32) == want_tag;
+              }
+              // split-K slots 1.. of the writer: added in slot order (the same sum on every rank)
+              if constexpr (TXS == 2)
+              for (uint32_t sl = 1; sl < x_slots; ++sl) {
+#pragma unroll
+                for (int q = 0; q < 4; ++q) {
+                  const ulonglong2 w = ld_tagged2(src + uint64_t(sl) * kx + 2 * q);
+                  v[j][2 * q] += __uint_as_float(static_cast<uint32_t>(w.x));
+                  v[j][2 * q + 1] += __uint_as_float(static_cast<uint32_t>(w.y));
+                  tags_ok &= static_cast<uint32_t>(w.x >> 32) == want_tag &&
+                             static_cast<uint32_t>(w.y >> 32) == want_tag;
+                }
+              }
+            } else {
+              const float4* src = reinterpret_cast<const float4*>(mj.x + kb * kQK + 8 * lane);
+              const float4 p0 = __ldcg(src), p1 = __ldcg(src + 1);
+              v[j][0] = p0.x, v[j][1] = p0.y, v[j][2] = p0.z, v[j][3] = p0.w;
+              v[j][4] = p1.x, v[j][5] = p1.y, v[j][6] = p1.z, v[j][7] = p1.w;
+            }
+          }
+        }
+        if constexpr (TX) {
+          if (!tags_ok) {
+            // some element is not this step's yet: wait for each, bounded (at once when this CTA
+            // or an earlier launch already gave up); unrolled, so that v stays in registers
+            uint64_t t0 = 0;
+#pragma unroll
+            for (int j = 0; j < kXG; ++j) {
+              const uint32_t kb = xb0 + j * nw;
+              if (kb >= kb_hi) break;
+              const unsigned long long* src =
+                  reinterpret_cast<const unsigned long long*>(mj.x) + kb * kQK + 8 * lane;
+#pragma unroll
+              for (int i = 0; i < 8; ++i) {
+                float sum = 0.f;
+                for (uint32_t sl = 0; sl < x_slots; ++sl) {
+                  const unsigned long long* at = src + uint64_t(sl) * kx + i;
+                  unsigned long long w = ld_tagged(at);
+                  while (static_cast<uint32_t>(w >> 32) != want_tag) {
+                    if (*reinterpret_cast<volatile int*>(&s_failed) ||
+                        (a.err && *reinterpret_cast<volatile unsigned*>(a.err)))
+                      break;
+                    if (t0 == 0) t0 = globaltimer();
+                    if (globaltimer() - t0 > kWaitBudgetNs) {
+                      report_error(a.err, kErrWaitPeer);
+                      s_failed = 1;
+                      break;
+                    }
+                    w = ld_tagged(at);
+                  }
+                  sum = sl ? sum + __uint_as_float(static_cast<uint32_t>(w))
+                           : __uint_as_float(static_cast<uint32_t>(w));
+                }
+                v[j][i] = sum;
+              }
+            }
+          }
+        }
+#pragma unroll
+        for (int j = 0; j < kXG; ++j) {
+          const uint32_t kb = xb0 + j * nw;
+          if (kb >= kb_hi) break;
+          float mx = 0.f;
+#pragma unroll
+          for (int i = 0; i < 8; ++i) mx = fmaxf(mx, fabsf(v[j][i]));
+#pragma unroll
+          for (int o = 16; o; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+          double sq = 0.0;  // only the RMS norm needs it
+          if (mj.prologue == KQ_PROLOGUE_RMSNORM) {
+#pragma unroll
+            for (int i = 0; i < 8; ++i)
+              sq = fma(static_cast<double>(v[j][i]), static_cast<double>(v[j][i]), sq);
+#pragma unroll
+            for (int o = 16; o; o >>= 1) sq += __shfl_xor_sync(0xffffffffu, sq, o);
+          }
+          // 24-bit fixed point for the block: the power of two that brings max |x| into
+          // [2^21, 2^22), so that x = (L2 2^16 + L1 2^8 + L0) 2^-sh with signed byte limbs
+          // |L2| <= 64, |L1|, |L0| <= 128 (an integer-valued x stays exact).
+          int e = 1;
+          if (mx > 0.f && isfinite(mx)) e = exponent_of(mx);  // mx = f * 2^e, f in [0.5, 1)
+          const int shv = mx > 0.f ? max(-126, min(126, 22 - e)) : 0;
+          const float sc = pow2f(shv);
+          if (lane == 0) {
+            s_sq[warp][0] += sq;
+            ublk[kb] = pow2f(-shv);
+          }
+          uint32_t pk[3][2] = {{0u, 0u}, {0u, 0u}, {0u, 0u}};  // limb bytes, 4 to a word
+          int tl[3] = {0, 0, 0};                              // per-limb sums (Q6_K)
+          int tx = 0;                                         // sum of X (Q4_K, Q5_K)
+#pragma unroll
+          for (int i = 0; i < 8; ++i) {
+            const int X = __float2int_rn(v[j][i] * sc);
+            const int l0 = ((X + 128) & 255) - 128;
+            const int x1 = (X - l0) >> 8;
+            const int l1 = ((x1 + 128) & 255) - 128;
+            const int l2 = (x1 - l1) >> 8;
+            const uint32_t sft = 8 * (i & 3);
+            pk[0][i >> 2] |= (static_cast<uint32_t>(l0) & 0xffu) << sft;
+            pk[1][i >> 2] |= (static_cast<uint32_t>(l1) & 0xffu) << sft;
+            pk[2][i >> 2] |= (static_cast<uint32_t>(l2) & 0xffu) << sft;
+            tl[0] += l0, tl[1] += l1, tl[2] += l2;
+            tx += X;
+          }
+          // chunk `lane` of the block: 24 bytes, 8 of each limb
+          const uint32_t at = table_s + ((kb - kb_lo) * 32 + lane) * 24;
+#pragma unroll
+          for (int l = 0; l < 3; ++l)
+            asm volatile("st.shared.v2.u32 [%0], {%1, %2};" ::"r"(at + 8 * l), "r"(pk[l][0]), "r"(pk[l][1])
+                         : "memory");
+          if constexpr (QT == 6) {
+            // C init of the MMAs: -32 * (sum of each limb over each 16-element sub-block), so that
+            // A = q (unsigned) gives sum (q - 32) x exactly; sub-block sb is lanes 2 sb, 2 sb + 1.
+            // Entry ((kb' * 2 + half) * 3 + l) * 8 + (sub-block within the half), kb' = kb - kb_lo.
+            const uint32_t sb = lane >> 1;
+#pragma unroll
+            for (int l = 0; l < 3; ++l) {
+              const int t = tl[l] + __shfl_xor_sync(0xffffffffu, tl[l], 1);
+              if ((lane & 1) == 0)
+                asm volatile("st.shared.s32 [%0], %1;" ::"r"(
+                                 mtable_s + (((kb - kb_lo) * 2 + (sb >> 3)) * 24 + l * 8 + (sb & 7)) * 4),
+                             "r"(-32 * t)
+                             : "memory");
+            }
+          } else {
+            // the sum of x (in limb units) over each 32-element sub-block, lanes 4 r .. 4 r + 3,
+            // for the min term
+            int t = tx + __shfl_xor_sync(0xffffffffu, tx, 1);
+            t += __shfl_xor_sync(0xffffffffu, t, 2);
+            if ((lane & 3) == 0)
+              asm volatile("st.shared.f32 [%0], %1;" ::"r"(mtable_s + ((kb - kb_lo) * 8 + (lane >> 2)) * 4),
+                           "f"(static_cast<float>(t))
+                           : "memory");
+          }
+        }
+      }
     } else {
     const uint32_t nxb = a.nb * B;
     for (uint32_t xb0 = warp; xb0 < nxb; xb0 += 4 * nw) {
@@ -1233,11 +1224,14 @@ __device__ __forceinline__ void consume_job(const WarpMmaArgs& a, const JobArgs&
       }
     }
     }
-    // a zeroed region that lanes without a B column read their fragments from
-    for (uint32_t i = tid; i < kZeroBytes / 4; i += nthr)
-      asm volatile("st.shared.u32 [%0], %1;" ::"r"(ring_s + a.zero_off + 4 * i), "r"(0u) : "memory");
-    named_barrier(1, nthr);
-    if (tid < B) {
+    // a zeroed region that lanes without a B column read their fragments from (the second part
+    // of x has it already; its warps go on alone: each reads only the entries it built)
+    if constexpr (PART != 2) {
+      for (uint32_t i = tid; i < kZeroBytes / 4; i += nthr)
+        asm volatile("st.shared.u32 [%0], %1;" ::"r"(ring_s + a.zero_off + 4 * i), "r"(0u) : "memory");
+      named_barrier(1, nthr);
+    }
+    if (PART != 2 && tid < B) {
       float ns = 1.f;
       if (mj.prologue == KQ_PROLOGUE_RMSNORM) {
         double t = 0.0;
@@ -1396,9 +1390,10 @@ __device__ __forceinline__ void consume_job(const WarpMmaArgs& a, const JobArgs&
   };
 
   // The band is done: this warp's partial rows go to the reduction buffer; every fb bands (and
-  // after the last) the warps meet and sum them in a fixed order into y. part: 0, or with x in
-  // two parts 1 (store the partial rows, no flush: fb covers every band) and 2 (add to them).
-  auto band_end = [&](uint32_t band, uint32_t& bi, uint32_t part = 0) {
+  // after the last) the warps meet and sum them in a fixed order into y. With x in two parts
+  // (PART 1, 2): the first stores the partial rows (no flush: fb covers every band), the second
+  // adds to them.
+  auto band_end = [&](uint32_t band, uint32_t& bi) {
     if constexpr (QT == 6 || I8) {
       // the four threads of a row hold different sub-blocks of vector 0
 #pragma unroll
@@ -1409,7 +1404,7 @@ __device__ __forceinline__ void consume_job(const WarpMmaArgs& a, const JobArgs&
       if (c == 0) {
         float* rg = &red[((bi * nw + warp) * kTileRows + pg) * B];
         float* rh = &red[((bi * nw + warp) * kTileRows + ph) * B];
-        if (XP && part == 2) {
+        if (PART == 2) {
           // (the first part's partial of the same row, written by this thread)
           *rg += yacc[0][0];
           *rh += yacc[1][0];
@@ -1430,7 +1425,7 @@ __device__ __forceinline__ void consume_job(const WarpMmaArgs& a, const JobArgs&
     }
     yacc[0][0] = yacc[0][1] = yacc[1][0] = yacc[1][1] = 0.f;
 
-    if ((!XP || part != 1) && (bi + 1 == a.fb || band + 1 == nbands)) {
+    if (PART != 1 && (bi + 1 == a.fb || band + 1 == nbands)) {
       // Flush: sum every warp's partial of each row in a fixed order and write y.
       named_barrier(1, nthr);
       const uint32_t band0 = band - bi;
@@ -1490,9 +1485,9 @@ __device__ __forceinline__ void consume_job(const WarpMmaArgs& a, const JobArgs&
       const uint32_t off_g = pg_rb + fkb * kBlk, off_h = ph_rb + fkb * kBlk;
       uint32_t kt_lo, kt_hi;
       cta_ktiles(nkt, a.ksplit, kt_lo, kt_hi);
-      // part: 0 (x whole), or 1 and 2 (x in two parts: the K-tiles [kt_a, kt_z) of every band,
-      // whose x-blocks are the table's from kb_base on)
-      auto tmap_loop = [&](auto cls, uint32_t kt_a, uint32_t kt_z, uint32_t kb_base, uint32_t part) {
+      // the K-tiles [kt_a, kt_z) of every band (all, or with x in two parts those of the part),
+      // whose x-blocks are the table's from kb_base on
+      auto tmap_loop = [&](auto cls, uint32_t kt_a, uint32_t kt_z, uint32_t kb_base) {
         constexpr int F = decltype(cls)::value;
         uint32_t bi = 0;
         for (uint32_t band = 0; band < nbands; ++band) {
@@ -1532,35 +1527,17 @@ __device__ __forceinline__ void consume_job(const WarpMmaArgs& a, const JobArgs&
               phase ^= 1;
             }
           }
-          band_end(band, bi, part);
+          band_end(band, bi);
         }
       };
-      auto run = [&](uint32_t kt_a, uint32_t kt_z, uint32_t kb_base, uint32_t pm) {
-        switch (residue_class(fkb * kBlk)) {
-          case 16: tmap_loop(std::integral_constant<int, 16>(), kt_a, kt_z, kb_base, pm); break;
-          case 8: tmap_loop(std::integral_constant<int, 8>(), kt_a, kt_z, kb_base, pm); break;
-          case 4: tmap_loop(std::integral_constant<int, 4>(), kt_a, kt_z, kb_base, pm); break;
-          case 2: tmap_loop(std::integral_constant<int, 2>(), kt_a, kt_z, kb_base, pm); break;
-          default: tmap_loop(std::integral_constant<int, 6>(), kt_a, kt_z, kb_base, pm); break;
-        }
-      };
-      if constexpr (XP) {
-        // x in two parts (the kernel compiled for them): every band's first K-tiles, then the
-        // second's. Warp w reads only the table entries of its own block of each K-tile, x-blocks
-        // w, w + nw, ... (nw = the K-tile's blocks), which are the ones the table builder gives
-        // warp w: each warp builds its share of the second part's table over its own entries as
-        // soon as it is done with the first, with no barrier.
-        for (uint32_t part = 0; part < 2; ++part) {
-          if (part) {
-            __syncwarp();
-            x_table_i8<QT, TXS, TX ? 1 : 2>(a, mj, sh, ublk, table_s, mtable_s, warp, lane, nw,
-                                            a.xpart * kq, a.nb);
-            __syncwarp();
-          }
-          run(part ? a.xpart : 0u, part ? kt_hi : a.xpart, part ? a.xpart * kq : 0u, part + 1);
-        }
-      } else {
-        run(kt_lo, kt_hi, 0u, 0u);
+      const uint32_t kt_a = PART == 2 ? a.xpart : kt_lo, kt_z = PART == 1 ? a.xpart : kt_hi;
+      const uint32_t kb_base = PART == 2 ? a.xpart * kq : 0u;
+      switch (residue_class(fkb * kBlk)) {
+        case 16: tmap_loop(std::integral_constant<int, 16>(), kt_a, kt_z, kb_base); break;
+        case 8: tmap_loop(std::integral_constant<int, 8>(), kt_a, kt_z, kb_base); break;
+        case 4: tmap_loop(std::integral_constant<int, 4>(), kt_a, kt_z, kb_base); break;
+        case 2: tmap_loop(std::integral_constant<int, 2>(), kt_a, kt_z, kb_base); break;
+        default: tmap_loop(std::integral_constant<int, 6>(), kt_a, kt_z, kb_base); break;
       }
       return;
     }
@@ -1867,7 +1844,14 @@ __global__ void __launch_bounds__((kMaxWarps + 1) * 32, 1) warpmma_kernel(const 
     return;
   }
   pdl_wait();  // x may be the previous kernel's output
-  consume_job<QT, NT, HILO, I8, 0, XP>(a, v, nullptr, base, sh, s, phase);
+  if constexpr (XP) {
+    // x in two parts: the first part's table and K-tiles, then the second's (the ring position
+    // and the partial rows in shared memory carry over)
+    consume_job<QT, NT, HILO, I8, 0, 1>(a, v, nullptr, base, sh, s, phase);
+    consume_job<QT, NT, HILO, I8, 0, 2>(a, v, nullptr, base, sh, s, phase);
+  } else {
+    consume_job<QT, NT, HILO, I8>(a, v, nullptr, base, sh, s, phase);
+  }
 }
 
 __device__ __forceinline__ unsigned long long ld_acquire_gpu(const unsigned long long* p) {
@@ -1947,7 +1931,12 @@ __global__ void __launch_bounds__((kMaxWarps + 1) * 32, 1)
     }
   }
   named_barrier(1, nthr);
-  consume_job<QT, 1, false, true, TXS, XP>(a, v, &q.y, base, sh, s, phase);
+  if constexpr (XP) {
+    consume_job<QT, 1, false, true, TXS, 1>(a, v, &q.y, base, sh, s, phase);
+    consume_job<QT, 1, false, true, TXS, 2>(a, v, &q.y, base, sh, s, phase);
+  } else {
+    consume_job<QT, 1, false, true, TXS>(a, v, &q.y, base, sh, s, phase);
+  }
   if (q.y.tagged) return;  // no counts
   named_barrier(1, nthr);  // every consumer's outputs are stored
   if (threadIdx.x == 0 && q.y.npush) {
@@ -2105,11 +2094,10 @@ const void* push_fn_t(uint32_t type) {
          : type == KQ_TYPE_Q5_K ? reinterpret_cast<const void*>(&warpmma_push_kernel<5, TXS>)
                                 : reinterpret_cast<const void*>(&warpmma_push_kernel<6, TXS>);
 }
-// (xp: the Q6_K kernel compiled for x in two parts, plain or tagged x with one slot)
+// (xp: the Q6_K kernel compiled for x in two parts, plain x)
 const void* push_fn(uint32_t type, int txs, bool xp = false) {
-  if (xp && type == KQ_TYPE_Q6_K && txs < 2)
-    return txs == 0 ? reinterpret_cast<const void*>(&warpmma_push_kernel<6, 0, true>)
-                    : reinterpret_cast<const void*>(&warpmma_push_kernel<6, 1, true>);
+  if (xp && type == KQ_TYPE_Q6_K && txs == 0)
+    return reinterpret_cast<const void*>(&warpmma_push_kernel<6, 0, true>);
   return txs == 0 ? push_fn_t<0>(type) : txs == 1 ? push_fn_t<1>(type) : push_fn_t<2>(type);
 }
 
@@ -2161,7 +2149,8 @@ struct WarpMmaPlan {
 // Chooses the variant, the tiles and the shared-memory layout of one matvec (arguments already
 // checked by the caller), as the standalone launch uses them.
 int warpmma_plan(kq_ctx* ctx, const kq_matvec_desc& d, uint64_t ldx, uint64_t ldy, const char* call,
-                 WarpMmaPlan& plan, uint32_t ksplit = 1, bool compact = true, bool tmap_fixed = true) {
+                 WarpMmaPlan& plan, uint32_t ksplit = 1, bool compact = true, bool tmap_fixed = true,
+                 bool xparts = true) {
   const bool q4 = d.type == KQ_TYPE_Q4_K;
   const bool q5 = d.type == KQ_TYPE_Q5_K;  // Q4_K's layout plus qh: the Q4_K forms, integer only
   const bool q45 = q4 || q5;
@@ -2331,7 +2320,7 @@ int warpmma_plan(kq_ctx* ctx, const kq_matvec_desc& d, uint64_t ldx, uint64_t ld
     const uint64_t tail_ = table + ublk_bytes + kZeroBytes + 16 + uint64_t(bands) * band_red + 2 * 8 * 8 + 128;
     return tail_ < uint64_t(ctx->max_smem) ? (uint64_t(ctx->max_smem) - tail_) / slot : 0;
   };
-  // x in two parts (Q6_K tensor-map tiles of a lone launch or a push with one x slot, warp w on
+  // x in two parts (Q6_K tensor-map tiles of a lone launch or a push of a plain x, warp w on
   // block w, no prologue or epilogue): when the whole x table (3.75 bytes an element: K = 28672
   // takes 105 KB) leaves room for only two ring slots, the table holds the first half of the
   // K-tiles, then the second's (each warp rebuilds its own entries once every band has had its
@@ -2339,7 +2328,7 @@ int warpmma_plan(kq_ctx* ctx, const kq_matvec_desc& d, uint64_t ldx, uint64_t ld
   // 54 KB keeps more of the CTA's weights in flight.
   uint32_t xpart = 0;
   const uint32_t cta_bands = static_cast<uint32_t>((rpc + kTileRows - 1) / kTileRows);
-  if (tmap && mode == 5 && nw == nwc && tmap_fixed && !(d.flags & kFlagWarpPerBlock) && ksplit <= 1 &&
+  if (xparts && tmap && mode == 5 && nw == nwc && tmap_fixed && !(d.flags & kFlagWarpPerBlock) && ksplit <= 1 &&
       d.prologue == KQ_PROLOGUE_NONE && d.epilogue == KQ_EPILOGUE_NONE && nkt >= 2 &&
       cta_bands <= 16 && ring_for(table_bytes + mtable_bytes, 16) < 3) {
     const uint32_t kh = (nkt + 1) / 2, nbh = kh * (nb / nkt);
@@ -2521,8 +2510,12 @@ int warpmma_push(kq_ctx* ctx, const kq_matvec_desc& d, const kq_push_desc& push,
   // (the fixed-block loop on tensor-map tiles: Q6_K only, and not with split-K slots; the Q4_K
   // and Q5_K push kernels are compiled without it, which cost them registers)
   const uint32_t ks = std::min<uint32_t>(std::max<uint32_t>(push.ksplit, 1), 8);
+  const bool tagged = (push.flags & KQ_PUSH_TAGGED) != 0;
+  const bool tx = tagged && (push.wait_counter || (push.flags & KQ_PUSH_TAGGED_X));
+  // (x in two parts only for a plain x: with a tagged x, the second part's table waits for its
+  // loads with no tiles to hide them, and measured slower on B200 than the whole table)
   int rc = warpmma_plan(ctx, d, ldx, ldy, call, plan, ks, true,
-                        d.type == KQ_TYPE_Q6_K && push.x_slots <= 1);
+                        d.type == KQ_TYPE_Q6_K && push.x_slots <= 1, !tx);
   if (rc) return rc;
   if (plan.mode != (d.type == KQ_TYPE_Q4_K ? 4 : d.type == KQ_TYPE_Q5_K ? 6 : 5))
     return fail(KQ_E_UNSUPPORTED, call, "k " + std::to_string(d.k) + " does not fit the integer kernel");
@@ -2537,8 +2530,6 @@ int warpmma_push(kq_ctx* ctx, const kq_matvec_desc& d, const kq_push_desc& push,
   q.epoch = reinterpret_cast<const unsigned long long*>(push.epoch);
   q.wait_mul = push.wait_mul;
   q.wait_add = push.wait_add;
-  const bool tagged = (push.flags & KQ_PUSH_TAGGED) != 0;
-  const bool tx = tagged && (push.wait_counter || (push.flags & KQ_PUSH_TAGGED_X));
   q.y.tagged = tagged ? 1u : 0u;
   q.push_mul = push.push_mul;
   q.push_add = push.push_add;
