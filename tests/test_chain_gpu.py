@@ -113,14 +113,21 @@ def _stack_logits(kernels, cfg, xs, chain, graph=True):
     return out
 
 
-@pytest.mark.parametrize("name,layers", [("tiny", None), ("7b", 2), ("70b", 2)])
-def test_chain_stack_equals_launch_per_projection_and_reference(kernels, name, layers):
+@pytest.mark.parametrize("name,layers,exact", [("tiny", None, True), ("7b", 2, True), ("70b", 2, False)])
+def test_chain_stack_equals_launch_per_projection_and_reference(kernels, name, layers, exact):
+    """The chain stack's logits equal the launch-per-projection stack's bit for bit, except where a
+    lone launch takes x in two parts (the 70B down projection, K = 28672: its partial sums are
+    added in another order than the chain's), where they agree within 2e-5 of the largest logit;
+    both within 1e-4 of it against the f64 reference."""
     cfg = st.CONFIGS[name] if layers is None else dataclasses.replace(st.CONFIGS[name], layers=layers)
     xs = [np.random.default_rng(11 + t).standard_normal(cfg.hidden).astype(np.float32) for t in range(3)]
     got = _stack_logits(kernels, cfg, xs, chain=True)
     base = _stack_logits(kernels, cfg, xs, chain=False)
     for t, x in enumerate(xs):
-        assert np.array_equal(got[t], base[t]), f"token {t}"
+        if exact:
+            assert np.array_equal(got[t], base[t]), f"token {t}"
+        else:
+            assert np.abs(got[t] - base[t]).max() <= 2e-5 * np.abs(base[t]).max(), f"token {t}"
         if t == 0:
             ref = st.reference_logits(cfg, x)
             assert np.abs(got[t] - ref).max() <= 1e-4 * np.abs(ref).max()
